@@ -1,0 +1,321 @@
+#!/usr/bin/env python
+"""Codec frames/s of qwen3-tts.cpp's per-frame codec-token loop on B200.
+
+Workload (default): BASELINE.json configs[0] — greedy F16 frame loop, batch 1,
+seeded random-init GGUF with the 0.6B layout, ICL prompt with 55 reference
+frames (64 talker prefill positions), repetition penalty 1.05, EOS suppressed
+by eos_bias = -1e9.  `--config q8` runs configs[1] (Q8_0, 128 prefill).
+
+A step = one codec frame: codebook-0 sampling, the 2-token code-predictor
+prefill, 14 code-predictor steps with on-device sampling, the next-step
+embedding sum and one 28-layer talker step.  Each rank runs its own utterance
+on its own GPU (weak scaling, no collective on the data path); the timed
+region is bracketed by a barrier + synchronize and the device time is the max
+over ranks.  Every frame streams 3.3 GB of weights (> 126 MB L2), so no L2
+flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "qwen3-tts.cpp_b200")
+sys.path.insert(0, ROOT)
+
+METRIC = "codec frames/s"
+UNIT = "frames/s"
+# SURVEY 8d algorithmic bytes per frame per sequence (weights); KV added per frame below.
+WEIGHT_BYTES = {"f16": 3_309_305_856, "q8": 1_790_509_056}
+KV_TALKER_PER_POS = 114_688      # 28 layers x (K+V) x 8 heads x 128 x 2 B
+KV_CP_PER_POS = 20_480           # 5 layers x (K+V) x 8 x 128 x 2 B
+CONFIGS = {
+    "f16": dict(wtype="f16", n_ref=55, prefill=64,
+                workload="BASELINE configs[0]: greedy F16 frame loop, batch 1, ICL prefill 64, rep 1.05"),
+    "q8": dict(wtype="q8_0", n_ref=119, prefill=128,
+               workload="BASELINE configs[1]: greedy Q8_0 frame loop, batch 1, ICL prefill 128, rep 1.05"),
+}
+
+
+def _pkg():
+    spec = importlib.util.spec_from_file_location("qtts_b200", os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["qtts_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _inputs(seed: int, n_ref: int):
+    rng = np.random.default_rng(seed)
+    tgt = rng.integers(0, 151643, 24).astype(np.int32)
+    ref = rng.integers(0, 151643, 30).astype(np.int32)
+    codes = rng.integers(0, 2048, (n_ref, 16)).astype(np.int32)
+    spk = rng.standard_normal(1024).astype(np.float32)
+    spk /= np.linalg.norm(spk)
+    return tgt, ref, codes, spk
+
+
+def _model(cfg, rank: int, local_rank: int, barrier):
+    pkg = _pkg()
+    d = os.environ.get("QTTS_MODEL_DIR", os.path.join(ROOT, ".models"))
+    path = os.path.join(d, f"synth-full-{cfg['wtype']}-s0.gguf")
+    if local_rank == 0 and not os.path.exists(path):
+        pkg.synth_gguf.ensure_gguf(d, pkg.synth_gguf.FULL, cfg["wtype"], seed=0)
+    barrier()
+    return pkg, path
+
+
+class ClockSampler:
+    """Polls SM clock and throttle reasons through NVML while the timed region runs."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.ok = [], set(), False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.ok:
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_per_launch():
+    """DRAM bytes per k_gemv launch from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "k_gemv_frame_ncu.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_frames_per_s(path: str, n_ref_prefill: int, budget_s: float, max_frames: int):
+    """The CPU oracle port on all host cores: frames after a prefill of the same length."""
+    from oracle import Oracle
+    cores = os.cpu_count() or 1
+    o = Oracle(path, threads=cores)
+    H = o.cfg["hidden"]
+    rng = np.random.default_rng(7)
+    rows = (rng.standard_normal((n_ref_prefill, H)) * 0.1).astype(np.float32)
+    o.init_kv(n_ref_prefill + max_frames + 16)
+    hid, lg = o.forward_prefill(rows)
+    hidden = hid[-1]
+    pos, frames, t_used = n_ref_prefill, 0, 0.0
+    cb0 = int(np.argmax(lg[:2048]))
+    while frames < max_frames and t_used < budget_s:
+        t0 = time.perf_counter()
+        codes, _ = o.predict_codes(hidden, cb0)
+        step = o.lookup(0, [cb0])[0]
+        for g in range(15):
+            step = step + o.lookup(g + 1, [int(codes[g])])[0]
+        lg, hidden = o.forward_step(step, pos)
+        cb0 = int(np.argmax(lg[:2048]))
+        t_used += time.perf_counter() - t0
+        pos += 1
+        frames += 1
+    return frames / t_used, cores, frames, t_used
+
+
+def run_reference(args, cfg):
+    """Reference arm: the CPU port of the path (the reference's ggml build is not
+    buildable: its ggml submodule is empty), rank 0 only, all host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    pkg, path = _model(cfg, 0, 0, lambda: None)
+    for _ in range(max(0, args.warmup)):
+        pass
+    fps, cores, frames, secs = cpu_frames_per_s(path, cfg["prefill"], budget_s=1e9, max_frames=args.steps)
+    line = {"impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": frames, "warmup": args.warmup, "ms_per_step": 1000.0 * secs / max(frames, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16" if cfg["wtype"] == "f16" else "q8_0", "data": "synthetic (seeded random-init GGUF, 0.6B layout)",
+            "config": {"workload": cfg["workload"], "l2": "inputs larger than L2 (weights streamed every frame)"},
+            "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{frames} frames (talker step + 15 code-predictor passes) after a {cfg['prefill']}-row prefill; "
+                                       "CPU oracle port (reference ggml build not buildable: ggml submodule absent)"},
+            "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="f16")
+    ap.add_argument("--profile-frames", type=int, default=4)
+    ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    pkg, path = _model(cfg, rank, local, barrier)
+    eng = pkg.Engine(path, local)
+    tgt, ref, codes, spk = _inputs(1000 + rank, cfg["n_ref"])
+    gen = dict(speaker=spk, ref_text=ref, ref_codes=codes, rep_penalty=1.05, temperature=0.0, top_k=0, eos_bias=-1e9)
+    K, W = args.steps, args.warmup
+
+    # ---- device-resident timing: inputs in HBM, K graph-replayed frames
+    plen = eng.generate_begin(tgt, W + K, **gen)
+    assert plen == cfg["prefill"], plen
+    eng.run_frames(W)
+    t0 = eng.timing()["frames_ms"]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        got = eng.run_frames(K)
+    barrier()
+    torch.cuda.synchronize()
+    ms = eng.timing()["frames_ms"] - t0
+    assert got == K, got
+    ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    launches_per_frame = eng.timing()["kernel_launches"]
+
+    # ---- per-kernel roofline: eager replay with events around each launch
+    eng.generate_begin(tgt, W + args.profile_frames, **gen)
+    eng.run_frames(W)
+    prof = eng.profile_frames(args.profile_frames)
+
+    # ---- end to end through the C ABI with host buffers (prompt in, codes out)
+    eng.generate(tgt, 2, **gen)            # untimed warm call
+    barrier()
+    torch.cuda.synchronize()
+    t_e0 = time.perf_counter()
+    out = eng.generate(tgt, K, **gen)
+    t_e = time.perf_counter() - t_e0
+    assert out["n_frames"] == K
+    et = torch.tensor([t_e], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    t_e = float(et.item())
+    H = eng.cfg["hidden_size"]
+    n_text_rows = 3 + 3 + (len(ref) - 8) + (len(tgt) - 8) + 1
+    n_lookup_rows = 3 + 2 + 1 + 16 * cfg["n_ref"]
+    h2d = (4 * (len(tgt) + len(ref) + codes.size) + 4 * H * (plen + 1) + 4 * n_text_rows + 4 * n_lookup_rows)
+    d2h = 4 * H * (n_text_rows + n_lookup_rows) + 4 * 16 * K + 4 * H + 1024 * ((K + 15) // 16)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peak, peak_kind = _peaks()
+    g = prof["gemv"]
+    achieved = (g["bytes"] / g["launches"]) / (g["ms"] / g["launches"] / 1e3) / 1e9 if g["launches"] else None
+    frame_ms = ms_max / K
+    kv_pos_mean = plen + W + K / 2.0
+    frame_bytes = WEIGHT_BYTES[args.config] + KV_TALKER_PER_POS * kv_pos_mean + KV_CP_PER_POS * 135
+    traffic = _traffic_per_launch()
+    prof_total = sum(prof[c]["ms"] for c in ("gemv", "attention", "sample", "other"))
+    line = {
+        "metric": METRIC, "value": world * K / (ms_max / 1e3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": frame_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16" if args.config == "f16" else "q8_0",
+        "data": "synthetic (seeded random-init GGUF with the 0.6B layout; random prompt ids and reference codes)",
+        "config": {"workload": cfg["workload"], "batch_per_gpu": 1, "prefill": plen, "frames_timed": K,
+                   "parallelism": f"independent utterance per GPU x{world}",
+                   "l2": "inputs larger than L2 (3.3 GB of weights streamed per frame), no flush"},
+        "roofline": {"bound": "hbm", "kernel": "k_gemv (all GEMV launches of a frame, eager replay)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": (achieved / peak) if achieved else None, "traffic": traffic,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
+                     "bytes_per_launch": g["bytes"] / max(g["launches"], 1),
+                     "launches_per_frame": g["launches"] / max(prof["frames"], 1),
+                     "share_of_frame": g["ms"] / prof_total if prof_total else None,
+                     "frame_algorithmic_gbs": frame_bytes / (frame_ms / 1e3) / 1e9,
+                     "frame_frac": frame_bytes / (frame_ms / 1e3) / 1e9 / peak},
+        "kernel_classes": {c: {"launches_per_frame": prof[c]["launches"] / max(prof["frames"], 1),
+                               "ms_per_frame": prof[c]["ms"] / max(prof["frames"], 1)}
+                           for c in ("gemv", "attention", "sample", "other")},
+        "e2e": {"value": world * K / t_e, "unit": UNIT, "h2d_bytes_per_step": h2d / K, "d2h_bytes_per_step": d2h / K,
+                "includes": "qtts_generate: prompt upload, prefill, K frames, codes download"},
+        "gpu_launches": launches_per_frame * K,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        fps, cores, frames, secs = cpu_frames_per_s(path, plen, args.cpu_budget_s, 16)
+        line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": f"{frames} frames after a {plen}-row prefill in {secs:.1f} s "
+                                          "(CPU oracle port, OpenMP over all host threads)"}
+    print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

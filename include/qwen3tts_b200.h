@@ -1,0 +1,181 @@
+/* qwen3tts_b200.h — C ABI of the B200 codec-token engine.
+ *
+ * One engine = one GPU, one sequence at a time, exactly like the reference's
+ * TTSTransformer (src/tts_transformer.h:198-422).  Every entry point below
+ * replaces one TTSTransformer member; the C++ drop-in class in
+ * tts_transformer.h forwards to these.  Conventions follow the reference:
+ * functions return 1 (true) / 0 (false) where the reference returns bool, and
+ * the message is read with qtts_get_error() (src/tts_transformer.h:328).
+ * Buffers are plain host pointers owned by the caller; sizes are in elements.
+ * No torch, CUDA or ggml type appears in any signature.
+ */
+#ifndef QWEN3TTS_B200_H
+#define QWEN3TTS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct qtts_engine qtts_engine;
+
+/* Field-for-field copy of tts_transformer_config (src/tts_transformer.h:59-103)
+ * plus the weight type of the layer matrices (1 = F16, 8 = Q8_0). */
+typedef struct qtts_config {
+    int32_t text_vocab_size, text_embd_dim;
+    int32_t hidden_size, n_layers, n_attention_heads, n_key_value_heads, intermediate_size, head_dim;
+    float rms_norm_eps, rope_theta;
+    int32_t mrope_section[3];
+    int32_t codec_vocab_size, n_codebooks;
+    int32_t code_pred_layers, code_pred_vocab_size, code_pred_hidden_size, code_pred_intermediate_size;
+    float code_pred_rope_theta;
+    int32_t codec_pad_id, codec_bos_id, codec_eos_id;
+    int32_t tts_bos_token_id, tts_eos_token_id, tts_pad_token_id;
+    int32_t codec_think_id, codec_nothink_id, codec_think_bos_id, codec_think_eos_id;
+    int32_t english_language_id;
+    int32_t weight_type;
+} qtts_config;
+
+/* Arguments of TTSTransformer::generate / generate_icl
+ * (src/tts_transformer.h:293-324).  ICL mode when ref_codec_tokens != NULL.
+ * seed keys the Philox stream of sampled decoding (the reference's std::mt19937
+ * has no seed setter, src/tts_transformer.h:403). */
+typedef struct qtts_generate_params {
+    const int32_t * text_tokens; int32_t n_tokens;
+    const int32_t * ref_text_tokens; int32_t n_ref_text;
+    const int32_t * ref_codec_tokens; int32_t n_ref_frames;   /* [n_ref_frames x 16] */
+    const float * speaker_embd;                                /* [hidden] or NULL */
+    int32_t max_len;
+    int32_t language_id;
+    float repetition_penalty;
+    float temperature;
+    int32_t top_k;
+    const int32_t * instruct_tokens; int32_t n_instruct;
+    float eos_bias;
+    int32_t target_frames;
+    int32_t rep_loop_detect;
+    uint64_t seed;
+} qtts_generate_params;
+
+/* FrameCallback (src/tts_transformer.h:291): return 0 to stop generation. */
+typedef int32_t (*qtts_frame_callback)(const int32_t * frame_codes, int32_t n_codebooks,
+                                       int32_t frame_index, void * user_data);
+
+/* Device-side timings of the last call (CUDA events on the engine stream). */
+typedef struct qtts_timing {
+    float prefill_ms;        /* forward_prefill of the last generate */
+    float frames_ms;         /* frame loop of the last generate / run_frames */
+    int32_t frames;          /* frames in frames_ms */
+    int32_t kernel_launches; /* engine kernels launched per frame */
+} qtts_timing;
+
+/* Per-kernel-class statistics of qtts_profile_frames (classes: 0 = GEMV,
+ * 1 = attention, 2 = sampling, 3 = other). */
+typedef struct qtts_kernel_stats {
+    int32_t launches;
+    float total_ms;
+    double bytes;            /* algorithmic bytes (weights + activations) */
+} qtts_kernel_stats;
+
+/* TTSTransformer::load_model (src/tts_transformer.h:204; src/tts_transformer.cpp:68-173).
+ * device < 0 selects QWEN3_TTS_DEVICE or 0.  Returns NULL on failure;
+ * qtts_create_error() then holds the message (per thread). */
+qtts_engine * qtts_create(const char * gguf_path, int32_t device);
+const char * qtts_create_error(void);
+/* TTSTransformer::unload_model + destructor (src/tts_transformer.cpp:21-51). */
+void qtts_destroy(qtts_engine * e);
+/* TTSTransformer::get_error (src/tts_transformer.h:328). */
+const char * qtts_get_error(const qtts_engine * e);
+/* TTSTransformer::get_config (src/tts_transformer.h:326). */
+int32_t qtts_get_config(const qtts_engine * e, qtts_config * out);
+/* TTSTransformer::set_n_threads (src/tts_transformer.h:208): accepted, no effect on a GPU engine. */
+void qtts_set_n_threads(qtts_engine * e, int32_t n_threads);
+
+/* KV caches (src/tts_transformer.h:230-239; src/tts_transformer.cpp:731-837). */
+int32_t qtts_init_kv_cache(qtts_engine * e, int32_t n_ctx);
+void qtts_clear_kv_cache(qtts_engine * e);
+int32_t qtts_init_code_pred_kv_cache(qtts_engine * e, int32_t n_ctx);
+void qtts_clear_code_pred_kv_cache(qtts_engine * e);
+
+/* TTSTransformer::forward_prefill (src/tts_transformer.h:250; .cpp:2217-2347).
+ * hidden_out: [n_tokens x hidden] post-norm rows or NULL; logits_out: [codec_vocab]
+ * of the last row or NULL. */
+int32_t qtts_forward_prefill(qtts_engine * e, const float * prefill_embd, int32_t n_tokens, int32_t n_past,
+                             float * hidden_out, float * logits_out);
+/* TTSTransformer::forward_step (src/tts_transformer.h:261; .cpp:2379-2509). */
+int32_t qtts_forward_step(qtts_engine * e, const float * step_embd, int32_t n_past,
+                          float * logits_out, float * hidden_out);
+/* TTSTransformer::forward_text (src/tts_transformer.h:246; .cpp:2349-2377). */
+int32_t qtts_forward_text(qtts_engine * e, const int32_t * text_tokens, int32_t n_tokens,
+                          const float * speaker_embd, int32_t n_past, float * hidden_out);
+/* TTSTransformer::forward_codec (src/tts_transformer.h:258; .cpp:2511-2521). */
+int32_t qtts_forward_codec(qtts_engine * e, int32_t codec_token, int32_t n_past, float * logits_out);
+/* TTSTransformer::get_hidden_states (src/tts_transformer.h:266; .cpp:2523-2529). */
+int32_t qtts_get_hidden_states(const qtts_engine * e, float * hidden_out);
+/* TTSTransformer::predict_codes (legacy, src/tts_transformer.h:272; .cpp:2531-2581).
+ * logits_out: [(n_codebooks-1) x code_pred_vocab]. */
+int32_t qtts_predict_codes(qtts_engine * e, const float * hidden, const int32_t * prev_codes, float * logits_out);
+/* TTSTransformer::predict_codes_autoregressive (src/tts_transformer.h:279; .cpp:2711-2976).
+ * codes_out: [n_codebooks-1]. */
+int32_t qtts_predict_codes_autoregressive(qtts_engine * e, const float * hidden, int32_t codebook_0_token,
+                                          float temperature, int32_t top_k, int32_t * codes_out);
+
+/* project_text_tokens (src/tts_transformer.cpp:963-1028): out [n x hidden]. */
+int32_t qtts_project_text(qtts_engine * e, const int32_t * tokens, int32_t n, float * out);
+/* lookup_embedding_rows (src/tts_transformer.cpp:839-961).  table: 0 = talker
+ * codec_embd, 1..n_codebooks-1 = code_pred.codec_embd[table-1], -1 = text_embd. */
+int32_t qtts_lookup_embedding_rows(qtts_engine * e, int32_t table, const int32_t * ids, int32_t n, float * out);
+
+/* TTSTransformer::generate / generate_icl (src/tts_transformer.h:293-324;
+ * .cpp:3007-3656).  codes_out: [max_len x n_codebooks]; *n_frames_out frames
+ * are valid.  on_frame may be NULL. */
+int32_t qtts_generate(qtts_engine * e, const qtts_generate_params * p, qtts_frame_callback on_frame,
+                      void * user_data, int32_t * codes_out, int32_t * n_frames_out);
+
+/* Streaming pieces of qtts_generate: begin builds and runs the prefill and arms
+ * the device frame state; run_frames then advances up to n frames on the device
+ * (stopping at EOS) and copies their codes to codes_out ([n x n_codebooks]).
+ * Returns the number of frames produced, -1 on error. */
+int32_t qtts_generate_begin(qtts_engine * e, const qtts_generate_params * p);
+int32_t qtts_run_frames(qtts_engine * e, int32_t n, int32_t * codes_out);
+
+/* Sampling seed of the Philox stream (sampled decoding is reproducible). */
+void qtts_set_seed(qtts_engine * e, uint64_t seed);
+/* Record the raw codebook-0 logits ([cap x codec_vocab]) and code-predictor
+ * logits ([cap x (n_codebooks-1) x code_pred_vocab]) of each generated frame into
+ * host buffers (either may be NULL; cap 0 disables). */
+int32_t qtts_set_debug_logits(qtts_engine * e, float * talker_logits, float * cp_logits, int32_t cap_frames);
+/* TTSTransformer::set_attn_dump (src/tts_transformer.h:224): keep the
+ * post-softmax row of talker layer `layer` for every generated frame. */
+int32_t qtts_set_attn_dump(qtts_engine * e, int32_t enabled, int32_t layer);
+/* Number of attention rows kept and row r ([n_kv x n_head] values). */
+int32_t qtts_attn_rows(const qtts_engine * e);
+int32_t qtts_attn_row(const qtts_engine * e, int32_t r, float * out, int32_t cap);
+int32_t qtts_get_timing(const qtts_engine * e, qtts_timing * out);
+/* Advance up to n frames of the active generation kernel by kernel (no CUDA
+ * graph) with CUDA events around each launch; fills stats[0..n_classes).
+ * Returns frames produced or -1.  For measurement only. */
+int32_t qtts_profile_frames(qtts_engine * e, int32_t n, qtts_kernel_stats * stats, int32_t n_classes);
+
+/* ---- Kernel-level entry points (one engine kernel on host data) ----------
+ * ggml_mul_mat (+ optional ggml_rms_norm prologue) as the engine computes it,
+ * src/tts_transformer.cpp:1656-1661: y[nv][rows] = W[rows][cols] . x[nv][cols].
+ * wtype 1 = F16 (w: [rows][cols] halves), 8 = Q8_0 (w: GGUF blocks
+ * [rows][cols/32] x 34 bytes).  act_f32 keeps x unrounded (the F32-cast
+ * ffn_down of :1746-1748).  block_dots, if not NULL, receives the per-block
+ * int32 Q8_0 dot products [nv][rows][cols/32]. */
+int32_t qtts_op_gemv(int32_t device, int32_t wtype, const void * w, int32_t rows, int32_t cols, const float * x,
+                     int32_t nv, const float * norm_gain, float eps, int32_t act_f32, float * y, int32_t * block_dots);
+/* One sampling decision (src/tts_transformer.cpp:3108-3184 for cb 0, :2750-2788
+ * for cb >= 1).  presence: optional [V] 0/1 set of earlier codebook-0 tokens.
+ * Returns the token (eos_id when codebook 0 samples EOS), -1 on error. */
+int32_t qtts_op_sample(int32_t device, const float * logits, int32_t V, int32_t cb, float temperature, int32_t top_k,
+                       float rep_penalty, const int32_t * presence, float eos_bias, int32_t target_frames,
+                       int32_t frame, int32_t eos_id, int32_t suppress_start, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN3TTS_B200_H */

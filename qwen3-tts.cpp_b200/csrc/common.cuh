@@ -1,0 +1,121 @@
+// common.cuh — device helpers shared by the frame-loop kernels (sm_100a).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define QTTS_HD 128          // head_dim: fixed for the Qwen3 talker and code predictor
+#define QTTS_MAX_CB 16       // codebooks per frame
+#define QTTS_WARPS 16        // warps per GEMV CTA
+#define QTTS_MAX_NV 8        // activation rows per weight pass
+
+namespace qtts {
+
+enum WType : int { W_F32 = 0, W_F16 = 1, W_Q8_0 = 8 };
+
+// ggml layout matrix: rows x cols, row-major (ne0 = cols contiguous).
+struct DMat {
+    int type = W_F16;
+    int rows = 0, cols = 0;
+    const void * w = nullptr;        // F16 [rows][cols] or int8 quants [rows][cols]
+    const __half * d = nullptr;      // Q8_0 block scales [rows][cols/32]
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Block-wide double sum; `red` is >= 32 doubles of shared memory.  All threads
+// receive the total.
+__device__ __forceinline__ double block_sum_d(double v, double * red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_sum_d(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double t = lane < nw ? red[lane] : 0.0;
+    t = warp_sum_d(t);
+    return t;
+}
+__device__ __forceinline__ float block_max(float v, float * red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = lane < nw ? red[lane] : -INFINITY;
+    return warp_max(t);
+}
+
+// Streaming 16-byte load that bypasses L1 (weights are read once per pass).
+__device__ __forceinline__ uint4 ld_stream(const void * p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
+
+// 8 F16 weights (one uint4) dotted with 8 F32 activations, F32 accumulate
+// (each product of an F16 weight with an F16-representable activation is exact).
+__device__ __forceinline__ float dot8(const uint4 & w, const float * x, float acc) {
+    const __half2 * h = reinterpret_cast<const __half2 *>(&w);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float2 f = __half22float2(h[k]);
+        acc = fmaf(f.x, x[2 * k], acc);
+        acc = fmaf(f.y, x[2 * k + 1], acc);
+    }
+    return acc;
+}
+
+// SiLU as ggml's scalar definition: x / (1 + exp(-x)).
+__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+// Philox4x32-10 (Salmon et al., SC'11).  Same function as the CPU oracle.
+__device__ __forceinline__ void philox(uint32_t c[4], uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t lo0 = 0xD2511F53u * c[0], hi0 = __umulhi(0xD2511F53u, c[0]);
+        const uint32_t lo1 = 0xCD9E8D57u * c[2], hi1 = __umulhi(0xCD9E8D57u, c[2]);
+        const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+        c[0] = n0; c[1] = lo1; c[2] = n2; c[3] = lo0;
+        k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
+    }
+}
+__device__ __forceinline__ double uniform01(uint64_t seed, uint32_t frame, uint32_t cb) {
+    uint32_t c[4] = {frame, cb, 0x51a3u, 0u};
+    philox(c, (uint32_t) seed, (uint32_t)(seed >> 32));
+    const uint64_t bits = ((uint64_t) c[0] << 32) | c[1];
+    return (double)(bits >> 11) * (1.0 / 9007199254740992.0);
+}
+
+// Order-preserving map float -> uint32 (ascending float = ascending key).
+__device__ __forceinline__ uint32_t f2key(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    return __uint_as_float(u);
+}
+
+}  // namespace qtts

@@ -1,0 +1,1432 @@
+// engine.cu — B200 engine for the TTSTransformer decode path, behind the C ABI
+// of include/qwen3tts_b200.h.
+//
+// Layout in HBM (one engine per GPU):
+//   * weights: one allocation.  Per layer the Q, K and V matrices are fused into
+//     one [NH*D + 2*NKV*D, H] matrix; F16 matrices keep the GGUF row-major
+//     layout; Q8_0 matrices are split at load time into an int8 quant plane
+//     [rows][cols] and an F16 scale plane [rows][cols/32] (same 34 bytes per 32
+//     weights, 16-byte aligned rows for vector loads).
+//   * KV caches: F16 [layer][pos][kv_head][128] (the reference's
+//     [head_dim, n_kv_heads, n_ctx] ggml tensors, src/tts_transformer.cpp:757-770).
+//   * RoPE tables: (cos, sin) per position and pair index, computed once with the
+//     ggml_rope_cache_init recurrence.
+//   * frame state (positions, codes, EOS flag, codebook-0 presence set) lives in
+//     device memory, so a single captured CUDA graph replays every frame: talker
+//     cb0 sampling, the 2-token code-predictor prefill, 14 code-predictor steps
+//     with on-device sampling, the next-step embedding sum and the 28-layer talker
+//     step, with no host round trip inside a frame.
+#include "../../include/qwen3tts_b200.h"
+#include "gguf.hpp"
+#include "kernels.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace qtts {
+
+#define QCHECK(call)                                                                   \
+    do {                                                                               \
+        cudaError_t e_ = (call);                                                       \
+        if (e_ != cudaSuccess) {                                                       \
+            err = std::string(#call) + ": " + cudaGetErrorString(e_);                  \
+            return false;                                                              \
+        }                                                                              \
+    } while (0)
+
+enum KernelClass { KC_GEMV = 0, KC_ATTN = 1, KC_SAMPLE = 2, KC_OTHER = 3, KC_N = 4 };
+
+struct LayerW {
+    DMat qkv, o, gate, up, down;
+    const float * attn_norm = nullptr, * ffn_norm = nullptr, * q_norm = nullptr, * k_norm = nullptr;
+};
+
+struct GenSession {
+    bool active = false;
+    int max_len = 0, prefill_len = 0, trailing_len = 0, produced = 0;
+    bool done = false;
+};
+
+struct Engine {
+    int dev = 0, n_sm = 148;
+    cudaStream_t stream = nullptr;
+    qtts_config cfg{};
+    std::string err;
+
+    // weights
+    uint8_t * wbuf = nullptr;
+    size_t wbytes = 0, wused = 0;
+    std::vector<LayerW> L, CPL;
+    const __half * text_embd = nullptr, * codec_embd = nullptr;
+    std::vector<const __half *> cp_embd;
+    const __half ** d_cp_embd = nullptr;
+    DMat codec_head, fc1, fc2;
+    std::vector<DMat> cp_head;
+    const float * fc1_b = nullptr, * fc2_b = nullptr, * out_norm = nullptr, * cp_out_norm = nullptr;
+
+    // rope tables and caches
+    float2 * rope_t = nullptr, * rope_cp = nullptr;
+    __half * kc = nullptr, * vc = nullptr;
+    int n_ctx = 0, n_used = 0;
+    __half * cpk = nullptr, * cpv = nullptr;
+    int cp_ctx = 0;
+
+    // activations (rows <= QTTS_MAX_NV)
+    float * x = nullptr, * xcp = nullptr, * qkv = nullptr, * att = nullptr, * hbuf = nullptr;
+    float * logits = nullptr, * cp_logits = nullptr, * hidden = nullptr, * hid_rows = nullptr;
+    float * tmp_a = nullptr, * tmp_b = nullptr;
+    int * d_ids = nullptr;
+    int ids_cap = 0;
+
+    // frame state
+    DevState * st = nullptr;
+    SampleParams * sp = nullptr;
+    int * d_codes = nullptr;
+    int codes_cap = 0;
+    float * trailing = nullptr;
+    int trailing_cap = 0;
+    float * pad = nullptr;
+    float * dbg_t = nullptr, * dbg_cp = nullptr;
+    int dbg_cap = 0;
+    float * h_dbg_t = nullptr, * h_dbg_cp = nullptr;
+    int h_dbg_cap = 0;
+    float * d_attn = nullptr;
+    size_t attn_cap = 0;
+    bool attn_dump = false;
+    int attn_layer = 27;
+    std::vector<std::vector<float>> attn_rows;
+
+    cudaGraphExec_t graph = nullptr;
+    bool graph_ok = false;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    std::vector<float> last_hidden;
+    uint64_t seed = 0;
+    uint32_t api_calls = 0;
+    qtts_timing timing{};
+    int launches = 0;
+    int launches_per_frame = 0;
+    GenSession sess;
+    // eager profiling: CUDA events around every launch, accumulated per kernel class
+    bool profiling = false;
+    struct ProfEv { int cls; double bytes; cudaEvent_t a, b; };
+    std::vector<ProfEv> prof_evs;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_used = 0;
+    cudaEvent_t pool_event() {
+        if (ev_used == ev_pool.size()) { cudaEvent_t e; cudaEventCreate(&e); ev_pool.push_back(e); }
+        return ev_pool[ev_used++];
+    }
+    void prof_begin(int cls, double bytes) {
+        if (!profiling) return;
+        ProfEv p{cls, bytes, pool_event(), pool_event()};
+        cudaEventRecord(p.a, stream);
+        prof_evs.push_back(p);
+    }
+    void prof_end() { if (profiling) cudaEventRecord(prof_evs.back().b, stream); }
+
+    ~Engine() {
+        for (auto e : ev_pool) cudaEventDestroy(e);
+        release();
+    }
+
+    int QD() const { return cfg.n_attention_heads * QTTS_HD; }
+    int KD() const { return cfg.n_key_value_heads * QTTS_HD; }
+    int QKVD() const { return QD() + 2 * KD(); }
+
+    void release() {
+        if (dev >= 0) cudaSetDevice(dev);
+        if (graph) { cudaGraphExecDestroy(graph); graph = nullptr; }
+        void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
+                         cp_logits, hidden, hid_rows, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
+                         dbg_t, dbg_cp, d_attn};
+        for (void * p : ptrs) if (p) cudaFree(p);
+        wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
+        x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = hid_rows = tmp_a = tmp_b = nullptr;
+        d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
+        dbg_t = dbg_cp = nullptr; d_attn = nullptr;
+        if (ev0) cudaEventDestroy(ev0);
+        if (ev1) cudaEventDestroy(ev1);
+        ev0 = ev1 = nullptr;
+        if (stream) cudaStreamDestroy(stream);
+        stream = nullptr;
+    }
+
+    // ------------------------------------------------------------ loading
+    bool load(const char * path, int device);
+    bool upload_weights(const GgufFile & g);
+    bool alloc_activations();
+    bool init_kv(int ctx);
+    bool init_cp_kv(int ctx);
+    void build_rope(std::vector<float2> & t, int n_pos, float base);
+
+    // ------------------------------------------------------------ launches
+    bool gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
+              float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn, const int * done);
+    bool layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, int ctx, const float2 * rope, float * X,
+                int M, const int * pos_ptr, int pos_static, bool f32_mode, const int * done, int ffn,
+                float * dump = nullptr, int dump_layer = -1);
+    bool enqueue_cp(bool sample_cb0);
+    bool enqueue_talker_step(const int * pos_ptr, int pos_static, const int * done, bool with_dump);
+    bool enqueue_frame();
+    bool capture_graph();
+    bool sync(const char * what);
+
+    // ------------------------------------------------------------ API pieces
+    bool prefill(const float * rows_host, int n, int n_past, float * hidden_out, float * logits_out);
+    bool project_text(const int32_t * toks, int n, std::vector<float> & out);
+    bool lookup(int table, const int32_t * ids, int n, std::vector<float> & out);
+    bool build_prefill(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
+                       std::vector<float> & padv);
+    bool build_prefill_icl(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
+                           std::vector<float> & padv);
+    int begin(const qtts_generate_params * p);
+    int run_frames(int n, int32_t * codes_out);
+};
+
+static thread_local std::string g_create_error;
+
+void Engine::build_rope(std::vector<float2> & t, int n_pos, float base) {
+    // ggml_rope_cache_init (ext_factor 0, freq_scale 1, attn_factor 1): theta for
+    // pair i is pos * s^i accumulated by repeated F32 multiplication.
+    const int half = QTTS_HD / 2;
+    t.resize((size_t) n_pos * half);
+    const float theta_scale = powf(base, -2.0f / (float) QTTS_HD);
+    for (int p = 0; p < n_pos; ++p) {
+        float theta = (float) p;
+        for (int i = 0; i < half; ++i) {
+            t[(size_t) p * half + i] = make_float2(cosf(theta), sinf(theta));
+            theta *= theta_scale;
+        }
+    }
+}
+
+bool Engine::load(const char * path, int device) {
+    if (device < 0) {
+        const char * env = getenv("QWEN3_TTS_DEVICE");
+        device = env && *env ? atoi(env) : 0;
+    }
+    dev = device;
+    QCHECK(cudaSetDevice(dev));
+    QCHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    QCHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    QCHECK(cudaEventCreate(&ev0));
+    QCHECK(cudaEventCreate(&ev1));
+
+    GgufFile g;
+    if (!g.open(path, err)) return false;
+    // parse_config (src/tts_transformer.cpp:228-377), same aliases and defaults
+    qtts_config & c = cfg;
+    c.text_vocab_size = (int) g.get_int({"qwen3-tts.text.vocab_size", "qwen3-tts.text_vocab_size"}, 151936);
+    c.text_embd_dim = (int) g.get_int({"qwen3-tts.text.embedding_dim", "qwen3-tts.text_hidden_size"}, 2048);
+    c.hidden_size = (int) g.get_int({"qwen3-tts.talker.embedding_length", "qwen3-tts.embedding_length"}, 1024);
+    c.n_layers = (int) g.get_int({"qwen3-tts.talker.block_count", "qwen3-tts.block_count"}, 28);
+    c.n_attention_heads = (int) g.get_int({"qwen3-tts.talker.attention.head_count", "qwen3-tts.attention.head_count"}, 16);
+    c.n_key_value_heads = (int) g.get_int({"qwen3-tts.talker.attention.head_count_kv", "qwen3-tts.attention.head_count_kv"}, 8);
+    c.intermediate_size = (int) g.get_int({"qwen3-tts.talker.feed_forward_length", "qwen3-tts.feed_forward_length"}, 3072);
+    c.head_dim = (int) g.get_int({"qwen3-tts.talker.attention.key_length", "qwen3-tts.attention.key_length"}, 128);
+    c.rms_norm_eps = (float) g.get_float({"qwen3-tts.talker.attention.layer_norm_rms_epsilon", "qwen3-tts.attention.layer_norm_rms_epsilon"}, 1e-6);
+    c.rope_theta = (float) g.get_float({"qwen3-tts.talker.rope.freq_base", "qwen3-tts.rope.freq_base"}, 1000000.0);
+    c.mrope_section[0] = 24; c.mrope_section[1] = 20; c.mrope_section[2] = 20;
+    c.codec_vocab_size = (int) g.get_int({"qwen3-tts.talker.codec_vocab_size", "qwen3-tts.vocab_size"}, 3072);
+    c.n_codebooks = (int) g.get_int({"qwen3-tts.talker.num_codebooks", "qwen3-tts.num_code_groups"}, 16);
+    c.code_pred_layers = (int) g.get_int({"qwen3-tts.code_pred.layer_count", "qwen3-tts.code_predictor.layer_count"}, 5);
+    c.code_pred_vocab_size = (int) g.get_int({"qwen3-tts.code_pred.vocab_size", "qwen3-tts.code_predictor.vocab_size"}, 2048);
+    c.code_pred_hidden_size = (int) g.get_int({"qwen3-tts.code_pred.embedding_length", "qwen3-tts.code_predictor.embedding_length"}, 1024);
+    c.code_pred_intermediate_size = (int) g.get_int({"qwen3-tts.code_pred.feed_forward_length", "qwen3-tts.code_predictor.feed_forward_length"}, 3072);
+    c.code_pred_rope_theta = (float) g.get_float({"qwen3-tts.code_pred.rope.freq_base", "qwen3-tts.code_predictor.rope.freq_base"}, c.rope_theta);
+    c.codec_pad_id = (int) g.get_int({"qwen3-tts.codec.pad_id"}, 2148);
+    c.codec_bos_id = (int) g.get_int({"qwen3-tts.codec.bos_id"}, 2149);
+    c.codec_eos_id = (int) g.get_int({"qwen3-tts.codec.eos_id", "qwen3-tts.codec.eos_token_id"}, 2150);
+    c.tts_bos_token_id = (int) g.get_int({"qwen3-tts.tts_bos_token_id", "qwen3-tts.tts.bos_token_id", "qwen3-tts.tts.bos_id"}, 151672);
+    c.tts_eos_token_id = (int) g.get_int({"qwen3-tts.tts_eos_token_id", "qwen3-tts.tts.eos_token_id", "qwen3-tts.tts.eos_id"}, 151673);
+    c.tts_pad_token_id = (int) g.get_int({"qwen3-tts.tts_pad_token_id", "qwen3-tts.tts.pad_token_id", "qwen3-tts.tts.pad_id"}, 151671);
+    c.codec_think_id = (int) g.get_int({"qwen3-tts.codec.think_id", "qwen3-tts.codec_think_id"}, 2154);
+    c.codec_nothink_id = (int) g.get_int({"qwen3-tts.codec.nothink_id", "qwen3-tts.codec_nothink_id"}, 2155);
+    c.codec_think_bos_id = (int) g.get_int({"qwen3-tts.codec.think_bos_id", "qwen3-tts.codec_think_bos_id"}, 2156);
+    c.codec_think_eos_id = (int) g.get_int({"qwen3-tts.codec.think_eos_id", "qwen3-tts.codec_think_eos_id"}, 2157);
+    c.english_language_id = (int) g.get_int({"qwen3-tts.language.english_id", "qwen3-tts.codec.language.english_id", "qwen3-tts.language_id"}, 2050);
+
+    if (c.head_dim != QTTS_HD) { err = "head_dim must be 128"; return false; }
+    if (c.code_pred_hidden_size != c.hidden_size || g.find("code_pred.mtp_proj.weight")) {
+        err = "code predictor width differs from the talker (mtp_proj layout) - not supported";
+        return false;
+    }
+    if (c.n_codebooks < 2 || c.n_codebooks > QTTS_MAX_CB) { err = "n_codebooks out of range"; return false; }
+    if (c.codec_vocab_size > SAMPLE_THREADS * SAMPLE_PER_T || c.code_pred_vocab_size > SAMPLE_THREADS * SAMPLE_PER_T) {
+        err = "vocabulary larger than 4096 is not supported"; return false;
+    }
+    if (c.n_attention_heads % c.n_key_value_heads || c.n_attention_heads / c.n_key_value_heads > ATT_MAX_GROUP ||
+        c.n_attention_heads + c.n_key_value_heads > 32) {
+        err = "unsupported head configuration"; return false;
+    }
+    if (c.hidden_size % 256 || c.intermediate_size % 32 || c.code_pred_intermediate_size % 32 || c.text_embd_dim % 32) {
+        err = "hidden/ffn/text widths must be multiples of 256/32/32"; return false;
+    }
+    if (!upload_weights(g)) return false;
+    if (!alloc_activations()) return false;
+    if (!init_cp_kv(16)) return false;
+    return true;
+}
+
+bool Engine::upload_weights(const GgufFile & g) {
+    const qtts_config & c = cfg;
+    struct Need { std::string name; int rows, cols; bool matrix; };
+    auto mat_bytes = [](const GgufTensor * t) -> size_t {
+        const size_t n = (size_t) t->ne[0] * t->ne[1];
+        return t->type == GGML_Q8_0 ? n + (n / 32) * 2 + 512 : t->nbytes + 256;
+    };
+    auto get = [&](const std::string & name, int ne0, int ne1, const GgufTensor *& out) -> bool {
+        out = g.find(name);
+        if (!out) { err = "missing tensor " + name; return false; }
+        if (out->ne[0] != ne0 || out->ne[1] != ne1) { err = "unexpected shape for " + name; return false; }
+        if (ne1 > 1 && out->type != GGML_F16 && out->type != GGML_Q8_0) {
+            err = "unsupported weight type for " + name + " (F16 or Q8_0 expected)"; return false;
+        }
+        if (ne1 == 1 && out->type != GGML_F32) { err = "1-D tensor " + name + " must be F32"; return false; }
+        return true;
+    };
+    // Pass 1: size.
+    const int H = c.hidden_size, TD = c.text_embd_dim;
+    std::vector<std::pair<std::string, std::pair<int, int>>> all;
+    auto add = [&](const std::string & n, int ne0, int ne1) { all.push_back({n, {ne0, ne1}}); };
+    add("talker.text_embd.weight", TD, c.text_vocab_size);
+    add("talker.text_proj.fc1.weight", TD, TD);
+    add("talker.text_proj.fc1.bias", TD, 1);
+    add("talker.text_proj.fc2.weight", TD, H);
+    add("talker.text_proj.fc2.bias", H, 1);
+    add("talker.codec_embd.weight", H, c.codec_vocab_size);
+    add("talker.codec_head.weight", H, c.codec_vocab_size);
+    add("talker.output_norm.weight", H, 1);
+    add("code_pred.output_norm.weight", H, 1);
+    auto add_layers = [&](const char * pfx, int n, int ffn) {
+        for (int i = 0; i < n; ++i) {
+            std::string p = std::string(pfx) + std::to_string(i) + ".";
+            add(p + "attn_norm.weight", H, 1);
+            add(p + "attn_q.weight", H, QD());
+            add(p + "attn_k.weight", H, KD());
+            add(p + "attn_v.weight", H, KD());
+            add(p + "attn_output.weight", QD(), H);
+            add(p + "attn_q_norm.weight", QTTS_HD, 1);
+            add(p + "attn_k_norm.weight", QTTS_HD, 1);
+            add(p + "ffn_norm.weight", H, 1);
+            add(p + "ffn_gate.weight", H, ffn);
+            add(p + "ffn_up.weight", H, ffn);
+            add(p + "ffn_down.weight", ffn, H);
+        }
+    };
+    add_layers("talker.blk.", c.n_layers, c.intermediate_size);
+    add_layers("code_pred.blk.", c.code_pred_layers, c.code_pred_intermediate_size);
+    for (int gi = 0; gi < c.n_codebooks - 1; ++gi) {
+        add("code_pred.codec_embd." + std::to_string(gi) + ".weight", H, c.code_pred_vocab_size);
+        add("code_pred.lm_head." + std::to_string(gi) + ".weight", H, c.code_pred_vocab_size);
+    }
+    size_t total = 0;
+    for (auto & n : all) {
+        const GgufTensor * t;
+        if (!get(n.first, n.second.first, n.second.second, t)) return false;
+        total += mat_bytes(t);
+    }
+    for (auto & n : all)
+        if (n.first.find("embd") != std::string::npos && g.find(n.first)->type != GGML_F16) {
+            err = "embedding " + n.first + " must be F16"; return false;
+        }
+    QCHECK(cudaMalloc(&wbuf, total));
+    wbytes = total; wused = 0;
+
+    std::vector<uint8_t> stage;
+    auto alloc = [&](size_t bytes) -> uint8_t * {
+        uint8_t * p = wbuf + wused;
+        wused += (bytes + 255) & ~(size_t) 255;
+        return p;
+    };
+    auto up_raw = [&](const GgufTensor * t) -> const void * {
+        uint8_t * p = alloc(t->nbytes);
+        if (cudaMemcpy(p, t->data, t->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+        return p;
+    };
+    // Matrix upload; several GGUF tensors may be stacked along rows (QKV fusion).
+    auto up_mat = [&](std::initializer_list<const GgufTensor *> parts, DMat & m) -> bool {
+        const GgufTensor * t0 = *parts.begin();
+        m.type = t0->type == GGML_Q8_0 ? W_Q8_0 : W_F16;
+        m.cols = (int) t0->ne[0];
+        m.rows = 0;
+        for (auto * t : parts) {
+            if (t->type != t0->type || t->ne[0] != t0->ne[0]) { err = "mixed types in fused matrix " + t->name; return false; }
+            m.rows += (int) t->ne[1];
+        }
+        if (m.type == W_F16) {
+            uint8_t * p = alloc((size_t) m.rows * m.cols * 2);
+            size_t off = 0;
+            for (auto * t : parts) {
+                if (cudaMemcpy(p + off, t->data, t->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) { err = "upload failed"; return false; }
+                off += t->nbytes;
+            }
+            m.w = p; m.d = nullptr;
+        } else {
+            const int nb = m.cols / 32;
+            uint8_t * q = alloc((size_t) m.rows * m.cols);
+            uint8_t * d = alloc((size_t) m.rows * nb * 2);
+            size_t roff = 0;
+            for (auto * t : parts) {
+                const size_t rows = (size_t) t->ne[1];
+                stage.resize(rows * m.cols + rows * nb * 2);
+                uint8_t * sq = stage.data();
+                uint8_t * sd = stage.data() + rows * m.cols;
+                for (size_t r = 0; r < rows; ++r)
+                    for (int b = 0; b < nb; ++b) {
+                        const uint8_t * blk = t->data + (r * nb + b) * 34;
+                        memcpy(sd + (r * nb + b) * 2, blk, 2);
+                        memcpy(sq + r * m.cols + (size_t) b * 32, blk + 2, 32);
+                    }
+                if (cudaMemcpy(q + roff * m.cols, sq, rows * m.cols, cudaMemcpyHostToDevice) != cudaSuccess ||
+                    cudaMemcpy(d + roff * nb * 2, sd, rows * nb * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+                    err = "upload failed"; return false;
+                }
+                roff += rows;
+            }
+            m.w = q; m.d = reinterpret_cast<const __half *>(d);
+        }
+        return true;
+    };
+    auto T = [&](const std::string & n) { return g.find(n); };
+    text_embd = (const __half *) up_raw(T("talker.text_embd.weight"));
+    codec_embd = (const __half *) up_raw(T("talker.codec_embd.weight"));
+    if (!up_mat({T("talker.text_proj.fc1.weight")}, fc1) || !up_mat({T("talker.text_proj.fc2.weight")}, fc2) ||
+        !up_mat({T("talker.codec_head.weight")}, codec_head))
+        return false;
+    fc1_b = (const float *) up_raw(T("talker.text_proj.fc1.bias"));
+    fc2_b = (const float *) up_raw(T("talker.text_proj.fc2.bias"));
+    out_norm = (const float *) up_raw(T("talker.output_norm.weight"));
+    cp_out_norm = (const float *) up_raw(T("code_pred.output_norm.weight"));
+    auto load_layers = [&](const char * pfx, int n, std::vector<LayerW> & out) -> bool {
+        out.resize(n);
+        for (int i = 0; i < n; ++i) {
+            std::string p = std::string(pfx) + std::to_string(i) + ".";
+            LayerW & l = out[i];
+            if (!up_mat({T(p + "attn_q.weight"), T(p + "attn_k.weight"), T(p + "attn_v.weight")}, l.qkv) ||
+                !up_mat({T(p + "attn_output.weight")}, l.o) || !up_mat({T(p + "ffn_gate.weight")}, l.gate) ||
+                !up_mat({T(p + "ffn_up.weight")}, l.up) || !up_mat({T(p + "ffn_down.weight")}, l.down))
+                return false;
+            if (l.gate.type != l.up.type) { err = "gate/up types differ"; return false; }
+            l.attn_norm = (const float *) up_raw(T(p + "attn_norm.weight"));
+            l.ffn_norm = (const float *) up_raw(T(p + "ffn_norm.weight"));
+            l.q_norm = (const float *) up_raw(T(p + "attn_q_norm.weight"));
+            l.k_norm = (const float *) up_raw(T(p + "attn_k_norm.weight"));
+        }
+        return true;
+    };
+    if (!load_layers("talker.blk.", c.n_layers, L) || !load_layers("code_pred.blk.", c.code_pred_layers, CPL)) return false;
+    cp_embd.resize(c.n_codebooks - 1);
+    cp_head.resize(c.n_codebooks - 1);
+    for (int gi = 0; gi < c.n_codebooks - 1; ++gi) {
+        cp_embd[gi] = (const __half *) up_raw(T("code_pred.codec_embd." + std::to_string(gi) + ".weight"));
+        if (!up_mat({T("code_pred.lm_head." + std::to_string(gi) + ".weight")}, cp_head[gi])) return false;
+    }
+    cfg.weight_type = L[0].qkv.type;
+    QCHECK(cudaMalloc(&d_cp_embd, sizeof(void *) * cp_embd.size()));
+    QCHECK(cudaMemcpy(d_cp_embd, cp_embd.data(), sizeof(void *) * cp_embd.size(), cudaMemcpyHostToDevice));
+    if (wused > wbytes) { err = "weight arena overflow"; return false; }
+    return true;
+}
+
+bool Engine::alloc_activations() {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size, NV = QTTS_MAX_NV;
+    const int FF = std::max(c.intermediate_size, c.code_pred_intermediate_size);
+    QCHECK(cudaMalloc(&x, sizeof(float) * NV * H));
+    QCHECK(cudaMalloc(&xcp, sizeof(float) * 2 * H));
+    QCHECK(cudaMalloc(&qkv, sizeof(float) * NV * QKVD()));
+    QCHECK(cudaMalloc(&att, sizeof(float) * NV * QD()));
+    QCHECK(cudaMalloc(&hbuf, sizeof(float) * NV * std::max(FF, c.text_embd_dim)));
+    QCHECK(cudaMalloc(&logits, sizeof(float) * c.codec_vocab_size));
+    QCHECK(cudaMalloc(&cp_logits, sizeof(float) * c.code_pred_vocab_size * (c.n_codebooks - 1)));
+    QCHECK(cudaMalloc(&hidden, sizeof(float) * H));
+    QCHECK(cudaMalloc(&hid_rows, sizeof(float) * NV * H));
+    QCHECK(cudaMalloc(&tmp_a, sizeof(float) * NV * std::max(H, c.text_embd_dim)));
+    QCHECK(cudaMalloc(&tmp_b, sizeof(float) * NV * std::max(H, c.text_embd_dim)));
+    QCHECK(cudaMalloc(&st, sizeof(DevState)));
+    QCHECK(cudaMemset(st, 0, sizeof(DevState)));
+    QCHECK(cudaMalloc(&sp, sizeof(SampleParams)));
+    QCHECK(cudaMemset(sp, 0, sizeof(SampleParams)));
+    QCHECK(cudaMalloc(&pad, sizeof(float) * H));
+    ids_cap = 4096;
+    QCHECK(cudaMalloc(&d_ids, sizeof(int) * ids_cap));
+    // large dynamic shared memory for the GEMV instantiations
+    QCHECK(cudaFuncSetAttribute(k_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    QCHECK(cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    QCHECK(cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    return true;
+}
+
+bool Engine::init_kv(int ctx) {
+    if (ctx <= 0) { err = "n_ctx must be > 0"; return false; }
+    const qtts_config & c = cfg;
+    if (kc) { cudaFree(kc); kc = nullptr; }
+    if (vc) { cudaFree(vc); vc = nullptr; }
+    if (rope_t) { cudaFree(rope_t); rope_t = nullptr; }
+    const size_t per = (size_t) c.n_layers * ctx * c.n_key_value_heads * QTTS_HD;
+    QCHECK(cudaMalloc(&kc, per * sizeof(__half)));
+    QCHECK(cudaMalloc(&vc, per * sizeof(__half)));
+    std::vector<float2> t;
+    build_rope(t, ctx, c.rope_theta);
+    QCHECK(cudaMalloc(&rope_t, t.size() * sizeof(float2)));
+    QCHECK(cudaMemcpy(rope_t, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    const size_t smem = attn_smem_bytes(ctx, c.n_attention_heads / c.n_key_value_heads);
+    if (smem > 220 * 1024) { err = "context too long for the attention kernel"; return false; }
+    QCHECK(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) std::max<size_t>(smem, 48 * 1024)));
+    n_ctx = ctx;
+    n_used = 0;
+    graph_ok = false;
+    return true;
+}
+
+bool Engine::init_cp_kv(int ctx) {
+    const qtts_config & c = cfg;
+    if (ctx < 16) ctx = 16;
+    if (cpk) { cudaFree(cpk); cpk = nullptr; }
+    if (cpv) { cudaFree(cpv); cpv = nullptr; }
+    if (rope_cp) { cudaFree(rope_cp); rope_cp = nullptr; }
+    const size_t per = (size_t) c.code_pred_layers * ctx * c.n_key_value_heads * QTTS_HD;
+    QCHECK(cudaMalloc(&cpk, per * sizeof(__half)));
+    QCHECK(cudaMalloc(&cpv, per * sizeof(__half)));
+    std::vector<float2> t;
+    build_rope(t, ctx, c.code_pred_rope_theta);
+    QCHECK(cudaMalloc(&rope_cp, t.size() * sizeof(float2)));
+    QCHECK(cudaMemcpy(rope_cp, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    cp_ctx = ctx;
+    graph_ok = false;
+    return true;
+}
+
+bool Engine::sync(const char * what) {
+    cudaError_t e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { err = std::string(what) + ": " + cudaGetErrorString(e); return false; }
+    return true;
+}
+
+// ---------------------------------------------------------------- launches
+bool Engine::gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
+                  float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
+                  const int * done) {
+    GemvArgs a{};
+    a.A = A;
+    if (B) a.B = *B;
+    a.x = xin; a.ldx = ldx; a.nv = nv;
+    a.norm_g = norm; a.eps = cfg.rms_norm_eps; a.act = act;
+    a.y = y; a.ldy = ldy; a.resid = resid; a.ldr = ldr; a.epi = epi;
+    a.xn_out = xn_out; a.ldxn = ldxn; a.done = done;
+    int ncta = std::min(n_sm, A.rows);
+    const int rpc = (A.rows + ncta - 1) / ncta;
+    ncta = (A.rows + rpc - 1) / rpc;
+    const int nchunk = A.type == W_F16 ? A.cols / 8 : A.cols / 16;
+    int ks = (2 * QTTS_WARPS + rpc - 1) / rpc;
+    ks = std::max(1, std::min(ks, std::max(1, nchunk / 32)));
+    a.kslices = ks;
+    const int NVt = nv == 1 ? 1 : nv == 2 ? 2 : 8;
+    const size_t smem = gemv_smem_bytes(A.type, A.cols, NVt, rpc, ks);
+    if (nv > QTTS_MAX_NV || smem > 200 * 1024) { err = "gemv shape too large"; return false; }
+    const double wb = A.type == W_F16 ? (double) A.rows * A.cols * 2.0 : (double) A.rows * A.cols * 34.0 / 32.0;
+    prof_begin(KC_GEMV, wb * (B ? 2.0 : 1.0) + 4.0 * nv * ((double) A.cols + A.rows));
+    if (NVt == 1) k_gemv<1><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a);
+    else if (NVt == 2) k_gemv<2><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a);
+    else k_gemv<8><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a);
+    prof_end();
+    ++launches;
+    return true;
+}
+
+bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, int ctx, const float2 * rope, float * X,
+                    int M, const int * pos_ptr, int pos_static, bool f32_mode, const int * done, int ffn,
+                    float * dump, int dump_layer) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size, NH = c.n_attention_heads, NKV = c.n_key_value_heads;
+    const int G = NH / NKV;
+    const size_t layer_elems = (size_t) ctx * NKV * QTTS_HD;
+    const size_t att_smem = attn_smem_bytes(f32_mode ? M : ctx, G);
+    for (size_t il = 0; il < Ls.size(); ++il) {
+        LayerW & l = Ls[il];
+        if (!gemv(l.qkv, nullptr, X, H, M, l.attn_norm, ACT_F16, qkv, QKVD(), nullptr, 0, EPI_STORE, nullptr, 0, done))
+            return false;
+        QkArgs qa{};
+        qa.qkv = qkv; qa.ldq = QKVD(); qa.n_heads = NH; qa.n_kv_heads = NKV;
+        qa.q_norm = l.q_norm; qa.k_norm = l.k_norm; qa.eps = c.rms_norm_eps; qa.rope = rope;
+        qa.kc = kbase + il * layer_elems; qa.vc = vbase + il * layer_elems;
+        qa.pos_ptr = pos_ptr; qa.pos_static = pos_static; qa.keep_f32_k = f32_mode ? 1 : 0; qa.done = done;
+        prof_begin(KC_OTHER, 0.0);
+        k_qk_rope_store<<<M, 32 * (NH + NKV), 0, stream>>>(qa);
+        prof_end();
+        ++launches;
+        AttnArgs aa{};
+        aa.q = qkv; aa.ldq = QKVD(); aa.kc = qa.kc; aa.vc = qa.vc;
+        aa.kf = qkv + QD(); aa.vf = qkv + QD() + KD(); aa.ldkv = QKVD(); aa.f32_mode = f32_mode ? 1 : 0;
+        aa.n_heads = NH; aa.n_kv_heads = NKV; aa.pos_ptr = pos_ptr; aa.pos_static = pos_static;
+        aa.scale = 1.0f / sqrtf((float) QTTS_HD);
+        aa.out = att; aa.ldo = QD(); aa.done = done;
+        aa.dump = ((int) il == dump_layer) ? dump : nullptr;
+        aa.dump_stride = ctx; aa.st = st;
+        prof_begin(KC_ATTN, 0.0);
+        k_attention<<<dim3(NKV, M), ATT_THREADS, att_smem, stream>>>(aa);
+        prof_end();
+        ++launches;
+        if (!gemv(l.o, nullptr, att, QD(), M, nullptr, ACT_F16, X, H, X, H, EPI_RESID, nullptr, 0, done)) return false;
+        if (!gemv(l.gate, &l.up, X, H, M, l.ffn_norm, ACT_F16, hbuf, ffn, nullptr, 0, EPI_SWIGLU, nullptr, 0, done))
+            return false;
+        // ffn_down: F16 weights are cast to F32 by the reference (F32 x F32 mul_mat)
+        if (!gemv(l.down, nullptr, hbuf, ffn, M, nullptr, ACT_F32, X, H, X, H, EPI_RESID, nullptr, 0, done)) return false;
+    }
+    return true;
+}
+
+// Code predictor for the current frame state: 2-token prefill, head 0, then 14
+// single-token steps, each followed by on-device sampling into st->codes.
+bool Engine::enqueue_cp(bool sample_cb0) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size, V1 = c.code_pred_vocab_size, NG = c.n_codebooks - 1;
+    const int * done = &st->done;
+    if (sample_cb0) {
+        prof_begin(KC_SAMPLE, 0.0);
+        k_sample<<<1, SAMPLE_THREADS, 0, stream>>>(logits, c.codec_vocab_size, 0, st, sp, d_codes, codes_cap);
+        prof_end();
+        ++launches;
+    }
+    InputArgs ia{};
+    ia.H = H; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
+    ia.trailing = trailing; ia.pad = pad; ia.out = xcp; ia.st = st; ia.n_cb = c.n_codebooks;
+    ia.mode = IN_CP_PREFILL;
+    k_frame_inputs<<<1, 256, 0, stream>>>(ia);
+    ++launches;
+    if (!layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 2, nullptr, 0, true, done, c.code_pred_intermediate_size)) return false;
+    if (!gemv(cp_head[0], nullptr, xcp + H, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE, nullptr, 0, done))
+        return false;
+    prof_begin(KC_SAMPLE, 0.0);
+    k_sample<<<1, SAMPLE_THREADS, 0, stream>>>(cp_logits, V1, 1, st, sp, d_codes, codes_cap);
+    prof_end();
+    ++launches;
+    for (int gstep = 1; gstep < NG; ++gstep) {
+        ia.mode = IN_CP_STEP; ia.g = gstep;
+        k_frame_inputs<<<1, 256, 0, stream>>>(ia);
+        ++launches;
+        if (!layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 1, nullptr, gstep + 1, false, done, c.code_pred_intermediate_size))
+            return false;
+        if (!gemv(cp_head[gstep], nullptr, xcp, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE, nullptr, 0, done))
+            return false;
+        prof_begin(KC_SAMPLE, 0.0);
+        k_sample<<<1, SAMPLE_THREADS, 0, stream>>>(cp_logits, V1, gstep + 1, st, sp, d_codes, codes_cap);
+        prof_end();
+        ++launches;
+    }
+    return true;
+}
+
+bool Engine::enqueue_talker_step(const int * pos_ptr, int pos_static, const int * done, bool with_dump) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size;
+    if (!layers(L, kc, vc, n_ctx, rope_t, x, 1, pos_ptr, pos_static, false, done, c.intermediate_size,
+                with_dump && attn_dump ? d_attn : nullptr, attn_layer))
+        return false;
+    return gemv(codec_head, nullptr, x, H, 1, out_norm, ACT_F16, logits, c.codec_vocab_size, nullptr, 0, EPI_STORE,
+                hidden, H, done);
+}
+
+bool Engine::enqueue_frame() {
+    if (!enqueue_cp(true)) return false;
+    InputArgs ia{};
+    ia.H = cfg.hidden_size; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
+    ia.trailing = trailing; ia.pad = pad; ia.out = x; ia.st = st; ia.n_cb = cfg.n_codebooks;
+    ia.mode = IN_TALKER;
+    k_frame_inputs<<<1, 256, 0, stream>>>(ia);
+    ++launches;
+    if (!enqueue_talker_step(&st->pos, 0, &st->done, true)) return false;
+    k_frame_end<<<1, 32, 0, stream>>>(st);
+    ++launches;
+    return true;
+}
+
+bool Engine::capture_graph() {
+    if (graph) { cudaGraphExecDestroy(graph); graph = nullptr; }
+    cudaGraph_t gr = nullptr;
+    QCHECK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    launches = 0;
+    const bool ok = enqueue_frame();
+    cudaError_t ce = cudaStreamEndCapture(stream, &gr);
+    if (!ok) { if (gr) cudaGraphDestroy(gr); return false; }
+    if (ce != cudaSuccess) { err = std::string("graph capture: ") + cudaGetErrorString(ce); return false; }
+    launches_per_frame = launches;
+    ce = cudaGraphInstantiate(&graph, gr, 0);
+    cudaGraphDestroy(gr);
+    if (ce != cudaSuccess) { err = std::string("graph instantiate: ") + cudaGetErrorString(ce); return false; }
+    graph_ok = true;
+    return true;
+}
+
+// ---------------------------------------------------------------- prefill & helpers
+bool Engine::prefill(const float * rows_host, int n, int n_past, float * hidden_out, float * logits_out) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size;
+    if (n <= 0) { err = "n_tokens must be > 0"; return false; }
+    if (n_ctx == 0 && !init_kv(std::max(256, n_past + n + 16))) return false;
+    if (n_past + n > n_ctx) { err = "Context length exceeded"; return false; }
+    QCHECK(cudaEventRecord(ev0, stream));
+    for (int c0 = 0; c0 < n; c0 += QTTS_MAX_NV) {
+        const int M = std::min(QTTS_MAX_NV, n - c0);
+        QCHECK(cudaMemcpyAsync(x, rows_host + (size_t) c0 * H, sizeof(float) * M * H, cudaMemcpyHostToDevice, stream));
+        if (!layers(L, kc, vc, n_ctx, rope_t, x, M, nullptr, n_past + c0, false, nullptr, c.intermediate_size)) return false;
+        if (hidden_out) {
+            k_rmsnorm_rows<<<M, 256, 0, stream>>>(x, H, out_norm, c.rms_norm_eps, H, hid_rows, H);
+            QCHECK(cudaMemcpyAsync(hidden_out + (size_t) c0 * H, hid_rows, sizeof(float) * M * H, cudaMemcpyDeviceToHost, stream));
+        }
+        if (c0 + M == n) {
+            if (!gemv(codec_head, nullptr, x + (size_t)(M - 1) * H, H, 1, out_norm, ACT_F16, logits, c.codec_vocab_size,
+                      nullptr, 0, EPI_STORE, hidden, H, nullptr))
+                return false;
+        }
+        // the next chunk's upload overwrites x: keep the stream ordered (same stream)
+        if (c0 + M < n && !sync("prefill chunk")) return false;
+    }
+    QCHECK(cudaEventRecord(ev1, stream));
+    last_hidden.resize(H);
+    QCHECK(cudaMemcpyAsync(last_hidden.data(), hidden, sizeof(float) * H, cudaMemcpyDeviceToHost, stream));
+    if (logits_out)
+        QCHECK(cudaMemcpyAsync(logits_out, logits, sizeof(float) * c.codec_vocab_size, cudaMemcpyDeviceToHost, stream));
+    if (!sync("forward_prefill")) return false;
+    cudaEventElapsedTime(&timing.prefill_ms, ev0, ev1);
+    n_used = n_past + n;
+    return true;
+}
+
+bool Engine::lookup(int table, const int32_t * ids, int n, std::vector<float> & out) {
+    const qtts_config & c = cfg;
+    if (n <= 0) { out.clear(); return true; }
+    const __half * tab;
+    int dim, vocab;
+    if (table == 0) { tab = codec_embd; dim = c.hidden_size; vocab = c.codec_vocab_size; }
+    else if (table < 0) { tab = text_embd; dim = c.text_embd_dim; vocab = c.text_vocab_size; }
+    else if (table < c.n_codebooks) { tab = cp_embd[table - 1]; dim = c.hidden_size; vocab = c.code_pred_vocab_size; }
+    else { err = "Embedding tensor not found"; return false; }
+    for (int i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= vocab) { err = "Embedding token ID out of range"; return false; }
+    out.resize((size_t) n * dim);
+    const int step = QTTS_MAX_NV;   // rows staged through tmp_a per round trip
+    for (int c0 = 0; c0 < n; c0 += step) {
+        const int m = std::min(step, n - c0);
+        QCHECK(cudaMemcpyAsync(d_ids, ids + c0, sizeof(int) * m, cudaMemcpyHostToDevice, stream));
+        k_gather_rows<<<m, 256, 0, stream>>>(tab, dim, d_ids, m, tmp_a);
+        QCHECK(cudaMemcpyAsync(out.data() + (size_t) c0 * dim, tmp_a, sizeof(float) * m * dim, cudaMemcpyDeviceToHost, stream));
+        if (!sync("lookup_embedding_rows")) return false;
+    }
+    return true;
+}
+
+// project_text_tokens (src/tts_transformer.cpp:963-1028) on the device.
+bool Engine::project_text(const int32_t * toks, int n, std::vector<float> & out) {
+    const qtts_config & c = cfg;
+    const int TD = c.text_embd_dim, H = c.hidden_size;
+    if (n <= 0) { out.clear(); return true; }
+    for (int i = 0; i < n; ++i)
+        if (toks[i] < 0 || toks[i] >= c.text_vocab_size) { err = "Embedding token ID out of range"; return false; }
+    out.resize((size_t) n * H);
+    for (int c0 = 0; c0 < n; c0 += QTTS_MAX_NV) {
+        const int m = std::min(QTTS_MAX_NV, n - c0);
+        QCHECK(cudaMemcpyAsync(d_ids, toks + c0, sizeof(int) * m, cudaMemcpyHostToDevice, stream));
+        k_gather_rows<<<m, 256, 0, stream>>>(text_embd, TD, d_ids, m, tmp_a);
+        if (!gemv(fc1, nullptr, tmp_a, TD, m, nullptr, ACT_F16, hbuf, TD, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
+        k_bias_silu<<<32, 256, 0, stream>>>(hbuf, fc1_b, TD, TD, m);
+        if (!gemv(fc2, nullptr, hbuf, TD, m, nullptr, ACT_F16, tmp_b, H, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
+        k_bias_add<<<32, 256, 0, stream>>>(tmp_b, fc2_b, H, H, m);
+        QCHECK(cudaMemcpyAsync(out.data() + (size_t) c0 * H, tmp_b, sizeof(float) * m * H, cudaMemcpyDeviceToHost, stream));
+        if (!sync("project_text_tokens")) return false;
+    }
+    return true;
+}
+
+// build_prefill_graph (src/tts_transformer.cpp:1030-1186): host F32 assembly of
+// projected text rows and codec embedding rows, as in the reference.
+bool Engine::build_prefill(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
+                           std::vector<float> & padv) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size;
+    if (!p->text_tokens) { err = "text_tokens is null"; return false; }
+    if (p->n_tokens < 4) { err = "Need at least 4 text tokens for prefill"; return false; }
+    int32_t special[3] = {c.tts_bos_token_id, c.tts_eos_token_id, c.tts_pad_token_id};
+    std::vector<float> sp3, role, first, cpe, te;
+    if (!project_text(special, 3, sp3) || !project_text(p->text_tokens, 3, role)) return false;
+    const float * bos = sp3.data();
+    const float * eos = sp3.data() + H;
+    padv.assign(sp3.data() + 2 * H, sp3.data() + 3 * H);
+    std::vector<int32_t> ctoks;
+    if (p->language_id < 0) ctoks = {c.codec_nothink_id, c.codec_think_bos_id, c.codec_think_eos_id};
+    else ctoks = {c.codec_think_id, c.codec_think_bos_id, p->language_id, c.codec_think_eos_id};
+    int32_t tail[2] = {c.codec_pad_id, c.codec_bos_id};
+    if (!lookup(0, ctoks.data(), (int) ctoks.size(), cpe) || !lookup(0, tail, 2, te)) return false;
+    const bool spk = p->speaker_embd != nullptr;
+    const int cin = (int) ctoks.size() + (spk ? 1 : 0) + 2;
+    std::vector<float> ci((size_t) cin * H);
+    memcpy(ci.data(), cpe.data(), cpe.size() * 4);
+    int dst = (int) ctoks.size();
+    if (spk) { memcpy(ci.data() + (size_t) dst * H, p->speaker_embd, H * 4); ++dst; }
+    memcpy(ci.data() + (size_t) dst * H, te.data(), te.size() * 4);
+    const int ov = cin - 1;
+    std::vector<float> cov((size_t) ov * H);
+    for (int t = 0; t < ov; ++t) {
+        const float * o = (t == ov - 1) ? bos : padv.data();
+        for (int d = 0; d < H; ++d) cov[(size_t) t * H + d] = o[d] + ci[(size_t) t * H + d];
+    }
+    if (!project_text(p->text_tokens + 3, 1, first)) return false;
+    std::vector<float> fb(H);
+    for (int d = 0; d < H; ++d) fb[d] = first[d] + ci[(size_t)(cin - 1) * H + d];
+    std::vector<float> ins;
+    int ilen = 0;
+    if (p->instruct_tokens && p->n_instruct > 0) {
+        if (!project_text(p->instruct_tokens, p->n_instruct, ins)) return false;
+        ilen = p->n_instruct;
+    }
+    const int plen = ilen + 3 + ov + 1;
+    rows.assign((size_t) plen * H, 0.0f);
+    if (ilen) memcpy(rows.data(), ins.data(), ins.size() * 4);
+    memcpy(rows.data() + (size_t) ilen * H, role.data(), role.size() * 4);
+    memcpy(rows.data() + (size_t)(ilen + 3) * H, cov.data(), cov.size() * 4);
+    memcpy(rows.data() + (size_t)(plen - 1) * H, fb.data(), H * 4);
+    const int ntrail = std::max(0, p->n_tokens - 9);
+    std::vector<float> tp;
+    if (ntrail > 0 && !project_text(p->text_tokens + 4, ntrail, tp)) return false;
+    trail.assign((size_t)(ntrail + 1) * H, 0.0f);
+    if (ntrail > 0) memcpy(trail.data(), tp.data(), tp.size() * 4);
+    memcpy(trail.data() + (size_t) ntrail * H, eos, H * 4);
+    return true;
+}
+
+// build_prefill_graph_icl (src/tts_transformer.cpp:1188-1472).
+bool Engine::build_prefill_icl(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
+                               std::vector<float> & padv) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size;
+    if (!p->text_tokens || p->n_tokens < 4) { err = "ICL: need at least 4 target text tokens"; return false; }
+    if (!p->ref_codec_tokens || p->n_ref_frames < 1) { err = "ICL: need at least 1 reference codec frame"; return false; }
+    int32_t special[3] = {c.tts_bos_token_id, c.tts_eos_token_id, c.tts_pad_token_id};
+    std::vector<float> sp3, role, cpe, te;
+    if (!project_text(special, 3, sp3) || !project_text(p->text_tokens, 3, role)) return false;
+    const float * bos = sp3.data();
+    padv.assign(sp3.data() + 2 * H, sp3.data() + 3 * H);
+    int32_t ctoks[3] = {c.codec_nothink_id, c.codec_think_bos_id, c.codec_think_eos_id};
+    int32_t tail[2] = {c.codec_pad_id, c.codec_bos_id};
+    if (!lookup(0, ctoks, 3, cpe) || !lookup(0, tail, 2, te)) return false;
+    const bool spk = p->speaker_embd != nullptr;
+    const int cin = 3 + (spk ? 1 : 0) + 2;
+    std::vector<float> ci((size_t) cin * H);
+    memcpy(ci.data(), cpe.data(), cpe.size() * 4);
+    int dst = 3;
+    if (spk) { memcpy(ci.data() + (size_t) dst * H, p->speaker_embd, H * 4); ++dst; }
+    memcpy(ci.data() + (size_t) dst * H, te.data(), te.size() * 4);
+    const int ov = cin - 1;
+    rows.assign((size_t)(3 + ov) * H, 0.0f);
+    memcpy(rows.data(), role.data(), role.size() * 4);
+    for (int t = 0; t < ov; ++t) {
+        const float * o = (t == ov - 1) ? bos : padv.data();
+        for (int d = 0; d < H; ++d) rows[(size_t)(3 + t) * H + d] = o[d] + ci[(size_t) t * H + d];
+    }
+    int rs = 3, re = p->n_ref_text - 5; if (re < rs) re = rs;
+    int ts = 3, tend = p->n_tokens - 5; if (tend < ts) tend = ts;
+    std::vector<int32_t> comb;
+    for (int i = rs; i < re && i < p->n_ref_text; ++i) comb.push_back(p->ref_text_tokens[i]);
+    for (int i = ts; i < tend && i < p->n_tokens; ++i) comb.push_back(p->text_tokens[i]);
+    comb.push_back(c.tts_eos_token_id);
+    const int nct = p->n_ref_frames + 1;
+    std::vector<float> cf((size_t) nct * H, 0.0f), r0, r1;
+    int32_t cbos = c.codec_bos_id;
+    if (!lookup(0, &cbos, 1, r0)) return false;
+    memcpy(cf.data(), r0.data(), H * 4);
+    // per reference frame: codec_embd[cb0] then += code_pred_embd[cb-1][code], in codebook order
+    std::vector<int32_t> col((size_t) p->n_ref_frames);
+    for (int cb = 0; cb < 16 && cb < c.n_codebooks; ++cb) {
+        for (int f = 0; f < p->n_ref_frames; ++f) col[f] = p->ref_codec_tokens[(size_t) f * 16 + cb];
+        if (!lookup(cb, col.data(), p->n_ref_frames, r1)) return false;
+        for (int f = 0; f < p->n_ref_frames; ++f) {
+            float * d = cf.data() + (size_t)(f + 1) * H;
+            const float * s = r1.data() + (size_t) f * H;
+            if (cb == 0) memcpy(d, s, H * 4);
+            else for (int k = 0; k < H; ++k) d[k] += s[k];
+        }
+    }
+    const int nt = (int) comb.size();
+    std::vector<float> tp;
+    if (!project_text(comb.data(), nt, tp)) return false;
+    const int icl = nct;
+    const size_t base = rows.size() / H;
+    rows.resize((base + icl) * H, 0.0f);
+    for (int i = 0; i < icl; ++i) {
+        float * d = rows.data() + (base + i) * H;
+        const float * t = i < nt ? tp.data() + (size_t) i * H : padv.data();
+        for (int k = 0; k < H; ++k) d[k] = 0.0f + t[k];
+        const float * cr = cf.data() + (size_t) i * H;
+        for (int k = 0; k < H; ++k) d[k] += cr[k];
+    }
+    trail.clear();
+    if (nt > nct) trail.assign(tp.data() + (size_t) nct * H, tp.data() + (size_t) nt * H);
+    return true;
+}
+
+int Engine::begin(const qtts_generate_params * p) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size;
+    sess = GenSession{};
+    attn_rows.clear();
+    std::vector<float> rows, trail, padv;
+    const bool icl = p->ref_codec_tokens != nullptr;
+    if (icl) { if (!build_prefill_icl(p, rows, trail, padv)) return -1; }
+    else if (!build_prefill(p, rows, trail, padv)) return -1;
+    const int plen = (int)(rows.size() / H), tlen = (int)(trail.size() / H);
+    const int required = plen + p->max_len + 8;
+    if (n_ctx < required || n_ctx > std::max(required * 2, 512)) { if (!init_kv(required)) return -1; }
+    n_used = 0;
+    // device buffers sized for this call (re-capture when they grow)
+    if (p->max_len > codes_cap) {
+        if (d_codes) cudaFree(d_codes);
+        codes_cap = std::max(p->max_len, 256);
+        if (cudaMalloc(&d_codes, sizeof(int) * codes_cap * c.n_codebooks) != cudaSuccess) { err = "alloc codes"; return -1; }
+        graph_ok = false;
+    }
+    if (std::max(tlen, 1) > trailing_cap) {
+        if (trailing) cudaFree(trailing);
+        trailing_cap = std::max(tlen, 256);
+        if (cudaMalloc(&trailing, sizeof(float) * trailing_cap * H) != cudaSuccess) { err = "alloc trailing"; return -1; }
+        graph_ok = false;
+    }
+    if (attn_dump) {
+        const size_t need = (size_t) p->max_len * c.n_attention_heads * n_ctx;
+        if (need > attn_cap) {
+            if (d_attn) cudaFree(d_attn);
+            attn_cap = need;
+            if (cudaMalloc(&d_attn, sizeof(float) * attn_cap) != cudaSuccess) { err = "alloc attn dump"; return -1; }
+            graph_ok = false;
+        }
+    }
+    if (h_dbg_cap > 0 && (h_dbg_t || h_dbg_cp)) {
+        const int cap = std::min(h_dbg_cap, p->max_len);
+        if (cap > dbg_cap) {
+            if (dbg_t) cudaFree(dbg_t);
+            if (dbg_cp) cudaFree(dbg_cp);
+            dbg_cap = cap;
+            if (cudaMalloc(&dbg_t, sizeof(float) * dbg_cap * c.codec_vocab_size) != cudaSuccess ||
+                cudaMalloc(&dbg_cp, sizeof(float) * dbg_cap * (c.n_codebooks - 1) * c.code_pred_vocab_size) != cudaSuccess) {
+                err = "alloc debug logits"; return -1;
+            }
+        }
+    }
+    if (!prefill(rows.data(), plen, 0, nullptr, nullptr)) return -1;
+    if (tlen > 0 && cudaMemcpyAsync(trailing, trail.data(), sizeof(float) * tlen * H, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+        err = "upload trailing"; return -1;
+    }
+    if (cudaMemcpyAsync(pad, padv.data(), sizeof(float) * H, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+        err = "upload pad"; return -1;
+    }
+    DevState hs{};
+    hs.pos = plen; hs.frame = 0; hs.done = 0; hs.n_out = 0; hs.n_trailing = tlen;
+    SampleParams P{};
+    P.temperature = p->temperature; P.top_k = p->top_k; P.rep_penalty = p->repetition_penalty;
+    P.eos_bias = p->eos_bias; P.target_frames = p->target_frames; P.eos_id = c.codec_eos_id;
+    P.suppress_start = c.codec_vocab_size - 1024; P.seed = p->seed ? p->seed : seed;
+    P.record_logits = (h_dbg_cap > 0 && (h_dbg_t || h_dbg_cp)) ? 1 : 0;
+    P.dbg_talker = dbg_t; P.dbg_cp = dbg_cp; P.dbg_cap = P.record_logits ? std::min(dbg_cap, p->max_len) : 0;
+    P.n_cb = c.n_codebooks;
+    if (cudaMemcpyAsync(st, &hs, sizeof(hs), cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        cudaMemcpyAsync(sp, &P, sizeof(P), cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+        err = "upload state"; return -1;
+    }
+    if (!sync("generate setup")) return -1;
+    if (!graph_ok && !capture_graph()) return -1;
+    sess.active = true;
+    sess.max_len = p->max_len;
+    sess.prefill_len = plen;
+    sess.trailing_len = tlen;
+    timing.frames_ms = 0.0f;
+    timing.frames = 0;
+    timing.kernel_launches = launches_per_frame;
+    return plen;
+}
+
+int Engine::run_frames(int n, int32_t * codes_out) {
+    const int NCB = cfg.n_codebooks;
+    if (!sess.active) { err = "no active generation"; return -1; }
+    if (sess.done) return 0;
+    n = std::min(n, sess.max_len - sess.produced);
+    if (n <= 0) return 0;
+    if (cudaEventRecord(ev0, stream) != cudaSuccess) { err = "event"; return -1; }
+    for (int i = 0; i < n; ++i)
+        if (cudaGraphLaunch(graph, stream) != cudaSuccess) { err = "graph launch failed"; return -1; }
+    if (cudaEventRecord(ev1, stream) != cudaSuccess) { err = "event"; return -1; }
+    DevState hs;
+    if (cudaMemcpyAsync(&hs, st, sizeof(hs), cudaMemcpyDeviceToHost, stream) != cudaSuccess) { err = "state readback"; return -1; }
+    if (!sync("frame loop")) return -1;
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, ev0, ev1);
+    timing.frames_ms += ms;
+    const int got = hs.n_out - sess.produced;
+    timing.frames += got;
+    if (got > 0 && codes_out) {
+        if (cudaMemcpy(codes_out, d_codes + (size_t) sess.produced * NCB, sizeof(int) * got * NCB, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            err = "codes readback"; return -1;
+        }
+    }
+    if (attn_dump && got > 0) {
+        const int NH = cfg.n_attention_heads;
+        std::vector<float> buf((size_t) NH * n_ctx);
+        for (int f = sess.produced; f < sess.produced + got; ++f) {
+            if (cudaMemcpy(buf.data(), d_attn + (size_t) f * NH * n_ctx, sizeof(float) * buf.size(), cudaMemcpyDeviceToHost) != cudaSuccess) {
+                err = "attn readback"; return -1;
+            }
+            const int nkv = sess.prefill_len + f + 1;
+            std::vector<float> row((size_t) NH * nkv);
+            for (int h = 0; h < NH; ++h) memcpy(row.data() + (size_t) h * nkv, buf.data() + (size_t) h * n_ctx, sizeof(float) * nkv);
+            attn_rows.push_back(std::move(row));
+        }
+    }
+    if (h_dbg_cap > 0 && got > 0) {
+        const int f0 = sess.produced, f1 = std::min(sess.produced + got + (hs.done ? 1 : 0), std::min(dbg_cap, h_dbg_cap));
+        if (f1 > f0) {
+            if (h_dbg_t) cudaMemcpy(h_dbg_t + (size_t) f0 * cfg.codec_vocab_size, dbg_t + (size_t) f0 * cfg.codec_vocab_size,
+                                    sizeof(float) * (f1 - f0) * cfg.codec_vocab_size, cudaMemcpyDeviceToHost);
+            const size_t per = (size_t)(NCB - 1) * cfg.code_pred_vocab_size;
+            if (h_dbg_cp) cudaMemcpy(h_dbg_cp + f0 * per, dbg_cp + f0 * per, sizeof(float) * (f1 - f0) * per, cudaMemcpyDeviceToHost);
+        }
+    }
+    sess.produced = hs.n_out;
+    sess.done = hs.done != 0;
+    n_used = hs.pos;
+    return got;
+}
+
+}  // namespace qtts
+
+using qtts::Engine;
+
+// ================================================================ C ABI
+extern "C" {
+
+// ---------------------------------------------------------------- kernel-level entry points
+// These run one engine kernel on caller-provided host data (device buffers are
+// allocated per call); the parity tests use them to check a kernel in isolation.
+int32_t qtts_op_gemv(int32_t device, int32_t wtype, const void * w, int32_t rows, int32_t cols, const float * xin,
+                     int32_t nv, const float * norm_gain, float eps, int32_t act_f32, float * y, int32_t * block_dots) {
+    using namespace qtts;
+    if (!w || !xin || !y || rows <= 0 || cols <= 0 || nv <= 0 || nv > QTTS_MAX_NV) return 0;
+    if (wtype != W_F16 && wtype != W_Q8_0) return 0;
+    if ((wtype == W_F16 && cols % 8) || (wtype == W_Q8_0 && cols % 32)) return 0;
+    if (cudaSetDevice(device) != cudaSuccess) return 0;
+    int n_sm = 148;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device);
+    const int nb = cols / 32;
+    std::vector<uint8_t> q, d;
+    DMat A; A.type = wtype; A.rows = rows; A.cols = cols;
+    void * dw = nullptr, * dd = nullptr, * dx = nullptr, * dy = nullptr, * dg = nullptr, * dbd = nullptr;
+    bool ok = true;
+    auto chk = [&](cudaError_t e) { if (e != cudaSuccess) ok = false; };
+    if (wtype == W_F16) {
+        chk(cudaMalloc(&dw, (size_t) rows * cols * 2));
+        chk(cudaMemcpy(dw, w, (size_t) rows * cols * 2, cudaMemcpyHostToDevice));
+    } else {
+        q.resize((size_t) rows * cols); d.resize((size_t) rows * nb * 2);
+        const uint8_t * src = static_cast<const uint8_t *>(w);
+        for (size_t r = 0; r < (size_t) rows; ++r)
+            for (int b = 0; b < nb; ++b) {
+                memcpy(&d[(r * nb + b) * 2], src + (r * nb + b) * 34, 2);
+                memcpy(&q[r * cols + (size_t) b * 32], src + (r * nb + b) * 34 + 2, 32);
+            }
+        chk(cudaMalloc(&dw, q.size())); chk(cudaMalloc(&dd, d.size()));
+        chk(cudaMemcpy(dw, q.data(), q.size(), cudaMemcpyHostToDevice));
+        chk(cudaMemcpy(dd, d.data(), d.size(), cudaMemcpyHostToDevice));
+    }
+    A.w = dw; A.d = (const __half *) dd;
+    chk(cudaMalloc(&dx, sizeof(float) * nv * cols));
+    chk(cudaMalloc(&dy, sizeof(float) * nv * rows));
+    chk(cudaMemcpy(dx, xin, sizeof(float) * nv * cols, cudaMemcpyHostToDevice));
+    if (norm_gain) { chk(cudaMalloc(&dg, sizeof(float) * cols)); chk(cudaMemcpy(dg, norm_gain, sizeof(float) * cols, cudaMemcpyHostToDevice)); }
+    if (block_dots && wtype == W_Q8_0) { chk(cudaMalloc(&dbd, sizeof(int) * nv * rows * nb)); chk(cudaMemset(dbd, 0, sizeof(int) * nv * rows * nb)); }
+    if (ok) {
+        GemvArgs a{};
+        a.A = A; a.x = (const float *) dx; a.ldx = cols; a.nv = nv; a.norm_g = (const float *) dg; a.eps = eps;
+        a.act = act_f32 ? ACT_F32 : ACT_F16; a.y = (float *) dy; a.ldy = rows; a.epi = EPI_STORE;
+        a.block_dots = (int *) dbd;
+        int ncta = std::min(n_sm, rows);
+        const int rpc = (rows + ncta - 1) / ncta;
+        ncta = (rows + rpc - 1) / rpc;
+        const int nchunk = wtype == W_F16 ? cols / 8 : cols / 16;
+        int ks = (2 * QTTS_WARPS + rpc - 1) / rpc;
+        a.kslices = std::max(1, std::min(ks, std::max(1, nchunk / 32)));
+        const int NVt = nv == 1 ? 1 : nv == 2 ? 2 : 8;
+        const size_t smem = gemv_smem_bytes(wtype, cols, NVt, rpc, a.kslices);
+        cudaFuncSetAttribute(k_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (smem > 200 * 1024) ok = false;
+        else if (NVt == 1) k_gemv<1><<<ncta, QTTS_WARPS * 32, smem>>>(a);
+        else if (NVt == 2) k_gemv<2><<<ncta, QTTS_WARPS * 32, smem>>>(a);
+        else k_gemv<8><<<ncta, QTTS_WARPS * 32, smem>>>(a);
+        chk(cudaGetLastError());
+        chk(cudaDeviceSynchronize());
+        if (ok) chk(cudaMemcpy(y, dy, sizeof(float) * nv * rows, cudaMemcpyDeviceToHost));
+        if (ok && dbd) chk(cudaMemcpy(block_dots, dbd, sizeof(int) * nv * rows * nb, cudaMemcpyDeviceToHost));
+    }
+    void * all[] = {dw, dd, dx, dy, dg, dbd};
+    for (void * p : all) if (p) cudaFree(p);
+    return ok ? 1 : 0;
+}
+
+// One sampling decision with the engine's sampler (cb 0 = codebook-0 rules with
+// suppression/penalty/EOS bias; cb >= 1 = code-predictor rules).  presence:
+// optional [vocab] 0/1 set of earlier codebook-0 tokens.  Returns the token or
+// -1 (EOS for cb 0 returns eos_id).
+int32_t qtts_op_sample(int32_t device, const float * logits_in, int32_t V, int32_t cb, float temperature, int32_t top_k,
+                       float rep_penalty, const int32_t * presence, float eos_bias, int32_t target_frames, int32_t frame,
+                       int32_t eos_id, int32_t suppress_start, uint64_t seed) {
+    using namespace qtts;
+    if (!logits_in || V <= 0 || V > SAMPLE_THREADS * SAMPLE_PER_T) return -1;
+    if (cudaSetDevice(device) != cudaSuccess) return -1;
+    float * dl = nullptr; DevState * dst = nullptr; SampleParams * dsp = nullptr;
+    DevState hs{};
+    hs.frame = frame;
+    if (presence) for (int i = 0; i < V; ++i) if (presence[i]) hs.presence[i >> 5] |= 1u << (i & 31);
+    SampleParams P{};
+    P.temperature = temperature; P.top_k = top_k; P.rep_penalty = rep_penalty; P.eos_bias = eos_bias;
+    P.target_frames = target_frames; P.eos_id = eos_id; P.suppress_start = suppress_start; P.seed = seed; P.n_cb = 16;
+    int tok = -1;
+    if (cudaMalloc(&dl, sizeof(float) * V) == cudaSuccess && cudaMalloc(&dst, sizeof(DevState)) == cudaSuccess &&
+        cudaMalloc(&dsp, sizeof(SampleParams)) == cudaSuccess) {
+        cudaMemcpy(dl, logits_in, sizeof(float) * V, cudaMemcpyHostToDevice);
+        cudaMemcpy(dst, &hs, sizeof(hs), cudaMemcpyHostToDevice);
+        cudaMemcpy(dsp, &P, sizeof(P), cudaMemcpyHostToDevice);
+        k_sample<<<1, SAMPLE_THREADS>>>(dl, V, cb, dst, dsp, nullptr, 0);
+        if (cudaDeviceSynchronize() == cudaSuccess && cudaMemcpy(&hs, dst, sizeof(hs), cudaMemcpyDeviceToHost) == cudaSuccess)
+            tok = (cb == 0 && hs.done) ? eos_id : hs.codes[cb];
+    }
+    if (dl) cudaFree(dl);
+    if (dst) cudaFree(dst);
+    if (dsp) cudaFree(dsp);
+    return tok;
+}
+
+qtts_engine * qtts_create(const char * gguf_path, int32_t device) {
+    qtts::g_create_error.clear();
+    if (!gguf_path) { qtts::g_create_error = "gguf_path is null"; return nullptr; }
+    auto e = std::make_unique<Engine>();
+    if (!e->load(gguf_path, device)) {
+        qtts::g_create_error = e->err;
+        return nullptr;
+    }
+    return reinterpret_cast<qtts_engine *>(e.release());
+}
+
+const char * qtts_create_error(void) { return qtts::g_create_error.c_str(); }
+
+void qtts_destroy(qtts_engine * h) { delete reinterpret_cast<Engine *>(h); }
+
+const char * qtts_get_error(const qtts_engine * h) {
+    return h ? reinterpret_cast<const Engine *>(h)->err.c_str() : "null engine";
+}
+
+int32_t qtts_get_config(const qtts_engine * h, qtts_config * out) {
+    if (!h || !out) return 0;
+    *out = reinterpret_cast<const Engine *>(h)->cfg;
+    return 1;
+}
+
+void qtts_set_n_threads(qtts_engine *, int32_t) {}
+
+#define ENG(h) Engine & E = *reinterpret_cast<Engine *>(h); cudaSetDevice(E.dev)
+
+int32_t qtts_init_kv_cache(qtts_engine * h, int32_t n_ctx) { if (!h) return 0; ENG(h); return E.init_kv(n_ctx) ? 1 : 0; }
+void qtts_clear_kv_cache(qtts_engine * h) { if (h) reinterpret_cast<Engine *>(h)->n_used = 0; }
+int32_t qtts_init_code_pred_kv_cache(qtts_engine * h, int32_t n_ctx) { if (!h) return 0; ENG(h); return E.init_cp_kv(n_ctx) ? 1 : 0; }
+void qtts_clear_code_pred_kv_cache(qtts_engine *) {}
+
+int32_t qtts_forward_prefill(qtts_engine * h, const float * embd, int32_t n, int32_t n_past, float * hidden_out,
+                             float * logits_out) {
+    if (!h) return 0;
+    ENG(h);
+    if (!embd) { E.err = "prefill_embd is null"; return 0; }
+    E.sess.active = false;
+    return E.prefill(embd, n, n_past, hidden_out, logits_out) ? 1 : 0;
+}
+
+int32_t qtts_forward_step(qtts_engine * h, const float * embd, int32_t n_past, float * logits_out, float * hidden_out) {
+    if (!h) return 0;
+    ENG(h);
+    if (!embd) { E.err = "step_embd is null"; return 0; }
+    E.sess.active = false;
+    if (E.n_ctx == 0 && !E.init_kv(std::max(256, n_past + 1 + 16))) return 0;
+    if (n_past + 1 > E.n_ctx) { E.err = "Context length exceeded"; return 0; }
+    const int H = E.cfg.hidden_size;
+    if (cudaMemcpyAsync(E.x, embd, sizeof(float) * H, cudaMemcpyHostToDevice, E.stream) != cudaSuccess) { E.err = "upload"; return 0; }
+    if (!E.enqueue_talker_step(nullptr, n_past, nullptr, false)) return 0;
+    E.last_hidden.resize(H);
+    cudaMemcpyAsync(E.last_hidden.data(), E.hidden, sizeof(float) * H, cudaMemcpyDeviceToHost, E.stream);
+    if (logits_out) cudaMemcpyAsync(logits_out, E.logits, sizeof(float) * E.cfg.codec_vocab_size, cudaMemcpyDeviceToHost, E.stream);
+    if (!E.sync("forward_step")) return 0;
+    if (hidden_out) memcpy(hidden_out, E.last_hidden.data(), sizeof(float) * H);
+    E.n_used = n_past + 1;
+    return 1;
+}
+
+int32_t qtts_forward_text(qtts_engine * h, const int32_t * toks, int32_t n, const float * spk, int32_t n_past,
+                          float * hidden_out) {
+    if (!h) return 0;
+    ENG(h);
+    if (!toks) { E.err = "text_tokens is null"; return 0; }
+    if (n <= 0) { E.err = "n_tokens must be > 0"; return 0; }
+    std::vector<float> proj;
+    if (!E.project_text(toks, n, proj)) return 0;
+    const int H = E.cfg.hidden_size;
+    if (spk)
+        for (int t = 0; t < n; ++t)
+            for (int d = 0; d < H; ++d) proj[(size_t) t * H + d] += spk[d];
+    return qtts_forward_prefill(h, proj.data(), n, n_past, hidden_out, nullptr);
+}
+
+int32_t qtts_forward_codec(qtts_engine * h, int32_t tok, int32_t n_past, float * logits_out) {
+    if (!h) return 0;
+    ENG(h);
+    std::vector<float> row;
+    if (!E.lookup(0, &tok, 1, row)) return 0;
+    return qtts_forward_step(h, row.data(), n_past, logits_out, nullptr);
+}
+
+int32_t qtts_get_hidden_states(const qtts_engine * h, float * out) {
+    if (!h || !out) return 0;
+    const Engine & E = *reinterpret_cast<const Engine *>(h);
+    if (E.sess.active) {
+        cudaSetDevice(E.dev);
+        cudaMemcpy(out, E.hidden, sizeof(float) * E.cfg.hidden_size, cudaMemcpyDeviceToHost);
+        return 1;
+    }
+    if (E.last_hidden.empty()) return 0;
+    memcpy(out, E.last_hidden.data(), sizeof(float) * E.last_hidden.size());
+    return 1;
+}
+
+int32_t qtts_predict_codes_autoregressive(qtts_engine * h, const float * hidden, int32_t cb0, float temperature,
+                                          int32_t top_k, int32_t * codes_out) {
+    if (!h) return 0;
+    ENG(h);
+    const qtts_config & c = E.cfg;
+    if (!hidden || !codes_out) { E.err = "null argument"; return 0; }
+    if (cb0 < 0 || cb0 >= c.codec_vocab_size) { E.err = "Embedding token ID out of range"; return 0; }
+    E.sess.active = false;
+    qtts::DevState hs{};
+    hs.codes[0] = cb0;
+    hs.frame = (int) E.api_calls++;
+    qtts::SampleParams P{};
+    P.temperature = temperature; P.top_k = top_k; P.rep_penalty = 1.0f; P.eos_id = c.codec_eos_id;
+    P.suppress_start = c.codec_vocab_size; P.seed = E.seed; P.n_cb = c.n_codebooks;
+    cudaMemcpyAsync(E.hidden, hidden, sizeof(float) * c.hidden_size, cudaMemcpyHostToDevice, E.stream);
+    cudaMemcpyAsync(E.st, &hs, sizeof(hs), cudaMemcpyHostToDevice, E.stream);
+    cudaMemcpyAsync(E.sp, &P, sizeof(P), cudaMemcpyHostToDevice, E.stream);
+    int saved_cap = E.codes_cap;
+    E.codes_cap = 0;   // no frame output rows
+    const bool ok = E.enqueue_cp(false);
+    E.codes_cap = saved_cap;
+    if (!ok) return 0;
+    cudaMemcpyAsync(&hs, E.st, sizeof(hs), cudaMemcpyDeviceToHost, E.stream);
+    if (!E.sync("predict_codes_autoregressive")) return 0;
+    for (int g = 1; g < c.n_codebooks; ++g) codes_out[g - 1] = hs.codes[g];
+    return 1;
+}
+
+// Legacy non-autoregressive predictor (build_code_pred_graph,
+// src/tts_transformer.cpp:1771-1899): one row, no RoPE, attention over itself
+// (softmax of one score is exactly 1, so the output is V), no output norm, all
+// heads on the final row.
+int32_t qtts_predict_codes(qtts_engine * h, const float * hidden, const int32_t * prev_codes, float * logits_out) {
+    if (!h) return 0;
+    ENG(h);
+    const qtts_config & c = E.cfg;
+    const int H = c.hidden_size, NG = c.n_codebooks - 1, V1 = c.code_pred_vocab_size;
+    if (!hidden || !logits_out) { E.err = "null argument"; return 0; }
+    E.sess.active = false;
+    std::vector<float> row(hidden, hidden + H), r;
+    if (prev_codes)
+        for (int cb = 0; cb < NG; ++cb) {
+            if (!E.lookup(cb + 1, prev_codes + cb, 1, r)) return 0;
+            for (int d = 0; d < H; ++d) row[d] += r[d];
+        }
+    cudaMemcpyAsync(E.xcp, row.data(), sizeof(float) * H, cudaMemcpyHostToDevice, E.stream);
+    for (auto & l : E.CPL) {
+        E.gemv(l.qkv, nullptr, E.xcp, H, 1, l.attn_norm, qtts::ACT_F16, E.qkv, E.QKVD(), nullptr, 0, qtts::EPI_STORE, nullptr, 0, nullptr);
+        qtts::AttnArgs aa{};
+        aa.q = E.qkv; aa.ldq = E.QKVD(); aa.kf = E.qkv + E.QD(); aa.vf = E.qkv + E.QD() + E.KD(); aa.ldkv = E.QKVD();
+        aa.f32_mode = 1; aa.n_heads = c.n_attention_heads; aa.n_kv_heads = c.n_key_value_heads;
+        aa.pos_static = 0; aa.scale = 1.0f / sqrtf(128.0f); aa.out = E.att; aa.ldo = E.QD(); aa.st = E.st;
+        qtts::k_attention<<<dim3(c.n_key_value_heads, 1), qtts::ATT_THREADS,
+                            qtts::attn_smem_bytes(1, c.n_attention_heads / c.n_key_value_heads), E.stream>>>(aa);
+        E.gemv(l.o, nullptr, E.att, E.QD(), 1, nullptr, qtts::ACT_F16, E.xcp, H, E.xcp, H, qtts::EPI_RESID, nullptr, 0, nullptr);
+        E.gemv(l.gate, &l.up, E.xcp, H, 1, l.ffn_norm, qtts::ACT_F16, E.hbuf, c.code_pred_intermediate_size, nullptr, 0,
+               qtts::EPI_SWIGLU, nullptr, 0, nullptr);
+        E.gemv(l.down, nullptr, E.hbuf, c.code_pred_intermediate_size, 1, nullptr, qtts::ACT_F32, E.xcp, H, E.xcp, H,
+               qtts::EPI_RESID, nullptr, 0, nullptr);
+    }
+    for (int g = 0; g < NG; ++g)
+        E.gemv(E.cp_head[g], nullptr, E.xcp, H, 1, nullptr, qtts::ACT_F16, E.cp_logits + (size_t) g * V1, V1, nullptr, 0,
+               qtts::EPI_STORE, nullptr, 0, nullptr);
+    cudaMemcpyAsync(logits_out, E.cp_logits, sizeof(float) * NG * V1, cudaMemcpyDeviceToHost, E.stream);
+    return E.sync("predict_codes") ? 1 : 0;
+}
+
+int32_t qtts_project_text(qtts_engine * h, const int32_t * toks, int32_t n, float * out) {
+    if (!h || !toks || !out) return 0;
+    ENG(h);
+    std::vector<float> v;
+    if (!E.project_text(toks, n, v)) return 0;
+    memcpy(out, v.data(), v.size() * 4);
+    return 1;
+}
+
+int32_t qtts_lookup_embedding_rows(qtts_engine * h, int32_t table, const int32_t * ids, int32_t n, float * out) {
+    if (!h || !ids || !out) return 0;
+    ENG(h);
+    std::vector<float> v;
+    if (!E.lookup(table, ids, n, v)) return 0;
+    memcpy(out, v.data(), v.size() * 4);
+    return 1;
+}
+
+int32_t qtts_generate_begin(qtts_engine * h, const qtts_generate_params * p) {
+    if (!h || !p) return -1;
+    ENG(h);
+    if (p->max_len <= 0) { E.err = ""; E.sess = qtts::GenSession{}; return 0; }
+    return E.begin(p);
+}
+
+int32_t qtts_run_frames(qtts_engine * h, int32_t n, int32_t * codes_out) {
+    if (!h) return -1;
+    ENG(h);
+    return E.run_frames(n, codes_out);
+}
+
+int32_t qtts_generate(qtts_engine * h, const qtts_generate_params * p, qtts_frame_callback on_frame, void * user,
+                      int32_t * codes_out, int32_t * n_frames_out) {
+    if (!h || !p) return 0;
+    ENG(h);
+    if (n_frames_out) *n_frames_out = 0;
+    if (p->max_len <= 0) return 1;
+    const int NCB = E.cfg.n_codebooks;
+    if (E.begin(p) < 0) return 0;
+    std::vector<int32_t> out;
+    out.reserve((size_t) p->max_len * NCB);
+    std::vector<int32_t> chunk;
+    std::vector<std::vector<int32_t>> rep;
+    int run = 0, run_start = 0, emitted = 0;
+    bool stop = false, eos = false;
+    const int CH = 16;
+    while (!stop && emitted < p->max_len) {
+        chunk.resize((size_t) CH * NCB);
+        const int got = E.run_frames(std::min(CH, p->max_len - emitted), chunk.data());
+        if (got < 0) return 0;
+        for (int f = 0; f < got && !stop; ++f) {
+            const int32_t * fc = chunk.data() + (size_t) f * NCB;
+            out.insert(out.end(), fc, fc + NCB);
+            const int frame = emitted++;
+            if (on_frame && !on_frame(fc, NCB, frame, user)) { stop = true; break; }
+            // repetition-loop detection (src/tts_transformer.cpp:3217-3254)
+            if (p->rep_loop_detect) rep.emplace_back(fc, fc + NCB);
+            const size_t nf = rep.size();
+            bool is_rep = false;
+            for (int back = 1; back <= 6 && !is_rep && (size_t) back < nf; ++back) {
+                int match = 0;
+                for (int cb = 0; cb < NCB; ++cb) if (rep[nf - 1][cb] == rep[nf - 1 - back][cb]) ++match;
+                if (match >= 10) is_rep = true;
+            }
+            if (is_rep) { if (run == 0) run_start = (int)(nf - 1); ++run; } else run = 0;
+            if (run >= 5) {
+                fprintf(stderr, "  Repetition loop detected at frame %d, truncating %d frames\n", (int)(nf - 1), run);
+                out.resize((size_t) run_start * NCB);
+                stop = true;
+            }
+        }
+        if (E.sess.done) { eos = true; break; }
+        if (got == 0) break;
+    }
+    // attention rows: one per talker step the reference would have run
+    if (E.attn_dump) {
+        const size_t keep = eos && !stop ? (size_t) emitted : (size_t) std::max(0, emitted - 1);
+        if (E.attn_rows.size() > keep) E.attn_rows.resize(keep);
+    }
+    const int n = (int)(out.size() / NCB);
+    if (codes_out) memcpy(codes_out, out.data(), out.size() * sizeof(int32_t));
+    if (n_frames_out) *n_frames_out = n;
+    E.sess.active = false;
+    return 1;
+}
+
+void qtts_set_seed(qtts_engine * h, uint64_t s) { if (h) reinterpret_cast<Engine *>(h)->seed = s; }
+
+int32_t qtts_set_debug_logits(qtts_engine * h, float * tl, float * cl, int32_t cap) {
+    if (!h) return 0;
+    Engine & E = *reinterpret_cast<Engine *>(h);
+    E.h_dbg_t = tl; E.h_dbg_cp = cl; E.h_dbg_cap = cap > 0 ? cap : 0;
+    return 1;
+}
+
+int32_t qtts_set_attn_dump(qtts_engine * h, int32_t enabled, int32_t layer) {
+    if (!h) return 0;
+    Engine & E = *reinterpret_cast<Engine *>(h);
+    if (layer < 0 || layer >= E.cfg.n_layers) { E.err = "attn dump layer out of range"; return 0; }
+    E.attn_dump = enabled != 0;
+    E.attn_layer = layer;
+    E.graph_ok = false;
+    return 1;
+}
+
+int32_t qtts_attn_rows(const qtts_engine * h) { return h ? (int32_t) reinterpret_cast<const Engine *>(h)->attn_rows.size() : 0; }
+
+int32_t qtts_attn_row(const qtts_engine * h, int32_t r, float * out, int32_t cap) {
+    if (!h) return -1;
+    const Engine & E = *reinterpret_cast<const Engine *>(h);
+    if (r < 0 || r >= (int) E.attn_rows.size()) return -1;
+    const auto & row = E.attn_rows[r];
+    if (out) memcpy(out, row.data(), sizeof(float) * std::min<size_t>(row.size(), (size_t) std::max(cap, 0)));
+    return (int32_t) row.size();
+}
+
+// Runs up to n frames of the active generation eagerly (no graph) with CUDA
+// events around every launch; out[class] = {launches, total ms, algorithmic bytes}.
+int32_t qtts_profile_frames(qtts_engine * h, int32_t n, qtts_kernel_stats * out, int32_t n_classes) {
+    if (!h || !out) return -1;
+    ENG(h);
+    if (!E.sess.active) { E.err = "no active generation"; return -1; }
+    n = std::min(n, E.sess.max_len - E.sess.produced);
+    E.profiling = true;
+    E.prof_evs.clear();
+    E.ev_used = 0;
+    bool ok = true;
+    for (int i = 0; i < n && ok; ++i) ok = E.enqueue_frame();
+    E.profiling = false;
+    qtts::DevState hs;
+    cudaMemcpyAsync(&hs, E.st, sizeof(hs), cudaMemcpyDeviceToHost, E.stream);
+    if (!ok || !E.sync("profile frames")) return -1;
+    for (int c = 0; c < n_classes; ++c) out[c] = qtts_kernel_stats{0, 0.0f, 0.0};
+    for (auto & p : E.prof_evs) {
+        if (p.cls >= n_classes) continue;
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, p.a, p.b);
+        out[p.cls].launches += 1;
+        out[p.cls].total_ms += ms;
+        out[p.cls].bytes += p.bytes;
+    }
+    const int got = hs.n_out - E.sess.produced;
+    E.sess.produced = hs.n_out;
+    E.sess.done = hs.done != 0;
+    return got;
+}
+
+int32_t qtts_get_timing(const qtts_engine * h, qtts_timing * out) {
+    if (!h || !out) return 0;
+    *out = reinterpret_cast<const Engine *>(h)->timing;
+    return 1;
+}
+
+}  // extern "C"

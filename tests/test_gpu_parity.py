@@ -1,0 +1,221 @@
+"""GPU parity: the B200 engine (through its C ABI) against the CPU oracle.
+
+Contract: greedy codec tokens identical to the
+reference path except at recorded near-ties (top-2 logit gap < 1e-3); logits
+within max-abs 2e-2 (F16) / 5e-2 (Q8_0); per-block Q8_0 int8 dots bit-exact.
+Tie handling: the oracle replays the engine's codes and counts a divergence as
+a mismatch unless the oracle's own top-2 gap there is below TIE_TOL.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import gguf
+from conftest import icl_inputs, text_ids
+from oracle import Oracle, quantize_q8_0, uniform01
+
+pytestmark = pytest.mark.gpu
+
+TIE_TOL = 1e-3
+LOGIT_TOL = {"f16": 2e-2, "q8": 5e-2}
+
+
+@pytest.fixture(scope="module")
+def eng_tiny(qtts, tiny_f16):
+    return qtts.Engine(tiny_f16, 0)
+
+
+@pytest.fixture(scope="module")
+def eng_tiny_q8(qtts, tiny_q8):
+    return qtts.Engine(tiny_q8, 0)
+
+
+# ---------------------------------------------------------------- kernels
+@pytest.mark.parametrize("rows,cols,nv", [(4096, 1024, 1), (1024, 3072, 1), (3072, 1024, 2), (333, 256, 8), (64, 2048, 3)])
+def test_gemv_f16_matches_fp64(qtts, rows, cols, nv):
+    from qtts_b200.engine import op_gemv
+    rng = np.random.default_rng(rows + cols)
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float16)
+    x = rng.standard_normal((nv, cols)).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+    for norm, act32 in [(None, False), (g, False), (None, True)]:
+        y = op_gemv(w, 1, rows, cols, x, norm_gain=norm, act_f32=act32)
+        xs = x.astype(np.float64)
+        if norm is not None:
+            ms = (x.astype(np.float64) ** 2).mean(axis=1, keepdims=True).astype(np.float32)
+            xs = (x * (np.float32(1) / np.sqrt(ms + np.float32(1e-6))) * norm).astype(np.float64)
+        if not act32:
+            xs = xs.astype(np.float32).astype(np.float16).astype(np.float64)
+        ref = xs @ w.astype(np.float64).T
+        assert np.abs(y - ref).max() < 2e-5 * max(1.0, np.abs(ref).max())
+
+
+@pytest.mark.parametrize("rows,cols,nv", [(4096, 1024, 1), (1024, 3072, 2), (100, 512, 8)])
+def test_gemv_q8_block_dots_bit_exact(qtts, rows, cols, nv):
+    from qtts_b200.engine import op_gemv
+    rng = np.random.default_rng(rows * 7 + cols)
+    wf = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    wq = gguf.quants.quantize(wf, gguf.GGMLQuantizationType.Q8_0)       # reference converter's quantiser
+    x = rng.standard_normal((nv, cols)).astype(np.float32) * rng.uniform(0.01, 5.0, (nv, 1)).astype(np.float32)
+    y, bd = op_gemv(wq, 8, rows, cols, x, want_block_dots=True)
+    nb = cols // 32
+    qw = wq.reshape(rows, nb, 34)[:, :, 2:].copy().view(np.int8).astype(np.int64)
+    dw = wq.reshape(rows, nb, 34)[:, :, :2].copy().view(np.float16).astype(np.float64)[:, :, 0]
+    for v in range(nv):
+        qa, da = quantize_q8_0(x[v])          # quantize_row_q8_0_ref semantics
+        qa = qa.reshape(nb, 32).astype(np.int64)
+        exact = np.einsum("rbj,bj->rb", qw, qa)
+        assert np.array_equal(bd[v], exact), "per-block int8 dots must be bit-exact"
+        ref = (exact * dw * da.view(np.float16).astype(np.float64)[None, :]).sum(axis=1)
+        assert np.abs(y[v] - ref).max() < 1e-5 * max(1.0, np.abs(ref).max())
+
+
+def test_sampler_rules_match_oracle(qtts):
+    from qtts_b200.engine import op_sample
+    L = Oracle.lib()
+    import ctypes as C
+    rng = np.random.default_rng(9)
+    # argmax: first index wins; suppression [V-1024, V) except EOS; presence penalty; EOS bias ramp
+    lg = rng.standard_normal(3072).astype(np.float32)
+    lg[100] = lg[200] = 9.0
+    assert op_sample(lg, 0, suppress_start=2048) == 100
+    lg2 = lg.copy(); lg2[2500] = 50.0
+    assert op_sample(lg2, 0, suppress_start=2048) == 100          # suppressed
+    pres = np.zeros(3072, np.int32); pres[100] = 1
+    assert op_sample(lg, 0, rep_penalty=1.05, presence=pres, suppress_start=2048) == 200
+    assert op_sample(lg, 0, eos_bias=20.0, suppress_start=2048) == 2150
+    assert op_sample(lg, 0, eos_bias=0.0, target_frames=1, frame=300, suppress_start=2048) in (100, 2150)
+    # sampled: same draw as the oracle's inverse-CDF rule
+    for trial in range(40):
+        lg = rng.standard_normal(2048).astype(np.float32) * 2
+        if trial % 5 == 0:
+            lg[::7] = 1.5                                            # many ties at the top-k threshold
+        k = [0, 50, 7, 1][trial % 4]
+        got = op_sample(lg, 3, temperature=0.9, top_k=k, seed=11, frame=trial)
+        u = uniform01(11, trial, 3)
+        want = L.orc_sample(lg.copy().ctypes.data_as(C.POINTER(C.c_float)), 2048, 0.9, k, u)
+        assert got == want, (trial, got, want)
+
+
+# ---------------------------------------------------------------- forward passes
+@pytest.mark.parametrize("which", ["f16", "q8"])
+def test_prefill_and_step_logits(which, request):
+    path = request.getfixturevalue("tiny_f16" if which == "f16" else "tiny_q8")
+    eng = request.getfixturevalue("eng_tiny" if which == "f16" else "eng_tiny_q8")
+    o = Oracle(path)
+    rng = np.random.default_rng(12)
+    rows = (rng.standard_normal((13, 256)) * 0.1).astype(np.float32)
+    eng.init_kv_cache(64)
+    o.init_kv(64)
+    he, le = eng.forward_prefill(rows, 0)
+    ho, lo = o.forward_prefill(rows, 0)
+    assert np.abs(le - lo).max() < 1e-3 and np.abs(he - ho).max() < 1e-3
+    step = (rng.standard_normal(256) * 0.1).astype(np.float32)
+    le2, he2 = eng.forward_step(step, 13)
+    lo2, ho2 = o.forward_step(step, 13)
+    assert np.abs(le2 - lo2).max() < 1e-3 and np.abs(he2 - ho2).max() < 1e-3
+    ce = eng.predict_codes_autoregressive(he2, 77, 0.0, 0)
+    co, cpl = o.predict_codes(ho2, 77)
+    first = np.nonzero(ce != co)[0]
+    if first.size:
+        g = first[0]
+        assert cpl[g][co[g]] - cpl[g][ce[g]] < TIE_TOL
+
+
+def _check_follow(o, eng_out, tag, **kw):
+    r = o.generate(follow=eng_out["codes"], want_logits=True, tie_tol=TIE_TOL, **kw)
+    assert r["n_mismatch"] == 0, (tag, r)
+    assert r["n_frames"] == eng_out["n_frames"], (tag, r["n_frames"], eng_out["n_frames"])
+    return r
+
+
+@pytest.mark.parametrize("which", ["f16", "q8"])
+def test_generate_greedy_token_parity(which, request):
+    path = request.getfixturevalue("tiny_f16" if which == "f16" else "tiny_q8")
+    eng = request.getfixturevalue("eng_tiny" if which == "f16" else "eng_tiny_q8")
+    o = Oracle(path)
+    rng = np.random.default_rng(21)
+    text = text_ids(rng, 24)
+    spk = np.zeros(256, np.float32)
+    kw = dict(speaker=spk, rep_penalty=1.05, temperature=0.0, top_k=0, eos_bias=-1e9)
+    e = eng.generate(text, 24, want_logits=True, **kw)
+    assert e["n_frames"] == 24
+    r = _check_follow(o, e, which, text=text, max_len=24, **kw)
+    n = e["n_frames"]
+    assert np.abs(e["talker_logits"][:n] - r["talker_logits"][:n]).max() < LOGIT_TOL[which]
+    assert np.abs(e["cp_logits"][:n] - r["cp_logits"][:n]).max() < LOGIT_TOL[which]
+
+
+def test_generate_icl_and_instruct(eng_tiny, tiny_f16):
+    o = Oracle(tiny_f16)
+    rng = np.random.default_rng(22)
+    tgt, ref, codes, _ = icl_inputs(rng, 20, n_target_text=40)
+    spk = rng.standard_normal(256).astype(np.float32)
+    kw = dict(speaker=spk, ref_text=ref, ref_codes=codes, eos_bias=-1e9)
+    e = eng_tiny.generate(tgt, 12, **kw)
+    _check_follow(o, e, "icl", text=tgt, max_len=12, **kw)
+    ins = text_ids(rng, 7)
+    kw2 = dict(speaker=None, instruct=ins, language_id=-1, eos_bias=-1e9)
+    e2 = eng_tiny.generate(tgt, 6, **kw2)
+    _check_follow(o, e2, "instruct", text=tgt, max_len=6, **kw2)
+
+
+def test_generate_sampled_reproducible(eng_tiny, tiny_f16):
+    o = Oracle(tiny_f16)
+    rng = np.random.default_rng(23)
+    text = text_ids(rng, 30)
+    kw = dict(speaker=np.zeros(256, np.float32), temperature=0.9, top_k=50, rep_penalty=1.05, seed=1234, eos_bias=-1e9)
+    a = eng_tiny.generate(text, 16, **kw)
+    b = eng_tiny.generate(text, 16, **kw)
+    assert np.array_equal(a["codes"], b["codes"])
+    r = o.generate(text=text, max_len=16, follow=a["codes"], tie_tol=1e-6, **kw)
+    assert r["n_mismatch"] == 0, r
+
+
+def test_stop_conditions(eng_tiny, tiny_f16):
+    o = Oracle(tiny_f16)
+    rng = np.random.default_rng(24)
+    text = text_ids(rng, 20)
+    # EOS forced on the first frame
+    assert eng_tiny.generate(text, 8, eos_bias=1e9)["n_frames"] == 0
+    # callback abort keeps the frames up to and including the aborting one
+    seen = []
+    e = eng_tiny.generate(text, 30, eos_bias=-1e9, on_frame=lambda codes, f: (seen.append(f), f < 4)[1])
+    assert e["n_frames"] == 5 and seen == [0, 1, 2, 3, 4]
+    # repetition-loop detection: same decision as the oracle on the same codes
+    e2 = eng_tiny.generate(text, 40, eos_bias=-1e9, rep_penalty=1.0, rep_loop_detect=True)
+    r2 = o.generate(text, 40, eos_bias=-1e9, rep_penalty=1.0, rep_loop_detect=True)
+    if r2["n_mismatch"] == 0 and np.array_equal(r2["codes"][: e2["n_frames"]], e2["codes"]):
+        assert r2["n_frames"] == e2["n_frames"]
+
+
+# ---------------------------------------------------------------- full-size (0.6B layout)
+def test_full_f16_config1_shape(qtts, full_f16):
+    """BASELINE config 1 shape: ICL, 55 reference frames -> 64 prefill, greedy."""
+    eng = qtts.Engine(full_f16, 0)
+    o = Oracle(full_f16)
+    rng = np.random.default_rng(101)
+    tgt, ref, codes, spk = icl_inputs(rng, 55)
+    kw = dict(speaker=spk, ref_text=ref, ref_codes=codes, rep_penalty=1.05, temperature=0.0, top_k=0, eos_bias=-1e9)
+    e = eng.generate(tgt, 12, want_logits=True, **kw)
+    r = _check_follow(o, e, "full-f16", text=tgt, max_len=12, **kw)
+    assert r["prefill_len"] == 64
+    n = e["n_frames"]
+    assert np.abs(e["talker_logits"][:n] - r["talker_logits"][:n]).max() < LOGIT_TOL["f16"]
+    eng.close()
+
+
+def test_full_q8_config2_shape(qtts, full_q8):
+    """BASELINE config 2 shape: Q8_0, 119 reference frames -> 128 prefill."""
+    eng = qtts.Engine(full_q8, 0)
+    o = Oracle(full_q8)
+    rng = np.random.default_rng(102)
+    tgt, ref, codes, spk = icl_inputs(rng, 119)
+    kw = dict(speaker=spk, ref_text=ref, ref_codes=codes, rep_penalty=1.05, temperature=0.0, top_k=0, eos_bias=-1e9)
+    e = eng.generate(tgt, 8, want_logits=True, **kw)
+    r = _check_follow(o, e, "full-q8", text=tgt, max_len=8, **kw)
+    assert r["prefill_len"] == 128
+    n = e["n_frames"]
+    assert np.abs(e["talker_logits"][:n] - r["talker_logits"][:n]).max() < LOGIT_TOL["q8"]
+    eng.close()
