@@ -144,8 +144,8 @@ def _traffic_per_launch():
 
 def cpu_frames_per_s(path: str, n_ref_prefill: int, budget_s: float, max_frames: int):
     """The CPU oracle port on all host cores: frames after a prefill of the same length."""
-    from oracle import Oracle
-    cores = os.cpu_count() or 1
+    from oracle import Oracle, available_cpus
+    cores = available_cpus()
     o = Oracle(path, threads=cores)
     H = o.cfg["hidden"]
     rng = np.random.default_rng(7)

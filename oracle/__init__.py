@@ -15,6 +15,28 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB = os.path.join(_HERE, "liboracle.so")
+# OpenMP threads spin only briefly before sleeping between parallel regions: the
+# oracle shares the host with the GPU driver thread and other processes.
+os.environ.setdefault("GOMP_SPINCOUNT", "20000")
+
+
+def available_cpus() -> int:
+    """CPUs this process may actually use (affinity and cgroup CPU quota)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        quota, period = open("/sys/fs/cgroup/cpu.max").read().split()[:2]
+        if quota != "max":
+            n = min(n, max(1, int(int(quota) / int(period))))
+    except (OSError, ValueError):
+        pass
+    try:
+        q = int(open("/sys/fs/cgroup/cpu/cpu.cfs_quota_us").read())
+        p = int(open("/sys/fs/cgroup/cpu/cpu.cfs_period_us").read())
+        if q > 0:
+            n = min(n, max(1, q // p))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
 
 
 def build(force: bool = False) -> str:
@@ -95,8 +117,7 @@ class Oracle:
 
     def __init__(self, path: str, threads: int | None = None):
         L = self.lib()
-        if threads:
-            L.orc_set_threads(int(threads))
+        L.orc_set_threads(int(threads) if threads else available_cpus())
         err = C.create_string_buffer(512)
         self.h = L.orc_load(path.encode(), err, 512)
         if not self.h:

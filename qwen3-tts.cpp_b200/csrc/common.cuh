@@ -14,11 +14,12 @@ namespace qtts {
 enum WType : int { W_F32 = 0, W_F16 = 1, W_Q8_0 = 8 };
 
 // ggml layout matrix: rows x cols, row-major (ne0 = cols contiguous).
+// Trivially constructible (it is copied into shared memory); zero-initialise with {}.
 struct DMat {
-    int type = W_F16;
-    int rows = 0, cols = 0;
-    const void * w = nullptr;        // F16 [rows][cols] or int8 quants [rows][cols]
-    const __half * d = nullptr;      // Q8_0 block scales [rows][cols/32]
+    int type;
+    int rows, cols;
+    const void * w;        // F16 [rows][cols] or int8 quants [rows][cols]
+    const __half * d;      // Q8_0 block scales [rows][cols/32]
 };
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -18,7 +18,7 @@
 //     step, with no host round trip inside a frame.
 #include "../../include/qwen3tts_b200.h"
 #include "gguf.hpp"
-#include "kernels.cuh"
+#include "persistent.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -112,6 +112,18 @@ struct Engine {
     int launches = 0;
     int launches_per_frame = 0;
     GenSession sess;
+    // persistent frame kernel (one cooperative launch per run of frames)
+    bool use_persistent = true;
+    std::vector<POp> prog;
+    POp * d_prog = nullptr;
+    size_t prog_cap = 0;
+    size_t prog_smem = 0;
+    unsigned * d_flags = nullptr;
+    int * d_err = nullptr;
+    bool prog_ok = false;
+    int pf0[16];
+    int n_pf0 = 0;
+    double pf_lead_bytes = 24.0 * 1024 * 1024;
     // eager profiling: CUDA events around every launch, accumulated per kernel class
     bool profiling = false;
     struct ProfEv { int cls; double bytes; cudaEvent_t a, b; };
@@ -144,12 +156,12 @@ struct Engine {
         if (graph) { cudaGraphExecDestroy(graph); graph = nullptr; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
                          cp_logits, hidden, hid_rows, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
-                         dbg_t, dbg_cp, d_attn};
+                         dbg_t, dbg_cp, d_attn, d_prog, d_flags, d_err};
         for (void * p : ptrs) if (p) cudaFree(p);
         wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
         x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = hid_rows = tmp_a = tmp_b = nullptr;
         d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
-        dbg_t = dbg_cp = nullptr; d_attn = nullptr;
+        dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_prog = nullptr; d_flags = nullptr; d_err = nullptr;
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         ev0 = ev1 = nullptr;
@@ -175,6 +187,11 @@ struct Engine {
     bool enqueue_talker_step(const int * pos_ptr, int pos_static, const int * done, bool with_dump);
     bool enqueue_frame();
     bool capture_graph();
+    GemvArgs make_gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
+                       float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
+                       const int * done, int * ncta_out, size_t * smem_out);
+    bool build_program();
+    bool launch_persistent(int n);
     bool sync(const char * what);
 
     // ------------------------------------------------------------ API pieces
@@ -268,6 +285,8 @@ bool Engine::load(const char * path, int device) {
     if (c.hidden_size % 256 || c.intermediate_size % 32 || c.code_pred_intermediate_size % 32 || c.text_embd_dim % 32) {
         err = "hidden/ffn/text widths must be multiples of 256/32/32"; return false;
     }
+    if (const char * m = getenv("QTTS_FRAME_MODE")) use_persistent = strcmp(m, "graph") != 0;
+    if (const char * lb = getenv("QTTS_PF_LEAD_MB")) pf_lead_bytes = atof(lb) * 1024.0 * 1024.0;
     if (!upload_weights(g)) return false;
     if (!alloc_activations()) return false;
     if (!init_cp_kv(16)) return false;
@@ -482,7 +501,7 @@ bool Engine::init_kv(int ctx) {
     QCHECK(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) std::max<size_t>(smem, 48 * 1024)));
     n_ctx = ctx;
     n_used = 0;
-    graph_ok = false;
+    graph_ok = false; prog_ok = false;
     return true;
 }
 
@@ -500,7 +519,7 @@ bool Engine::init_cp_kv(int ctx) {
     QCHECK(cudaMalloc(&rope_cp, t.size() * sizeof(float2)));
     QCHECK(cudaMemcpy(rope_cp, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
     cp_ctx = ctx;
-    graph_ok = false;
+    graph_ok = false; prog_ok = false;
     return true;
 }
 
@@ -512,9 +531,9 @@ bool Engine::sync(const char * what) {
 }
 
 // ---------------------------------------------------------------- launches
-bool Engine::gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
-                  float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
-                  const int * done) {
+GemvArgs Engine::make_gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm,
+                           int act, float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out,
+                           int ldxn, const int * done, int * ncta_out, size_t * smem_out) {
     GemvArgs a{};
     a.A = A;
     if (B) a.B = *B;
@@ -530,7 +549,18 @@ bool Engine::gemv(const DMat & A, const DMat * B, const float * xin, int ldx, in
     ks = std::max(1, std::min(ks, std::max(1, nchunk / 32)));
     a.kslices = ks;
     const int NVt = nv == 1 ? 1 : nv == 2 ? 2 : 8;
-    const size_t smem = gemv_smem_bytes(A.type, A.cols, NVt, rpc, ks);
+    *ncta_out = ncta;
+    *smem_out = gemv_smem_bytes(A.type, A.cols, NVt, rpc, ks);
+    return a;
+}
+
+bool Engine::gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
+                  float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
+                  const int * done) {
+    int ncta;
+    size_t smem;
+    GemvArgs a = make_gemv(A, B, xin, ldx, nv, norm, act, y, ldy, resid, ldr, epi, xn_out, ldxn, done, &ncta, &smem);
+    const int NVt = nv == 1 ? 1 : nv == 2 ? 2 : 8;
     if (nv > QTTS_MAX_NV || smem > 200 * 1024) { err = "gemv shape too large"; return false; }
     const double wb = A.type == W_F16 ? (double) A.rows * A.cols * 2.0 : (double) A.rows * A.cols * 34.0 / 32.0;
     prof_begin(KC_GEMV, wb * (B ? 2.0 : 1.0) + 4.0 * nv * ((double) A.cols + A.rows));
@@ -663,6 +693,146 @@ bool Engine::capture_graph() {
     cudaGraphDestroy(gr);
     if (ce != cudaSuccess) { err = std::string("graph instantiate: ") + cudaGetErrorString(ce); return false; }
     graph_ok = true;
+    return true;
+}
+
+// ---------------------------------------------------------------- persistent frame program
+// The same op sequence as enqueue_frame(), as descriptors for k_frame_persistent.
+bool Engine::build_program() {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size, V1 = c.code_pred_vocab_size, NG = c.n_codebooks - 1;
+    const int NH = c.n_attention_heads, NKV = c.n_key_value_heads, G = NH / NKV;
+    prog.clear();
+    prog_smem = 0;
+    auto push_gemv = [&](const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
+                         float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
+                         int barrier) {
+        POp op{};
+        op.type = P_GEMV; op.barrier = barrier; op.nv = nv;
+        int ncta; size_t sm;
+        op.g = make_gemv(A, B, xin, ldx, nv, norm, act, y, ldy, resid, ldr, epi, xn_out, ldxn, nullptr, &ncta, &sm);
+        prog_smem = std::max(prog_smem, sm);
+        prog.push_back(op);
+    };
+    auto push_layers = [&](std::vector<LayerW> & Ls, __half * kbase, __half * vbase, int ctx, const float2 * rope,
+                           float * X, int M, const int * pos_ptr, int pos_static, bool f32, int ffn, float * dump,
+                           int dump_layer) {
+        const size_t layer_elems = (size_t) ctx * NKV * QTTS_HD;
+        for (size_t il = 0; il < Ls.size(); ++il) {
+            LayerW & l = Ls[il];
+            push_gemv(l.qkv, nullptr, X, H, M, l.attn_norm, ACT_F16, qkv, QKVD(), nullptr, 0, EPI_STORE, nullptr, 0, 1);
+            POp op{};
+            op.type = P_ATTN; op.barrier = 1;
+            FusedAttn & a = op.a;
+            a.qkv = qkv; a.ldq = QKVD(); a.n_heads = NH; a.n_kv_heads = NKV;
+            a.q_norm = l.q_norm; a.k_norm = l.k_norm; a.eps = c.rms_norm_eps; a.rope = rope;
+            a.kc = kbase + il * layer_elems; a.vc = vbase + il * layer_elems;
+            a.pos_ptr = pos_ptr; a.pos_static = pos_static; a.M = M; a.f32_mode = f32 ? 1 : 0;
+            a.scale = 1.0f / sqrtf((float) QTTS_HD); a.out = att; a.ldo = QD();
+            a.dump = ((int) il == dump_layer) ? dump : nullptr; a.dump_stride = ctx;
+            prog_smem = std::max(prog_smem, fused_attn_smem(f32 ? M : ctx, G, M));
+            prog.push_back(op);
+            push_gemv(l.o, nullptr, att, QD(), M, nullptr, ACT_F16, X, H, X, H, EPI_RESID, nullptr, 0, 1);
+            push_gemv(l.gate, &l.up, X, H, M, l.ffn_norm, ACT_F16, hbuf, ffn, nullptr, 0, EPI_SWIGLU, nullptr, 0, 1);
+            push_gemv(l.down, nullptr, hbuf, ffn, M, nullptr, ACT_F32, X, H, X, H, EPI_RESID, nullptr, 0, 1);
+        }
+    };
+    auto push_sample = [&](const float * lg, int V, int cb) {
+        POp op{};
+        op.type = P_SAMPLE; op.barrier = 1; op.logits = lg; op.V = V; op.cb = cb;
+        prog.push_back(op);
+    };
+    InputArgs ia{};
+    ia.H = H; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
+    ia.trailing = trailing; ia.pad = pad; ia.st = st; ia.n_cb = c.n_codebooks;
+    auto push_input = [&](int mode, int g, float * out) {
+        POp op{};
+        op.type = P_INPUT; op.barrier = 1;
+        op.in = ia; op.in.mode = mode; op.in.g = g; op.in.out = out;
+        prog.push_back(op);
+    };
+    push_sample(logits, c.codec_vocab_size, 0);
+    push_input(IN_CP_PREFILL, 0, xcp);
+    push_layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 2, nullptr, 0, true, c.code_pred_intermediate_size, nullptr, -1);
+    push_gemv(cp_head[0], nullptr, xcp + H, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE, nullptr, 0, 1);
+    push_sample(cp_logits, V1, 1);
+    for (int gstep = 1; gstep < NG; ++gstep) {
+        push_input(IN_CP_STEP, gstep, xcp);
+        push_layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 1, nullptr, gstep + 1, false, c.code_pred_intermediate_size,
+                    nullptr, -1);
+        push_gemv(cp_head[gstep], nullptr, xcp, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE,
+                  nullptr, 0, 1);
+        push_sample(cp_logits, V1, gstep + 1);
+    }
+    push_input(IN_TALKER, 0, x);
+    push_layers(L, kc, vc, n_ctx, rope_t, x, 1, &st->pos, 0, false, c.intermediate_size, attn_dump ? d_attn : nullptr,
+                attn_layer);
+    push_gemv(codec_head, nullptr, x, H, 1, out_norm, ACT_F16, logits, c.codec_vocab_size, nullptr, 0, EPI_STORE,
+              hidden, H, 0);
+    {
+        POp op{};
+        op.type = P_FRAME_END; op.barrier = 1;
+        prog.push_back(op);
+    }
+
+    // L2 prefetch schedule: each GEMV's weights are prefetched by the op that
+    // runs pf_lead_bytes earlier in the (cyclic) weight stream.
+    auto wbytes = [](const GemvArgs & g) {
+        auto one = [](const DMat & m) -> double {
+            if (!m.w) return 0.0;
+            return m.type == W_F16 ? (double) m.rows * m.cols * 2.0 : (double) m.rows * m.cols * 34.0 / 32.0;
+        };
+        return one(g.A) + one(g.B);
+    };
+    std::vector<int> gi;
+    std::vector<double> pb, sz;
+    double T = 0.0;
+    for (size_t i = 0; i < prog.size(); ++i)
+        if (prog[i].type == P_GEMV) { gi.push_back((int) i); pb.push_back(T); sz.push_back(wbytes(prog[i].g)); T += sz.back(); }
+    const double lead = std::min(pf_lead_bytes, T * 0.5);
+    n_pf0 = 0;
+    for (size_t k = 0; k < gi.size(); ++k) {
+        if (pb[k] < lead && n_pf0 < 16) pf0[n_pf0++] = gi[k];
+        double t = pb[k] - lead;
+        if (t < 0) t += T;
+        size_t m = std::upper_bound(pb.begin(), pb.end(), t) - pb.begin();
+        m = m == 0 ? 0 : m - 1;
+        for (size_t site = gi[m]; site < prog.size(); ++site) {
+            if (prog[site].n_pf < 6) { prog[site].pf[prog[site].n_pf++] = gi[k]; break; }
+        }
+    }
+    // upload
+    if (prog.size() > prog_cap) {
+        if (d_prog) cudaFree(d_prog);
+        prog_cap = prog.size();
+        QCHECK(cudaMalloc(&d_prog, sizeof(POp) * prog_cap));
+    }
+    QCHECK(cudaMemcpy(d_prog, prog.data(), sizeof(POp) * prog.size(), cudaMemcpyHostToDevice));
+    if (!d_flags) {
+        QCHECK(cudaMalloc(&d_flags, sizeof(unsigned) * 1024));
+        QCHECK(cudaMalloc(&d_err, sizeof(int)));
+    }
+    if (prog_smem + 8 * 1024 > 227 * 1024) { err = "persistent kernel shared memory too large"; return false; }
+    QCHECK(cudaFuncSetAttribute(k_frame_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) prog_smem));
+    int nb = 0;
+    QCHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_frame_persistent, PK_THREADS, prog_smem));
+    if (nb < 1) { err = "persistent frame kernel does not fit on an SM"; return false; }
+    prog_ok = true;
+    return true;
+}
+
+bool Engine::launch_persistent(int n) {
+    PersistentArgs pa{};
+    pa.ops = d_prog; pa.n_ops = (int) prog.size(); pa.n_frames = n; pa.st = st; pa.sp = sp;
+    pa.out_codes = d_codes; pa.out_cap = codes_cap; pa.flags = d_flags; pa.err = d_err;
+    pa.n_pf0 = n_pf0;
+    for (int k = 0; k < n_pf0; ++k) pa.pf0[k] = pf0[k];
+    QCHECK(cudaMemsetAsync(d_flags, 0, sizeof(unsigned) * n_sm, stream));
+    QCHECK(cudaMemsetAsync(d_err, 0, sizeof(int), stream));
+    void * args[] = {&pa};
+    QCHECK(cudaLaunchCooperativeKernel((const void *) k_frame_persistent, dim3(n_sm), dim3(PK_THREADS), args,
+                                       prog_smem, stream));
+    ++launches;
     return true;
 }
 
@@ -890,13 +1060,13 @@ int Engine::begin(const qtts_generate_params * p) {
         if (d_codes) cudaFree(d_codes);
         codes_cap = std::max(p->max_len, 256);
         if (cudaMalloc(&d_codes, sizeof(int) * codes_cap * c.n_codebooks) != cudaSuccess) { err = "alloc codes"; return -1; }
-        graph_ok = false;
+        graph_ok = false; prog_ok = false;
     }
     if (std::max(tlen, 1) > trailing_cap) {
         if (trailing) cudaFree(trailing);
         trailing_cap = std::max(tlen, 256);
         if (cudaMalloc(&trailing, sizeof(float) * trailing_cap * H) != cudaSuccess) { err = "alloc trailing"; return -1; }
-        graph_ok = false;
+        graph_ok = false; prog_ok = false;
     }
     if (attn_dump) {
         const size_t need = (size_t) p->max_len * c.n_attention_heads * n_ctx;
@@ -904,7 +1074,7 @@ int Engine::begin(const qtts_generate_params * p) {
             if (d_attn) cudaFree(d_attn);
             attn_cap = need;
             if (cudaMalloc(&d_attn, sizeof(float) * attn_cap) != cudaSuccess) { err = "alloc attn dump"; return -1; }
-            graph_ok = false;
+            graph_ok = false; prog_ok = false;
         }
     }
     if (h_dbg_cap > 0 && (h_dbg_t || h_dbg_cp)) {
@@ -940,7 +1110,11 @@ int Engine::begin(const qtts_generate_params * p) {
         err = "upload state"; return -1;
     }
     if (!sync("generate setup")) return -1;
-    if (!graph_ok && !capture_graph()) return -1;
+    if (use_persistent) {
+        if (!prog_ok && !build_program()) return -1;
+        if (!graph_ok) { launches = 0; graph_ok = false; }
+        launches_per_frame = 1;
+    } else if (!graph_ok && !capture_graph()) return -1;
     sess.active = true;
     sess.max_len = p->max_len;
     sess.prefill_len = plen;
@@ -958,12 +1132,21 @@ int Engine::run_frames(int n, int32_t * codes_out) {
     n = std::min(n, sess.max_len - sess.produced);
     if (n <= 0) return 0;
     if (cudaEventRecord(ev0, stream) != cudaSuccess) { err = "event"; return -1; }
-    for (int i = 0; i < n; ++i)
-        if (cudaGraphLaunch(graph, stream) != cudaSuccess) { err = "graph launch failed"; return -1; }
+    if (use_persistent) {
+        if (!launch_persistent(n)) return -1;
+    } else {
+        for (int i = 0; i < n; ++i)
+            if (cudaGraphLaunch(graph, stream) != cudaSuccess) { err = "graph launch failed"; return -1; }
+    }
     if (cudaEventRecord(ev1, stream) != cudaSuccess) { err = "event"; return -1; }
     DevState hs;
+    int kerr = 0;
     if (cudaMemcpyAsync(&hs, st, sizeof(hs), cudaMemcpyDeviceToHost, stream) != cudaSuccess) { err = "state readback"; return -1; }
+    if (use_persistent && cudaMemcpyAsync(&kerr, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) {
+        err = "error flag readback"; return -1;
+    }
     if (!sync("frame loop")) return -1;
+    if (kerr) { err = "persistent frame kernel: grid barrier timed out"; sess.active = false; return -1; }
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, ev0, ev1);
     timing.frames_ms += ms;
@@ -1377,7 +1560,7 @@ int32_t qtts_set_attn_dump(qtts_engine * h, int32_t enabled, int32_t layer) {
     if (layer < 0 || layer >= E.cfg.n_layers) { E.err = "attn dump layer out of range"; return 0; }
     E.attn_dump = enabled != 0;
     E.attn_layer = layer;
-    E.graph_ok = false;
+    E.graph_ok = false; E.prog_ok = false;
     return 1;
 }
 

@@ -49,7 +49,7 @@ __host__ __device__ inline size_t gemv_smem_bytes(int type, int cols, int nv, in
 }
 
 template <int NV>
-__device__ __forceinline__ void gemv_prologue(const GemvArgs & a, float * xs, int8_t * qa, float * da) {
+__device__ __forceinline__ void gemv_prologue(const GemvArgs & a, float * xs, int8_t * qa, float * da, const int cta) {
     __shared__ double red[32];
     const int cols = a.A.cols;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -72,7 +72,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs & a, float * xs, in
             const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
             for (int c = tid; c < cols; c += nt) xr[c] = __fmul_rn(__fmul_rn(xr[c], scale), a.norm_g[c]);
         }
-        if (a.xn_out && blockIdx.x == 0)
+        if (a.xn_out && cta == 0)
             for (int c = tid; c < cols; c += nt) a.xn_out[(size_t) v * a.ldxn + c] = xr[c];
     }
     __syncthreads();
@@ -111,18 +111,16 @@ __device__ __forceinline__ void gemv_store(const GemvArgs & a, int r, int v, flo
 // partial dots go to shared memory and are summed in slice order, so the
 // result depends only on (rows, grid, kslices), never on scheduling.
 template <int NV>
-__global__ void __launch_bounds__(QTTS_WARPS * 32) k_gemv(GemvArgs a) {
-    if (a.done && *a.done) return;
+__device__ __forceinline__ void gemv_body(const GemvArgs & a, const int cta, const int ncta, uint8_t * smem_raw) {
     const int cols = a.A.cols, rows = a.A.rows;
-    const int rpc = (rows + gridDim.x - 1) / gridDim.x;
-    const int r0 = blockIdx.x * rpc, r1 = min(rows, r0 + rpc);
+    const int rpc = (rows + ncta - 1) / ncta;
+    const int r0 = cta * rpc, r1 = min(rows, r0 + rpc);
     if (r0 >= r1) return;
-    extern __shared__ __align__(16) uint8_t smem_raw[];
     float * xs = reinterpret_cast<float *>(smem_raw);
     int8_t * qa = reinterpret_cast<int8_t *>(xs + (size_t) NV * cols);
     float * da = reinterpret_cast<float *>(qa + (size_t)(a.A.type == W_Q8_0 ? NV * cols : 0));
     float * part = da + (a.A.type == W_Q8_0 ? NV * (cols / 32) : 0);
-    gemv_prologue<NV>(a, xs, qa, da);
+    gemv_prologue<NV>(a, xs, qa, da, cta);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const bool dual = a.B.w != nullptr;
@@ -274,6 +272,13 @@ __global__ void __launch_bounds__(QTTS_WARPS * 32) k_gemv(GemvArgs a) {
         }
         gemv_store<NV>(a, r0 + rl, v, sa, sb);
     }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(QTTS_WARPS * 32) k_gemv(GemvArgs a) {
+    if (a.done && *a.done) return;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    gemv_body<NV>(a, blockIdx.x, gridDim.x, smem_raw);
 }
 
 // ---------------------------------------------------------------------------
@@ -528,10 +533,12 @@ struct SampleParams {
 };
 
 constexpr int SAMPLE_THREADS = 1024;
-constexpr int SAMPLE_PER_T = 4;   // vocab <= 4096
+constexpr int SAMPLE_PER_T = 4;   // vocab <= SAMPLE_THREADS * SAMPLE_PER_T = 4096
+constexpr int SAMPLE_MAX_V = 4096;
 
 // k-th largest key among valid elements (radix select, 8 bits per pass).
-__device__ uint32_t block_kth_largest(const uint32_t key[SAMPLE_PER_T], const bool valid[SAMPLE_PER_T], int k) {
+template <int PT>
+__device__ uint32_t block_kth_largest(const uint32_t * key, const bool * valid, int k) {
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_prefix, s_k;
     const int tid = threadIdx.x;
@@ -542,7 +549,7 @@ __device__ uint32_t block_kth_largest(const uint32_t key[SAMPLE_PER_T], const bo
         const uint32_t prefix = s_prefix;
         const uint32_t hi = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
 #pragma unroll
-        for (int e = 0; e < SAMPLE_PER_T; ++e)
+        for (int e = 0; e < PT; ++e)
             if (valid[e] && ((key[e] & hi) == (prefix & hi))) atomicAdd(&hist[(key[e] >> shift) & 255u], 1u);
         __syncthreads();
         if (tid < 32) {
@@ -605,23 +612,22 @@ __device__ double block_exscan_d(double v, double * total) {
     return wsum[warp] + (incl - v);
 }
 
+// One sampling decision by the whole block; every thread returns the token.
 // cb == 0: codebook-0 rules of generate() (suppression, presence penalty, EOS
-// bias ramp, EOS stop).  cb >= 1: code-predictor sample_or_argmax.
-__global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits, int V, int cb, DevState * st,
-                                                           const SampleParams * sp, int * out_codes, int out_cap) {
-    if (st->done) return;
+// bias ramp).  cb >= 1: code-predictor sample_or_argmax.  PT elements per thread
+// (contiguous), blockDim.x * PT >= V.
+template <int PT>
+__device__ int sample_body(const float * logits, int V, int cb, const DevState * st, const SampleParams & P, int frame) {
     __shared__ float redf[32];
     __shared__ double redd[32];
     __shared__ unsigned long long best;
     __shared__ int pick;
     const int tid = threadIdx.x;
-    const SampleParams P = *sp;
-    const int frame = st->frame;
-    float l[SAMPLE_PER_T];
-    bool valid[SAMPLE_PER_T];
+    float l[PT];
+    bool valid[PT];
 #pragma unroll
-    for (int e = 0; e < SAMPLE_PER_T; ++e) {
-        const int i = tid * SAMPLE_PER_T + e;
+    for (int e = 0; e < PT; ++e) {
+        const int i = tid * PT + e;
         valid[e] = i < V;
         l[e] = valid[e] ? logits[i] : -INFINITY;
         if (valid[e] && P.record_logits && frame < P.dbg_cap) {
@@ -632,8 +638,8 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits,
     float eb = 0.0f;
     if (cb == 0) {
 #pragma unroll
-        for (int e = 0; e < SAMPLE_PER_T; ++e) {
-            const int i = tid * SAMPLE_PER_T + e;
+        for (int e = 0; e < PT; ++e) {
+            const int i = tid * PT + e;
             if (!valid[e]) continue;
             if (i >= P.suppress_start && i != P.eos_id) l[e] = -INFINITY;
             if (P.rep_penalty != 1.0f && (st->presence[i >> 5] >> (i & 31) & 1u))
@@ -649,18 +655,19 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits,
     if (P.temperature <= 0.0f) {
         if (cb == 0 && eb != 0.0f) {
 #pragma unroll
-            for (int e = 0; e < SAMPLE_PER_T; ++e)
-                if (valid[e] && tid * SAMPLE_PER_T + e == P.eos_id) l[e] = __fadd_rn(l[e], eb);
+            for (int e = 0; e < PT; ++e)
+                if (valid[e] && tid * PT + e == P.eos_id) l[e] = __fadd_rn(l[e], eb);
         }
         // first index of the maximum (strict >): key = (orderable value, ~index)
         unsigned long long mine = 0ull;
 #pragma unroll
-        for (int e = 0; e < SAMPLE_PER_T; ++e) {
+        for (int e = 0; e < PT; ++e) {
             if (!valid[e] || l[e] != l[e]) continue;
             const unsigned long long k = ((unsigned long long) f2key(l[e]) << 32) |
-                                         (unsigned long long)(0xFFFFFFFFu - (uint32_t)(tid * SAMPLE_PER_T + e));
+                                         (unsigned long long)(0xFFFFFFFFu - (uint32_t)(tid * PT + e));
             mine = k > mine ? k : mine;
         }
+        __syncthreads();
         if (tid == 0) best = 0ull;
         __syncthreads();
         atomicMax(&best, mine);
@@ -668,36 +675,36 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits,
         tok = best == 0ull ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
     } else {
 #pragma unroll
-        for (int e = 0; e < SAMPLE_PER_T; ++e) {
+        for (int e = 0; e < PT; ++e) {
             if (!valid[e]) continue;
             l[e] = __fdiv_rn(l[e], P.temperature);
-            if (cb == 0 && eb != 0.0f && tid * SAMPLE_PER_T + e == P.eos_id) l[e] = __fadd_rn(l[e], eb);
+            if (cb == 0 && eb != 0.0f && tid * PT + e == P.eos_id) l[e] = __fadd_rn(l[e], eb);
         }
         if (P.top_k > 0 && P.top_k < V) {
-            uint32_t key[SAMPLE_PER_T];
+            uint32_t key[PT];
 #pragma unroll
-            for (int e = 0; e < SAMPLE_PER_T; ++e) key[e] = f2key(l[e]);
-            const float thr = key2f(block_kth_largest(key, valid, P.top_k));
+            for (int e = 0; e < PT; ++e) key[e] = f2key(l[e]);
+            const float thr = key2f(block_kth_largest<PT>(key, valid, P.top_k));
 #pragma unroll
-            for (int e = 0; e < SAMPLE_PER_T; ++e)
+            for (int e = 0; e < PT; ++e)
                 if (valid[e] && l[e] < thr) l[e] = -INFINITY;
         }
         float mx = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < SAMPLE_PER_T; ++e) if (valid[e]) mx = fmaxf(mx, l[e]);
+        for (int e = 0; e < PT; ++e) if (valid[e]) mx = fmaxf(mx, l[e]);
         mx = block_max(mx, redf);
-        float ev[SAMPLE_PER_T];
+        float ev[PT];
         double s = 0.0;
 #pragma unroll
-        for (int e = 0; e < SAMPLE_PER_T; ++e) {
+        for (int e = 0; e < PT; ++e) {
             ev[e] = valid[e] ? expf(__fsub_rn(l[e], mx)) : 0.0f;
             s += (double) ev[e];
         }
         const double sum = block_sum_d(s, redd);
-        float p[SAMPLE_PER_T];
+        float p[PT];
         double loc = 0.0;
 #pragma unroll
-        for (int e = 0; e < SAMPLE_PER_T; ++e) {
+        for (int e = 0; e < PT; ++e) {
             p[e] = valid[e] ? (float)((double) ev[e] / sum) : 0.0f;
             loc += (double) p[e];
         }
@@ -708,11 +715,11 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits,
         __syncthreads();
         int cand = 0x7fffffff, lastpos = -1;
 #pragma unroll
-        for (int e = 0; e < SAMPLE_PER_T; ++e) {
+        for (int e = 0; e < PT; ++e) {
             cum += (double) p[e];
             if (p[e] > 0.0f) {
-                lastpos = tid * SAMPLE_PER_T + e;
-                if (cum > target && cand == 0x7fffffff) cand = tid * SAMPLE_PER_T + e;
+                lastpos = tid * PT + e;
+                if (cum > target && cand == 0x7fffffff) cand = tid * PT + e;
             }
         }
         atomicMin(&pick, cand);
@@ -725,20 +732,34 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits,
             __syncthreads();
         }
         tok = pick < 0 ? 0 : pick;
+        __syncthreads();
     }
-    if (tid == 0) {
-        if (cb == 0) {
-            if (tok == P.eos_id) {
-                st->done = 1;
-            } else {
-                st->codes[0] = tok;
-                st->presence[tok >> 5] |= 1u << (tok & 31);
-            }
-        } else {
-            st->codes[cb] = tok;
+    return tok;
+}
+
+// Records a sampled token in the frame state (thread 0 only).
+__device__ __forceinline__ void sample_commit(int tok, int cb, DevState * st, const SampleParams & P, int * out_codes,
+                                              int out_cap, int frame) {
+    if (cb == 0) {
+        if (tok == P.eos_id) {
+            st->done = 1;
+            return;
         }
-        if (!(cb == 0 && tok == P.eos_id) && out_codes && frame < out_cap) out_codes[(size_t) frame * P.n_cb + cb] = tok;
+        st->codes[0] = tok;
+        st->presence[tok >> 5] |= 1u << (tok & 31);
+    } else {
+        st->codes[cb] = tok;
     }
+    if (out_codes && frame < out_cap) out_codes[(size_t) frame * P.n_cb + cb] = tok;
+}
+
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits, int V, int cb, DevState * st,
+                                                           const SampleParams * sp, int * out_codes, int out_cap) {
+    if (st->done) return;
+    const SampleParams P = *sp;
+    const int frame = st->frame;
+    const int tok = sample_body<SAMPLE_PER_T>(logits, V, cb, st, P, frame);
+    if (threadIdx.x == 0) sample_commit(tok, cb, st, P, out_codes, out_cap, frame);
 }
 
 // ---------------------------------------------------------------------------

@@ -36,8 +36,11 @@ def qtts():
 
 
 @pytest.fixture(scope="session")
-def model_dir(tmp_path_factory):
-    return str(tmp_path_factory.mktemp("models"))
+def model_dir():
+    """Seeded GGUFs are cached here (git- and gpurun-ignored); bench.py uses the same files."""
+    d = os.environ.get("QTTS_MODEL_DIR", os.path.join(ROOT, ".models"))
+    os.makedirs(d, exist_ok=True)
+    return d
 
 
 @pytest.fixture(scope="session")

@@ -103,7 +103,7 @@ def test_sampler_rules_match_oracle(qtts):
 def test_prefill_and_step_logits(which, request):
     path = request.getfixturevalue("tiny_f16" if which == "f16" else "tiny_q8")
     eng = request.getfixturevalue("eng_tiny" if which == "f16" else "eng_tiny_q8")
-    o = Oracle(path)
+    o = Oracle(path, threads=4)
     rng = np.random.default_rng(12)
     rows = (rng.standard_normal((13, 256)) * 0.1).astype(np.float32)
     eng.init_kv_cache(64)
@@ -134,7 +134,7 @@ def _check_follow(o, eng_out, tag, **kw):
 def test_generate_greedy_token_parity(which, request):
     path = request.getfixturevalue("tiny_f16" if which == "f16" else "tiny_q8")
     eng = request.getfixturevalue("eng_tiny" if which == "f16" else "eng_tiny_q8")
-    o = Oracle(path)
+    o = Oracle(path, threads=4)
     rng = np.random.default_rng(21)
     text = text_ids(rng, 24)
     spk = np.zeros(256, np.float32)
@@ -148,7 +148,7 @@ def test_generate_greedy_token_parity(which, request):
 
 
 def test_generate_icl_and_instruct(eng_tiny, tiny_f16):
-    o = Oracle(tiny_f16)
+    o = Oracle(tiny_f16, threads=4)
     rng = np.random.default_rng(22)
     tgt, ref, codes, _ = icl_inputs(rng, 20, n_target_text=40)
     spk = rng.standard_normal(256).astype(np.float32)
@@ -162,7 +162,7 @@ def test_generate_icl_and_instruct(eng_tiny, tiny_f16):
 
 
 def test_generate_sampled_reproducible(eng_tiny, tiny_f16):
-    o = Oracle(tiny_f16)
+    o = Oracle(tiny_f16, threads=4)
     rng = np.random.default_rng(23)
     text = text_ids(rng, 30)
     kw = dict(speaker=np.zeros(256, np.float32), temperature=0.9, top_k=50, rep_penalty=1.05, seed=1234, eos_bias=-1e9)
@@ -174,7 +174,7 @@ def test_generate_sampled_reproducible(eng_tiny, tiny_f16):
 
 
 def test_stop_conditions(eng_tiny, tiny_f16):
-    o = Oracle(tiny_f16)
+    o = Oracle(tiny_f16, threads=4)
     rng = np.random.default_rng(24)
     text = text_ids(rng, 20)
     # EOS forced on the first frame

@@ -33,7 +33,7 @@ def test_q8_0_quantiser_matches_gguf_py():
 
 
 def test_gguf_reader_rows_match_gguf_py(tiny_f16):
-    o = Oracle(tiny_f16)
+    o = Oracle(tiny_f16, threads=4)
     r = gguf.GGUFReader(tiny_f16)
     byname = {t.name: t for t in r.tensors}
     ids = np.array([0, 5, 2148, 2149, 3071], np.int32)
@@ -48,7 +48,7 @@ def test_gguf_reader_rows_match_gguf_py(tiny_f16):
 @pytest.mark.parametrize("which", ["tiny_f16", "tiny_q8"])
 def test_oracle_matches_numpy_statement(which, request):
     path = request.getfixturevalue(which)
-    o, npm = Oracle(path), NpModel(path)
+    o, npm = Oracle(path, threads=4), NpModel(path)
     rng = np.random.default_rng(3)
     rows = (rng.standard_normal((6, 256)) * 0.1).astype(np.float32)
     hid_o, lg_o = o.forward_prefill(rows)
@@ -110,7 +110,7 @@ PREFILL_LAYOUT = [
 
 
 def test_prefill_layout_matches_reference_token_types(tiny_f16):
-    o = Oracle(tiny_f16)
+    o = Oracle(tiny_f16, threads=4)
     rng = np.random.default_rng(4)
     text = text_ids(rng, 14)
     spk = rng.standard_normal(256).astype(np.float32)
@@ -133,7 +133,7 @@ def test_prefill_layout_matches_reference_token_types(tiny_f16):
 
 
 def test_icl_prefill_length(tiny_f16):
-    o = Oracle(tiny_f16)
+    o = Oracle(tiny_f16, threads=4)
     rng = np.random.default_rng(5)
     tgt, ref, codes, _ = icl_inputs(rng, 55)
     spk = rng.standard_normal(256).astype(np.float32)
@@ -155,7 +155,7 @@ def test_sampling_rules():
 
 
 def test_oracle_follow_self_and_eos(tiny_f16):
-    o = Oracle(tiny_f16)
+    o = Oracle(tiny_f16, threads=4)
     rng = np.random.default_rng(6)
     text = text_ids(rng, 20)
     a = o.generate(text, 6, eos_bias=-1e9)
