@@ -7,5 +7,5 @@ binding (engine.py) and the seeded-GGUF writer used for synthetic models
 (synth_gguf.py).  The directory name is not a Python identifier; load it with
 importlib (see tests/conftest.py).
 """
-from . import build, synth_gguf  # noqa: F401
+from . import build, scheduler, synth_gguf  # noqa: F401
 from .engine import Engine, exported_symbols, lib  # noqa: F401

@@ -21,7 +21,9 @@
 #include "persistent.cuh"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
+#include <thread>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -523,8 +525,24 @@ bool Engine::init_cp_kv(int ctx) {
     return true;
 }
 
+// Waits for the engine stream with a time limit (QTTS_SYNC_TIMEOUT_S, default
+// 300 s): a stream that never drains is reported as an error instead of
+// blocking the caller forever.
 bool Engine::sync(const char * what) {
-    cudaError_t e = cudaStreamSynchronize(stream);
+    static const double limit_s = [] {
+        const char * v = getenv("QTTS_SYNC_TIMEOUT_S");
+        return v && *v ? atof(v) : 300.0;
+    }();
+    const auto t0 = std::chrono::steady_clock::now();
+    cudaError_t e;
+    int spins = 0;
+    while ((e = cudaStreamQuery(stream)) == cudaErrorNotReady) {
+        if (++spins > 1000) std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit_s) {
+            err = std::string(what) + ": GPU work did not complete within the sync time limit";
+            return false;
+        }
+    }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { err = std::string(what) + ": " + cudaGetErrorString(e); return false; }
     return true;

@@ -426,10 +426,17 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
     __syncthreads();
 
     // scores: 8-lane groups, each lane 16 dims
+    // Every lane of a warp runs the same number of iterations (the 8-lane
+    // groups' shuffles use the full mask); out-of-range keys compute on zeros.
     const int sub = lane & 7, slot = lane >> 3;
-    for (int j = warp * 4 + slot; j < n; j += (ATT_THREADS / 32) * 4) {
+    for (int j0 = warp * 4; j0 < n; j0 += (ATT_THREADS / 32) * 4) {
+        const int j = j0 + slot;
+        const bool jv = j < n;
         float kv[16];
-        if (a.f32_mode) {
+        if (!jv) {
+#pragma unroll
+            for (int d = 0; d < 16; ++d) kv[d] = 0.0f;
+        } else if (a.f32_mode) {
             const float4 * kp = reinterpret_cast<const float4 *>(a.kf + (size_t) j * a.ldkv + g * QTTS_HD + sub * 16);
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
@@ -457,7 +464,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
             s += __shfl_xor_sync(0xffffffffu, s, 4);
             s += __shfl_xor_sync(0xffffffffu, s, 2);
             s += __shfl_xor_sync(0xffffffffu, s, 1);
-            if (sub == 0) sc[h * n + j] = __fmul_rn(s, a.scale);
+            if (sub == 0 && jv) sc[h * n + j] = __fmul_rn(s, a.scale);
         }
     }
     __syncthreads();

@@ -82,7 +82,7 @@ __device__ __forceinline__ bool grid_barrier(unsigned * flags, unsigned epoch, i
             for (int c = lane; c < (int) gridDim.x; c += 32)
                 if (ld_acquire_u32(flags + c) < epoch) mine = false;
             if (__all_sync(0xffffffffu, mine)) { ok = true; break; }
-            if (*(volatile int *) err) break;
+            if (__any_sync(0xffffffffu, *(volatile int *) err != 0)) break;   // warp-uniform exit
         }
         if (lane == 0) {
             if (!ok) atomicExch(err, 1);
@@ -169,11 +169,17 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
     }
     __syncthreads();
 
+    // uniform trip count per warp (full-mask shuffles below); out-of-range keys use zeros
     const int sub = lane & 7, slot = lane >> 3;
     const int nwarps = blockDim.x >> 5;
-    for (int j = warp * 4 + slot; j < n; j += nwarps * 4) {
+    for (int j0 = warp * 4; j0 < n; j0 += nwarps * 4) {
+        const int j = j0 + slot;
+        const bool jv = j < n;
         float kv[16];
-        if (a.f32_mode) {
+        if (!jv) {
+#pragma unroll
+            for (int d = 0; d < 16; ++d) kv[d] = 0.0f;
+        } else if (a.f32_mode) {
 #pragma unroll
             for (int d = 0; d < 16; ++d) kv[d] = ks[j * QTTS_HD + sub * 16 + d];
         } else {
@@ -197,7 +203,7 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
             s += __shfl_xor_sync(0xffffffffu, s, 4);
             s += __shfl_xor_sync(0xffffffffu, s, 2);
             s += __shfl_xor_sync(0xffffffffu, s, 1);
-            if (sub == 0) sc[h * n + j] = __fmul_rn(s, a.scale);
+            if (sub == 0 && jv) sc[h * n + j] = __fmul_rn(s, a.scale);
         }
     }
     __syncthreads();
