@@ -108,13 +108,17 @@ def test_prefill_and_step_logits(which, request):
     rows = (rng.standard_normal((13, 256)) * 0.1).astype(np.float32)
     eng.init_kv_cache(64)
     o.init_kv(64)
+    # F16: only reduction order differs (tight bound).  Q8_0: a 1-ulp difference in
+    # an activation can move one int8 quant of its block, so the bound is the
+    # north-star Q8_0 logit tolerance.
+    tol = 1e-3 if which == "f16" else LOGIT_TOL["q8"]
     he, le = eng.forward_prefill(rows, 0)
     ho, lo = o.forward_prefill(rows, 0)
-    assert np.abs(le - lo).max() < 1e-3 and np.abs(he - ho).max() < 1e-3
+    assert np.abs(le - lo).max() < tol and np.abs(he - ho).max() < tol
     step = (rng.standard_normal(256) * 0.1).astype(np.float32)
     le2, he2 = eng.forward_step(step, 13)
     lo2, ho2 = o.forward_step(step, 13)
-    assert np.abs(le2 - lo2).max() < 1e-3 and np.abs(he2 - ho2).max() < 1e-3
+    assert np.abs(le2 - lo2).max() < tol and np.abs(he2 - ho2).max() < tol
     ce = eng.predict_codes_autoregressive(he2, 77, 0.0, 0)
     co, cpl = o.predict_codes(ho2, 77)
     first = np.nonzero(ce != co)[0]
