@@ -173,6 +173,27 @@ int32_t qtts_op_gemv(int32_t device, int32_t wtype, const void * w, int32_t rows
 int32_t qtts_op_sample(int32_t device, const float * logits, int32_t V, int32_t cb, float temperature, int32_t top_k,
                        float rep_penalty, const int32_t * presence, float eos_bias, int32_t target_frames,
                        int32_t frame, int32_t eos_id, int32_t suppress_start, uint64_t seed);
+/* The same sampling decision as qtts_op_sample, for callers that cannot
+ * allocate device memory: a real-time streaming loop, where the device-wide
+ * synchronisation of a cudaMalloc/cudaFree pair per call would stall audio
+ * output, and host applications that own all device memory through their own
+ * pool and do not let libraries allocate.  This entry point has no
+ * counterpart in the reference.
+ * Inputs and the output are DEVICE pointers owned by the caller: logits [V],
+ * presence [V] (0/1, optional), token_out [1] (written on `stream`, which may be
+ * NULL for the default stream).  The sampler's state lives in a fixed 4 KiB
+ * __device__ array inside the library (every GPU that loads the library holds
+ * it until exit), so V is limited to 4096: larger vocabularies return -2 with
+ * a message on stderr.  No cudaMalloc, cudaFree or allocating routine is
+ * called.  The first call on a device looks up the array's device address
+ * (with that device current) and should happen before any stream capture.
+ * All calls share the array: the kernel clears the state it reads at every
+ * call, and calls that overlap on the GPU (concurrent streams) race.
+ * Returns 1 on a successful launch, 0 on invalid arguments or a CUDA error. */
+int32_t qtts_op_sample_noalloc(int32_t device, const float * logits, int32_t V, int32_t cb, float temperature,
+                               int32_t top_k, float rep_penalty, const int32_t * presence, float eos_bias,
+                               int32_t target_frames, int32_t frame, int32_t eos_id, int32_t suppress_start,
+                               uint64_t seed, int32_t * token_out, void * stream);
 
 #ifdef __cplusplus
 }

@@ -28,6 +28,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1310,6 +1311,78 @@ int32_t qtts_op_sample(int32_t device, const float * logits_in, int32_t V, int32
     if (dst) cudaFree(dst);
     if (dsp) cudaFree(dsp);
     return tok;
+}
+
+// ---------------------------------------------------------------- sampler without allocation
+// Fixed device scratch for qtts_op_sample_noalloc: the sampler's frame state
+// (presence set, stop flag, codes) lives here instead of in memory allocated per
+// call.  Every GPU that loads the library holds this array until exit.
+#define QTTS_NOALLOC_SCRATCH_BYTES 4096
+#define QTTS_NOALLOC_MAX_VOCAB 4096
+static __device__ __align__(256) unsigned char g_sample_scratch[QTTS_NOALLOC_SCRATCH_BYTES];
+static_assert(sizeof(qtts::DevState) <= QTTS_NOALLOC_SCRATCH_BYTES, "sampler state exceeds the fixed scratch");
+
+namespace qtts {
+// Same decision as k_sample, with the frame state in the caller-independent
+// scratch.  Clears the state first: the array keeps the previous call's bytes.
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_sample_noalloc(const float * logits, int V, int cb, int frame,
+                                                                   DevState * st, SampleParams P,
+                                                                   const int32_t * presence, int32_t * token_out) {
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) {
+        uint32_t bits = 0;
+        if (presence)
+            for (int b = 0; b < 32; ++b) {
+                const int t = i * 32 + b;
+                if (t < V && presence[t]) bits |= 1u << b;
+            }
+        st->presence[i] = bits;
+    }
+    if (threadIdx.x < QTTS_MAX_CB) st->codes[threadIdx.x] = 0;
+    if (threadIdx.x == 0) { st->done = 0; st->frame = frame; st->pos = 0; st->n_out = 0; st->n_trailing = 0; }
+    __syncthreads();
+    const int tok = sample_body<SAMPLE_PER_T>(logits, V, cb, st, P, frame);
+    if (threadIdx.x == 0) {
+        sample_commit(tok, cb, st, P, nullptr, 0, frame);
+        *token_out = (cb == 0 && st->done) ? P.eos_id : st->codes[cb];
+    }
+}
+}  // namespace qtts
+
+// Device address of g_sample_scratch, resolved once per device (host code must
+// not pass the symbol itself: on the host it is only a stand-in).
+static std::mutex g_scratch_mu;
+static void * g_scratch_ptr[64];
+
+int32_t qtts_op_sample_noalloc(int32_t device, const float * logits, int32_t V, int32_t cb, float temperature,
+                               int32_t top_k, float rep_penalty, const int32_t * presence, float eos_bias,
+                               int32_t target_frames, int32_t frame, int32_t eos_id, int32_t suppress_start,
+                               uint64_t seed, int32_t * token_out, void * stream) {
+    using namespace qtts;
+    if (V > QTTS_NOALLOC_MAX_VOCAB) {
+        fprintf(stderr, "qtts_op_sample_noalloc: vocabulary %d exceeds the fixed scratch limit of %d tokens\n", V,
+                QTTS_NOALLOC_MAX_VOCAB);
+        return -2;
+    }
+    if (!logits || !token_out || V <= 0 || cb < 0 || cb >= QTTS_MAX_CB || device < 0 || device >= 64) return 0;
+    if (cudaSetDevice(device) != cudaSuccess) return 0;
+    void * scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        if (!g_scratch_ptr[device]) {
+            if (cudaGetSymbolAddress(&g_scratch_ptr[device], g_sample_scratch) != cudaSuccess) {
+                g_scratch_ptr[device] = nullptr;
+                return 0;
+            }
+        }
+        scratch = g_scratch_ptr[device];
+    }
+    SampleParams P{};
+    P.temperature = temperature; P.top_k = top_k; P.rep_penalty = rep_penalty; P.eos_bias = eos_bias;
+    P.target_frames = target_frames; P.eos_id = eos_id; P.suppress_start = suppress_start; P.seed = seed;
+    P.n_cb = QTTS_MAX_CB;
+    k_sample_noalloc<<<1, SAMPLE_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+        logits, V, cb, frame, static_cast<DevState *>(scratch), P, presence, token_out);
+    return cudaGetLastError() == cudaSuccess ? 1 : 0;
 }
 
 qtts_engine * qtts_create(const char * gguf_path, int32_t device) {

@@ -111,6 +111,9 @@ def lib():
                                      C.c_float, C.c_int32, _f32p, _i32p]),
         "qtts_op_sample": (C.c_int32, [C.c_int32, _f32p, C.c_int32, C.c_int32, C.c_float, C.c_int32, C.c_float, _i32p,
                                        C.c_float, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_uint64]),
+        "qtts_op_sample_noalloc": (C.c_int32, [C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_float, C.c_int32,
+                                               C.c_float, C.c_void_p, C.c_float, C.c_int32, C.c_int32, C.c_int32,
+                                               C.c_int32, C.c_uint64, C.c_void_p, C.c_void_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
