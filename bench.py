@@ -128,13 +128,13 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _traffic_per_launch():
-    """DRAM bytes per k_gemv launch from the committed ncu summary, if present."""
-    p = os.path.join(ROOT, "profiles", "k_gemv_frame_ncu.md")
+def _profile_figure(fname: str, key: str):
+    """A figure from a committed ncu summary under profiles/ (`key: value` line)."""
+    p = os.path.join(ROOT, "profiles", fname)
     if not os.path.exists(p):
         return None
     for line in open(p):
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        if line.strip().startswith(key + ":"):
             try:
                 return float(line.split(":", 1)[1].strip().split()[0])
             except ValueError:
@@ -277,12 +277,26 @@ def main():
 
     peak, peak_kind = _peaks()
     g = prof["gemv"]
-    achieved = (g["bytes"] / g["launches"]) / (g["ms"] / g["launches"] / 1e3) / 1e9 if g["launches"] else None
+    gemv_gbs = (g["bytes"] / g["launches"]) / (g["ms"] / g["launches"] / 1e3) / 1e9 if g["launches"] else None
     frame_ms = ms_max / K
     kv_pos_mean = plen + W + K / 2.0
     frame_bytes = WEIGHT_BYTES[args.config] + KV_TALKER_PER_POS * kv_pos_mean + KV_CP_PER_POS * 135
-    traffic = _traffic_per_launch()
     prof_total = sum(prof[c]["ms"] for c in ("gemv", "attention", "sample", "other"))
+    persistent = launches_per_frame == 1
+    if persistent:
+        # one cooperative launch runs all K frames: bytes per launch = K frames of weights + KV
+        kernel = "k_frame_persistent (one cooperative launch per run of K frames)"
+        bytes_per_launch = frame_bytes * K
+        achieved = bytes_per_launch / (ms_max / 1e3) / 1e9
+        tpf = _profile_figure(f"k_frame_persistent_{args.config}.md", "dram_bytes_per_frame")
+        traffic = tpf * K if tpf else None
+        launches_per_frame_k = 1.0 / K
+    else:
+        kernel = "k_gemv (all GEMV launches of a frame, eager replay)"
+        bytes_per_launch = g["bytes"] / max(g["launches"], 1)
+        achieved = gemv_gbs
+        traffic = _profile_figure(f"k_gemv_{args.config}.md", "dram_bytes_per_launch")
+        launches_per_frame_k = g["launches"] / max(prof["frames"], 1)
     line = {
         "metric": METRIC, "value": world * K / (ms_max / 1e3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": frame_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -291,21 +305,22 @@ def main():
         "config": {"workload": cfg["workload"], "batch_per_gpu": 1, "prefill": plen, "frames_timed": K,
                    "parallelism": f"independent utterance per GPU x{world}",
                    "l2": "inputs larger than L2 (3.3 GB of weights streamed per frame), no flush"},
-        "roofline": {"bound": "hbm", "kernel": "k_gemv (all GEMV launches of a frame, eager replay)",
+        "roofline": {"bound": "hbm", "kernel": kernel,
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
-                     "bytes_per_launch": g["bytes"] / max(g["launches"], 1),
-                     "launches_per_frame": g["launches"] / max(prof["frames"], 1),
-                     "share_of_frame": g["ms"] / prof_total if prof_total else None,
+                     "bytes_per_launch": bytes_per_launch,
+                     "launches_per_frame": launches_per_frame_k,
+                     "frame_algorithmic_bytes": frame_bytes,
                      "frame_algorithmic_gbs": frame_bytes / (frame_ms / 1e3) / 1e9,
-                     "frame_frac": frame_bytes / (frame_ms / 1e3) / 1e9 / peak},
+                     "eager_gemv_gbs": gemv_gbs,
+                     "eager_gemv_share": g["ms"] / prof_total if prof_total else None},
         "kernel_classes": {c: {"launches_per_frame": prof[c]["launches"] / max(prof["frames"], 1),
                                "ms_per_frame": prof[c]["ms"] / max(prof["frames"], 1)}
                            for c in ("gemv", "attention", "sample", "other")},
         "e2e": {"value": world * K / t_e, "unit": UNIT, "h2d_bytes_per_step": h2d / K, "d2h_bytes_per_step": d2h / K,
                 "includes": "qtts_generate: prompt upload, prefill, K frames, codes download"},
-        "gpu_launches": launches_per_frame * K,
+        "gpu_launches": 1 if persistent else launches_per_frame * K,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:

@@ -69,7 +69,7 @@ class GenResult(C.Structure):
     _fields_ = [
         ("n_frames", C.c_int32), ("prefill_len", C.c_int32), ("n_mismatch", C.c_int32),
         ("n_ties", C.c_int32), ("first_mismatch", C.c_int32), ("truncated", C.c_int32),
-        ("max_tie_gap", C.c_float), ("min_decision_gap", C.c_float),
+        ("max_tie_gap", C.c_float), ("min_decision_gap", C.c_float), ("max_mismatch_gap", C.c_float),
     ]
 
 
@@ -232,7 +232,8 @@ class Oracle:
         n = r.n_frames
         out = dict(codes=codes[:n].copy(), n_frames=n, prefill_len=r.prefill_len, n_mismatch=r.n_mismatch,
                    n_ties=r.n_ties, first_mismatch=r.first_mismatch, truncated=bool(r.truncated),
-                   max_tie_gap=r.max_tie_gap, min_decision_gap=r.min_decision_gap)
+                   max_tie_gap=r.max_tie_gap, min_decision_gap=r.min_decision_gap,
+                   max_mismatch_gap=r.max_mismatch_gap)
         if want_logits:
             out["talker_logits"] = tl[:max(n, 1)]
             out["cp_logits"] = cl[:n]

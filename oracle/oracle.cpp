@@ -444,6 +444,15 @@ static double uniform01(uint64_t seed, uint32_t frame, uint32_t cb) {
     return (double)(bits >> 11) * (1.0 / 9007199254740992.0);
 }
 
+// A sampled decision is near a tie when the uniform draw lies within 1e-6 of a
+// bucket edge of the inverse CDF, or when the top-k threshold is within 1e-3 of
+// the best excluded logit (the kept set can then differ by reduction order).
+// Returned on the greedy gap scale: the smaller of (edge distance scaled to the
+// 1e-3 tie threshold) and the threshold gap.
+static double sampled_tie_measure(double edge_gap, double topk_gap) {
+    return std::min(edge_gap * 1e3, topk_gap);
+}
+
 static int32_t argmax(const float * d, int n) {  // src/tts_transformer.cpp:2583-2593
     int32_t mi = 0; float mv = d[0];
     for (int i = 1; i < n; ++i) if (d[i] > mv) { mv = d[i]; mi = i; }
@@ -454,13 +463,20 @@ static int32_t argmax(const float * d, int n) {  // src/tts_transformer.cpp:2583
 // draw.  Returns the token; *cdf_gap receives the distance of the draw from
 // the nearest bucket edge (for the near-tie bookkeeping).
 static int32_t sample_tok(float * lg, int n, float temperature, int top_k, double u,
-                          bool scale_temp, float eos_bias, int eos_id, double * edge_gap) {
+                          bool scale_temp, float eos_bias, int eos_id, double * edge_gap,
+                          double * topk_gap = nullptr) {
     if (scale_temp) for (int i = 0; i < n; ++i) lg[i] /= temperature;
     if (eos_bias != 0.0f && eos_id >= 0) lg[eos_id] += eos_bias;
+    if (topk_gap) *topk_gap = 1e30;
     if (top_k > 0 && top_k < n) {
         std::vector<float> sv(lg, lg + n);
         std::nth_element(sv.begin(), sv.begin() + (top_k - 1), sv.end(), std::greater<float>());
         const float thr = sv[top_k - 1];
+        if (topk_gap) {   // distance from the threshold to the best excluded logit
+            float below = -INFINITY;
+            for (int i = 0; i < n; ++i) if (lg[i] < thr) below = std::max(below, lg[i]);
+            *topk_gap = (double) thr - (double) below;
+        }
         for (int i = 0; i < n; ++i) if (lg[i] < thr) lg[i] = -INFINITY;
     }
     float mx = *std::max_element(lg, lg + n);
@@ -509,6 +525,7 @@ struct orc_gen_args {
 struct orc_gen_result {
     int32_t n_frames; int32_t prefill_len; int32_t n_mismatch; int32_t n_ties;
     int32_t first_mismatch; int32_t truncated; float max_tie_gap; float min_decision_gap;
+    float max_mismatch_gap;
 };
 
 void orc_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
@@ -701,13 +718,14 @@ static void predict_codes(Model & m, const float * hidden, int cb0, float temper
         }
         cp_pass(m, g, rows.data(), lg.data());
         if (logits_dump) memcpy(logits_dump + (size_t) g * V, lg.data(), V * 4);
-        int pick; double gap = 1e30;
+        int pick; double gap = 1e30, kgap = 1e30;
         std::vector<float> work(lg);
         if (temperature <= 0.0f) {
             pick = argmax(work.data(), V);
         } else {
             pick = sample_tok(work.data(), V, temperature, top_k, uniform01(seed, frame, (uint32_t)(g + 1)),
-                              true, 0.0f, -1, &gap);
+                              true, 0.0f, -1, &gap, &kgap);
+            gap = sampled_tie_measure(gap, kgap);
         }
         if (temperature <= 0.0f) {  // record the top-2 gap of this decision
             float best = -INFINITY, second = -INFINITY;
@@ -719,7 +737,11 @@ static void predict_codes(Model & m, const float * hidden, int cb0, float temper
         if (follow && follow[g] != pick) {
             float d = temperature <= 0.0f ? work[pick] - work[follow[g]] : (float) gap;
             if (d <= tie_tol) { res->n_ties++; res->max_tie_gap = std::max(res->max_tie_gap, d); }
-            else { if (res->first_mismatch < 0) res->first_mismatch = *dec_index; res->n_mismatch++; }
+            else {
+                if (res->first_mismatch < 0) res->first_mismatch = *dec_index;
+                res->n_mismatch++;
+                res->max_mismatch_gap = std::max(res->max_mismatch_gap, d);
+            }
             pick = follow[g];
         }
         (*dec_index)++;
@@ -902,13 +924,14 @@ int orc_generate(void * h, const orc_gen_args * a, orc_gen_result * r) {
             eb += 0.1f * (float)(frame - a->target_frames);
             if (eb > 6.0f) eb = 6.0f;
         }
-        int next; double gap = 1e30;
+        int next; double gap = 1e30, kgap = 1e30;
         if (a->temperature <= 0.0f) {
             if (eb != 0.0f) logits[c.codec_eos] += eb;
             next = argmax(logits.data(), V);
         } else {
             next = sample_tok(logits.data(), V, a->temperature, a->top_k, uniform01(a->seed, (uint32_t) frame, 0u),
-                              true, eb, c.codec_eos, &gap);
+                              true, eb, c.codec_eos, &gap, &kgap);
+            gap = sampled_tie_measure(gap, kgap);
         }
         const int32_t * fol = nullptr;
         if (a->follow) {
@@ -917,7 +940,11 @@ int orc_generate(void * h, const orc_gen_args * a, orc_gen_result * r) {
             if (want != next) {
                 float d = a->temperature <= 0.0f ? logits[next] - logits[want] : (float) gap;
                 if (d <= a->tie_tol) { r->n_ties++; r->max_tie_gap = std::max(r->max_tie_gap, d); }
-                else { if (r->first_mismatch < 0) r->first_mismatch = dec; r->n_mismatch++; }
+                else {
+                    if (r->first_mismatch < 0) r->first_mismatch = dec;
+                    r->n_mismatch++;
+                    r->max_mismatch_gap = std::max(r->max_mismatch_gap, d);
+                }
                 next = want;
             }
         }

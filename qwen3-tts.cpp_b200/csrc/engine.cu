@@ -126,6 +126,8 @@ struct Engine {
     bool prog_ok = false;
     int pf0[16];
     int n_pf0 = 0;
+    int pk_first[2] = {0, 0};
+    size_t pk_wbuf = 0, pk_dyn = 0;
     double pf_lead_bytes = 24.0 * 1024 * 1024;
     // eager profiling: CUDA events around every launch, accumulated per kernel class
     bool profiling = false;
@@ -794,30 +796,67 @@ bool Engine::build_program() {
         prog.push_back(op);
     }
 
+    // Weight staging.  The k-th GEMV of the frame reads shared-memory buffer
+    // k & 1; its row slice is copied there by the op that follows GEMV k-2
+    // (cyclically; the first two are copied at launch start), i.e. about one op
+    // ahead and before the grid barrier that precedes it.  Every frame has an
+    // even number of GEMVs (4L + 1 + 15 (4L_cp + 1)), so the buffer parity of a
+    // GEMV is the same in every frame.
+    std::vector<int> gi;
+    for (size_t i = 0; i < prog.size(); ++i)
+        if (prog[i].type == P_GEMV) gi.push_back((int) i);
+    const int m = (int) gi.size();
+    if (m < 2 || (m & 1)) { err = "unexpected GEMV count in the frame program"; return false; }
+    for (int k = 0; k < m; ++k) {
+        prog[gi[k]].slot = k & 1;
+        const int prev = gi[(k - 2 + m) % m];
+        POp & site = prog[(prev + 1) % prog.size()];
+        site.issue = 1;
+        site.issue_slot = k & 1;
+        site.iA = prog[gi[k]].g.A;
+        site.iB = prog[gi[k]].g.B;
+    }
+    pk_first[0] = gi[0];
+    pk_first[1] = gi[1];
+    // Shared memory: two weight buffers sized for the largest per-CTA slice,
+    // then the work area (GEMV activations / attention scores).
+    size_t wb = 0;
+    for (int k = 0; k < m; ++k) {
+        const GemvArgs & g = prog[gi[k]].g;
+        const int rpc = (g.A.rows + n_sm - 1) / n_sm;
+        const size_t es = g.A.type == W_F16 ? 2 : 1;
+        const size_t per = (size_t) rpc * g.A.cols * es + (g.A.type == W_Q8_0 ? (size_t) rpc * (g.A.cols / 32) * 2 : 0);
+        wb = std::max(wb, per * (g.B.w ? 2 : 1));
+    }
+    pk_wbuf = (wb + 127) & ~(size_t) 127;
+
     // L2 prefetch schedule: each GEMV's weights are prefetched by the op that
     // runs pf_lead_bytes earlier in the (cyclic) weight stream.
     auto wbytes = [](const GemvArgs & g) {
-        auto one = [](const DMat & m) -> double {
-            if (!m.w) return 0.0;
-            return m.type == W_F16 ? (double) m.rows * m.cols * 2.0 : (double) m.rows * m.cols * 34.0 / 32.0;
+        auto one = [](const DMat & mm) -> double {
+            if (!mm.w) return 0.0;
+            return mm.type == W_F16 ? (double) mm.rows * mm.cols * 2.0 : (double) mm.rows * mm.cols * 34.0 / 32.0;
         };
         return one(g.A) + one(g.B);
     };
-    std::vector<int> gi;
     std::vector<double> pb, sz;
     double T = 0.0;
-    for (size_t i = 0; i < prog.size(); ++i)
-        if (prog[i].type == P_GEMV) { gi.push_back((int) i); pb.push_back(T); sz.push_back(wbytes(prog[i].g)); T += sz.back(); }
+    for (int k = 0; k < m; ++k) { pb.push_back(T); sz.push_back(wbytes(prog[gi[k]].g)); T += sz.back(); }
     const double lead = std::min(pf_lead_bytes, T * 0.5);
     n_pf0 = 0;
-    for (size_t k = 0; k < gi.size(); ++k) {
+    for (int k = 0; k < m; ++k) {
         if (pb[k] < lead && n_pf0 < 16) pf0[n_pf0++] = gi[k];
         double t = pb[k] - lead;
         if (t < 0) t += T;
-        size_t m = std::upper_bound(pb.begin(), pb.end(), t) - pb.begin();
-        m = m == 0 ? 0 : m - 1;
-        for (size_t site = gi[m]; site < prog.size(); ++site) {
-            if (prog[site].n_pf < 6) { prog[site].pf[prog[site].n_pf++] = gi[k]; break; }
+        size_t j = std::upper_bound(pb.begin(), pb.end(), t) - pb.begin();
+        j = j == 0 ? 0 : j - 1;
+        for (size_t site = gi[j]; site < prog.size(); ++site) {
+            if (prog[site].n_pf < PK_MAX_PF) {
+                prog[site].pfA[prog[site].n_pf] = prog[gi[k]].g.A;
+                prog[site].pfB[prog[site].n_pf] = prog[gi[k]].g.B;
+                prog[site].n_pf++;
+                break;
+            }
         }
     }
     // upload
@@ -831,10 +870,14 @@ bool Engine::build_program() {
         QCHECK(cudaMalloc(&d_flags, sizeof(unsigned) * 1024));
         QCHECK(cudaMalloc(&d_err, sizeof(int)));
     }
-    if (prog_smem + 8 * 1024 > 227 * 1024) { err = "persistent kernel shared memory too large"; return false; }
-    QCHECK(cudaFuncSetAttribute(k_frame_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) prog_smem));
+    const size_t dyn = 2 * pk_wbuf + ((prog_smem + 127) & ~(size_t) 127);
+    cudaFuncAttributes fa{};
+    QCHECK(cudaFuncGetAttributes(&fa, k_frame_persistent));
+    if (dyn + fa.sharedSizeBytes > 227 * 1024) { err = "persistent kernel shared memory too large for this context"; return false; }
+    QCHECK(cudaFuncSetAttribute(k_frame_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) dyn));
+    pk_dyn = dyn;
     int nb = 0;
-    QCHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_frame_persistent, PK_THREADS, prog_smem));
+    QCHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_frame_persistent, PK_THREADS, dyn));
     if (nb < 1) { err = "persistent frame kernel does not fit on an SM"; return false; }
     prog_ok = true;
     return true;
@@ -846,11 +889,14 @@ bool Engine::launch_persistent(int n) {
     pa.out_codes = d_codes; pa.out_cap = codes_cap; pa.flags = d_flags; pa.err = d_err;
     pa.n_pf0 = n_pf0;
     for (int k = 0; k < n_pf0; ++k) pa.pf0[k] = pf0[k];
+    pa.wbuf_bytes = (int) pk_wbuf;
+    pa.first_gemv[0] = pk_first[0];
+    pa.first_gemv[1] = pk_first[1];
     QCHECK(cudaMemsetAsync(d_flags, 0, sizeof(unsigned) * n_sm, stream));
     QCHECK(cudaMemsetAsync(d_err, 0, sizeof(int), stream));
     void * args[] = {&pa};
     QCHECK(cudaLaunchCooperativeKernel((const void *) k_frame_persistent, dim3(n_sm), dim3(PK_THREADS), args,
-                                       prog_smem, stream));
+                                       pk_dyn, stream));
     ++launches;
     return true;
 }

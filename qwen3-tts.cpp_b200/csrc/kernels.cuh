@@ -110,12 +110,30 @@ __device__ __forceinline__ void gemv_store(const GemvArgs & a, int r, int v, flo
 // and issues all 16-byte loads of an iteration before the math.  Per-item
 // partial dots go to shared memory and are summed in slice order, so the
 // result depends only on (rows, grid, kslices), never on scheduling.
-template <int NV>
-__device__ __forceinline__ void gemv_body(const GemvArgs & a, const int cta, const int ncta, uint8_t * smem_raw) {
+// Where a CTA reads its weight rows from: global memory (streaming loads) or a
+// shared-memory copy of its row slice [r0, r1) (persistent frame kernel).
+struct WSrc {
+    const uint8_t * a, * b;       // F16 halves or int8 quants, row stride cols * elem size
+    const __half * sa, * sb;      // Q8_0 scales, row stride cols / 32
+    int rbase;                    // first row held by the pointers (0 for global)
+};
+
+template <bool SMEM>
+__device__ __forceinline__ uint4 ld_w16(const uint8_t * p) {
+    if constexpr (SMEM) return *reinterpret_cast<const uint4 *>(p);
+    else return ld_stream(p);
+}
+
+template <int NV, bool SMEM = false>
+__device__ __forceinline__ void gemv_body(const GemvArgs & a, const int cta, const int ncta, uint8_t * smem_raw,
+                                          const WSrc * wsrc = nullptr) {
     const int cols = a.A.cols, rows = a.A.rows;
     const int rpc = (rows + ncta - 1) / ncta;
     const int r0 = cta * rpc, r1 = min(rows, r0 + rpc);
     if (r0 >= r1) return;
+    WSrc src;
+    if (SMEM) src = *wsrc;
+    else src = WSrc{static_cast<const uint8_t *>(a.A.w), static_cast<const uint8_t *>(a.B.w), a.A.d, a.B.d, 0};
     float * xs = reinterpret_cast<float *>(smem_raw);
     int8_t * qa = reinterpret_cast<int8_t *>(xs + (size_t) NV * cols);
     float * da = reinterpret_cast<float *>(qa + (size_t)(a.A.type == W_Q8_0 ? NV * cols : 0));
@@ -131,8 +149,6 @@ __device__ __forceinline__ void gemv_body(const GemvArgs & a, const int cta, con
     if (a.A.type == W_F16) {
         const int nchunk = cols / 8;
         const int sl = (nchunk + S - 1) / S;
-        const __half * WA = static_cast<const __half *>(a.A.w);
-        const __half * WB = static_cast<const __half *>(a.B.w);
         for (int it0 = warp * IU; it0 < n_items; it0 += QTTS_WARPS * IU) {
             float accA[IU][NV], accB[IU][NV];
             int row[IU], cbeg[IU], cend[IU];
@@ -154,9 +170,9 @@ __device__ __forceinline__ void gemv_body(const GemvArgs & a, const int cta, con
                     for (int k = 0; k < KU; ++k) {
                         const int c = cbeg[u] + cc + lane + 32 * k;
                         const bool ok = c < cend[u];
-                        const size_t off = (size_t) row[u] * cols + (size_t) c * 8;
-                        wa[u][k] = ok ? ld_stream(WA + off) : make_uint4(0, 0, 0, 0);
-                        wb[u][k] = (ok && dual) ? ld_stream(WB + off) : make_uint4(0, 0, 0, 0);
+                        const size_t off = ((size_t)(row[u] - src.rbase) * cols + (size_t) c * 8) * 2;
+                        wa[u][k] = ok ? ld_w16<SMEM>(src.a + off) : make_uint4(0, 0, 0, 0);
+                        wb[u][k] = (ok && dual) ? ld_w16<SMEM>(src.b + off) : make_uint4(0, 0, 0, 0);
                     }
 #pragma unroll
                 for (int u = 0; u < IU; ++u)
@@ -187,8 +203,6 @@ __device__ __forceinline__ void gemv_body(const GemvArgs & a, const int cta, con
     } else {  // Q8_0: 16 quants per lane-chunk, lane pairs form one 32-block
         const int nchunk = cols / 16, nb = cols / 32;
         const int sl = (((nchunk + S - 1) / S) + 1) & ~1;   // even: slices start on a block
-        const int8_t * QA = static_cast<const int8_t *>(a.A.w);
-        const int8_t * QB = static_cast<const int8_t *>(a.B.w);
         for (int it0 = warp * IU; it0 < n_items; it0 += QTTS_WARPS * IU) {
             float accA[IU][NV], accB[IU][NV];
             int row[IU], cbeg[IU], cend[IU];
@@ -211,11 +225,11 @@ __device__ __forceinline__ void gemv_body(const GemvArgs & a, const int cta, con
                     for (int k = 0; k < KU; ++k) {
                         const int c = cbeg[u] + cc + lane + 32 * k;
                         const bool ok = c < cend[u];
-                        const size_t ro = (size_t) row[u];
-                        wa[u][k] = ok ? ld_stream(QA + ro * cols + (size_t) c * 16) : make_uint4(0, 0, 0, 0);
-                        wb[u][k] = (ok && dual) ? ld_stream(QB + ro * cols + (size_t) c * 16) : make_uint4(0, 0, 0, 0);
-                        swa[u][k] = ok ? __half2float(a.A.d[ro * nb + (c >> 1)]) : 0.0f;
-                        swb[u][k] = (ok && dual) ? __half2float(a.B.d[ro * nb + (c >> 1)]) : 0.0f;
+                        const size_t ro = (size_t)(row[u] - src.rbase);
+                        wa[u][k] = ok ? ld_w16<SMEM>(src.a + ro * cols + (size_t) c * 16) : make_uint4(0, 0, 0, 0);
+                        wb[u][k] = (ok && dual) ? ld_w16<SMEM>(src.b + ro * cols + (size_t) c * 16) : make_uint4(0, 0, 0, 0);
+                        swa[u][k] = ok ? __half2float(src.sa[ro * nb + (c >> 1)]) : 0.0f;
+                        swb[u][k] = (ok && dual) ? __half2float(src.sb[ro * nb + (c >> 1)]) : 0.0f;
                     }
 #pragma unroll
                 for (int u = 0; u < IU; ++u)

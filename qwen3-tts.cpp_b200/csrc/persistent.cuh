@@ -42,14 +42,20 @@ struct FusedAttn {
     int dump_stride;
 };
 
+constexpr int PK_MAX_PF = 3;
+
 struct alignas(16) POp {
     int type;
     int barrier;              // grid barrier after this op
     int nv;                   // GEMV rows (1 or 2)
     int cb, V;                // sampler
+    int slot;                 // GEMV: shared-memory weight buffer holding this op's slice
+    int issue;                // copy the slice of (iA, iB) into buffer issue_slot at op start
+    int issue_slot;
+    int n_pf;                 // GEMV weight matrices to prefetch into L2 at op start
     const float * logits;
-    int n_pf;                 // GEMV ops whose weight slices this op prefetches into L2
-    int pf[6];
+    DMat iA, iB;
+    DMat pfA[PK_MAX_PF], pfB[PK_MAX_PF];
     GemvArgs g;
     FusedAttn a;
     InputArgs in;
@@ -58,6 +64,11 @@ struct alignas(16) POp {
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned * p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned * p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 __device__ __forceinline__ void st_release_u32(unsigned * p, unsigned v) {
@@ -80,13 +91,13 @@ __device__ __forceinline__ bool grid_barrier(unsigned * flags, unsigned epoch, i
         for (unsigned long long it = 0; it < PK_SPIN_LIMIT; ++it) {
             bool mine = true;
             for (int c = lane; c < (int) gridDim.x; c += 32)
-                if (ld_acquire_u32(flags + c) < epoch) mine = false;
+                if (ld_relaxed_u32(flags + c) < epoch) mine = false;
             if (__all_sync(0xffffffffu, mine)) { ok = true; break; }
             if (__any_sync(0xffffffffu, *(volatile int *) err != 0)) break;   // warp-uniform exit
         }
+        __threadfence();   // acquire side: order the peers' writes before this CTA's reads
         if (lane == 0) {
             if (!ok) atomicExch(err, 1);
-            __threadfence();
             s_ok = ok;
         }
     }
@@ -105,19 +116,94 @@ __device__ __forceinline__ void prefetch_l2(const void * p, size_t bytes) {
 }
 
 // This CTA's row slice of a GEMV's weights (same split as gemv_body).
-__device__ __forceinline__ void prefetch_gemv_slice(const GemvArgs & g, int cta, int ncta) {
-    const int rows = g.A.rows, cols = g.A.cols;
+__device__ __forceinline__ void prefetch_mat_slice(const DMat & M, int cta, int ncta) {
+    if (!M.w) return;
+    const int rows = M.rows, cols = M.cols;
     const int rpc = (rows + ncta - 1) / ncta;
     const int r0 = cta * rpc, r1 = min(rows, r0 + rpc);
     if (r0 >= r1) return;
-    const size_t es = g.A.type == W_F16 ? 2 : 1;
-    const DMat * mats[2] = {&g.A, &g.B};
-    for (int m = 0; m < 2; ++m) {
-        const DMat & M = *mats[m];
-        if (!M.w) continue;
-        prefetch_l2(static_cast<const char *>(M.w) + (size_t) r0 * cols * es, (size_t)(r1 - r0) * cols * es);
-        if (M.type == W_Q8_0)
-            prefetch_l2(M.d + (size_t) r0 * (cols / 32), (size_t)(r1 - r0) * (cols / 32) * 2);
+    const size_t es = M.type == W_F16 ? 2 : 1;
+    prefetch_l2(static_cast<const char *>(M.w) + (size_t) r0 * cols * es, (size_t)(r1 - r0) * cols * es);
+    if (M.type == W_Q8_0) prefetch_l2(M.d + (size_t) r0 * (cols / 32), (size_t)(r1 - r0) * (cols / 32) * 2);
+}
+__device__ __forceinline__ void prefetch_gemv_slice(const GemvArgs & g, int cta, int ncta) {
+    prefetch_mat_slice(g.A, cta, ncta);
+    prefetch_mat_slice(g.B, cta, ncta);
+}
+
+// ---- shared-memory weight slices (TMA bulk copies completed on an mbarrier)
+__device__ __forceinline__ uint32_t smem_u32(const void * p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t * m, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(m)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t * m, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t * m, unsigned parity) {
+    unsigned ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok) : "r"(smem_u32(m)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait: false when the phase did not complete within the limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t * m, unsigned parity) {
+    for (unsigned long long it = 0; it < PK_SPIN_LIMIT; ++it)
+        if (mbar_try_wait(m, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, unsigned bytes, uint64_t * m) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(m)) : "memory");
+}
+
+struct SliceGeom {
+    int r0, r1;
+    size_t bytesA, bytesS;   // per matrix: quants/halves, scales
+};
+__device__ __forceinline__ SliceGeom slice_geom(const DMat & A, int cta, int ncta) {
+    SliceGeom g;
+    const int rpc = (A.rows + ncta - 1) / ncta;
+    g.r0 = cta * rpc;
+    g.r1 = min(A.rows, g.r0 + rpc);
+    const int n = g.r1 > g.r0 ? g.r1 - g.r0 : 0;
+    g.bytesA = (size_t) n * A.cols * (A.type == W_F16 ? 2 : 1);
+    g.bytesS = A.type == W_Q8_0 ? (size_t) n * (A.cols / 32) * 2 : 0;
+    return g;
+}
+// Buffer layout: A rows | B rows | A scales | B scales.
+__device__ __forceinline__ WSrc slice_src(const DMat & A, const DMat & B, const uint8_t * buf, int cta, int ncta) {
+    const SliceGeom g = slice_geom(A, cta, ncta);
+    const int nm = B.w ? 2 : 1;
+    WSrc s;
+    s.a = buf;
+    s.b = buf + g.bytesA;
+    s.sa = reinterpret_cast<const __half *>(buf + nm * g.bytesA);
+    s.sb = reinterpret_cast<const __half *>(buf + nm * g.bytesA + g.bytesS);
+    s.rbase = g.r0;
+    return s;
+}
+// One thread: copy this CTA's slice of (A, B) into buf, completing on m.
+__device__ __forceinline__ void issue_slice(const DMat & A, const DMat & B, uint8_t * buf, uint64_t * m, int cta,
+                                            int ncta) {
+    const SliceGeom g = slice_geom(A, cta, ncta);
+    const int nm = B.w ? 2 : 1;
+    const size_t es = A.type == W_F16 ? 2 : 1;
+    mbar_expect_tx(m, (unsigned)(nm * (g.bytesA + g.bytesS)));
+    if (g.r1 <= g.r0) return;
+    const DMat * mats[2] = {&A, &B};
+    for (int k = 0; k < nm; ++k) {
+        const char * src = static_cast<const char *>(mats[k]->w) + (size_t) g.r0 * A.cols * es;
+        uint8_t * dst = buf + k * g.bytesA;
+        for (size_t o = 0; o < g.bytesA; o += 32768) {
+            const unsigned n = (unsigned)(g.bytesA - o < 32768 ? g.bytesA - o : 32768);
+            bulk_g2s(dst + o, src + o, n, m);
+        }
+        if (g.bytesS) {
+            const char * ss = reinterpret_cast<const char *>(mats[k]->d + (size_t) g.r0 * (A.cols / 32));
+            bulk_g2s(buf + nm * g.bytesA + k * g.bytesS, ss, (unsigned) g.bytesS, m);
+        }
     }
 }
 
@@ -291,36 +377,88 @@ struct PersistentArgs {
     int out_cap;
     unsigned * flags;          // [gridDim.x], zeroed before the launch
     int * err;
-    int n_pf0;                 // ops prefetched at launch start
+    int wbuf_bytes;            // bytes of each of the two weight buffers
+    int n_pf0;                 // GEMVs prefetched into L2 at launch start
     int pf0[16];
+    int first_gemv[2];         // the first two GEMV ops (their slices are copied at launch start)
 };
 
+__device__ __forceinline__ void pk_drain(uint64_t * mbar, const int * pending, unsigned * phase) {
+    for (int b = 0; b < 2; ++b)
+        if (pending[b]) { mbar_wait(&mbar[b], phase[b] & 1u); phase[b]++; }
+}
+
 __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentArgs P) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ POp op;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ POp desc[2];
+    __shared__ __align__(8) uint64_t mbar[2];
     __shared__ int s_done;
     const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x;
+    uint8_t * wbuf[2] = {smem, smem + P.wbuf_bytes};
+    uint8_t * work = smem + 2 * (size_t) P.wbuf_bytes;
+    unsigned phase[2] = {0u, 0u};
+    int pending[2] = {0, 0};
     unsigned epoch = 0;
-    if (tid == 0)
+    constexpr int NW = (int)(sizeof(POp) / 8);
+
+    if (tid == 0) {
+        mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    {
+        const unsigned long long * src = reinterpret_cast<const unsigned long long *>(P.ops);
+        unsigned long long * dst = reinterpret_cast<unsigned long long *>(&desc[0]);
+        for (int w = tid; w < NW; w += blockDim.x) dst[w] = src[w];
+    }
+    __syncthreads();
+    if (tid == 0) {
         for (int k = 0; k < P.n_pf0; ++k) prefetch_gemv_slice(P.ops[P.pf0[k]].g, cta, ncta);
+        for (int b = 0; b < 2; ++b) {
+            const POp & g = P.ops[P.first_gemv[b]];
+            issue_slice(g.g.A, g.g.B, wbuf[g.slot], &mbar[g.slot], cta, ncta);
+        }
+    }
+    pending[0] = pending[1] = 1;
+
+    long long s = 0;   // position in the op stream
     for (int f = 0; f < P.n_frames; ++f) {
-        for (int oi = 0; oi < P.n_ops; ++oi) {
-            // stage the op descriptor in shared memory
-            {
-                const unsigned long long * src = reinterpret_cast<const unsigned long long *>(P.ops + oi);
-                unsigned long long * dst = reinterpret_cast<unsigned long long *>(&op);
-                for (int w = tid; w < (int)(sizeof(POp) / 8); w += blockDim.x) dst[w] = src[w];
+        for (int oi = 0; oi < P.n_ops; ++oi, ++s) {
+            const POp & op = desc[s & 1];
+            // stage the next descriptor (loads now, shared-memory stores before the barrier)
+            const int nx = oi + 1 < P.n_ops ? oi + 1 : 0;
+            const unsigned long long * nsrc = reinterpret_cast<const unsigned long long *>(P.ops + nx);
+            unsigned long long nw0 = tid < NW ? nsrc[tid] : 0ull;
+            unsigned long long nw1 = tid + (int) blockDim.x < NW ? nsrc[tid + blockDim.x] : 0ull;
+            if (tid == 0) {
+                if (op.issue) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue_slice(op.iA, op.iB, wbuf[op.issue_slot], &mbar[op.issue_slot], cta, ncta);
+                }
+                for (int k = 0; k < op.n_pf; ++k) {
+                    prefetch_mat_slice(op.pfA[k], cta, ncta);
+                    prefetch_mat_slice(op.pfB[k], cta, ncta);
+                }
             }
-            __syncthreads();
-            if (tid == 0)
-                for (int k = 0; k < op.n_pf; ++k) prefetch_gemv_slice(P.ops[op.pf[k]].g, cta, ncta);
+            if (op.issue) pending[op.issue_slot] = 1;
             switch (op.type) {
-                case P_GEMV:
-                    if (op.nv == 1) gemv_body<1>(op.g, cta, ncta, smem);
-                    else gemv_body<2>(op.g, cta, ncta, smem);
+                case P_GEMV: {
+                    const int b = op.slot;
+                    const bool ok = mbar_wait(&mbar[b], phase[b] & 1u);
+                    if (__syncthreads_or(!ok)) {      // block-uniform: a copy did not land in time
+                        if (tid == 0) atomicExch(P.err, 2);
+                        pk_drain(mbar, pending, phase);
+                        return;
+                    }
+                    phase[b]++;
+                    pending[b] = 0;
+                    const WSrc src = slice_src(op.g.A, op.g.B, wbuf[b], cta, ncta);
+                    if (op.nv == 1) gemv_body<1, true>(op.g, cta, ncta, work, &src);
+                    else gemv_body<2, true>(op.g, cta, ncta, work, &src);
                     break;
+                }
                 case P_ATTN:
-                    for (int u = cta; u < op.a.n_kv_heads * op.a.M; u += ncta) fused_attn_body(op.a, u, smem, P.st);
+                    for (int u = cta; u < op.a.n_kv_heads * op.a.M; u += ncta) fused_attn_body(op.a, u, work, P.st);
                     break;
                 case P_SAMPLE:
                     if (cta == 0) {
@@ -343,18 +481,26 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
                 default:
                     break;
             }
+            __syncthreads();   // everyone is done with desc[s & 1]
+            {
+                unsigned long long * ndst = reinterpret_cast<unsigned long long *>(&desc[(s + 1) & 1]);
+                if (tid < NW) ndst[tid] = nw0;
+                if (tid + (int) blockDim.x < NW) ndst[tid + blockDim.x] = nw1;
+            }
+            const int was_sample0 = op.type == P_SAMPLE && op.cb == 0;
             if (op.barrier) {
-                if (!grid_barrier(P.flags, ++epoch, P.err)) return;
-                if (op.type == P_SAMPLE && op.cb == 0) {
+                if (!grid_barrier(P.flags, ++epoch, P.err)) { pk_drain(mbar, pending, phase); return; }
+                if (was_sample0) {
                     if (tid == 0) s_done = *(volatile int *) &P.st->done;
                     __syncthreads();
-                    if (s_done) return;
+                    if (s_done) { pk_drain(mbar, pending, phase); return; }
                 }
             } else {
                 __syncthreads();
             }
         }
     }
+    pk_drain(mbar, pending, phase);
 }
 
 }  // namespace qtts
