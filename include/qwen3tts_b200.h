@@ -158,6 +158,13 @@ int32_t qtts_get_timing(const qtts_engine * e, qtts_timing * out);
  * Returns frames produced or -1.  For measurement only. */
 int32_t qtts_profile_frames(qtts_engine * e, int32_t n, qtts_kernel_stats * stats, int32_t n_classes);
 
+/* Diagnostics of the persistent frame kernel, enabled by QTTS_PK_TRACE=1 at
+ * run time: the op types of the frame program (1 GEMV, 2 attention, 3 sampler,
+ * 4 embedding gather, 5 frame end) and, for the last run, CTA 0's %globaltimer
+ * (start, work done) pair of every op.  Both return the count available. */
+int32_t qtts_program_ops(const qtts_engine * e, int32_t * types, int32_t cap);
+int32_t qtts_op_trace(const qtts_engine * e, unsigned long long * out, int32_t cap);
+
 /* ---- Kernel-level entry points (one engine kernel on host data) ----------
  * ggml_mul_mat (+ optional ggml_rms_norm prologue) as the engine computes it,
  * src/tts_transformer.cpp:1656-1661: y[nv][rows] = W[rows][cols] . x[nv][cols].

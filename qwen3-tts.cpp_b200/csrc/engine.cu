@@ -127,6 +127,8 @@ struct Engine {
     int pf0[16];
     int n_pf0 = 0;
     int pk_first[2] = {0, 0};
+    unsigned long long * d_trace = nullptr;   // QTTS_PK_TRACE=1: per-op timestamps of CTA 0
+    size_t trace_cap = 0, trace_n = 0;
     size_t pk_wbuf = 0, pk_dyn = 0;
     double pf_lead_bytes = 24.0 * 1024 * 1024;
     // eager profiling: CUDA events around every launch, accumulated per kernel class
@@ -161,12 +163,13 @@ struct Engine {
         if (graph) { cudaGraphExecDestroy(graph); graph = nullptr; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
                          cp_logits, hidden, hid_rows, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
-                         dbg_t, dbg_cp, d_attn, d_prog, d_flags, d_err};
+                         dbg_t, dbg_cp, d_attn, d_prog, d_flags, d_err, d_trace};
         for (void * p : ptrs) if (p) cudaFree(p);
         wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
         x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = hid_rows = tmp_a = tmp_b = nullptr;
         d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
         dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_prog = nullptr; d_flags = nullptr; d_err = nullptr;
+        d_trace = nullptr;
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         ev0 = ev1 = nullptr;
@@ -890,6 +893,19 @@ bool Engine::launch_persistent(int n) {
     pa.n_pf0 = n_pf0;
     for (int k = 0; k < n_pf0; ++k) pa.pf0[k] = pf0[k];
     pa.wbuf_bytes = (int) pk_wbuf;
+    pa.trace = nullptr;
+    trace_n = 0;
+    if (getenv("QTTS_PK_TRACE")) {
+        const size_t need = (size_t) 2 * prog.size() * n;
+        if (need > trace_cap) {
+            if (d_trace) cudaFree(d_trace);
+            trace_cap = need;
+            QCHECK(cudaMalloc(&d_trace, sizeof(unsigned long long) * trace_cap));
+        }
+        QCHECK(cudaMemsetAsync(d_trace, 0, sizeof(unsigned long long) * need, stream));
+        pa.trace = d_trace;
+        trace_n = need;
+    }
     pa.first_gemv[0] = pk_first[0];
     pa.first_gemv[1] = pk_first[1];
     QCHECK(cudaMemsetAsync(d_flags, 0, sizeof(unsigned) * n_sm, stream));
@@ -1741,6 +1757,26 @@ int32_t qtts_profile_frames(qtts_engine * h, int32_t n, qtts_kernel_stats * out,
     E.sess.produced = hs.n_out;
     E.sess.done = hs.done != 0;
     return got;
+}
+
+// Diagnostics of the persistent frame kernel (QTTS_PK_TRACE=1): the op types of
+// the frame program, and CTA 0's (start, work done) %globaltimer pairs of every
+// op of the last run.  Both return the number of values available.
+int32_t qtts_program_ops(const qtts_engine * h, int32_t * types, int32_t cap) {
+    if (!h) return -1;
+    const Engine & E = *reinterpret_cast<const Engine *>(h);
+    const int n = (int) E.prog.size();
+    for (int i = 0; i < n && i < cap; ++i) types[i] = E.prog[i].type;
+    return n;
+}
+int32_t qtts_op_trace(const qtts_engine * h, unsigned long long * out, int32_t cap) {
+    if (!h) return -1;
+    const Engine & E = *reinterpret_cast<const Engine *>(h);
+    if (!E.d_trace || !E.trace_n) return 0;
+    cudaSetDevice(E.dev);
+    const size_t n = std::min(E.trace_n, (size_t) std::max(cap, 0));
+    if (out && n) cudaMemcpy(out, E.d_trace, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost);
+    return (int32_t) E.trace_n;
 }
 
 int32_t qtts_get_timing(const qtts_engine * h, qtts_timing * out) {

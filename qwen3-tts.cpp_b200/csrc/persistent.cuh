@@ -381,7 +381,14 @@ struct PersistentArgs {
     int n_pf0;                 // GEMVs prefetched into L2 at launch start
     int pf0[16];
     int first_gemv[2];         // the first two GEMV ops (their slices are copied at launch start)
+    unsigned long long * trace;  // optional: CTA 0 records %globaltimer per op (start, work done)
 };
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ void pk_drain(uint64_t * mbar, const int * pending, unsigned * phase) {
     for (int b = 0; b < 2; ++b)
@@ -425,6 +432,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
     for (int f = 0; f < P.n_frames; ++f) {
         for (int oi = 0; oi < P.n_ops; ++oi, ++s) {
             const POp & op = desc[s & 1];
+            if (P.trace && cta == 0 && tid == 0) P.trace[2 * s] = globaltimer_ns();
             // stage the next descriptor (loads now, shared-memory stores before the barrier)
             const int nx = oi + 1 < P.n_ops ? oi + 1 : 0;
             const unsigned long long * nsrc = reinterpret_cast<const unsigned long long *>(P.ops + nx);
@@ -482,6 +490,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
                     break;
             }
             __syncthreads();   // everyone is done with desc[s & 1]
+            if (P.trace && cta == 0 && tid == 0) P.trace[2 * s + 1] = globaltimer_ns();
             {
                 unsigned long long * ndst = reinterpret_cast<unsigned long long *>(&desc[(s + 1) & 1]);
                 if (tid < NW) ndst[tid] = nw0;

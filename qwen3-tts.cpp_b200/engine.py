@@ -106,6 +106,8 @@ def lib():
         "qtts_attn_rows": (C.c_int32, [C.c_void_p]),
         "qtts_attn_row": (C.c_int32, [C.c_void_p, C.c_int32, _f32p, C.c_int32]),
         "qtts_get_timing": (C.c_int32, [C.c_void_p, C.POINTER(Timing)]),
+        "qtts_program_ops": (C.c_int32, [C.c_void_p, _i32p, C.c_int32]),
+        "qtts_op_trace": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64), C.c_int32]),
         "qtts_profile_frames": (C.c_int32, [C.c_void_p, C.c_int32, C.POINTER(KernelStats), C.c_int32]),
         "qtts_op_gemv": (C.c_int32, [C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32, _f32p,
                                      C.c_float, C.c_int32, _f32p, _i32p]),
@@ -299,6 +301,16 @@ class Engine:
             raise RuntimeError("profile_frames failed: " + self.error())
         return {"frames": got, **{KERNEL_CLASSES[i]: dict(launches=st[i].launches, ms=st[i].total_ms, bytes=st[i].bytes)
                                   for i in range(4)}}
+
+    def op_trace(self):
+        """(op types, CTA-0 timestamps [runs*ops][2]) of the last persistent run (QTTS_PK_TRACE=1)."""
+        n = lib().qtts_program_ops(self.h, None, 0)
+        types = np.zeros(max(n, 1), np.int32)
+        lib().qtts_program_ops(self.h, _p(types, C.c_int32), n)
+        m = lib().qtts_op_trace(self.h, None, 0)
+        tr = np.zeros(max(m, 1), np.uint64)
+        lib().qtts_op_trace(self.h, tr.ctypes.data_as(C.POINTER(C.c_uint64)), m)
+        return types[:n], tr[:m].reshape(-1, 2)
 
     def run_frames(self, n: int, codes_out: np.ndarray | None = None) -> int:
         ptr = None if codes_out is None else _p(codes_out, C.c_int32)

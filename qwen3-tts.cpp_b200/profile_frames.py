@@ -43,6 +43,19 @@ def main():
                        temperature=0.0, top_k=0, eos_bias=-1e9)
     got = eng.run_frames(a.frames)
     print(f"frames={got} {eng.timing()}")
+    if os.environ.get("QTTS_PK_TRACE"):
+        types, tr = eng.op_trace()
+        names = {1: "gemv", 2: "attn", 3: "sample", 4: "input", 5: "frame_end"}
+        n = len(types)
+        t = tr[: n * got].astype(np.int64)
+        work = t[:, 1] - t[:, 0]
+        total = np.diff(np.append(t[:, 0], t[-1, 1]))
+        wait = total - work
+        for ty in sorted(set(types.tolist())):
+            idx = np.nonzero(np.tile(types, got) == ty)[0]
+            print(f"op {names.get(ty, ty):9s} n={len(idx)//max(got,1):4d}/frame  work {work[idx].mean()/1e3:7.2f} us"
+                  f"  barrier+next {wait[idx].mean()/1e3:7.2f} us")
+        print(f"frame span {(t[-1, 1] - t[0, 0]) / 1e3 / max(got, 1):.1f} us")
     eng.close()
 
 
