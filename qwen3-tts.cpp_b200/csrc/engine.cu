@@ -191,13 +191,15 @@ struct Engine {
     bool layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, int ctx, const float2 * rope, float * X,
                 int M, const int * pos_ptr, int pos_static, bool f32_mode, const int * done, int ffn,
                 float * dump = nullptr, int dump_layer = -1);
+    FusedAttn fused_attn_args(const LayerW & l, __half * kc_l, __half * vc_l, const float2 * rope, int M,
+                              const int * pos_ptr, int pos_static, bool f32, float * dump, int dump_stride);
     bool enqueue_cp(bool sample_cb0);
     bool enqueue_talker_step(const int * pos_ptr, int pos_static, const int * done, bool with_dump);
     bool enqueue_frame();
     bool capture_graph();
     GemvArgs make_gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
                        float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
-                       const int * done, int * ncta_out, size_t * smem_out);
+                       const int * done, int * ncta_out, size_t * slice_out, size_t * smem_out);
     bool build_program();
     bool launch_persistent(int n);
     bool sync(const char * what);
@@ -485,9 +487,10 @@ bool Engine::alloc_activations() {
     ids_cap = 4096;
     QCHECK(cudaMalloc(&d_ids, sizeof(int) * ids_cap));
     // large dynamic shared memory for the GEMV instantiations
-    QCHECK(cudaFuncSetAttribute(k_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    QCHECK(cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    QCHECK(cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    QCHECK(cudaFuncSetAttribute(k_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX));
+    QCHECK(cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX));
+    QCHECK(cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX));
+    QCHECK(cudaFuncSetAttribute(k_fused_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return true;
 }
 
@@ -555,9 +558,29 @@ bool Engine::sync(const char * what) {
 }
 
 // ---------------------------------------------------------------- launches
+// Grid and shared memory of a stand-alone k_gemv launch: one CTA per SM while
+// its weight slice and work area fit, more CTAs (smaller slices) otherwise.
+static bool gemv_shape(const DMat & A, bool dual, bool has_gain, int nvt, int n_sm, int * ncta_out, size_t * slice_out,
+                       size_t * smem_out) {
+    int ncta = std::min(n_sm, A.rows);
+    for (;;) {
+        const int rpc = gemv_rpc(A.rows, ncta);
+        const size_t slice = (slice_layout(A, dual, has_gain, rpc).total + 127) & ~(size_t) 127;
+        const size_t smem = slice + gemv_work_bytes(A.type, A.cols, nvt, rpc);
+        if (smem <= QTTS_GEMV_SMEM_MAX) {
+            *ncta_out = (A.rows + rpc - 1) / rpc;
+            *slice_out = slice;
+            *smem_out = smem;
+            return true;
+        }
+        if (ncta >= A.rows) return false;
+        ncta = std::min(A.rows, ncta * 2);
+    }
+}
+
 GemvArgs Engine::make_gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm,
                            int act, float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out,
-                           int ldxn, const int * done, int * ncta_out, size_t * smem_out) {
+                           int ldxn, const int * done, int * ncta_out, size_t * slice_out, size_t * smem_out) {
     GemvArgs a{};
     a.A = A;
     if (B) a.B = *B;
@@ -565,16 +588,8 @@ GemvArgs Engine::make_gemv(const DMat & A, const DMat * B, const float * xin, in
     a.norm_g = norm; a.eps = cfg.rms_norm_eps; a.act = act;
     a.y = y; a.ldy = ldy; a.resid = resid; a.ldr = ldr; a.epi = epi;
     a.xn_out = xn_out; a.ldxn = ldxn; a.done = done;
-    int ncta = std::min(n_sm, A.rows);
-    const int rpc = (A.rows + ncta - 1) / ncta;
-    ncta = (A.rows + rpc - 1) / rpc;
-    const int nchunk = A.type == W_F16 ? A.cols / 8 : A.cols / 16;
-    int ks = (2 * QTTS_WARPS + rpc - 1) / rpc;
-    ks = std::max(1, std::min(ks, std::max(1, nchunk / 32)));
-    a.kslices = ks;
     const int NVt = nv == 1 ? 1 : nv == 2 ? 2 : 8;
-    *ncta_out = ncta;
-    *smem_out = gemv_smem_bytes(A.type, A.cols, NVt, rpc, ks);
+    if (!gemv_shape(A, B != nullptr, norm != nullptr, NVt, n_sm, ncta_out, slice_out, smem_out)) *ncta_out = 0;
     return a;
 }
 
@@ -582,18 +597,32 @@ bool Engine::gemv(const DMat & A, const DMat * B, const float * xin, int ldx, in
                   float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
                   const int * done) {
     int ncta;
-    size_t smem;
-    GemvArgs a = make_gemv(A, B, xin, ldx, nv, norm, act, y, ldy, resid, ldr, epi, xn_out, ldxn, done, &ncta, &smem);
+    size_t slice, smem;
+    GemvArgs a = make_gemv(A, B, xin, ldx, nv, norm, act, y, ldy, resid, ldr, epi, xn_out, ldxn, done, &ncta, &slice,
+                           &smem);
     const int NVt = nv == 1 ? 1 : nv == 2 ? 2 : 8;
-    if (nv > QTTS_MAX_NV || smem > 200 * 1024) { err = "gemv shape too large"; return false; }
+    if (nv > QTTS_MAX_NV || ncta == 0) { err = "gemv shape too large"; return false; }
     const double wb = A.type == W_F16 ? (double) A.rows * A.cols * 2.0 : (double) A.rows * A.cols * 34.0 / 32.0;
     prof_begin(KC_GEMV, wb * (B ? 2.0 : 1.0) + 4.0 * nv * ((double) A.cols + A.rows));
-    if (NVt == 1) k_gemv<1><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a);
-    else if (NVt == 2) k_gemv<2><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a);
-    else k_gemv<8><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a);
+    if (NVt == 1) k_gemv<1><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a, slice);
+    else if (NVt == 2) k_gemv<2><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a, slice);
+    else k_gemv<8><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a, slice);
     prof_end();
     ++launches;
     return true;
+}
+
+FusedAttn Engine::fused_attn_args(const LayerW & l, __half * kc_l, __half * vc_l, const float2 * rope, int M,
+                                  const int * pos_ptr, int pos_static, bool f32, float * dump, int dump_stride) {
+    const qtts_config & c = cfg;
+    FusedAttn a{};
+    a.qkv = qkv; a.ldq = QKVD(); a.n_heads = c.n_attention_heads; a.n_kv_heads = c.n_key_value_heads;
+    a.q_norm = l.q_norm; a.k_norm = l.k_norm; a.eps = c.rms_norm_eps; a.rope = rope;
+    a.kc = kc_l; a.vc = vc_l;
+    a.pos_ptr = pos_ptr; a.pos_static = pos_static; a.M = M; a.f32_mode = f32 ? 1 : 0;
+    a.scale = 1.0f / sqrtf((float) QTTS_HD); a.out = att; a.ldo = QD();
+    a.dump = dump; a.dump_stride = dump_stride;
+    return a;
 }
 
 bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, int ctx, const float2 * rope, float * X,
@@ -608,27 +637,40 @@ bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, in
         LayerW & l = Ls[il];
         if (!gemv(l.qkv, nullptr, X, H, M, l.attn_norm, ACT_F16, qkv, QKVD(), nullptr, 0, EPI_STORE, nullptr, 0, done))
             return false;
-        QkArgs qa{};
-        qa.qkv = qkv; qa.ldq = QKVD(); qa.n_heads = NH; qa.n_kv_heads = NKV;
-        qa.q_norm = l.q_norm; qa.k_norm = l.k_norm; qa.eps = c.rms_norm_eps; qa.rope = rope;
-        qa.kc = kbase + il * layer_elems; qa.vc = vbase + il * layer_elems;
-        qa.pos_ptr = pos_ptr; qa.pos_static = pos_static; qa.keep_f32_k = f32_mode ? 1 : 0; qa.done = done;
-        prof_begin(KC_OTHER, 0.0);
-        k_qk_rope_store<<<M, 32 * (NH + NKV), 0, stream>>>(qa);
-        prof_end();
-        ++launches;
-        AttnArgs aa{};
-        aa.q = qkv; aa.ldq = QKVD(); aa.kc = qa.kc; aa.vc = qa.vc;
-        aa.kf = qkv + QD(); aa.vf = qkv + QD() + KD(); aa.ldkv = QKVD(); aa.f32_mode = f32_mode ? 1 : 0;
-        aa.n_heads = NH; aa.n_kv_heads = NKV; aa.pos_ptr = pos_ptr; aa.pos_static = pos_static;
-        aa.scale = 1.0f / sqrtf((float) QTTS_HD);
-        aa.out = att; aa.ldo = QD(); aa.done = done;
-        aa.dump = ((int) il == dump_layer) ? dump : nullptr;
-        aa.dump_stride = ctx; aa.st = st;
-        prof_begin(KC_ATTN, 0.0);
-        k_attention<<<dim3(NKV, M), ATT_THREADS, att_smem, stream>>>(aa);
-        prof_end();
-        ++launches;
+        if (f32_mode || M == 1) {
+            // frame steps and the code-predictor 2-token prefill: one fused unit per (kv head, row)
+            FusedAttn fa = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, M, pos_ptr,
+                                           pos_static, f32_mode, ((int) il == dump_layer) ? dump : nullptr, ctx);
+            fa.done = done;
+            const size_t fsm = fused_attn_smem(f32_mode ? M : ctx, G, M);
+            if (fsm > 200 * 1024) { err = "context too long for the fused attention kernel"; return false; }
+            prof_begin(KC_ATTN, 0.0);
+            k_fused_attention<<<NKV * M, FA_THREADS, fsm, stream>>>(fa, st);
+            prof_end();
+            ++launches;
+        } else {
+            QkArgs qa{};
+            qa.qkv = qkv; qa.ldq = QKVD(); qa.n_heads = NH; qa.n_kv_heads = NKV;
+            qa.q_norm = l.q_norm; qa.k_norm = l.k_norm; qa.eps = c.rms_norm_eps; qa.rope = rope;
+            qa.kc = kbase + il * layer_elems; qa.vc = vbase + il * layer_elems;
+            qa.pos_ptr = pos_ptr; qa.pos_static = pos_static; qa.keep_f32_k = 0; qa.done = done;
+            prof_begin(KC_OTHER, 0.0);
+            k_qk_rope_store<<<M, 32 * (NH + NKV), 0, stream>>>(qa);
+            prof_end();
+            ++launches;
+            AttnArgs aa{};
+            aa.q = qkv; aa.ldq = QKVD(); aa.kc = qa.kc; aa.vc = qa.vc;
+            aa.kf = qkv + QD(); aa.vf = qkv + QD() + KD(); aa.ldkv = QKVD(); aa.f32_mode = 0;
+            aa.n_heads = NH; aa.n_kv_heads = NKV; aa.pos_ptr = pos_ptr; aa.pos_static = pos_static;
+            aa.scale = 1.0f / sqrtf((float) QTTS_HD);
+            aa.out = att; aa.ldo = QD(); aa.done = done;
+            aa.dump = ((int) il == dump_layer) ? dump : nullptr;
+            aa.dump_stride = ctx; aa.st = st;
+            prof_begin(KC_ATTN, 0.0);
+            k_attention<<<dim3(NKV, M), ATT_THREADS, att_smem, stream>>>(aa);
+            prof_end();
+            ++launches;
+        }
         if (!gemv(l.o, nullptr, att, QD(), M, nullptr, ACT_F16, X, H, X, H, EPI_RESID, nullptr, 0, done)) return false;
         if (!gemv(l.gate, &l.up, X, H, M, l.ffn_norm, ACT_F16, hbuf, ffn, nullptr, 0, EPI_SWIGLU, nullptr, 0, done))
             return false;
@@ -733,9 +775,9 @@ bool Engine::build_program() {
                          int barrier) {
         POp op{};
         op.type = P_GEMV; op.barrier = barrier; op.nv = nv;
-        int ncta; size_t sm;
-        op.g = make_gemv(A, B, xin, ldx, nv, norm, act, y, ldy, resid, ldr, epi, xn_out, ldxn, nullptr, &ncta, &sm);
-        prog_smem = std::max(prog_smem, sm);
+        int ncta; size_t sl, sm;
+        op.g = make_gemv(A, B, xin, ldx, nv, norm, act, y, ldy, resid, ldr, epi, xn_out, ldxn, nullptr, &ncta, &sl, &sm);
+        prog_smem = std::max(prog_smem, gemv_work_bytes(A.type, A.cols, nv, gemv_rpc(A.rows, n_sm)));
         prog.push_back(op);
     };
     auto push_layers = [&](std::vector<LayerW> & Ls, __half * kbase, __half * vbase, int ctx, const float2 * rope,
@@ -747,13 +789,8 @@ bool Engine::build_program() {
             push_gemv(l.qkv, nullptr, X, H, M, l.attn_norm, ACT_F16, qkv, QKVD(), nullptr, 0, EPI_STORE, nullptr, 0, 1);
             POp op{};
             op.type = P_ATTN; op.barrier = 1;
-            FusedAttn & a = op.a;
-            a.qkv = qkv; a.ldq = QKVD(); a.n_heads = NH; a.n_kv_heads = NKV;
-            a.q_norm = l.q_norm; a.k_norm = l.k_norm; a.eps = c.rms_norm_eps; a.rope = rope;
-            a.kc = kbase + il * layer_elems; a.vc = vbase + il * layer_elems;
-            a.pos_ptr = pos_ptr; a.pos_static = pos_static; a.M = M; a.f32_mode = f32 ? 1 : 0;
-            a.scale = 1.0f / sqrtf((float) QTTS_HD); a.out = att; a.ldo = QD();
-            a.dump = ((int) il == dump_layer) ? dump : nullptr; a.dump_stride = ctx;
+            op.a = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, M, pos_ptr, pos_static,
+                                   f32, ((int) il == dump_layer) ? dump : nullptr, ctx);
             prog_smem = std::max(prog_smem, fused_attn_smem(f32 ? M : ctx, G, M));
             prog.push_back(op);
             push_gemv(l.o, nullptr, att, QD(), M, nullptr, ACT_F16, X, H, X, H, EPI_RESID, nullptr, 0, 1);
@@ -770,9 +807,15 @@ bool Engine::build_program() {
     ia.H = H; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
     ia.trailing = trailing; ia.pad = pad; ia.st = st; ia.n_cb = c.n_codebooks;
     auto push_input = [&](int mode, int g, float * out) {
+        InputArgs in = ia;
+        in.mode = mode; in.g = g; in.out = out;
+        if (!prog.empty() && prog.back().type == P_SAMPLE && !prog.back().has_in) {
+            prog.back().has_in = 1;   // CTA 0 samples, then builds the inputs: no grid barrier between
+            prog.back().in = in;
+            return;
+        }
         POp op{};
-        op.type = P_INPUT; op.barrier = 1;
-        op.in = ia; op.in.mode = mode; op.in.g = g; op.in.out = out;
+        op.type = P_INPUT; op.barrier = 1; op.in = in;
         prog.push_back(op);
     };
     push_sample(logits, c.codec_vocab_size, 0);
@@ -800,9 +843,8 @@ bool Engine::build_program() {
     }
 
     // Weight staging.  The k-th GEMV of the frame reads shared-memory buffer
-    // k & 1; its row slice is copied there by the op that follows GEMV k-2
-    // (cyclically; the first two are copied at launch start), i.e. about one op
-    // ahead and before the grid barrier that precedes it.  Every frame has an
+    // k & 1; its row slice is copied there while the grid waits at the barrier
+    // after GEMV k-2 (cyclically; the first two are copied at launch start).  Every frame has an
     // even number of GEMVs (4L + 1 + 15 (4L_cp + 1)), so the buffer parity of a
     // GEMV is the same in every frame.
     std::vector<int> gi;
@@ -812,12 +854,12 @@ bool Engine::build_program() {
     if (m < 2 || (m & 1)) { err = "unexpected GEMV count in the frame program"; return false; }
     for (int k = 0; k < m; ++k) {
         prog[gi[k]].slot = k & 1;
-        const int prev = gi[(k - 2 + m) % m];
-        POp & site = prog[(prev + 1) % prog.size()];
+        POp & site = prog[gi[(k - 2 + m) % m]];
         site.issue = 1;
         site.issue_slot = k & 1;
         site.iA = prog[gi[k]].g.A;
         site.iB = prog[gi[k]].g.B;
+        site.iG = prog[gi[k]].g.norm_g;
     }
     pk_first[0] = gi[0];
     pk_first[1] = gi[1];
@@ -826,10 +868,7 @@ bool Engine::build_program() {
     size_t wb = 0;
     for (int k = 0; k < m; ++k) {
         const GemvArgs & g = prog[gi[k]].g;
-        const int rpc = (g.A.rows + n_sm - 1) / n_sm;
-        const size_t es = g.A.type == W_F16 ? 2 : 1;
-        const size_t per = (size_t) rpc * g.A.cols * es + (g.A.type == W_Q8_0 ? (size_t) rpc * (g.A.cols / 32) * 2 : 0);
-        wb = std::max(wb, per * (g.B.w ? 2 : 1));
+        wb = std::max(wb, slice_layout(g.A, g.B.w != nullptr, g.norm_g != nullptr, gemv_rpc(g.A.rows, n_sm)).total);
     }
     pk_wbuf = (wb + 127) & ~(size_t) 127;
 
@@ -896,7 +935,7 @@ bool Engine::launch_persistent(int n) {
     pa.trace = nullptr;
     trace_n = 0;
     if (getenv("QTTS_PK_TRACE")) {
-        const size_t need = (size_t) 2 * prog.size() * n;
+        const size_t need = (size_t) PK_TRACE_SLOTS * prog.size() * n;
         if (need > trace_cap) {
             if (d_trace) cudaFree(d_trace);
             trace_cap = need;
@@ -1317,21 +1356,17 @@ int32_t qtts_op_gemv(int32_t device, int32_t wtype, const void * w, int32_t rows
         a.A = A; a.x = (const float *) dx; a.ldx = cols; a.nv = nv; a.norm_g = (const float *) dg; a.eps = eps;
         a.act = act_f32 ? ACT_F32 : ACT_F16; a.y = (float *) dy; a.ldy = rows; a.epi = EPI_STORE;
         a.block_dots = (int *) dbd;
-        int ncta = std::min(n_sm, rows);
-        const int rpc = (rows + ncta - 1) / ncta;
-        ncta = (rows + rpc - 1) / rpc;
-        const int nchunk = wtype == W_F16 ? cols / 8 : cols / 16;
-        int ks = (2 * QTTS_WARPS + rpc - 1) / rpc;
-        a.kslices = std::max(1, std::min(ks, std::max(1, nchunk / 32)));
         const int NVt = nv == 1 ? 1 : nv == 2 ? 2 : 8;
-        const size_t smem = gemv_smem_bytes(wtype, cols, NVt, rpc, a.kslices);
-        cudaFuncSetAttribute(k_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (smem > 200 * 1024) ok = false;
-        else if (NVt == 1) k_gemv<1><<<ncta, QTTS_WARPS * 32, smem>>>(a);
-        else if (NVt == 2) k_gemv<2><<<ncta, QTTS_WARPS * 32, smem>>>(a);
-        else k_gemv<8><<<ncta, QTTS_WARPS * 32, smem>>>(a);
+        int ncta = 0;
+        size_t slice = 0, smem = 0;
+        if (!gemv_shape(A, false, dg != nullptr, NVt, n_sm, &ncta, &slice, &smem)) ok = false;
+        cudaFuncSetAttribute(k_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX);
+        cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX);
+        cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX);
+        if (!ok) {}
+        else if (NVt == 1) k_gemv<1><<<ncta, QTTS_WARPS * 32, smem>>>(a, slice);
+        else if (NVt == 2) k_gemv<2><<<ncta, QTTS_WARPS * 32, smem>>>(a, slice);
+        else k_gemv<8><<<ncta, QTTS_WARPS * 32, smem>>>(a, slice);
         chk(cudaGetLastError());
         chk(cudaDeviceSynchronize());
         if (ok) chk(cudaMemcpy(y, dy, sizeof(float) * nv * rows, cudaMemcpyDeviceToHost));

@@ -32,267 +32,288 @@ struct GemvArgs {
     const float * resid;    // EPI_RESID: y = acc + resid (resid may alias y)
     int ldr;
     int epi;
-    float * xn_out;         // CTA 0 writes the normalised input rows here (F32)
+    float * xn_out;         // the CTA owning row 0 writes the normalised input rows here (F32)
     int ldxn;
     const int * done;       // frame-loop stop flag (skip when *done)
-    int kslices;            // k-slices per row inside a CTA
     int * block_dots;       // Q8_0 test hook: per-block int32 dots [nv][rows][cols/32] (nullptr: off)
 };
 
-// Shared memory: float xs[NV][cols]; Q8_0 additionally int8 qa[NV][cols] and
-// float da[NV][cols/32]; then the per-item partials float[rpc*kslices][NV][2].
-__host__ __device__ inline size_t gemv_smem_bytes(int type, int cols, int nv, int rpc, int kslices) {
-    size_t b = (size_t) nv * cols * 4;
+constexpr size_t QTTS_GEMV_SMEM_MAX = 200 * 1024;   // dynamic shared memory of a stand-alone k_gemv
+
+// Rows [r0, r1) of a GEMV belong to CTA `cta` of `ncta` (rpc = ceil(rows / ncta)).
+__host__ __device__ inline int gemv_rpc(int rows, int ncta) { return (rows + ncta - 1) / ncta; }
+
+// A CTA's weight slice as staged in shared memory:
+//   A rows | B rows | A scales | B scales | RMSNorm gain (F32, cols)
+struct SliceLayout {
+    size_t bA, bS, gain_off, total;
+};
+__host__ __device__ inline SliceLayout slice_layout(const DMat & A, bool dual, bool has_gain, int nrow) {
+    SliceLayout L;
+    const bool q8 = A.type == W_Q8_0;
+    L.bA = (size_t) nrow * A.cols * (q8 ? 1 : 2);
+    L.bS = q8 ? (size_t) nrow * (A.cols / 32) * 2 : 0;
+    const int nm = dual ? 2 : 1;
+    L.gain_off = nm * (L.bA + L.bS);
+    L.total = L.gain_off + (has_gain ? (size_t) A.cols * 4 : 0);
+    return L;
+}
+
+// Shared-memory work area of a GEMV: x [NV][cols] F32, residuals [NV][rpc],
+// Q8_0: activation quants [NV][cols] and scales [NV][cols/32].
+__host__ __device__ inline size_t gemv_work_bytes(int type, int cols, int nv, int rpc) {
+    size_t b = (size_t) nv * cols * 4 + (size_t) nv * ((rpc + 3) & ~3) * 4;
     if (type == W_Q8_0) b += (size_t) nv * cols + (size_t) nv * (cols / 32) * 4;
-    b += (size_t) rpc * kslices * nv * 2 * 4;
     return b;
 }
 
-template <int NV>
-__device__ __forceinline__ void gemv_prologue(const GemvArgs & a, float * xs, int8_t * qa, float * da, const int cta) {
-    __shared__ double red[32];
-    const int cols = a.A.cols;
-    const int tid = threadIdx.x, nt = blockDim.x;
-    for (int v = 0; v < NV; ++v) {
-        float * xr = xs + (size_t) v * cols;
-        if (v >= a.nv) {
-            for (int c = tid; c < cols; c += nt) xr[c] = 0.0f;
-            continue;
+// One thread: copy the CTA's slice of (A, B) and the norm gain into `buf`,
+// completing on mbarrier m (expect_tx covers every byte, so the phase completes
+// even when this CTA owns no rows).
+__device__ __forceinline__ void issue_gemv_slice(const DMat & A, const DMat & B, const float * gain, uint8_t * buf,
+                                                 uint64_t * m, int cta, int ncta) {
+    const int rpc = gemv_rpc(A.rows, ncta);
+    const int r0 = cta * rpc, r1 = min(A.rows, r0 + rpc);
+    const int nrow = r1 > r0 ? r1 - r0 : 0;
+    const bool dual = B.w != nullptr;
+    const SliceLayout L = slice_layout(A, dual, gain != nullptr, nrow);
+    mbar_expect_tx(m, nrow ? (unsigned) L.total : 0u);
+    if (!nrow) return;
+    const size_t es = A.type == W_Q8_0 ? 1 : 2;
+    const DMat * mats[2] = {&A, &B};
+    for (int k = 0; k < (dual ? 2 : 1); ++k) {
+        const char * src = static_cast<const char *>(mats[k]->w) + (size_t) r0 * A.cols * es;
+        for (size_t o = 0; o < L.bA; o += 32768) {
+            const unsigned n = (unsigned)(L.bA - o < 32768 ? L.bA - o : 32768);
+            bulk_g2s(buf + k * L.bA + o, src + o, n, m);
         }
-        const float * src = a.x + (size_t) v * a.ldx;
-        double ss = 0.0;
-        for (int c = tid; c < cols; c += nt) {
-            const float t = src[c];
-            xr[c] = t;
-            ss += (double) __fmul_rn(t, t);
-        }
-        if (a.norm_g) {
-            ss = block_sum_d(ss, red);
-            const float mean = (float)(ss / (double) cols);
-            const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
-            for (int c = tid; c < cols; c += nt) xr[c] = __fmul_rn(__fmul_rn(xr[c], scale), a.norm_g[c]);
-        }
-        if (a.xn_out && cta == 0)
-            for (int c = tid; c < cols; c += nt) a.xn_out[(size_t) v * a.ldxn + c] = xr[c];
+        if (L.bS)
+            bulk_g2s(buf + (dual ? 2 : 1) * L.bA + k * L.bS, mats[k]->d + (size_t) r0 * (A.cols / 32), (unsigned) L.bS, m);
     }
-    __syncthreads();
-    if (a.A.type == W_F16) {
-        if (a.act == ACT_F16)
-            for (int i = tid; i < NV * cols; i += nt) xs[i] = round_f16(xs[i]);
-    } else {  // Q8_0: quantize_row_q8_0_ref per 32-block, one warp per block
-        const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
-        const int nb = cols / 32;
-        for (int blk = warp; blk < NV * nb; blk += nw) {
-            const int v = blk / nb, b = blk % nb;
-            const float val = xs[(size_t) v * cols + b * 32 + lane];
-            const float amax = warp_max(fabsf(val));
-            const float d = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-            qa[(size_t) v * cols + b * 32 + lane] = (int8_t) roundf(__fmul_rn(val, id));
-            if (lane == 0) da[(size_t) v * nb + b] = __half2float(__float2half_rn(d));
-        }
-    }
-    __syncthreads();
+    if (gain) bulk_g2s(buf + L.gain_off, gain, (unsigned)(A.cols * 4), m);
 }
 
-template <int NV>
-__device__ __forceinline__ void gemv_store(const GemvArgs & a, int r, int v, float accA, float accB) {
-    if (v >= a.nv) return;
+__device__ __forceinline__ void gemv_store(const GemvArgs & a, int r, int v, float accA, float accB, const float * rs,
+                                           int rl, int rstride) {
     float out;
     if (a.epi == EPI_SWIGLU) out = __fmul_rn(silu(accA), accB);
-    else if (a.epi == EPI_RESID) out = __fadd_rn(accA, a.resid[(size_t) v * a.ldr + r]);
+    else if (a.epi == EPI_RESID) out = __fadd_rn(accA, rs[v * rstride + rl]);
     else out = accA;
     a.y[(size_t) v * a.ldy + r] = out;
 }
 
-// Rows of A (and B) are split into contiguous per-CTA ranges.  Inside a CTA
-// the work items are (row, k-slice) pairs; a warp takes two items at a time
-// and issues all 16-byte loads of an iteration before the math.  Per-item
-// partial dots go to shared memory and are summed in slice order, so the
-// result depends only on (rows, grid, kslices), never on scheduling.
-// Where a CTA reads its weight rows from: global memory (streaming loads) or a
-// shared-memory copy of its row slice [r0, r1) (persistent frame kernel).
-struct WSrc {
-    const uint8_t * a, * b;       // F16 halves or int8 quants, row stride cols * elem size
-    const __half * sa, * sb;      // Q8_0 scales, row stride cols / 32
-    int rbase;                    // first row held by the pointers (0 for global)
-};
-
-template <bool SMEM>
-__device__ __forceinline__ uint4 ld_w16(const uint8_t * p) {
-    if constexpr (SMEM) return *reinterpret_cast<const uint4 *>(p);
-    else return ld_stream(p);
-}
-
-template <int NV, bool SMEM = false>
-__device__ __forceinline__ void gemv_body(const GemvArgs & a, const int cta, const int ncta, uint8_t * smem_raw,
-                                          const WSrc * wsrc = nullptr) {
+// GEMV over this CTA's rows [r0, r1) with the weight slice in shared memory
+// (`wsm`, layout slice_layout; complete once mbarrier `m` reaches `parity`, or
+// immediately when m == nullptr).  Latency-oriented: one burst of global loads
+// (activations, residuals), one block barrier, per-warp RMSNorm scale, one warp
+// per row.  Reduction order of a row: lane l accumulates the 16-byte chunks
+// l, l+32, ... in order (8 sequential FMAs per F16 chunk; one block term per
+// lane pair for Q8_0), then a butterfly over the 32 lanes.
+template <int NV>
+__device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, const int ncta, const uint8_t * wsm,
+                                           uint8_t * work, uint64_t * m, unsigned parity,
+                                           unsigned long long * ready_stamp = nullptr) {
     const int cols = a.A.cols, rows = a.A.rows;
-    const int rpc = (rows + ncta - 1) / ncta;
+    const int rpc = gemv_rpc(rows, ncta);
     const int r0 = cta * rpc, r1 = min(rows, r0 + rpc);
-    if (r0 >= r1) return;
-    WSrc src;
-    if (SMEM) src = *wsrc;
-    else src = WSrc{static_cast<const uint8_t *>(a.A.w), static_cast<const uint8_t *>(a.B.w), a.A.d, a.B.d, 0};
-    float * xs = reinterpret_cast<float *>(smem_raw);
-    int8_t * qa = reinterpret_cast<int8_t *>(xs + (size_t) NV * cols);
-    float * da = reinterpret_cast<float *>(qa + (size_t)(a.A.type == W_Q8_0 ? NV * cols : 0));
-    float * part = da + (a.A.type == W_Q8_0 ? NV * (cols / 32) : 0);
-    gemv_prologue<NV>(a, xs, qa, da, cta);
+    const int nrow = r1 > r0 ? r1 - r0 : 0;
+    const bool q8 = a.A.type == W_Q8_0, dual = a.B.w != nullptr;
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+    const int nv = a.nv;
+    const int rstride = (rpc + 3) & ~3;
+    float * xs = reinterpret_cast<float *>(work);
+    float * rs = xs + NV * cols;
+    int8_t * qa = reinterpret_cast<int8_t *>(rs + NV * rstride);
+    float * da = reinterpret_cast<float *>(qa + (q8 ? NV * cols : 0));
 
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool dual = a.B.w != nullptr;
-    const int S = a.kslices;
-    const int nrow = r1 - r0, n_items = nrow * S;
-    constexpr int IU = 2, KU = 4;
+    // 1. activations and residuals: every load issued before any is used
+    const int c4 = cols / 4;
+    for (int base = 0; base < nv * c4; base += nt * 4) {
+        float4 t[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = base + tid + k * nt;
+            const int v = i >= c4 ? (i >= 2 * c4 ? i / c4 : 1) : 0;
+            if (i < nv * c4) t[k] = reinterpret_cast<const float4 *>(a.x + (size_t) v * a.ldx)[i - v * c4];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = base + tid + k * nt;
+            if (i < nv * c4) reinterpret_cast<float4 *>(xs)[i] = t[k];
+        }
+    }
+    if (a.epi == EPI_RESID)
+        for (int v = 0; v < nv; ++v)
+            for (int r = tid; r < nrow; r += nt) rs[v * rstride + r] = a.resid[(size_t) v * a.ldr + r0 + r];
+    __syncthreads();
+    if (m) {   // the weight slice (and gain) must have landed
+        const bool ok = mbar_wait(m, parity);
+        if (__syncthreads_or(!ok)) return false;
+        if (ready_stamp && threadIdx.x == 0) {   // diagnostics: latest weight arrival over the CTAs
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+            atomicMax(ready_stamp, t);
+        }
+    }
+    const SliceLayout L = slice_layout(a.A, dual, a.norm_g != nullptr, nrow);
+    const float * gain = a.norm_g ? reinterpret_cast<const float *>(wsm + L.gain_off) : nullptr;
 
-    if (a.A.type == W_F16) {
+    // 2. RMSNorm: every warp computes the scale of each row vector (double sum,
+    //    lane-strided then butterfly), then normalises its share of the columns
+    //    in place; F16 weights also round the activation to F16 here.
+    if (gain) {
+        float sc[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            sc[v] = 1.0f;
+            if (v < nv) {
+                double ss = 0.0;
+                for (int c = lane; c < cols; c += 32) { const float t = xs[v * cols + c]; ss += (double) __fmul_rn(t, t); }
+                ss = warp_sum_d(ss);
+                const float mean = (float)(ss / (double) cols);
+                sc[v] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
+            }
+        }
+        __syncthreads();   // every warp has read the raw rows
+        for (int i = tid; i < nv * cols; i += nt) {
+            const int v = i / cols, c = i - v * cols;
+            float s1 = 1.0f;
+#pragma unroll
+            for (int u = 0; u < NV; ++u) if (u == v) s1 = sc[u];
+            const float t = __fmul_rn(__fmul_rn(xs[i], s1), gain[c]);
+            if (a.xn_out && r0 == 0) a.xn_out[(size_t) v * a.ldxn + c] = t;   // hidden_states (post-norm, unrounded)
+            xs[i] = (!q8 && a.act == ACT_F16) ? round_f16(t) : t;
+        }
+        __syncthreads();
+    } else {
+        if (a.xn_out && r0 == 0)
+            for (int i = tid; i < nv * cols; i += nt) a.xn_out[(size_t)(i / cols) * a.ldxn + i % cols] = xs[i];
+        if (!q8 && a.act == ACT_F16) {
+            for (int i = tid; i < nv * cols; i += nt) xs[i] = round_f16(xs[i]);
+            __syncthreads();
+        }
+    }
+
+    if (!q8) {
+        const uint8_t * wa = wsm;
+        const uint8_t * wb = wsm + L.bA;
         const int nchunk = cols / 8;
-        const int sl = (nchunk + S - 1) / S;
-        for (int it0 = warp * IU; it0 < n_items; it0 += QTTS_WARPS * IU) {
-            float accA[IU][NV], accB[IU][NV];
-            int row[IU], cbeg[IU], cend[IU];
+        for (int rl = warp; rl < nrow; rl += nw) {
+            float acc[NV], accb[NV];
 #pragma unroll
-            for (int u = 0; u < IU; ++u) {
-                const int it = it0 + u;
-                const bool iv = it < n_items;
-                row[u] = r0 + (iv ? it / S : 0);
-                cbeg[u] = (iv ? it % S : 0) * sl;
-                cend[u] = iv ? min(nchunk, cbeg[u] + sl) : 0;
-#pragma unroll
-                for (int v = 0; v < NV; ++v) accA[u][v] = accB[u][v] = 0.0f;
-            }
-            for (int cc = 0; cc < sl; cc += 32 * KU) {
-                uint4 wa[IU][KU], wb[IU][KU];
-#pragma unroll
-                for (int u = 0; u < IU; ++u)
-#pragma unroll
-                    for (int k = 0; k < KU; ++k) {
-                        const int c = cbeg[u] + cc + lane + 32 * k;
-                        const bool ok = c < cend[u];
-                        const size_t off = ((size_t)(row[u] - src.rbase) * cols + (size_t) c * 8) * 2;
-                        wa[u][k] = ok ? ld_w16<SMEM>(src.a + off) : make_uint4(0, 0, 0, 0);
-                        wb[u][k] = (ok && dual) ? ld_w16<SMEM>(src.b + off) : make_uint4(0, 0, 0, 0);
-                    }
-#pragma unroll
-                for (int u = 0; u < IU; ++u)
-#pragma unroll
-                    for (int k = 0; k < KU; ++k) {
-                        const int c = cbeg[u] + cc + lane + 32 * k;
-                        if (c >= cend[u]) continue;
-#pragma unroll
-                        for (int v = 0; v < NV; ++v) {
-                            const float * xv = xs + (size_t) v * cols + (size_t) c * 8;
-                            accA[u][v] = dot8(wa[u][k], xv, accA[u][v]);
-                            if (dual) accB[u][v] = dot8(wb[u][k], xv, accB[u][v]);
-                        }
-                    }
-            }
-#pragma unroll
-            for (int u = 0; u < IU; ++u)
+            for (int v = 0; v < NV; ++v) acc[v] = accb[v] = 0.0f;
+            const uint4 * ra = reinterpret_cast<const uint4 *>(wa + (size_t) rl * cols * 2);
+            const uint4 * rb = reinterpret_cast<const uint4 *>(wb + (size_t) rl * cols * 2);
+            for (int c = lane; c < nchunk; c += 32) {
+                const uint4 w = ra[c];
+                const uint4 w2 = dual ? rb[c] : make_uint4(0, 0, 0, 0);
 #pragma unroll
                 for (int v = 0; v < NV; ++v) {
-                    const float sa = warp_sum(accA[u][v]);
-                    const float sb = dual ? warp_sum(accB[u][v]) : 0.0f;
-                    if (lane == 0 && it0 + u < n_items) {
-                        part[((size_t)(it0 + u) * NV + v) * 2 + 0] = sa;
-                        part[((size_t)(it0 + u) * NV + v) * 2 + 1] = sb;
-                    }
+                    if (v >= nv) continue;
+                    const float4 x0 = reinterpret_cast<const float4 *>(xs + v * cols)[2 * c];
+                    const float4 x1 = reinterpret_cast<const float4 *>(xs + v * cols)[2 * c + 1];
+                    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    acc[v] = dot8(w, xv, acc[v]);
+                    if (dual) accb[v] = dot8(w2, xv, accb[v]);
                 }
-        }
-    } else {  // Q8_0: 16 quants per lane-chunk, lane pairs form one 32-block
-        const int nchunk = cols / 16, nb = cols / 32;
-        const int sl = (((nchunk + S - 1) / S) + 1) & ~1;   // even: slices start on a block
-        for (int it0 = warp * IU; it0 < n_items; it0 += QTTS_WARPS * IU) {
-            float accA[IU][NV], accB[IU][NV];
-            int row[IU], cbeg[IU], cend[IU];
-#pragma unroll
-            for (int u = 0; u < IU; ++u) {
-                const int it = it0 + u;
-                const bool iv = it < n_items;
-                row[u] = r0 + (iv ? it / S : 0);
-                cbeg[u] = (iv ? it % S : 0) * sl;
-                cend[u] = iv ? min(nchunk, cbeg[u] + sl) : 0;
-#pragma unroll
-                for (int v = 0; v < NV; ++v) accA[u][v] = accB[u][v] = 0.0f;
-            }
-            for (int cc = 0; cc < sl; cc += 32 * KU) {
-                uint4 wa[IU][KU], wb[IU][KU];
-                float swa[IU][KU], swb[IU][KU];
-#pragma unroll
-                for (int u = 0; u < IU; ++u)
-#pragma unroll
-                    for (int k = 0; k < KU; ++k) {
-                        const int c = cbeg[u] + cc + lane + 32 * k;
-                        const bool ok = c < cend[u];
-                        const size_t ro = (size_t)(row[u] - src.rbase);
-                        wa[u][k] = ok ? ld_w16<SMEM>(src.a + ro * cols + (size_t) c * 16) : make_uint4(0, 0, 0, 0);
-                        wb[u][k] = (ok && dual) ? ld_w16<SMEM>(src.b + ro * cols + (size_t) c * 16) : make_uint4(0, 0, 0, 0);
-                        swa[u][k] = ok ? __half2float(src.sa[ro * nb + (c >> 1)]) : 0.0f;
-                        swb[u][k] = (ok && dual) ? __half2float(src.sb[ro * nb + (c >> 1)]) : 0.0f;
-                    }
-#pragma unroll
-                for (int u = 0; u < IU; ++u)
-#pragma unroll
-                    for (int k = 0; k < KU; ++k) {
-                        const int c = cbeg[u] + cc + lane + 32 * k;
-                        const bool okc = c < cend[u];   // uniform within a lane pair
-#pragma unroll
-                        for (int v = 0; v < NV; ++v) {
-                            const int4 xq = okc ? *reinterpret_cast<const int4 *>(qa + (size_t) v * cols + (size_t) c * 16)
-                                                : make_int4(0, 0, 0, 0);
-                            const float dx = okc ? da[(size_t) v * nb + (c >> 1)] : 0.0f;
-                            int ia = __dp4a((int) wa[u][k].x, xq.x, 0);
-                            ia = __dp4a((int) wa[u][k].y, xq.y, ia);
-                            ia = __dp4a((int) wa[u][k].z, xq.z, ia);
-                            ia = __dp4a((int) wa[u][k].w, xq.w, ia);
-                            ia += __shfl_xor_sync(0xffffffffu, ia, 1);   // 32-block int32 dot
-                            if (a.block_dots && !(lane & 1) && okc && v < a.nv)
-                                a.block_dots[((size_t) v * rows + row[u]) * nb + (c >> 1)] = ia;
-                            if (!(lane & 1) && okc)
-                                accA[u][v] = __fadd_rn(accA[u][v], __fmul_rn((float) ia, __fmul_rn(swa[u][k], dx)));
-                            if (dual) {
-                                int ib = __dp4a((int) wb[u][k].x, xq.x, 0);
-                                ib = __dp4a((int) wb[u][k].y, xq.y, ib);
-                                ib = __dp4a((int) wb[u][k].z, xq.z, ib);
-                                ib = __dp4a((int) wb[u][k].w, xq.w, ib);
-                                ib += __shfl_xor_sync(0xffffffffu, ib, 1);
-                                if (!(lane & 1) && okc)
-                                    accB[u][v] = __fadd_rn(accB[u][v], __fmul_rn((float) ib, __fmul_rn(swb[u][k], dx)));
-                            }
-                        }
-                    }
             }
 #pragma unroll
-            for (int u = 0; u < IU; ++u)
-#pragma unroll
-                for (int v = 0; v < NV; ++v) {
-                    const float s1 = warp_sum(accA[u][v]);
-                    const float s2 = dual ? warp_sum(accB[u][v]) : 0.0f;
-                    if (lane == 0 && it0 + u < n_items) {
-                        part[((size_t)(it0 + u) * NV + v) * 2 + 0] = s1;
-                        part[((size_t)(it0 + u) * NV + v) * 2 + 1] = s2;
-                    }
-                }
+            for (int v = 0; v < NV; ++v) {
+                if (v >= nv) continue;
+                const float s1 = warp_sum(acc[v]);
+                const float s2 = dual ? warp_sum(accb[v]) : 0.0f;
+                if (lane == 0) gemv_store(a, r0 + rl, v, s1, s2, rs, rl, rstride);
+            }
         }
+        return true;
+    }
+
+    // Q8_0: quantise the (normalised) activation once per 32-block, as
+    // quantize_row_q8_0_ref: d = amax / 127, id = 1 / d, q = roundf(x * id).
+    const int nb = cols / 32;
+    for (int blk = warp; blk < nv * nb; blk += nw) {
+        const int v = blk / nb, b = blk % nb;
+        const float val = xs[v * cols + b * 32 + lane];
+        const float amax = warp_max(fabsf(val));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        qa[v * cols + b * 32 + lane] = (int8_t) roundf(__fmul_rn(val, id));
+        if (lane == 0) da[v * nb + b] = __half2float(__float2half_rn(d));
     }
     __syncthreads();
-    for (int t = threadIdx.x; t < nrow * NV; t += blockDim.x) {
-        const int rl = t / NV, v = t % NV;
-        float sa = 0.0f, sb = 0.0f;
-        for (int s2 = 0; s2 < S; ++s2) {
-            sa = __fadd_rn(sa, part[((size_t)(rl * S + s2) * NV + v) * 2 + 0]);
-            sb = __fadd_rn(sb, part[((size_t)(rl * S + s2) * NV + v) * 2 + 1]);
+    const uint8_t * qwa = wsm;
+    const uint8_t * qwb = wsm + L.bA;
+    const __half * swa = reinterpret_cast<const __half *>(wsm + (dual ? 2 : 1) * L.bA);
+    const __half * swb = reinterpret_cast<const __half *>(wsm + (dual ? 2 : 1) * L.bA + L.bS);
+    const int nchunk = cols / 16;
+    for (int rl = warp; rl < nrow; rl += nw) {
+        float acc[NV], accb[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[v] = accb[v] = 0.0f;
+        const int4 * ra = reinterpret_cast<const int4 *>(qwa + (size_t) rl * cols);
+        const int4 * rb = reinterpret_cast<const int4 *>(qwb + (size_t) rl * cols);
+        for (int c0 = 0; c0 < nchunk; c0 += 32) {      // uniform trip count: full-mask shuffles inside
+            const int c = c0 + lane;
+            const bool ok = c < nchunk;                   // uniform within a lane pair (nchunk is even)
+            const int4 w = ok ? ra[c] : make_int4(0, 0, 0, 0);
+            const int4 w2 = (ok && dual) ? rb[c] : make_int4(0, 0, 0, 0);
+            const float dwa = ok ? __half2float(swa[rl * nb + (c >> 1)]) : 0.0f;
+            const float dwb = (ok && dual) ? __half2float(swb[rl * nb + (c >> 1)]) : 0.0f;
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                if (v >= nv) continue;
+                const int4 xq = ok ? reinterpret_cast<const int4 *>(qa + v * cols)[c] : make_int4(0, 0, 0, 0);
+                const float dx = ok ? da[v * nb + (c >> 1)] : 0.0f;
+                int ia = __dp4a(w.x, xq.x, 0);
+                ia = __dp4a(w.y, xq.y, ia);
+                ia = __dp4a(w.z, xq.z, ia);
+                ia = __dp4a(w.w, xq.w, ia);
+                ia += __shfl_xor_sync(0xffffffffu, ia, 1);   // the 32-block int32 dot
+                if (a.block_dots && ok && !(lane & 1))
+                    a.block_dots[((size_t) v * rows + r0 + rl) * nb + (c >> 1)] = ia;
+                if (ok && !(lane & 1)) acc[v] = __fadd_rn(acc[v], __fmul_rn((float) ia, __fmul_rn(dwa, dx)));
+                if (dual) {
+                    int ib = __dp4a(w2.x, xq.x, 0);
+                    ib = __dp4a(w2.y, xq.y, ib);
+                    ib = __dp4a(w2.z, xq.z, ib);
+                    ib = __dp4a(w2.w, xq.w, ib);
+                    ib += __shfl_xor_sync(0xffffffffu, ib, 1);
+                    if (ok && !(lane & 1)) accb[v] = __fadd_rn(accb[v], __fmul_rn((float) ib, __fmul_rn(dwb, dx)));
+                }
+            }
         }
-        gemv_store<NV>(a, r0 + rl, v, sa, sb);
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            if (v >= nv) continue;
+            const float s1 = warp_sum(acc[v]);
+            const float s2 = dual ? warp_sum(accb[v]) : 0.0f;
+            if (lane == 0) gemv_store(a, r0 + rl, v, s1, s2, rs, rl, rstride);
+        }
     }
+    return true;
 }
 
+// Stand-alone GEMV launch (CUDA-graph path, prefill, kernel tests): thread 0
+// stages this CTA's weight slice into shared memory with TMA bulk copies while
+// all threads load the activations.
 template <int NV>
-__global__ void __launch_bounds__(QTTS_WARPS * 32) k_gemv(GemvArgs a) {
+__global__ void __launch_bounds__(QTTS_WARPS * 32) k_gemv(GemvArgs a, size_t slice_bytes) {
     if (a.done && *a.done) return;
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    gemv_body<NV>(a, blockIdx.x, gridDim.x, smem_raw);
+    const int rpc = gemv_rpc(a.A.rows, gridDim.x);
+    if ((int) blockIdx.x * rpc >= a.A.rows) return;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t mbar;
+    if (threadIdx.x == 0) {
+        mbar_init(&mbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        issue_gemv_slice(a.A, a.B, a.norm_g, smem_raw, &mbar, blockIdx.x, gridDim.x);
+    }
+    __syncthreads();
+    if (!gemv_slice<NV>(a, blockIdx.x, gridDim.x, smem_raw, smem_raw + slice_bytes, &mbar, 0u)) {
+        // the copy did not complete within the wait limit: wait once more (bounded) so
+        // no bulk copy is in flight when the block exits, and leave the output unwritten
+        mbar_wait(&mbar, 0u);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -421,7 +442,7 @@ __host__ __device__ inline size_t attn_smem_bytes(int max_keys, int group) {
 
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
     if (a.done && *a.done) return;
-    extern __shared__ __align__(16) uint8_t smem_raw[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
     const int g = blockIdx.x, i = blockIdx.y;
     const int G = a.n_heads / a.n_kv_heads;
     const int n_past = a.pos_ptr ? *a.pos_ptr : a.pos_static;
@@ -535,6 +556,235 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
                                   __fadd_rn(part[2 * G * QTTS_HD + t], part[3 * G * QTTS_HD + t]));
         a.out[(size_t) i * a.ldo + (size_t)(g * G) * QTTS_HD + t] = s;
     }
+}
+
+// ---------------------------------------------------------------------------
+// Fused q/k RMSNorm + RoPE + KV append + attention for one (kv head, query row)
+// unit of a frame step (M = 1, F16 cache) or of the code-predictor 2-token
+// prefill (M = 2, F32 K/V of this call; unit row i normalises k rows 0..i itself,
+// so no unit reads another unit's output).  Same arithmetic as
+// k_qk_rope_store + k_attention (src/tts_transformer.cpp:1660-1712 for the
+// talker step, :2000-2011 / :2130-2160 for the code predictor), restructured
+// for latency: every global load of the unit (q/k/v rows, norm gains, RoPE
+// row, the first FA_KPASS cached keys and values) is issued before the first
+// block barrier, and the whole unit takes four barriers.
+struct FusedAttn {
+    float * qkv;              // raw q|k|v rows [M][ldq]
+    int ldq;
+    int n_heads, n_kv_heads;
+    const float * q_norm, * k_norm;
+    float eps;
+    const float2 * rope;      // [pos][64]
+    __half * kc, * vc;        // cache base of this layer [ctx][NKV][128]
+    const int * pos_ptr;
+    int pos_static;
+    int M;
+    int f32_mode;
+    float scale;
+    float * out;
+    int ldo;
+    float * dump;             // post-softmax rows [frame][n_heads][dump_stride] or nullptr
+    int dump_stride;
+    const int * done;         // stand-alone launch: skip when *done
+};
+
+constexpr int FA_THREADS = 512;
+constexpr int FA_KIT = 2;                              // key iterations per pass (16 warps x 4 keys each)
+constexpr int FA_KPASS = FA_KIT * (FA_THREADS / 32) * 4;  // keys per pass: 128
+constexpr int FA_NPG = FA_THREADS / 64;                // PV position groups: 8
+constexpr int FA_VIT = FA_KPASS / FA_NPG;              // V rows per thread per pass: 16
+
+// Shared memory of one unit: q heads [G][128], new K/V rows [M][128] x 2,
+// scores [G][n_max] and PV partial sums [FA_NPG][G][128] (F32).
+__host__ __device__ inline size_t fused_attn_smem(int max_keys, int G, int M) {
+    const size_t nk = (size_t)((max_keys + 3) & ~3);
+    return 4 * ((size_t) G * QTTS_HD + 2 * (size_t) M * QTTS_HD + G * nk + (size_t) FA_NPG * G * QTTS_HD) + 64;
+}
+
+__device__ __forceinline__ void fa_load_k(const FusedAttn & a, int j, int g, int sub, uint4 & k0, uint4 & k1) {
+    const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + ((size_t) j * a.n_kv_heads + g) * QTTS_HD + sub * 16);
+    k0 = kp[0];
+    k1 = kp[1];
+}
+
+// n_past: position of query row 0; frame: dump row (the persistent kernel
+// passes both from its own counters).
+__device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * smem, const DevState * st,
+                                const int n_past, const int frame) {
+    const int NKV = a.n_kv_heads, G = a.n_heads / a.n_kv_heads;
+    const int g = unit % NKV, i = unit / NKV;
+    const int pos = n_past + i;
+    const int n = a.f32_mode ? (i + 1) : (n_past + 1);   // keys attended
+    const int nc = a.f32_mode ? 0 : n_past;                // keys read from the cache
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
+    const int nk4 = (n + 3) & ~3;
+    float * qs = reinterpret_cast<float *>(smem);          // [G][128]
+    float * kn = qs + G * QTTS_HD;                         // [M][128] keys computed here
+    float * vn = kn + a.M * QTTS_HD;                       // [M][128]
+    float * sc = vn + a.M * QTTS_HD;                       // [G][nk4]
+    float * part = sc + G * nk4;                           // [FA_NPG][G][128]
+    const int jn0 = a.f32_mode ? 0 : n_past;               // first key held in kn/vn
+
+    // 1. loads: cached keys/values of the first pass go to registers
+    const int sub = lane & 7, slot = lane >> 3;
+    const int pg = tid >> 6, d2 = tid & 63;
+    uint4 kr[FA_KIT][2];
+    __half2 vr[FA_VIT];
+#pragma unroll
+    for (int it = 0; it < FA_KIT; ++it) {
+        const int j = it * (FA_THREADS / 8) + warp * 4 + slot;
+        if (j < nc) fa_load_k(a, j, g, sub, kr[it][0], kr[it][1]);
+        else kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int t = 0; t < FA_VIT; ++t) {
+        const int j = pg + t * FA_NPG;
+        vr[t] = j < nc ? *reinterpret_cast<const __half2 *>(a.vc + ((size_t) j * NKV + g) * QTTS_HD + 2 * d2)
+                       : __float2half2_rn(0.0f);
+    }
+    if (warp < G) {
+        const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
+        const float * qh = a.qkv + (size_t) i * a.ldq + (size_t)(g * G + warp) * QTTS_HD + lane * 4;
+        float x[4] = {qh[0], qh[1], qh[2], qh[3]};
+        head_norm_rope(x, a.q_norm, a.eps, rp, lane);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) qs[warp * QTTS_HD + lane * 4 + k] = a.f32_mode ? x[k] : round_f16(x[k]);
+    } else if (warp < G + (a.f32_mode ? i + 1 : 1)) {
+        const int j = a.f32_mode ? warp - G : i;           // row of this call whose k/v this warp prepares
+        const float2 * rp = a.rope + (size_t)(n_past + j) * (QTTS_HD / 2);
+        const float * kp = a.qkv + (size_t) j * a.ldq + QD + g * QTTS_HD + lane * 4;
+        const float * vp = a.qkv + (size_t) j * a.ldq + QD + KD + g * QTTS_HD + lane * 4;
+        float x[4] = {kp[0], kp[1], kp[2], kp[3]};
+        const float v[4] = {vp[0], vp[1], vp[2], vp[3]};
+        head_norm_rope(x, a.k_norm, a.eps, rp, lane);
+        const int r = a.f32_mode ? j : 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __half kh = __float2half_rn(x[k]), vh = __float2half_rn(v[k]);
+            kn[r * QTTS_HD + lane * 4 + k] = a.f32_mode ? x[k] : __half2float(kh);
+            vn[r * QTTS_HD + lane * 4 + k] = a.f32_mode ? v[k] : __half2float(vh);
+            if (j == i) {
+                a.kc[((size_t) pos * NKV + g) * QTTS_HD + lane * 4 + k] = kh;
+                a.vc[((size_t) pos * NKV + g) * QTTS_HD + lane * 4 + k] = vh;
+            }
+        }
+    }
+    __syncthreads();   // barrier 1: q heads and new k/v rows are in shared memory
+
+    // 2. scores; 8 lanes per key (16 dims each), 4 keys per warp per iteration
+    for (int p0 = 0; p0 < n; p0 += FA_KPASS) {
+#pragma unroll
+        for (int it = 0; it < FA_KIT; ++it) {
+            const int j = p0 + it * (FA_THREADS / 8) + warp * 4 + slot;
+            if (p0 > 0) {
+                if (j < nc) fa_load_k(a, j, g, sub, kr[it][0], kr[it][1]);
+                else kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
+            }
+            float kv[16];
+            if (j < nc) {
+#pragma unroll
+                for (int h8 = 0; h8 < 2; ++h8) {
+                    const __half2 * hp = reinterpret_cast<const __half2 *>(&kr[it][h8]);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 f = __half22float2(hp[k]);
+                        kv[8 * h8 + 2 * k] = f.x;
+                        kv[8 * h8 + 2 * k + 1] = f.y;
+                    }
+                }
+            } else if (j < n) {
+#pragma unroll
+                for (int d = 0; d < 16; ++d) kv[d] = kn[(j - jn0) * QTTS_HD + sub * 16 + d];
+            } else {
+#pragma unroll
+                for (int d = 0; d < 16; ++d) kv[d] = 0.0f;
+            }
+#pragma unroll
+            for (int h = 0; h < ATT_MAX_GROUP; ++h) {
+                if (h >= G) break;                      // G is uniform: shuffles stay full-warp
+                const float * qh = qs + h * QTTS_HD + sub * 16;
+                float s = 0.0f;
+#pragma unroll
+                for (int d = 0; d < 16; ++d) s = fmaf(kv[d], qh[d], s);
+                s += __shfl_xor_sync(0xffffffffu, s, 4);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                if (sub == 0 && j < n) sc[h * nk4 + j] = __fmul_rn(s, a.scale);
+            }
+        }
+    }
+    __syncthreads();   // barrier 2
+
+    // 3. softmax, one warp per head: max, expf, double sum, e * (float)(1/sum)
+    if (warp < G) {
+        float * row = sc + warp * nk4;
+        float mx = -INFINITY;
+        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, row[j]);
+        mx = warp_max(mx);
+        double sum = 0.0;
+        for (int j = lane; j < n; j += 32) {
+            const float e = expf(__fsub_rn(row[j], mx));
+            row[j] = e;
+            sum += (double) e;
+        }
+        sum = warp_sum_d(sum);
+        const float inv = (float)(1.0 / sum);
+        float * drow = a.dump ? a.dump + ((size_t) frame * a.n_heads + g * G + warp) * a.dump_stride : nullptr;
+        for (int j = lane; j < n; j += 32) {
+            const float pj = __fmul_rn(row[j], inv);
+            if (drow) drow[j] = pj;
+            row[j] = a.f32_mode ? pj : round_f16(pj);
+        }
+    }
+    __syncthreads();   // barrier 3
+
+    // 4. P x V: position group pg takes keys pg, pg + 8, ...; thread d2 two dims of all G heads
+    float acc[ATT_MAX_GROUP][2];
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_GROUP; ++h) acc[h][0] = acc[h][1] = 0.0f;
+    for (int p0 = 0; p0 < n; p0 += FA_KPASS) {
+#pragma unroll
+        for (int t = 0; t < FA_VIT; ++t) {
+            const int j = p0 + pg + t * FA_NPG;
+            float2 v;
+            if (j < nc) {
+                if (p0 > 0) vr[t] = *reinterpret_cast<const __half2 *>(a.vc + ((size_t) j * NKV + g) * QTTS_HD + 2 * d2);
+                v = __half22float2(vr[t]);
+            } else if (j < n) {
+                v = make_float2(vn[(j - jn0) * QTTS_HD + 2 * d2], vn[(j - jn0) * QTTS_HD + 2 * d2 + 1]);
+            } else {
+                break;
+            }
+#pragma unroll
+            for (int h = 0; h < ATT_MAX_GROUP; ++h)
+                if (h < G) {
+                    const float pj = sc[h * nk4 + j];
+                    acc[h][0] = fmaf(pj, v.x, acc[h][0]);
+                    acc[h][1] = fmaf(pj, v.y, acc[h][1]);
+                }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_GROUP; ++h)
+        if (h < G) {
+            part[(pg * G + h) * QTTS_HD + 2 * d2] = acc[h][0];
+            part[(pg * G + h) * QTTS_HD + 2 * d2 + 1] = acc[h][1];
+        }
+    __syncthreads();   // barrier 4
+    for (int t = tid; t < G * QTTS_HD; t += blockDim.x) {
+        float s = 0.0f;
+#pragma unroll
+        for (int q = 0; q < FA_NPG; ++q) s = __fadd_rn(s, part[q * G * QTTS_HD + t]);
+        a.out[(size_t) i * a.ldo + (size_t)(g * G) * QTTS_HD + t] = s;
+    }
+}
+
+// Stand-alone launch of the fused unit (CUDA-graph frame path): one CTA per unit.
+__global__ void __launch_bounds__(FA_THREADS) k_fused_attention(FusedAttn a, const DevState * st) {
+    if (a.done && *a.done) return;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    fused_attn_body(a, blockIdx.x, smem_raw, st, a.pos_ptr ? *a.pos_ptr : a.pos_static, st->frame);
 }
 
 struct SampleParams {

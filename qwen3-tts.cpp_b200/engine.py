@@ -303,14 +303,16 @@ class Engine:
                                   for i in range(4)}}
 
     def op_trace(self):
-        """(op types, CTA-0 timestamps [runs*ops][2]) of the last persistent run (QTTS_PK_TRACE=1)."""
+        """(op types, timestamps [frames*ops][5]) of the last persistent run with QTTS_PK_TRACE=1:
+        CTA 0 op start, CTA 0 copies issued, latest weight arrival over CTAs, CTA 0 work done,
+        latest work done over CTAs (ns, %globaltimer)."""
         n = lib().qtts_program_ops(self.h, None, 0)
         types = np.zeros(max(n, 1), np.int32)
         lib().qtts_program_ops(self.h, _p(types, C.c_int32), n)
         m = lib().qtts_op_trace(self.h, None, 0)
         tr = np.zeros(max(m, 1), np.uint64)
         lib().qtts_op_trace(self.h, tr.ctypes.data_as(C.POINTER(C.c_uint64)), m)
-        return types[:n], tr[:m].reshape(-1, 2)
+        return types[:n], tr[:m].reshape(-1, 5)
 
     def run_frames(self, n: int, codes_out: np.ndarray | None = None) -> int:
         ptr = None if codes_out is None else _p(codes_out, C.c_int32)

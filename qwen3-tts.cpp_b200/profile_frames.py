@@ -48,14 +48,18 @@ def main():
         names = {1: "gemv", 2: "attn", 3: "sample", 4: "input", 5: "frame_end"}
         n = len(types)
         t = tr[: n * got].astype(np.int64)
-        work = t[:, 1] - t[:, 0]
-        total = np.diff(np.append(t[:, 0], t[-1, 1]))
-        wait = total - work
+        nxt = np.append(t[1:, 0], t[-1, 4])
+        issue = t[:, 1] - t[:, 0]
+        ready = np.where(t[:, 2] > 0, t[:, 2] - t[:, 0], 0)
+        work0 = t[:, 3] - t[:, 0]
+        straggle = t[:, 4] - t[:, 3]
+        barrier = nxt - t[:, 4]
         for ty in sorted(set(types.tolist())):
             idx = np.nonzero(np.tile(types, got) == ty)[0]
-            print(f"op {names.get(ty, ty):9s} n={len(idx)//max(got,1):4d}/frame  work {work[idx].mean()/1e3:7.2f} us"
-                  f"  barrier+next {wait[idx].mean()/1e3:7.2f} us")
-        print(f"frame span {(t[-1, 1] - t[0, 0]) / 1e3 / max(got, 1):.1f} us")
+            print(f"op {names.get(ty, ty):9s} n={len(idx)//max(got,1):4d}/frame  issue {issue[idx].mean()/1e3:5.2f}"
+                  f"  last-weights {ready[idx].mean()/1e3:5.2f}  cta0-done {work0[idx].mean()/1e3:5.2f}"
+                  f"  last-done +{straggle[idx].mean()/1e3:5.2f}  barrier+next {barrier[idx].mean()/1e3:5.2f} us")
+        print(f"frame span {(t[-1, 4] - t[0, 0]) / 1e3 / max(got, 1):.1f} us")
     eng.close()
 
 
