@@ -770,6 +770,7 @@ bool Engine::build_program() {
     const int NH = c.n_attention_heads, NKV = c.n_key_value_heads, G = NH / NKV;
     prog.clear();
     prog_smem = 0;
+    bool prog_bad = false;
     auto push_gemv = [&](const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
                          float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
                          int barrier) {
@@ -809,14 +810,14 @@ bool Engine::build_program() {
     auto push_input = [&](int mode, int g, float * out) {
         InputArgs in = ia;
         in.mode = mode; in.g = g; in.out = out;
+        in.step_tab = mode == IN_CP_STEP ? cp_embd[g - 1] : nullptr;
         if (!prog.empty() && prog.back().type == P_SAMPLE && !prog.back().has_in) {
             prog.back().has_in = 1;   // CTA 0 samples, then builds the inputs: no grid barrier between
             prog.back().in = in;
             return;
         }
-        POp op{};
-        op.type = P_INPUT; op.barrier = 1; op.in = in;
-        prog.push_back(op);
+        err = "frame program: inputs must follow a sampler";
+        prog_bad = true;
     };
     push_sample(logits, c.codec_vocab_size, 0);
     push_input(IN_CP_PREFILL, 0, xcp);
@@ -832,6 +833,7 @@ bool Engine::build_program() {
         push_sample(cp_logits, V1, gstep + 1);
     }
     push_input(IN_TALKER, 0, x);
+    if (prog_bad) return false;
     push_layers(L, kc, vc, n_ctx, rope_t, x, 1, &st->pos, 0, false, c.intermediate_size, attn_dump ? d_attn : nullptr,
                 attn_layer);
     push_gemv(codec_head, nullptr, x, H, 1, out_norm, ACT_F16, logits, c.codec_vocab_size, nullptr, 0, EPI_STORE,

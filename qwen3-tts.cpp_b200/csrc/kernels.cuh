@@ -102,17 +102,26 @@ __device__ __forceinline__ void gemv_store(const GemvArgs & a, int r, int v, flo
     a.y[(size_t) v * a.ldy + r] = out;
 }
 
+// Activation rows live in shared memory in a two-plane layout per row: column
+// c = 8*k + w sits at (w / 4) * cols/2 + 4*k + w % 4, so the lane that owns the
+// 8-column chunk k reads two conflict-free float4 (plane 0 and plane 1).
+__device__ __forceinline__ int xpos(int c, int cols) { return ((c & 7) >> 2) * (cols >> 1) + ((c >> 3) << 2) + (c & 3); }
+
 // GEMV over this CTA's rows [r0, r1) with the weight slice in shared memory
 // (`wsm`, layout slice_layout; complete once mbarrier `m` reaches `parity`, or
 // immediately when m == nullptr).  Latency-oriented: one burst of global loads
-// (activations, residuals), one block barrier, per-warp RMSNorm scale, one warp
-// per row.  Reduction order of a row: lane l accumulates the 16-byte chunks
-// l, l+32, ... in order (8 sequential FMAs per F16 chunk; one block term per
-// lane pair for Q8_0), then a butterfly over the 32 lanes.
+// (activations, residuals), one warp per row, three block barriers.  The
+// RMSNorm sum of squares is a double sum over the CTA (thread-strided partials,
+// warp butterfly, then the 16 warp partials in order); normalisation and F16
+// rounding happen once, in place.  Reduction order of a row: lane l
+// accumulates the 8-column chunks l, l+32, ... in order (8 sequential FMAs per
+// F16 chunk; one 32-block term per lane pair for Q8_0), then a butterfly over
+// the 32 lanes.
 template <int NV>
 __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, const int ncta, const uint8_t * wsm,
                                            uint8_t * work, uint64_t * m, unsigned parity,
                                            unsigned long long * ready_stamp = nullptr) {
+    __shared__ double s_red[QTTS_WARPS][NV];
     const int cols = a.A.cols, rows = a.A.rows;
     const int rpc = gemv_rpc(rows, ncta);
     const int r0 = cta * rpc, r1 = min(rows, r0 + rpc);
@@ -125,93 +134,88 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
     float * rs = xs + NV * cols;
     int8_t * qa = reinterpret_cast<int8_t *>(rs + NV * rstride);
     float * da = reinterpret_cast<float *>(qa + (q8 ? NV * cols : 0));
+    const int c4 = cols >> 2, h8 = cols >> 3;
 
-    // 1. activations and residuals: every load issued before any is used
-    const int c4 = cols / 4;
-    for (int base = 0; base < nv * c4; base += nt * 4) {
-        float4 t[4];
+    // 1. activations (float4 i = columns 4i..4i+3 -> plane i & 1, chunk i >> 1) and residuals
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int i = base + tid + k * nt;
-            const int v = i >= c4 ? (i >= 2 * c4 ? i / c4 : 1) : 0;
-            if (i < nv * c4) t[k] = reinterpret_cast<const float4 *>(a.x + (size_t) v * a.ldx)[i - v * c4];
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int i = base + tid + k * nt;
-            if (i < nv * c4) reinterpret_cast<float4 *>(xs)[i] = t[k];
-        }
+    for (int v = 0; v < NV; ++v) {
+        if (v >= nv) break;
+        const float4 * src = reinterpret_cast<const float4 *>(a.x + (size_t) v * a.ldx);
+        float4 * dst = reinterpret_cast<float4 *>(xs + v * cols);
+        for (int i = tid; i < c4; i += nt) dst[(i & 1) * h8 + (i >> 1)] = src[i];
     }
     if (a.epi == EPI_RESID)
         for (int v = 0; v < nv; ++v)
             for (int r = tid; r < nrow; r += nt) rs[v * rstride + r] = a.resid[(size_t) v * a.ldr + r0 + r];
     __syncthreads();
-    if (m) {   // the weight slice (and gain) must have landed
-        const bool ok = mbar_wait(m, parity);
-        if (__syncthreads_or(!ok)) return false;
-        if (ready_stamp && threadIdx.x == 0) {   // diagnostics: latest weight arrival over the CTAs
+
+    // 2. RMSNorm partial sums; thread 0 waits for the weight slice
+    const bool has_norm = a.norm_g != nullptr;
+    if (has_norm) {
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            if (v >= nv) break;
+            double ss = 0.0;
+            for (int p = tid; p < cols; p += nt) { const float t = xs[v * cols + p]; ss += (double) __fmul_rn(t, t); }
+            ss = warp_sum_d(ss);
+            if (lane == 0) s_red[warp][v] = ss;
+        }
+    }
+    bool ok = true;
+    if (m && tid == 0) {
+        ok = mbar_wait(m, parity);
+        if (ok && ready_stamp) {   // diagnostics: latest weight arrival over the CTAs
             unsigned long long t;
             asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
             atomicMax(ready_stamp, t);
         }
     }
-    const SliceLayout L = slice_layout(a.A, dual, a.norm_g != nullptr, nrow);
-    const float * gain = a.norm_g ? reinterpret_cast<const float *>(wsm + L.gain_off) : nullptr;
+    if (__syncthreads_or(!ok)) return false;
+    const SliceLayout L = slice_layout(a.A, dual, has_norm, nrow);
+    const float * gain = has_norm ? reinterpret_cast<const float *>(wsm + L.gain_off) : nullptr;
 
-    // 2. RMSNorm: every warp computes the scale of each row vector (double sum,
-    //    lane-strided then butterfly), then normalises its share of the columns
-    //    in place; F16 weights also round the activation to F16 here.
-    if (gain) {
-        float sc[NV];
+    // 3. normalise (x * scale) * gain, round to F16 for F16 weights with an F16 activation
+    const bool round16 = !q8 && a.act == ACT_F16;
+    if (has_norm || round16 || a.xn_out) {
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
-            sc[v] = 1.0f;
-            if (v < nv) {
+            if (v >= nv) break;
+            float scale = 1.0f;
+            if (has_norm) {
                 double ss = 0.0;
-                for (int c = lane; c < cols; c += 32) { const float t = xs[v * cols + c]; ss += (double) __fmul_rn(t, t); }
-                ss = warp_sum_d(ss);
-                const float mean = (float)(ss / (double) cols);
-                sc[v] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
+                for (int w = 0; w < nw; ++w) ss += s_red[w][v];
+                scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(ss / (double) cols), a.eps)));
+            }
+            const int half = cols >> 1;
+            for (int p = tid; p < cols; p += nt) {
+                const int q = p >= half ? p - half : p;              // column of planar position p
+                const int c = ((q >> 2) << 3) + (p >= half ? 4 : 0) + (q & 3);
+                float t = xs[v * cols + p];
+                if (has_norm) t = __fmul_rn(__fmul_rn(t, scale), gain[c]);
+                if (a.xn_out && r0 == 0) a.xn_out[(size_t) v * a.ldxn + c] = t;   // hidden_states (post-norm, unrounded)
+                xs[v * cols + p] = round16 ? round_f16(t) : t;
             }
         }
-        __syncthreads();   // every warp has read the raw rows
-        for (int i = tid; i < nv * cols; i += nt) {
-            const int v = i / cols, c = i - v * cols;
-            float s1 = 1.0f;
-#pragma unroll
-            for (int u = 0; u < NV; ++u) if (u == v) s1 = sc[u];
-            const float t = __fmul_rn(__fmul_rn(xs[i], s1), gain[c]);
-            if (a.xn_out && r0 == 0) a.xn_out[(size_t) v * a.ldxn + c] = t;   // hidden_states (post-norm, unrounded)
-            xs[i] = (!q8 && a.act == ACT_F16) ? round_f16(t) : t;
-        }
         __syncthreads();
-    } else {
-        if (a.xn_out && r0 == 0)
-            for (int i = tid; i < nv * cols; i += nt) a.xn_out[(size_t)(i / cols) * a.ldxn + i % cols] = xs[i];
-        if (!q8 && a.act == ACT_F16) {
-            for (int i = tid; i < nv * cols; i += nt) xs[i] = round_f16(xs[i]);
-            __syncthreads();
-        }
     }
 
     if (!q8) {
         const uint8_t * wa = wsm;
         const uint8_t * wb = wsm + L.bA;
-        const int nchunk = cols / 8;
         for (int rl = warp; rl < nrow; rl += nw) {
             float acc[NV], accb[NV];
 #pragma unroll
             for (int v = 0; v < NV; ++v) acc[v] = accb[v] = 0.0f;
             const uint4 * ra = reinterpret_cast<const uint4 *>(wa + (size_t) rl * cols * 2);
             const uint4 * rb = reinterpret_cast<const uint4 *>(wb + (size_t) rl * cols * 2);
-            for (int c = lane; c < nchunk; c += 32) {
+            for (int c = lane; c < h8; c += 32) {
                 const uint4 w = ra[c];
                 const uint4 w2 = dual ? rb[c] : make_uint4(0, 0, 0, 0);
 #pragma unroll
                 for (int v = 0; v < NV; ++v) {
                     if (v >= nv) continue;
-                    const float4 x0 = reinterpret_cast<const float4 *>(xs + v * cols)[2 * c];
-                    const float4 x1 = reinterpret_cast<const float4 *>(xs + v * cols)[2 * c + 1];
+                    const float4 x0 = reinterpret_cast<const float4 *>(xs + v * cols)[c];
+                    const float4 x1 = reinterpret_cast<const float4 *>(xs + v * cols)[h8 + c];
                     const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                     acc[v] = dot8(w, xv, acc[v]);
                     if (dual) accb[v] = dot8(w2, xv, accb[v]);
@@ -233,7 +237,7 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
     const int nb = cols / 32;
     for (int blk = warp; blk < nv * nb; blk += nw) {
         const int v = blk / nb, b = blk % nb;
-        const float val = xs[v * cols + b * 32 + lane];
+        const float val = xs[v * cols + xpos(b * 32 + lane, cols)];
         const float amax = warp_max(fabsf(val));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
@@ -312,7 +316,7 @@ __global__ void __launch_bounds__(QTTS_WARPS * 32) k_gemv(GemvArgs a, size_t sli
     if (!gemv_slice<NV>(a, blockIdx.x, gridDim.x, smem_raw, smem_raw + slice_bytes, &mbar, 0u)) {
         // the copy did not complete within the wait limit: wait once more (bounded) so
         // no bulk copy is in flight when the block exits, and leave the output unwritten
-        mbar_wait(&mbar, 0u);
+        if (threadIdx.x == 0) mbar_wait(&mbar, 0u);
     }
 }
 
@@ -335,7 +339,18 @@ struct QkArgs {
     const int * done;
 };
 
-__device__ __forceinline__ void head_norm_rope(float x[4], const float * g, float eps, const float2 * rp, int lane) {
+// Per-lane parameters of a head's RMSNorm + NEOX RoPE: lane owns dims
+// 4*lane .. 4*lane+3; the rotation pairs dim d with d +- 64.
+__device__ __forceinline__ void head_params(const float * g, const float2 * rp, int lane, float gv[4], float2 cs[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int d = lane * 4 + k;
+        gv[k] = g ? g[d] : 1.0f;
+        cs[k] = rp[lane < 16 ? d : d - 64];
+    }
+}
+
+__device__ __forceinline__ void head_norm_rope_v(float x[4], const float gv[4], const float2 cs[4], float eps, int lane) {
     double ss = 0.0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) ss += (double) __fmul_rn(x[k], x[k]);
@@ -343,24 +358,22 @@ __device__ __forceinline__ void head_norm_rope(float x[4], const float * g, floa
     const float mean = (float)(ss / (double) QTTS_HD);
     const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, eps)));
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const float t = __fmul_rn(x[k], scale);
-        x[k] = g ? __fmul_rn(t, g[lane * 4 + k]) : t;
-    }
+    for (int k = 0; k < 4; ++k) x[k] = __fmul_rn(__fmul_rn(x[k], scale), gv[k]);
     float o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) o[k] = __shfl_xor_sync(0xffffffffu, x[k], 16);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int d = lane * 4 + k;
-        if (lane < 16) {  // first half: x0 = x[d], x1 = x[d + 64]
-            const float2 cs = rp[d];
-            x[k] = __fsub_rn(__fmul_rn(x[k], cs.x), __fmul_rn(o[k], cs.y));
-        } else {          // second half: x0 = x[d - 64], x1 = x[d]
-            const float2 cs = rp[d - 64];
-            x[k] = __fadd_rn(__fmul_rn(o[k], cs.y), __fmul_rn(x[k], cs.x));
-        }
+        if (lane < 16) x[k] = __fsub_rn(__fmul_rn(x[k], cs[k].x), __fmul_rn(o[k], cs[k].y));   // x0 = x[d], x1 = x[d + 64]
+        else x[k] = __fadd_rn(__fmul_rn(o[k], cs[k].y), __fmul_rn(x[k], cs[k].x));              // x0 = x[d - 64], x1 = x[d]
     }
+}
+
+__device__ __forceinline__ void head_norm_rope(float x[4], const float * g, float eps, const float2 * rp, int lane) {
+    float gv[4];
+    float2 cs[4];
+    head_params(g, rp, lane, gv, cs);
+    head_norm_rope_v(x, gv, cs, eps, lane);
 }
 
 __global__ void k_qk_rope_store(QkArgs a) {
@@ -645,19 +658,25 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
     }
     if (warp < G) {
         const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
-        const float * qh = a.qkv + (size_t) i * a.ldq + (size_t)(g * G + warp) * QTTS_HD + lane * 4;
-        float x[4] = {qh[0], qh[1], qh[2], qh[3]};
-        head_norm_rope(x, a.q_norm, a.eps, rp, lane);
+        const float4 q4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) i * a.ldq + (size_t)(g * G + warp) * QTTS_HD + lane * 4);
+        float gv[4];
+        float2 cs[4];
+        head_params(a.q_norm, rp, lane, gv, cs);               // all loads in flight together
+        float x[4] = {q4.x, q4.y, q4.z, q4.w};
+        head_norm_rope_v(x, gv, cs, a.eps, lane);
 #pragma unroll
         for (int k = 0; k < 4; ++k) qs[warp * QTTS_HD + lane * 4 + k] = a.f32_mode ? x[k] : round_f16(x[k]);
     } else if (warp < G + (a.f32_mode ? i + 1 : 1)) {
         const int j = a.f32_mode ? warp - G : i;           // row of this call whose k/v this warp prepares
         const float2 * rp = a.rope + (size_t)(n_past + j) * (QTTS_HD / 2);
-        const float * kp = a.qkv + (size_t) j * a.ldq + QD + g * QTTS_HD + lane * 4;
-        const float * vp = a.qkv + (size_t) j * a.ldq + QD + KD + g * QTTS_HD + lane * 4;
-        float x[4] = {kp[0], kp[1], kp[2], kp[3]};
-        const float v[4] = {vp[0], vp[1], vp[2], vp[3]};
-        head_norm_rope(x, a.k_norm, a.eps, rp, lane);
+        const float4 k4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) j * a.ldq + QD + g * QTTS_HD + lane * 4);
+        const float4 v4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) j * a.ldq + QD + KD + g * QTTS_HD + lane * 4);
+        float gv[4];
+        float2 cs[4];
+        head_params(a.k_norm, rp, lane, gv, cs);
+        float x[4] = {k4.x, k4.y, k4.z, k4.w};
+        const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+        head_norm_rope_v(x, gv, cs, a.eps, lane);
         const int r = a.f32_mode ? j : 0;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -1048,6 +1067,7 @@ struct InputArgs {
     float * out;                  // [rows][H]
     DevState * st;
     int n_cb;
+    const __half * step_tab;      // IN_CP_STEP: cp_embd[g - 1] (persistent path)
 };
 
 __global__ void k_frame_inputs(InputArgs a) {

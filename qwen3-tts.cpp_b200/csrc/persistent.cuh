@@ -99,20 +99,31 @@ __device__ __forceinline__ void prefetch_gemv_slice(const GemvArgs & g, int cta,
     prefetch_mat_slice(g.B, cta, ncta);
 }
 
-__device__ void frame_inputs_body(const InputArgs & a, const int frame) {
-    const DevState * st = a.st;
+// Inputs of the next pass, built by CTA 0 right after it sampled: codes[0..cb]
+// (shared memory) hold this frame's codes so far, tabs[1..n_cb-1] the
+// code-predictor embedding tables, n_trailing the trailing text rows.  Same
+// sums in the same order as k_frame_inputs.
+__device__ void frame_inputs_body(const InputArgs & a, const int frame, const int * codes,
+                                  const __half * const * tabs, const int n_trailing) {
     for (int h = threadIdx.x; h < a.H; h += blockDim.x) {
         if (a.mode == IN_CP_PREFILL) {
             a.out[h] = a.hidden[h];
-            a.out[a.H + h] = __half2float(a.codec_embd[(size_t) st->codes[0] * a.H + h]);
+            a.out[a.H + h] = __half2float(a.codec_embd[(size_t) codes[0] * a.H + h]);
         } else if (a.mode == IN_CP_STEP) {
-            a.out[h] = __half2float(a.cp_embd[a.g - 1][(size_t) st->codes[a.g] * a.H + h]);
+            a.out[h] = __half2float(a.step_tab[(size_t) codes[a.g] * a.H + h]);
         } else {
-            float s = __half2float(a.codec_embd[(size_t) st->codes[0] * a.H + h]);
-            for (int cb = 1; cb < a.n_cb; ++cb)
-                s = __fadd_rn(s, __half2float(a.cp_embd[cb - 1][(size_t) st->codes[cb] * a.H + h]));
-            const float * tr = frame < st->n_trailing ? a.trailing + (size_t) frame * a.H : a.pad;
-            a.out[h] = __fadd_rn(s, tr[h]);
+            float e[QTTS_MAX_CB];
+            e[0] = __half2float(a.codec_embd[(size_t) codes[0] * a.H + h]);
+#pragma unroll
+            for (int cb = 1; cb < QTTS_MAX_CB; ++cb)
+                e[cb] = cb < a.n_cb ? __half2float(tabs[cb][(size_t) codes[cb] * a.H + h]) : 0.0f;
+            const float * tr = frame < n_trailing ? a.trailing + (size_t) frame * a.H : a.pad;
+            const float t = tr[h];
+            float s = e[0];
+#pragma unroll
+            for (int cb = 1; cb < QTTS_MAX_CB; ++cb)
+                if (cb < a.n_cb) s = __fadd_rn(s, e[cb]);
+            a.out[h] = __fadd_rn(s, t);
         }
     }
 }
@@ -141,9 +152,13 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     return t;
 }
 
-__device__ __forceinline__ void pk_drain(uint64_t * mbar, const int * pending, unsigned * phase) {
+// Waits (bounded) for the copies still in flight into either weight buffer.
+// pending / phase hold one bit per buffer (no per-thread arrays: those would
+// live in local memory).
+__device__ __forceinline__ void pk_drain(uint64_t * mbar, unsigned pending, unsigned phase) {
+    if (threadIdx.x != 0) return;
     for (int b = 0; b < 2; ++b)
-        if (pending[b]) { mbar_wait(&mbar[b], phase[b] & 1u); phase[b]++; }
+        if (pending >> b & 1u) mbar_wait(mbar + b, phase >> b & 1u);
 }
 
 __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentArgs P) {
@@ -151,11 +166,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
     __shared__ POp desc[2];
     __shared__ __align__(8) uint64_t mbar[2];
     __shared__ int s_done;
+    __shared__ SampleParams s_sp;
+    __shared__ int s_codes[QTTS_MAX_CB];
+    __shared__ const __half * s_tabs[QTTS_MAX_CB];
     const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x;
-    uint8_t * wbuf[2] = {smem, smem + P.wbuf_bytes};
     uint8_t * work = smem + 2 * (size_t) P.wbuf_bytes;
-    unsigned phase[2] = {0u, 0u};
-    int pending[2] = {0, 0};
+    unsigned phase = 0u, pending = 0u;   // bit b: parity of buffer b's next completion / copy in flight
     unsigned epoch = 0;
     constexpr int NW = (int)(sizeof(POp) / 8);
 
@@ -174,16 +190,19 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
         for (int k = 0; k < P.n_pf0; ++k) prefetch_gemv_slice(P.ops[P.pf0[k]].g, cta, ncta);
         for (int b = 0; b < 2; ++b) {
             const POp & g = P.ops[P.first_gemv[b]];
-            issue_gemv_slice(g.g.A, g.g.B, g.g.norm_g, wbuf[g.slot], &mbar[g.slot], cta, ncta);
+            issue_gemv_slice(g.g.A, g.g.B, g.g.norm_g, smem + (size_t) g.slot * P.wbuf_bytes, mbar + g.slot, cta, ncta);
         }
     }
-    pending[0] = pending[1] = 1;
+    pending = 3u;
 
     // Every frame advances the position and the frame index by one (a frame
     // that samples EOS ends the launch), so both follow from their values at
     // launch; CTA 0 still writes them back to the frame state at frame end.
     const int pos0 = *(volatile const int *) &P.st->pos;
     const int frame0 = *(volatile const int *) &P.st->frame;
+    const int n_trailing = P.st->n_trailing;
+    if (tid == 0) s_sp = *P.sp;
+    __syncthreads();
 
     long long s = 0;   // position in the op stream
     for (int f = 0; f < P.n_frames; ++f) {
@@ -198,16 +217,18 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
             switch (op.type) {
                 case P_GEMV: {
                     const int b = op.slot;
+                    const uint8_t * wb = smem + (size_t) b * P.wbuf_bytes;
+                    const unsigned par = phase >> b & 1u;
                     unsigned long long * rs = P.trace ? P.trace + PK_TRACE_SLOTS * s + 2 : nullptr;
-                    const bool ok = op.nv == 1 ? gemv_slice<1>(op.g, cta, ncta, wbuf[b], work, &mbar[b], phase[b] & 1u, rs)
-                                               : gemv_slice<2>(op.g, cta, ncta, wbuf[b], work, &mbar[b], phase[b] & 1u, rs);
+                    const bool ok = op.nv == 1 ? gemv_slice<1>(op.g, cta, ncta, wb, work, mbar + b, par, rs)
+                                               : gemv_slice<2>(op.g, cta, ncta, wb, work, mbar + b, par, rs);
                     if (!ok) {                          // block-uniform: a copy did not land in time
                         if (tid == 0) atomicExch(P.err, 2);
                         pk_drain(mbar, pending, phase);
                         return;
                     }
-                    phase[b]++;
-                    pending[b] = 0;
+                    phase ^= 1u << b;
+                    pending &= ~(1u << b);
                     break;
                 }
                 case P_ATTN: {
@@ -220,18 +241,26 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
                 }
                 case P_SAMPLE:
                     if (cta == 0) {
-                        const SampleParams sp = *P.sp;
                         const int frame = frame0 + f;
-                        const int tok = sample_body<8>(op.logits, op.V, op.cb, P.st, sp, frame);
-                        if (tid == 0) sample_commit(tok, op.cb, P.st, sp, P.out_codes, P.out_cap, frame);
+                        // earlier codes and table pointers for the talker input, loaded while sampling
+                        int c_pre = 0;
+                        const __half * t_pre = nullptr;
+                        if (op.has_in && op.in.mode == IN_TALKER) {
+                            if (tid < op.cb) c_pre = P.st->codes[tid];
+                            if (tid >= 1 && tid < op.in.n_cb) t_pre = op.in.cp_embd[tid - 1];
+                        }
+                        const int tok = sample_body<8>(op.logits, op.V, op.cb, P.st, s_sp, frame);
+                        if (tid == 0) sample_commit(tok, op.cb, P.st, s_sp, P.out_codes, P.out_cap, frame);
                         if (op.has_in) {
-                            __syncthreads();           // the sampled code is in the frame state
-                            frame_inputs_body(op.in, frame);
+                            if (tid < op.cb) s_codes[tid] = c_pre;
+                            if (tid == 0) s_codes[op.cb] = tok;
+                            if (tid < QTTS_MAX_CB) s_tabs[tid] = t_pre;
+                            __syncthreads();
+                            frame_inputs_body(op.in, frame, s_codes, s_tabs, n_trailing);
                         }
                     }
                     break;
-                case P_INPUT:
-                    if (cta == 0) frame_inputs_body(op.in, frame0 + f);
+                case P_INPUT:   // inputs built right after a sampler: the program never emits it alone
                     break;
                 case P_FRAME_END:
                     if (cta == 0 && tid == 0 && !P.st->done) {
@@ -258,7 +287,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
             auto side = [&]() {
                 if (op.issue) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    issue_gemv_slice(op.iA, op.iB, op.iG, wbuf[op.issue_slot], &mbar[op.issue_slot], cta, ncta);
+                    issue_gemv_slice(op.iA, op.iB, op.iG, smem + (size_t) op.issue_slot * P.wbuf_bytes,
+                                     mbar + op.issue_slot, cta, ncta);
                 }
                 for (int k = 0; k < op.n_pf; ++k) {
                     prefetch_mat_slice(op.pfA[k], cta, ncta);
@@ -266,7 +296,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
                 }
                 if (P.trace && cta == 0) P.trace[PK_TRACE_SLOTS * s + 1] = globaltimer_ns();
             };
-            if (op.issue) pending[op.issue_slot] = 1;
+            if (op.issue) pending |= 1u << op.issue_slot;
             const int was_sample0 = op.type == P_SAMPLE && op.cb == 0;
             if (op.barrier) {
                 if (!grid_barrier(P.flags, ++epoch, P.err, side)) { pk_drain(mbar, pending, phase); return; }
