@@ -642,10 +642,10 @@ bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, in
             FusedAttn fa = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, M, pos_ptr,
                                            pos_static, f32_mode, ((int) il == dump_layer) ? dump : nullptr, ctx);
             fa.done = done;
-            const size_t fsm = fused_attn_smem(f32_mode ? M : ctx, G, M);
+            const size_t fsm = fused_attn_smem(f32_mode ? M : ctx, M);
             if (fsm > 200 * 1024) { err = "context too long for the fused attention kernel"; return false; }
             prof_begin(KC_ATTN, 0.0);
-            k_fused_attention<<<NKV * M, FA_THREADS, fsm, stream>>>(fa, st);
+            k_fused_attention<<<NH * M, FA_THREADS, fsm, stream>>>(fa, st);
             prof_end();
             ++launches;
         } else {
@@ -767,7 +767,7 @@ bool Engine::capture_graph() {
 bool Engine::build_program() {
     const qtts_config & c = cfg;
     const int H = c.hidden_size, V1 = c.code_pred_vocab_size, NG = c.n_codebooks - 1;
-    const int NH = c.n_attention_heads, NKV = c.n_key_value_heads, G = NH / NKV;
+    const int NKV = c.n_key_value_heads;
     prog.clear();
     prog_smem = 0;
     bool prog_bad = false;
@@ -792,7 +792,7 @@ bool Engine::build_program() {
             op.type = P_ATTN; op.barrier = 1;
             op.a = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, M, pos_ptr, pos_static,
                                    f32, ((int) il == dump_layer) ? dump : nullptr, ctx);
-            prog_smem = std::max(prog_smem, fused_attn_smem(f32 ? M : ctx, G, M));
+            prog_smem = std::max(prog_smem, fused_attn_smem(f32 ? M : ctx, M));
             prog.push_back(op);
             push_gemv(l.o, nullptr, att, QD(), M, nullptr, ACT_F16, X, H, X, H, EPI_RESID, nullptr, 0, 1);
             push_gemv(l.gate, &l.up, X, H, M, l.ffn_norm, ACT_F16, hbuf, ffn, nullptr, 0, EPI_SWIGLU, nullptr, 0, 1);

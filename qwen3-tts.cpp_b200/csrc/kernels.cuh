@@ -572,15 +572,17 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Fused q/k RMSNorm + RoPE + KV append + attention for one (kv head, query row)
-// unit of a frame step (M = 1, F16 cache) or of the code-predictor 2-token
-// prefill (M = 2, F32 K/V of this call; unit row i normalises k rows 0..i itself,
-// so no unit reads another unit's output).  Same arithmetic as
+// Fused q/k RMSNorm + RoPE + KV append + attention for one (query head, query
+// row) unit of a frame step (M = 1, F16 cache) or of the code-predictor 2-token
+// prefill (M = 2, F32 K/V of this call; unit row i normalises k rows 0..i
+// itself, so no unit reads another unit's output).  Same arithmetic as
 // k_qk_rope_store + k_attention (src/tts_transformer.cpp:1660-1712 for the
 // talker step, :2000-2011 / :2130-2160 for the code predictor), restructured
-// for latency: every global load of the unit (q/k/v rows, norm gains, RoPE
-// row, the first FA_KPASS cached keys and values) is issued before the first
-// block barrier, and the whole unit takes four barriers.
+// for latency: one query head per CTA (the dependent chains of a unit are
+// short), every global load of the unit (q/k/v rows, norm gains, RoPE row, the
+// first FA_KPASS cached keys and values) issued before the first block
+// barrier, four barriers in all.  The first query head of each kv group
+// appends the group's new K/V row to the cache.
 struct FusedAttn {
     float * qkv;              // raw q|k|v rows [M][ldq]
     int ldq;
@@ -602,72 +604,73 @@ struct FusedAttn {
 };
 
 constexpr int FA_THREADS = 512;
-constexpr int FA_KIT = 2;                              // key iterations per pass (16 warps x 4 keys each)
+constexpr int FA_KIT = 2;                                 // key iterations per pass (16 warps x 4 keys each)
 constexpr int FA_KPASS = FA_KIT * (FA_THREADS / 32) * 4;  // keys per pass: 128
-constexpr int FA_NPG = FA_THREADS / 64;                // PV position groups: 8
-constexpr int FA_VIT = FA_KPASS / FA_NPG;              // V rows per thread per pass: 16
+constexpr int FA_NPG = FA_THREADS / 64;                   // PV position groups: 8
+constexpr int FA_VIT = FA_KPASS / FA_NPG;                 // V rows per thread per pass: 16
 
-// Shared memory of one unit: q heads [G][128], new K/V rows [M][128] x 2,
-// scores [G][n_max] and PV partial sums [FA_NPG][G][128] (F32).
-__host__ __device__ inline size_t fused_attn_smem(int max_keys, int G, int M) {
+// Shared memory of one unit: q head [128], new K/V rows [M][128] x 2, scores
+// [n_max] and PV partial sums [FA_NPG][128] (F32).
+__host__ __device__ inline size_t fused_attn_smem(int max_keys, int M) {
     const size_t nk = (size_t)((max_keys + 3) & ~3);
-    return 4 * ((size_t) G * QTTS_HD + 2 * (size_t) M * QTTS_HD + G * nk + (size_t) FA_NPG * G * QTTS_HD) + 64;
+    return 4 * ((size_t) QTTS_HD + 2 * (size_t) M * QTTS_HD + nk + (size_t) FA_NPG * QTTS_HD) + 64;
 }
 
-__device__ __forceinline__ void fa_load_k(const FusedAttn & a, int j, int g, int sub, uint4 & k0, uint4 & k1) {
-    const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + ((size_t) j * a.n_kv_heads + g) * QTTS_HD + sub * 16);
-    k0 = kp[0];
-    k1 = kp[1];
-}
-
-// n_past: position of query row 0; frame: dump row (the persistent kernel
-// passes both from its own counters).
-__device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * smem, const DevState * st,
-                                const int n_past, const int frame) {
+// n_past: position of query row 0; frame: dump row.
+__device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * smem, const int n_past,
+                                const int frame) {
     const int NKV = a.n_kv_heads, G = a.n_heads / a.n_kv_heads;
-    const int g = unit % NKV, i = unit / NKV;
+    const int hq = unit % a.n_heads, i = unit / a.n_heads, g = hq / G;
+    const bool writer = hq % G == 0;                        // appends this group's K/V row
     const int pos = n_past + i;
-    const int n = a.f32_mode ? (i + 1) : (n_past + 1);   // keys attended
-    const int nc = a.f32_mode ? 0 : n_past;                // keys read from the cache
+    const int n = a.f32_mode ? (i + 1) : (n_past + 1);     // keys attended
+    const int nc = a.f32_mode ? 0 : n_past;                 // keys read from the cache
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
-    const int nk4 = (n + 3) & ~3;
-    float * qs = reinterpret_cast<float *>(smem);          // [G][128]
-    float * kn = qs + G * QTTS_HD;                         // [M][128] keys computed here
-    float * vn = kn + a.M * QTTS_HD;                       // [M][128]
-    float * sc = vn + a.M * QTTS_HD;                       // [G][nk4]
-    float * part = sc + G * nk4;                           // [FA_NPG][G][128]
-    const int jn0 = a.f32_mode ? 0 : n_past;               // first key held in kn/vn
+    float * qs = reinterpret_cast<float *>(smem);           // [128]
+    float * kn = qs + QTTS_HD;                              // [M][128] keys computed here
+    float * vn = kn + a.M * QTTS_HD;                        // [M][128]
+    float * sc = vn + a.M * QTTS_HD;                        // [n]
+    float * part = sc + ((n + 3) & ~3);                     // [FA_NPG][128]
+    const int jn0 = a.f32_mode ? 0 : n_past;                // first key held in kn/vn
+    const __half * kbase = a.kc + (size_t) g * QTTS_HD;
+    const __half * vbase = a.vc + (size_t) g * QTTS_HD;
+    const size_t pstride = (size_t) NKV * QTTS_HD;          // cache elements per position
 
     // 1. loads: cached keys/values of the first pass go to registers
     const int sub = lane & 7, slot = lane >> 3;
     const int pg = tid >> 6, d2 = tid & 63;
     uint4 kr[FA_KIT][2];
-    __half2 vr[FA_VIT];
 #pragma unroll
     for (int it = 0; it < FA_KIT; ++it) {
         const int j = it * (FA_THREADS / 8) + warp * 4 + slot;
-        if (j < nc) fa_load_k(a, j, g, sub, kr[it][0], kr[it][1]);
-        else kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
+        if (j < nc) {
+            const uint4 * kp = reinterpret_cast<const uint4 *>(kbase + (size_t) j * pstride + sub * 16);
+            kr[it][0] = kp[0];
+            kr[it][1] = kp[1];
+        } else {
+            kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
+        }
     }
+    __half2 vr[FA_VIT];
+    {
+        const __half2 * vp = reinterpret_cast<const __half2 *>(vbase + (size_t) pg * pstride) + d2;
+        const size_t vstep = (size_t) FA_NPG * pstride / 2;
 #pragma unroll
-    for (int t = 0; t < FA_VIT; ++t) {
-        const int j = pg + t * FA_NPG;
-        vr[t] = j < nc ? *reinterpret_cast<const __half2 *>(a.vc + ((size_t) j * NKV + g) * QTTS_HD + 2 * d2)
-                       : __float2half2_rn(0.0f);
+        for (int t = 0; t < FA_VIT; ++t) vr[t] = pg + t * FA_NPG < nc ? vp[t * vstep] : __float2half2_rn(0.0f);
     }
-    if (warp < G) {
+    if (warp == 0) {
         const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
-        const float4 q4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) i * a.ldq + (size_t)(g * G + warp) * QTTS_HD + lane * 4);
+        const float4 q4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) i * a.ldq + (size_t) hq * QTTS_HD + lane * 4);
         float gv[4];
         float2 cs[4];
-        head_params(a.q_norm, rp, lane, gv, cs);               // all loads in flight together
+        head_params(a.q_norm, rp, lane, gv, cs);            // all loads in flight together
         float x[4] = {q4.x, q4.y, q4.z, q4.w};
         head_norm_rope_v(x, gv, cs, a.eps, lane);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) qs[warp * QTTS_HD + lane * 4 + k] = a.f32_mode ? x[k] : round_f16(x[k]);
-    } else if (warp < G + (a.f32_mode ? i + 1 : 1)) {
-        const int j = a.f32_mode ? warp - G : i;           // row of this call whose k/v this warp prepares
+        for (int k = 0; k < 4; ++k) qs[lane * 4 + k] = a.f32_mode ? x[k] : round_f16(x[k]);
+    } else if (warp <= (a.f32_mode ? i + 1 : 1)) {
+        const int j = a.f32_mode ? warp - 1 : i;            // row of this call whose k/v this warp prepares
         const float2 * rp = a.rope + (size_t)(n_past + j) * (QTTS_HD / 2);
         const float4 k4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) j * a.ldq + QD + g * QTTS_HD + lane * 4);
         const float4 v4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) j * a.ldq + QD + KD + g * QTTS_HD + lane * 4);
@@ -683,24 +686,32 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
             const __half kh = __float2half_rn(x[k]), vh = __float2half_rn(v[k]);
             kn[r * QTTS_HD + lane * 4 + k] = a.f32_mode ? x[k] : __half2float(kh);
             vn[r * QTTS_HD + lane * 4 + k] = a.f32_mode ? v[k] : __half2float(vh);
-            if (j == i) {
-                a.kc[((size_t) pos * NKV + g) * QTTS_HD + lane * 4 + k] = kh;
-                a.vc[((size_t) pos * NKV + g) * QTTS_HD + lane * 4 + k] = vh;
+            if (j == i && writer) {
+                a.kc[(size_t) pos * pstride + g * QTTS_HD + lane * 4 + k] = kh;
+                a.vc[(size_t) pos * pstride + g * QTTS_HD + lane * 4 + k] = vh;
             }
         }
     }
-    __syncthreads();   // barrier 1: q heads and new k/v rows are in shared memory
+    __syncthreads();   // barrier 1: q head and new k/v rows are in shared memory
 
     // 2. scores; 8 lanes per key (16 dims each), 4 keys per warp per iteration
+    float q16[16];
+#pragma unroll
+    for (int d = 0; d < 16; ++d) q16[d] = qs[sub * 16 + d];
     for (int p0 = 0; p0 < n; p0 += FA_KPASS) {
 #pragma unroll
         for (int it = 0; it < FA_KIT; ++it) {
             const int j = p0 + it * (FA_THREADS / 8) + warp * 4 + slot;
             if (p0 > 0) {
-                if (j < nc) fa_load_k(a, j, g, sub, kr[it][0], kr[it][1]);
-                else kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
+                if (j < nc) {
+                    const uint4 * kp = reinterpret_cast<const uint4 *>(kbase + (size_t) j * pstride + sub * 16);
+                    kr[it][0] = kp[0];
+                    kr[it][1] = kp[1];
+                } else {
+                    kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
+                }
             }
-            float kv[16];
+            float s = 0.0f;
             if (j < nc) {
 #pragma unroll
                 for (int h8 = 0; h8 < 2; ++h8) {
@@ -708,94 +719,74 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const float2 f = __half22float2(hp[k]);
-                        kv[8 * h8 + 2 * k] = f.x;
-                        kv[8 * h8 + 2 * k + 1] = f.y;
+                        s = fmaf(f.x, q16[8 * h8 + 2 * k], s);
+                        s = fmaf(f.y, q16[8 * h8 + 2 * k + 1], s);
                     }
                 }
             } else if (j < n) {
 #pragma unroll
-                for (int d = 0; d < 16; ++d) kv[d] = kn[(j - jn0) * QTTS_HD + sub * 16 + d];
-            } else {
-#pragma unroll
-                for (int d = 0; d < 16; ++d) kv[d] = 0.0f;
+                for (int d = 0; d < 16; ++d) s = fmaf(kn[(j - jn0) * QTTS_HD + sub * 16 + d], q16[d], s);
             }
-#pragma unroll
-            for (int h = 0; h < ATT_MAX_GROUP; ++h) {
-                if (h >= G) break;                      // G is uniform: shuffles stay full-warp
-                const float * qh = qs + h * QTTS_HD + sub * 16;
-                float s = 0.0f;
-#pragma unroll
-                for (int d = 0; d < 16; ++d) s = fmaf(kv[d], qh[d], s);
-                s += __shfl_xor_sync(0xffffffffu, s, 4);
-                s += __shfl_xor_sync(0xffffffffu, s, 2);
-                s += __shfl_xor_sync(0xffffffffu, s, 1);
-                if (sub == 0 && j < n) sc[h * nk4 + j] = __fmul_rn(s, a.scale);
-            }
+            s += __shfl_xor_sync(0xffffffffu, s, 4);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            if (sub == 0 && j < n) sc[j] = __fmul_rn(s, a.scale);
         }
     }
     __syncthreads();   // barrier 2
 
-    // 3. softmax, one warp per head: max, expf, double sum, e * (float)(1/sum)
-    if (warp < G) {
-        float * row = sc + warp * nk4;
+    // 3. softmax (warp 0): max, expf, double sum, e * (float)(1/sum)
+    if (warp == 0) {
         float mx = -INFINITY;
-        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, row[j]);
+        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sc[j]);
         mx = warp_max(mx);
         double sum = 0.0;
         for (int j = lane; j < n; j += 32) {
-            const float e = expf(__fsub_rn(row[j], mx));
-            row[j] = e;
+            const float e = expf(__fsub_rn(sc[j], mx));
+            sc[j] = e;
             sum += (double) e;
         }
         sum = warp_sum_d(sum);
         const float inv = (float)(1.0 / sum);
-        float * drow = a.dump ? a.dump + ((size_t) frame * a.n_heads + g * G + warp) * a.dump_stride : nullptr;
+        float * drow = a.dump ? a.dump + ((size_t) frame * a.n_heads + hq) * a.dump_stride : nullptr;
         for (int j = lane; j < n; j += 32) {
-            const float pj = __fmul_rn(row[j], inv);
+            const float pj = __fmul_rn(sc[j], inv);
             if (drow) drow[j] = pj;
-            row[j] = a.f32_mode ? pj : round_f16(pj);
+            sc[j] = a.f32_mode ? pj : round_f16(pj);
         }
     }
     __syncthreads();   // barrier 3
 
-    // 4. P x V: position group pg takes keys pg, pg + 8, ...; thread d2 two dims of all G heads
-    float acc[ATT_MAX_GROUP][2];
-#pragma unroll
-    for (int h = 0; h < ATT_MAX_GROUP; ++h) acc[h][0] = acc[h][1] = 0.0f;
+    // 4. P x V: position group pg takes keys pg, pg + 8, ...; thread d2 two dims
+    float acc0 = 0.0f, acc1 = 0.0f;
     for (int p0 = 0; p0 < n; p0 += FA_KPASS) {
+        const __half2 * vp = reinterpret_cast<const __half2 *>(vbase + (size_t)(p0 + pg) * pstride) + d2;
+        const size_t vstep = (size_t) FA_NPG * pstride / 2;
 #pragma unroll
         for (int t = 0; t < FA_VIT; ++t) {
             const int j = p0 + pg + t * FA_NPG;
             float2 v;
             if (j < nc) {
-                if (p0 > 0) vr[t] = *reinterpret_cast<const __half2 *>(a.vc + ((size_t) j * NKV + g) * QTTS_HD + 2 * d2);
+                if (p0 > 0) vr[t] = vp[t * vstep];
                 v = __half22float2(vr[t]);
             } else if (j < n) {
                 v = make_float2(vn[(j - jn0) * QTTS_HD + 2 * d2], vn[(j - jn0) * QTTS_HD + 2 * d2 + 1]);
             } else {
                 break;
             }
-#pragma unroll
-            for (int h = 0; h < ATT_MAX_GROUP; ++h)
-                if (h < G) {
-                    const float pj = sc[h * nk4 + j];
-                    acc[h][0] = fmaf(pj, v.x, acc[h][0]);
-                    acc[h][1] = fmaf(pj, v.y, acc[h][1]);
-                }
+            const float pj = sc[j];
+            acc0 = fmaf(pj, v.x, acc0);
+            acc1 = fmaf(pj, v.y, acc1);
         }
     }
-#pragma unroll
-    for (int h = 0; h < ATT_MAX_GROUP; ++h)
-        if (h < G) {
-            part[(pg * G + h) * QTTS_HD + 2 * d2] = acc[h][0];
-            part[(pg * G + h) * QTTS_HD + 2 * d2 + 1] = acc[h][1];
-        }
+    part[pg * QTTS_HD + 2 * d2] = acc0;
+    part[pg * QTTS_HD + 2 * d2 + 1] = acc1;
     __syncthreads();   // barrier 4
-    for (int t = tid; t < G * QTTS_HD; t += blockDim.x) {
+    if (tid < QTTS_HD) {
         float s = 0.0f;
 #pragma unroll
-        for (int q = 0; q < FA_NPG; ++q) s = __fadd_rn(s, part[q * G * QTTS_HD + t]);
-        a.out[(size_t) i * a.ldo + (size_t)(g * G) * QTTS_HD + t] = s;
+        for (int q = 0; q < FA_NPG; ++q) s = __fadd_rn(s, part[q * QTTS_HD + tid]);
+        a.out[(size_t) i * a.ldo + (size_t) hq * QTTS_HD + tid] = s;
     }
 }
 
@@ -803,7 +794,7 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
 __global__ void __launch_bounds__(FA_THREADS) k_fused_attention(FusedAttn a, const DevState * st) {
     if (a.done && *a.done) return;
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    fused_attn_body(a, blockIdx.x, smem_raw, st, a.pos_ptr ? *a.pos_ptr : a.pos_static, st->frame);
+    fused_attn_body(a, blockIdx.x, smem_raw, a.pos_ptr ? *a.pos_ptr : a.pos_static, st->frame);
 }
 
 struct SampleParams {

@@ -233,9 +233,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
                 }
                 case P_ATTN: {
                     const int np = op.a.pos_ptr ? pos0 + f : op.a.pos_static;
-                    for (int u = cta; u < op.a.n_kv_heads * op.a.M; u += ncta) {
-                        fused_attn_body(op.a, u, work, P.st, np, frame0 + f);
-                        if (u + ncta < op.a.n_kv_heads * op.a.M) __syncthreads();
+                    for (int u = cta; u < op.a.n_heads * op.a.M; u += ncta) {
+                        fused_attn_body(op.a, u, work, np, frame0 + f);
+                        if (u + ncta < op.a.n_heads * op.a.M) __syncthreads();
                     }
                     break;
                 }
