@@ -3,12 +3,15 @@
 
 Workload (default): BASELINE.json configs[0] — greedy F16 frame loop, batch 1,
 seeded random-init GGUF with the 0.6B layout, ICL prompt with 55 reference
-frames (64 talker prefill positions), repetition penalty 1.05, EOS suppressed
-by eos_bias = -1e9.  `--config q8` runs configs[1] (Q8_0, 128 prefill).
+frames (64 talker prefill positions), 32 frames per utterance, repetition
+penalty 1.05, EOS suppressed by eos_bias = -1e9.  `--config q8` runs
+configs[1] (Q8_0, 128 prefill, 256 frames).
 
 A step = one codec frame: codebook-0 sampling, the 2-token code-predictor
 prefill, 14 code-predictor steps with on-device sampling, the next-step
-embedding sum and one 28-layer talker step.  Each rank runs its own utterance
+embedding sum and one 28-layer talker step.  The K timed steps are K / F
+replays of the config's F-frame utterance (each replay rewinds the device
+frame state to frame 0 after the prefill).  Each rank runs its own utterance
 on its own GPU (weak scaling, no collective on the data path); the timed
 region is bracketed by a barrier + synchronize and the device time is the max
 over ranks.  Every frame streams 3.3 GB of weights (> 126 MB L2), so no L2
@@ -38,10 +41,10 @@ WEIGHT_BYTES = {"f16": 3_309_305_856, "q8": 1_790_509_056}
 KV_TALKER_PER_POS = 114_688      # 28 layers x (K+V) x 8 heads x 128 x 2 B
 KV_CP_PER_POS = 20_480           # 5 layers x (K+V) x 8 x 128 x 2 B
 CONFIGS = {
-    "f16": dict(wtype="f16", n_ref=55, prefill=64,
-                workload="BASELINE configs[0]: greedy F16 frame loop, batch 1, ICL prefill 64, rep 1.05"),
-    "q8": dict(wtype="q8_0", n_ref=119, prefill=128,
-               workload="BASELINE configs[1]: greedy Q8_0 frame loop, batch 1, ICL prefill 128, rep 1.05"),
+    "f16": dict(wtype="f16", n_ref=55, prefill=64, frames=32,
+                workload="BASELINE configs[0]: greedy F16 frame loop, batch 1, ICL prefill 64, 32 frames, rep 1.05"),
+    "q8": dict(wtype="q8_0", n_ref=119, prefill=128, frames=256,
+               workload="BASELINE configs[1]: greedy Q8_0 frame loop, batch 1, ICL prefill 128, 256 frames, rep 1.05"),
 }
 
 
@@ -75,12 +78,16 @@ def _model(cfg, rank: int, local_rank: int, barrier):
 
 
 class ClockSampler:
-    """Polls SM clock and throttle reasons through NVML while the timed region runs."""
+    """Polls SM clock and throttle reasons through NVML from a background thread.
+
+    Started before the warm-up (NVML's first calls are slow); mark() brackets the
+    timed region and summary() keeps the samples taken inside it."""
 
     REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
     def __init__(self, index: int):
-        self.samples, self.reasons, self.ok = [], set(), False
+        self.samples, self.ok = [], False   # (t, mhz, reasons bitmask)
+        self.t0 = self.t1 = None
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -95,14 +102,12 @@ class ClockSampler:
     def _run(self):
         while not self._stop.is_set():
             try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
                 r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if r & bit:
-                        self.reasons.add(name)
+                self.samples.append((time.perf_counter(), mhz, r))
             except Exception:
                 pass
-            time.sleep(0.002)
+            time.sleep(0.001)
 
     def __enter__(self):
         if self.ok:
@@ -115,9 +120,18 @@ class ClockSampler:
         if self.ok:
             self.t.join()
 
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+
     def summary(self):
-        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
-                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        inside = [(m, r) for t, m, r in self.samples
+                  if self.t0 is not None and self.t1 is not None and self.t0 <= t <= self.t1]
+        reasons = sorted({name for _, r in inside for bit, name in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median([m for m, _ in inside]) if inside else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside)}
 
 
 def _peaks():
@@ -195,7 +209,7 @@ def run_reference(args, cfg):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="f16")
@@ -228,17 +242,30 @@ def main():
     gen = dict(speaker=spk, ref_text=ref, ref_codes=codes, rep_penalty=1.05, temperature=0.0, top_k=0, eos_bias=-1e9)
     K, W = args.steps, args.warmup
 
-    # ---- device-resident timing: inputs in HBM, K graph-replayed frames
-    plen = eng.generate_begin(tgt, W + K, **gen)
-    assert plen == cfg["prefill"], plen
-    eng.run_frames(W)
-    t0 = eng.timing()["frames_ms"]
-    barrier()
-    torch.cuda.synchronize()
+    # ---- device-resident timing: inputs in HBM.  The utterance of the config
+    # (F frames after the prefill) is replayed K / F times: each replay rewinds
+    # the device frame state to frame 0 (no new prefill) and runs F frames in
+    # one persistent launch (or F graph launches).
+    F = cfg["frames"]
+    reps = max(1, (K + F - 1) // F)
+    K = reps * F
     with ClockSampler(local) as clk:
-        got = eng.run_frames(K)
-    barrier()
-    torch.cuda.synchronize()
+        plen = eng.generate_begin(tgt, F, **gen)
+        assert plen == cfg["prefill"], plen
+        eng.run_frames(W)
+        eng.generate_rewind()
+        eng.run_frames(F)
+        t0 = eng.timing()["frames_ms"]
+        barrier()
+        torch.cuda.synchronize()
+        clk.mark_start()
+        got = 0
+        for _ in range(reps):
+            eng.generate_rewind()
+            got += eng.run_frames(F)
+        barrier()
+        torch.cuda.synchronize()
+        clk.mark_end()
     ms = eng.timing()["frames_ms"] - t0
     assert got == K, got
     ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
@@ -252,14 +279,17 @@ def main():
     eng.run_frames(W)
     prof = eng.profile_frames(args.profile_frames)
 
-    # ---- end to end through the C ABI with host buffers (prompt in, codes out)
+    # ---- end to end through the C ABI with host buffers: each step of an
+    # utterance includes its share of the prompt upload, the prefill, the frames
+    # and the codes download (qtts_generate with host arrays), reps utterances.
     eng.generate(tgt, 2, **gen)            # untimed warm call
     barrier()
     torch.cuda.synchronize()
     t_e0 = time.perf_counter()
-    out = eng.generate(tgt, K, **gen)
+    for _ in range(reps):
+        out = eng.generate(tgt, F, **gen)
+        assert out["n_frames"] == F
     t_e = time.perf_counter() - t_e0
-    assert out["n_frames"] == K
     et = torch.tensor([t_e], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(et, op=dist.ReduceOp.MAX)
@@ -267,8 +297,8 @@ def main():
     H = eng.cfg["hidden_size"]
     n_text_rows = 3 + 3 + (len(ref) - 8) + (len(tgt) - 8) + 1
     n_lookup_rows = 3 + 2 + 1 + 16 * cfg["n_ref"]
-    h2d = (4 * (len(tgt) + len(ref) + codes.size) + 4 * H * (plen + 1) + 4 * n_text_rows + 4 * n_lookup_rows)
-    d2h = 4 * H * (n_text_rows + n_lookup_rows) + 4 * 16 * K + 4 * H + 1024 * ((K + 15) // 16)
+    h2d_utt = (4 * (len(tgt) + len(ref) + codes.size) + 4 * H * (plen + 1) + 4 * n_text_rows + 4 * n_lookup_rows)
+    d2h_utt = 4 * H * (n_text_rows + n_lookup_rows) + 4 * 16 * F + 4 * H + 1024 * ((F + 15) // 16)
 
     if world > 1:
         dist.destroy_process_group()
@@ -279,18 +309,18 @@ def main():
     g = prof["gemv"]
     gemv_gbs = (g["bytes"] / g["launches"]) / (g["ms"] / g["launches"] / 1e3) / 1e9 if g["launches"] else None
     frame_ms = ms_max / K
-    kv_pos_mean = plen + W + K / 2.0
+    kv_pos_mean = plen + F / 2.0
     frame_bytes = WEIGHT_BYTES[args.config] + KV_TALKER_PER_POS * kv_pos_mean + KV_CP_PER_POS * 135
     prof_total = sum(prof[c]["ms"] for c in ("gemv", "attention", "sample", "other"))
     persistent = launches_per_frame == 1
     if persistent:
-        # one cooperative launch runs all K frames: bytes per launch = K frames of weights + KV
-        kernel = "k_frame_persistent (one cooperative launch per run of K frames)"
-        bytes_per_launch = frame_bytes * K
-        achieved = bytes_per_launch / (ms_max / 1e3) / 1e9
+        # one cooperative launch runs the F frames of a replay: bytes per launch = F frames of weights + KV
+        kernel = f"k_frame_persistent (one cooperative launch per utterance replay of {F} frames)"
+        bytes_per_launch = frame_bytes * F
+        achieved = bytes_per_launch / (ms_max / reps / 1e3) / 1e9
         tpf = _profile_figure(f"k_frame_persistent_{args.config}.md", "dram_bytes_per_frame")
-        traffic = tpf * K if tpf else None
-        launches_per_frame_k = 1.0 / K
+        traffic = tpf * F if tpf else None
+        launches_per_frame_k = 1.0 / F
     else:
         kernel = "k_gemv (all GEMV launches of a frame, eager replay)"
         bytes_per_launch = g["bytes"] / max(g["launches"], 1)
@@ -302,7 +332,8 @@ def main():
         "warmup": W, "ms_per_step": frame_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16" if args.config == "f16" else "q8_0",
         "data": "synthetic (seeded random-init GGUF with the 0.6B layout; random prompt ids and reference codes)",
-        "config": {"workload": cfg["workload"], "batch_per_gpu": 1, "prefill": plen, "frames_timed": K,
+        "config": {"workload": cfg["workload"], "batch_per_gpu": 1, "prefill": plen, "frames_per_utterance": F,
+                   "utterance_replays": reps, "frames_timed": K,
                    "parallelism": f"independent utterance per GPU x{world}",
                    "l2": "inputs larger than L2 (3.3 GB of weights streamed per frame), no flush"},
         "roofline": {"bound": "hbm", "kernel": kernel,
@@ -318,9 +349,10 @@ def main():
         "kernel_classes": {c: {"launches_per_frame": prof[c]["launches"] / max(prof["frames"], 1),
                                "ms_per_frame": prof[c]["ms"] / max(prof["frames"], 1)}
                            for c in ("gemv", "attention", "sample", "other")},
-        "e2e": {"value": world * K / t_e, "unit": UNIT, "h2d_bytes_per_step": h2d / K, "d2h_bytes_per_step": d2h / K,
-                "includes": "qtts_generate: prompt upload, prefill, K frames, codes download"},
-        "gpu_launches": 1 if persistent else launches_per_frame * K,
+        "e2e": {"value": world * K / t_e, "unit": UNIT, "h2d_bytes_per_step": h2d_utt / F,
+                "d2h_bytes_per_step": d2h_utt / F,
+                "includes": f"{reps} x qtts_generate of {F} frames: prompt upload, prefill, frames, codes download"},
+        "gpu_launches": reps if persistent else launches_per_frame * K,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:

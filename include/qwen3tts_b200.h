@@ -139,6 +139,12 @@ int32_t qtts_generate(qtts_engine * e, const qtts_generate_params * p, qtts_fram
  * Returns the number of frames produced, -1 on error. */
 int32_t qtts_generate_begin(qtts_engine * e, const qtts_generate_params * p);
 int32_t qtts_run_frames(qtts_engine * e, int32_t n, int32_t * codes_out);
+/* Rewinds the active generation to frame 0 (the state right after begin's
+ * prefill) so an utterance can be replayed without running its prefill again;
+ * KV positions past the prefill are rewritten as frames are regenerated.
+ * Returns 0, or -1 with no active generation.  No counterpart in the
+ * reference (benchmark and streaming-restart helper). */
+int32_t qtts_generate_rewind(qtts_engine * e);
 
 /* Sampling seed of the Philox stream (sampled decoding is reproducible). */
 void qtts_set_seed(qtts_engine * e, uint64_t seed);

@@ -54,6 +54,7 @@ struct GenSession {
     bool active = false;
     int max_len = 0, prefill_len = 0, trailing_len = 0, produced = 0;
     bool done = false;
+    DevState st0{};   // frame state right after the prefill (rewind target)
 };
 
 struct Engine {
@@ -214,6 +215,7 @@ struct Engine {
                            std::vector<float> & padv);
     int begin(const qtts_generate_params * p);
     int run_frames(int n, int32_t * codes_out);
+    int rewind();
 };
 
 static thread_local std::string g_create_error;
@@ -1232,6 +1234,7 @@ int Engine::begin(const qtts_generate_params * p) {
         err = "upload state"; return -1;
     }
     if (!sync("generate setup")) return -1;
+    sess.st0 = hs;
     if (use_persistent) {
         if (!prog_ok && !build_program()) return -1;
         if (!graph_ok) { launches = 0; graph_ok = false; }
@@ -1245,6 +1248,20 @@ int Engine::begin(const qtts_generate_params * p) {
     timing.frames = 0;
     timing.kernel_launches = launches_per_frame;
     return plen;
+}
+
+// Back to frame 0 of the active generation: the frame state after the
+// prefill is restored; KV positions past the prefill are rewritten as frames
+// are generated again.
+int Engine::rewind() {
+    if (!sess.active) { err = "no active generation"; return -1; }
+    if (cudaMemcpyAsync(st, &sess.st0, sizeof(DevState), cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+        err = "rewind state"; return -1;
+    }
+    sess.produced = 0;
+    sess.done = false;
+    n_used = sess.st0.pos;
+    return 0;
 }
 
 int Engine::run_frames(int n, int32_t * codes_out) {
@@ -1678,6 +1695,12 @@ int32_t qtts_run_frames(qtts_engine * h, int32_t n, int32_t * codes_out) {
     if (!h) return -1;
     ENG(h);
     return E.run_frames(n, codes_out);
+}
+
+int32_t qtts_generate_rewind(qtts_engine * h) {
+    if (!h) return -1;
+    ENG(h);
+    return E.rewind();
 }
 
 int32_t qtts_generate(qtts_engine * h, const qtts_generate_params * p, qtts_frame_callback on_frame, void * user,

@@ -100,6 +100,7 @@ def lib():
         "qtts_generate": (C.c_int32, [C.c_void_p, C.POINTER(GenParams), FRAME_CB, C.c_void_p, _i32p, _i32p]),
         "qtts_generate_begin": (C.c_int32, [C.c_void_p, C.POINTER(GenParams)]),
         "qtts_run_frames": (C.c_int32, [C.c_void_p, C.c_int32, _i32p]),
+        "qtts_generate_rewind": (C.c_int32, [C.c_void_p]),
         "qtts_set_seed": (None, [C.c_void_p, C.c_uint64]),
         "qtts_set_debug_logits": (C.c_int32, [C.c_void_p, _f32p, _f32p, C.c_int32]),
         "qtts_set_attn_dump": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32]),
@@ -320,6 +321,11 @@ class Engine:
         if rc < 0:
             raise RuntimeError("run_frames failed: " + self.error())
         return rc
+
+    def generate_rewind(self) -> None:
+        """Back to frame 0 of the active generation (replay without a new prefill)."""
+        if lib().qtts_generate_rewind(self.h) < 0:
+            raise RuntimeError("rewind failed: " + self.error())
 
 
 def op_gemv(w, wtype: int, rows: int, cols: int, x, norm_gain=None, eps=1e-6, act_f32=False, want_block_dots=False,

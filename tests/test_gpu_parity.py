@@ -249,3 +249,24 @@ def test_persistent_kernel_matches_graph_path(qtts, tiny_f16, tiny_q8, monkeypat
         assert np.array_equal(a["codes"], b["codes"])
         assert np.array_equal(a["talker_logits"][:20], b["talker_logits"][:20])
         assert np.array_equal(a["cp_logits"], b["cp_logits"])
+
+
+@pytest.mark.gpu
+def test_rewind_replays_the_utterance(qtts, tiny_f16, monkeypatch):
+    """qtts_generate_rewind restores the post-prefill frame state: a replay of the
+    same utterance (greedy, repetition penalty on) yields the same codes, in both
+    frame modes."""
+    rng = np.random.default_rng(31)
+    text = text_ids(rng, 20)
+    for mode in ("persistent", "graph"):
+        monkeypatch.setenv("QTTS_FRAME_MODE", mode)
+        eng = qtts.Engine(tiny_f16, 0)
+        eng.generate_begin(text, 12, speaker=np.zeros(256, np.float32), eos_bias=-1e9, rep_penalty=1.05)
+        a = np.zeros((12, 16), np.int32)
+        assert eng.run_frames(12, a) == 12
+        for _ in range(2):
+            eng.generate_rewind()
+            b = np.zeros((12, 16), np.int32)
+            assert eng.run_frames(12, b) == 12
+            assert np.array_equal(a, b)
+        eng.close()
