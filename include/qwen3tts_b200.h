@@ -171,6 +171,18 @@ int32_t qtts_profile_frames(qtts_engine * e, int32_t n, qtts_kernel_stats * stat
 int32_t qtts_program_ops(const qtts_engine * e, int32_t * types, int32_t cap);
 int32_t qtts_op_trace(const qtts_engine * e, unsigned long long * out, int32_t cap);
 
+/* One tcgen05 tensor-core GEMM as the batched and prefill paths run it
+ * (test entry; no reference counterpart): y[m][r] = sum_k W[r][k] * a[m][k],
+ * W F16 row-major [rows x cols] (host), activations a = x[m x cols] after an
+ * optional RMSNorm with norm_gain, rounded to F16 (act 0) or split into F16
+ * hi + lo parts (act 1, the F32-activation ffn_down semantics).  epi 0 stores,
+ * 1 adds resid[m x rows], 2 is SwiGLU: y = silu(W a) * (w_up a) with w_up the up
+ * matrix.  rows (x2 for SwiGLU) % 128 == 0, cols % 64 == 0, m <= 256 (128 with
+ * act 1).  Returns 1 on success. */
+int32_t qtts_op_gemm_tc(int32_t device, const uint16_t * w, const uint16_t * w_up, int32_t rows, int32_t cols,
+                        const float * x, int32_t m, const float * norm_gain, float eps, int32_t act, int32_t epi,
+                        const float * resid, float * y);
+
 /* ---- Kernel-level entry points (one engine kernel on host data) ----------
  * ggml_mul_mat (+ optional ggml_rms_norm prologue) as the engine computes it,
  * src/tts_transformer.cpp:1656-1661: y[nv][rows] = W[rows][cols] . x[nv][cols].

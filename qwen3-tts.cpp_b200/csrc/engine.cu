@@ -19,6 +19,7 @@
 #include "../../include/qwen3tts_b200.h"
 #include "gguf.hpp"
 #include "persistent.cuh"
+#include "gemm_tc.cuh"
 
 #include <algorithm>
 #include <chrono>
@@ -84,6 +85,7 @@ struct Engine {
     // activations (rows <= QTTS_MAX_NV)
     float * x = nullptr, * xcp = nullptr, * qkv = nullptr, * att = nullptr, * hbuf = nullptr;
     float * logits = nullptr, * cp_logits = nullptr, * hidden = nullptr, * hid_rows = nullptr;
+    float * logits0 = nullptr, * hidden0 = nullptr;   // prefill outputs kept for rewind
     float * tmp_a = nullptr, * tmp_b = nullptr;
     int * d_ids = nullptr;
     int ids_cap = 0;
@@ -164,10 +166,11 @@ struct Engine {
         if (graph) { cudaGraphExecDestroy(graph); graph = nullptr; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
                          cp_logits, hidden, hid_rows, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
-                         dbg_t, dbg_cp, d_attn, d_prog, d_flags, d_err, d_trace};
+                         dbg_t, dbg_cp, d_attn, d_prog, d_flags, d_err, d_trace, logits0, hidden0};
         for (void * p : ptrs) if (p) cudaFree(p);
         wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
         x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = hid_rows = tmp_a = tmp_b = nullptr;
+        logits0 = hidden0 = nullptr;
         d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
         dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_prog = nullptr; d_flags = nullptr; d_err = nullptr;
         d_trace = nullptr;
@@ -478,6 +481,8 @@ bool Engine::alloc_activations() {
     QCHECK(cudaMalloc(&logits, sizeof(float) * c.codec_vocab_size));
     QCHECK(cudaMalloc(&cp_logits, sizeof(float) * c.code_pred_vocab_size * (c.n_codebooks - 1)));
     QCHECK(cudaMalloc(&hidden, sizeof(float) * H));
+    QCHECK(cudaMalloc(&logits0, sizeof(float) * c.codec_vocab_size));
+    QCHECK(cudaMalloc(&hidden0, sizeof(float) * H));
     QCHECK(cudaMalloc(&hid_rows, sizeof(float) * NV * H));
     QCHECK(cudaMalloc(&tmp_a, sizeof(float) * NV * std::max(H, c.text_embd_dim)));
     QCHECK(cudaMalloc(&tmp_b, sizeof(float) * NV * std::max(H, c.text_embd_dim)));
@@ -1233,6 +1238,10 @@ int Engine::begin(const qtts_generate_params * p) {
         cudaMemcpyAsync(sp, &P, sizeof(P), cudaMemcpyHostToDevice, stream) != cudaSuccess) {
         err = "upload state"; return -1;
     }
+    if (cudaMemcpyAsync(logits0, logits, sizeof(float) * c.codec_vocab_size, cudaMemcpyDeviceToDevice, stream) != cudaSuccess ||
+        cudaMemcpyAsync(hidden0, hidden, sizeof(float) * H, cudaMemcpyDeviceToDevice, stream) != cudaSuccess) {
+        err = "snapshot prefill outputs"; return -1;
+    }
     if (!sync("generate setup")) return -1;
     sess.st0 = hs;
     if (use_persistent) {
@@ -1250,12 +1259,14 @@ int Engine::begin(const qtts_generate_params * p) {
     return plen;
 }
 
-// Back to frame 0 of the active generation: the frame state after the
-// prefill is restored; KV positions past the prefill are rewritten as frames
-// are generated again.
+// Back to frame 0 of the active generation: the frame state and the
+// prefill's logits and hidden row are restored; KV positions past the prefill
+// are rewritten as frames are generated again.
 int Engine::rewind() {
     if (!sess.active) { err = "no active generation"; return -1; }
-    if (cudaMemcpyAsync(st, &sess.st0, sizeof(DevState), cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+    if (cudaMemcpyAsync(st, &sess.st0, sizeof(DevState), cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        cudaMemcpyAsync(logits, logits0, sizeof(float) * cfg.codec_vocab_size, cudaMemcpyDeviceToDevice, stream) != cudaSuccess ||
+        cudaMemcpyAsync(hidden, hidden0, sizeof(float) * cfg.hidden_size, cudaMemcpyDeviceToDevice, stream) != cudaSuccess) {
         err = "rewind state"; return -1;
     }
     sess.produced = 0;
@@ -1334,6 +1345,65 @@ extern "C" {
 // ---------------------------------------------------------------- kernel-level entry points
 // These run one engine kernel on caller-provided host data (device buffers are
 // allocated per call); the parity tests use them to check a kernel in isolation.
+int32_t qtts_op_gemm_tc(int32_t device, const uint16_t * w, const uint16_t * w_up, int32_t rows, int32_t cols,
+                        const float * xin, int32_t m, const float * norm_gain, float eps, int32_t act, int32_t epi,
+                        const float * resid, float * y) {
+    using namespace qtts;
+    const bool swiglu = epi == TC_EPI_SWIGLU;
+    const int rows_w = swiglu ? 2 * rows : rows;
+    const int mp = (m + 15) / 16 * 16;
+    const int np = act == TC_ACT_SPLIT ? 2 * mp : mp;
+    if (!w || !xin || !y || m <= 0 || rows <= 0 || rows_w % TC_BM || cols % TC_BK || np > TC_MAX_N ||
+        (swiglu && !w_up) || (epi == TC_EPI_RESID && !resid) || epi < 0 || epi > 2 || act < 0 || act > 1)
+        return 0;
+    if (cudaSetDevice(device) != cudaSuccess) return 0;
+    void * dw = nullptr, * dw2 = nullptr, * dwt = nullptr, * dx = nullptr, * dxt = nullptr, * dy = nullptr,
+         * dg = nullptr, * derr = nullptr;
+    bool ok = true;
+    auto chk = [&](cudaError_t e) { if (e != cudaSuccess) ok = false; };
+    const size_t wb = (size_t) rows * cols * 2;
+    const int ycols = rows;
+    chk(cudaMalloc(&dw, wb));
+    if (swiglu) chk(cudaMalloc(&dw2, wb));
+    chk(cudaMalloc(&dwt, (size_t) rows_w * cols * 2));
+    chk(cudaMalloc(&dx, sizeof(float) * m * cols));
+    chk(cudaMalloc(&dxt, (size_t) np * cols * 2));
+    chk(cudaMalloc(&dy, sizeof(float) * m * ycols));
+    chk(cudaMalloc(&derr, sizeof(int)));
+    if (norm_gain) chk(cudaMalloc(&dg, sizeof(float) * cols));
+    if (ok) {
+        chk(cudaMemcpy(dw, w, wb, cudaMemcpyHostToDevice));
+        if (swiglu) chk(cudaMemcpy(dw2, w_up, wb, cudaMemcpyHostToDevice));
+        chk(cudaMemcpy(dx, xin, sizeof(float) * m * cols, cudaMemcpyHostToDevice));
+        if (resid) chk(cudaMemcpy(dy, resid, sizeof(float) * m * ycols, cudaMemcpyHostToDevice));
+        if (norm_gain) chk(cudaMemcpy(dg, norm_gain, sizeof(float) * cols, cudaMemcpyHostToDevice));
+        chk(cudaMemset(derr, 0, sizeof(int)));
+    }
+    if (ok) {
+        k_tile_weights<<<rows_w, 128>>>((const __half *) dw, (const __half *) dw2, rows_w, cols, (uint8_t *) dwt);
+        PackArgs pa{};
+        pa.x = (const float *) dx; pa.ldx = cols; pa.m_real = m; pa.np = np; pa.cols = cols;
+        pa.gain = (const float *) dg; pa.eps = eps; pa.act = act; pa.out = (uint8_t *) dxt;
+        k_pack_act<<<act == TC_ACT_SPLIT ? np / 2 : np, 256>>>(pa);
+        GemmTcArgs g{};
+        g.w = (const uint8_t *) dwt; g.x = (const uint8_t *) dxt; g.rows_w = rows_w; g.cols = cols; g.np = np;
+        g.m_real = m; g.split = act == TC_ACT_SPLIT; g.epi = epi; g.y = (float *) dy; g.ldy = ycols;
+        g.resid = (const float *) dy; g.ldr = ycols; g.err = (int *) derr;
+        const size_t sm = tc_smem_bytes(np);
+        chk(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm));
+        if (ok) k_gemm_tc<<<rows_w / TC_BM, TC_THREADS, sm>>>(g);
+        chk(cudaGetLastError());
+        chk(cudaDeviceSynchronize());
+        int herr = 0;
+        if (ok) chk(cudaMemcpy(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost));
+        if (herr) ok = false;
+        if (ok) chk(cudaMemcpy(y, dy, sizeof(float) * m * ycols, cudaMemcpyDeviceToHost));
+    }
+    void * all[] = {dw, dw2, dwt, dx, dxt, dy, dg, derr};
+    for (void * p : all) if (p) cudaFree(p);
+    return ok ? 1 : 0;
+}
+
 int32_t qtts_op_gemv(int32_t device, int32_t wtype, const void * w, int32_t rows, int32_t cols, const float * xin,
                      int32_t nv, const float * norm_gain, float eps, int32_t act_f32, float * y, int32_t * block_dots) {
     using namespace qtts;

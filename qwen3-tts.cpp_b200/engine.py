@@ -110,6 +110,8 @@ def lib():
         "qtts_program_ops": (C.c_int32, [C.c_void_p, _i32p, C.c_int32]),
         "qtts_op_trace": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64), C.c_int32]),
         "qtts_profile_frames": (C.c_int32, [C.c_void_p, C.c_int32, C.POINTER(KernelStats), C.c_int32]),
+        "qtts_op_gemm_tc": (C.c_int32, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32,
+                                        _f32p, C.c_float, C.c_int32, C.c_int32, _f32p, _f32p]),
         "qtts_op_gemv": (C.c_int32, [C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32, _f32p,
                                      C.c_float, C.c_int32, _f32p, _i32p]),
         "qtts_op_sample": (C.c_int32, [C.c_int32, _f32p, C.c_int32, C.c_int32, C.c_float, C.c_int32, C.c_float, _i32p,
@@ -342,6 +344,29 @@ def op_gemv(w, wtype: int, rows: int, cols: int, x, norm_gain=None, eps=1e-6, ac
     if not rc:
         raise RuntimeError("qtts_op_gemv failed")
     return (y, bd) if want_block_dots else y
+
+
+TC_ACT_F16, TC_ACT_SPLIT = 0, 1
+TC_EPI_STORE, TC_EPI_RESID, TC_EPI_SWIGLU = 0, 1, 2
+
+
+def op_gemm_tc(w, x, w_up=None, norm_gain=None, eps=1e-6, act=TC_ACT_F16, epi=TC_EPI_STORE, resid=None,
+               device: int = 0):
+    """Run the tcgen05 GEMM once: y [m][rows] (see qtts_op_gemm_tc)."""
+    w = np.ascontiguousarray(w, dtype=np.float16)
+    rows, cols = w.shape
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, cols)
+    m = x.shape[0]
+    wu = None if w_up is None else np.ascontiguousarray(w_up, dtype=np.float16)
+    g = None if norm_gain is None else np.ascontiguousarray(norm_gain, dtype=np.float32)
+    r = None if resid is None else np.ascontiguousarray(resid, dtype=np.float32)
+    y = np.zeros((m, rows), np.float32)
+    rc = lib().qtts_op_gemm_tc(device, w.ctypes.data_as(C.c_void_p), None if wu is None else wu.ctypes.data_as(C.c_void_p),
+                               rows, cols, _p(x, C.c_float), m, _p(g, C.c_float), eps, act, epi, _p(r, C.c_float),
+                               _p(y, C.c_float))
+    if not rc:
+        raise RuntimeError("qtts_op_gemm_tc failed")
+    return y
 
 
 def op_sample(logits, cb: int, temperature=0.0, top_k=0, rep_penalty=1.0, presence=None, eos_bias=0.0,
