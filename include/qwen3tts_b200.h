@@ -220,6 +220,30 @@ int32_t qtts_op_sample_noalloc(int32_t device, const float * logits, int32_t V, 
                                int32_t target_frames, int32_t frame, int32_t eos_id, int32_t suppress_start,
                                uint64_t seed, int32_t * token_out, void * stream);
 
+/* ---- batched frame loop (B independent utterances on one GPU; no reference
+ * counterpart: the reference serves one sequence per TTSTransformer).
+ * Every projection is a tcgen05 tensor-core GEMM over the batch rows, the
+ * talker KV lives in 64-position pages, and each sequence keeps its own frame
+ * state.  Weights are shared with the engine (F16 models only).
+ *   create: max_batch <= 64 sequences, max_positions = prompt + frames capacity
+ *           per sequence, max_frames = codes capacity per sequence; NULL on
+ *           failure (qtts_get_error(e) holds the message).
+ *   begin:  runs each sequence's prefill (params[i], as qtts_generate) and arms
+ *           the batch; sampling parameters come from params[0].  0 / -1.
+ *   run:    advances up to n_frames frames for the whole batch; returns the
+ *           number of sequence-frames produced, -1 on error.
+ *   codes:  codes_out [n][max_frames][n_codebooks], n_frames_out [n].
+ *   timing: device time of all run calls since begin, sequence-frames, kernels
+ *           launched per frame. */
+typedef struct qtts_batch qtts_batch;
+qtts_batch * qtts_batch_create(qtts_engine * e, int32_t max_batch, int32_t max_positions, int32_t max_frames);
+int32_t qtts_batch_begin(qtts_batch * b, int32_t n, const qtts_generate_params * params);
+int32_t qtts_batch_run(qtts_batch * b, int32_t n_frames);
+int32_t qtts_batch_codes(qtts_batch * b, int32_t * codes_out, int32_t * n_frames_out);
+int32_t qtts_batch_timing(const qtts_batch * b, float * frames_ms, int32_t * seq_frames, int32_t * launches_per_frame);
+const char * qtts_batch_error(const qtts_batch * b);
+void qtts_batch_free(qtts_batch * b);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,340 @@
+// batch_engine.cuh — the frame loop for B independent utterances on one GPU
+// (BASELINE configs 4 and 5: batched F16 serving, paged F16 KV cache).
+//
+// One frame for all B sequences is one CUDA graph: every projection is a
+// tcgen05 tensor-core GEMM over the B (or 2B) activation rows (gemm_tc.cuh),
+// the code predictor's attention runs the fused unit per (sequence, head,
+// row), the talker's attention streams each sequence's KV pages through shared
+// memory with bulk copies (one CTA per (sequence, kv head), exact two-pass
+// softmax as ggml_soft_max), and samplers / input builders run one CTA per
+// sequence.  Sequences keep their own frame state (position, codes, presence
+// set, EOS flag), so they may have different prompt lengths and stop at
+// different frames; a finished sequence's rows are still multiplied (the GEMM
+// is one pass over the weights either way) but its attention, sampling and
+// state are frozen.
+//
+// KV pages: BP_PAGE positions of every talker layer, laid out
+// [page][layer][K|V][kv_head][BP_PAGE][128] F16, so one (page, layer, head)
+// block of K or V is 16 KB contiguous (one bulk copy).  A sequence's pages come
+// from a pool through its row of the page table.  This file is included into
+// engine.cu after the Engine definition (it shares the Engine's weights).
+#pragma once
+
+namespace qtts {
+
+constexpr int BP_PAGE = 64;           // positions per KV page
+constexpr int PA_THREADS = 256;
+constexpr int PA_RING = 8;            // page blocks in flight per CTA
+
+__host__ __device__ inline size_t bp_page_elems(int n_layers, int nkv) {
+    return (size_t) n_layers * 2 * nkv * BP_PAGE * QTTS_HD;
+}
+__host__ __device__ inline size_t bp_off(int page, int layer, int kv, int head, int p, int n_layers, int nkv) {
+    return ((((size_t) page * n_layers + layer) * 2 + kv) * nkv + head) * (size_t) BP_PAGE * QTTS_HD +
+           (size_t) p * QTTS_HD;
+}
+
+// ---- talker attention over paged KV ---------------------------------------
+struct PagedAttnArgs {
+    float * qkv;              // [B][ldq] raw q|k|v rows
+    int ldq;
+    int n_heads, n_kv_heads, n_layers, layer;
+    const float * q_norm, * k_norm;
+    float eps;
+    const float2 * rope;      // [pos][64]
+    __half * pool;
+    const int * page_table;   // [B][max_pages]
+    int max_pages;
+    const DevState * st;      // [B]
+    float scale;
+    float * out;              // [B][ldo]
+    int ldo;
+    int n_max;                // capacity of the score buffer (positions)
+};
+
+__host__ __device__ inline size_t paged_attn_smem(int n_max, int G) {
+    return (size_t) PA_RING * BP_PAGE * QTTS_HD * 2 + (size_t) G * ((n_max + 3) & ~3) * 4 + (size_t) G * QTTS_HD * 4 +
+           2 * QTTS_HD * 4 + (size_t)(PA_THREADS / 64) * G * QTTS_HD * 4 + 256;
+}
+
+// One CTA per (sequence b, kv head g): the G query heads of the group share
+// every K/V load.  Item i of the stream is page (i mod np) of K (i < np) or V.
+__global__ void __launch_bounds__(PA_THREADS, 1) k_attn_paged(PagedAttnArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[PA_RING];
+    const int NKV = a.n_kv_heads, G = a.n_heads / NKV;
+    const int b = blockIdx.x / NKV, g = blockIdx.x % NKV;
+    const DevState & S = a.st[b];
+    if (S.done) return;
+    const int pos = S.pos, n = pos + 1, np = (n + BP_PAGE - 1) / BP_PAGE;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = PA_THREADS / 32;
+    const int nk4 = (n + 3) & ~3;
+    __half * ring = reinterpret_cast<__half *>(smem);
+    float * sc = reinterpret_cast<float *>(smem + (size_t) PA_RING * BP_PAGE * QTTS_HD * 2);   // [G][nk4]
+    float * qs = sc + G * ((a.n_max + 3) & ~3);                                                  // [G][128]
+    float * kcur = qs + G * QTTS_HD;                                                             // [128]
+    float * vcur = kcur + QTTS_HD;                                                               // [128]
+    float * part = vcur + QTTS_HD;                                                               // [4][G][128]
+    const int * pt = a.page_table + (size_t) b * a.max_pages;
+    const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
+    const unsigned blk = BP_PAGE * QTTS_HD * 2;
+    const int nitems = 2 * np;
+
+    int issued = 0, consumed = 0;   // stream items (meaningful in thread 0, which issues and waits)
+    if (tid == 0) {
+        for (int s = 0; s < PA_RING; ++s) mbar_init(&full[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int i = 0; i < PA_RING && i < nitems; ++i) {
+            const int kv = i >= np, page = i % np;
+            mbar_expect_tx(&full[i], blk);
+            bulk_g2s(ring + (size_t) i * BP_PAGE * QTTS_HD,
+                     a.pool + bp_off(pt[page], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[i]);
+            issued = i + 1;
+        }
+    }
+    // q heads and the new k/v row (the row is also appended to its page)
+    const float * row = a.qkv + (size_t) b * a.ldq;
+    if (warp < G) {
+        const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
+        const float4 q4 = *reinterpret_cast<const float4 *>(row + (size_t)(g * G + warp) * QTTS_HD + lane * 4);
+        float gv[4];
+        float2 cs[4];
+        head_params(a.q_norm, rp, lane, gv, cs);
+        float x[4] = {q4.x, q4.y, q4.z, q4.w};
+        head_norm_rope_v(x, gv, cs, a.eps, lane);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) qs[warp * QTTS_HD + lane * 4 + k] = round_f16(x[k]);
+    } else if (warp == G) {
+        const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
+        const float4 k4 = *reinterpret_cast<const float4 *>(row + QD + g * QTTS_HD + lane * 4);
+        const float4 v4 = *reinterpret_cast<const float4 *>(row + QD + KD + g * QTTS_HD + lane * 4);
+        float gv[4];
+        float2 cs[4];
+        head_params(a.k_norm, rp, lane, gv, cs);
+        float x[4] = {k4.x, k4.y, k4.z, k4.w};
+        const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+        head_norm_rope_v(x, gv, cs, a.eps, lane);
+        const int pg = pt[pos / BP_PAGE], p = pos % BP_PAGE;
+        __half * kd = a.pool + bp_off(pg, a.layer, 0, g, p, a.n_layers, NKV) + lane * 4;
+        __half * vd = a.pool + bp_off(pg, a.layer, 1, g, p, a.n_layers, NKV) + lane * 4;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __half kh = __float2half_rn(x[k]), vh = __float2half_rn(v[k]);
+            kd[k] = kh;
+            vd[k] = vh;
+            kcur[lane * 4 + k] = __half2float(kh);
+            vcur[lane * 4 + k] = __half2float(vh);
+        }
+    }
+    __syncthreads();
+
+    // scores: per page, 8 lanes per position (16 dims each), 4 positions per warp step
+    const int sub = lane & 7, slot = lane >> 3;
+    bool ok = true;
+    for (int i = 0; i < np; ++i) {
+        const int s = i % PA_RING;
+        if (tid == 0) { ok = mbar_wait(&full[s], (i / PA_RING) & 1); consumed += ok; }
+        if (__syncthreads_or(!ok)) { ok = false; break; }
+        const __half * kb = ring + (size_t) s * BP_PAGE * QTTS_HD;
+        for (int p0 = warp * 4; p0 < BP_PAGE; p0 += nw * 4) {
+            const int p = p0 + slot, j = i * BP_PAGE + p;
+            float kv[16];
+            if (j == pos) {
+#pragma unroll
+                for (int d = 0; d < 16; ++d) kv[d] = kcur[sub * 16 + d];
+            } else {
+                const uint4 * kp = reinterpret_cast<const uint4 *>(kb + (size_t) p * QTTS_HD + sub * 16);
+#pragma unroll
+                for (int h8 = 0; h8 < 2; ++h8) {
+                    const uint4 u = kp[h8];
+                    const __half2 * hp = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 f = __half22float2(hp[k]);
+                        kv[8 * h8 + 2 * k] = f.x;
+                        kv[8 * h8 + 2 * k + 1] = f.y;
+                    }
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < ATT_MAX_GROUP; ++h) {
+                if (h >= G) break;
+                float acc = 0.0f;
+#pragma unroll
+                for (int d = 0; d < 16; ++d) acc = fmaf(kv[d], qs[h * QTTS_HD + sub * 16 + d], acc);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                if (sub == 0 && j < n) sc[h * nk4 + j] = __fmul_rn(acc, a.scale);
+            }
+        }
+        __syncthreads();   // slot s is free again
+        const int nx = i + PA_RING;
+        if (tid == 0 && nx < nitems) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const int kv = nx >= np, page = nx % np;
+            mbar_expect_tx(&full[s], blk);
+            bulk_g2s(ring + (size_t) s * BP_PAGE * QTTS_HD,
+                     a.pool + bp_off(pt[page], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[s]);
+            issued = nx + 1;
+        }
+    }
+    // softmax per head: max, expf, double sum, e * (float)(1/sum), rounded to F16
+    if (ok && warp < G) {
+        float * r = sc + warp * nk4;
+        float mx = -INFINITY;
+        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, r[j]);
+        mx = warp_max(mx);
+        double sum = 0.0;
+        for (int j = lane; j < n; j += 32) {
+            const float e = expf(__fsub_rn(r[j], mx));
+            r[j] = e;
+            sum += (double) e;
+        }
+        sum = warp_sum_d(sum);
+        const float inv = (float)(1.0 / sum);
+        for (int j = lane; j < n; j += 32) r[j] = round_f16(__fmul_rn(r[j], inv));
+    }
+    // P x V: thread (position group pq, dims 2 d2 .. 2 d2 + 1) for all G heads
+    const int pq = tid >> 6, d2 = tid & 63;
+    float acc[ATT_MAX_GROUP][2];
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_GROUP; ++h) acc[h][0] = acc[h][1] = 0.0f;
+    for (int i = np; ok && i < nitems; ++i) {
+        const int s = i % PA_RING, page = i - np;
+        if (tid == 0) { ok = mbar_wait(&full[s], (i / PA_RING) & 1); consumed += ok; }
+        if (__syncthreads_or(!ok)) { ok = false; break; }
+        const __half * vb = ring + (size_t) s * BP_PAGE * QTTS_HD;
+        for (int p = pq; p < BP_PAGE; p += PA_THREADS / 64) {
+            const int j = page * BP_PAGE + p;
+            if (j >= n) break;
+            float2 v;
+            if (j == pos) v = make_float2(vcur[2 * d2], vcur[2 * d2 + 1]);
+            else v = __half22float2(*reinterpret_cast<const __half2 *>(vb + (size_t) p * QTTS_HD + 2 * d2));
+#pragma unroll
+            for (int h = 0; h < ATT_MAX_GROUP; ++h)
+                if (h < G) {
+                    const float pj = sc[h * nk4 + j];
+                    acc[h][0] = fmaf(pj, v.x, acc[h][0]);
+                    acc[h][1] = fmaf(pj, v.y, acc[h][1]);
+                }
+        }
+        __syncthreads();
+        const int nx = i + PA_RING;
+        if (tid == 0 && nx < nitems) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const int kv = nx >= np, pg = nx % np;
+            mbar_expect_tx(&full[s], blk);
+            bulk_g2s(ring + (size_t) s * BP_PAGE * QTTS_HD,
+                     a.pool + bp_off(pt[pg], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[s]);
+            issued = nx + 1;
+        }
+    }
+    if (!ok) {
+        // a copy did not land within the wait limit: wait (bounded) for those still in flight
+        if (tid == 0)
+            for (int j = consumed; j < issued; ++j) mbar_wait(&full[j % PA_RING], (j / PA_RING) & 1);
+        return;
+    }
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_GROUP; ++h)
+        if (h < G) {
+            part[(pq * G + h) * QTTS_HD + 2 * d2] = acc[h][0];
+            part[(pq * G + h) * QTTS_HD + 2 * d2 + 1] = acc[h][1];
+        }
+    __syncthreads();
+    for (int t = tid; t < G * QTTS_HD; t += PA_THREADS) {
+        float s = 0.0f;
+        for (int q = 0; q < PA_THREADS / 64; ++q) s = __fadd_rn(s, part[q * G * QTTS_HD + t]);
+        a.out[(size_t) b * a.ldo + (size_t)(g * G) * QTTS_HD + t] = s;
+    }
+}
+
+// ---- code-predictor attention for B sequences ------------------------------
+// Unit (b, u): the fused unit u of sequence b, whose qkv / att rows start at row
+// b * M and whose code-predictor cache is its own [ctx][NKV][128] slab.
+__global__ void __launch_bounds__(FA_THREADS) k_cp_attn_batch(FusedAttn a, size_t cache_stride, const DevState * st,
+                                                              int units) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const int b = blockIdx.x / units, u = blockIdx.x % units;
+    if (st[b].done) return;
+    FusedAttn s = a;
+    s.qkv += (size_t) b * a.M * a.ldq;
+    s.kc += (size_t) b * cache_stride;
+    s.vc += (size_t) b * cache_stride;
+    s.out += (size_t) b * a.M * a.ldo;
+    fused_attn_body(s, u, smem_raw, a.pos_static, 0);
+}
+
+// ---- per-sequence samplers, inputs and frame end ---------------------------
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_sample_batch(const float * logits, int ldl, int V, int cb,
+                                                                 DevState * st, const SampleParams * sp,
+                                                                 int * out_codes, int out_cap) {
+    const int b = blockIdx.x;
+    DevState * s = st + b;
+    if (s->done) return;
+    SampleParams P = *sp;
+    P.seed += 0x9E3779B97F4A7C15ull * (unsigned long long) b;   // independent Philox stream per sequence
+    P.record_logits = 0;
+    const int frame = s->frame;
+    const int tok = sample_body<SAMPLE_PER_T>(logits + (size_t) b * ldl, V, cb, s, P, frame);
+    if (threadIdx.x == 0) sample_commit(tok, cb, s, P, out_codes + (size_t) b * out_cap * P.n_cb, out_cap, frame);
+}
+
+struct BatchInputArgs {
+    int mode, g, H, n_cb;
+    const __half * codec_embd;
+    const __half * const * cp_embd;
+    const float * hidden;        // [B][H]
+    const float * trailing;      // [B][trail_cap][H]
+    int trail_cap;
+    const float * pad;           // [H]
+    float * out;
+    const DevState * st;
+};
+
+__global__ void k_inputs_batch(BatchInputArgs a) {
+    const int b = blockIdx.x;
+    const DevState & S = a.st[b];
+    if (S.done) return;
+    const int H = a.H;
+    for (int h = threadIdx.x; h < H; h += blockDim.x) {
+        if (a.mode == IN_CP_PREFILL) {
+            a.out[(size_t)(2 * b) * H + h] = a.hidden[(size_t) b * H + h];
+            a.out[(size_t)(2 * b + 1) * H + h] = __half2float(a.codec_embd[(size_t) S.codes[0] * H + h]);
+        } else if (a.mode == IN_CP_STEP) {
+            a.out[(size_t) b * H + h] = __half2float(a.cp_embd[a.g - 1][(size_t) S.codes[a.g] * H + h]);
+        } else {
+            float s = __half2float(a.codec_embd[(size_t) S.codes[0] * H + h]);
+            for (int cb = 1; cb < a.n_cb; ++cb)
+                s = __fadd_rn(s, __half2float(a.cp_embd[cb - 1][(size_t) S.codes[cb] * H + h]));
+            const float * tr = S.frame < S.n_trailing ? a.trailing + ((size_t) b * a.trail_cap + S.frame) * H : a.pad;
+            a.out[(size_t) b * H + h] = __fadd_rn(s, tr[h]);
+        }
+    }
+}
+
+__global__ void k_frame_end_batch(DevState * st, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B && !st[b].done) {
+        st[b].pos += 1;
+        st[b].frame += 1;
+        st[b].n_out += 1;
+    }
+}
+
+// Copy a prefill's KV rows [0, n) from the contiguous cache [layer][ctx][NKV][128]
+// into the sequence's pages.
+__global__ void k_kv_to_pages(const __half * kc, const __half * vc, int ctx, int n, int n_layers, int nkv,
+                              const int * pt, __half * pool) {
+    const int j = blockIdx.x, layer = blockIdx.y;
+    if (j >= n) return;
+    const size_t src = ((size_t) layer * ctx + j) * nkv * QTTS_HD;
+    for (int t = threadIdx.x; t < nkv * QTTS_HD; t += blockDim.x) {
+        const int h = t / QTTS_HD, d = t % QTTS_HD;
+        pool[bp_off(pt[j / BP_PAGE], layer, 0, h, j % BP_PAGE, n_layers, nkv) + d] = kc[src + t];
+        pool[bp_off(pt[j / BP_PAGE], layer, 1, h, j % BP_PAGE, n_layers, nkv) + d] = vc[src + t];
+    }
+}
+
+}  // namespace qtts

@@ -20,6 +20,7 @@
 #include "gguf.hpp"
 #include "persistent.cuh"
 #include "gemm_tc.cuh"
+#include "batch_engine.cuh"
 
 #include <algorithm>
 #include <chrono>
@@ -1337,6 +1338,8 @@ int Engine::run_frames(int n, int32_t * codes_out) {
 
 }  // namespace qtts
 
+#include "batch_host.cuh"
+
 using qtts::Engine;
 
 // ================================================================ C ABI
@@ -1916,3 +1919,48 @@ int32_t qtts_get_timing(const qtts_engine * h, qtts_timing * out) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- batched frame loop (configs 4, 5)
+struct qtts_batch { qtts::BatchEngine be; };
+
+qtts_batch * qtts_batch_create(qtts_engine * h, int32_t max_batch, int32_t max_positions, int32_t max_frames) {
+    if (!h || max_positions <= 0 || max_frames <= 0) return nullptr;
+    ENG(h);
+    auto * b = new qtts_batch();
+    if (!b->be.create(&E, max_batch, max_positions, max_frames)) {
+        E.err = b->be.err;
+        delete b;
+        return nullptr;
+    }
+    return b;
+}
+
+int32_t qtts_batch_begin(qtts_batch * b, int32_t n, const qtts_generate_params * params) {
+    if (!b || !params) return -1;
+    cudaSetDevice(b->be.dev);
+    return b->be.begin(n, params);
+}
+
+int32_t qtts_batch_run(qtts_batch * b, int32_t n_frames) {
+    if (!b) return -1;
+    cudaSetDevice(b->be.dev);
+    return b->be.run(n_frames);
+}
+
+int32_t qtts_batch_codes(qtts_batch * b, int32_t * codes_out, int32_t * n_frames_out) {
+    if (!b) return 0;
+    cudaSetDevice(b->be.dev);
+    return b->be.read_codes(codes_out, n_frames_out) ? 1 : 0;
+}
+
+int32_t qtts_batch_timing(const qtts_batch * b, float * frames_ms, int32_t * seq_frames, int32_t * launches_per_frame) {
+    if (!b) return 0;
+    if (frames_ms) *frames_ms = b->be.frames_ms;
+    if (seq_frames) *seq_frames = b->be.seq_frames;
+    if (launches_per_frame) *launches_per_frame = b->be.launches;
+    return 1;
+}
+
+const char * qtts_batch_error(const qtts_batch * b) { return b ? b->be.err.c_str() : "null batch"; }
+
+void qtts_batch_free(qtts_batch * b) { delete b; }

@@ -177,7 +177,7 @@ __host__ __device__ inline size_t tc_smem_bytes(int np) { return TC_STAGES * tc_
 
 // One CTA per 128-row weight tile, full K.
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
-    extern __shared__ __align__(1024) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t tc_smem[];
     __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], done;
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
         for (int i = 0; i < nk; ++i) {
             const int s = i % TC_STAGES;
             if (i >= TC_STAGES && !mbar_wait(&empty[s], ((i / TC_STAGES) - 1) & 1)) { s_fail = 1; break; }
-            uint8_t * dst = smem + s * sbytes;
+            uint8_t * dst = tc_smem + s * sbytes;
             mbar_expect_tx(&full[s], (unsigned) sbytes);
             bulk_g2s(dst, wsrc + (size_t) i * wtile, (unsigned) wtile, &full[s]);
             bulk_g2s(dst + wtile, g.x + (size_t) i * xtile, (unsigned) xtile, &full[s]);
@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
             const int s = i % TC_STAGES;
             if (!mbar_wait(&full[s], (i / TC_STAGES) & 1)) { s_fail = 1; break; }
             tc_fence_after();
-            const uint32_t a0 = smem_u32(smem + s * sbytes), b0 = a0 + (uint32_t) wtile;
+            const uint32_t a0 = smem_u32(tc_smem + s * sbytes), b0 = a0 + (uint32_t) wtile;
 #pragma unroll
             for (int kk = 0; kk < TC_BK / 16; ++kk)
                 tc_mma(tmem, tc_smem_desc(a0 + kk * 256), tc_smem_desc(b0 + kk * 256), idesc, (i | kk) != 0);

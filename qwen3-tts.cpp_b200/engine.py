@@ -110,6 +110,14 @@ def lib():
         "qtts_program_ops": (C.c_int32, [C.c_void_p, _i32p, C.c_int32]),
         "qtts_op_trace": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64), C.c_int32]),
         "qtts_profile_frames": (C.c_int32, [C.c_void_p, C.c_int32, C.POINTER(KernelStats), C.c_int32]),
+        "qtts_batch_create": (C.c_void_p, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
+        "qtts_batch_begin": (C.c_int32, [C.c_void_p, C.c_int32, C.c_void_p]),
+        "qtts_batch_run": (C.c_int32, [C.c_void_p, C.c_int32]),
+        "qtts_batch_codes": (C.c_int32, [C.c_void_p, _i32p, _i32p]),
+        "qtts_batch_timing": (C.c_int32, [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int32),
+                                          C.POINTER(C.c_int32)]),
+        "qtts_batch_error": (C.c_char_p, [C.c_void_p]),
+        "qtts_batch_free": (None, [C.c_void_p]),
         "qtts_op_gemm_tc": (C.c_int32, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32,
                                         _f32p, C.c_float, C.c_int32, C.c_int32, _f32p, _f32p]),
         "qtts_op_gemv": (C.c_int32, [C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32, _f32p,
@@ -344,6 +352,71 @@ def op_gemv(w, wtype: int, rows: int, cols: int, x, norm_gain=None, eps=1e-6, ac
     if not rc:
         raise RuntimeError("qtts_op_gemv failed")
     return (y, bd) if want_block_dots else y
+
+
+_GEN_DEFAULTS = dict(speaker=None, ref_text=None, ref_codes=None, language_id=2050, rep_penalty=1.05, temperature=0.0,
+                     top_k=0, instruct=None, eos_bias=0.0, target_frames=0, rep_loop_detect=False, seed=0)
+
+
+class Batch:
+    """Batched frame loop (qtts_batch_*): up to max_batch utterances advance one
+    frame per step together on the engine's GPU, sharing its weights."""
+
+    def __init__(self, eng: "Engine", max_batch: int, max_positions: int, max_frames: int):
+        self.eng = eng
+        self.max_frames = max_frames
+        self.ncb = eng.cfg["n_codebooks"]
+        self.h = lib().qtts_batch_create(eng.h, max_batch, max_positions, max_frames)
+        if not self.h:
+            raise RuntimeError("batch create failed: " + eng.error())
+        self.n = 0
+
+    def error(self) -> str:
+        return lib().qtts_batch_error(self.h).decode()
+
+    def begin(self, utterances) -> None:
+        """utterances: list of dicts with `text`, `max_len` and generate()'s keyword arguments."""
+        n = len(utterances)
+        params = (GenParams * n)()
+        self._keep = []
+        for i, u in enumerate(utterances):
+            args = dict(_GEN_DEFAULTS)
+            args.update({k: v for k, v in u.items() if k not in ("text", "max_len")})
+            p, keep = self.eng._params(u["text"], u["max_len"], **args)
+            params[i] = p
+            self._keep.append(keep)
+        if lib().qtts_batch_begin(self.h, n, params) < 0:
+            raise RuntimeError("batch begin failed: " + self.error())
+        self.n = n
+
+    def run(self, n_frames: int) -> int:
+        rc = lib().qtts_batch_run(self.h, n_frames)
+        if rc < 0:
+            raise RuntimeError("batch run failed: " + self.error())
+        return rc
+
+    def codes(self):
+        c = np.zeros((self.n, self.max_frames, self.ncb), np.int32)
+        nf = np.zeros(self.n, np.int32)
+        if not lib().qtts_batch_codes(self.h, _p(c, C.c_int32), _p(nf, C.c_int32)):
+            raise RuntimeError("batch codes failed: " + self.error())
+        return [c[i, :nf[i]].copy() for i in range(self.n)]
+
+    def timing(self) -> dict:
+        ms, fr, la = C.c_float(0), C.c_int32(0), C.c_int32(0)
+        lib().qtts_batch_timing(self.h, C.byref(ms), C.byref(fr), C.byref(la))
+        return {"frames_ms": ms.value, "seq_frames": fr.value, "launches_per_frame": la.value}
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().qtts_batch_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 TC_ACT_F16, TC_ACT_SPLIT = 0, 1

@@ -1,0 +1,63 @@
+"""Batched frame loop (tcgen05 GEMMs, paged KV, per-sequence state) against the
+CPU oracle: every sequence of the batch, with its own prompt and prompt length,
+follows the oracle's greedy decisions (divergence allowed only at recorded
+near-ties, as for the single-sequence engine)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import text_ids
+from oracle import Oracle
+
+pytestmark = pytest.mark.gpu
+TIE_TOL = 1e-3
+
+
+def _utterances(rng, n, frames, hidden):
+    out = []
+    for i in range(n):
+        u = dict(text=text_ids(rng, 14 + 5 * i), max_len=frames, eos_bias=-1e9, rep_penalty=1.05)
+        if i % 2:
+            u["speaker"] = rng.standard_normal(hidden).astype(np.float32)
+        out.append(u)
+    return out
+
+
+@pytest.mark.parametrize("n", [1, 5])
+def test_batch_matches_oracle(qtts, tiny_f16, n):
+    rng = np.random.default_rng(40 + n)
+    eng = qtts.Engine(tiny_f16, 0)
+    H = eng.cfg["hidden_size"]
+    frames = 10
+    utts = _utterances(rng, n, frames, H)
+    b = qtts.engine.Batch(eng, max_batch=8, max_positions=256, max_frames=frames)
+    b.begin(utts)
+    assert b.run(frames) == n * frames
+    codes = b.codes()
+    o = Oracle(tiny_f16)
+    for i, u in enumerate(utts):
+        assert codes[i].shape == (frames, 16)
+        kw = {k: v for k, v in u.items() if k not in ("text", "max_len")}
+        r = o.generate(u["text"], frames, follow=codes[i], tie_tol=TIE_TOL, **kw)
+        assert r["n_mismatch"] == 0, (i, r["n_mismatch"], r["max_mismatch_gap"], r["first_mismatch"])
+        assert r["n_frames"] == frames
+    b.close()
+    eng.close()
+
+
+def test_batch_sequence_independence(qtts, tiny_f16):
+    """A sequence's codes do not depend on the other sequences of the batch."""
+    rng = np.random.default_rng(77)
+    eng = qtts.Engine(tiny_f16, 0)
+    utts = _utterances(rng, 4, 8, eng.cfg["hidden_size"])
+    b = qtts.engine.Batch(eng, max_batch=4, max_positions=256, max_frames=8)
+    b.begin(utts)
+    b.run(8)
+    together = b.codes()
+    b.begin(utts[2:3])
+    b.run(8)
+    alone = b.codes()
+    assert np.array_equal(together[2], alone[0])
+    b.close()
+    eng.close()
