@@ -241,6 +241,12 @@ int32_t qtts_batch_begin(qtts_batch * b, int32_t n, const qtts_generate_params *
 int32_t qtts_batch_run(qtts_batch * b, int32_t n_frames);
 int32_t qtts_batch_codes(qtts_batch * b, int32_t * codes_out, int32_t * n_frames_out);
 int32_t qtts_batch_timing(const qtts_batch * b, float * frames_ms, int32_t * seq_frames, int32_t * launches_per_frame);
+/* Runs n_frames frames eagerly with CUDA events around every launch (frames
+ * advance as with run).  Per frame, for the 10 kernel classes (pack, GEMM
+ * qkv / o / gate-up / down / heads, code-predictor attention, talker attention,
+ * samplers, other): device ms into ms_per_frame[10], launches into
+ * launches_per_frame[10]. */
+int32_t qtts_batch_profile(qtts_batch * b, int32_t n_frames, float * ms_per_frame, int32_t * launches_per_frame);
 const char * qtts_batch_error(const qtts_batch * b);
 void qtts_batch_free(qtts_batch * b);
 

@@ -50,6 +50,8 @@ struct PagedAttnArgs {
     float * out;              // [B][ldo]
     int ldo;
     int n_max;                // capacity of the score buffer (positions)
+    uint8_t * xt;             // optional: output also as F16 tiles (row b) for the O-projection GEMM
+    int xt_np;
 };
 
 __host__ __device__ inline size_t paged_attn_smem(int n_max, int G) {
@@ -247,6 +249,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) k_attn_paged(PagedAttnArgs a) {
         float s = 0.0f;
         for (int q = 0; q < PA_THREADS / 64; ++q) s = __fadd_rn(s, part[q * G * QTTS_HD + t]);
         a.out[(size_t) b * a.ldo + (size_t)(g * G) * QTTS_HD + t] = s;
+        if (a.xt) *reinterpret_cast<__half *>(a.xt + tc_x_off(b, g * G * QTTS_HD + t, a.xt_np)) = __float2half_rn(s);
     }
 }
 
@@ -263,6 +266,7 @@ __global__ void __launch_bounds__(FA_THREADS) k_cp_attn_batch(FusedAttn a, size_
     s.kc += (size_t) b * cache_stride;
     s.vc += (size_t) b * cache_stride;
     s.out += (size_t) b * a.M * a.ldo;
+    s.xt_row0 = b * a.M;
     fused_attn_body(s, u, smem_raw, a.pos_static, 0);
 }
 

@@ -21,7 +21,7 @@ struct BatchEngine {
     std::vector<void *> owned;
     float * x = nullptr, * xcp = nullptr, * qkv = nullptr, * att = nullptr, * hbuf = nullptr;
     float * logits = nullptr, * cp_logits = nullptr, * hidden = nullptr, * trail = nullptr, * pad = nullptr;
-    uint8_t * xt = nullptr;
+    uint8_t * xt = nullptr, * xt2 = nullptr;   // tiled activations: pack target / producer-written
     DevState * st = nullptr;
     SampleParams * sp = nullptr;
     int * codes = nullptr, * page_table = nullptr, * d_err = nullptr;
@@ -35,6 +35,26 @@ struct BatchEngine {
     int seq_frames = 0;
     std::vector<int> produced;
     int launches = 0;
+    // eager per-class profile (events around every launch; not used in the graph)
+    enum { BC_PACK = 0, BC_GEMM_QKV, BC_GEMM_O, BC_GEMM_GU, BC_GEMM_DOWN, BC_GEMM_HEAD, BC_ATTN_CP, BC_ATTN_TALKER,
+           BC_SAMPLE, BC_OTHER, BC_N };
+    bool prof = false;
+    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_ev;
+    int prof_cls = BC_OTHER;
+    cudaEvent_t prof_a = nullptr;
+    void pb(int cls) {
+        if (!prof) return;
+        prof_cls = cls;
+        cudaEventCreate(&prof_a);
+        cudaEventRecord(prof_a, stream);
+    }
+    void pe() {
+        if (!prof) return;
+        cudaEvent_t b;
+        cudaEventCreate(&b);
+        cudaEventRecord(b, stream);
+        prof_ev.push_back({prof_cls, {prof_a, b}});
+    }
 
     template <class T>
     bool alloc(T ** p, size_t bytes) {
@@ -98,6 +118,7 @@ struct BatchEngine {
             !alloc(&hbuf, sizeof(float) * R * std::max(FF, CFF)) || !alloc(&logits, sizeof(float) * Bmax * V0) ||
             !alloc(&cp_logits, sizeof(float) * Bmax * V1) || !alloc(&hidden, sizeof(float) * Bmax * H) ||
             !alloc(&pad, sizeof(float) * H) || !alloc(&xt, (size_t) TC_MAX_N * maxc * 2) ||
+            !alloc(&xt2, (size_t) TC_MAX_N * maxc * 2) ||
             !alloc(&st, sizeof(DevState) * Bmax) || !alloc(&sp, sizeof(SampleParams)) ||
             !alloc(&codes, sizeof(int) * Bmax * max_frames * NCB) || !alloc(&d_err, sizeof(int)))
             return false;
@@ -124,6 +145,7 @@ struct BatchEngine {
         }
         const size_t tcs = tc_smem_bytes(TC_MAX_N);
         if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) tcs) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
             cudaFuncSetAttribute(k_attn_paged, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int) paged_attn_smem(n_max, NH / NKV)) != cudaSuccess ||
             cudaFuncSetAttribute(k_cp_attn_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess) {
@@ -135,37 +157,58 @@ struct BatchEngine {
     }
 
     // Y = W a (+ epilogue) for m activation rows: pack (RMSNorm, F16 / hi-lo) + tcgen05 GEMM.
+    // xin == nullptr: the activation tiles are already in xt2 (written by the producer).
+    // xt_next: SwiGLU only, also write h as hi/lo tiles into xt2 for the down GEMM.
     void gemm(const uint8_t * wt, int rows_w, int cols, const float * xin, int ldx, int m, const float * norm, int act,
-              int epi, float * y, int ldy, const float * resid, float * xn_out = nullptr) {
+              int epi, float * y, int ldy, const float * resid, float * xn_out = nullptr, bool xt_next = false) {
         const int mp = (m + 15) / 16 * 16;
         const int np = act == TC_ACT_SPLIT ? 2 * mp : mp;
-        PackArgs pa{};
-        pa.x = xin; pa.ldx = ldx; pa.m_real = m; pa.np = np; pa.cols = cols; pa.gain = norm;
-        pa.eps = E->cfg.rms_norm_eps; pa.act = act; pa.out = xt; pa.xn_out = xn_out; pa.ldxn = H;
-        k_pack_act<<<act == TC_ACT_SPLIT ? np / 2 : np, 256, 0, stream>>>(pa);
+        const uint8_t * xsrc = xt2;
+        if (xin) {
+            PackArgs pa{};
+            pa.x = xin; pa.ldx = ldx; pa.m_real = m; pa.np = np; pa.cols = cols; pa.gain = norm;
+            pa.eps = E->cfg.rms_norm_eps; pa.act = act; pa.out = xt; pa.xn_out = xn_out; pa.ldxn = H;
+            pb(BC_PACK);
+            k_pack_act<<<act == TC_ACT_SPLIT ? np / 2 : np, 256, 0, stream>>>(pa);
+            pe();
+            launches += 1;
+            xsrc = xt;
+        }
         GemmTcArgs g{};
-        g.w = wt; g.x = xt; g.rows_w = rows_w; g.cols = cols; g.np = np; g.m_real = m;
+        g.w = wt; g.x = xsrc; g.rows_w = rows_w; g.cols = cols; g.np = np; g.m_real = m;
         g.split = act == TC_ACT_SPLIT; g.epi = epi; g.y = y; g.ldy = ldy; g.resid = resid; g.ldr = ldy; g.err = d_err;
-        k_gemm_tc<<<rows_w / TC_BM, TC_THREADS, tc_smem_bytes(np), stream>>>(g);
-        launches += 2;
+        if (xt_next) { g.xt_out = xt2; g.xt_np = 2 * mp; }
+        g.ksplit = tc_choose_split(rows_w / TC_BM, cols / TC_BK);
+        pb(gemm_cls);
+        tc_launch(g, tc_smem_bytes(np), stream);
+        pe();
+        launches += 1;
     }
+    int gemm_cls = BC_GEMM_QKV;
 
     void cp_layers(int M, bool f32, int pos_static) {
         const int rows = B * M;
         for (size_t il = 0; il < E->CPL.size(); ++il) {
             const LayerW & l = E->CPL[il];
             const TiledLayer & t = TCP[il];
+            gemm_cls = BC_GEMM_QKV;
             gemm(t.qkv, QKVD, H, xcp, H, rows, l.attn_norm, TC_ACT_F16, TC_EPI_STORE, qkv, QKVD, nullptr);
             FusedAttn fa{};
             fa.qkv = qkv; fa.ldq = QKVD; fa.n_heads = NH; fa.n_kv_heads = NKV; fa.q_norm = l.q_norm;
             fa.k_norm = l.k_norm; fa.eps = E->cfg.rms_norm_eps; fa.rope = E->rope_cp;
             fa.kc = cpk + il * cp_layer; fa.vc = cpv + il * cp_layer; fa.pos_static = pos_static; fa.M = M;
             fa.f32_mode = f32 ? 1 : 0; fa.scale = 1.0f / sqrtf((float) QTTS_HD); fa.out = att; fa.ldo = QD;
+            fa.xt = xt2; fa.xt_np = (rows + 15) / 16 * 16;
             const size_t fsm = fused_attn_smem(f32 ? M : 16, M);
+            pb(BC_ATTN_CP);
             k_cp_attn_batch<<<B * NH * M, FA_THREADS, fsm, stream>>>(fa, cp_stride, st, NH * M);
-            gemm(t.o, H, QD, att, QD, rows, nullptr, TC_ACT_F16, TC_EPI_RESID, xcp, H, xcp);
-            gemm(t.gu, 2 * CFF, H, xcp, H, rows, l.ffn_norm, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, CFF, nullptr);
-            gemm(t.down, H, CFF, hbuf, CFF, rows, nullptr, TC_ACT_SPLIT, TC_EPI_RESID, xcp, H, xcp);
+            pe();
+            gemm_cls = BC_GEMM_O;
+            gemm(t.o, H, QD, nullptr, QD, rows, nullptr, TC_ACT_F16, TC_EPI_RESID, xcp, H, xcp);
+            gemm_cls = BC_GEMM_GU;
+            gemm(t.gu, 2 * CFF, H, xcp, H, rows, l.ffn_norm, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, CFF, nullptr, nullptr, true);
+            gemm_cls = BC_GEMM_DOWN;
+            gemm(t.down, H, CFF, nullptr, CFF, rows, nullptr, TC_ACT_SPLIT, TC_EPI_RESID, xcp, H, xcp);
             launches += 1;
         }
     }
@@ -175,16 +218,23 @@ struct BatchEngine {
         for (size_t il = 0; il < E->L.size(); ++il) {
             const LayerW & l = E->L[il];
             const TiledLayer & t = TL[il];
+            gemm_cls = BC_GEMM_QKV;
             gemm(t.qkv, QKVD, H, x, H, B, l.attn_norm, TC_ACT_F16, TC_EPI_STORE, qkv, QKVD, nullptr);
             PagedAttnArgs pa{};
             pa.qkv = qkv; pa.ldq = QKVD; pa.n_heads = NH; pa.n_kv_heads = NKV; pa.n_layers = (int) E->L.size();
             pa.layer = (int) il; pa.q_norm = l.q_norm; pa.k_norm = l.k_norm; pa.eps = E->cfg.rms_norm_eps;
             pa.rope = rope_t; pa.pool = pool; pa.page_table = page_table; pa.max_pages = max_pages; pa.st = st;
             pa.scale = 1.0f / sqrtf((float) QTTS_HD); pa.out = att; pa.ldo = QD; pa.n_max = n_max;
+            pa.xt = xt2; pa.xt_np = (B + 15) / 16 * 16;
+            pb(BC_ATTN_TALKER);
             k_attn_paged<<<B * NKV, PA_THREADS, paged_attn_smem(n_max, G), stream>>>(pa);
-            gemm(t.o, H, QD, att, QD, B, nullptr, TC_ACT_F16, TC_EPI_RESID, x, H, x);
-            gemm(t.gu, 2 * FF, H, x, H, B, l.ffn_norm, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, FF, nullptr);
-            gemm(t.down, H, FF, hbuf, FF, B, nullptr, TC_ACT_SPLIT, TC_EPI_RESID, x, H, x);
+            pe();
+            gemm_cls = BC_GEMM_O;
+            gemm(t.o, H, QD, nullptr, QD, B, nullptr, TC_ACT_F16, TC_EPI_RESID, x, H, x);
+            gemm_cls = BC_GEMM_GU;
+            gemm(t.gu, 2 * FF, H, x, H, B, l.ffn_norm, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, FF, nullptr, nullptr, true);
+            gemm_cls = BC_GEMM_DOWN;
+            gemm(t.down, H, FF, nullptr, FF, B, nullptr, TC_ACT_SPLIT, TC_EPI_RESID, x, H, x);
             launches += 1;
         }
     }
@@ -192,26 +242,35 @@ struct BatchEngine {
     void enqueue_frame() {
         const int NG = NCB - 1;
         launches = 0;
+        pb(BC_SAMPLE);
         k_sample_batch<<<B, SAMPLE_THREADS, 0, stream>>>(logits, V0, V0, 0, st, sp, codes, max_frames);
+        pe();
         BatchInputArgs ia{};
         ia.H = H; ia.n_cb = NCB; ia.codec_embd = E->codec_embd; ia.cp_embd = E->d_cp_embd; ia.hidden = hidden;
         ia.trailing = trail; ia.trail_cap = trail_cap; ia.pad = pad; ia.st = st;
         ia.mode = IN_CP_PREFILL; ia.out = xcp;
         k_inputs_batch<<<B, 256, 0, stream>>>(ia);
         cp_layers(2, true, 0);
+        gemm_cls = BC_GEMM_HEAD;
         gemm(cp_head_t[0], V1, H, xcp + H, 2 * H, B, E->cp_out_norm, TC_ACT_F16, TC_EPI_STORE, cp_logits, V1, nullptr);
+        pb(BC_SAMPLE);
         k_sample_batch<<<B, SAMPLE_THREADS, 0, stream>>>(cp_logits, V1, V1, 1, st, sp, codes, max_frames);
+        pe();
         for (int gs = 1; gs < NG; ++gs) {
             ia.mode = IN_CP_STEP; ia.g = gs;
             k_inputs_batch<<<B, 256, 0, stream>>>(ia);
             cp_layers(1, false, gs + 1);
+            gemm_cls = BC_GEMM_HEAD;
             gemm(cp_head_t[gs], V1, H, xcp, H, B, E->cp_out_norm, TC_ACT_F16, TC_EPI_STORE, cp_logits, V1, nullptr);
+            pb(BC_SAMPLE);
             k_sample_batch<<<B, SAMPLE_THREADS, 0, stream>>>(cp_logits, V1, V1, gs + 1, st, sp, codes, max_frames);
+            pe();
             launches += 2;
         }
         ia.mode = IN_TALKER; ia.out = x;
         k_inputs_batch<<<B, 256, 0, stream>>>(ia);
         talker_layers();
+        gemm_cls = BC_GEMM_HEAD;
         gemm(codec_head_t, V0, H, x, H, B, E->out_norm, TC_ACT_F16, TC_EPI_STORE, logits, V0, nullptr, hidden);
         k_frame_end_batch<<<(B + 127) / 128, 128, 0, stream>>>(st, B);
         launches += 5;
@@ -297,6 +356,32 @@ struct BatchEngine {
         }
         seq_frames += adv;
         return adv;
+    }
+
+    // Runs n frames eagerly with events around every launch; ms_out[BC_N] and
+    // launches_out[BC_N] per frame.
+    bool profile(int n, float * ms_out, int * launches_out) {
+        if (B <= 0) { err = "no active batch"; return false; }
+        prof = true;
+        prof_ev.clear();
+        for (int i = 0; i < n; ++i) enqueue_frame();
+        prof = false;
+        if (cudaStreamSynchronize(stream) != cudaSuccess) { err = "profile frame"; return false; }
+        for (int c = 0; c < BC_N; ++c) { ms_out[c] = 0.0f; launches_out[c] = 0; }
+        for (auto & e : prof_ev) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, e.second.first, e.second.second);
+            ms_out[e.first] += ms / n;
+            launches_out[e.first] += 1;
+            cudaEventDestroy(e.second.first);
+            cudaEventDestroy(e.second.second);
+        }
+        for (int c = 0; c < BC_N; ++c) launches_out[c] /= n;
+        prof_ev.clear();
+        std::vector<DevState> hs(B);
+        cudaMemcpy(hs.data(), st, sizeof(DevState) * B, cudaMemcpyDeviceToHost);
+        for (int b = 0; b < B; ++b) produced[b] = hs[b].n_out;
+        return true;
     }
 
     bool read_codes(int32_t * out, int32_t * nf) {

@@ -119,6 +119,27 @@ __device__ __forceinline__ float key2f(uint32_t k) {
     return __uint_as_float(u);
 }
 
+constexpr int TC_BM = 128;          // tcgen05 GEMM: weight rows per tile (MMA M)
+constexpr int TC_BK = 64;           // k per tile (four K=16 MMAs)
+
+// Byte offset of element (row r, column k) inside a tile of `rows` x 64.
+__host__ __device__ inline size_t tc_tile_off(int r, int k) {
+    return (size_t)(r >> 3) * 1024 + (size_t)((k & 63) >> 3) * 128 + (size_t)(r & 7) * 16 + (size_t)(k & 7) * 2;
+}
+
+// Tiled activation rows: k-tile tk of X[np][cols] at tk * np * 128 bytes.
+__host__ __device__ inline size_t tc_x_off(int m, int k, int np) {
+    return (size_t)(k / TC_BK) * np * 128 + tc_tile_off(m, k);
+}
+
+// One F32 activation as F16 hi + lo in the tiled layout (rows m and np/2 + m).
+__device__ __forceinline__ void tc_store_split(uint8_t * xt, int m, int k, int np, float v) {
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+    *reinterpret_cast<__half *>(xt + tc_x_off(m, k, np)) = hi;
+    *reinterpret_cast<__half *>(xt + tc_x_off(np / 2 + m, k, np)) = lo;
+}
+
 constexpr unsigned long long QTTS_SPIN_LIMIT = 1ull << 22;   // polls before a bounded wait gives up
 
 // ---- shared-memory weight slices (TMA bulk copies completed on an mbarrier)

@@ -1392,9 +1392,11 @@ int32_t qtts_op_gemm_tc(int32_t device, const uint16_t * w, const uint16_t * w_u
         g.w = (const uint8_t *) dwt; g.x = (const uint8_t *) dxt; g.rows_w = rows_w; g.cols = cols; g.np = np;
         g.m_real = m; g.split = act == TC_ACT_SPLIT; g.epi = epi; g.y = (float *) dy; g.ldy = ycols;
         g.resid = (const float *) dy; g.ldr = ycols; g.err = (int *) derr;
+        g.ksplit = tc_choose_split(rows_w / TC_BM, cols / TC_BK);
         const size_t sm = tc_smem_bytes(np);
         chk(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm));
-        if (ok) k_gemm_tc<<<rows_w / TC_BM, TC_THREADS, sm>>>(g);
+        chk(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        if (ok) chk(tc_launch(g, sm, 0));
         chk(cudaGetLastError());
         chk(cudaDeviceSynchronize());
         int herr = 0;
@@ -1959,6 +1961,12 @@ int32_t qtts_batch_timing(const qtts_batch * b, float * frames_ms, int32_t * seq
     if (seq_frames) *seq_frames = b->be.seq_frames;
     if (launches_per_frame) *launches_per_frame = b->be.launches;
     return 1;
+}
+
+int32_t qtts_batch_profile(qtts_batch * b, int32_t n_frames, float * ms_per_frame, int32_t * launches_per_frame) {
+    if (!b || n_frames <= 0 || !ms_per_frame || !launches_per_frame) return 0;
+    cudaSetDevice(b->be.dev);
+    return b->be.profile(n_frames, ms_per_frame, launches_per_frame) ? 1 : 0;
 }
 
 const char * qtts_batch_error(const qtts_batch * b) { return b ? b->be.err.c_str() : "null batch"; }

@@ -23,25 +23,13 @@
 
 namespace qtts {
 
-constexpr int TC_BM = 128;          // weight rows per tile (MMA M)
-constexpr int TC_BK = 64;           // k per tile (four K=16 MMAs)
 constexpr int TC_STAGES = 4;
 constexpr int TC_THREADS = 128;
 constexpr int TC_MAX_N = 256;       // activation rows (MMA N) per launch
 
-// Byte offset of element (row r, column k) inside a tile of `rows` x 64.
-__host__ __device__ inline size_t tc_tile_off(int r, int k) {
-    return (size_t)(r >> 3) * 1024 + (size_t)((k & 63) >> 3) * 128 + (size_t)(r & 7) * 16 + (size_t)(k & 7) * 2;
-}
-
 // Tiled weight matrix: tile (tn, tk) of W[rows][cols] at ((tn * (cols/64)) + tk) * 16 KB.
 __host__ __device__ inline size_t tc_w_off(int r, int k, int cols) {
     return ((size_t)(r / TC_BM) * (cols / TC_BK) + (size_t)(k / TC_BK)) * (TC_BM * TC_BK * 2) + tc_tile_off(r % TC_BM, k);
-}
-
-// Tiled activation rows: k-tile tk of X[np][cols] at tk * np * 128 bytes.
-__host__ __device__ inline size_t tc_x_off(int m, int k, int np) {
-    return (size_t)(k / TC_BK) * np * 128 + tc_tile_off(m, k);
 }
 
 // Repack row-major F16 W[rows][cols] into tiles (rows % 128 == 0, cols % 64 == 0).
@@ -136,6 +124,9 @@ struct GemmTcArgs {
     const float * resid;      // EPI_RESID (may alias y)
     int ldr;
     int * err;                // set on a wait timeout
+    uint8_t * xt_out;         // SwiGLU: also write h as F16 hi/lo tiles (rows m, xt_np/2 + m) for the down GEMM
+    int xt_np;
+    int ksplit;               // CTAs per weight tile along k (a cluster of that size; 1 = no split)
 };
 
 __device__ __forceinline__ uint64_t tc_smem_desc(uint32_t saddr) {
@@ -175,7 +166,23 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
 __host__ __device__ inline size_t tc_stage_bytes(int np) { return (size_t) TC_BM * TC_BK * 2 + (size_t) np * 128; }
 __host__ __device__ inline size_t tc_smem_bytes(int np) { return TC_STAGES * tc_stage_bytes(np) + 1024; }
 
-// One CTA per 128-row weight tile, full K.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(const float * local, uint32_t rank) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(ra)
+                 : "memory");
+    return v;
+}
+
+// One CTA per (128-row weight tile, k slice).  With ksplit S > 1 the S CTAs
+// of a tile form a thread-block cluster: each accumulates its k slice in TMEM,
+// parks the partial tile in its shared memory, and after a cluster barrier CTA
+// r reduces rows [r*128/S, (r+1)*128/S) over the S partials in rank order
+// (distributed shared memory reads; deterministic) and runs the epilogue.
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     extern __shared__ __align__(128) uint8_t tc_smem[];
     __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], done;
@@ -183,8 +190,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     __shared__ int s_fail;
     __shared__ float s_swg[TC_BM / 2][33];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tn = blockIdx.x;
-    const int nk = g.cols / TC_BK;
+    const int S = g.ksplit > 1 ? g.ksplit : 1;
+    const int tn = blockIdx.x / S, rank = blockIdx.x % S;
+    const int nk_all = g.cols / TC_BK;
+    const int k0 = rank * nk_all / S, nk = (rank + 1) * nk_all / S - k0;
     const size_t wtile = (size_t) TC_BM * TC_BK * 2, xtile = (size_t) g.np * 128;
     const size_t sbytes = wtile + xtile;
     int ncols = 32;
@@ -209,14 +218,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     int issued = 0;
     if (tid == 0) {
         // producer: W tile (tn, k) and X k-tile into stage k % STAGES
-        const uint8_t * wsrc = g.w + (size_t) tn * nk * wtile;
+        const uint8_t * wsrc = g.w + ((size_t) tn * nk_all + k0) * wtile;
+        const uint8_t * xsrc = g.x + (size_t) k0 * xtile;
         for (int i = 0; i < nk; ++i) {
             const int s = i % TC_STAGES;
             if (i >= TC_STAGES && !mbar_wait(&empty[s], ((i / TC_STAGES) - 1) & 1)) { s_fail = 1; break; }
             uint8_t * dst = tc_smem + s * sbytes;
             mbar_expect_tx(&full[s], (unsigned) sbytes);
             bulk_g2s(dst, wsrc + (size_t) i * wtile, (unsigned) wtile, &full[s]);
-            bulk_g2s(dst + wtile, g.x + (size_t) i * xtile, (unsigned) xtile, &full[s]);
+            bulk_g2s(dst + wtile, xsrc + (size_t) i * xtile, (unsigned) xtile, &full[s]);
             issued = i + 1;
         }
     } else if (tid == 32) {
@@ -240,9 +250,77 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     if (tid == 0) ok = mbar_wait(&done, 0);
     const int bad = __syncthreads_or(!ok || s_fail);
     tc_fence_after();
-    if (bad) {
-        if (tid == 0) atomicExch(g.err, 1);
-    } else {
+    if (bad && tid == 0) atomicExch(g.err, 1);
+    if (S > 1) {
+        // every CTA of the cluster reaches both cluster barriers (a failed one skips the work only)
+        const int mcols = g.split ? g.np / 2 : g.np;
+        const int pc = g.m_real < mcols ? g.m_real : mcols;     // partial columns kept
+        const int pc4 = (pc + 3) & ~3;                               // partial row stride (float4 aligned)
+        float * P = reinterpret_cast<float *>(tc_smem);          // [128][pc4], over the drained stage ring
+        if (!bad) {
+            const int r_tile = warp * 32 + lane;
+            const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+            for (int c0 = 0; c0 < pc; c0 += 16) {
+                float v[16];
+                tc_ld16(trow + (uint32_t) c0, v);
+                if (g.split) {
+                    float w2[16];
+                    tc_ld16(trow + (uint32_t)(g.np / 2 + c0), w2);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], w2[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (c0 + j < pc4) P[r_tile * pc4 + c0 + j] = v[j];
+            }
+        }
+        cluster_sync_all();
+        if (!bad) {
+            // CTA `rank` reduces rows [rank*rs, (rank+1)*rs); a thread owns 4 consecutive
+            // columns of one row and issues the S remote float4 loads before adding
+            const bool swg = g.epi == TC_EPI_SWIGLU;
+            const int rs = (swg ? TC_BM / 2 : TC_BM) / S;
+            const int nq = pc4 / 4;
+            for (int idx = tid; idx < rs * nq; idx += TC_THREADS) {
+                const int rl = idx % rs, m0 = (idx / rs) * 4;
+                const int rt = rank * rs + rl;
+                float4 part[8], upp[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (q < S) {
+                        part[q] = ld_cluster_f32x4(P + rt * pc4 + m0, (uint32_t) q);
+                        if (swg) upp[q] = ld_cluster_f32x4(P + (rt + TC_BM / 2) * pc4 + m0, (uint32_t) q);
+                    }
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, up[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (q < S) {
+                        acc[0] = __fadd_rn(acc[0], part[q].x); acc[1] = __fadd_rn(acc[1], part[q].y);
+                        acc[2] = __fadd_rn(acc[2], part[q].z); acc[3] = __fadd_rn(acc[3], part[q].w);
+                        if (swg) {
+                            up[0] = __fadd_rn(up[0], upp[q].x); up[1] = __fadd_rn(up[1], upp[q].y);
+                            up[2] = __fadd_rn(up[2], upp[q].z); up[3] = __fadd_rn(up[3], upp[q].w);
+                        }
+                    }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int m = m0 + j;
+                    if (m >= pc) break;
+                    if (swg) {
+                        const float h = __fmul_rn(silu(acc[j]), up[j]);
+                        g.y[(size_t) m * g.ldy + tn * (TC_BM / 2) + rt] = h;
+                        if (g.xt_out) tc_store_split(g.xt_out, m, tn * (TC_BM / 2) + rt, g.xt_np, h);
+                    } else {
+                        const int row = tn * TC_BM + rt;
+                        float o = acc[j];
+                        if (g.epi == TC_EPI_RESID) o = __fadd_rn(o, g.resid[(size_t) m * g.ldr + row]);
+                        g.y[(size_t) m * g.ldy + row] = o;
+                    }
+                }
+            }
+        }
+        cluster_sync_all();   // no CTA leaves while a peer may still read its partial
+    } else if (!bad) {
         const int r_tile = warp * 32 + lane;                    // TMEM lane = weight row in the tile
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
         const int mcols = g.split ? g.np / 2 : g.np;
@@ -268,6 +346,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
                         if (m >= g.m_real) break;
                         const float h = __fmul_rn(silu(v[j]), s_swg[r_tile][j]);
                         g.y[(size_t) m * g.ldy + col] = h;
+                        if (g.xt_out) tc_store_split(g.xt_out, m, col, g.xt_np, h);
                     }
                 }
                 __syncthreads();
@@ -290,6 +369,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     tc_fence_before();
     __syncthreads();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+}
+
+// k-split for a GEMM of `tiles` weight tiles and nk 64-k tiles: the smallest
+// power of two giving >= 64 CTAs, at most 8 (the portable cluster size) and at
+// most nk.
+inline int tc_choose_split(int tiles, int nk) {
+    int S = 1;
+    while (tiles * S < 64 && S < 8 && S * 2 <= nk) S *= 2;
+    return S;
+}
+
+// Launch k_gemm_tc with g.ksplit CTAs per weight tile as a cluster.
+inline cudaError_t tc_launch(const GemmTcArgs & g, size_t smem, cudaStream_t stream) {
+    const int S = g.ksplit > 1 ? g.ksplit : 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)((g.rows_w / TC_BM) * S));
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned) S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_gemm_tc, g);
 }
 
 }  // namespace qtts

@@ -601,6 +601,8 @@ struct FusedAttn {
     float * dump;             // post-softmax rows [frame][n_heads][dump_stride] or nullptr
     int dump_stride;
     const int * done;         // stand-alone launch: skip when *done
+    uint8_t * xt;             // optional: output also as F16 tiles for the O-projection GEMM (row xt_row0 + i)
+    int xt_np, xt_row0;
 };
 
 constexpr int FA_THREADS = 512;
@@ -787,6 +789,8 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
 #pragma unroll
         for (int q = 0; q < FA_NPG; ++q) s = __fadd_rn(s, part[q * QTTS_HD + tid]);
         a.out[(size_t) i * a.ldo + (size_t) hq * QTTS_HD + tid] = s;
+        if (a.xt)
+            *reinterpret_cast<__half *>(a.xt + tc_x_off(a.xt_row0 + i, hq * QTTS_HD + tid, a.xt_np)) = __float2half_rn(s);
     }
 }
 

@@ -117,6 +117,7 @@ def lib():
         "qtts_batch_timing": (C.c_int32, [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int32),
                                           C.POINTER(C.c_int32)]),
         "qtts_batch_error": (C.c_char_p, [C.c_void_p]),
+        "qtts_batch_profile": (C.c_int32, [C.c_void_p, C.c_int32, _f32p, _i32p]),
         "qtts_batch_free": (None, [C.c_void_p]),
         "qtts_op_gemm_tc": (C.c_int32, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32,
                                         _f32p, C.c_float, C.c_int32, C.c_int32, _f32p, _f32p]),
@@ -401,6 +402,17 @@ class Batch:
         if not lib().qtts_batch_codes(self.h, _p(c, C.c_int32), _p(nf, C.c_int32)):
             raise RuntimeError("batch codes failed: " + self.error())
         return [c[i, :nf[i]].copy() for i in range(self.n)]
+
+    BATCH_CLASSES = ["pack", "gemm_qkv", "gemm_o", "gemm_gu", "gemm_down", "gemm_head", "attn_cp", "attn_talker",
+                     "sample", "other"]
+
+    def profile(self, n_frames: int) -> dict:
+        ms = np.zeros(10, np.float32)
+        la = np.zeros(10, np.int32)
+        if not lib().qtts_batch_profile(self.h, n_frames, _p(ms, C.c_float), _p(la, C.c_int32)):
+            raise RuntimeError("batch profile failed: " + self.error())
+        return {c: {"ms_per_frame": float(ms[i]), "launches_per_frame": int(la[i])}
+                for i, c in enumerate(self.BATCH_CLASSES)}
 
     def timing(self) -> dict:
         ms, fr, la = C.c_float(0), C.c_int32(0), C.c_int32(0)
