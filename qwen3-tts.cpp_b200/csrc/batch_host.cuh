@@ -143,7 +143,7 @@ struct BatchEngine {
         if (cudaMemcpy(rope_t, rt.data(), sizeof(float2) * rt.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
             err = "rope"; return false;
         }
-        const size_t tcs = tc_smem_bytes(TC_MAX_N);
+        const size_t tcs = 201 * 1024;
         if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) tcs) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
             cudaFuncSetAttribute(k_attn_paged, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -178,9 +178,9 @@ struct BatchEngine {
         g.w = wt; g.x = xsrc; g.rows_w = rows_w; g.cols = cols; g.np = np; g.m_real = m;
         g.split = act == TC_ACT_SPLIT; g.epi = epi; g.y = y; g.ldy = ldy; g.resid = resid; g.ldr = ldy; g.err = d_err;
         if (xt_next) { g.xt_out = xt2; g.xt_np = 2 * mp; }
-        g.ksplit = tc_choose_split(rows_w / TC_BM, cols / TC_BK);
+        g.ksplit = tc_choose_split(g);
         pb(gemm_cls);
-        tc_launch(g, tc_smem_bytes(np), stream);
+        tc_launch(g, stream);
         pe();
         launches += 1;
     }

@@ -1392,11 +1392,10 @@ int32_t qtts_op_gemm_tc(int32_t device, const uint16_t * w, const uint16_t * w_u
         g.w = (const uint8_t *) dwt; g.x = (const uint8_t *) dxt; g.rows_w = rows_w; g.cols = cols; g.np = np;
         g.m_real = m; g.split = act == TC_ACT_SPLIT; g.epi = epi; g.y = (float *) dy; g.ldy = ycols;
         g.resid = (const float *) dy; g.ldr = ycols; g.err = (int *) derr;
-        g.ksplit = tc_choose_split(rows_w / TC_BM, cols / TC_BK);
-        const size_t sm = tc_smem_bytes(np);
-        chk(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm));
+        g.ksplit = tc_choose_split(g);
+        chk(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024));
         chk(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        if (ok) chk(tc_launch(g, sm, 0));
+        if (ok) chk(tc_launch(g, 0));
         chk(cudaGetLastError());
         chk(cudaDeviceSynchronize());
         int herr = 0;

@@ -23,7 +23,7 @@
 
 namespace qtts {
 
-constexpr int TC_STAGES = 4;
+constexpr int TC_MAX_STAGES = 8;   // shared-memory ring depth (as many as fit in ~200 KB)
 constexpr int TC_THREADS = 128;
 constexpr int TC_MAX_N = 256;       // activation rows (MMA N) per launch
 
@@ -151,6 +151,14 @@ __device__ __forceinline__ void tc_commit(uint64_t * m) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
+__device__ __forceinline__ void tc_ld16_nowait(uint32_t taddr, float * v) {
+    uint32_t * r = reinterpret_cast<uint32_t *>(v);
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                   "=r"(r[15])
+                 : "r"(taddr));
+}
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
     uint32_t r[16];
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -164,28 +172,36 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
 }
 
 __host__ __device__ inline size_t tc_stage_bytes(int np) { return (size_t) TC_BM * TC_BK * 2 + (size_t) np * 128; }
-__host__ __device__ inline size_t tc_smem_bytes(int np) { return TC_STAGES * tc_stage_bytes(np) + 1024; }
+// Split-K partial slots [128][ps] (F32) placed after the ring: ps = columns
+// kept (m_real, at most the MMA columns of one half for hi/lo inputs) rounded to
+// 4, plus 4 so that 16-byte lanes at a row stride hit distinct banks.
+__host__ __device__ inline size_t tc_partial_bytes(int np, int split, int m_real, int ksplit) {
+    if (ksplit <= 1) return 0;
+    const int mcols = split ? np / 2 : np;
+    const int pc = m_real < mcols ? m_real : mcols;
+    return (size_t) TC_BM * (((pc + 3) & ~3) + 4) * 4;
+}
+__host__ __device__ inline int tc_stages(int np, size_t pbytes) {
+    const int n = (int)((200 * 1024 - pbytes) / tc_stage_bytes(np));
+    return n > TC_MAX_STAGES ? TC_MAX_STAGES : (n < 2 ? 2 : n);
+}
+__host__ __device__ inline size_t tc_smem_bytes(int np, size_t pbytes = 0) {
+    return tc_stages(np, pbytes) * tc_stage_bytes(np) + pbytes + 1024;
+}
 
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float4 ld_cluster_f32x4(const float * local, uint32_t rank) {
-    uint32_t ra;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(ra)
-                 : "memory");
-    return v;
-}
 
 // One CTA per (128-row weight tile, k slice).  With ksplit S > 1 the S CTAs
-// of a tile form a thread-block cluster: each accumulates its k slice in TMEM,
-// parks the partial tile in its shared memory, and after a cluster barrier CTA
-// r reduces rows [r*128/S, (r+1)*128/S) over the S partials in rank order
-// (distributed shared memory reads; deterministic) and runs the epilogue.
+// of a tile form a thread-block cluster: each accumulates its k slice in TMEM
+// and pushes each partial row into the shared memory of the CTA that owns the
+// row (distributed shared memory stores); after a cluster barrier CTA r sums
+// its rows [r*128/S, (r+1)*128/S) over the S slots in rank order
+// (deterministic) and runs the epilogue.
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     extern __shared__ __align__(128) uint8_t tc_smem[];
-    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], done;
+    __shared__ __align__(8) uint64_t full[TC_MAX_STAGES], empty[TC_MAX_STAGES], done;
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
     __shared__ float s_swg[TC_BM / 2][33];
@@ -196,33 +212,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     const int k0 = rank * nk_all / S, nk = (rank + 1) * nk_all / S - k0;
     const size_t wtile = (size_t) TC_BM * TC_BK * 2, xtile = (size_t) g.np * 128;
     const size_t sbytes = wtile + xtile;
+    const size_t pbytes = tc_partial_bytes(g.np, g.split, g.m_real, g.ksplit);
+    const int NST = tc_stages(g.np, pbytes);
     int ncols = 32;
     while (ncols < g.np) ncols <<= 1;
 
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(ncols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
-    }
-    if (tid == 32) {
-        for (int s = 0; s < TC_STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    // thread 0: barriers, then the first NST copies at once (they overlap the TMEM allocation)
+    int issued = 0;
+    const uint8_t * wsrc = g.w + ((size_t) tn * nk_all + k0) * wtile;
+    const uint8_t * xsrc = g.x + (size_t) k0 * xtile;
+    if (tid == 0) {
+        for (int s = 0; s < NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(&done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_fail = 0;
+        for (int i = 0; i < nk && i < NST; ++i) {
+            uint8_t * dst = tc_smem + i * sbytes;
+            mbar_expect_tx(&full[i], (unsigned) sbytes);
+            bulk_g2s(dst, wsrc + (size_t) i * wtile, (unsigned) wtile, &full[i]);
+            bulk_g2s(dst + wtile, xsrc + (size_t) i * xtile, (unsigned) xtile, &full[i]);
+            issued = i + 1;
+        }
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    int issued = 0;
     if (tid == 0) {
-        // producer: W tile (tn, k) and X k-tile into stage k % STAGES
-        const uint8_t * wsrc = g.w + ((size_t) tn * nk_all + k0) * wtile;
-        const uint8_t * xsrc = g.x + (size_t) k0 * xtile;
-        for (int i = 0; i < nk; ++i) {
-            const int s = i % TC_STAGES;
-            if (i >= TC_STAGES && !mbar_wait(&empty[s], ((i / TC_STAGES) - 1) & 1)) { s_fail = 1; break; }
+        // producer: W tile (tn, k) and X k-tile into stage k % NST
+        for (int i = issued; i < nk; ++i) {
+            const int s = i % NST;
+            if (!mbar_wait(&empty[s], ((i / NST) - 1) & 1)) { s_fail = 1; break; }
             uint8_t * dst = tc_smem + s * sbytes;
             mbar_expect_tx(&full[s], (unsigned) sbytes);
             bulk_g2s(dst, wsrc + (size_t) i * wtile, (unsigned) wtile, &full[s]);
@@ -234,8 +260,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
         const uint32_t idesc = tc_idesc(g.np);
         int i = 0;
         for (; i < nk; ++i) {
-            const int s = i % TC_STAGES;
-            if (!mbar_wait(&full[s], (i / TC_STAGES) & 1)) { s_fail = 1; break; }
+            const int s = i % NST;
+            if (!mbar_wait(&full[s], (i / NST) & 1)) { s_fail = 1; break; }
             tc_fence_after();
             const uint32_t a0 = smem_u32(tc_smem + s * sbytes), b0 = a0 + (uint32_t) wtile;
 #pragma unroll
@@ -252,56 +278,70 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     tc_fence_after();
     if (bad && tid == 0) atomicExch(g.err, 1);
     if (S > 1) {
-        // every CTA of the cluster reaches both cluster barriers (a failed one skips the work only)
+        // Every CTA of the cluster reaches both cluster barriers (a failed one skips
+        // the work only).  Push: the thread holding TMEM row r stores its partial
+        // into slot [my rank] of the row's owner (CTA r / rs) with remote 16-byte
+        // stores; after the barrier each owner sums its S slots in rank order.
+        const bool swg = g.epi == TC_EPI_SWIGLU;
         const int mcols = g.split ? g.np / 2 : g.np;
         const int pc = g.m_real < mcols ? g.m_real : mcols;     // partial columns kept
-        const int pc4 = (pc + 3) & ~3;                               // partial row stride (float4 aligned)
-        float * P = reinterpret_cast<float *>(tc_smem);          // [128][pc4], over the drained stage ring
+        const int pc4 = (pc + 3) & ~3;
+        const int ps = pc4 + 4;                                      // row stride: 16-byte lanes hit distinct banks
+        const int rs = (swg ? TC_BM / 2 : TC_BM) / S;                // rows (gate rows for SwiGLU) owned per CTA
+        const int orows = swg ? 2 * rs : rs;                         // rows held per slot (gate + up for SwiGLU)
+        float * P = reinterpret_cast<float *>(tc_smem + NST * sbytes);   // [S][orows][ps], after the ring
         if (!bad) {
             const int r_tile = warp * 32 + lane;
+            const int gr = swg ? (r_tile & (TC_BM / 2 - 1)) : r_tile;  // gate-row index for SwiGLU
+            const int owner = gr / rs;
+            const int orow = (gr % rs) + (swg && r_tile >= TC_BM / 2 ? rs : 0);
+            const uint32_t dst = smem_u32(P + ((size_t) rank * orows + orow) * ps);
+            uint32_t rdst;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(dst), "r"((uint32_t) owner));
             const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-            for (int c0 = 0; c0 < pc; c0 += 16) {
-                float v[16];
-                tc_ld16(trow + (uint32_t) c0, v);
-                if (g.split) {
-                    float w2[16];
-                    tc_ld16(trow + (uint32_t)(g.np / 2 + c0), w2);
+            const int grp = g.split ? 32 : 64;                       // columns per TMEM wait
+            for (int c0 = 0; c0 < pc; c0 += grp) {
+                float v[64];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], w2[j]);
+                for (int q = 0; q < 4; ++q) {
+                    const int cc = g.split ? (q >> 1) * 16 + (q & 1) * (g.np / 2) : q * 16;
+                    const bool want = g.split ? (q < 2 || c0 + 16 < pc) : (c0 + q * 16 < pc);   // warp-uniform
+                    if (want) tc_ld16_nowait(trow + (uint32_t)(c0 + cc), v + 16 * q);
+                }
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (g.split) {   // v[0..15] + v[16..31] = hi + lo of columns c0..c0+15, v[32..] the next 16
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        v[j] = __fadd_rn(v[j], v[16 + j]);
+                        v[16 + j] = __fadd_rn(v[32 + j], v[48 + j]);
+                    }
                 }
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (c0 + j < pc4) P[r_tile * pc4 + c0 + j] = v[j];
+                for (int j = 0; j < 64; j += 4)
+                    if (j < grp && c0 + j < pc4)
+                        asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(rdst + (uint32_t)(c0 + j) * 4),
+                                     "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]), "f"(v[j + 3])
+                                     : "memory");
             }
         }
         cluster_sync_all();
         if (!bad) {
-            // CTA `rank` reduces rows [rank*rs, (rank+1)*rs); a thread owns 4 consecutive
-            // columns of one row and issues the S remote float4 loads before adding
-            const bool swg = g.epi == TC_EPI_SWIGLU;
-            const int rs = (swg ? TC_BM / 2 : TC_BM) / S;
+            // this CTA owns rows [rank*rs, (rank+1)*rs): a thread takes 4 consecutive columns of one row
             const int nq = pc4 / 4;
             for (int idx = tid; idx < rs * nq; idx += TC_THREADS) {
                 const int rl = idx % rs, m0 = (idx / rs) * 4;
                 const int rt = rank * rs + rl;
-                float4 part[8], upp[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    if (q < S) {
-                        part[q] = ld_cluster_f32x4(P + rt * pc4 + m0, (uint32_t) q);
-                        if (swg) upp[q] = ld_cluster_f32x4(P + (rt + TC_BM / 2) * pc4 + m0, (uint32_t) q);
-                    }
                 float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, up[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    if (q < S) {
-                        acc[0] = __fadd_rn(acc[0], part[q].x); acc[1] = __fadd_rn(acc[1], part[q].y);
-                        acc[2] = __fadd_rn(acc[2], part[q].z); acc[3] = __fadd_rn(acc[3], part[q].w);
-                        if (swg) {
-                            up[0] = __fadd_rn(up[0], upp[q].x); up[1] = __fadd_rn(up[1], upp[q].y);
-                            up[2] = __fadd_rn(up[2], upp[q].z); up[3] = __fadd_rn(up[3], upp[q].w);
-                        }
+                for (int q = 0; q < S; ++q) {
+                    const float4 a4 = *reinterpret_cast<const float4 *>(P + ((size_t) q * orows + rl) * ps + m0);
+                    acc[0] = __fadd_rn(acc[0], a4.x); acc[1] = __fadd_rn(acc[1], a4.y);
+                    acc[2] = __fadd_rn(acc[2], a4.z); acc[3] = __fadd_rn(acc[3], a4.w);
+                    if (swg) {
+                        const float4 u4 = *reinterpret_cast<const float4 *>(P + ((size_t) q * orows + rs + rl) * ps + m0);
+                        up[0] = __fadd_rn(up[0], u4.x); up[1] = __fadd_rn(up[1], u4.y);
+                        up[2] = __fadd_rn(up[2], u4.z); up[3] = __fadd_rn(up[3], u4.w);
                     }
+                }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int m = m0 + j;
@@ -319,7 +359,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
                 }
             }
         }
-        cluster_sync_all();   // no CTA leaves while a peer may still read its partial
+        // (no second cluster barrier: after the first one no CTA touches a peer's memory)
     } else if (!bad) {
         const int r_tile = warp * 32 + lane;                    // TMEM lane = weight row in the tile
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
@@ -364,25 +404,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     }
     // after a timeout: wait (bounded) for the copies still in flight, then free TMEM
     if (tid == 0 && bad)
-        for (int j = issued > TC_STAGES ? issued - TC_STAGES : 0; j < issued; ++j)
-            mbar_wait(&full[j % TC_STAGES], (j / TC_STAGES) & 1);
+        for (int j = issued > NST ? issued - NST : 0; j < issued; ++j)
+            mbar_wait(&full[j % NST], (j / NST) & 1);
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
 }
 
-// k-split for a GEMM of `tiles` weight tiles and nk 64-k tiles: the smallest
-// power of two giving >= 64 CTAs, at most 8 (the portable cluster size) and at
-// most nk.
-inline int tc_choose_split(int tiles, int nk) {
+// k-split of a GEMM: the smallest power of two giving >= 64 CTAs, at most 8
+// (the portable cluster size), at most the 64-k tiles, and only while the ring
+// plus the partial slots fit the 201 KB of dynamic shared memory.
+inline int tc_choose_split(const GemmTcArgs & g) {
+    const int tiles = g.rows_w / TC_BM, nk = g.cols / TC_BK;
     int S = 1;
-    while (tiles * S < 64 && S < 8 && S * 2 <= nk) S *= 2;
+    while (tiles * S < 64 && S < 8 && S * 2 <= nk &&
+           tc_smem_bytes(g.np, tc_partial_bytes(g.np, g.split, g.m_real, S * 2)) <= 201 * 1024)
+        S *= 2;
     return S;
 }
 
 // Launch k_gemm_tc with g.ksplit CTAs per weight tile as a cluster.
-inline cudaError_t tc_launch(const GemmTcArgs & g, size_t smem, cudaStream_t stream) {
+inline cudaError_t tc_launch(const GemmTcArgs & g, cudaStream_t stream) {
     const int S = g.ksplit > 1 ? g.ksplit : 1;
+    const size_t smem = tc_smem_bytes(g.np, tc_partial_bytes(g.np, g.split, g.m_real, g.ksplit));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)((g.rows_w / TC_BM) * S));
     cfg.blockDim = dim3(TC_THREADS);
