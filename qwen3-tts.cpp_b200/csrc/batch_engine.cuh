@@ -254,20 +254,129 @@ __global__ void __launch_bounds__(PA_THREADS, 1) k_attn_paged(PagedAttnArgs a) {
 }
 
 // ---- code-predictor attention for B sequences ------------------------------
-// Unit (b, u): the fused unit u of sequence b, whose qkv / att rows start at row
-// b * M and whose code-predictor cache is its own [ctx][NKV][128] slab.
-__global__ void __launch_bounds__(FA_THREADS) k_cp_attn_batch(FusedAttn a, size_t cache_stride, const DevState * st,
-                                                              int units) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    const int b = blockIdx.x / units, u = blockIdx.x % units;
+// Code-predictor attention with one warp per (sequence b, query head, row i)
+// unit: at most 17 keys, so lane j scores key j over all 128 dims (q broadcast
+// from shared memory), the softmax is a warp reduction (max, expf, double sum,
+// e * (float)(1/sum), F16-rounded in cache mode), and lane l accumulates dims
+// 4l..4l+3 of P x V.  Arithmetic as the fused unit (per-head q/k RMSNorm,
+// NEOX RoPE, F16 q / K / V / p in cache mode, F32 K / V of this call in the
+// 2-token prefill); the warp of the first query head of a kv group appends the
+// group's new K/V row to the sequence's cache.
+constexpr int CPW_WARPS = 16;
+
+__global__ void __launch_bounds__(CPW_WARPS * 32) k_cp_attn_warp(FusedAttn a, size_t cache_stride, const DevState * st,
+                                                                 int B) {
+    __shared__ float sq[CPW_WARPS][QTTS_HD];
+    __shared__ float sk[CPW_WARPS][2][QTTS_HD];
+    __shared__ float sv[CPW_WARPS][2][QTTS_HD];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NH = a.n_heads, NKV = a.n_kv_heads, G = NH / NKV, M = a.M;
+    const int unit = blockIdx.x * CPW_WARPS + warp;
+    if (unit >= B * NH * M) return;
+    const int b = unit / (NH * M), r = unit % (NH * M), i = r / NH, hq = r % NH, g = hq / G;
     if (st[b].done) return;
-    FusedAttn s = a;
-    s.qkv += (size_t) b * a.M * a.ldq;
-    s.kc += (size_t) b * cache_stride;
-    s.vc += (size_t) b * cache_stride;
-    s.out += (size_t) b * a.M * a.ldo;
-    s.xt_row0 = b * a.M;
-    fused_attn_body(s, u, smem_raw, a.pos_static, 0);
+    const bool f32 = a.f32_mode != 0;
+    const int n_past = a.pos_static, pos = n_past + i;
+    const int n = f32 ? i + 1 : n_past + 1, nc = f32 ? 0 : n_past;
+    const int QD = NH * QTTS_HD, KD = NKV * QTTS_HD;
+    const size_t pstride = (size_t) NKV * QTTS_HD;
+    const float * qkv = a.qkv + (size_t) b * M * a.ldq;
+    __half * kc = a.kc + (size_t) b * cache_stride;
+    __half * vc = a.vc + (size_t) b * cache_stride;
+
+    // q head of row i
+    {
+        const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
+        const float4 q4 = *reinterpret_cast<const float4 *>(qkv + (size_t) i * a.ldq + (size_t) hq * QTTS_HD + lane * 4);
+        float gv[4];
+        float2 cs[4];
+        head_params(a.q_norm, rp, lane, gv, cs);
+        float x[4] = {q4.x, q4.y, q4.z, q4.w};
+        head_norm_rope_v(x, gv, cs, a.eps, lane);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) sq[warp][lane * 4 + k] = f32 ? x[k] : round_f16(x[k]);
+    }
+    // k/v rows computed here: rows 0..i of this call (prefill) or the current row
+    const int nrow = f32 ? i + 1 : 1;
+    for (int rr = 0; rr < nrow; ++rr) {
+        const int j = f32 ? rr : i;
+        const float2 * rp = a.rope + (size_t)(n_past + j) * (QTTS_HD / 2);
+        const float4 k4 = *reinterpret_cast<const float4 *>(qkv + (size_t) j * a.ldq + QD + g * QTTS_HD + lane * 4);
+        const float4 v4 = *reinterpret_cast<const float4 *>(qkv + (size_t) j * a.ldq + QD + KD + g * QTTS_HD + lane * 4);
+        float gv[4];
+        float2 cs[4];
+        head_params(a.k_norm, rp, lane, gv, cs);
+        float x[4] = {k4.x, k4.y, k4.z, k4.w};
+        const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+        head_norm_rope_v(x, gv, cs, a.eps, lane);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __half kh = __float2half_rn(x[k]), vh = __float2half_rn(v[k]);
+            sk[warp][rr][lane * 4 + k] = f32 ? x[k] : __half2float(kh);
+            sv[warp][rr][lane * 4 + k] = f32 ? v[k] : __half2float(vh);
+            if (j == i && hq % G == 0) {
+                kc[(size_t)(n_past + j) * pstride + g * QTTS_HD + lane * 4 + k] = kh;
+                vc[(size_t)(n_past + j) * pstride + g * QTTS_HD + lane * 4 + k] = vh;
+            }
+        }
+    }
+    __syncwarp();
+    // scores: lane j <-> key j
+    float sj = -INFINITY;
+    if (lane < n) {
+        float acc = 0.0f;
+        if (lane < nc) {
+            const uint4 * kp = reinterpret_cast<const uint4 *>(kc + (size_t) lane * pstride + g * QTTS_HD);
+#pragma unroll 4
+            for (int c = 0; c < QTTS_HD / 8; ++c) {
+                const uint4 u = kp[c];
+                const __half2 * hp = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float2 f = __half22float2(hp[k]);
+                    acc = fmaf(f.x, sq[warp][c * 8 + 2 * k], acc);
+                    acc = fmaf(f.y, sq[warp][c * 8 + 2 * k + 1], acc);
+                }
+            }
+        } else {
+            const float * kr = sk[warp][f32 ? lane : 0];
+            for (int d = 0; d < QTTS_HD; ++d) acc = fmaf(kr[d], sq[warp][d], acc);
+        }
+        sj = __fmul_rn(acc, a.scale);
+    }
+    const float mx = warp_max(sj);
+    const float e = lane < n ? expf(__fsub_rn(sj, mx)) : 0.0f;
+    const double sum = warp_sum_d(lane < n ? (double) e : 0.0);
+    const float inv = (float)(1.0 / sum);
+    float p = __fmul_rn(e, inv);
+    if (!f32) p = round_f16(p);
+    // P x V: lane owns dims 4 lane .. 4 lane + 3
+    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = 0; j < n; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        float v[4];
+        if (j < nc) {
+            const uint2 u = *reinterpret_cast<const uint2 *>(vc + (size_t) j * pstride + g * QTTS_HD + lane * 4);
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+            v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+        } else {
+            const float * vr = sv[warp][f32 ? j : 0];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = vr[lane * 4 + k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = fmaf(pj, v[k], o[k]);
+    }
+    const int row = b * M + i;
+    *reinterpret_cast<float4 *>(a.out + (size_t) row * a.ldo + (size_t) hq * QTTS_HD + lane * 4) =
+        make_float4(o[0], o[1], o[2], o[3]);
+    if (a.xt) {
+        __align__(8) __half h4[4] = {__float2half_rn(o[0]), __float2half_rn(o[1]), __float2half_rn(o[2]),
+                                      __float2half_rn(o[3])};
+        *reinterpret_cast<uint2 *>(a.xt + tc_x_off(row, hq * QTTS_HD + lane * 4, a.xt_np)) =
+            *reinterpret_cast<const uint2 *>(h4);
+    }
 }
 
 // ---- per-sequence samplers, inputs and frame end ---------------------------

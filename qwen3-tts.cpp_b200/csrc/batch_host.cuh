@@ -147,8 +147,7 @@ struct BatchEngine {
         if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) tcs) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
             cudaFuncSetAttribute(k_attn_paged, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int) paged_attn_smem(n_max, NH / NKV)) != cudaSuccess ||
-            cudaFuncSetAttribute(k_cp_attn_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess) {
+                                 (int) paged_attn_smem(n_max, NH / NKV)) != cudaSuccess) {
             err = "kernel attributes (context too long?)"; return false;
         }
         if (paged_attn_smem(n_max, NH / NKV) > 220 * 1024) { err = "max_positions too large for the paged attention"; return false; }
@@ -199,9 +198,8 @@ struct BatchEngine {
             fa.kc = cpk + il * cp_layer; fa.vc = cpv + il * cp_layer; fa.pos_static = pos_static; fa.M = M;
             fa.f32_mode = f32 ? 1 : 0; fa.scale = 1.0f / sqrtf((float) QTTS_HD); fa.out = att; fa.ldo = QD;
             fa.xt = xt2; fa.xt_np = (rows + 15) / 16 * 16;
-            const size_t fsm = fused_attn_smem(f32 ? M : 16, M);
             pb(BC_ATTN_CP);
-            k_cp_attn_batch<<<B * NH * M, FA_THREADS, fsm, stream>>>(fa, cp_stride, st, NH * M);
+            k_cp_attn_warp<<<(B * NH * M + CPW_WARPS - 1) / CPW_WARPS, CPW_WARPS * 32, 0, stream>>>(fa, cp_stride, st, B);
             pe();
             gemm_cls = BC_GEMM_O;
             gemm(t.o, H, QD, nullptr, QD, rows, nullptr, TC_ACT_F16, TC_EPI_RESID, xcp, H, xcp);
