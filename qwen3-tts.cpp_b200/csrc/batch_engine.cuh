@@ -24,7 +24,7 @@ namespace qtts {
 
 constexpr int BP_PAGE = 64;           // positions per KV page
 constexpr int PA_THREADS = 256;
-constexpr int PA_RING = 8;            // page blocks in flight per CTA
+constexpr int PA_RING = 4;            // page blocks in flight per CTA (two CTAs per SM)
 
 __host__ __device__ inline size_t bp_page_elems(int n_layers, int nkv) {
     return (size_t) n_layers * 2 * nkv * BP_PAGE * QTTS_HD;
@@ -61,7 +61,7 @@ __host__ __device__ inline size_t paged_attn_smem(int n_max, int G) {
 
 // One CTA per (sequence b, kv head g): the G query heads of the group share
 // every K/V load.  Item i of the stream is page (i mod np) of K (i < np) or V.
-__global__ void __launch_bounds__(PA_THREADS, 1) k_attn_paged(PagedAttnArgs a) {
+__global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[PA_RING];
     const int NKV = a.n_kv_heads, G = a.n_heads / NKV;
