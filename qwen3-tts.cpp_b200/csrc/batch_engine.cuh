@@ -64,6 +64,8 @@ __host__ __device__ inline size_t paged_attn_smem(int n_max, int G) {
 __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[PA_RING];
+    pdl_trigger();
+    pdl_wait();
     const int NKV = a.n_kv_heads, G = a.n_heads / NKV;
     const int b = blockIdx.x / NKV, g = blockIdx.x % NKV;
     const DevState & S = a.st[b];
@@ -269,6 +271,8 @@ __global__ void __launch_bounds__(CPW_WARPS * 32) k_cp_attn_warp(FusedAttn a, si
     __shared__ float sq[CPW_WARPS][QTTS_HD];
     __shared__ float sk[CPW_WARPS][2][QTTS_HD];
     __shared__ float sv[CPW_WARPS][2][QTTS_HD];
+    pdl_trigger();
+    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NH = a.n_heads, NKV = a.n_kv_heads, G = NH / NKV, M = a.M;
     const int unit = blockIdx.x * CPW_WARPS + warp;
@@ -383,6 +387,8 @@ __global__ void __launch_bounds__(CPW_WARPS * 32) k_cp_attn_warp(FusedAttn a, si
 __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample_batch(const float * logits, int ldl, int V, int cb,
                                                                  DevState * st, const SampleParams * sp,
                                                                  int * out_codes, int out_cap) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x;
     DevState * s = st + b;
     if (s->done) return;
@@ -407,6 +413,8 @@ struct BatchInputArgs {
 };
 
 __global__ void k_inputs_batch(BatchInputArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x;
     const DevState & S = a.st[b];
     if (S.done) return;
@@ -428,6 +436,8 @@ __global__ void k_inputs_batch(BatchInputArgs a) {
 }
 
 __global__ void k_frame_end_batch(DevState * st, int B) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B && !st[b].done) {
         st[b].pos += 1;

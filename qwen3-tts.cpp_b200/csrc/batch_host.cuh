@@ -168,7 +168,7 @@ struct BatchEngine {
             pa.x = xin; pa.ldx = ldx; pa.m_real = m; pa.np = np; pa.cols = cols; pa.gain = norm;
             pa.eps = E->cfg.rms_norm_eps; pa.act = act; pa.out = xt; pa.xn_out = xn_out; pa.ldxn = H;
             pb(BC_PACK);
-            k_pack_act<<<act == TC_ACT_SPLIT ? np / 2 : np, 256, 0, stream>>>(pa);
+            pdl_launch(k_pack_act, dim3(act == TC_ACT_SPLIT ? np / 2 : np), dim3(256), 0, stream, pa);
             pe();
             launches += 1;
             xsrc = xt;
@@ -199,7 +199,8 @@ struct BatchEngine {
             fa.f32_mode = f32 ? 1 : 0; fa.scale = 1.0f / sqrtf((float) QTTS_HD); fa.out = att; fa.ldo = QD;
             fa.xt = xt2; fa.xt_np = (rows + 15) / 16 * 16;
             pb(BC_ATTN_CP);
-            k_cp_attn_warp<<<(B * NH * M + CPW_WARPS - 1) / CPW_WARPS, CPW_WARPS * 32, 0, stream>>>(fa, cp_stride, st, B);
+            pdl_launch(k_cp_attn_warp, dim3((B * NH * M + CPW_WARPS - 1) / CPW_WARPS), dim3(CPW_WARPS * 32), 0, stream, fa,
+                       cp_stride, (const DevState *) st, B);
             pe();
             gemm_cls = BC_GEMM_O;
             gemm(t.o, H, QD, nullptr, QD, rows, nullptr, TC_ACT_F16, TC_EPI_RESID, xcp, H, xcp);
@@ -225,7 +226,7 @@ struct BatchEngine {
             pa.scale = 1.0f / sqrtf((float) QTTS_HD); pa.out = att; pa.ldo = QD; pa.n_max = n_max;
             pa.xt = xt2; pa.xt_np = (B + 15) / 16 * 16;
             pb(BC_ATTN_TALKER);
-            k_attn_paged<<<B * NKV, PA_THREADS, paged_attn_smem(n_max, G), stream>>>(pa);
+            pdl_launch(k_attn_paged, dim3(B * NKV), dim3(PA_THREADS), paged_attn_smem(n_max, G), stream, pa);
             pe();
             gemm_cls = BC_GEMM_O;
             gemm(t.o, H, QD, nullptr, QD, B, nullptr, TC_ACT_F16, TC_EPI_RESID, x, H, x);
@@ -241,36 +242,39 @@ struct BatchEngine {
         const int NG = NCB - 1;
         launches = 0;
         pb(BC_SAMPLE);
-        k_sample_batch<<<B, SAMPLE_THREADS, 0, stream>>>(logits, V0, V0, 0, st, sp, codes, max_frames);
+        pdl_launch(k_sample_batch, dim3(B), dim3(SAMPLE_THREADS), 0, stream, (const float *) logits, V0, V0, 0, st,
+                   (const SampleParams *) sp, codes, max_frames);
         pe();
         BatchInputArgs ia{};
         ia.H = H; ia.n_cb = NCB; ia.codec_embd = E->codec_embd; ia.cp_embd = E->d_cp_embd; ia.hidden = hidden;
         ia.trailing = trail; ia.trail_cap = trail_cap; ia.pad = pad; ia.st = st;
         ia.mode = IN_CP_PREFILL; ia.out = xcp;
-        k_inputs_batch<<<B, 256, 0, stream>>>(ia);
+        pdl_launch(k_inputs_batch, dim3(B), dim3(256), 0, stream, ia);
         cp_layers(2, true, 0);
         gemm_cls = BC_GEMM_HEAD;
         gemm(cp_head_t[0], V1, H, xcp + H, 2 * H, B, E->cp_out_norm, TC_ACT_F16, TC_EPI_STORE, cp_logits, V1, nullptr);
         pb(BC_SAMPLE);
-        k_sample_batch<<<B, SAMPLE_THREADS, 0, stream>>>(cp_logits, V1, V1, 1, st, sp, codes, max_frames);
+        pdl_launch(k_sample_batch, dim3(B), dim3(SAMPLE_THREADS), 0, stream, (const float *) cp_logits, V1, V1, 1, st,
+                   (const SampleParams *) sp, codes, max_frames);
         pe();
         for (int gs = 1; gs < NG; ++gs) {
             ia.mode = IN_CP_STEP; ia.g = gs;
-            k_inputs_batch<<<B, 256, 0, stream>>>(ia);
+            pdl_launch(k_inputs_batch, dim3(B), dim3(256), 0, stream, ia);
             cp_layers(1, false, gs + 1);
             gemm_cls = BC_GEMM_HEAD;
             gemm(cp_head_t[gs], V1, H, xcp, H, B, E->cp_out_norm, TC_ACT_F16, TC_EPI_STORE, cp_logits, V1, nullptr);
             pb(BC_SAMPLE);
-            k_sample_batch<<<B, SAMPLE_THREADS, 0, stream>>>(cp_logits, V1, V1, gs + 1, st, sp, codes, max_frames);
+            pdl_launch(k_sample_batch, dim3(B), dim3(SAMPLE_THREADS), 0, stream, (const float *) cp_logits, V1, V1, gs + 1,
+                       st, (const SampleParams *) sp, codes, max_frames);
             pe();
             launches += 2;
         }
         ia.mode = IN_TALKER; ia.out = x;
-        k_inputs_batch<<<B, 256, 0, stream>>>(ia);
+        pdl_launch(k_inputs_batch, dim3(B), dim3(256), 0, stream, ia);
         talker_layers();
         gemm_cls = BC_GEMM_HEAD;
         gemm(codec_head_t, V0, H, x, H, B, E->out_norm, TC_ACT_F16, TC_EPI_STORE, logits, V0, nullptr, hidden);
-        k_frame_end_batch<<<(B + 127) / 128, 128, 0, stream>>>(st, B);
+        pdl_launch(k_frame_end_batch, dim3((B + 127) / 128), dim3(128), 0, stream, st, B);
         launches += 5;
     }
 

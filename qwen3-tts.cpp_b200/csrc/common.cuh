@@ -140,6 +140,13 @@ __device__ __forceinline__ void tc_store_split(uint8_t * xt, int m, int k, int n
     *reinterpret_cast<__half *>(xt + tc_x_off(np / 2 + m, k, np)) = lo;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while its predecessor runs; pdl_wait() returns once
+// the predecessor grid has completed and its writes are visible (a no-op for a
+// normal launch), pdl_trigger() lets the successor start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 constexpr unsigned long long QTTS_SPIN_LIMIT = 1ull << 22;   // polls before a bounded wait gives up
 
 // ---- shared-memory weight slices (TMA bulk copies completed on an mbarrier)

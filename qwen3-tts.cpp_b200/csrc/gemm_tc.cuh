@@ -20,6 +20,7 @@
 // 32w..32w+31 = weight rows) into the epilogue.  Every wait is bounded.
 #pragma once
 #include "common.cuh"
+#include <utility>
 
 namespace qtts {
 
@@ -74,6 +75,8 @@ struct PackArgs {
 __global__ void __launch_bounds__(256) k_pack_act(PackArgs a) {
     __shared__ double red[8];
     __shared__ float s_scale;
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;                         // packed row (for TC_ACT_SPLIT: m < np/2)
     const int tid = threadIdx.x;
     const bool real = m < a.m_real;
@@ -221,16 +224,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     int issued = 0;
     const uint8_t * wsrc = g.w + ((size_t) tn * nk_all + k0) * wtile;
     const uint8_t * xsrc = g.x + (size_t) k0 * xtile;
+    pdl_trigger();
     if (tid == 0) {
         for (int s = 0; s < NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(&done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_fail = 0;
+        // weight tiles are read-only: their copies start before the predecessor finishes
         for (int i = 0; i < nk && i < NST; ++i) {
-            uint8_t * dst = tc_smem + i * sbytes;
             mbar_expect_tx(&full[i], (unsigned) sbytes);
-            bulk_g2s(dst, wsrc + (size_t) i * wtile, (unsigned) wtile, &full[i]);
-            bulk_g2s(dst + wtile, xsrc + (size_t) i * xtile, (unsigned) xtile, &full[i]);
+            bulk_g2s(tc_smem + i * sbytes, wsrc + (size_t) i * wtile, (unsigned) wtile, &full[i]);
             issued = i + 1;
         }
     }
@@ -243,6 +246,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(GemmTcArgs g) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    pdl_wait();   // activations, residuals and outputs follow the predecessor in stream order
+    if (tid == 0)
+        for (int i = 0; i < issued; ++i)
+            bulk_g2s(tc_smem + i * sbytes + wtile, xsrc + (size_t) i * xtile, (unsigned) xtile, &full[i]);
 
     if (tid == 0) {
         // producer: W tile (tn, k) and X k-tile into stage k % NST
@@ -432,14 +439,33 @@ inline cudaError_t tc_launch(const GemmTcArgs & g, cudaStream_t stream) {
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned) S;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, k_gemm_tc, g);
+}
+
+// Launch any kernel with programmatic stream serialization (see pdl_wait).
+template <class... KArgs, class... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args &&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_gemm_tc, g);
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace qtts
