@@ -163,7 +163,7 @@ def cpu_frames_per_s(path: str, n_ref_prefill: int, budget_s: float, max_frames:
     """The CPU oracle port on all host cores: frames after a prefill of the same length."""
     from oracle import Oracle, available_cpus
     cores = available_cpus()
-    o = Oracle(path, threads=cores)
+    o = Oracle(path, threads=cores, engine_order=False)
     H = o.cfg["hidden"]
     rng = np.random.default_rng(7)
     rows = (rng.standard_normal((n_ref_prefill, H)) * 0.1).astype(np.float32)

@@ -112,12 +112,19 @@ class Oracle:
             L.orc_sample.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_float, C.c_int, C.c_double]
             L.orc_forward_talker_rows.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.c_int, C.c_int]
             L.orc_set_threads.argtypes = [C.c_int]
+            L.orc_set_engine_order.argtypes = [C.c_int]
+            L.orc_expf.restype = C.c_float
+            L.orc_expf.argtypes = [C.c_float]
             cls._lib = L
         return cls._lib
 
-    def __init__(self, path: str, threads: int | None = None):
+    def __init__(self, path: str, threads: int | None = None, engine_order: bool = True):
+        """engine_order: run every reduction in the engine's order (the parity
+        checker's mode; process-wide); False: plain sequential / AVX2 orders,
+        used for the CPU baseline timing."""
         L = self.lib()
         L.orc_set_threads(int(threads) if threads else available_cpus())
+        L.orc_set_engine_order(1 if engine_order else 0)
         err = C.create_string_buffer(512)
         self.h = L.orc_load(path.encode(), err, 512)
         if not self.h:
@@ -240,6 +247,12 @@ class Oracle:
         if want_prefill:
             out["prefill"] = pf[:r.prefill_len].copy()
         return out
+
+
+def expf(x) -> np.ndarray:
+    """The oracle's exp (Cody-Waite + degree-7 Taylor, as the engine's)."""
+    L = Oracle.lib()
+    return np.array([L.orc_expf(float(v)) for v in np.ravel(np.asarray(x, np.float32))], np.float32)
 
 
 def quantize_q8_0(x: np.ndarray):

@@ -16,7 +16,13 @@
 //     quantize_row_q8_0_ref (d = amax/127, id = 1/d, q = roundf(x*id), d stored
 //     as F16), int32 dot per block, sum += isum * (d_w * d_a) in F32.
 //   * rms_norm: sum of squares in double, scale = 1/sqrtf(mean + eps).
-//   * softmax: max, expf(x - max), sum in double, y = e * (float)(1/sum).
+//   * softmax: max, exp(x - max), sum in double, y = e * (float)(1/sum).
+//   * exp (softmax, SiLU): Cody-Waite reduction + degree-7 Taylor polynomial
+//     (qexpf), the method the engine uses, so both give the same bits.
+//   * Summation orders: by default every reduction (GEMV rows, RMSNorm sums,
+//     attention scores, softmax sums, P x V) runs in the engine's order (see
+//     g_eng), so engine and oracle agree before each F16 rounding and Q8_0
+//     quantisation; ggml's own order depends on its SIMD path.
 //   * RoPE NEOX: theta_i = pos * s^i by repeated F32 multiplication,
 //     s = powf(base, -2/n_dims) (ggml_rope_cache_init).
 //   * KV caches F16; talker prefill/step and code-predictor steps read K/V from
@@ -212,6 +218,155 @@ static const Tensor * need(Model & m, const std::string & name) {
     return &it->second;
 }
 
+// ---------------------------------------------------------------- engine-order arithmetic
+// The engine's reductions run in a fixed order (lanes, butterflies, thread
+// strides).  With g_eng set (the default) the oracle performs every reduction
+// in that same order, so engine and oracle agree bit for bit before every
+// rounding and quantisation step (the Q8_0 activation quantiser turns a last-bit
+// difference into a whole int8 level).  With g_eng clear it uses plain
+// sequential / AVX2 orders (faster; the CPU baseline timing uses it).  Either
+// order is a valid restatement of the reference's F32 accumulations, whose
+// own order depends on ggml's SIMD path.
+static bool g_eng = true;
+
+// e^x by Cody-Waite reduction and a degree-7 Taylor polynomial: the method the
+// engine's qtts_expf uses, with the same explicitly rounded operations.
+static inline float qexpf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.97208404541015625f) return 0.0f;
+    const float n = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(-n, 0.693145751953125f, x);
+    r = fmaf(-n, 1.428606765330187045037746429443359375e-06f, r);
+    float p = 1.98412701138295233249664306640625e-04f;
+    p = fmaf(p, r, 1.38888892251998186111450195312500e-03f);
+    p = fmaf(p, r, 8.33333376795053482055664062500000e-03f);
+    p = fmaf(p, r, 4.16666679084300994873046875000000e-02f);
+    p = fmaf(p, r, 1.66666671633720397949218750000000e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int ni = (int) n;
+    if (ni > 127) { p = p * 2.0f; ni -= 1; }
+    if (ni < -126) { p = p * 5.42101086242752217003726400434970855712890625e-20f; ni += 64; }
+    uint32_t bits = (uint32_t)(ni + 127) << 23;
+    float sc;
+    memcpy(&sc, &bits, 4);
+    return p * sc;
+}
+
+// Lane 0's value after the xor butterfly 16, 8, 4, 2, 1 over 32 lanes.
+static inline float bfly0(const float * v) {
+    float a[32];
+    memcpy(a, v, sizeof(a));
+    for (int o = 16; o > 0; o >>= 1) {
+        float b[32];
+        for (int l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ o];
+        memcpy(a, b, sizeof(a));
+    }
+    return a[0];
+}
+// Every lane's value after the same butterfly on doubles.
+static inline void bfly_all_d(double * a) {
+    for (int o = 16; o > 0; o >>= 1) {
+        double b[32];
+        for (int l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ o];
+        memcpy(a, b, sizeof(b));
+    }
+}
+
+// RMSNorm scale of a GEMV prologue (512 threads): thread t sums the squares at
+// planar positions t, t+512, ... (the two-plane activation layout: position p
+// holds column ((q >> 2) << 3) + 4 [p >= cols/2] + (q & 3), q = p mod cols/2),
+// lane 0 of each warp keeps its butterfly sum, the 16 warp sums add in order.
+static float gemv_norm_scale(const float * x, int cols, float eps) {
+    const int half = cols / 2;
+    double warp_sum[16];
+    for (int w = 0; w < 16; ++w) {
+        double lanes[32];
+        for (int l = 0; l < 32; ++l) {
+            double ss = 0.0;
+            for (int p = w * 32 + l; p < cols; p += 512) {
+                const int q = p >= half ? p - half : p;
+                const int c = ((q >> 2) << 3) + (p >= half ? 4 : 0) + (q & 3);
+                ss += (double)(x[c] * x[c]);
+            }
+            lanes[l] = ss;
+        }
+        bfly_all_d(lanes);
+        warp_sum[w] = lanes[0];
+    }
+    double ss = 0.0;
+    for (int w = 0; w < 16; ++w) ss += warp_sum[w];
+    const float mean = (float)(ss / (double) cols);
+    return 1.0f / sqrtf(mean + eps);
+}
+
+// GEMV row dot in the engine's order: lane l chains 8-column chunks l, l+32, ...
+// (eight fused multiply-adds per chunk, in column order), then the butterfly.
+static inline float dot_f16_eng(const uint16_t * w, const float * x, int cols) {
+    float lanes[32];
+    const int nch = cols / 8;
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int c = l; c < nch; c += 32)
+            for (int e = 0; e < 8; ++e) acc = fmaf(h2f(w[8 * c + e]), x[8 * c + e], acc);
+        lanes[l] = acc;
+    }
+    return bfly0(lanes);
+}
+// Q8_0 row dot in the engine's order: lane 2j adds the 32-blocks j, j+16, ...
+// (isum * (d_w * d_a) each), odd lanes hold 0, then the butterfly.
+static inline float dot_q8_eng(const uint8_t * row, const int8_t * qa, const uint16_t * da, int nb) {
+    float lanes[32] = {0.0f};
+    for (int j = 0; j < 16; ++j) {
+        float acc = 0.0f;
+        for (int b = j; b < nb; b += 16) {
+            uint16_t dw;
+            memcpy(&dw, row + b * 34, 2);
+            const int8_t * qw = (const int8_t *)(row + b * 34 + 2);
+            int32_t isum = 0;
+            for (int k = 0; k < 32; ++k) isum += (int32_t) qw[k] * (int32_t) qa[b * 32 + k];
+            acc = acc + (float) isum * (h2f(dw) * h2f(da[b]));
+        }
+        lanes[2 * j] = acc;
+    }
+    return bfly0(lanes);
+}
+
+// Per-head RMSNorm of q / k as the engine's warp does it: lane l squares its 4
+// dims (double, in order), the butterfly gives each lane its own sum, and each
+// lane scales its dims with its own scale.
+static void head_norm_eng(float * x, int D, float eps, const float * gain) {
+    double ss[32];
+    for (int l = 0; l < 32; ++l) {
+        double t = 0.0;
+        for (int k = 0; k < 4; ++k) t += (double)(x[l * 4 + k] * x[l * 4 + k]);
+        ss[l] = t;
+    }
+    bfly_all_d(ss);
+    for (int l = 0; l < 32; ++l) {
+        const float mean = (float)(ss[l] / (double) D);
+        const float scale = 1.0f / sqrtf(mean + eps);
+        for (int k = 0; k < 4; ++k) {
+            const float t = x[l * 4 + k] * scale;
+            x[l * 4 + k] = gain ? t * gain[l * 4 + k] : t;
+        }
+    }
+}
+
+// QK score of one key in the engine's order: lanes of an 8-lane group chain 16
+// dims each, combined ((s0+s4)+(s2+s6)) + ((s1+s5)+(s3+s7)).
+static inline float score_eng(const float * k, const float * q) {
+    float s[8];
+    for (int g = 0; g < 8; ++g) {
+        float a = 0.0f;
+        for (int d = 0; d < 16; ++d) a = fmaf(k[g * 16 + d], q[g * 16 + d], a);
+        s[g] = a;
+    }
+    return ((s[0] + s[4]) + (s[2] + s[6])) + ((s[1] + s[5]) + (s[3] + s[7]));
+}
+
 // ---------------------------------------------------------------- kernels
 // y[r] = W[r,:] . x  for a weight matrix with ne0 = cols (input), ne1 = rows.
 // mode: 0 = ggml F16 semantics (x rounded to F16); 1 = weight cast to F32 (x
@@ -269,7 +424,8 @@ static void mul_mat(const Tensor * W, const float * x, int n_vec, float * y, boo
         #pragma omp parallel for schedule(static)
         for (int r = 0; r < rows; ++r)
             for (int v = 0; v < n_vec; ++v)
-                y[(size_t) v * rows + r] = dot_f16_f32acc(w + (size_t) r * cols, xh.data() + (size_t) v * cols, cols);
+                y[(size_t) v * rows + r] = g_eng ? dot_f16_eng(w + (size_t) r * cols, xh.data() + (size_t) v * cols, cols)
+                                                 : dot_f16_f32acc(w + (size_t) r * cols, xh.data() + (size_t) v * cols, cols);
         return;
     }
     if (W->type == T_Q8_0) {
@@ -281,6 +437,10 @@ static void mul_mat(const Tensor * W, const float * x, int n_vec, float * y, boo
         for (int r = 0; r < rows; ++r) {
             const uint8_t * row = w + (size_t) r * nb * 34;
             for (int v = 0; v < n_vec; ++v) {
+                if (g_eng) {
+                    y[(size_t) v * rows + r] = dot_q8_eng(row, qx[v].q.data(), qx[v].d.data(), nb);
+                    continue;
+                }
                 float s = 0.0f;
                 for (int b = 0; b < nb; ++b) {
                     uint16_t dw; memcpy(&dw, row + b * 34, 2);
@@ -307,6 +467,14 @@ static void rms_norm(const float * x, int n, float eps, const float * gain, floa
 
 static const float * f32p(const Tensor * t) { return (const float *) t->data; }
 
+// RMSNorm of a GEMV input (attn_norm, ffn_norm, output norms): the engine
+// computes it in the GEMV prologue, with gemv_norm_scale's summation order.
+static void rms_norm_in(const float * x, int n, float eps, const float * gain, float * y) {
+    if (!g_eng) { rms_norm(x, n, eps, gain, y); return; }
+    const float scale = gemv_norm_scale(x, n, eps);
+    for (int i = 0; i < n; ++i) { const float t = x[i] * scale; y[i] = gain ? t * gain[i] : t; }
+}
+
 // ggml_rope_cache_init with ext_factor 0, freq_scale 1, attn_factor 1.
 static void rope_cache(int pos, int n_dims, float base, float * cs /*[n_dims] cos,sin pairs*/) {
     const float theta_scale = powf(base, -2.0f / (float) n_dims);
@@ -328,7 +496,7 @@ static void rope_neox(float * x, int D, const float * cs) {
     }
 }
 
-static inline float silu(float x) { return x / (1.0f + expf(-x)); }
+static inline float silu(float x) { return x / (1.0f + qexpf(-x)); }
 
 // One decoder stack over M token rows X[M][H] at positions n_past..n_past+M-1.
 // kv_from_cache: attention reads F16 K/V from the cache (talker graphs and the
@@ -349,19 +517,21 @@ static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, fl
     const int n_kv_tot = n_past + M;
     for (size_t il = 0; il < layers.size(); ++il) {
         const Layer & ly = layers[il];
-        for (int i = 0; i < M; ++i) rms_norm(&X[(size_t) i * H], H, c.eps, f32p(ly.attn_norm), &xn[(size_t) i * H]);
+        for (int i = 0; i < M; ++i) rms_norm_in(&X[(size_t) i * H], H, c.eps, f32p(ly.attn_norm), &xn[(size_t) i * H]);
         mul_mat(ly.q, xn.data(), M, q.data());
         mul_mat(ly.k, xn.data(), M, k.data());
         mul_mat(ly.v, xn.data(), M, v.data());
         for (int i = 0; i < M; ++i) {
             for (int h = 0; h < NH; ++h) {
                 float * qh = &q[(size_t) i * QD + h * D];
-                rms_norm(qh, D, c.eps, ly.q_norm ? f32p(ly.q_norm) : nullptr, qh);
+                if (g_eng) head_norm_eng(qh, D, c.eps, ly.q_norm ? f32p(ly.q_norm) : nullptr);
+                else rms_norm(qh, D, c.eps, ly.q_norm ? f32p(ly.q_norm) : nullptr, qh);
                 rope_neox(qh, D, &cs[(size_t) i * D]);
             }
             for (int h = 0; h < NKV; ++h) {
                 float * kh = &k[(size_t) i * KD + h * D];
-                rms_norm(kh, D, c.eps, ly.k_norm ? f32p(ly.k_norm) : nullptr, kh);
+                if (g_eng) head_norm_eng(kh, D, c.eps, ly.k_norm ? f32p(ly.k_norm) : nullptr);
+                else rms_norm(kh, D, c.eps, ly.k_norm ? f32p(ly.k_norm) : nullptr, kh);
                 rope_neox(kh, D, &cs[(size_t) i * D]);
             }
             uint16_t * kc = cache.K((int) il, n_past + i);
@@ -378,6 +548,75 @@ static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, fl
                 std::vector<float> s(nk), p(nk), qh(D);
                 const float * qsrc = &q[(size_t) i * QD + h * D];
                 for (int d = 0; d < D; ++d) qh[d] = kv_from_cache ? round_f16(qsrc[d]) : qsrc[d];
+                if (g_eng) {
+                    // the engine's fused unit (frame steps, the code-predictor prefill, one-row
+                    // prefill chunks) or its prefill kernel (chunks of 2-8 rows)
+                    const int chunk = std::min(8, M - (i / 8) * 8);
+                    const bool fused = !kv_from_cache || M == 1 || chunk == 1;
+                    const int nkey = kv_from_cache ? n_past + i + 1 : i + 1;
+                    std::vector<float> kf(D);
+                    for (int j = 0; j < nkey; ++j) {
+                        if (kv_from_cache) {
+                            const uint16_t * kj = cache.K((int) il, j) + g * D;
+                            for (int d = 0; d < D; ++d) kf[d] = h2f(kj[d]);
+                            s[j] = score_eng(kf.data(), qh.data()) * kq_scale;
+                        } else {
+                            s[j] = score_eng(&k[(size_t) j * KD + g * D], qh.data()) * kq_scale;
+                        }
+                    }
+                    float mx = -INFINITY;
+                    for (int j = 0; j < nkey; ++j) mx = std::max(mx, s[j]);
+                    for (int j = 0; j < nkey; ++j) p[j] = qexpf(s[j] - mx);
+                    double lane[32];
+                    if (fused) {
+                        for (int l = 0; l < 32; ++l) {
+                            double t = 0.0;
+                            for (int j = l; j < nkey; j += 32) t += (double) p[j];
+                            lane[l] = t;
+                        }
+                        bfly_all_d(lane);
+                    } else {
+                        double red[32] = {0.0};
+                        for (int w = 0; w < 8; ++w) {
+                            double tl[32];
+                            for (int l = 0; l < 32; ++l) {
+                                double t = 0.0;
+                                for (int j = w * 32 + l; j < nkey; j += 256) t += (double) p[j];
+                                tl[l] = t;
+                            }
+                            bfly_all_d(tl);
+                            red[w] = tl[0];
+                        }
+                        memcpy(lane, red, sizeof(lane));
+                        bfly_all_d(lane);
+                    }
+                    for (int j = 0; j < nkey; ++j) {
+                        const float inv = (float)(1.0 / lane[j & 31]);
+                        p[j] = p[j] * inv;
+                        if (kv_from_cache) p[j] = round_f16(p[j]);
+                    }
+                    const int npg = fused ? 8 : 4;
+                    float * out = &att[(size_t) i * QD + h * D];
+                    for (int d = 0; d < D; ++d) {
+                        float part[8];
+                        for (int pg = 0; pg < npg; ++pg) {
+                            float acc = 0.0f;
+                            for (int j = pg; j < nkey; j += npg) {
+                                const float vj = kv_from_cache ? h2f(cache.V((int) il, j)[g * D + d]) : v[(size_t) j * KD + g * D + d];
+                                acc = fmaf(p[j], vj, acc);
+                            }
+                            part[pg] = acc;
+                        }
+                        if (fused) {
+                            float t = 0.0f;
+                            for (int pg = 0; pg < 8; ++pg) t = t + part[pg];
+                            out[d] = t;
+                        } else {
+                            out[d] = (part[0] + part[1]) + (part[2] + part[3]);
+                        }
+                    }
+                    continue;
+                }
                 float mx = -INFINITY;
                 for (int j = 0; j < nk; ++j) {
                     float dot = 0.0f;
@@ -394,7 +633,7 @@ static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, fl
                     mx = std::max(mx, sc);
                 }
                 double sum = 0.0;
-                for (int j = 0; j < nk; ++j) { float e = expf(s[j] - mx); p[j] = e; sum += (double) e; }
+                for (int j = 0; j < nk; ++j) { float e = qexpf(s[j] - mx); p[j] = e; sum += (double) e; }
                 const float inv = (float)(1.0 / sum);
                 for (int j = 0; j < nk; ++j) p[j] *= inv;
                 float * out = &att[(size_t) i * QD + h * D];
@@ -412,7 +651,7 @@ static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, fl
             }
         mul_mat(ly.o, att.data(), M, o.data());
         for (size_t t = 0; t < (size_t) M * H; ++t) X[t] = o[t] + X[t];
-        for (int i = 0; i < M; ++i) rms_norm(&X[(size_t) i * H], H, c.eps, f32p(ly.ffn_norm), &xn[(size_t) i * H]);
+        for (int i = 0; i < M; ++i) rms_norm_in(&X[(size_t) i * H], H, c.eps, f32p(ly.ffn_norm), &xn[(size_t) i * H]);
         mul_mat(ly.gate, xn.data(), M, gt.data());
         mul_mat(ly.up, xn.data(), M, up.data());
         for (size_t t = 0; t < (size_t) M * ffn; ++t) hh[t] = silu(gt[t]) * up[t];
@@ -482,7 +721,7 @@ static int32_t sample_tok(float * lg, int n, float temperature, int top_k, doubl
     float mx = *std::max_element(lg, lg + n);
     std::vector<float> p(n);
     double sum = 0.0;
-    for (int i = 0; i < n; ++i) { p[i] = expf(lg[i] - mx); sum += p[i]; }
+    for (int i = 0; i < n; ++i) { p[i] = qexpf(lg[i] - mx); sum += p[i]; }
     for (int i = 0; i < n; ++i) p[i] = (float)(p[i] / sum);
     double tot = 0.0;
     for (int i = 0; i < n; ++i) tot += (double) p[i];
@@ -529,6 +768,9 @@ struct orc_gen_result {
 };
 
 void orc_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
+// 1 (default): every reduction in the engine's order; 0: plain sequential / AVX2 orders.
+void orc_set_engine_order(int on) { g_eng = on != 0; }
+float orc_expf(float x) { return qexpf(x); }
 int orc_get_threads() { return omp_get_max_threads(); }
 
 void * orc_load(const char * path, char * err, int errlen) {
@@ -666,7 +908,7 @@ int orc_forward_prefill(void * h, const float * embd, int n, int n_past, float *
     if (n_past + n > m.cache.n_ctx) return -1;
     std::vector<float> X(embd, embd + (size_t) n * H), hs((size_t) n * H);
     forward_stack(m, m.L, m.cache, m.c.theta, X, n, n_past, true, m.c.ffn);
-    for (int i = 0; i < n; ++i) rms_norm(&X[(size_t) i * H], H, m.c.eps, f32p(m.out_norm), &hs[(size_t) i * H]);
+    for (int i = 0; i < n; ++i) rms_norm_in(&X[(size_t) i * H], H, m.c.eps, f32p(m.out_norm), &hs[(size_t) i * H]);
     if (hidden_out) memcpy(hidden_out, hs.data(), hs.size() * 4);
     m.last_hidden.assign(hs.end() - H, hs.end());
     if (logits_out) mul_mat(m.codec_head, m.last_hidden.data(), 1, logits_out);
@@ -682,7 +924,7 @@ int orc_forward_step(void * h, const float * embd, int n_past, float * logits_ou
     std::vector<float> X(embd, embd + H);
     forward_stack(m, m.L, m.cache, m.c.theta, X, 1, n_past, true, m.c.ffn);
     m.last_hidden.resize(H);
-    rms_norm(X.data(), H, m.c.eps, f32p(m.out_norm), m.last_hidden.data());
+    rms_norm_in(X.data(), H, m.c.eps, f32p(m.out_norm), m.last_hidden.data());
     if (hidden_out) memcpy(hidden_out, m.last_hidden.data(), H * 4);
     if (logits_out) mul_mat(m.codec_head, m.last_hidden.data(), 1, logits_out);
     return 0;
@@ -695,7 +937,7 @@ static void cp_pass(Model & m, int gen_step, const float * rows, float * logits)
     const int n_past = gen_step == 0 ? 0 : gen_step + 1;
     std::vector<float> X(rows, rows + (size_t) M * H), hn(H);
     forward_stack(m, m.CPL, m.cp_cache, m.c.cp_theta, X, M, n_past, /*kv_from_cache=*/gen_step != 0, m.c.cp_ffn);
-    rms_norm(&X[(size_t)(M - 1) * H], H, m.c.eps, f32p(m.cp_out_norm), hn.data());
+    rms_norm_in(&X[(size_t)(M - 1) * H], H, m.c.eps, f32p(m.cp_out_norm), hn.data());
     mul_mat(m.cp_head[gen_step], hn.data(), 1, logits);
 }
 

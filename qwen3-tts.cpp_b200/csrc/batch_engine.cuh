@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
         mx = warp_max(mx);
         double sum = 0.0;
         for (int j = lane; j < n; j += 32) {
-            const float e = expf(__fsub_rn(r[j], mx));
+            const float e = qtts_expf(__fsub_rn(r[j], mx));
             r[j] = e;
             sum += (double) e;
         }
@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(CPW_WARPS * 32) k_cp_attn_warp(FusedAttn a, si
         sj = __fmul_rn(acc, a.scale);
     }
     const float mx = warp_max(sj);
-    const float e = lane < n ? expf(__fsub_rn(sj, mx)) : 0.0f;
+    const float e = lane < n ? qtts_expf(__fsub_rn(sj, mx)) : 0.0f;
     const double sum = warp_sum_d(lane < n ? (double) e : 0.0);
     const float inv = (float)(1.0 / sum);
     float p = __fmul_rn(e, inv);

@@ -88,8 +88,37 @@ __device__ __forceinline__ float dot8(const uint4 & w, const float * x, float ac
     return acc;
 }
 
+// e^x by Cody-Waite range reduction and a Taylor polynomial: x = n ln2 + r with
+// n = rint(x log2 e), ln2 split into a 16-bit head (n * head is exact) and a
+// tail, |r| <= ln2/2; e^r = sum_{k<=7} r^k / k! by Horner (truncation error
+// ~5e-9 relative, below half a float ulp); the result is P(r) * 2^n, scaled in
+// two steps near the ends of the range so subnormal results round once.
+// Every operation is an explicitly rounded IEEE operation, so the CPU oracle's
+// restatement of the same method gives the same bits.  Accuracy: within 2 ulp
+// of e^x (checked against float64 in the tests).
+__device__ __forceinline__ float qtts_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.97208404541015625f) return 0.0f;
+    const float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = __fmaf_rn(-n, 0.693145751953125f, x);
+    r = __fmaf_rn(-n, 1.428606765330187045037746429443359375e-06f, r);
+    float p = 1.98412701138295233249664306640625e-04f;       // 1/7!
+    p = __fmaf_rn(p, r, 1.38888892251998186111450195312500e-03f);   // 1/6!
+    p = __fmaf_rn(p, r, 8.33333376795053482055664062500000e-03f);   // 1/5!
+    p = __fmaf_rn(p, r, 4.16666679084300994873046875000000e-02f);   // 1/4!
+    p = __fmaf_rn(p, r, 1.66666671633720397949218750000000e-01f);   // 1/3!
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    int ni = (int) n;
+    if (ni > 127) { p = __fmul_rn(p, 2.0f); ni -= 1; }
+    if (ni < -126) { p = __fmul_rn(p, 5.42101086242752217003726400434970855712890625e-20f); ni += 64; }   // 2^-64
+    return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
 // SiLU as ggml's scalar definition: x / (1 + exp(-x)).
-__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, qtts_expf(-x))); }
 
 // Philox4x32-10 (Salmon et al., SC'11).  Same function as the CPU oracle.
 __device__ __forceinline__ void philox(uint32_t c[4], uint32_t k0, uint32_t k1) {

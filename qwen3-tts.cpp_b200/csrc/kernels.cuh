@@ -524,7 +524,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
         mx = block_max(mx, redf);
         double sum = 0.0;
         for (int j = tid; j < n; j += blockDim.x) {
-            const float e = expf(__fsub_rn(sc[h * n + j], mx));
+            const float e = qtts_expf(__fsub_rn(sc[h * n + j], mx));
             sc[h * n + j] = e;
             sum += (double) e;
         }
@@ -744,7 +744,7 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
         mx = warp_max(mx);
         double sum = 0.0;
         for (int j = lane; j < n; j += 32) {
-            const float e = expf(__fsub_rn(sc[j], mx));
+            const float e = qtts_expf(__fsub_rn(sc[j], mx));
             sc[j] = e;
             sum += (double) e;
         }
@@ -982,7 +982,7 @@ __device__ int sample_body(const float * logits, int V, int cb, const DevState *
         double s = 0.0;
 #pragma unroll
         for (int e = 0; e < PT; ++e) {
-            ev[e] = valid[e] ? expf(__fsub_rn(l[e], mx)) : 0.0f;
+            ev[e] = valid[e] ? qtts_expf(__fsub_rn(l[e], mx)) : 0.0f;
             s += (double) ev[e];
         }
         const double sum = block_sum_d(s, redd);

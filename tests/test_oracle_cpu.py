@@ -165,3 +165,36 @@ def test_oracle_follow_self_and_eos(tiny_f16):
     assert e["n_frames"] == 0
     t = o.generate(text, 40, eos_bias=0.0, target_frames=2)
     assert t["n_frames"] <= 40
+
+
+def test_oracle_expf_within_2_ulp():
+    """The exp shared by engine and oracle (Cody-Waite + degree-7 Taylor) is
+    within 2 ulp of e^x over the range the softmax and SiLU use, and saturates
+    to 0 / inf outside the float range."""
+    from oracle import expf
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.uniform(-87.0, 88.0, 20000), rng.uniform(-1.0, 1.0, 20000),
+                        np.array([0.0, -0.0, 1.0, -1.0, 88.5, -87.3, -100.0])]).astype(np.float32)
+    y = expf(x).astype(np.float64)
+    ref = np.exp(x.astype(np.float64))
+    ulp = np.spacing(ref.astype(np.float32)).astype(np.float64)
+    assert np.all(np.abs(y - ref) <= 2 * ulp), float(np.max(np.abs(y - ref) / ulp))
+    assert expf(np.array([200.0]))[0] == np.inf and expf(np.array([-200.0]))[0] == 0.0
+
+
+def test_engine_order_matches_plain_order(tiny_f16):
+    """The oracle's engine-order reductions and its plain orders are the same
+    arithmetic up to summation order: step logits agree to float rounding."""
+    from oracle import Oracle
+    rng = np.random.default_rng(8)
+    outs = []
+    for eng in (True, False):
+        o = Oracle(tiny_f16, threads=4, engine_order=eng)
+        H = o.cfg["hidden"]
+        rows = (rng.standard_normal((12, H)) * 0.1).astype(np.float32) if not outs else rows
+        o.init_kv(64)
+        _, lg = o.forward_prefill(rows)
+        outs.append(lg)
+        o.close()
+    Oracle(tiny_f16, threads=4, engine_order=True).close()
+    assert np.abs(outs[0] - outs[1]).max() < 1e-3
