@@ -120,7 +120,7 @@ struct Engine {
     int launches_per_frame = 0;
     GenSession sess;
     // persistent frame kernel (one cooperative launch per run of frames)
-    bool use_persistent = true;
+    bool use_persistent = false;   // QTTS_FRAME_MODE=persistent selects the single-launch frame kernel
     std::vector<POp> prog;
     POp * d_prog = nullptr;
     size_t prog_cap = 0;
@@ -301,7 +301,7 @@ bool Engine::load(const char * path, int device) {
     if (c.hidden_size % 256 || c.intermediate_size % 32 || c.code_pred_intermediate_size % 32 || c.text_embd_dim % 32) {
         err = "hidden/ffn/text widths must be multiples of 256/32/32"; return false;
     }
-    if (const char * m = getenv("QTTS_FRAME_MODE")) use_persistent = strcmp(m, "graph") != 0;
+    if (const char * m = getenv("QTTS_FRAME_MODE")) use_persistent = strcmp(m, "persistent") == 0;
     if (const char * lb = getenv("QTTS_PF_LEAD_MB")) pf_lead_bytes = atof(lb) * 1024.0 * 1024.0;
     if (!upload_weights(g)) return false;
     if (!alloc_activations()) return false;
@@ -570,7 +570,7 @@ bool Engine::sync(const char * what) {
 // its weight slice and work area fit, more CTAs (smaller slices) otherwise.
 static bool gemv_shape(const DMat & A, bool dual, bool has_gain, int nvt, int n_sm, int * ncta_out, size_t * slice_out,
                        size_t * smem_out) {
-    int ncta = std::min(n_sm, A.rows);
+    int ncta = std::min(2 * n_sm, A.rows);   // two CTAs per SM: half the rows each, and room for the next kernel under PDL
     for (;;) {
         const int rpc = gemv_rpc(A.rows, ncta);
         const size_t slice = (slice_layout(A, dual, has_gain, rpc).total + 127) & ~(size_t) 127;
@@ -612,9 +612,9 @@ bool Engine::gemv(const DMat & A, const DMat * B, const float * xin, int ldx, in
     if (nv > QTTS_MAX_NV || ncta == 0) { err = "gemv shape too large"; return false; }
     const double wb = A.type == W_F16 ? (double) A.rows * A.cols * 2.0 : (double) A.rows * A.cols * 34.0 / 32.0;
     prof_begin(KC_GEMV, wb * (B ? 2.0 : 1.0) + 4.0 * nv * ((double) A.cols + A.rows));
-    if (NVt == 1) k_gemv<1><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a, slice);
-    else if (NVt == 2) k_gemv<2><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a, slice);
-    else k_gemv<8><<<ncta, QTTS_WARPS * 32, smem, stream>>>(a, slice);
+    if (NVt == 1) pdl_launch(k_gemv<1>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
+    else if (NVt == 2) pdl_launch(k_gemv<2>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
+    else pdl_launch(k_gemv<8>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
     prof_end();
     ++launches;
     return true;
@@ -653,7 +653,7 @@ bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, in
             const size_t fsm = fused_attn_smem(f32_mode ? M : ctx, M);
             if (fsm > 200 * 1024) { err = "context too long for the fused attention kernel"; return false; }
             prof_begin(KC_ATTN, 0.0);
-            k_fused_attention<<<NH * M, FA_THREADS, fsm, stream>>>(fa, st);
+            pdl_launch(k_fused_attention, dim3(NH * M), dim3(FA_THREADS), fsm, stream, fa, (const DevState *) st);
             prof_end();
             ++launches;
         } else {
@@ -696,7 +696,8 @@ bool Engine::enqueue_cp(bool sample_cb0) {
     const int * done = &st->done;
     if (sample_cb0) {
         prof_begin(KC_SAMPLE, 0.0);
-        k_sample<<<1, SAMPLE_THREADS, 0, stream>>>(logits, c.codec_vocab_size, 0, st, sp, d_codes, codes_cap);
+        pdl_launch(k_sample, dim3(1), dim3(SAMPLE_THREADS), 0, stream, (const float *) logits, c.codec_vocab_size, 0, st,
+                   (const SampleParams *) sp, d_codes, codes_cap);
         prof_end();
         ++launches;
     }
@@ -704,25 +705,27 @@ bool Engine::enqueue_cp(bool sample_cb0) {
     ia.H = H; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
     ia.trailing = trailing; ia.pad = pad; ia.out = xcp; ia.st = st; ia.n_cb = c.n_codebooks;
     ia.mode = IN_CP_PREFILL;
-    k_frame_inputs<<<1, 256, 0, stream>>>(ia);
+    pdl_launch(k_frame_inputs, dim3(1), dim3(256), 0, stream, ia);
     ++launches;
     if (!layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 2, nullptr, 0, true, done, c.code_pred_intermediate_size)) return false;
     if (!gemv(cp_head[0], nullptr, xcp + H, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE, nullptr, 0, done))
         return false;
     prof_begin(KC_SAMPLE, 0.0);
-    k_sample<<<1, SAMPLE_THREADS, 0, stream>>>(cp_logits, V1, 1, st, sp, d_codes, codes_cap);
+    pdl_launch(k_sample, dim3(1), dim3(SAMPLE_THREADS), 0, stream, (const float *) cp_logits, V1, 1, st,
+               (const SampleParams *) sp, d_codes, codes_cap);
     prof_end();
     ++launches;
     for (int gstep = 1; gstep < NG; ++gstep) {
         ia.mode = IN_CP_STEP; ia.g = gstep;
-        k_frame_inputs<<<1, 256, 0, stream>>>(ia);
+        pdl_launch(k_frame_inputs, dim3(1), dim3(256), 0, stream, ia);
         ++launches;
         if (!layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 1, nullptr, gstep + 1, false, done, c.code_pred_intermediate_size))
             return false;
         if (!gemv(cp_head[gstep], nullptr, xcp, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE, nullptr, 0, done))
             return false;
         prof_begin(KC_SAMPLE, 0.0);
-        k_sample<<<1, SAMPLE_THREADS, 0, stream>>>(cp_logits, V1, gstep + 1, st, sp, d_codes, codes_cap);
+        pdl_launch(k_sample, dim3(1), dim3(SAMPLE_THREADS), 0, stream, (const float *) cp_logits, V1, gstep + 1, st,
+                   (const SampleParams *) sp, d_codes, codes_cap);
         prof_end();
         ++launches;
     }
@@ -745,10 +748,10 @@ bool Engine::enqueue_frame() {
     ia.H = cfg.hidden_size; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
     ia.trailing = trailing; ia.pad = pad; ia.out = x; ia.st = st; ia.n_cb = cfg.n_codebooks;
     ia.mode = IN_TALKER;
-    k_frame_inputs<<<1, 256, 0, stream>>>(ia);
+    pdl_launch(k_frame_inputs, dim3(1), dim3(256), 0, stream, ia);
     ++launches;
     if (!enqueue_talker_step(&st->pos, 0, &st->done, true)) return false;
-    k_frame_end<<<1, 32, 0, stream>>>(st);
+    pdl_launch(k_frame_end, dim3(1), dim3(32), 0, stream, st);
     ++launches;
     return true;
 }

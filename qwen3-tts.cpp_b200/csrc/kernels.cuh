@@ -299,20 +299,26 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
 
 // Stand-alone GEMV launch (CUDA-graph path, prefill, kernel tests): thread 0
 // stages this CTA's weight slice into shared memory with TMA bulk copies while
-// all threads load the activations.
+// all threads load the activations.  Launched with programmatic dependent
+// launch, the copy starts while the previous kernel still runs.
 template <int NV>
 __global__ void __launch_bounds__(QTTS_WARPS * 32) k_gemv(GemvArgs a, size_t slice_bytes) {
-    if (a.done && *a.done) return;
+    pdl_trigger();
     const int rpc = gemv_rpc(a.A.rows, gridDim.x);
     if ((int) blockIdx.x * rpc >= a.A.rows) return;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t mbar;
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0) {   // the weight slice is read-only: its copy may start before the predecessor ends
         mbar_init(&mbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         issue_gemv_slice(a.A, a.B, a.norm_g, smem_raw, &mbar, blockIdx.x, gridDim.x);
     }
     __syncthreads();
+    pdl_wait();               // activations, the stop flag and the outputs follow the predecessor
+    if (a.done && *a.done) {
+        if (threadIdx.x == 0) mbar_wait(&mbar, 0u);   // no bulk copy in flight at exit
+        return;
+    }
     if (!gemv_slice<NV>(a, blockIdx.x, gridDim.x, smem_raw, smem_raw + slice_bytes, &mbar, 0u)) {
         // the copy did not complete within the wait limit: wait once more (bounded) so
         // no bulk copy is in flight when the block exits, and leave the output unwritten
@@ -796,6 +802,8 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
 
 // Stand-alone launch of the fused unit (CUDA-graph frame path): one CTA per unit.
 __global__ void __launch_bounds__(FA_THREADS) k_fused_attention(FusedAttn a, const DevState * st) {
+    pdl_trigger();
+    pdl_wait();
     if (a.done && *a.done) return;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     fused_attn_body(a, blockIdx.x, smem_raw, a.pos_ptr ? *a.pos_ptr : a.pos_static, st->frame);
@@ -1040,6 +1048,8 @@ __device__ __forceinline__ void sample_commit(int tok, int cb, DevState * st, co
 
 __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits, int V, int cb, DevState * st,
                                                            const SampleParams * sp, int * out_codes, int out_cap) {
+    pdl_trigger();
+    pdl_wait();
     if (st->done) return;
     const SampleParams P = *sp;
     const int frame = st->frame;
@@ -1066,6 +1076,8 @@ struct InputArgs {
 };
 
 __global__ void k_frame_inputs(InputArgs a) {
+    pdl_trigger();
+    pdl_wait();
     if (a.st->done) return;
     const DevState * st = a.st;
     for (int h = threadIdx.x; h < a.H; h += blockDim.x) {
@@ -1085,6 +1097,8 @@ __global__ void k_frame_inputs(InputArgs a) {
 }
 
 __global__ void k_frame_end(DevState * st) {
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x == 0 && !st->done) {
         st->pos += 1;
         st->frame += 1;
