@@ -198,7 +198,7 @@ struct Engine {
                 float * dump = nullptr, int dump_layer = -1);
     FusedAttn fused_attn_args(const LayerW & l, __half * kc_l, __half * vc_l, const float2 * rope, int M,
                               const int * pos_ptr, int pos_static, bool f32, float * dump, int dump_stride);
-    bool enqueue_cp(bool sample_cb0);
+    bool enqueue_cp(bool sample_cb0, const InputArgs * last_in = nullptr);
     bool enqueue_talker_step(const int * pos_ptr, int pos_static, const int * done, bool with_dump);
     bool enqueue_frame();
     bool capture_graph();
@@ -689,46 +689,46 @@ bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, in
 }
 
 // Code predictor for the current frame state: 2-token prefill, head 0, then 14
-// single-token steps, each followed by on-device sampling into st->codes.
-bool Engine::enqueue_cp(bool sample_cb0) {
+// single-token steps.  Each sampler also builds the next pass's input rows
+// (k_sample_inputs); last_in: the inputs after the last code-predictor sampler
+// (the next talker step), or nullptr for a plain sampler.
+bool Engine::enqueue_cp(bool sample_cb0, const InputArgs * last_in) {
     const qtts_config & c = cfg;
     const int H = c.hidden_size, V1 = c.code_pred_vocab_size, NG = c.n_codebooks - 1;
     const int * done = &st->done;
-    if (sample_cb0) {
-        prof_begin(KC_SAMPLE, 0.0);
-        pdl_launch(k_sample, dim3(1), dim3(SAMPLE_THREADS), 0, stream, (const float *) logits, c.codec_vocab_size, 0, st,
-                   (const SampleParams *) sp, d_codes, codes_cap);
-        prof_end();
-        ++launches;
-    }
     InputArgs ia{};
     ia.H = H; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
     ia.trailing = trailing; ia.pad = pad; ia.out = xcp; ia.st = st; ia.n_cb = c.n_codebooks;
     ia.mode = IN_CP_PREFILL;
-    pdl_launch(k_frame_inputs, dim3(1), dim3(256), 0, stream, ia);
-    ++launches;
+    auto sample = [&](const float * lg, int V, int cb, const InputArgs * in) {
+        prof_begin(KC_SAMPLE, 0.0);
+        if (in)
+            pdl_launch(k_sample_inputs, dim3(1), dim3(SAMPLE_THREADS), 0, stream, lg, V, cb, st,
+                       (const SampleParams *) sp, d_codes, codes_cap, *in);
+        else
+            pdl_launch(k_sample, dim3(1), dim3(SAMPLE_THREADS), 0, stream, lg, V, cb, st, (const SampleParams *) sp,
+                       d_codes, codes_cap);
+        prof_end();
+        ++launches;
+    };
+    if (sample_cb0) {
+        sample(logits, c.codec_vocab_size, 0, &ia);
+    } else {
+        pdl_launch(k_frame_inputs, dim3(1), dim3(256), 0, stream, ia);
+        ++launches;
+    }
     if (!layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 2, nullptr, 0, true, done, c.code_pred_intermediate_size)) return false;
     if (!gemv(cp_head[0], nullptr, xcp + H, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE, nullptr, 0, done))
         return false;
-    prof_begin(KC_SAMPLE, 0.0);
-    pdl_launch(k_sample, dim3(1), dim3(SAMPLE_THREADS), 0, stream, (const float *) cp_logits, V1, 1, st,
-               (const SampleParams *) sp, d_codes, codes_cap);
-    prof_end();
-    ++launches;
     for (int gstep = 1; gstep < NG; ++gstep) {
-        ia.mode = IN_CP_STEP; ia.g = gstep;
-        pdl_launch(k_frame_inputs, dim3(1), dim3(256), 0, stream, ia);
-        ++launches;
+        ia.mode = IN_CP_STEP; ia.g = gstep; ia.step_tab = cp_embd[gstep - 1];
+        sample(cp_logits, V1, gstep, &ia);   // codebook gstep, then the step's input row
         if (!layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 1, nullptr, gstep + 1, false, done, c.code_pred_intermediate_size))
             return false;
         if (!gemv(cp_head[gstep], nullptr, xcp, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE, nullptr, 0, done))
             return false;
-        prof_begin(KC_SAMPLE, 0.0);
-        pdl_launch(k_sample, dim3(1), dim3(SAMPLE_THREADS), 0, stream, (const float *) cp_logits, V1, gstep + 1, st,
-                   (const SampleParams *) sp, d_codes, codes_cap);
-        prof_end();
-        ++launches;
     }
+    sample(cp_logits, V1, NG, last_in);
     return true;
 }
 
@@ -743,13 +743,11 @@ bool Engine::enqueue_talker_step(const int * pos_ptr, int pos_static, const int 
 }
 
 bool Engine::enqueue_frame() {
-    if (!enqueue_cp(true)) return false;
     InputArgs ia{};
     ia.H = cfg.hidden_size; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
     ia.trailing = trailing; ia.pad = pad; ia.out = x; ia.st = st; ia.n_cb = cfg.n_codebooks;
     ia.mode = IN_TALKER;
-    pdl_launch(k_frame_inputs, dim3(1), dim3(256), 0, stream, ia);
-    ++launches;
+    if (!enqueue_cp(true, &ia)) return false;
     if (!enqueue_talker_step(&st->pos, 0, &st->done, true)) return false;
     pdl_launch(k_frame_end, dim3(1), dim3(32), 0, stream, st);
     ++launches;

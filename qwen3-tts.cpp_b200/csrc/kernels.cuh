@@ -804,9 +804,12 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
 __global__ void __launch_bounds__(FA_THREADS) k_fused_attention(FusedAttn a, const DevState * st) {
     pdl_trigger();
     pdl_wait();
-    if (a.done && *a.done) return;
+    const int dn = a.done ? *a.done : 0;   // stop flag, position and frame: one round trip
+    const int np = a.pos_ptr ? *a.pos_ptr : a.pos_static;
+    const int frame = st->frame;
+    if (dn) return;
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    fused_attn_body(a, blockIdx.x, smem_raw, a.pos_ptr ? *a.pos_ptr : a.pos_static, st->frame);
+    fused_attn_body(a, blockIdx.x, smem_raw, np, frame);
 }
 
 struct SampleParams {
@@ -1050,9 +1053,9 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float * logits,
                                                            const SampleParams * sp, int * out_codes, int out_cap) {
     pdl_trigger();
     pdl_wait();
-    if (st->done) return;
+    const int dn = st->done, frame = st->frame;   // loaded together with the parameters
     const SampleParams P = *sp;
-    const int frame = st->frame;
+    if (dn) return;
     const int tok = sample_body<SAMPLE_PER_T>(logits, V, cb, st, P, frame);
     if (threadIdx.x == 0) sample_commit(tok, cb, st, P, out_codes, out_cap, frame);
 }
@@ -1074,6 +1077,67 @@ struct InputArgs {
     int n_cb;
     const __half * step_tab;      // IN_CP_STEP: cp_embd[g - 1] (persistent path)
 };
+
+// Inputs of the next pass, built by the sampling CTA right after it sampled:
+// codes[0..cb] (shared memory) hold this frame's codes so far, tabs[1..n_cb-1] the
+// code-predictor embedding tables, n_trailing the trailing text rows.  Same
+// sums in the same order as k_frame_inputs.
+__device__ void frame_inputs_body(const InputArgs & a, const int frame, const int * codes,
+                                  const __half * const * tabs, const int n_trailing) {
+    for (int h = threadIdx.x; h < a.H; h += blockDim.x) {
+        if (a.mode == IN_CP_PREFILL) {
+            a.out[h] = a.hidden[h];
+            a.out[a.H + h] = __half2float(a.codec_embd[(size_t) codes[0] * a.H + h]);
+        } else if (a.mode == IN_CP_STEP) {
+            a.out[h] = __half2float(a.step_tab[(size_t) codes[a.g] * a.H + h]);
+        } else {
+            float e[QTTS_MAX_CB];
+            e[0] = __half2float(a.codec_embd[(size_t) codes[0] * a.H + h]);
+#pragma unroll
+            for (int cb = 1; cb < QTTS_MAX_CB; ++cb)
+                e[cb] = cb < a.n_cb ? __half2float(tabs[cb][(size_t) codes[cb] * a.H + h]) : 0.0f;
+            const float * tr = frame < n_trailing ? a.trailing + (size_t) frame * a.H : a.pad;
+            const float t = tr[h];
+            float s = e[0];
+#pragma unroll
+            for (int cb = 1; cb < QTTS_MAX_CB; ++cb)
+                if (cb < a.n_cb) s = __fadd_rn(s, e[cb]);
+            a.out[h] = __fadd_rn(s, t);
+        }
+    }
+}
+
+// Sampler of codebook cb followed by the next input rows (CUDA-graph frame
+// path): one launch instead of k_sample + k_frame_inputs, with the decisions of
+// k_sample and the sums of frame_inputs_body.  `in.mode` IN_CP_PREFILL follows
+// codebook 0, IN_CP_STEP (g = cb) a code-predictor codebook, IN_TALKER the last
+// codebook of the frame.
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_sample_inputs(const float * logits, int V, int cb, DevState * st,
+                                                                  const SampleParams * sp, int * out_codes,
+                                                                  int out_cap, InputArgs in) {
+    __shared__ int s_codes[QTTS_MAX_CB];
+    __shared__ const __half * s_tabs[QTTS_MAX_CB];
+    pdl_trigger();
+    pdl_wait();
+    const int tid = threadIdx.x;
+    // frame state, earlier codes and table pointers: loaded together, before the sampler needs them
+    const int dn = st->done, frame = st->frame, n_trailing = st->n_trailing;
+    const SampleParams P = *sp;
+    int c_pre = 0;
+    const __half * t_pre = nullptr;
+    if (in.mode == IN_TALKER) {
+        if (tid < cb) c_pre = st->codes[tid];
+        if (tid >= 1 && tid < in.n_cb) t_pre = in.cp_embd[tid - 1];
+    }
+    if (dn) return;
+    const int tok = sample_body<SAMPLE_PER_T>(logits, V, cb, st, P, frame);
+    if (tid == 0) sample_commit(tok, cb, st, P, out_codes, out_cap, frame);
+    if (tid < cb) s_codes[tid] = c_pre;
+    if (tid == 0) s_codes[cb] = tok;
+    if (tid < QTTS_MAX_CB) s_tabs[tid] = t_pre;
+    __syncthreads();
+    frame_inputs_body(in, frame, s_codes, s_tabs, n_trailing);
+}
 
 __global__ void k_frame_inputs(InputArgs a) {
     pdl_trigger();

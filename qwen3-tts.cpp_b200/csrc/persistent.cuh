@@ -99,35 +99,6 @@ __device__ __forceinline__ void prefetch_gemv_slice(const GemvArgs & g, int cta,
     prefetch_mat_slice(g.B, cta, ncta);
 }
 
-// Inputs of the next pass, built by CTA 0 right after it sampled: codes[0..cb]
-// (shared memory) hold this frame's codes so far, tabs[1..n_cb-1] the
-// code-predictor embedding tables, n_trailing the trailing text rows.  Same
-// sums in the same order as k_frame_inputs.
-__device__ void frame_inputs_body(const InputArgs & a, const int frame, const int * codes,
-                                  const __half * const * tabs, const int n_trailing) {
-    for (int h = threadIdx.x; h < a.H; h += blockDim.x) {
-        if (a.mode == IN_CP_PREFILL) {
-            a.out[h] = a.hidden[h];
-            a.out[a.H + h] = __half2float(a.codec_embd[(size_t) codes[0] * a.H + h]);
-        } else if (a.mode == IN_CP_STEP) {
-            a.out[h] = __half2float(a.step_tab[(size_t) codes[a.g] * a.H + h]);
-        } else {
-            float e[QTTS_MAX_CB];
-            e[0] = __half2float(a.codec_embd[(size_t) codes[0] * a.H + h]);
-#pragma unroll
-            for (int cb = 1; cb < QTTS_MAX_CB; ++cb)
-                e[cb] = cb < a.n_cb ? __half2float(tabs[cb][(size_t) codes[cb] * a.H + h]) : 0.0f;
-            const float * tr = frame < n_trailing ? a.trailing + (size_t) frame * a.H : a.pad;
-            const float t = tr[h];
-            float s = e[0];
-#pragma unroll
-            for (int cb = 1; cb < QTTS_MAX_CB; ++cb)
-                if (cb < a.n_cb) s = __fadd_rn(s, e[cb]);
-            a.out[h] = __fadd_rn(s, t);
-        }
-    }
-}
-
 struct PersistentArgs {
     const POp * ops;
     int n_ops;
