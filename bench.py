@@ -308,6 +308,8 @@ def run_batch(args, cfg):
     kv_mean = float(np.mean([u.prefill for u in mine])) + W + K / 2.0
     frame_bytes = WEIGHT_BYTES["f16"] + B * (KV_TALKER_PER_POS * kv_mean + KV_CP_PER_POS * 135)
     achieved = frame_bytes / (frame_ms / 1e3) / 1e9
+    ratio = _profile_figure("k_gemm_tc_batch16.md", "dram_bytes_per_algorithmic_byte")   # ncu, batched GEMMs
+    traffic = ratio * frame_bytes if ratio else None
     flops = 2.0 * (WEIGHT_BYTES["f16"] / 2.0) * B
     line = {
         "metric": METRIC, "value": frames_all / (ms_max / 1e3), "unit": UNIT, "n_gpus": world, "steps": K,
@@ -318,7 +320,7 @@ def run_batch(args, cfg):
                    "parallelism": f"LPT utterance sharding over {world} GPU(s), one batch per GPU",
                    "l2": "inputs larger than L2 (3.3 GB of weights + KV streamed per frame), no flush"},
         "roofline": {"bound": "hbm", "kernel": "batched frame (CUDA graph: tcgen05 GEMMs + paged attention)",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "frame_algorithmic_bytes": frame_bytes, "launches_per_frame": tm["launches_per_frame"],
                      "tensor_tflops": flops / (frame_ms / 1e3) / 1e12},
@@ -460,7 +462,9 @@ def main():
         kernel = "k_gemv (all GEMV launches of a frame, eager replay)"
         bytes_per_launch = g["bytes"] / max(g["launches"], 1)
         achieved = gemv_gbs
-        traffic = _profile_figure(f"k_gemv_{args.config}.md", "dram_bytes_per_launch")
+        # ncu: DRAM bytes per algorithmic byte over captured frame GEMVs, times this run's mean launch
+        ratio = _profile_figure(f"k_gemv_{args.config}.md", "dram_bytes_per_algorithmic_byte")
+        traffic = ratio * bytes_per_launch if ratio else None
         launches_per_frame_k = g["launches"] / max(prof["frames"], 1)
     line = {
         "metric": METRIC, "value": world * K / (ms_max / 1e3), "unit": UNIT, "n_gpus": world, "steps": K,
