@@ -433,8 +433,10 @@ def main():
     t_e = float(et.item())
     H = eng.cfg["hidden_size"]
     n_text_rows = 3 + 3 + (len(ref) - 8) + (len(tgt) - 8) + 1
-    n_lookup_rows = 3 + 2 + 1 + 16 * cfg["n_ref"]
-    h2d_utt = (4 * (len(tgt) + len(ref) + codes.size) + 4 * H * (plen + 1) + 4 * n_text_rows + 4 * n_lookup_rows)
+    # embedding rows read back for the host assembly: 6 special rows + one summed
+    # codec row per reference frame (the reference codes go up once, counted above)
+    n_lookup_rows = 3 + 2 + 1 + cfg["n_ref"]
+    h2d_utt = (4 * (len(tgt) + len(ref) + codes.size) + 4 * H * (plen + 1) + 4 * n_text_rows + 4 * 6)
     d2h_utt = 4 * H * (n_text_rows + n_lookup_rows) + 4 * 16 * F + 4 * H + 1024 * ((F + 15) // 16)
 
     if world > 1:

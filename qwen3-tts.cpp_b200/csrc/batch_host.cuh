@@ -8,6 +8,51 @@ struct TiledLayer {
     uint8_t * qkv = nullptr, * o = nullptr, * gu = nullptr, * down = nullptr;
 };
 
+// A weight matrix (or a gate/up pair, interleaved in 64-row groups) copied
+// into the canonical tcgen05 tile layout of k_gemm_tc.
+inline bool tile_check(const DMat & W, const DMat * W2, std::string & err) {
+    const int rows_w = W2 ? 2 * W.rows : W.rows;
+    if (W.type != W_F16) { err = "tensor-core path: F16 weights only"; return false; }
+    if (rows_w % TC_BM || W.cols % TC_BK || (W2 && W.rows % (TC_BM / 2))) { err = "tensor-core path: matrix shape"; return false; }
+    return true;
+}
+inline bool tile_launch(const DMat & W, const DMat * W2, uint8_t * out, cudaStream_t stream) {
+    const int rows_w = W2 ? 2 * W.rows : W.rows;
+    k_tile_weights<<<rows_w, 128, 0, stream>>>((const __half *) W.w, W2 ? (const __half *) W2->w : nullptr, rows_w,
+                                              W.cols, out);
+    return cudaGetLastError() == cudaSuccess;
+}
+
+// Pack (RMSNorm, F16 / hi-lo) + tcgen05 GEMM for m activation rows on `stream`
+// (shared by the batched frame and the tensor-core prefill).  xin == nullptr:
+// the activation tiles are already in xt2 (written by the producer).  xt_next:
+// SwiGLU only, also write h as hi/lo tiles into xt2 for the down GEMM.
+struct TcGemm {
+    cudaStream_t stream = nullptr;
+    uint8_t * xt = nullptr, * xt2 = nullptr;
+    int * d_err = nullptr;
+    float eps = 0.0f;
+    int ldxn = 0;
+    int launches = 0;
+    void pack(const float * xin, int ldx, int m, int np, int cols, const float * norm, int act, float * xn_out) {
+        PackArgs pa{};
+        pa.x = xin; pa.ldx = ldx; pa.m_real = m; pa.np = np; pa.cols = cols; pa.gain = norm;
+        pa.eps = eps; pa.act = act; pa.out = xt; pa.xn_out = xn_out; pa.ldxn = ldxn;
+        pdl_launch(k_pack_act, dim3(act == TC_ACT_SPLIT ? np / 2 : np), dim3(256), 0, stream, pa);
+        launches += 1;
+    }
+    void gemm(const uint8_t * wt, int rows_w, int cols, const uint8_t * xsrc, int m, int np, int act, int epi,
+              float * y, int ldy, const float * resid, bool xt_next, int mp) {
+        GemmTcArgs g{};
+        g.w = wt; g.x = xsrc; g.rows_w = rows_w; g.cols = cols; g.np = np; g.m_real = m;
+        g.split = act == TC_ACT_SPLIT; g.epi = epi; g.y = y; g.ldy = ldy; g.resid = resid; g.ldr = ldy; g.err = d_err;
+        if (xt_next) { g.xt_out = xt2; g.xt_np = 2 * mp; }
+        g.ksplit = tc_choose_split(g);
+        tc_launch(g, stream);
+        launches += 1;
+    }
+};
+
 struct BatchEngine {
     Engine * E = nullptr;
     int dev = 0;
@@ -73,13 +118,9 @@ struct BatchEngine {
     }
 
     bool tile(const DMat & W, const DMat * W2, uint8_t ** out) {
-        const int rows_w = W2 ? 2 * W.rows : W.rows;
-        if (W.type != W_F16) { err = "batched path: F16 weights only"; return false; }
-        if (rows_w % TC_BM || W.cols % TC_BK || (W2 && W.rows % (TC_BM / 2))) { err = "batched path: matrix shape"; return false; }
-        if (!alloc(out, (size_t) rows_w * W.cols * 2)) return false;
-        k_tile_weights<<<rows_w, 128, 0, stream>>>((const __half *) W.w, W2 ? (const __half *) W2->w : nullptr, rows_w,
-                                                  W.cols, *out);
-        return cudaGetLastError() == cudaSuccess;
+        if (!tile_check(W, W2, err)) return false;
+        if (!alloc(out, (size_t)(W2 ? 2 * W.rows : W.rows) * W.cols * 2)) return false;
+        return tile_launch(W, W2, *out, stream);
     }
 
     bool create(Engine * eng, int bmax, int nmax, int mframes) {
@@ -162,26 +203,16 @@ struct BatchEngine {
               int epi, float * y, int ldy, const float * resid, float * xn_out = nullptr, bool xt_next = false) {
         const int mp = (m + 15) / 16 * 16;
         const int np = act == TC_ACT_SPLIT ? 2 * mp : mp;
-        const uint8_t * xsrc = xt2;
+        TcGemm t{stream, xt, xt2, d_err, E->cfg.rms_norm_eps, H, 0};
         if (xin) {
-            PackArgs pa{};
-            pa.x = xin; pa.ldx = ldx; pa.m_real = m; pa.np = np; pa.cols = cols; pa.gain = norm;
-            pa.eps = E->cfg.rms_norm_eps; pa.act = act; pa.out = xt; pa.xn_out = xn_out; pa.ldxn = H;
             pb(BC_PACK);
-            pdl_launch(k_pack_act, dim3(act == TC_ACT_SPLIT ? np / 2 : np), dim3(256), 0, stream, pa);
+            t.pack(xin, ldx, m, np, cols, norm, act, xn_out);
             pe();
-            launches += 1;
-            xsrc = xt;
         }
-        GemmTcArgs g{};
-        g.w = wt; g.x = xsrc; g.rows_w = rows_w; g.cols = cols; g.np = np; g.m_real = m;
-        g.split = act == TC_ACT_SPLIT; g.epi = epi; g.y = y; g.ldy = ldy; g.resid = resid; g.ldr = ldy; g.err = d_err;
-        if (xt_next) { g.xt_out = xt2; g.xt_np = 2 * mp; }
-        g.ksplit = tc_choose_split(g);
         pb(gemm_cls);
-        tc_launch(g, stream);
+        t.gemm(wt, rows_w, cols, xin ? xt : xt2, m, np, act, epi, y, ldy, resid, xt_next, mp);
         pe();
-        launches += 1;
+        launches += t.launches;
     }
     int gemm_cls = BC_GEMM_QKV;
 
@@ -396,5 +427,109 @@ struct BatchEngine {
         return true;
     }
 };
+
+// Tensor-core talker prefill (F16 weights): forward_prefill over up to
+// PREFILL_TC_ROWS prompt rows per call with the batched path's tcgen05 GEMMs
+// (weights tiled once, on first use), the prefill attention kernels and the
+// engine's KV cache.  Per layer: pack+GEMM q|k|v, q/k norm + RoPE + KV append,
+// causal attention, GEMM O (+ residual), pack+GEMM gate/up (SwiGLU, h written
+// as hi/lo tiles), GEMM down (+ residual).
+struct PrefillTC {
+    Engine * E = nullptr;
+    std::string err;
+    std::vector<TiledLayer> TL;
+    std::vector<void *> owned;
+    float * qkv = nullptr, * att = nullptr, * hbuf = nullptr;
+    uint8_t * xt = nullptr, * xt2 = nullptr;
+    int * d_err = nullptr;
+
+    template <class T>
+    bool alloc(T ** p, size_t bytes) {
+        if (cudaMalloc(p, bytes) != cudaSuccess) { err = "prefill: out of device memory"; return false; }
+        owned.push_back(*p);
+        return true;
+    }
+    ~PrefillTC() { for (void * p : owned) cudaFree(p); }
+
+    bool tile(const DMat & W, const DMat * W2, uint8_t ** out) {
+        if (!tile_check(W, W2, err)) return false;
+        if (!alloc(out, (size_t)(W2 ? 2 * W.rows : W.rows) * W.cols * 2)) return false;
+        return tile_launch(W, W2, *out, E->stream);
+    }
+
+    bool create(Engine * eng) {
+        E = eng;
+        const qtts_config & c = eng->cfg;
+        const int R = PREFILL_TC_ROWS, H = c.hidden_size, QD = eng->QD(), FF = c.intermediate_size;
+        TL.resize(E->L.size());
+        for (size_t i = 0; i < E->L.size(); ++i) {
+            LayerW & l = E->L[i];
+            if (!tile(l.qkv, nullptr, &TL[i].qkv) || !tile(l.o, nullptr, &TL[i].o) || !tile(l.gate, &l.up, &TL[i].gu) ||
+                !tile(l.down, nullptr, &TL[i].down))
+                return false;
+        }
+        const int maxc = std::max(std::max(H, QD), FF);
+        if (!alloc(&qkv, sizeof(float) * R * eng->QKVD()) || !alloc(&att, sizeof(float) * R * QD) ||
+            !alloc(&hbuf, sizeof(float) * R * FF) || !alloc(&xt, (size_t) TC_MAX_N * maxc * 2) ||
+            !alloc(&xt2, (size_t) TC_MAX_N * maxc * 2) || !alloc(&d_err, sizeof(int)))
+            return false;
+        if (cudaMemsetAsync(d_err, 0, sizeof(int), E->stream) != cudaSuccess) { err = "prefill: memset"; return false; }
+        if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+            err = "prefill: kernel attributes"; return false;
+        }
+        return true;
+    }
+
+    // All talker layers over rows X[M][H] at positions n_past .. n_past + M - 1.
+    bool layers(float * X, int M, int n_past) {
+        const qtts_config & c = E->cfg;
+        const int H = c.hidden_size, QD = E->QD(), QKVD = E->QKVD(), FF = c.intermediate_size;
+        const int G = c.n_attention_heads / c.n_key_value_heads;
+        if (M < 1 || M > PREFILL_TC_ROWS) { err = "prefill: chunk size"; return false; }
+        const size_t layer_elems = (size_t) E->n_ctx * c.n_key_value_heads * QTTS_HD;
+        const size_t att_smem = attn_smem_bytes(E->n_ctx, G);
+        const int mp = (M + 15) / 16 * 16;
+        TcGemm t{E->stream, xt, xt2, d_err, c.rms_norm_eps, H, 0};
+        for (size_t il = 0; il < E->L.size(); ++il) {
+            const LayerW & l = E->L[il];
+            const TiledLayer & w = TL[il];
+            t.pack(X, H, M, mp, H, l.attn_norm, TC_ACT_F16, nullptr);
+            t.gemm(w.qkv, QKVD, H, xt, M, mp, TC_ACT_F16, TC_EPI_STORE, qkv, QKVD, nullptr, false, mp);
+            E->prefill_attention(l, E->kc + il * layer_elems, E->vc + il * layer_elems, E->rope_t, qkv, QKVD, M,
+                                 nullptr, n_past, nullptr, att, QD, nullptr, 0, att_smem);
+            t.pack(att, QD, M, mp, QD, nullptr, TC_ACT_F16, nullptr);
+            t.gemm(w.o, H, QD, xt, M, mp, TC_ACT_F16, TC_EPI_RESID, X, H, X, false, mp);
+            t.pack(X, H, M, mp, H, l.ffn_norm, TC_ACT_F16, nullptr);
+            t.gemm(w.gu, 2 * FF, H, xt, M, mp, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, FF, nullptr, true, mp);
+            // ffn_down: F32 activation (F16 weight cast to F32 by the reference) as F16 hi + lo
+            t.gemm(w.down, H, FF, xt2, M, 2 * mp, TC_ACT_SPLIT, TC_EPI_RESID, X, H, X, false, mp);
+        }
+        E->launches += t.launches;
+        if (cudaGetLastError() != cudaSuccess) { err = "prefill: launch failed"; return false; }
+        return true;
+    }
+};
+
+bool prefill_tc_layers(Engine & E, float * X, int M, int n_past) {
+    if (!E.ptc) {
+        PrefillTC * p = new PrefillTC();
+        if (!p->create(&E)) { E.err = p->err; delete p; return false; }
+        E.ptc = p;
+    }
+    if (!E.ptc->layers(X, M, n_past)) { E.err = E.ptc->err; return false; }
+    return true;
+}
+
+bool prefill_tc_check(Engine & E) {
+    int e = 0;
+    if (!E.ptc || cudaMemcpy(&e, E.ptc->d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess || e != 0) {
+        E.err = "prefill: tensor-core GEMM error " + std::to_string(e);
+        return false;
+    }
+    return true;
+}
+
+void prefill_tc_free(PrefillTC * p) { delete p; }
 
 }  // namespace qtts

@@ -59,6 +59,14 @@ struct GenSession {
     DevState st0{};   // frame state right after the prefill (rewind target)
 };
 
+struct Engine;
+struct PrefillTC;
+constexpr int PREFILL_TC_ROWS = 128;   // prompt rows per tensor-core chunk (hi/lo ffn_down doubles MMA N to 256)
+// Tensor-core talker prefill (defined with the batched path's host code).
+bool prefill_tc_layers(Engine & E, float * X, int M, int n_past);
+bool prefill_tc_check(Engine & E);   // after a sync: no GEMM reported an error
+void prefill_tc_free(PrefillTC * p);
+
 struct Engine {
     int dev = 0, n_sm = 148;
     cudaStream_t stream = nullptr;
@@ -90,6 +98,9 @@ struct Engine {
     float * tmp_a = nullptr, * tmp_b = nullptr;
     int * d_ids = nullptr;
     int ids_cap = 0;
+    float * d_prow = nullptr;   // prefill rows [prow_cap][H], uploaded once per prefill
+    int prow_cap = 0;
+    PrefillTC * ptc = nullptr;  // tensor-core prefill (created on first use)
 
     // frame state
     DevState * st = nullptr;
@@ -165,6 +176,8 @@ struct Engine {
     void release() {
         if (dev >= 0) cudaSetDevice(dev);
         if (graph) { cudaGraphExecDestroy(graph); graph = nullptr; }
+        if (ptc) { prefill_tc_free(ptc); ptc = nullptr; }
+        if (d_prow) { cudaFree(d_prow); d_prow = nullptr; prow_cap = 0; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
                          cp_logits, hidden, hid_rows, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
                          dbg_t, dbg_cp, d_attn, d_prog, d_flags, d_err, d_trace, logits0, hidden0};
@@ -198,6 +211,9 @@ struct Engine {
                 float * dump = nullptr, int dump_layer = -1);
     FusedAttn fused_attn_args(const LayerW & l, __half * kc_l, __half * vc_l, const float2 * rope, int M,
                               const int * pos_ptr, int pos_static, bool f32, float * dump, int dump_stride);
+    void prefill_attention(const LayerW & l, __half * kc_l, __half * vc_l, const float2 * rope, const float * q,
+                           int ldq, int M, const int * pos_ptr, int pos_static, const int * done, float * out, int ldo,
+                           float * dump, int dump_stride, size_t smem);
     bool enqueue_cp(bool sample_cb0, const InputArgs * last_in = nullptr);
     bool enqueue_talker_step(const int * pos_ptr, int pos_static, const int * done, bool with_dump);
     bool enqueue_frame();
@@ -213,6 +229,7 @@ struct Engine {
     bool prefill(const float * rows_host, int n, int n_past, float * hidden_out, float * logits_out);
     bool project_text(const int32_t * toks, int n, std::vector<float> & out);
     bool lookup(int table, const int32_t * ids, int n, std::vector<float> & out);
+    bool icl_codec_rows(const int32_t * codes, int n_frames, float * out_host);
     bool build_prefill(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
                        std::vector<float> & padv);
     bool build_prefill_icl(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
@@ -633,6 +650,36 @@ FusedAttn Engine::fused_attn_args(const LayerW & l, __half * kc_l, __half * vc_l
     return a;
 }
 
+// Prefill attention over M rows (chunks of the prompt): q/k norm + RoPE + F16
+// KV append for the rows, then causal attention over the cache.  q: the
+// rows' q|k|v [M][ldq]; out: [M][ldo].
+void Engine::prefill_attention(const LayerW & l, __half * kc_l, __half * vc_l, const float2 * rope, const float * q,
+                               int ldq, int M, const int * pos_ptr, int pos_static, const int * done, float * out,
+                               int ldo, float * dump, int dump_stride, size_t smem) {
+    const qtts_config & c = cfg;
+    const int NH = c.n_attention_heads, NKV = c.n_key_value_heads;
+    QkArgs qa{};
+    qa.qkv = const_cast<float *>(q); qa.ldq = ldq; qa.n_heads = NH; qa.n_kv_heads = NKV;
+    qa.q_norm = l.q_norm; qa.k_norm = l.k_norm; qa.eps = c.rms_norm_eps; qa.rope = rope;
+    qa.kc = kc_l; qa.vc = vc_l;
+    qa.pos_ptr = pos_ptr; qa.pos_static = pos_static; qa.keep_f32_k = 0; qa.done = done;
+    prof_begin(KC_OTHER, 0.0);
+    k_qk_rope_store<<<M, 32 * (NH + NKV), 0, stream>>>(qa);
+    prof_end();
+    ++launches;
+    AttnArgs aa{};
+    aa.q = q; aa.ldq = ldq; aa.kc = kc_l; aa.vc = vc_l;
+    aa.kf = q + QD(); aa.vf = q + QD() + KD(); aa.ldkv = ldq; aa.f32_mode = 0;
+    aa.n_heads = NH; aa.n_kv_heads = NKV; aa.pos_ptr = pos_ptr; aa.pos_static = pos_static;
+    aa.scale = 1.0f / sqrtf((float) QTTS_HD);
+    aa.out = out; aa.ldo = ldo; aa.done = done;
+    aa.dump = dump; aa.dump_stride = dump_stride; aa.st = st;
+    prof_begin(KC_ATTN, 0.0);
+    k_attention<<<dim3(NKV, M), ATT_THREADS, smem, stream>>>(aa);
+    prof_end();
+    ++launches;
+}
+
 bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, int ctx, const float2 * rope, float * X,
                     int M, const int * pos_ptr, int pos_static, bool f32_mode, const int * done, int ffn,
                     float * dump, int dump_layer) {
@@ -657,27 +704,8 @@ bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, in
             prof_end();
             ++launches;
         } else {
-            QkArgs qa{};
-            qa.qkv = qkv; qa.ldq = QKVD(); qa.n_heads = NH; qa.n_kv_heads = NKV;
-            qa.q_norm = l.q_norm; qa.k_norm = l.k_norm; qa.eps = c.rms_norm_eps; qa.rope = rope;
-            qa.kc = kbase + il * layer_elems; qa.vc = vbase + il * layer_elems;
-            qa.pos_ptr = pos_ptr; qa.pos_static = pos_static; qa.keep_f32_k = 0; qa.done = done;
-            prof_begin(KC_OTHER, 0.0);
-            k_qk_rope_store<<<M, 32 * (NH + NKV), 0, stream>>>(qa);
-            prof_end();
-            ++launches;
-            AttnArgs aa{};
-            aa.q = qkv; aa.ldq = QKVD(); aa.kc = qa.kc; aa.vc = qa.vc;
-            aa.kf = qkv + QD(); aa.vf = qkv + QD() + KD(); aa.ldkv = QKVD(); aa.f32_mode = 0;
-            aa.n_heads = NH; aa.n_kv_heads = NKV; aa.pos_ptr = pos_ptr; aa.pos_static = pos_static;
-            aa.scale = 1.0f / sqrtf((float) QTTS_HD);
-            aa.out = att; aa.ldo = QD(); aa.done = done;
-            aa.dump = ((int) il == dump_layer) ? dump : nullptr;
-            aa.dump_stride = ctx; aa.st = st;
-            prof_begin(KC_ATTN, 0.0);
-            k_attention<<<dim3(NKV, M), ATT_THREADS, att_smem, stream>>>(aa);
-            prof_end();
-            ++launches;
+            prefill_attention(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, qkv, QKVD(), M, pos_ptr,
+                              pos_static, done, att, QD(), ((int) il == dump_layer) ? dump : nullptr, ctx, att_smem);
         }
         if (!gemv(l.o, nullptr, att, QD(), M, nullptr, ACT_F16, X, H, X, H, EPI_RESID, nullptr, 0, done)) return false;
         if (!gemv(l.gate, &l.up, X, H, M, l.ffn_norm, ACT_F16, hbuf, ffn, nullptr, 0, EPI_SWIGLU, nullptr, 0, done))
@@ -974,22 +1002,36 @@ bool Engine::prefill(const float * rows_host, int n, int n_past, float * hidden_
     if (n <= 0) { err = "n_tokens must be > 0"; return false; }
     if (n_ctx == 0 && !init_kv(std::max(256, n_past + n + 16))) return false;
     if (n_past + n > n_ctx) { err = "Context length exceeded"; return false; }
+    // rows uploaded once; chunks of 8 rows through the GEMV path, or of up to 128
+    // rows through tcgen05 GEMMs (F16 weights; QTTS_PREFILL=gemv|tc, default tc
+    // for prompts of more than 8 rows)
+    if (n > prow_cap) {
+        if (d_prow) cudaFree(d_prow);
+        prow_cap = std::max(n, 256);
+        if (cudaMalloc(&d_prow, sizeof(float) * (size_t) prow_cap * H) != cudaSuccess) {
+            d_prow = nullptr; prow_cap = 0; err = "alloc prefill rows"; return false;
+        }
+    }
+    const char * pm = getenv("QTTS_PREFILL");
+    const bool f16w = L[0].qkv.type == W_F16;
+    const bool tc = f16w && (pm && *pm ? strcmp(pm, "tc") == 0 : n > QTTS_MAX_NV);
+    const int chunk = tc ? PREFILL_TC_ROWS : QTTS_MAX_NV;
     QCHECK(cudaEventRecord(ev0, stream));
-    for (int c0 = 0; c0 < n; c0 += QTTS_MAX_NV) {
-        const int M = std::min(QTTS_MAX_NV, n - c0);
-        QCHECK(cudaMemcpyAsync(x, rows_host + (size_t) c0 * H, sizeof(float) * M * H, cudaMemcpyHostToDevice, stream));
-        if (!layers(L, kc, vc, n_ctx, rope_t, x, M, nullptr, n_past + c0, false, nullptr, c.intermediate_size)) return false;
-        if (hidden_out) {
-            k_rmsnorm_rows<<<M, 256, 0, stream>>>(x, H, out_norm, c.rms_norm_eps, H, hid_rows, H);
-            QCHECK(cudaMemcpyAsync(hidden_out + (size_t) c0 * H, hid_rows, sizeof(float) * M * H, cudaMemcpyDeviceToHost, stream));
-        }
-        if (c0 + M == n) {
-            if (!gemv(codec_head, nullptr, x + (size_t)(M - 1) * H, H, 1, out_norm, ACT_F16, logits, c.codec_vocab_size,
-                      nullptr, 0, EPI_STORE, hidden, H, nullptr))
-                return false;
-        }
-        // the next chunk's upload overwrites x: keep the stream ordered (same stream)
-        if (c0 + M < n && !sync("prefill chunk")) return false;
+    QCHECK(cudaMemcpyAsync(d_prow, rows_host, sizeof(float) * (size_t) n * H, cudaMemcpyHostToDevice, stream));
+    for (int c0 = 0; c0 < n; c0 += chunk) {
+        const int M = std::min(chunk, n - c0);
+        float * X = d_prow + (size_t) c0 * H;
+        if (tc) { if (!prefill_tc_layers(*this, X, M, n_past + c0)) return false; }
+        else if (!layers(L, kc, vc, n_ctx, rope_t, X, M, nullptr, n_past + c0, false, nullptr, c.intermediate_size))
+            return false;
+    }
+    // last row: output norm + codec head (the GEMV writes the normed row to `hidden`)
+    if (!gemv(codec_head, nullptr, d_prow + (size_t)(n - 1) * H, H, 1, out_norm, ACT_F16, logits, c.codec_vocab_size,
+              nullptr, 0, EPI_STORE, hidden, H, nullptr))
+        return false;
+    if (hidden_out) {   // every row's hidden state, normalised in place after the head has read the last row
+        k_rmsnorm_rows<<<n, 256, 0, stream>>>(d_prow, H, out_norm, c.rms_norm_eps, H, d_prow, H);
+        QCHECK(cudaMemcpyAsync(hidden_out, d_prow, sizeof(float) * (size_t) n * H, cudaMemcpyDeviceToHost, stream));
     }
     QCHECK(cudaEventRecord(ev1, stream));
     last_hidden.resize(H);
@@ -997,6 +1039,7 @@ bool Engine::prefill(const float * rows_host, int n, int n_past, float * hidden_
     if (logits_out)
         QCHECK(cudaMemcpyAsync(logits_out, logits, sizeof(float) * c.codec_vocab_size, cudaMemcpyDeviceToHost, stream));
     if (!sync("forward_prefill")) return false;
+    if (tc && !prefill_tc_check(*this)) return false;
     cudaEventElapsedTime(&timing.prefill_ms, ev0, ev1);
     n_used = n_past + n;
     return true;
@@ -1023,6 +1066,36 @@ bool Engine::lookup(int table, const int32_t * ids, int n, std::vector<float> & 
         if (!sync("lookup_embedding_rows")) return false;
     }
     return true;
+}
+
+// Summed codec rows of n_frames reference frames ([n_frames][16] codes) into
+// out_host[n_frames][H]: one upload, one kernel, one download.
+bool Engine::icl_codec_rows(const int32_t * codes, int n_frames, float * out_host) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size, NCB = std::min(16, c.n_codebooks);
+    for (int f = 0; f < n_frames; ++f)
+        for (int cb = 0; cb < NCB; ++cb) {
+            const int id = codes[(size_t) f * 16 + cb];
+            if (id < 0 || id >= (cb == 0 ? c.codec_vocab_size : c.code_pred_vocab_size)) {
+                err = "Embedding token ID out of range"; return false;
+            }
+        }
+    if ((size_t) n_frames * 16 > (size_t) ids_cap || n_frames > prow_cap) {
+        if (d_ids) cudaFree(d_ids);
+        ids_cap = std::max(ids_cap, n_frames * 16);
+        if (cudaMalloc(&d_ids, sizeof(int) * ids_cap) != cudaSuccess) { d_ids = nullptr; ids_cap = 0; err = "alloc ids"; return false; }
+        if (n_frames > prow_cap) {
+            if (d_prow) cudaFree(d_prow);
+            prow_cap = std::max(n_frames, 256);
+            if (cudaMalloc(&d_prow, sizeof(float) * (size_t) prow_cap * H) != cudaSuccess) {
+                d_prow = nullptr; prow_cap = 0; err = "alloc prefill rows"; return false;
+            }
+        }
+    }
+    QCHECK(cudaMemcpyAsync(d_ids, codes, sizeof(int) * n_frames * 16, cudaMemcpyHostToDevice, stream));
+    k_icl_codec_rows<<<n_frames, 256, 0, stream>>>(codec_embd, d_cp_embd, d_ids, NCB, H, d_prow);
+    QCHECK(cudaMemcpyAsync(out_host, d_prow, sizeof(float) * (size_t) n_frames * H, cudaMemcpyDeviceToHost, stream));
+    return sync("lookup_embedding_rows");
 }
 
 // project_text_tokens (src/tts_transformer.cpp:963-1028) on the device.
@@ -1139,22 +1212,13 @@ bool Engine::build_prefill_icl(const qtts_generate_params * p, std::vector<float
     for (int i = ts; i < tend && i < p->n_tokens; ++i) comb.push_back(p->text_tokens[i]);
     comb.push_back(c.tts_eos_token_id);
     const int nct = p->n_ref_frames + 1;
-    std::vector<float> cf((size_t) nct * H, 0.0f), r0, r1;
+    std::vector<float> cf((size_t) nct * H, 0.0f), r0;
     int32_t cbos = c.codec_bos_id;
     if (!lookup(0, &cbos, 1, r0)) return false;
     memcpy(cf.data(), r0.data(), H * 4);
-    // per reference frame: codec_embd[cb0] then += code_pred_embd[cb-1][code], in codebook order
-    std::vector<int32_t> col((size_t) p->n_ref_frames);
-    for (int cb = 0; cb < 16 && cb < c.n_codebooks; ++cb) {
-        for (int f = 0; f < p->n_ref_frames; ++f) col[f] = p->ref_codec_tokens[(size_t) f * 16 + cb];
-        if (!lookup(cb, col.data(), p->n_ref_frames, r1)) return false;
-        for (int f = 0; f < p->n_ref_frames; ++f) {
-            float * d = cf.data() + (size_t)(f + 1) * H;
-            const float * s = r1.data() + (size_t) f * H;
-            if (cb == 0) memcpy(d, s, H * 4);
-            else for (int k = 0; k < H; ++k) d[k] += s[k];
-        }
-    }
+    // per reference frame: codec_embd[cb0] then += code_pred_embd[cb-1][code], in
+    // codebook order, summed on the device in one pass (k_icl_codec_rows)
+    if (!icl_codec_rows(p->ref_codec_tokens, p->n_ref_frames, cf.data() + H)) return false;
     const int nt = (int) comb.size();
     std::vector<float> tp;
     if (!project_text(comb.data(), nt, tp)) return false;

@@ -1191,6 +1191,21 @@ __global__ void k_gather_rows(const __half * table, int dim, const int * ids, in
         out[(size_t) r * dim + c] = __half2float(table[(size_t) ids[r] * dim + c]);
 }
 
+// ICL reference-frame codec rows (build_prefill_graph_icl, src/tts_transformer.cpp:
+// 1188-1472): row f = codec_embd[code(f, 0)], then += code_pred_embd[cb - 1]
+// [code(f, cb)] for cb = 1 .. n_cb - 1, the host loop's F32 sums in codebook
+// order.  codes: [n_frames][16].
+__global__ void k_icl_codec_rows(const __half * codec_embd, const __half * const * cp_embd, const int * codes,
+                                 int n_cb, int H, float * out) {
+    const int f = blockIdx.x;
+    const int * cf = codes + (size_t) f * 16;
+    for (int h = threadIdx.x; h < H; h += blockDim.x) {
+        float s = __half2float(codec_embd[(size_t) cf[0] * H + h]);
+        for (int cb = 1; cb < n_cb; ++cb) s = __fadd_rn(s, __half2float(cp_embd[cb - 1][(size_t) cf[cb] * H + h]));
+        out[(size_t) f * H + h] = s;
+    }
+}
+
 // y = silu(x + b) in place (text projection fc1 epilogue).
 __global__ void k_bias_silu(float * x, const float * b, int n, int ld, int rows) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * rows; i += gridDim.x * blockDim.x) {

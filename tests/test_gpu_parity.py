@@ -8,9 +8,11 @@ a mismatch unless the oracle's own top-2 gap there is below TIE_TOL.
 
 The oracle runs its reductions in the engine's order with the same exp, so the
 single-sequence engine is held to more than the contract: its frame-loop
-logits equal the oracle's bit for bit (_check_follow).  The tolerances remain
-the bar for paths with other orders (tensor-core batched path, forward_prefill's
-hidden rows).
+logits equal the oracle's bit for bit (_check_follow).  Prompts here go
+through the GEMV prefill (QTTS_PREFILL=gemv), whose order the oracle restates;
+the tolerances remain the bar for paths with other orders (the tensor-core
+prefill, tests/test_gpu_prefill_tc.py; the tensor-core batched path;
+forward_prefill's hidden rows).
 """
 from __future__ import annotations
 
@@ -25,6 +27,11 @@ pytestmark = pytest.mark.gpu
 
 TIE_TOL = 1e-3
 LOGIT_TOL = {"f16": 2e-2, "q8": 5e-2}
+
+
+@pytest.fixture(autouse=True)
+def _gemv_prefill(monkeypatch):
+    monkeypatch.setenv("QTTS_PREFILL", "gemv")
 
 
 @pytest.fixture(scope="module")
