@@ -226,26 +226,48 @@ def test_full_f16_config1_shape(qtts, full_f16):
     rng = np.random.default_rng(101)
     tgt, ref, codes, spk = icl_inputs(rng, 55)
     kw = dict(speaker=spk, ref_text=ref, ref_codes=codes, rep_penalty=1.05, temperature=0.0, top_k=0, eos_bias=-1e9)
-    e = eng.generate(tgt, 12, want_logits=True, **kw)
-    r = _check_follow(o, e, "full-f16", text=tgt, max_len=12, **kw)
-    assert r["prefill_len"] == 64
+    e = eng.generate(tgt, 32, want_logits=True, **kw)
+    r = _check_follow(o, e, "full-f16", text=tgt, max_len=32, **kw)
+    assert r["prefill_len"] == 64 and e["n_frames"] == 32
     n = e["n_frames"]
     assert np.abs(e["talker_logits"][:n] - r["talker_logits"][:n]).max() < LOGIT_TOL["f16"]
     eng.close()
 
 
 def test_full_q8_config2_shape(qtts, full_q8):
-    """BASELINE config 2 shape: Q8_0, 119 reference frames -> 128 prefill."""
+    """Q8_0, 119 reference frames -> 128 prefill, 256 greedy frames."""
     eng = qtts.Engine(full_q8, 0)
     o = Oracle(full_q8)
     rng = np.random.default_rng(102)
     tgt, ref, codes, spk = icl_inputs(rng, 119)
     kw = dict(speaker=spk, ref_text=ref, ref_codes=codes, rep_penalty=1.05, temperature=0.0, top_k=0, eos_bias=-1e9)
-    e = eng.generate(tgt, 8, want_logits=True, **kw)
-    r = _check_follow(o, e, "full-q8", text=tgt, max_len=8, **kw)
-    assert r["prefill_len"] == 128
+    e = eng.generate(tgt, 256, want_logits=True, **kw)
+    r = _check_follow(o, e, "full-q8", text=tgt, max_len=256, **kw)
+    assert r["prefill_len"] == 128 and e["n_frames"] == 256
     n = e["n_frames"]
     assert np.abs(e["talker_logits"][:n] - r["talker_logits"][:n]).max() < LOGIT_TOL["q8"]
+    eng.close()
+
+
+def test_full_f16_config3_sampled(qtts, full_f16):
+    """plain-mode voice clone with 200 text tokens (prefill 10
+    + 192 trailing rows), a unit-norm Gaussian x-vector, temperature 0.9, top-k 50,
+    repetition penalty 1.05, fixed Philox seed, 512 frames.  Every sampled code
+    (8,192 decisions) is checked against the oracle's draw with the same uniform,
+    then a greedy rerun of the same prompt."""
+    eng = qtts.Engine(full_f16, 0)
+    o = Oracle(full_f16)
+    rng = np.random.default_rng(103)
+    text = text_ids(rng, 200)
+    spk = rng.standard_normal(1024).astype(np.float32)
+    spk /= np.linalg.norm(spk)
+    kw = dict(speaker=spk, temperature=0.9, top_k=50, rep_penalty=1.05, seed=2024, eos_bias=-1e9)
+    e = eng.generate(text, 512, want_logits=True, **kw)
+    r = _check_follow(o, e, "full-f16-sampled", text=text, max_len=512, **kw)
+    assert r["prefill_len"] == 10 and e["n_frames"] == 512
+    kg = dict(kw, temperature=0.0, top_k=0)
+    g = eng.generate(text, 32, want_logits=True, **kg)
+    _check_follow(o, g, "full-f16-greedy", text=text, max_len=32, **kg)
     eng.close()
 
 
