@@ -48,6 +48,10 @@ CONFIGS = {
     "batch": dict(wtype="f16", n_utts=64, p_lo=32, p_hi=512, frames=1024,
                   workload="BASELINE configs[3]: batched F16 serving, 64 utterances, ICL prefill U[32,512], "
                            "1024 greedy frames each, paged F16 KV, tcgen05 GEMMs"),
+    "q8long": dict(wtype="q8_0", utts_per_gpu=32, p_lo=512, p_hi=512, frames=4096, e2e_frames=256,
+                   workload="BASELINE configs[4]: long-form Q8_0 serving, 32 utterances per GPU (256 on 8), "
+                            "ICL prefill 512, up to 4096 greedy frames each, paged F16 KV; Q8_0 projections as "
+                            "8-row GEMV chunks, F16 heads as tcgen05 GEMMs"),
 }
 
 
@@ -211,7 +215,9 @@ def run_reference(args, cfg):
 
 def run_batch(args, cfg):
     """the 64 utterances are LPT-sharded over the ranks; each rank
-    runs its share as one batch (one CUDA-graph frame for all its sequences)."""
+    runs its share as one batch (one CUDA-graph frame for all its sequences).
+    32 utterances per rank (weak scaling), timed over the first
+    frames of their 4096-frame budget."""
     import torch
     import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -230,8 +236,9 @@ def run_batch(args, cfg):
     from qtts_b200.scheduler import Utterance, lpt_partition
     F = cfg["frames"]
     rng = np.random.default_rng(4242)
-    P = rng.integers(cfg["p_lo"], cfg["p_hi"] + 1, cfg["n_utts"])
-    utts = [Utterance(uid=i, prefill=int(P[i]), frames=F) for i in range(cfg["n_utts"])]
+    n_utts = cfg["n_utts"] if "n_utts" in cfg else cfg["utts_per_gpu"] * world
+    P = rng.integers(cfg["p_lo"], cfg["p_hi"] + 1, n_utts)
+    utts = [Utterance(uid=i, prefill=int(P[i]), frames=F) for i in range(n_utts)]
     mine = lpt_partition(utts, world)[rank]
     eng = pkg.Engine(path, local)
     H = eng.cfg["hidden_size"]
@@ -278,16 +285,17 @@ def run_batch(args, cfg):
         ms_max, frames_all = ms, float(got)
 
     # e2e through the public API: prompts from host memory, per-sequence prefill,
-    # all F frames, codes back to the host
+    # the frames (all F, or the config's bounded e2e run), codes back to the host
+    FE = min(F, cfg.get("e2e_frames", F))
     barrier()
     torch.cuda.synchronize()
     te0 = time.perf_counter()
     bt.begin(plist)
-    bt.run(F)
+    bt.run(FE)
     codes = bt.codes()
     te = time.perf_counter() - te0
-    assert all(c.shape[0] == F for c in codes)
-    et = torch.tensor([te, float(B * F)], dtype=torch.float64, device="cuda")
+    assert all(c.shape[0] == FE for c in codes)
+    et = torch.tensor([te, float(B * FE)], dtype=torch.float64, device="cuda")
     if world > 1:
         e1 = et[:1].clone()
         dist.all_reduce(e1, op=dist.ReduceOp.MAX)
@@ -295,9 +303,9 @@ def run_batch(args, cfg):
         dist.all_reduce(e2, op=dist.ReduceOp.SUM)
         te_max, e2e_frames = float(e1.item()), float(e2.item())
     else:
-        te_max, e2e_frames = te, float(B * F)
+        te_max, e2e_frames = te, float(B * FE)
     h2d = sum(4 * (p["text"].size + p["ref_text"].size + p["ref_codes"].size + H) for p in plist)
-    d2h = 4 * B * F * 16
+    d2h = 4 * B * F * 16   # the codes buffer read back holds max_frames rows per sequence
     bt.close()
     if world > 1:
         dist.destroy_process_group()
@@ -306,27 +314,33 @@ def run_batch(args, cfg):
     peak, peak_kind = _peaks()
     frame_ms = ms_max / K
     kv_mean = float(np.mean([u.prefill for u in mine])) + W + K / 2.0
-    frame_bytes = WEIGHT_BYTES["f16"] + B * (KV_TALKER_PER_POS * kv_mean + KV_CP_PER_POS * 135)
+    wkey = "f16" if cfg["wtype"] == "f16" else "q8"
+    frame_bytes = WEIGHT_BYTES[wkey] + B * (KV_TALKER_PER_POS * kv_mean + KV_CP_PER_POS * 135)
     achieved = frame_bytes / (frame_ms / 1e3) / 1e9
-    ratio = _profile_figure("k_gemm_tc_batch16.md", "dram_bytes_per_algorithmic_byte")   # ncu, batched GEMMs
+    # ncu DRAM / algorithmic bytes of the batched projections (tcgen05 GEMMs for F16, 8-row GEMVs for Q8_0)
+    ratio = _profile_figure("k_gemm_tc_batch16.md" if wkey == "f16" else "k_gemv_q8.md", "dram_bytes_per_algorithmic_byte")
     traffic = ratio * frame_bytes if ratio else None
     flops = 2.0 * (WEIGHT_BYTES["f16"] / 2.0) * B
+    weak = "utts_per_gpu" in cfg
     line = {
         "metric": METRIC, "value": frames_all / (ms_max / 1e3), "unit": UNIT, "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": frame_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f16", "data": "synthetic (seeded random-init GGUF with the 0.6B layout; random prompts, P ~ U[32,512])",
-        "config": {"workload": cfg["workload"], "utterances": cfg["n_utts"], "batch_per_gpu": B,
+        "warmup": W, "ms_per_step": frame_ms, "higher_is_better": True, "scaling": "weak" if weak else "strong",
+        "vs_baseline": None, "dtype": "f16" if wkey == "f16" else "q8_0",
+        "data": f"synthetic (seeded random-init GGUF with the 0.6B layout; random prompts, "
+                f"P ~ U[{cfg['p_lo']},{cfg['p_hi']}])",
+        "config": {"workload": cfg["workload"], "utterances": n_utts, "batch_per_gpu": B,
                    "frames_per_utterance": F, "frames_timed_per_sequence": K,
                    "parallelism": f"LPT utterance sharding over {world} GPU(s), one batch per GPU",
                    "l2": "inputs larger than L2 (3.3 GB of weights + KV streamed per frame), no flush"},
-        "roofline": {"bound": "hbm", "kernel": "batched frame (CUDA graph: tcgen05 GEMMs + paged attention)",
+        "roofline": {"bound": "hbm", "kernel": "batched frame (CUDA graph: tcgen05 GEMMs + paged attention)" if wkey == "f16"
+                     else "batched frame (CUDA graph: Q8_0 GEMV chunks, tcgen05 heads, paged attention)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "frame_algorithmic_bytes": frame_bytes, "launches_per_frame": tm["launches_per_frame"],
                      "tensor_tflops": flops / (frame_ms / 1e3) / 1e12},
         "e2e": {"value": e2e_frames / te_max, "unit": UNIT, "h2d_bytes_per_step": h2d / (B * F),
                 "d2h_bytes_per_step": d2h / (B * F),
-                "includes": "qtts_batch_begin (prompt upload + per-sequence prefill) + all frames + codes download"},
+                "includes": f"qtts_batch_begin (prompt upload + per-sequence prefill) + {FE} frames + codes download"},
         "kernel_classes": prof,
         "gpu_launches": tm["launches_per_frame"] * K,
         "clocks": clk.summary(),
@@ -355,7 +369,7 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         return run_reference(args, cfg)
-    if args.config == "batch":
+    if args.config in ("batch", "q8long"):
         return run_batch(args, cfg)
     args.warmup = max(args.warmup, 3)
 

@@ -61,6 +61,7 @@ struct BatchEngine {
     int Bmax = 0, B = 0, n_max = 0, max_frames = 0, max_pages = 0, n_pages = 0, trail_cap = 0;
     int H = 0, NH = 0, NKV = 0, QD = 0, KD = 0, QKVD = 0, FF = 0, CFF = 0, V0 = 0, V1 = 0, NCB = 0;
     std::vector<TiledLayer> TL, TCP;
+    bool q8 = false;   // Q8_0 layer weights: projections through k_gemv in 8-row chunks (heads stay F16 tcgen05)
     std::vector<uint8_t *> cp_head_t;
     uint8_t * codec_head_t = nullptr;
     std::vector<void *> owned;
@@ -147,7 +148,8 @@ struct BatchEngine {
                     return false;
             return true;
         };
-        if (!tl(E->L, TL) || !tl(E->CPL, TCP)) return false;
+        q8 = E->L[0].qkv.type == W_Q8_0;
+        if (!q8 && (!tl(E->L, TL) || !tl(E->CPL, TCP))) return false;
         cp_head_t.resize(E->cp_head.size());
         for (size_t g = 0; g < E->cp_head.size(); ++g)
             if (!tile(E->cp_head[g], nullptr, &cp_head_t[g])) return false;
@@ -216,29 +218,74 @@ struct BatchEngine {
     }
     int gemm_cls = BC_GEMM_QKV;
 
+    // Q8_0 projection of m F32 rows: k_gemv over chunks of 8 rows (each row's
+    // int8 block dots and sums are the batch-1 GEMV's, bit for bit).
+    void gemv_rows(const DMat & A, const DMat * A2, const float * xin, int ldx, int m, const float * norm, int epi,
+                   float * y, int ldy, const float * resid) {
+        for (int r0 = 0; r0 < m; r0 += QTTS_MAX_NV) {
+            const int nv = std::min(QTTS_MAX_NV, m - r0);
+            int ncta = 0;
+            size_t slice = 0, smem = 0;
+            const GemvArgs a = E->make_gemv(A, A2, xin + (size_t) r0 * ldx, ldx, nv, norm, ACT_F16, y + (size_t) r0 * ldy,
+                                            ldy, resid ? resid + (size_t) r0 * ldy : nullptr, ldy, epi, nullptr, 0, nullptr,
+                                            &ncta, &slice, &smem);
+            pb(gemm_cls);
+            if (nv == 1) pdl_launch(k_gemv<1>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
+            else if (nv == 2) pdl_launch(k_gemv<2>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
+            else pdl_launch(k_gemv<8>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
+            pe();
+            launches += 1;
+        }
+    }
+
+    // One decoder layer's four projections over `rows` rows of X: tcgen05 GEMMs
+    // (F16) or 8-row GEMV chunks (Q8_0).  which: 0 q|k|v, 1 O (+ residual),
+    // 2 gate/up (SwiGLU), 3 down (+ residual).
+    void proj(int which, const LayerW & l, const TiledLayer & t, float * X, int rows, int ffn) {
+        const int cols_o = QD;
+        switch (which) {
+            case 0:
+                gemm_cls = BC_GEMM_QKV;
+                if (q8) gemv_rows(l.qkv, nullptr, X, H, rows, l.attn_norm, EPI_STORE, qkv, QKVD, nullptr);
+                else gemm(t.qkv, QKVD, H, X, H, rows, l.attn_norm, TC_ACT_F16, TC_EPI_STORE, qkv, QKVD, nullptr);
+                break;
+            case 1:
+                gemm_cls = BC_GEMM_O;
+                if (q8) gemv_rows(l.o, nullptr, att, cols_o, rows, nullptr, EPI_RESID, X, H, X);
+                else gemm(t.o, H, QD, nullptr, QD, rows, nullptr, TC_ACT_F16, TC_EPI_RESID, X, H, X);
+                break;
+            case 2:
+                gemm_cls = BC_GEMM_GU;
+                if (q8) gemv_rows(l.gate, &l.up, X, H, rows, l.ffn_norm, EPI_SWIGLU, hbuf, ffn, nullptr);
+                else gemm(t.gu, 2 * ffn, H, X, H, rows, l.ffn_norm, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, ffn, nullptr, nullptr, true);
+                break;
+            default:
+                gemm_cls = BC_GEMM_DOWN;
+                if (q8) gemv_rows(l.down, nullptr, hbuf, ffn, rows, nullptr, EPI_RESID, X, H, X);
+                else gemm(t.down, H, ffn, nullptr, ffn, rows, nullptr, TC_ACT_SPLIT, TC_EPI_RESID, X, H, X);
+                break;
+        }
+    }
+
     void cp_layers(int M, bool f32, int pos_static) {
         const int rows = B * M;
         for (size_t il = 0; il < E->CPL.size(); ++il) {
             const LayerW & l = E->CPL[il];
-            const TiledLayer & t = TCP[il];
-            gemm_cls = BC_GEMM_QKV;
-            gemm(t.qkv, QKVD, H, xcp, H, rows, l.attn_norm, TC_ACT_F16, TC_EPI_STORE, qkv, QKVD, nullptr);
+            const TiledLayer t = q8 ? TiledLayer{} : TCP[il];
+            proj(0, l, t, xcp, rows, CFF);
             FusedAttn fa{};
             fa.qkv = qkv; fa.ldq = QKVD; fa.n_heads = NH; fa.n_kv_heads = NKV; fa.q_norm = l.q_norm;
             fa.k_norm = l.k_norm; fa.eps = E->cfg.rms_norm_eps; fa.rope = E->rope_cp;
             fa.kc = cpk + il * cp_layer; fa.vc = cpv + il * cp_layer; fa.pos_static = pos_static; fa.M = M;
             fa.f32_mode = f32 ? 1 : 0; fa.scale = 1.0f / sqrtf((float) QTTS_HD); fa.out = att; fa.ldo = QD;
-            fa.xt = xt2; fa.xt_np = (rows + 15) / 16 * 16;
+            fa.xt = q8 ? nullptr : xt2; fa.xt_np = (rows + 15) / 16 * 16;
             pb(BC_ATTN_CP);
             pdl_launch(k_cp_attn_warp, dim3((B * NH * M + CPW_WARPS - 1) / CPW_WARPS), dim3(CPW_WARPS * 32), 0, stream, fa,
                        cp_stride, (const DevState *) st, B);
             pe();
-            gemm_cls = BC_GEMM_O;
-            gemm(t.o, H, QD, nullptr, QD, rows, nullptr, TC_ACT_F16, TC_EPI_RESID, xcp, H, xcp);
-            gemm_cls = BC_GEMM_GU;
-            gemm(t.gu, 2 * CFF, H, xcp, H, rows, l.ffn_norm, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, CFF, nullptr, nullptr, true);
-            gemm_cls = BC_GEMM_DOWN;
-            gemm(t.down, H, CFF, nullptr, CFF, rows, nullptr, TC_ACT_SPLIT, TC_EPI_RESID, xcp, H, xcp);
+            proj(1, l, t, xcp, rows, CFF);
+            proj(2, l, t, xcp, rows, CFF);
+            proj(3, l, t, xcp, rows, CFF);
             launches += 1;
         }
     }
@@ -247,24 +294,20 @@ struct BatchEngine {
         const int G = NH / NKV;
         for (size_t il = 0; il < E->L.size(); ++il) {
             const LayerW & l = E->L[il];
-            const TiledLayer & t = TL[il];
-            gemm_cls = BC_GEMM_QKV;
-            gemm(t.qkv, QKVD, H, x, H, B, l.attn_norm, TC_ACT_F16, TC_EPI_STORE, qkv, QKVD, nullptr);
+            const TiledLayer t = q8 ? TiledLayer{} : TL[il];
+            proj(0, l, t, x, B, FF);
             PagedAttnArgs pa{};
             pa.qkv = qkv; pa.ldq = QKVD; pa.n_heads = NH; pa.n_kv_heads = NKV; pa.n_layers = (int) E->L.size();
             pa.layer = (int) il; pa.q_norm = l.q_norm; pa.k_norm = l.k_norm; pa.eps = E->cfg.rms_norm_eps;
             pa.rope = rope_t; pa.pool = pool; pa.page_table = page_table; pa.max_pages = max_pages; pa.st = st;
             pa.scale = 1.0f / sqrtf((float) QTTS_HD); pa.out = att; pa.ldo = QD; pa.n_max = n_max;
-            pa.xt = xt2; pa.xt_np = (B + 15) / 16 * 16;
+            pa.xt = q8 ? nullptr : xt2; pa.xt_np = (B + 15) / 16 * 16;
             pb(BC_ATTN_TALKER);
             pdl_launch(k_attn_paged, dim3(B * NKV), dim3(PA_THREADS), paged_attn_smem(n_max, G), stream, pa);
             pe();
-            gemm_cls = BC_GEMM_O;
-            gemm(t.o, H, QD, nullptr, QD, B, nullptr, TC_ACT_F16, TC_EPI_RESID, x, H, x);
-            gemm_cls = BC_GEMM_GU;
-            gemm(t.gu, 2 * FF, H, x, H, B, l.ffn_norm, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, FF, nullptr, nullptr, true);
-            gemm_cls = BC_GEMM_DOWN;
-            gemm(t.down, H, FF, nullptr, FF, B, nullptr, TC_ACT_SPLIT, TC_EPI_RESID, x, H, x);
+            proj(1, l, t, x, B, FF);
+            proj(2, l, t, x, B, FF);
+            proj(3, l, t, x, B, FF);
             launches += 1;
         }
     }

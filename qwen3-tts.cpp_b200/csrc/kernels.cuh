@@ -234,15 +234,34 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
 
     // Q8_0: quantise the (normalised) activation once per 32-block, as
     // quantize_row_q8_0_ref: d = amax / 127, id = 1 / d, q = roundf(x * id).
+    // Eight lanes per block (four consecutive columns each, one 16-byte load
+    // from the two-plane layout), four blocks per warp pass.
     const int nb = cols / 32;
-    for (int blk = warp; blk < nv * nb; blk += nw) {
-        const int v = blk / nb, b = blk % nb;
-        const float val = xs[v * cols + xpos(b * 32 + lane, cols)];
-        const float amax = warp_max(fabsf(val));
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        qa[v * cols + b * 32 + lane] = (int8_t) roundf(__fmul_rn(val, id));
-        if (lane == 0) da[v * nb + b] = __half2float(__float2half_rn(d));
+    {
+        const int sub = lane & 7, grp = lane >> 3;
+        for (int blk0 = warp * 4; blk0 < nv * nb; blk0 += nw * 4) {
+            const int blk = blk0 + grp;
+            const bool okb = blk < nv * nb;
+            const int v = okb ? blk / nb : 0, b = okb ? blk % nb : 0;
+            const int c = b * 32 + sub * 4;
+            const float4 x4 = okb ? *reinterpret_cast<const float4 *>(xs + v * cols + xpos(c, cols))
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float am = fmaxf(fmaxf(fabsf(x4.x), fabsf(x4.y)), fmaxf(fabsf(x4.z), fabsf(x4.w)));
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+            const float d = __fdiv_rn(am, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            if (okb) {
+                char4 q;
+                q.x = (signed char) roundf(__fmul_rn(x4.x, id));
+                q.y = (signed char) roundf(__fmul_rn(x4.y, id));
+                q.z = (signed char) roundf(__fmul_rn(x4.z, id));
+                q.w = (signed char) roundf(__fmul_rn(x4.w, id));
+                *reinterpret_cast<char4 *>(qa + v * cols + c) = q;
+                if (sub == 0) da[v * nb + b] = __half2float(__float2half_rn(d));
+            }
+        }
     }
     __syncthreads();
     const uint8_t * qwa = wsm;

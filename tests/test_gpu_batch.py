@@ -24,10 +24,13 @@ def _utterances(rng, n, frames, hidden):
     return out
 
 
-@pytest.mark.parametrize("n", [1, 5])
-def test_batch_matches_oracle(qtts, tiny_f16, n):
+@pytest.mark.parametrize("which,n", [("f16", 1), ("f16", 5), ("q8", 1), ("q8", 5)])
+def test_batch_matches_oracle(qtts, request, which, n):
+    """F16: tcgen05 GEMMs.  Q8_0: the projections run as 8-row GEMV chunks (the
+    batch-1 kernel's int8 block dots), the F16 heads as tcgen05 GEMMs."""
+    path = request.getfixturevalue("tiny_f16" if which == "f16" else "tiny_q8")
     rng = np.random.default_rng(40 + n)
-    eng = qtts.Engine(tiny_f16, 0)
+    eng = qtts.Engine(path, 0)
     H = eng.cfg["hidden_size"]
     frames = 10
     utts = _utterances(rng, n, frames, H)
@@ -35,7 +38,7 @@ def test_batch_matches_oracle(qtts, tiny_f16, n):
     b.begin(utts)
     assert b.run(frames) == n * frames
     codes = b.codes()
-    o = Oracle(tiny_f16)
+    o = Oracle(path)
     for i, u in enumerate(utts):
         assert codes[i].shape == (frames, 16)
         kw = {k: v for k, v in u.items() if k not in ("text", "max_len")}
