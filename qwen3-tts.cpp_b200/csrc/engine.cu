@@ -93,7 +93,7 @@ struct Engine {
 
     // activations (rows <= QTTS_MAX_NV)
     float * x = nullptr, * xcp = nullptr, * qkv = nullptr, * att = nullptr, * hbuf = nullptr;
-    float * logits = nullptr, * cp_logits = nullptr, * hidden = nullptr, * hid_rows = nullptr;
+    float * logits = nullptr, * cp_logits = nullptr, * hidden = nullptr;
     float * logits0 = nullptr, * hidden0 = nullptr;   // prefill outputs kept for rewind
     float * tmp_a = nullptr, * tmp_b = nullptr;
     int * d_ids = nullptr;
@@ -179,11 +179,11 @@ struct Engine {
         if (ptc) { prefill_tc_free(ptc); ptc = nullptr; }
         if (d_prow) { cudaFree(d_prow); d_prow = nullptr; prow_cap = 0; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
-                         cp_logits, hidden, hid_rows, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
+                         cp_logits, hidden, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
                          dbg_t, dbg_cp, d_attn, d_prog, d_flags, d_err, d_trace, logits0, hidden0};
         for (void * p : ptrs) if (p) cudaFree(p);
         wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
-        x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = hid_rows = tmp_a = tmp_b = nullptr;
+        x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = tmp_a = tmp_b = nullptr;
         logits0 = hidden0 = nullptr;
         d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
         dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_prog = nullptr; d_flags = nullptr; d_err = nullptr;
@@ -501,7 +501,6 @@ bool Engine::alloc_activations() {
     QCHECK(cudaMalloc(&hidden, sizeof(float) * H));
     QCHECK(cudaMalloc(&logits0, sizeof(float) * c.codec_vocab_size));
     QCHECK(cudaMalloc(&hidden0, sizeof(float) * H));
-    QCHECK(cudaMalloc(&hid_rows, sizeof(float) * NV * H));
     QCHECK(cudaMalloc(&tmp_a, sizeof(float) * NV * std::max(H, c.text_embd_dim)));
     QCHECK(cudaMalloc(&tmp_b, sizeof(float) * NV * std::max(H, c.text_embd_dim)));
     QCHECK(cudaMalloc(&st, sizeof(DevState)));
