@@ -22,7 +22,9 @@
 //   * Summation orders: by default every reduction (GEMV rows, RMSNorm sums,
 //     attention scores, softmax sums, P x V) runs in the engine's order (see
 //     g_eng), so engine and oracle agree before each F16 rounding and Q8_0
-//     quantisation; ggml's own order depends on its SIMD path.
+//     quantisation; ggml's own order depends on its SIMD path.  Code-predictor
+//     steps (one row, at most 16 keys) follow the engine's one-warp-per-head
+//     attention (forward_stack's cp_step branch).
 //   * RoPE NEOX: theta_i = pos * s^i by repeated F32 multiplication,
 //     s = powf(base, -2/n_dims) (ggml_rope_cache_init).
 //   * KV caches F16; talker prefill/step and code-predictor steps read K/V from
@@ -504,7 +506,7 @@ static inline float silu(float x) { return x / (1.0f + qexpf(-x)); }
 // (code-predictor 2-token prefill).
 static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, float theta,
                           std::vector<float> & X, int M, int n_past, bool kv_from_cache,
-                          int ffn) {
+                          int ffn, bool cp_step = false) {
     const Config & c = m.c;
     const int H = c.hidden, D = c.head_dim, NH = c.n_heads, NKV = c.n_kv;
     const int QD = NH * D, KD = NKV * D;
@@ -548,6 +550,36 @@ static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, fl
                 std::vector<float> s(nk), p(nk), qh(D);
                 const float * qsrc = &q[(size_t) i * QD + h * D];
                 for (int d = 0; d < D; ++d) qh[d] = kv_from_cache ? round_f16(qsrc[d]) : qsrc[d];
+                if (g_eng && cp_step) {
+                    // the engine's code-predictor step: one warp per query head.  Key j on
+                    // lanes 2j, 2j + 1, each chaining 64 dims, the pair adding its halves;
+                    // double sum of the even lanes over the butterfly; P x V chains keys per dim.
+                    const int nkey = n_past + 1;   // <= 16
+                    std::vector<float> kf(D), e(16, 0.0f);
+                    float mx = -INFINITY;
+                    for (int j = 0; j < nkey; ++j) {
+                        const uint16_t * kj = cache.K((int) il, j) + g * D;
+                        for (int d = 0; d < D; ++d) kf[d] = h2f(kj[d]);
+                        float a0 = 0.0f, a1 = 0.0f;
+                        for (int d = 0; d < 64; ++d) a0 = fmaf(kf[d], qh[d], a0);
+                        for (int d = 64; d < 128; ++d) a1 = fmaf(kf[d], qh[d], a1);
+                        s[j] = (a0 + a1) * kq_scale;
+                        mx = std::max(mx, s[j]);
+                    }
+                    for (int j = 0; j < nkey; ++j) e[j] = qexpf(s[j] - mx);
+                    double lane[32];
+                    for (int l = 0; l < 32; ++l) lane[l] = (l & 1) ? 0.0 : (double) e[l >> 1];
+                    bfly_all_d(lane);
+                    const float inv = (float)(1.0 / lane[0]);
+                    for (int j = 0; j < nkey; ++j) p[j] = round_f16(e[j] * inv);
+                    float * out = &att[(size_t) i * QD + h * D];
+                    for (int d = 0; d < D; ++d) {
+                        float acc = 0.0f;
+                        for (int j = 0; j < nkey; ++j) acc = fmaf(p[j], h2f(cache.V((int) il, j)[g * D + d]), acc);
+                        out[d] = acc;
+                    }
+                    continue;
+                }
                 if (g_eng) {
                     // the engine's fused unit (frame steps, the code-predictor prefill, one-row
                     // prefill chunks) or its prefill kernel (chunks of 2-8 rows)
@@ -936,7 +968,8 @@ static void cp_pass(Model & m, int gen_step, const float * rows, float * logits)
     const int M = gen_step == 0 ? 2 : 1;
     const int n_past = gen_step == 0 ? 0 : gen_step + 1;
     std::vector<float> X(rows, rows + (size_t) M * H), hn(H);
-    forward_stack(m, m.CPL, m.cp_cache, m.c.cp_theta, X, M, n_past, /*kv_from_cache=*/gen_step != 0, m.c.cp_ffn);
+    forward_stack(m, m.CPL, m.cp_cache, m.c.cp_theta, X, M, n_past, /*kv_from_cache=*/gen_step != 0, m.c.cp_ffn,
+                  /*cp_step=*/gen_step != 0);
     rms_norm_in(&X[(size_t)(M - 1) * H], H, m.c.eps, f32p(m.cp_out_norm), hn.data());
     mul_mat(m.cp_head[gen_step], hn.data(), 1, logits);
 }

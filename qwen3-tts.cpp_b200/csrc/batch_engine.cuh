@@ -257,7 +257,9 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
 
 // ---- code-predictor attention for B sequences ------------------------------
 // Code-predictor attention with one warp per (sequence b, query head, row i)
-// unit: at most 17 keys, so lane j scores key j over all 128 dims (q broadcast
+// unit.  Steps (one row, keys from the cache) run cp_step_attn_body, the
+// batch-1 engine's per-head order.  The 2-token prefill (F32 K/V of the call):
+// at most 17 keys, so lane j scores key j over all 128 dims (q broadcast
 // from shared memory), the softmax is a warp reduction (max, expf, double sum,
 // e * (float)(1/sum), F16-rounded in cache mode), and lane l accumulates dims
 // 4l..4l+3 of P x V.  Arithmetic as the fused unit (per-head q/k RMSNorm,
@@ -280,6 +282,15 @@ __global__ void __launch_bounds__(CPW_WARPS * 32) k_cp_attn_warp(FusedAttn a, si
     const int b = unit / (NH * M), r = unit % (NH * M), i = r / NH, hq = r % NH, g = hq / G;
     if (st[b].done) return;
     const bool f32 = a.f32_mode != 0;
+    if (!f32 && M == 1) {   // code-predictor step: the batch-1 engine's per-head order
+        FusedAttn s = a;
+        s.qkv = a.qkv + (size_t) b * a.ldq;
+        s.kc = a.kc + (size_t) b * cache_stride;
+        s.vc = a.vc + (size_t) b * cache_stride;
+        s.out = a.out + (size_t) b * a.ldo;
+        cp_step_attn_body(s, hq, a.pos_static, b);
+        return;
+    }
     const int n_past = a.pos_static, pos = n_past + i;
     const int n = f32 ? i + 1 : n_past + 1, nc = f32 ? 0 : n_past;
     const int QD = NH * QTTS_HD, KD = NKV * QTTS_HD;

@@ -308,6 +308,7 @@ bool Engine::load(const char * path, int device) {
         return false;
     }
     if (c.n_codebooks < 2 || c.n_codebooks > QTTS_MAX_CB) { err = "n_codebooks out of range"; return false; }
+    static_assert(QTTS_MAX_CB <= CPA_MAX_KEYS, "code-predictor step attention covers every codebook position");
     if (c.codec_vocab_size > SAMPLE_THREADS * SAMPLE_PER_T || c.code_pred_vocab_size > SAMPLE_THREADS * SAMPLE_PER_T) {
         err = "vocabulary larger than 4096 is not supported"; return false;
     }
@@ -687,11 +688,23 @@ bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, in
     const int G = NH / NKV;
     const size_t layer_elems = (size_t) ctx * NKV * QTTS_HD;
     const size_t att_smem = attn_smem_bytes(f32_mode ? M : ctx, G);
+    // code-predictor steps (one row, at most 16 keys from the cache): one warp per query head
+    const bool cp_step = &Ls == &CPL && M == 1 && !f32_mode && !pos_ptr;
+    if (cp_step && pos_static + 1 > CPA_MAX_KEYS) { err = "code-predictor step beyond 16 positions"; return false; }
     for (size_t il = 0; il < Ls.size(); ++il) {
         LayerW & l = Ls[il];
         if (!gemv(l.qkv, nullptr, X, H, M, l.attn_norm, ACT_F16, qkv, QKVD(), nullptr, 0, EPI_STORE, nullptr, 0, done))
             return false;
-        if (f32_mode || M == 1) {
+        if (cp_step) {
+            FusedAttn fa = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, 1, nullptr,
+                                           pos_static, false, nullptr, ctx);
+            fa.done = done;
+            fa.warp_heads = 1;
+            prof_begin(KC_ATTN, 0.0);
+            pdl_launch(k_cp_step_attn, dim3(NH), dim3(32), 0, stream, fa);
+            prof_end();
+            ++launches;
+        } else if (f32_mode || M == 1) {
             // frame steps and the code-predictor 2-token prefill: one fused unit per (kv head, row)
             FusedAttn fa = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, M, pos_ptr,
                                            pos_static, f32_mode, ((int) il == dump_layer) ? dump : nullptr, ctx);
@@ -828,7 +841,8 @@ bool Engine::build_program() {
             op.type = P_ATTN; op.barrier = 1;
             op.a = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, M, pos_ptr, pos_static,
                                    f32, ((int) il == dump_layer) ? dump : nullptr, ctx);
-            prog_smem = std::max(prog_smem, fused_attn_smem(f32 ? M : ctx, M));
+            op.a.warp_heads = &Ls == &CPL && M == 1 && !f32 && !pos_ptr;   // code-predictor step
+            if (!op.a.warp_heads) prog_smem = std::max(prog_smem, fused_attn_smem(f32 ? M : ctx, M));
             prog.push_back(op);
             push_gemv(l.o, nullptr, att, QD(), M, nullptr, ACT_F16, X, H, X, H, EPI_RESID, nullptr, 0, 1);
             push_gemv(l.gate, &l.up, X, H, M, l.ffn_norm, ACT_F16, hbuf, ffn, nullptr, 0, EPI_SWIGLU, nullptr, 0, 1);

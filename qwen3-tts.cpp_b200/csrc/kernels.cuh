@@ -628,6 +628,7 @@ struct FusedAttn {
     const int * done;         // stand-alone launch: skip when *done
     uint8_t * xt;             // optional: output also as F16 tiles for the O-projection GEMM (row xt_row0 + i)
     int xt_np, xt_row0;
+    int warp_heads;           // code-predictor step: one warp per query head (cp_step_attn_warp)
 };
 
 constexpr int FA_THREADS = 512;
@@ -817,6 +818,125 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
         if (a.xt)
             *reinterpret_cast<__half *>(a.xt + tc_x_off(a.xt_row0 + i, hq * QTTS_HD + tid, a.xt_np)) = __float2half_rn(s);
     }
+}
+
+// Code-predictor step attention (one new row, at most 16 keys): query head hq
+// by one warp, the order the oracle restates for these steps (forward_stack's
+// cp_step branch).  The new row's q and k get the per-head RMSNorm and NEOX
+// RoPE of the fused unit; k and v are rounded to F16 and appended to the cache
+// by the group's first head.  Scores: key j belongs to lanes 2j, 2j + 1; lane
+// 2j + h chains the 64 dims [64h, 64h + 64) in dim order with fused
+// multiply-adds and the pair adds its halves.  Softmax: max, exp, a double sum
+// of the even lanes' values over the xor butterfly, p = round_f16(e * (float)(1
+// / sum)).  P x V: lane l owns dims 4l .. 4l + 3 and chains the keys in order.
+// Every global load (the q|k|v row, gains, RoPE, the cached K halves and V
+// quads) is issued before the first use; the new row's K/V stay in registers.
+constexpr int CPA_MAX_KEYS = 16;
+
+// xt_row >= 0 and a.xt set: the output row is also written as F16 tiles (row
+// xt_row) for a tcgen05 O-projection.
+__device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int hq, const int n_past,
+                                                  const int xt_row = -1) {
+    const int lane = threadIdx.x & 31;
+    const int NKV = a.n_kv_heads, G = a.n_heads / NKV, g = hq / G;
+    const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
+    const size_t pstride = (size_t) NKV * QTTS_HD;
+    const int h = lane & 1, jk = lane >> 1;
+    const float2 * rp = a.rope + (size_t) n_past * (QTTS_HD / 2);
+    const float4 q4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) hq * QTTS_HD + lane * 4);
+    const float4 k4 = *reinterpret_cast<const float4 *>(a.qkv + QD + (size_t) g * QTTS_HD + lane * 4);
+    const float4 v4 = *reinterpret_cast<const float4 *>(a.qkv + QD + KD + (size_t) g * QTTS_HD + lane * 4);
+    float gq[4], gk[4];
+    float2 cs[4];
+    head_params(a.q_norm, rp, lane, gq, cs);
+    head_params(a.k_norm, rp, lane, gk, cs);
+    uint4 kr[8];
+    {
+        const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + (size_t) jk * pstride + (size_t) g * QTTS_HD + 64 * h);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) kr[c] = jk < n_past ? kp[c] : make_uint4(0, 0, 0, 0);
+    }
+    uint2 vr[CPA_MAX_KEYS];
+    {
+        const __half * vb = a.vc + (size_t) g * QTTS_HD + lane * 4;
+#pragma unroll
+        for (int j = 0; j < CPA_MAX_KEYS; ++j)
+            vr[j] = j < n_past ? *reinterpret_cast<const uint2 *>(vb + (size_t) j * pstride) : make_uint2(0, 0);
+    }
+    float xq[4] = {q4.x, q4.y, q4.z, q4.w};
+    float xk[4] = {k4.x, k4.y, k4.z, k4.w};
+    head_norm_rope_v(xq, gq, cs, a.eps, lane);
+    head_norm_rope_v(xk, gk, cs, a.eps, lane);
+    float kn[4], vn[4];   // the new row's k, v (F16-rounded), dims 4 lane .. 4 lane + 3
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const __half kh = __float2half_rn(xk[k]), vh = __float2half_rn((&v4.x)[k]);
+        xq[k] = round_f16(xq[k]);
+        kn[k] = __half2float(kh);
+        vn[k] = __half2float(vh);
+        if (hq % G == 0) {
+            a.kc[(size_t) n_past * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = kh;
+            a.vc[(size_t) n_past * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = vh;
+        }
+    }
+    // score of key jk over dims [64h, 64h + 64): q and the new k come from lanes 16h .. 16h + 15
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const __half2 * hp = reinterpret_cast<const __half2 *>(&kr[c]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int d = 8 * c + e, src = 16 * h + (d >> 2);     // lane holding dim 64h + d
+            const float qd = __shfl_sync(0xffffffffu, xq[e & 3], src);
+            const float kd_new = __shfl_sync(0xffffffffu, kn[e & 3], src);
+            const float kd = jk < n_past ? (e & 1 ? __high2float(hp[e >> 1]) : __low2float(hp[e >> 1])) : kd_new;
+            acc = fmaf(kd, qd, acc);
+        }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    const int n = n_past + 1;
+    const float s = jk < n ? __fmul_rn(acc, a.scale) : -INFINITY;
+    const float mx = warp_max(s);
+    const float e = jk < n ? qtts_expf(__fsub_rn(s, mx)) : 0.0f;
+    const double sum = warp_sum_d(h ? 0.0 : (double) e);
+    const float p = round_f16(__fmul_rn(e, (float)(1.0 / sum)));
+    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < CPA_MAX_KEYS + 1; ++j) {
+        if (j >= n) break;
+        const float pj = __shfl_sync(0xffffffffu, p, 2 * j);
+        float v[4];
+        if (j < n_past) {
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[j < CPA_MAX_KEYS ? j : 0].x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[j < CPA_MAX_KEYS ? j : 0].y));
+            v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = vn[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = fmaf(pj, v[k], o[k]);
+    }
+    *reinterpret_cast<float4 *>(a.out + (size_t) hq * QTTS_HD + lane * 4) = make_float4(o[0], o[1], o[2], o[3]);
+    if (a.xt && xt_row >= 0) {
+        __align__(8) __half h4[4] = {__float2half_rn(o[0]), __float2half_rn(o[1]), __float2half_rn(o[2]),
+                                      __float2half_rn(o[3])};
+        *reinterpret_cast<uint2 *>(a.xt + tc_x_off(xt_row, hq * QTTS_HD + lane * 4, a.xt_np)) =
+            *reinterpret_cast<const uint2 *>(h4);
+    }
+}
+
+// The persistent kernel's call (out of line: its registers stay with the caller's).
+__device__ __noinline__ void cp_step_attn_warp(const FusedAttn & a, const int hq, const int n_past) {
+    cp_step_attn_body(a, hq, n_past);
+}
+
+// Stand-alone launch (CUDA-graph frame path): one 32-thread CTA per query head.
+__global__ void __launch_bounds__(32) k_cp_step_attn(FusedAttn a) {
+    pdl_trigger();
+    pdl_wait();
+    if (a.done && *a.done) return;
+    cp_step_attn_body(a, blockIdx.x, a.pos_static);
 }
 
 // Stand-alone launch of the fused unit (CUDA-graph frame path): one CTA per unit.

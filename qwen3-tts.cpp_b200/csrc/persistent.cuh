@@ -204,6 +204,11 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
                 }
                 case P_ATTN: {
                     const int np = op.a.pos_ptr ? pos0 + f : op.a.pos_static;
+                    if (op.a.warp_heads) {   // code-predictor step: warp 0 of CTAs 0 .. n_heads - 1
+                        if (tid < 32)
+                            for (int u = cta; u < op.a.n_heads; u += ncta) cp_step_attn_warp(op.a, u, np);
+                        break;
+                    }
                     for (int u = cta; u < op.a.n_heads * op.a.M; u += ncta) {
                         fused_attn_body(op.a, u, work, np, frame0 + f);
                         if (u + ncta < op.a.n_heads * op.a.M) __syncthreads();
