@@ -346,7 +346,7 @@ def run_batch(args, cfg):
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        fps, cores, frames, secs = cpu_frames_per_s(path, 64, args.cpu_budget_s, 16)
+        fps, cores, frames, secs = cpu_frames_per_s(path, 64, args.cpu_budget_s, 1024)
         line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
                                 "sample": f"{frames} frames of one sequence after a 64-row prefill in {secs:.1f} s "
                                           "(CPU oracle port, OpenMP over all host threads; the CPU path serves one "
@@ -511,7 +511,7 @@ def main():
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        fps, cores, frames, secs = cpu_frames_per_s(path, plen, args.cpu_budget_s, 16)
+        fps, cores, frames, secs = cpu_frames_per_s(path, plen, args.cpu_budget_s, 1024)
         line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
                                 "sample": f"{frames} frames after a {plen}-row prefill in {secs:.1f} s "
                                           "(CPU oracle port, OpenMP over all host threads)"}
