@@ -209,7 +209,7 @@ def run_reference(args, cfg):
                              "sample": f"{frames} frames (talker step + 15 code-predictor passes) after a {cfg.get('prefill', 64)}-row prefill; "
                                        "CPU oracle port (reference ggml build not buildable: ggml submodule absent)"},
             "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    emit(line)
     return 0
 
 
@@ -351,11 +351,27 @@ def run_batch(args, cfg):
                                 "sample": f"{frames} frames of one sequence after a 64-row prefill in {secs:.1f} s "
                                           "(CPU oracle port, OpenMP over all host threads; the CPU path serves one "
                                           "sequence at a time)"}
-    print(json.dumps(line))
+    emit(line)
     return 0
 
 
+_RESULT_OUT = None
+
+
+def emit(line: dict):
+    """The one JSON result line, on the process's original standard output."""
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    # Everything else a run prints (NCCL banners, library warnings) goes to
+    # stderr, so standard output carries exactly the result line.
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
@@ -515,7 +531,7 @@ def main():
         line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
                                 "sample": f"{frames} frames after a {plen}-row prefill in {secs:.1f} s "
                                           "(CPU oracle port, OpenMP over all host threads)"}
-    print(json.dumps(line))
+    emit(line)
     return 0
 
 
