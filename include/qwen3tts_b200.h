@@ -145,6 +145,13 @@ int32_t qtts_run_frames(qtts_engine * e, int32_t n, int32_t * codes_out);
  * Returns 0, or -1 with no active generation.  No counterpart in the
  * reference (benchmark and streaming-restart helper). */
 int32_t qtts_generate_rewind(qtts_engine * e);
+/* Codes -> vocoder handoff without a host copy (no reference counterpart; the
+ * reference hands codes to the decoder in host vectors, src/qwen3_tts.cpp:
+ * 271-316): *codes_dev = the engine's device buffer, frame f of the current (or
+ * last) generation at row f, [max_len][n_codebooks] int32, valid until the
+ * next generation starts; *n_frames = frames generated so far.  The pointer is
+ * on the engine's device.  Returns 0, or -1 before any generation. */
+int32_t qtts_codes_device(qtts_engine * e, const int32_t ** codes_dev, int32_t * n_frames);
 
 /* Sampling seed of the Philox stream (sampled decoding is reproducible). */
 void qtts_set_seed(qtts_engine * e, uint64_t seed);
@@ -222,9 +229,10 @@ int32_t qtts_op_sample_noalloc(int32_t device, const float * logits, int32_t V, 
 
 /* ---- batched frame loop (B independent utterances on one GPU; no reference
  * counterpart: the reference serves one sequence per TTSTransformer).
- * Every projection is a tcgen05 tensor-core GEMM over the batch rows, the
+ * Every projection of an F16 model is a tcgen05 tensor-core GEMM over the batch rows, the
  * talker KV lives in 64-position pages, and each sequence keeps its own frame
- * state.  Weights are shared with the engine (F16 models only).
+ * state.  Weights are shared with the engine (Q8_0 models: the layer
+ * projections run as 8-row GEMV chunks instead of tensor-core GEMMs).
  *   create: max_batch <= 64 sequences, max_positions = prompt + frames capacity
  *           per sequence, max_frames = codes capacity per sequence; NULL on
  *           failure (qtts_get_error(e) holds the message).
@@ -240,6 +248,10 @@ qtts_batch * qtts_batch_create(qtts_engine * e, int32_t max_batch, int32_t max_p
 int32_t qtts_batch_begin(qtts_batch * b, int32_t n, const qtts_generate_params * params);
 int32_t qtts_batch_run(qtts_batch * b, int32_t n_frames);
 int32_t qtts_batch_codes(qtts_batch * b, int32_t * codes_out, int32_t * n_frames_out);
+/* The batch's device code buffer [n][max_frames][n_codebooks] int32 (valid
+ * until the next begin) and, in n_frames_out [n], the frames each sequence has
+ * produced: the batched codes -> vocoder handoff.  0 / -1. */
+int32_t qtts_batch_codes_device(qtts_batch * b, const int32_t ** codes_dev, int32_t * n_frames_out);
 int32_t qtts_batch_timing(const qtts_batch * b, float * frames_ms, int32_t * seq_frames, int32_t * launches_per_frame);
 /* Runs n_frames frames eagerly with CUDA events around every launch (frames
  * advance as with run).  Per frame, for the 10 kernel classes (pack, GEMM

@@ -1855,6 +1855,15 @@ int32_t qtts_generate_rewind(qtts_engine * h) {
     return E.rewind();
 }
 
+int32_t qtts_codes_device(qtts_engine * h, const int32_t ** codes_dev, int32_t * n_frames) {
+    if (!h || !codes_dev) return -1;
+    ENG(h);
+    if (!E.d_codes) { E.err = "no generation has run"; return -1; }
+    *codes_dev = E.d_codes;
+    if (n_frames) *n_frames = E.sess.produced;
+    return 0;
+}
+
 int32_t qtts_generate(qtts_engine * h, const qtts_generate_params * p, qtts_frame_callback on_frame, void * user,
                       int32_t * codes_out, int32_t * n_frames_out) {
     if (!h || !p) return 0;
@@ -2030,6 +2039,13 @@ int32_t qtts_batch_codes(qtts_batch * b, int32_t * codes_out, int32_t * n_frames
     if (!b) return 0;
     cudaSetDevice(b->be.dev);
     return b->be.read_codes(codes_out, n_frames_out) ? 1 : 0;
+}
+
+int32_t qtts_batch_codes_device(qtts_batch * b, const int32_t ** codes_dev, int32_t * n_frames_out) {
+    if (!b || !codes_dev || b->be.B <= 0) return -1;
+    *codes_dev = b->be.codes;
+    if (n_frames_out) for (int i = 0; i < b->be.B; ++i) n_frames_out[i] = b->be.produced[i];
+    return 0;
 }
 
 int32_t qtts_batch_timing(const qtts_batch * b, float * frames_ms, int32_t * seq_frames, int32_t * launches_per_frame) {

@@ -101,6 +101,7 @@ def lib():
         "qtts_generate_begin": (C.c_int32, [C.c_void_p, C.POINTER(GenParams)]),
         "qtts_run_frames": (C.c_int32, [C.c_void_p, C.c_int32, _i32p]),
         "qtts_generate_rewind": (C.c_int32, [C.c_void_p]),
+        "qtts_codes_device": (C.c_int32, [C.c_void_p, C.POINTER(C.c_void_p), _i32p]),
         "qtts_set_seed": (None, [C.c_void_p, C.c_uint64]),
         "qtts_set_debug_logits": (C.c_int32, [C.c_void_p, _f32p, _f32p, C.c_int32]),
         "qtts_set_attn_dump": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32]),
@@ -114,6 +115,7 @@ def lib():
         "qtts_batch_begin": (C.c_int32, [C.c_void_p, C.c_int32, C.c_void_p]),
         "qtts_batch_run": (C.c_int32, [C.c_void_p, C.c_int32]),
         "qtts_batch_codes": (C.c_int32, [C.c_void_p, _i32p, _i32p]),
+        "qtts_batch_codes_device": (C.c_int32, [C.c_void_p, C.POINTER(C.c_void_p), _i32p]),
         "qtts_batch_timing": (C.c_int32, [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int32),
                                           C.POINTER(C.c_int32)]),
         "qtts_batch_error": (C.c_char_p, [C.c_void_p]),
@@ -338,6 +340,15 @@ class Engine:
         if lib().qtts_generate_rewind(self.h) < 0:
             raise RuntimeError("rewind failed: " + self.error())
 
+    def codes_device(self):
+        """(device address of the code buffer [max_len][n_codebooks] int32, frames
+        generated): the codes -> vocoder handoff without a host copy."""
+        ptr = C.c_void_p()
+        n = np.zeros(1, np.int32)
+        if lib().qtts_codes_device(self.h, C.byref(ptr), _p(n, C.c_int32)) < 0:
+            raise RuntimeError("codes_device failed: " + self.error())
+        return int(ptr.value or 0), int(n[0])
+
 
 def op_gemv(w, wtype: int, rows: int, cols: int, x, norm_gain=None, eps=1e-6, act_f32=False, want_block_dots=False,
             device: int = 0):
@@ -402,6 +413,15 @@ class Batch:
         if not lib().qtts_batch_codes(self.h, _p(c, C.c_int32), _p(nf, C.c_int32)):
             raise RuntimeError("batch codes failed: " + self.error())
         return [c[i, :nf[i]].copy() for i in range(self.n)]
+
+    def codes_device(self):
+        """(device address of the codes [n][max_frames][n_codebooks] int32, frames
+        per sequence): the batched codes -> vocoder handoff without a host copy."""
+        ptr = C.c_void_p()
+        nf = np.zeros(self.n, np.int32)
+        if lib().qtts_batch_codes_device(self.h, C.byref(ptr), _p(nf, C.c_int32)) < 0:
+            raise RuntimeError("batch codes_device failed: " + self.error())
+        return int(ptr.value or 0), nf
 
     BATCH_CLASSES = ["pack", "gemm_qkv", "gemm_o", "gemm_gu", "gemm_down", "gemm_head", "attn_cp", "attn_talker",
                      "sample", "other"]

@@ -64,3 +64,33 @@ def test_batch_sequence_independence(qtts, tiny_f16):
     assert np.array_equal(together[2], alone[0])
     b.close()
     eng.close()
+
+
+def test_codes_device_handoff(qtts, tiny_f16):
+    """The device code buffers (single sequence and batch) hold the codes the
+    host copies return: a GPU consumer can read them without a host round trip."""
+    import torch
+
+    class _Dev:   # a raw device int32 buffer seen through __cuda_array_interface__
+        def __init__(self, ptr, shape):
+            self.__cuda_array_interface__ = {"shape": shape, "typestr": "<i4", "data": (ptr, False), "version": 2}
+
+    rng = np.random.default_rng(90)
+    eng = qtts.Engine(tiny_f16, 0)
+    text = text_ids(rng, 20)
+    out = eng.generate(text, 7, eos_bias=-1e9)
+    ptr, n = eng.codes_device()
+    assert n == 7 and ptr != 0
+    dev = torch.as_tensor(_Dev(ptr, (n, 16)), device="cuda").cpu().numpy()
+    assert np.array_equal(dev, out["codes"])
+    utts = _utterances(rng, 3, 5, eng.cfg["hidden_size"])
+    b = qtts.engine.Batch(eng, max_batch=4, max_positions=256, max_frames=5)
+    b.begin(utts)
+    b.run(5)
+    host = b.codes()
+    bptr, nf = b.codes_device()
+    allc = torch.as_tensor(_Dev(bptr, (3, 5, 16)), device="cuda").cpu().numpy()
+    for i in range(3):
+        assert nf[i] == 5 and np.array_equal(allc[i, :nf[i]], host[i])
+    b.close()
+    eng.close()
