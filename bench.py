@@ -163,20 +163,34 @@ def _profile_figure(fname: str, key: str):
     return None
 
 
-def cpu_frames_per_s(path: str, n_ref_prefill: int, budget_s: float, max_frames: int):
-    """The CPU oracle port on all host cores: frames after a prefill of the same length."""
+def cpu_model() -> str:
+    """The host CPU's model name (for the CPU baseline's record)."""
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_frames_per_s(path: str, n_ref_prefill: int, budget_s: float, max_frames: int, warmup: int = 0):
+    """The CPU oracle port on all host cores: frames after a prefill of the same
+    length; `warmup` untimed frames first."""
     from oracle import Oracle, available_cpus
     cores = available_cpus()
     o = Oracle(path, threads=cores, engine_order=False)
     H = o.cfg["hidden"]
     rng = np.random.default_rng(7)
     rows = (rng.standard_normal((n_ref_prefill, H)) * 0.1).astype(np.float32)
-    o.init_kv(n_ref_prefill + max_frames + 16)
+    o.init_kv(n_ref_prefill + warmup + max_frames + 16)
     hid, lg = o.forward_prefill(rows)
     hidden = hid[-1]
     pos, frames, t_used = n_ref_prefill, 0, 0.0
     cb0 = int(np.argmax(lg[:2048]))
+    done_warm = 0
     while frames < max_frames and t_used < budget_s:
+        warm = done_warm < warmup
         t0 = time.perf_counter()
         codes, _ = o.predict_codes(hidden, cb0)
         step = o.lookup(0, [cb0])[0]
@@ -184,8 +198,11 @@ def cpu_frames_per_s(path: str, n_ref_prefill: int, budget_s: float, max_frames:
             step = step + o.lookup(g + 1, [int(codes[g])])[0]
         lg, hidden = o.forward_step(step, pos)
         cb0 = int(np.argmax(lg[:2048]))
-        t_used += time.perf_counter() - t0
         pos += 1
+        if warm:
+            done_warm += 1
+            continue
+        t_used += time.perf_counter() - t0
         frames += 1
     return frames / t_used, cores, frames, t_used
 
@@ -197,15 +214,14 @@ def run_reference(args, cfg):
     if rank != 0:
         return 0
     pkg, path = _model(cfg, 0, 0, lambda: None)
-    for _ in range(max(0, args.warmup)):
-        pass
-    fps, cores, frames, secs = cpu_frames_per_s(path, cfg.get("prefill", 64), budget_s=1e9, max_frames=args.steps)
+    fps, cores, frames, secs = cpu_frames_per_s(path, cfg.get("prefill", 64), budget_s=1e9, max_frames=args.steps,
+                                                warmup=max(0, args.warmup))
     line = {"impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": args.gpus,
             "steps": frames, "warmup": args.warmup, "ms_per_step": 1000.0 * secs / max(frames, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16" if cfg["wtype"] == "f16" else "q8_0", "data": "synthetic (seeded random-init GGUF, 0.6B layout)",
             "config": {"workload": cfg["workload"], "l2": "inputs larger than L2 (weights streamed every frame)"},
-            "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
                              "sample": f"{frames} frames (talker step + 15 code-predictor passes) after a {cfg.get('prefill', 64)}-row prefill; "
                                        "CPU oracle port (reference ggml build not buildable: ggml submodule absent)"},
             "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -346,8 +362,8 @@ def run_batch(args, cfg):
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        fps, cores, frames, secs = cpu_frames_per_s(path, 64, args.cpu_budget_s, 1024)
-        line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+        fps, cores, frames, secs = cpu_frames_per_s(path, 64, args.cpu_budget_s, 1024, warmup=2)
+        line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
                                 "sample": f"{frames} frames of one sequence after a 64-row prefill in {secs:.1f} s "
                                           "(CPU oracle port, OpenMP over all host threads; the CPU path serves one "
                                           "sequence at a time)"}
@@ -527,8 +543,8 @@ def main():
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
-        fps, cores, frames, secs = cpu_frames_per_s(path, plen, args.cpu_budget_s, 1024)
-        line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+        fps, cores, frames, secs = cpu_frames_per_s(path, plen, args.cpu_budget_s, 1024, warmup=2)
+        line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
                                 "sample": f"{frames} frames after a {plen}-row prefill in {secs:.1f} s "
                                           "(CPU oracle port, OpenMP over all host threads)"}
     emit(line)
