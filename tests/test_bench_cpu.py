@@ -59,3 +59,5 @@ def test_cpu_baseline_warmup_and_budget(tiny_f16):
     fps2, _, frames2, secs2 = bench.cpu_frames_per_s(tiny_f16, 13, budget_s=0.2, max_frames=100000)
     assert 1 <= frames2 < 100000 and secs2 >= 0.2 and fps2 > 0
     assert bench.cpu_model()
+    fps3, _, frames3, _ = bench.cpu_frames_per_s(tiny_f16, 13, budget_s=1e9, max_frames=9, warmup=1, windows=3)
+    assert frames3 == 9 and fps3 > 0   # three windows of three frames, median rate
