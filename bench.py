@@ -36,7 +36,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "codec frames/s"
 UNIT = "frames/s"
-# SURVEY 8d algorithmic bytes per frame per sequence (weights); KV added per frame below.
+# Algorithmic bytes per frame per sequence: every weight byte of the talker step and
+# of the 15 code-predictor passes once; KV added per frame below.
 WEIGHT_BYTES = {"f16": 3_309_305_856, "q8": 1_790_509_056}
 KV_TALKER_PER_POS = 114_688      # 28 layers x (K+V) x 8 heads x 128 x 2 B
 KV_CP_PER_POS = 20_480           # 5 layers x (K+V) x 8 x 128 x 2 B
@@ -222,6 +223,14 @@ def cpu_frames_per_s(path: str, n_ref_prefill: int, budget_s: float, max_frames:
     return frames / t_used, cores, frames, t_used
 
 
+def frames_config(cfg, args, world, plen, K, F):
+    """The `config` of a batch-1 line; the reference arm reports the same dict."""
+    return {"workload": cfg["workload"], "batch_per_gpu": 1, "prefill": plen, "frames_per_utterance": F,
+            "utterance_replays": (K + F - 1) // F, "frames_timed": K,
+            "parallelism": f"independent utterance per GPU x{world}",
+            "l2": "inputs larger than L2 (3.3 GB of weights streamed per frame), no flush"}
+
+
 def run_reference(args, cfg):
     """Reference arm: the CPU port of the path (the reference's ggml build is not
     buildable: its ggml submodule is empty), rank 0 only, all host cores."""
@@ -235,7 +244,7 @@ def run_reference(args, cfg):
             "steps": frames, "warmup": args.warmup, "ms_per_step": 1000.0 * secs / max(frames, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16" if cfg["wtype"] == "f16" else "q8_0", "data": "synthetic (seeded random-init GGUF, 0.6B layout)",
-            "config": {"workload": cfg["workload"], "l2": "inputs larger than L2 (weights streamed every frame)"},
+            "config": frames_config(cfg, args, args.gpus, cfg.get("prefill", 64), frames, cfg.get("frames", 32)),
             "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
                              "sample": f"{frames} frames (talker step + 15 code-predictor passes) after a {cfg.get('prefill', 64)}-row prefill; "
                                        "CPU oracle port (reference ggml build not buildable: ggml submodule absent)"},
@@ -387,6 +396,56 @@ def run_batch(args, cfg):
     return 0
 
 
+def run_ncu_workload(args):
+    """A small fixed workload for ncu captures (no timing, no JSON line):
+    `frames`: the config's ICL prefill and --frames frames through the frame
+    loop (QTTS_FRAME_MODE selects graph or persistent); `batch`: --batch
+    utterances with 64-position ICL prompts, --frames batched frames, then two
+    eagerly profiled frames.  A few GB on the device at most."""
+    pkg = _pkg()
+    d = os.environ.get("QTTS_MODEL_DIR", os.path.join(ROOT, ".models"))
+    cfg_m = pkg.synth_gguf.TINY if args.tiny else pkg.synth_gguf.FULL
+    if args.ncu_workload == "frames":
+        wtype = "f16" if args.config == "f16" else "q8_0"
+        path = pkg.synth_gguf.ensure_gguf(d, cfg_m, wtype, seed=0)
+        eng = pkg.Engine(path, 0)
+        rng = np.random.default_rng(1000)
+        n_ref = CONFIGS[args.config].get("n_ref", 55)
+        tgt = rng.integers(0, 151643, 24).astype(np.int32)
+        ref = rng.integers(0, 151643, 30).astype(np.int32)
+        codes = rng.integers(0, 2048, (n_ref, 16)).astype(np.int32)
+        spk = rng.standard_normal(cfg_m.hidden).astype(np.float32)
+        eng.generate_begin(tgt, args.frames, speaker=spk, ref_text=ref, ref_codes=codes, rep_penalty=1.05,
+                           temperature=0.0, top_k=0, eos_bias=-1e9)
+        got = eng.run_frames(args.frames)
+        print(f"frames={got} {eng.timing()}", file=sys.stderr)
+        eng.close()
+        return 0
+    path = pkg.synth_gguf.ensure_gguf(d, cfg_m, "f16", seed=0)
+    eng = pkg.Engine(path, 0)
+    H = eng.cfg["hidden_size"]
+    frames = args.frames + 2
+    utts = []
+    for i in range(args.batch):
+        r = np.random.default_rng(2000 + i)
+        utts.append(dict(text=r.integers(0, 151643, 24).astype(np.int32), max_len=frames,
+                         speaker=r.standard_normal(H).astype(np.float32),
+                         ref_text=r.integers(0, 151643, 30).astype(np.int32),
+                         ref_codes=r.integers(0, 2048, (55, 16)).astype(np.int32),
+                         rep_penalty=1.05, eos_bias=-1e9))
+    bt = pkg.engine.Batch(eng, max_batch=args.batch, max_positions=64 + frames + 1, max_frames=frames)
+    bt.begin(utts)
+    got = bt.run(args.frames)
+    prof = bt.profile(2)
+    print(f"batch={args.batch} sequence-frames={got} {bt.timing()}", file=sys.stderr)
+    for k, v in prof.items():
+        print(f"{k:12s} {v['launches_per_frame']:5d} launches/frame  {v['ms_per_frame']:8.3f} ms/frame (eager)",
+              file=sys.stderr)
+    bt.close()
+    eng.close()
+    return 0
+
+
 _RESULT_OUT = None
 
 
@@ -413,7 +472,14 @@ def main():
     ap.add_argument("--profile-frames", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-workload", choices=["frames", "batch"], default=None,
+                    help="run a small fixed workload for ncu captures instead of the benchmark")
+    ap.add_argument("--frames", type=int, default=2, help="--ncu-workload: frames to run")
+    ap.add_argument("--batch", type=int, default=16, help="--ncu-workload batch: utterances")
+    ap.add_argument("--tiny", action="store_true", help="--ncu-workload: the 2-layer test model")
     args = ap.parse_args()
+    if args.ncu_workload:
+        return run_ncu_workload(args)
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         return run_reference(args, cfg)
@@ -447,7 +513,7 @@ def main():
     # one persistent launch (or F graph launches).
     F = cfg["frames"]
     reps = max(1, (K + F - 1) // F)
-    K = reps * F
+    runs = [min(F, K - i * F) for i in range(reps)]   # whole replays, then the remainder of a partial one
     with ClockSampler(local) as clk:
         plen = eng.generate_begin(tgt, F, **gen)
         assert plen == cfg["prefill"], plen
@@ -459,9 +525,9 @@ def main():
         torch.cuda.synchronize()
         clk.mark_start()
         got = 0
-        for _ in range(reps):
+        for n in runs:
             eng.generate_rewind()
-            got += eng.run_frames(F)
+            got += eng.run_frames(n)
         barrier()
         torch.cuda.synchronize()
         clk.mark_end()
@@ -485,9 +551,9 @@ def main():
     barrier()
     torch.cuda.synchronize()
     t_e0 = time.perf_counter()
-    for _ in range(reps):
-        out = eng.generate(tgt, F, **gen)
-        assert out["n_frames"] == F
+    for n in runs:
+        out = eng.generate(tgt, n, **gen)
+        assert out["n_frames"] == n
     t_e = time.perf_counter() - t_e0
     et = torch.tensor([t_e], dtype=torch.float64, device="cuda")
     if world > 1:
@@ -499,7 +565,7 @@ def main():
     # codec row per reference frame (the reference codes go up once, counted above)
     n_lookup_rows = 3 + 2 + 1 + cfg["n_ref"]
     h2d_utt = (4 * (len(tgt) + len(ref) + codes.size) + 4 * H * (plen + 1) + 4 * n_text_rows + 4 * 6)
-    d2h_utt = 4 * H * (n_text_rows + n_lookup_rows) + 4 * 16 * F + 4 * H + 1024 * ((F + 15) // 16)
+    d2h_all = sum(4 * H * (n_text_rows + n_lookup_rows) + 4 * 16 * n + 4 * H + 1024 * ((n + 15) // 16) for n in runs)
 
     if world > 1:
         dist.destroy_process_group()
@@ -515,30 +581,30 @@ def main():
     prof_total = sum(prof[c]["ms"] for c in ("gemv", "attention", "sample", "other"))
     persistent = launches_per_frame == 1
     if persistent:
-        # one cooperative launch runs the F frames of a replay: bytes per launch = F frames of weights + KV
-        kernel = f"k_frame_persistent (one cooperative launch per utterance replay of {F} frames)"
-        bytes_per_launch = frame_bytes * F
+        # one cooperative launch runs the frames of a replay: bytes per launch = those frames' weights + KV,
+        # duration = the timed region / launches (CUDA events on the engine stream)
+        kernel = f"{eng.frame_kernel()} (one cooperative launch per utterance replay of up to {F} frames)"
+        bytes_per_launch = frame_bytes * K / reps
         achieved = bytes_per_launch / (ms_max / reps / 1e3) / 1e9
-        tpf = _profile_figure(f"k_frame_persistent_{args.config}.md", "dram_bytes_per_frame")
-        traffic = tpf * F if tpf else None
-        launches_per_frame_k = 1.0 / F
+        tpf = _profile_figure(f"{eng.frame_kernel()}_{args.config}.md", "dram_bytes_per_frame")
+        traffic = tpf * K / reps if tpf else None
+        launches_per_frame_k = reps / K
     else:
-        kernel = "k_gemv (all GEMV launches of a frame, eager replay)"
-        bytes_per_launch = g["bytes"] / max(g["launches"], 1)
-        achieved = gemv_gbs
-        # ncu: DRAM bytes per algorithmic byte over captured frame GEMVs, times this run's mean launch
+        # the timed path: the frame CUDA graph; its launches overlap under programmatic dependent
+        # launch, so the unit is the frame (algorithmic bytes of a frame / device time per frame)
+        kernel = f"frame CUDA graph ({launches_per_frame} launches per frame, programmatic dependent launch)"
+        bytes_per_launch = frame_bytes
+        achieved = frame_bytes / (frame_ms / 1e3) / 1e9
+        # ncu: DRAM bytes per algorithmic byte over captured frame GEMVs (the graph's bytes are GEMV weights)
         ratio = _profile_figure(f"k_gemv_{args.config}.md", "dram_bytes_per_algorithmic_byte")
-        traffic = ratio * bytes_per_launch if ratio else None
-        launches_per_frame_k = g["launches"] / max(prof["frames"], 1)
+        traffic = ratio * frame_bytes if ratio else None
+        launches_per_frame_k = float(launches_per_frame)
     line = {
         "metric": METRIC, "value": world * K / (ms_max / 1e3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": frame_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16" if args.config == "f16" else "q8_0",
         "data": "synthetic (seeded random-init GGUF with the 0.6B layout; random prompt ids and reference codes)",
-        "config": {"workload": cfg["workload"], "batch_per_gpu": 1, "prefill": plen, "frames_per_utterance": F,
-                   "utterance_replays": reps, "frames_timed": K,
-                   "parallelism": f"independent utterance per GPU x{world}",
-                   "l2": "inputs larger than L2 (3.3 GB of weights streamed per frame), no flush"},
+        "config": frames_config(cfg, args, world, plen, K, F),
         "roofline": {"bound": "hbm", "kernel": kernel,
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None, "traffic": traffic,
@@ -547,14 +613,15 @@ def main():
                      "launches_per_frame": launches_per_frame_k,
                      "frame_algorithmic_bytes": frame_bytes,
                      "frame_algorithmic_gbs": frame_bytes / (frame_ms / 1e3) / 1e9,
-                     "eager_gemv_gbs": gemv_gbs,
-                     "eager_gemv_share": g["ms"] / prof_total if prof_total else None},
+                     "eager_gemv_gbs_serialised": gemv_gbs,
+                     "eager_gemv_share_serialised": g["ms"] / prof_total if prof_total else None},
         "kernel_classes": {c: {"launches_per_frame": prof[c]["launches"] / max(prof["frames"], 1),
                                "ms_per_frame": prof[c]["ms"] / max(prof["frames"], 1)}
                            for c in ("gemv", "attention", "sample", "other")},
-        "e2e": {"value": world * K / t_e, "unit": UNIT, "h2d_bytes_per_step": h2d_utt / F,
-                "d2h_bytes_per_step": d2h_utt / F,
-                "includes": f"{reps} x qtts_generate of {F} frames: prompt upload, prefill, frames, codes download"},
+        "e2e": {"value": world * K / t_e, "unit": UNIT, "h2d_bytes_per_step": h2d_utt * reps / K,
+                "d2h_bytes_per_step": d2h_all / K,
+                "includes": f"{reps} x qtts_generate ({'+'.join(str(n) for n in runs)} frames): prompt upload, "
+                            "prefill, frames, codes download"},
         "gpu_launches": reps if persistent else launches_per_frame * K,
         "clocks": clk.summary(),
     }

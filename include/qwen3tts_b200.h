@@ -217,8 +217,11 @@ int32_t qtts_op_sample(int32_t device, const float * logits, int32_t V, int32_t 
  * __device__ array inside the library (every GPU that loads the library holds
  * it until exit), so V is limited to 4096: larger vocabularies return -2 with
  * a message on stderr.  No cudaMalloc, cudaFree or allocating routine is
- * called.  The first call on a device looks up the array's device address
- * (with that device current) and should happen before any stream capture.
+ * called by the entry point itself.  The first call on a device looks up the
+ * array's device address (with that device current) and makes the sampler's
+ * kernel resident: under CUDA's lazy module loading that first call may load
+ * the module, which allocates device memory and can synchronise.  Make one
+ * call per device outside the real-time loop, before any stream capture.
  * All calls share the array: the kernel clears the state it reads at every
  * call, and calls that overlap on the GPU (concurrent streams) race.
  * Returns 1 on a successful launch, 0 on invalid arguments or a CUDA error. */

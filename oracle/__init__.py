@@ -112,6 +112,10 @@ class Oracle:
             L.orc_sample.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_float, C.c_int, C.c_double]
             L.orc_forward_talker_rows.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.c_int, C.c_int]
             L.orc_set_threads.argtypes = [C.c_int]
+            L.orc_set_attn_dump.restype = None
+            L.orc_set_attn_dump.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
+            L.orc_attn_rows.restype = C.c_int
+            L.orc_attn_rows.argtypes = []
             L.orc_set_engine_order.argtypes = [C.c_int]
             L.orc_expf.restype = C.c_float
             L.orc_expf.argtypes = [C.c_float]
@@ -134,6 +138,21 @@ class Oracle:
         n = L.orc_config(self.h, iv, fv)
         self.cfg = dict(zip(CONFIG_KEYS, list(iv)[:n]))
         self.cfg.update(eps=fv[0], theta=fv[1], cp_theta=fv[2])
+
+    def generate_with_attn_dump(self, layer: int, stride: int, max_rows: int, **kw):
+        """generate(**kw) while recording the post-softmax rows of talker layer
+        `layer` at every decode step: returns (generate's result, rows
+        [n][n_heads][stride], zero beyond each row's key count)."""
+        nh = self.cfg["n_heads"]
+        buf = np.zeros((max_rows, nh, stride), np.float32)
+        L = self.lib()
+        L.orc_set_attn_dump(buf.ctypes.data_as(C.c_void_p), max_rows, stride, layer)
+        try:
+            r = self.generate(**kw)
+            n = L.orc_attn_rows()
+        finally:
+            L.orc_set_attn_dump(None, 0, 0, -1)
+        return r, buf[:n].copy()
 
     def close(self):
         if self.h:

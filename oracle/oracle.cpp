@@ -504,6 +504,20 @@ static inline float silu(float x) { return x / (1.0f + qexpf(-x)); }
 // kv_from_cache: attention reads F16 K/V from the cache (talker graphs and the
 // code-predictor step graph); otherwise attends over F32 Kcur/Vcur of this call
 // (code-predictor 2-token prefill).
+// Attention dump (set_attn_dump / write_attn_dump, src/tts_transformer.cpp:2978-3005
+// and the attn_rows capture in build_step_graph): the post-softmax row of one
+// talker layer per decode step, [row][n_heads][stride], before the F16
+// rounding that feeds P x V.  Filled by talker steps (orc_forward_step) only.
+static float * g_attn_buf = nullptr;
+static int g_attn_cap = 0, g_attn_stride = 0, g_attn_layer = -1, g_attn_rows = 0;
+static bool g_talker_step = false;
+
+static void attn_dump_row(int il, int h, int NH, const float * p, int n) {
+    if (!g_attn_buf || !g_talker_step || il != g_attn_layer || g_attn_rows >= g_attn_cap) return;
+    float * row = g_attn_buf + ((size_t) g_attn_rows * NH + h) * g_attn_stride;
+    for (int j = 0; j < n && j < g_attn_stride; ++j) row[j] = p[j];
+}
+
 static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, float theta,
                           std::vector<float> & X, int M, int n_past, bool kv_from_cache,
                           int ffn, bool cp_step = false) {
@@ -625,8 +639,10 @@ static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, fl
                     for (int j = 0; j < nkey; ++j) {
                         const float inv = (float)(1.0 / lane[j & 31]);
                         p[j] = p[j] * inv;
-                        if (kv_from_cache) p[j] = round_f16(p[j]);
                     }
+                    if (M == 1) attn_dump_row((int) il, h, NH, p.data(), nkey);
+                    if (kv_from_cache)
+                        for (int j = 0; j < nkey; ++j) p[j] = round_f16(p[j]);
                     const int npg = fused ? 8 : 4;
                     float * out = &att[(size_t) i * QD + h * D];
                     for (int d = 0; d < D; ++d) {
@@ -668,6 +684,7 @@ static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, fl
                 for (int j = 0; j < nk; ++j) { float e = qexpf(s[j] - mx); p[j] = e; sum += (double) e; }
                 const float inv = (float)(1.0 / sum);
                 for (int j = 0; j < nk; ++j) p[j] *= inv;
+                if (M == 1) attn_dump_row((int) il, h, NH, p.data(), nk);
                 float * out = &att[(size_t) i * QD + h * D];
                 for (int d = 0; d < D; ++d) out[d] = 0.0f;
                 for (int j = 0; j < nk; ++j) {
@@ -800,6 +817,12 @@ struct orc_gen_result {
 };
 
 void orc_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
+// Attention dump of talker layer `layer` for the following decode steps: row r
+// of buf [cap][n_heads][stride] holds step r's post-softmax rows (nullptr: off).
+void orc_set_attn_dump(float * buf, int cap, int stride, int layer) {
+    g_attn_buf = buf; g_attn_cap = cap; g_attn_stride = stride; g_attn_layer = layer; g_attn_rows = 0;
+}
+int orc_attn_rows() { return g_attn_rows; }
 // 1 (default): every reduction in the engine's order; 0: plain sequential / AVX2 orders.
 void orc_set_engine_order(int on) { g_eng = on != 0; }
 float orc_expf(float x) { return qexpf(x); }
@@ -954,7 +977,10 @@ int orc_forward_step(void * h, const float * embd, int n_past, float * logits_ou
     if (n_past + 1 > m.cache.n_ctx) return -1;
     const int H = m.c.hidden;
     std::vector<float> X(embd, embd + H);
+    g_talker_step = true;
     forward_stack(m, m.L, m.cache, m.c.theta, X, 1, n_past, true, m.c.ffn);
+    g_talker_step = false;
+    if (g_attn_buf && g_attn_layer >= 0 && g_attn_layer < (int) m.L.size() && g_attn_rows < g_attn_cap) ++g_attn_rows;
     m.last_hidden.resize(H);
     rms_norm_in(X.data(), H, m.c.eps, f32p(m.out_norm), m.last_hidden.data());
     if (hidden_out) memcpy(hidden_out, m.last_hidden.data(), H * 4);

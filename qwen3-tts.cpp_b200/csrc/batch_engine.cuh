@@ -446,7 +446,11 @@ __global__ void k_inputs_batch(BatchInputArgs a) {
     }
 }
 
-__global__ void k_frame_end_batch(DevState * st, int B) {
+// End of a batched frame: every live sequence advances one position.  A
+// sequence that has emitted its max_len frames stops here (done = 1), so its
+// position never passes the prompt + max_len rows its pages and RoPE rows were
+// sized for, and its code rows stay inside the max_frames buffer.
+__global__ void k_frame_end_batch(DevState * st, int B, const int * max_len) {
     pdl_trigger();
     pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -454,6 +458,7 @@ __global__ void k_frame_end_batch(DevState * st, int B) {
         st[b].pos += 1;
         st[b].frame += 1;
         st[b].n_out += 1;
+        if (st[b].n_out >= max_len[b]) st[b].done = 1;
     }
 }
 

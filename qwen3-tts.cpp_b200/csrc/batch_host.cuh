@@ -71,6 +71,8 @@ struct BatchEngine {
     DevState * st = nullptr;
     SampleParams * sp = nullptr;
     int * codes = nullptr, * page_table = nullptr, * d_err = nullptr;
+    int * d_max_len = nullptr;              // per-sequence frame budget (k_frame_end_batch stops a sequence there)
+    std::vector<int> max_len;
     __half * pool = nullptr, * cpk = nullptr, * cpv = nullptr;
     float2 * rope_t = nullptr;
     size_t cp_stride = 0, cp_layer = 0;
@@ -163,7 +165,8 @@ struct BatchEngine {
             !alloc(&pad, sizeof(float) * H) || !alloc(&xt, (size_t) TC_MAX_N * maxc * 2) ||
             !alloc(&xt2, (size_t) TC_MAX_N * maxc * 2) ||
             !alloc(&st, sizeof(DevState) * Bmax) || !alloc(&sp, sizeof(SampleParams)) ||
-            !alloc(&codes, sizeof(int) * Bmax * max_frames * NCB) || !alloc(&d_err, sizeof(int)))
+            !alloc(&codes, sizeof(int) * Bmax * max_frames * NCB) || !alloc(&d_err, sizeof(int)) ||
+            !alloc(&d_max_len, sizeof(int) * Bmax))
             return false;
         trail_cap = 1024;
         if (!alloc(&trail, sizeof(float) * Bmax * trail_cap * H)) return false;
@@ -348,7 +351,7 @@ struct BatchEngine {
         talker_layers();
         gemm_cls = BC_GEMM_HEAD;
         gemm(codec_head_t, V0, H, x, H, B, E->out_norm, TC_ACT_F16, TC_EPI_STORE, logits, V0, nullptr, hidden);
-        pdl_launch(k_frame_end_batch, dim3((B + 127) / 128), dim3(128), 0, stream, st, B);
+        pdl_launch(k_frame_end_batch, dim3((B + 127) / 128), dim3(128), 0, stream, st, B, (const int *) d_max_len);
         launches += 5;
     }
 
@@ -369,8 +372,10 @@ struct BatchEngine {
         if (n < 1 || n > Bmax) { err = "batch size out of range"; return -1; }
         const qtts_config & c = E->cfg;
         std::vector<DevState> hs(n);
+        max_len.assign(n, 0);
         for (int b = 0; b < n; ++b) {
-            if (ps[b].max_len > max_frames) { err = "max_len exceeds the batch's max_frames"; return -1; }
+            if (ps[b].max_len < 1 || ps[b].max_len > max_frames) { err = "max_len must be in [1, max_frames]"; return -1; }
+            max_len[b] = ps[b].max_len;
             if (E->begin(&ps[b]) < 0) { err = "prefill of sequence " + std::to_string(b) + ": " + E->err; return -1; }
             const int plen = E->sess.prefill_len, tlen = E->sess.trailing_len;
             if (plen + ps[b].max_len + 1 > n_max) { err = "prompt + max_len exceeds max_positions"; return -1; }
@@ -394,6 +399,7 @@ struct BatchEngine {
             E->sess.active = false;
         }
         if (cudaMemcpy(st, hs.data(), sizeof(DevState) * n, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(d_max_len, max_len.data(), sizeof(int) * n, cudaMemcpyHostToDevice) != cudaSuccess ||
             cudaMemset(d_err, 0, sizeof(int)) != cudaSuccess) {
             err = "batch state"; return -1;
         }
@@ -406,9 +412,14 @@ struct BatchEngine {
         return 0;
     }
 
-    // Runs up to n frames for the whole batch (stops early when every sequence is done).
+    // Runs up to n frames for the whole batch (stops early when every sequence is
+    // done).  n is clamped to the largest remaining budget (max_len - produced);
+    // sequences with smaller budgets stop on the device at their own max_len.
     int run(int n) {
         if (B <= 0) { err = "no active batch"; return -1; }
+        int left = 0;
+        for (int b = 0; b < B; ++b) left = std::max(left, max_len[b] - produced[b]);
+        n = std::max(0, std::min(n, left));
         if (cudaEventRecord(ev0, stream) != cudaSuccess) { err = "event"; return -1; }
         for (int i = 0; i < n; ++i)
             if (cudaGraphLaunch(graph, stream) != cudaSuccess) { err = "graph launch"; return -1; }

@@ -1637,7 +1637,13 @@ int32_t qtts_op_sample_noalloc(int32_t device, const float * logits, int32_t V, 
     {
         std::lock_guard<std::mutex> lk(g_scratch_mu);
         if (!g_scratch_ptr[device]) {
-            if (cudaGetSymbolAddress(&g_scratch_ptr[device], g_sample_scratch) != cudaSuccess) {
+            // First call on this device: resolve the array's device address and
+            // make the kernel's module resident now (under CUDA's lazy module
+            // loading, loading a module allocates device memory and may
+            // synchronise); later calls only launch.
+            cudaFuncAttributes fa{};
+            if (cudaGetSymbolAddress(&g_scratch_ptr[device], g_sample_scratch) != cudaSuccess ||
+                cudaFuncGetAttributes(&fa, k_sample_noalloc) != cudaSuccess) {
                 g_scratch_ptr[device] = nullptr;
                 return 0;
             }

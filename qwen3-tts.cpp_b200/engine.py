@@ -234,6 +234,11 @@ class Engine:
     def set_seed(self, seed: int):
         lib().qtts_set_seed(self.h, int(seed))
 
+    @staticmethod
+    def frame_kernel() -> str:
+        """Name of the kernel that runs the frames (QTTS_FRAME_MODE selects it)."""
+        return "k_frame_persistent" if os.environ.get("QTTS_FRAME_MODE") == "persistent" else "frame_graph"
+
     def timing(self) -> dict:
         t = Timing()
         lib().qtts_get_timing(self.h, C.byref(t))

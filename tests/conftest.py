@@ -37,7 +37,7 @@ def qtts():
 
 @pytest.fixture(scope="session")
 def model_dir():
-    """Seeded GGUFs are cached here (git- and gpurun-ignored); bench.py uses the same files."""
+    """Seeded GGUFs are cached here (kept out of the repository and of the GPU snapshot); bench.py uses the same files."""
     d = os.environ.get("QTTS_MODEL_DIR", os.path.join(ROOT, ".models"))
     os.makedirs(d, exist_ok=True)
     return d

@@ -156,3 +156,30 @@ class NpModel:
             logits.append(lg)
             codes.append(int(np.argmax(lg)))
         return np.array(codes), np.stack(logits)
+
+
+def legacy_predict_codes(path: str, hidden, prev_codes) -> np.ndarray:
+    """build_code_pred_graph (src/tts_transformer.cpp:1771-1899), the legacy
+    non-autoregressive predictor: one row = hidden + the 15 code-predictor
+    embeddings of prev_codes, the code-predictor layers with q/k norms and no
+    RoPE, self-attention over that single row (softmax of one score is 1, so
+    the output is V), no output norm, then every lm_head on the row.  Returns
+    logits [15][V]."""
+    m = NpModel(path)
+    x = np.asarray(hidden, np.float32).copy()
+    for cb in range(15):
+        x = x + m.t[f"code_pred.codec_embd.{cb}.weight"][1].astype(np.float32)[int(prev_codes[cb])]
+    X = x[None]
+    NH, NKV, D = m.NH, m.NKV, m.D
+    for il in range(m.cp_layers):
+        p = f"code_pred.blk.{il}."
+        xn = m.rms(X, m.vec(p + "attn_norm.weight"))
+        v = m.mul_mat(p + "attn_v.weight", xn).reshape(NKV, D)
+        att = np.concatenate([v[h // (NH // NKV)] for h in range(NH)])[None]
+        X = m.mul_mat(p + "attn_output.weight", att) + X
+        xn = m.rms(X, m.vec(p + "ffn_norm.weight"))
+        gt = m.mul_mat(p + "ffn_gate.weight", xn)
+        up = m.mul_mat(p + "ffn_up.weight", xn)
+        hh = (gt / (np.float32(1) + np.exp(-gt))) * up
+        X = m.mul_mat(p + "ffn_down.weight", hh, f32_cast=True) + X
+    return np.stack([m.mul_mat(f"code_pred.lm_head.{g}.weight", X)[0] for g in range(15)])

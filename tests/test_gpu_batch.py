@@ -94,3 +94,102 @@ def test_codes_device_handoff(qtts, tiny_f16):
         assert nf[i] == 5 and np.array_equal(allc[i, :nf[i]], host[i])
     b.close()
     eng.close()
+
+
+def test_batch_stops_each_sequence_at_its_max_len(qtts, tiny_f16):
+    """EOS suppressed, per-sequence max_len 3 / 7 / 5, run() asked for more
+    frames than any budget: each sequence stops at its own max_len on the device
+    (its position never passes prompt + max_len) and its codes follow the oracle."""
+    rng = np.random.default_rng(91)
+    eng = qtts.Engine(tiny_f16, 0)
+    H = eng.cfg["hidden_size"]
+    utts = _utterances(rng, 3, 8, H)
+    for u, m in zip(utts, (3, 7, 5)):
+        u["max_len"] = m
+    b = qtts.engine.Batch(eng, max_batch=4, max_positions=128, max_frames=8)
+    b.begin(utts)
+    assert b.run(50) == 3 + 7 + 5
+    assert b.run(10) == 0
+    codes = b.codes()
+    o = Oracle(tiny_f16)
+    for i, u in enumerate(utts):
+        assert codes[i].shape == (u["max_len"], 16)
+        kw = {k: v for k, v in u.items() if k not in ("text", "max_len")}
+        r = o.generate(u["text"], u["max_len"], follow=codes[i], tie_tol=TIE_TOL, **kw)
+        assert r["n_mismatch"] == 0 and r["n_frames"] == u["max_len"]
+    b.close()
+    eng.close()
+
+
+def _icl_utterance(seed, prefill, frames, hidden):
+    """An ICL utterance whose talker prefill is `prefill` positions (9 + reference frames)."""
+    r = np.random.default_rng(seed)
+    spk = r.standard_normal(hidden).astype(np.float32)
+    spk /= np.linalg.norm(spk)
+    return dict(text=text_ids(r, 24), max_len=frames, speaker=spk, ref_text=text_ids(r, 30),
+                ref_codes=r.integers(0, 2048, (prefill - 9, 16)).astype(np.int32),
+                rep_penalty=1.05, temperature=0.0, top_k=0, eos_bias=-1e9)
+
+
+def _follow(path, utts, codes, frames, idx, engine_order):
+    """Oracle replay of sequences `idx` of a batch (near-ties excepted)."""
+    o = Oracle(path, engine_order=engine_order)
+    for i in idx:
+        u = utts[i]
+        assert codes[i].shape == (frames, 16), (i, codes[i].shape)
+        kw = {k: v for k, v in u.items() if k not in ("text", "max_len")}
+        r = o.generate(u["text"], frames, follow=codes[i], tie_tol=TIE_TOL, **kw)
+        print("batch parity:", i, dict(n_mismatch=r["n_mismatch"], n_ties=r["n_ties"], max_tie_gap=r["max_tie_gap"],
+                                       max_mismatch_gap=r["max_mismatch_gap"]))
+        assert r["n_mismatch"] == 0, (i, r["n_mismatch"], r["max_mismatch_gap"], r["first_mismatch"])
+        assert r["n_frames"] == frames
+
+
+def test_full_batch64_config4_shape(qtts, full_f16):
+    """configs[3] shape on the 0.6B F16 model: 64 utterances, ICL prompts of
+    U[32, 512] positions, 64 greedy frames each through the tcgen05 batch path
+    (MMA N = 64, the split-K cluster sizes the projections use, up to 9 KV pages
+    per sequence).  Eight sequences, the shortest and longest prompts among
+    them, are replayed by the CPU oracle (ggml order: its prefill is the fast
+    one); every sequence must produce all 64 frames."""
+    eng = qtts.Engine(full_f16, 0)
+    H = eng.cfg["hidden_size"]
+    rng = np.random.default_rng(4242)
+    P = rng.integers(32, 513, 64)
+    frames = 64
+    utts = [_icl_utterance(5000 + i, int(P[i]), frames, H) for i in range(64)]
+    b = qtts.engine.Batch(eng, max_batch=64, max_positions=int(P.max()) + frames + 1, max_frames=frames)
+    b.begin(utts)
+    assert b.run(frames) == 64 * frames
+    codes = b.codes()
+    b.close()
+    eng.close()
+    order = np.argsort(P)
+    idx = sorted({int(order[0]), int(order[-1])} | {int(order[k]) for k in (9, 18, 27, 36, 45, 54)})
+    _follow(full_f16, utts, codes, frames, idx, engine_order=False)
+
+
+def test_full_q8_batch32_config5_shape(qtts, full_q8):
+    """configs[4] shape on the 0.6B Q8_0 model: 32 utterances with 512-position
+    prompts (8 KV pages each), 24 greedy frames (into the ninth page), four
+    sequences replayed by the CPU oracle; then one sequence run to 1,032
+    positions (17 pages) and replayed in full."""
+    eng = qtts.Engine(full_q8, 0)
+    H = eng.cfg["hidden_size"]
+    frames = 24
+    utts = [_icl_utterance(7000 + i, 512, frames, H) for i in range(32)]
+    b = qtts.engine.Batch(eng, max_batch=32, max_positions=512 + frames + 1, max_frames=frames)
+    b.begin(utts)
+    assert b.run(frames) == 32 * frames
+    codes = b.codes()
+    b.close()
+    _follow(full_q8, utts, codes, frames, [0, 10, 21, 31], engine_order=True)
+    long_frames = 520
+    lu = [_icl_utterance(7999, 512, long_frames, H)]
+    b = qtts.engine.Batch(eng, max_batch=1, max_positions=512 + long_frames + 1, max_frames=long_frames)
+    b.begin(lu)
+    assert b.run(long_frames) == long_frames
+    lc = b.codes()
+    b.close()
+    eng.close()
+    _follow(full_q8, lu, lc, long_frames, [0], engine_order=True)

@@ -211,11 +211,14 @@ def test_stop_conditions(eng_tiny, tiny_f16):
     seen = []
     e = eng_tiny.generate(text, 30, eos_bias=-1e9, on_frame=lambda codes, f: (seen.append(f), f < 4)[1])
     assert e["n_frames"] == 5 and seen == [0, 1, 2, 3, 4]
-    # repetition-loop detection: same decision as the oracle on the same codes
+    # repetition-loop detection on: engine and oracle agree on every code and on
+    # where the run stops (the oracle replays the engine's codes; any divergence
+    # or a different stopping frame fails)
     e2 = eng_tiny.generate(text, 40, eos_bias=-1e9, rep_penalty=1.0, rep_loop_detect=True)
-    r2 = o.generate(text, 40, eos_bias=-1e9, rep_penalty=1.0, rep_loop_detect=True)
-    if r2["n_mismatch"] == 0 and np.array_equal(r2["codes"][: e2["n_frames"]], e2["codes"]):
-        assert r2["n_frames"] == e2["n_frames"]
+    r2 = o.generate(text, 40, eos_bias=-1e9, rep_penalty=1.0, rep_loop_detect=True, follow=e2["codes"])
+    assert r2["n_mismatch"] == 0
+    assert r2["n_frames"] == e2["n_frames"]
+    assert np.array_equal(r2["codes"][: e2["n_frames"]], e2["codes"])
 
 
 # ---------------------------------------------------------------- full-size (0.6B layout)
