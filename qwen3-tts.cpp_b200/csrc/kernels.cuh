@@ -93,34 +93,78 @@ __device__ __forceinline__ void issue_gemv_slice(const DMat & A, const DMat & B,
     if (gain) bulk_g2s(buf + L.gain_off, gain, (unsigned)(A.cols * 4), m);
 }
 
-__device__ __forceinline__ void gemv_store(const GemvArgs & a, int r, int v, float accA, float accB, const float * rs,
-                                           int rl, int rstride) {
-    float out;
-    if (a.epi == EPI_SWIGLU) out = __fmul_rn(silu(accA), accB);
-    else if (a.epi == EPI_RESID) out = __fadd_rn(accA, rs[v * rstride + rl]);
-    else out = accA;
-    a.y[(size_t) v * a.ldy + r] = out;
+// Epilogue of output row rl (local) of activation row v: SwiGLU, residual add or store.
+__device__ __forceinline__ float gemv_epi(const GemvArgs & a, int v, float accA, float accB, const float * rs, int rl,
+                                          int rstride) {
+    if (a.epi == EPI_SWIGLU) return __fmul_rn(silu(accA), accB);
+    if (a.epi == EPI_RESID) return __fadd_rn(accA, rs[v * rstride + rl]);
+    return accA;
 }
+
+// Plain output store of a stand-alone or CUDA-graph GEMV: y[v][r].
+struct GemvStorePlain {
+    float * y;
+    int ldy;
+    __device__ __forceinline__ void operator()(int r, int, int v, float out) const { y[(size_t) v * ldy + r] = out; }
+};
 
 // Activation rows live in shared memory in a two-plane layout per row: column
 // c = 8*k + w sits at (w / 4) * cols/2 + 4*k + w % 4, so the lane that owns the
 // 8-column chunk k reads two conflict-free float4 (plane 0 and plane 1).
 __device__ __forceinline__ int xpos(int c, int cols) { return ((c & 7) >> 2) * (cols >> 1) + ((c >> 3) << 2) + (c & 3); }
 
+// Shared-memory work area of a GEMV (gemv_work_bytes): activation rows xs in the
+// two-plane layout, residual rows rs, then (Q8_0) activation quants and scales.
+struct GemvWork {
+    float * xs, * rs;
+    int8_t * qa;
+    float * da;
+};
+template <int NV>
+__device__ __forceinline__ GemvWork gemv_work(uint8_t * work, int cols, int rpc, bool q8) {
+    GemvWork w;
+    w.xs = reinterpret_cast<float *>(work);
+    w.rs = w.xs + NV * cols;
+    w.qa = reinterpret_cast<int8_t *>(w.rs + NV * ((rpc + 3) & ~3));
+    w.da = reinterpret_cast<float *>(w.qa + (q8 ? NV * cols : 0));
+    return w;
+}
+
+// Activation rows from global memory into the two-plane layout (float4 i =
+// columns 4i..4i+3 -> plane i & 1, chunk i >> 1) and this CTA's residual rows.
+template <int NV>
+__device__ __forceinline__ void gemv_load_global(const GemvArgs & a, int r0, int nrow, int rpc, const GemvWork & w) {
+    const int cols = a.A.cols, tid = threadIdx.x, nt = blockDim.x;
+    const int rstride = (rpc + 3) & ~3;
+    const int c4 = cols >> 2, h8 = cols >> 3;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+        if (v >= a.nv) break;
+        const float4 * src = reinterpret_cast<const float4 *>(a.x + (size_t) v * a.ldx);
+        float4 * dst = reinterpret_cast<float4 *>(w.xs + v * cols);
+        for (int i = tid; i < c4; i += nt) dst[(i & 1) * h8 + (i >> 1)] = src[i];
+    }
+    if (a.epi == EPI_RESID)
+        for (int v = 0; v < a.nv; ++v)
+            for (int r = tid; r < nrow; r += nt) w.rs[v * rstride + r] = a.resid[(size_t) v * a.ldr + r0 + r];
+}
+
 // GEMV over this CTA's rows [r0, r1) with the weight slice in shared memory
 // (`wsm`, layout slice_layout; complete once mbarrier `m` reaches `parity`, or
-// immediately when m == nullptr).  Latency-oriented: one burst of global loads
-// (activations, residuals), one warp per row, three block barriers.  The
-// RMSNorm sum of squares is a double sum over the CTA (thread-strided partials,
-// warp butterfly, then the 16 warp partials in order); normalisation and F16
+// immediately when m == nullptr) and the activation rows already in the work
+// area (two-plane layout; callers synchronise the block after filling it).
+// Latency-oriented: one warp per row, two block barriers.  The RMSNorm sum of
+// squares is a double sum over the CTA (thread-strided partials, warp
+// butterfly, then the 16 warp partials in order); normalisation and F16
 // rounding happen once, in place.  Reduction order of a row: lane l
 // accumulates the 8-column chunks l, l+32, ... in order (8 sequential FMAs per
 // F16 chunk; one 32-block term per lane pair for Q8_0), then a butterfly over
-// the 32 lanes.
-template <int NV>
-__device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, const int ncta, const uint8_t * wsm,
-                                           uint8_t * work, uint64_t * m, unsigned parity,
-                                           unsigned long long * ready_stamp = nullptr) {
+// the 32 lanes.  Outputs go through `store(r, rl, v, value)`; xn_smem (optional)
+// receives every CTA's unrounded normalised row 0 in column order.
+template <int NV, class Store>
+__device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, const int ncta, const uint8_t * wsm,
+                                             uint8_t * work, uint64_t * m, unsigned parity, const Store & store,
+                                             float * xn_smem = nullptr, unsigned long long * ready_stamp = nullptr) {
     __shared__ double s_red[QTTS_WARPS][NV];
     const int cols = a.A.cols, rows = a.A.rows;
     const int rpc = gemv_rpc(rows, ncta);
@@ -130,26 +174,14 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
     const int nv = a.nv;
     const int rstride = (rpc + 3) & ~3;
-    float * xs = reinterpret_cast<float *>(work);
-    float * rs = xs + NV * cols;
-    int8_t * qa = reinterpret_cast<int8_t *>(rs + NV * rstride);
-    float * da = reinterpret_cast<float *>(qa + (q8 ? NV * cols : 0));
-    const int c4 = cols >> 2, h8 = cols >> 3;
+    const GemvWork W = gemv_work<NV>(work, cols, rpc, q8);
+    float * xs = W.xs;
+    const float * rs = W.rs;
+    int8_t * qa = W.qa;
+    float * da = W.da;
+    const int h8 = cols >> 3;
 
-    // 1. activations (float4 i = columns 4i..4i+3 -> plane i & 1, chunk i >> 1) and residuals
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
-        if (v >= nv) break;
-        const float4 * src = reinterpret_cast<const float4 *>(a.x + (size_t) v * a.ldx);
-        float4 * dst = reinterpret_cast<float4 *>(xs + v * cols);
-        for (int i = tid; i < c4; i += nt) dst[(i & 1) * h8 + (i >> 1)] = src[i];
-    }
-    if (a.epi == EPI_RESID)
-        for (int v = 0; v < nv; ++v)
-            for (int r = tid; r < nrow; r += nt) rs[v * rstride + r] = a.resid[(size_t) v * a.ldr + r0 + r];
-    __syncthreads();
-
-    // 2. RMSNorm partial sums; thread 0 waits for the weight slice
+    // 1. RMSNorm partial sums; thread 0 waits for the weight slice
     const bool has_norm = a.norm_g != nullptr;
     if (has_norm) {
 #pragma unroll
@@ -174,9 +206,9 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
     const SliceLayout L = slice_layout(a.A, dual, has_norm, nrow);
     const float * gain = has_norm ? reinterpret_cast<const float *>(wsm + L.gain_off) : nullptr;
 
-    // 3. normalise (x * scale) * gain, round to F16 for F16 weights with an F16 activation
+    // 2. normalise (x * scale) * gain, round to F16 for F16 weights with an F16 activation
     const bool round16 = !q8 && a.act == ACT_F16;
-    if (has_norm || round16 || a.xn_out) {
+    if (has_norm || round16 || a.xn_out || xn_smem) {
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
             if (v >= nv) break;
@@ -193,6 +225,7 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
                 float t = xs[v * cols + p];
                 if (has_norm) t = __fmul_rn(__fmul_rn(t, scale), gain[c]);
                 if (a.xn_out && r0 == 0) a.xn_out[(size_t) v * a.ldxn + c] = t;   // hidden_states (post-norm, unrounded)
+                if (xn_smem && v == 0) xn_smem[c] = t;
                 xs[v * cols + p] = round16 ? round_f16(t) : t;
             }
         }
@@ -226,7 +259,7 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
                 if (v >= nv) continue;
                 const float s1 = warp_sum(acc[v]);
                 const float s2 = dual ? warp_sum(accb[v]) : 0.0f;
-                if (lane == 0) gemv_store(a, r0 + rl, v, s1, s2, rs, rl, rstride);
+                if (lane == 0) store(r0 + rl, rl, v, gemv_epi(a, v, s1, s2, rs, rl, rstride));
             }
         }
         return true;
@@ -310,10 +343,22 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
             if (v >= nv) continue;
             const float s1 = warp_sum(acc[v]);
             const float s2 = dual ? warp_sum(accb[v]) : 0.0f;
-            if (lane == 0) gemv_store(a, r0 + rl, v, s1, s2, rs, rl, rstride);
+            if (lane == 0) store(r0 + rl, rl, v, gemv_epi(a, v, s1, s2, rs, rl, rstride));
         }
     }
     return true;
+}
+
+// GEMV with activations and residuals read from global memory (gemv_load_global)
+// and outputs stored to a.y.
+template <int NV>
+__device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, const int ncta, const uint8_t * wsm,
+                                           uint8_t * work, uint64_t * m, unsigned parity) {
+    const int rpc = gemv_rpc(a.A.rows, ncta);
+    const int r0 = cta * rpc, r1 = min(a.A.rows, r0 + rpc);
+    gemv_load_global<NV>(a, r0, r1 > r0 ? r1 - r0 : 0, rpc, gemv_work<NV>(work, a.A.cols, rpc, a.A.type == W_Q8_0));
+    __syncthreads();
+    return gemv_compute<NV>(a, cta, ncta, wsm, work, m, parity, GemvStorePlain{a.y, a.ldy});
 }
 
 // Stand-alone GEMV launch (CUDA-graph path, prefill, kernel tests): thread 0

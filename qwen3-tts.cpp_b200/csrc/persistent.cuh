@@ -190,9 +190,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) k_frame_persistent(PersistentAr
                     const int b = op.slot;
                     const uint8_t * wb = smem + (size_t) b * P.wbuf_bytes;
                     const unsigned par = phase >> b & 1u;
-                    unsigned long long * rs = P.trace ? P.trace + PK_TRACE_SLOTS * s + 2 : nullptr;
-                    const bool ok = op.nv == 1 ? gemv_slice<1>(op.g, cta, ncta, wb, work, mbar + b, par, rs)
-                                               : gemv_slice<2>(op.g, cta, ncta, wb, work, mbar + b, par, rs);
+                    const bool ok = op.nv == 1 ? gemv_slice<1>(op.g, cta, ncta, wb, work, mbar + b, par)
+                                               : gemv_slice<2>(op.g, cta, ncta, wb, work, mbar + b, par);
                     if (!ok) {                          // block-uniform: a copy did not land in time
                         if (tid == 0) atomicExch(P.err, 2);
                         pk_drain(mbar, pending, phase);
