@@ -399,7 +399,7 @@ def run_batch(args, cfg):
 def run_ncu_workload(args):
     """A small fixed workload for ncu captures (no timing, no JSON line):
     `frames`: the config's ICL prefill and --frames frames through the frame
-    loop (QTTS_FRAME_MODE selects graph or persistent); `batch`: --batch
+    loop (QTTS_FRAME_MODE selects graph or dataflow); `batch`: --batch
     utterances with 64-position ICL prompts, --frames batched frames, then two
     eagerly profiled frames.  A few GB on the device at most."""
     pkg = _pkg()
@@ -510,7 +510,7 @@ def main():
     # ---- device-resident timing: inputs in HBM.  The utterance of the config
     # (F frames after the prefill) is replayed K / F times: each replay rewinds
     # the device frame state to frame 0 (no new prefill) and runs F frames in
-    # one persistent launch (or F graph launches).
+    # one dataflow-kernel launch (or F graph launches).
     F = cfg["frames"]
     reps = max(1, (K + F - 1) // F)
     runs = [min(F, K - i * F) for i in range(reps)]   # whole replays, then the remainder of a partial one

@@ -171,13 +171,6 @@ int32_t qtts_get_timing(const qtts_engine * e, qtts_timing * out);
  * Returns frames produced or -1.  For measurement only. */
 int32_t qtts_profile_frames(qtts_engine * e, int32_t n, qtts_kernel_stats * stats, int32_t n_classes);
 
-/* Diagnostics of the persistent frame kernel, enabled by QTTS_PK_TRACE=1 at
- * run time: the op types of the frame program (1 GEMV, 2 attention, 3 sampler,
- * 4 embedding gather, 5 frame end) and, for the last run, CTA 0's %globaltimer
- * (start, work done) pair of every op.  Both return the count available. */
-int32_t qtts_program_ops(const qtts_engine * e, int32_t * types, int32_t cap);
-int32_t qtts_op_trace(const qtts_engine * e, unsigned long long * out, int32_t cap);
-
 /* One tcgen05 tensor-core GEMM as the batched and prefill paths run it
  * (test entry; no reference counterpart): y[m][r] = sum_k W[r][k] * a[m][k],
  * W F16 row-major [rows x cols] (host), activations a = x[m x cols] after an

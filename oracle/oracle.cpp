@@ -732,13 +732,15 @@ static double uniform01(uint64_t seed, uint32_t frame, uint32_t cb) {
     return (double)(bits >> 11) * (1.0 / 9007199254740992.0);
 }
 
-// A sampled decision is near a tie when the uniform draw lies within 1e-6 of a
-// bucket edge of the inverse CDF, or when the top-k threshold is within 1e-3 of
-// the best excluded logit (the kept set can then differ by reduction order).
-// Returned on the greedy gap scale: the smaller of (edge distance scaled to the
-// 1e-3 tie threshold) and the threshold gap.
-static double sampled_tie_measure(double edge_gap, double topk_gap) {
-    return std::min(edge_gap * 1e3, topk_gap);
+// Near-tie measure of a sampled decision on the scale of a greedy top-2 logit
+// gap (a greedy pick flips once the logits move by half its gap).  Raw logits
+// moved by at most delta move every temperature-scaled logit by delta / T, so
+// they shift the inverse-CDF bucket edges by about 2 delta / T and the top-k
+// threshold gap (in scaled units) by 2 delta / T: the decision can flip only if
+// 2 delta >= T * min(distance of the draw from the nearest edge, threshold gap
+// to the best excluded logit).
+static double sampled_tie_measure(double edge_gap, double topk_gap, double temperature) {
+    return temperature * std::min(edge_gap, topk_gap);
 }
 
 static int32_t argmax(const float * d, int n) {  // src/tts_transformer.cpp:2583-2593
@@ -1026,7 +1028,7 @@ static void predict_codes(Model & m, const float * hidden, int cb0, float temper
         } else {
             pick = sample_tok(work.data(), V, temperature, top_k, uniform01(seed, frame, (uint32_t)(g + 1)),
                               true, 0.0f, -1, &gap, &kgap);
-            gap = sampled_tie_measure(gap, kgap);
+            gap = sampled_tie_measure(gap, kgap, temperature);
         }
         if (temperature <= 0.0f) {  // record the top-2 gap of this decision
             float best = -INFINITY, second = -INFINITY;
@@ -1232,7 +1234,7 @@ int orc_generate(void * h, const orc_gen_args * a, orc_gen_result * r) {
         } else {
             next = sample_tok(logits.data(), V, a->temperature, a->top_k, uniform01(a->seed, (uint32_t) frame, 0u),
                               true, eb, c.codec_eos, &gap, &kgap);
-            gap = sampled_tie_measure(gap, kgap);
+            gap = sampled_tie_measure(gap, kgap, a->temperature);
         }
         const int32_t * fol = nullptr;
         if (a->follow) {

@@ -18,7 +18,7 @@
 //     step, with no host round trip inside a frame.
 #include "../../include/qwen3tts_b200.h"
 #include "gguf.hpp"
-#include "persistent.cuh"
+#include "frame_dataflow.cuh"
 #include "gemm_tc.cuh"
 #include "batch_engine.cuh"
 
@@ -130,22 +130,27 @@ struct Engine {
     int launches = 0;
     int launches_per_frame = 0;
     GenSession sess;
-    // persistent frame kernel (one cooperative launch per run of frames)
-    bool use_persistent = false;   // QTTS_FRAME_MODE=persistent selects the single-launch frame kernel
-    std::vector<POp> prog;
-    POp * d_prog = nullptr;
+    // dataflow frame kernel (one cooperative launch per run of frames)
+    bool use_dataflow = false;   // QTTS_FRAME_MODE=dataflow selects the single-launch frame kernel
+    std::vector<DfOp> prog;
+    std::vector<FusedAttn> df_att;
+    DfOp * d_prog = nullptr;
     size_t prog_cap = 0;
-    size_t prog_smem = 0;
-    unsigned * d_flags = nullptr;
+    FusedAttn * d_df_att = nullptr;
+    size_t att_cap = 0;
+    unsigned long long * d_dfbuf = nullptr;   // tagged activation buffers
+    size_t df_buf_words = 0;
+    unsigned long long * df_bufp[DB_N] = {};
+    int df_slot_words[DB_N] = {}, df_writes[DB_N] = {};
+    unsigned df_tag_base = 1;
     int * d_err = nullptr;
     bool prog_ok = false;
-    int pf0[16];
-    int n_pf0 = 0;
-    int pk_first[2] = {0, 0};
-    unsigned long long * d_trace = nullptr;   // QTTS_PK_TRACE=1: per-op timestamps of CTA 0
-    size_t trace_cap = 0, trace_n = 0;
-    size_t pk_wbuf = 0, pk_dyn = 0;
-    double pf_lead_bytes = 24.0 * 1024 * 1024;
+    int df_first[2] = {0, 0};
+    int df_pf0[8];
+    int n_df_pf0 = 0;
+    int df_pf_lead = 4;          // GEMVs between a slice's L2 prefetch and its use (QTTS_DF_PF_LEAD)
+    size_t df_wbuf = 0, df_work = 0, df_dyn = 0;
+    int df_keys = 0;
     // eager profiling: CUDA events around every launch, accumulated per kernel class
     bool profiling = false;
     struct ProfEv { int cls; double bytes; cudaEvent_t a, b; };
@@ -180,14 +185,14 @@ struct Engine {
         if (d_prow) { cudaFree(d_prow); d_prow = nullptr; prow_cap = 0; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
                          cp_logits, hidden, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
-                         dbg_t, dbg_cp, d_attn, d_prog, d_flags, d_err, d_trace, logits0, hidden0};
+                         dbg_t, dbg_cp, d_attn, d_prog, d_df_att, d_dfbuf, d_err, logits0, hidden0};
         for (void * p : ptrs) if (p) cudaFree(p);
         wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
         x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = tmp_a = tmp_b = nullptr;
         logits0 = hidden0 = nullptr;
         d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
-        dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_prog = nullptr; d_flags = nullptr; d_err = nullptr;
-        d_trace = nullptr;
+        dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_prog = nullptr; d_df_att = nullptr; d_dfbuf = nullptr;
+        d_err = nullptr; df_buf_words = 0; prog_cap = 0; att_cap = 0; prog_ok = false;
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         ev0 = ev1 = nullptr;
@@ -221,8 +226,8 @@ struct Engine {
     GemvArgs make_gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
                        float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
                        const int * done, int * ncta_out, size_t * slice_out, size_t * smem_out);
-    bool build_program();
-    bool launch_persistent(int n);
+    bool build_program(int max_keys);   // max_keys: the longest talker attention row it serves
+    bool launch_dataflow(int n);
     bool sync(const char * what);
 
     // ------------------------------------------------------------ API pieces
@@ -319,8 +324,8 @@ bool Engine::load(const char * path, int device) {
     if (c.hidden_size % 256 || c.intermediate_size % 32 || c.code_pred_intermediate_size % 32 || c.text_embd_dim % 32) {
         err = "hidden/ffn/text widths must be multiples of 256/32/32"; return false;
     }
-    if (const char * m = getenv("QTTS_FRAME_MODE")) use_persistent = strcmp(m, "persistent") == 0;
-    if (const char * lb = getenv("QTTS_PF_LEAD_MB")) pf_lead_bytes = atof(lb) * 1024.0 * 1024.0;
+    if (const char * m = getenv("QTTS_FRAME_MODE")) use_dataflow = strcmp(m, "dataflow") == 0;
+    if (const char * v = getenv("QTTS_DF_PF_LEAD")) df_pf_lead = std::max(2, atoi(v));
     if (!upload_weights(g)) return false;
     if (!alloc_activations()) return false;
     if (!init_cp_kv(16)) return false;
@@ -811,199 +816,218 @@ bool Engine::capture_graph() {
     return true;
 }
 
-// ---------------------------------------------------------------- persistent frame program
-// The same op sequence as enqueue_frame(), as descriptors for k_frame_persistent.
-bool Engine::build_program() {
+// ---------------------------------------------------------------- dataflow frame program
+// The frame as k_frame_dataflow's op list: the same layers, heads and samplers
+// as enqueue_frame(), with each GEMV's input named by the op that produced it.
+// Pass g of the code predictor samples codebook g at its start (g = 0: the
+// talker logits), runs the code-predictor layers and lm_head[g]; the talker
+// step samples the last codebook, sums the next input and ends with the codec
+// head.
+bool Engine::build_program(int max_keys) {
     const qtts_config & c = cfg;
-    const int H = c.hidden_size, V1 = c.code_pred_vocab_size, NG = c.n_codebooks - 1;
-    const int NKV = c.n_key_value_heads;
+    df_keys = max_keys;
+    const int H = c.hidden_size, NG = c.n_codebooks - 1, NKV = c.n_key_value_heads;
     prog.clear();
-    prog_smem = 0;
-    bool prog_bad = false;
-    auto push_gemv = [&](const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
-                         float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
-                         int barrier) {
-        POp op{};
-        op.type = P_GEMV; op.barrier = barrier; op.nv = nv;
-        int ncta; size_t sl, sm;
-        op.g = make_gemv(A, B, xin, ldx, nv, norm, act, y, ldy, resid, ldr, epi, xn_out, ldxn, nullptr, &ncta, &sl, &sm);
-        prog_smem = std::max(prog_smem, gemv_work_bytes(A.type, A.cols, nv, gemv_rpc(A.rows, n_sm)));
-        prog.push_back(op);
+    df_att.clear();
+    int wr[DB_N] = {0};
+    const size_t cp_layer = (size_t) cp_ctx * NKV * QTTS_HD, t_layer = (size_t) n_ctx * NKV * QTTS_HD;
+    for (size_t il = 0; il < CPL.size(); ++il)
+        df_att.push_back(fused_attn_args(CPL[il], cpk + il * cp_layer, cpv + il * cp_layer, rope_cp, 2, nullptr, 0, true,
+                                         nullptr, cp_ctx));
+    for (size_t il = 0; il < L.size(); ++il)
+        df_att.push_back(fused_attn_args(L[il], kc + il * t_layer, vc + il * t_layer, rope_t, 1, nullptr, 0, false,
+                                         attn_dump && (int) il == attn_layer ? d_attn : nullptr, n_ctx));
+    auto gemv_op = [&](const DMat & A, const DMat * B, int nv, int pro, const float * norm, int act, int epi,
+                       int out_buf) {
+        DfOp op{};
+        op.type = DF_GEMV; op.pro = pro; op.nv = nv; op.A = A;
+        if (B) op.B = *B;
+        op.norm_g = norm; op.act = act; op.epi = epi;
+        op.in_buf = -1; op.in_op = 0;
+        op.out_buf = out_buf; op.out_wr = wr[out_buf]++;
+        return op;
     };
-    auto push_layers = [&](std::vector<LayerW> & Ls, __half * kbase, __half * vbase, int ctx, const float2 * rope,
-                           float * X, int M, const int * pos_ptr, int pos_static, bool f32, int ffn, float * dump,
-                           int dump_layer) {
-        const size_t layer_elems = (size_t) ctx * NKV * QTTS_HD;
-        for (size_t il = 0; il < Ls.size(); ++il) {
-            LayerW & l = Ls[il];
-            push_gemv(l.qkv, nullptr, X, H, M, l.attn_norm, ACT_F16, qkv, QKVD(), nullptr, 0, EPI_STORE, nullptr, 0, 1);
-            POp op{};
-            op.type = P_ATTN; op.barrier = 1;
-            op.a = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, M, pos_ptr, pos_static,
-                                   f32, ((int) il == dump_layer) ? dump : nullptr, ctx);
-            op.a.warp_heads = &Ls == &CPL && M == 1 && !f32 && !pos_ptr;   // code-predictor step
-            if (!op.a.warp_heads) prog_smem = std::max(prog_smem, fused_attn_smem(f32 ? M : ctx, M));
-            prog.push_back(op);
-            push_gemv(l.o, nullptr, att, QD(), M, nullptr, ACT_F16, X, H, X, H, EPI_RESID, nullptr, 0, 1);
-            push_gemv(l.gate, &l.up, X, H, M, l.ffn_norm, ACT_F16, hbuf, ffn, nullptr, 0, EPI_SWIGLU, nullptr, 0, 1);
-            push_gemv(l.down, nullptr, hbuf, ffn, M, nullptr, ACT_F32, X, H, X, H, EPI_RESID, nullptr, 0, 1);
+    auto from = [&](DfOp & op, int buf, int producer, int row) {
+        op.in_buf = buf; op.in_op = producer; op.in_wr = prog[producer].out_wr; op.in_row = row;
+    };
+    auto push = [&](const DfOp & op) { prog.push_back(op); return (int) prog.size() - 1; };
+    int head = -1;   // the last head op (its logits feed the next sampler)
+    for (int g = 0; g < NG; ++g) {
+        const int M = g == 0 ? 2 : 1;
+        int prev = -1;
+        for (size_t il = 0; il < CPL.size(); ++il) {
+            LayerW & l = CPL[il];
+            DfOp q = gemv_op(l.qkv, nullptr, M, il ? PRO_POLL : (g == 0 ? PRO_CB0 : PRO_CBG), l.attn_norm, ACT_F16,
+                             EPI_STORE, DB_QKV);
+            if (il) from(q, DB_XCP, prev, 0);
+            else if (g > 0) from(q, DB_LCP, head, 0);
+            else { q.in_buf = DB_LT; }   // the talker head of the previous frame: fixed up below
+            q.cb = g;
+            const int iq = push(q);
+            DfOp o = gemv_op(l.o, nullptr, M, g == 0 ? PRO_CPATTN2 : PRO_CPATTN, nullptr, ACT_F16, EPI_RESID, DB_XCP);
+            from(o, DB_QKV, iq, 0);
+            o.layer = (int) il; o.n_past = g == 0 ? 0 : g + 1;
+            const int io = push(o);
+            DfOp gu = gemv_op(l.gate, &l.up, M, PRO_POLL, l.ffn_norm, ACT_F16, EPI_SWIGLU, DB_H);
+            from(gu, DB_XCP, io, 0);
+            const int igu = push(gu);
+            DfOp dn = gemv_op(l.down, nullptr, M, PRO_POLL, nullptr, ACT_F32, EPI_RESID, DB_XCP);
+            from(dn, DB_H, igu, 0);
+            prev = push(dn);
         }
-    };
-    auto push_sample = [&](const float * lg, int V, int cb) {
-        POp op{};
-        op.type = P_SAMPLE; op.barrier = 1; op.logits = lg; op.V = V; op.cb = cb;
-        prog.push_back(op);
-    };
-    InputArgs ia{};
-    ia.H = H; ia.codec_embd = codec_embd; ia.cp_embd = d_cp_embd; ia.hidden = hidden;
-    ia.trailing = trailing; ia.pad = pad; ia.st = st; ia.n_cb = c.n_codebooks;
-    auto push_input = [&](int mode, int g, float * out) {
-        InputArgs in = ia;
-        in.mode = mode; in.g = g; in.out = out;
-        in.step_tab = mode == IN_CP_STEP ? cp_embd[g - 1] : nullptr;
-        if (!prog.empty() && prog.back().type == P_SAMPLE && !prog.back().has_in) {
-            prog.back().has_in = 1;   // CTA 0 samples, then builds the inputs: no grid barrier between
-            prog.back().in = in;
-            return;
-        }
-        err = "frame program: inputs must follow a sampler";
-        prog_bad = true;
-    };
-    push_sample(logits, c.codec_vocab_size, 0);
-    push_input(IN_CP_PREFILL, 0, xcp);
-    push_layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 2, nullptr, 0, true, c.code_pred_intermediate_size, nullptr, -1);
-    push_gemv(cp_head[0], nullptr, xcp + H, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE, nullptr, 0, 1);
-    push_sample(cp_logits, V1, 1);
-    for (int gstep = 1; gstep < NG; ++gstep) {
-        push_input(IN_CP_STEP, gstep, xcp);
-        push_layers(CPL, cpk, cpv, cp_ctx, rope_cp, xcp, 1, nullptr, gstep + 1, false, c.code_pred_intermediate_size,
-                    nullptr, -1);
-        push_gemv(cp_head[gstep], nullptr, xcp, H, 1, cp_out_norm, ACT_F16, cp_logits, V1, nullptr, 0, EPI_STORE,
-                  nullptr, 0, 1);
-        push_sample(cp_logits, V1, gstep + 1);
+        DfOp hd = gemv_op(cp_head[g], nullptr, 1, PRO_POLL, cp_out_norm, ACT_F16, EPI_STORE, DB_LCP);
+        from(hd, DB_XCP, prev, M - 1);
+        head = push(hd);
     }
-    push_input(IN_TALKER, 0, x);
-    if (prog_bad) return false;
-    push_layers(L, kc, vc, n_ctx, rope_t, x, 1, &st->pos, 0, false, c.intermediate_size, attn_dump ? d_attn : nullptr,
-                attn_layer);
-    push_gemv(codec_head, nullptr, x, H, 1, out_norm, ACT_F16, logits, c.codec_vocab_size, nullptr, 0, EPI_STORE,
-              hidden, H, 0);
-    {
-        POp op{};
-        op.type = P_FRAME_END; op.barrier = 1;
-        prog.push_back(op);
+    int prev = -1;
+    for (size_t il = 0; il < L.size(); ++il) {
+        LayerW & l = L[il];
+        DfOp q = gemv_op(l.qkv, nullptr, 1, il ? PRO_POLL : PRO_CBLAST, l.attn_norm, ACT_F16, EPI_STORE, DB_QKV);
+        if (il) from(q, DB_X, prev, 0);
+        else { from(q, DB_LCP, head, 0); q.cb = NG; }
+        const int iq = push(q);
+        DfOp t{};
+        t.type = DF_TATTN; t.layer = (int)(CPL.size() + il);
+        t.out_buf = DB_ATT; t.out_wr = wr[DB_ATT]++;
+        from(t, DB_QKV, iq, 0);
+        const int it = push(t);
+        DfOp o = gemv_op(l.o, nullptr, 1, PRO_POLL, nullptr, ACT_F16, EPI_RESID, DB_X);
+        from(o, DB_ATT, it, 0);
+        const int io = push(o);
+        DfOp gu = gemv_op(l.gate, &l.up, 1, PRO_POLL, l.ffn_norm, ACT_F16, EPI_SWIGLU, DB_H);
+        from(gu, DB_X, io, 0);
+        const int igu = push(gu);
+        DfOp dn = gemv_op(l.down, nullptr, 1, PRO_POLL, nullptr, ACT_F32, EPI_RESID, DB_X);
+        from(dn, DB_H, igu, 0);
+        prev = push(dn);
+    }
+    DfOp th = gemv_op(codec_head, nullptr, 1, PRO_POLL, out_norm, ACT_F16, EPI_STORE, DB_LT);
+    from(th, DB_X, prev, 0);
+    th.head = 1;
+    const int it_head = push(th);
+    const int n_ops = (int) prog.size();
+    prog[0].in_op = it_head - n_ops;   // previous frame's talker head
+    prog[0].in_wr = prog[it_head].out_wr;
+    if (wr[DB_LT] != 1) { err = "frame program: one talker head per frame expected"; return false; }
+    if (c.hidden_size != CPL[0].o.rows || CPL[0].o.rows != CPL[0].down.rows || L[0].o.rows != L[0].down.rows) {
+        err = "frame program: O and down projections must share the residual row split"; return false;
     }
 
-    // Weight staging.  The k-th GEMV of the frame reads shared-memory buffer
-    // k & 1; its row slice is copied there while the grid waits at the barrier
-    // after GEMV k-2 (cyclically; the first two are copied at launch start).  Every frame has an
-    // even number of GEMVs (4L + 1 + 15 (4L_cp + 1)), so the buffer parity of a
-    // GEMV is the same in every frame.
+    // Weight staging: GEMV j of the frame uses buffer j & 1 and its slice is
+    // copied once GEMV j - 2 is done (cyclically; the first two at launch); GEMV
+    // j prefetches the slice of GEMV j + df_pf_lead into L2.  The GEMV count per
+    // frame is even (15 (4 Lcp + 1) + 4 L + 1), so the parity holds across frames.
     std::vector<int> gi;
-    for (size_t i = 0; i < prog.size(); ++i)
-        if (prog[i].type == P_GEMV) gi.push_back((int) i);
+    for (int i = 0; i < n_ops; ++i)
+        if (prog[i].type == DF_GEMV) gi.push_back(i);
     const int m = (int) gi.size();
-    if (m < 2 || (m & 1)) { err = "unexpected GEMV count in the frame program"; return false; }
-    for (int k = 0; k < m; ++k) {
-        prog[gi[k]].slot = k & 1;
-        POp & site = prog[gi[(k - 2 + m) % m]];
-        site.issue = 1;
-        site.issue_slot = k & 1;
-        site.iA = prog[gi[k]].g.A;
-        site.iB = prog[gi[k]].g.B;
-        site.iG = prog[gi[k]].g.norm_g;
+    if (m < 4 || (m & 1)) { err = "unexpected GEMV count in the frame program"; return false; }
+    const int lead = std::max(2, std::min(df_pf_lead, m - 1));
+    for (int j = 0; j < m; ++j) {
+        DfOp & site = prog[gi[j]];
+        site.slot = j & 1;
+        const DfOp & nx = prog[gi[(j + 2) % m]];
+        site.iA = nx.A; site.iB = nx.B; site.iG = nx.norm_g;
+        const DfOp & pf = prog[gi[(j + lead) % m]];
+        site.pA = pf.A; site.pB = pf.B;
     }
-    pk_first[0] = gi[0];
-    pk_first[1] = gi[1];
-    // Shared memory: two weight buffers sized for the largest per-CTA slice,
-    // then the work area (GEMV activations / attention scores).
-    size_t wb = 0;
-    for (int k = 0; k < m; ++k) {
-        const GemvArgs & g = prog[gi[k]].g;
-        wb = std::max(wb, slice_layout(g.A, g.B.w != nullptr, g.norm_g != nullptr, gemv_rpc(g.A.rows, n_sm)).total);
-    }
-    pk_wbuf = (wb + 127) & ~(size_t) 127;
+    df_first[0] = gi[0];
+    df_first[1] = gi[1];
+    n_df_pf0 = 0;
+    for (int j = 2; j < lead && n_df_pf0 < 8; ++j) df_pf0[n_df_pf0++] = gi[j];
 
-    // L2 prefetch schedule: each GEMV's weights are prefetched by the op that
-    // runs pf_lead_bytes earlier in the (cyclic) weight stream.
-    auto wbytes = [](const GemvArgs & g) {
-        auto one = [](const DMat & mm) -> double {
-            if (!mm.w) return 0.0;
-            return mm.type == W_F16 ? (double) mm.rows * mm.cols * 2.0 : (double) mm.rows * mm.cols * 34.0 / 32.0;
-        };
-        return one(g.A) + one(g.B);
-    };
-    std::vector<double> pb, sz;
-    double T = 0.0;
-    for (int k = 0; k < m; ++k) { pb.push_back(T); sz.push_back(wbytes(prog[gi[k]].g)); T += sz.back(); }
-    const double lead = std::min(pf_lead_bytes, T * 0.5);
-    n_pf0 = 0;
-    for (int k = 0; k < m; ++k) {
-        if (pb[k] < lead && n_pf0 < 16) pf0[n_pf0++] = gi[k];
-        double t = pb[k] - lead;
-        if (t < 0) t += T;
-        size_t j = std::upper_bound(pb.begin(), pb.end(), t) - pb.begin();
-        j = j == 0 ? 0 : j - 1;
-        for (size_t site = gi[j]; site < prog.size(); ++site) {
-            if (prog[site].n_pf < PK_MAX_PF) {
-                prog[site].pfA[prog[site].n_pf] = prog[gi[k]].g.A;
-                prog[site].pfB[prog[site].n_pf] = prog[gi[k]].g.B;
-                prog[site].n_pf++;
-                break;
-            }
+    // shared memory: two weight buffers, the work area, the attention table, the hidden row
+    size_t wb = 0, work = 0;
+    const int QKVD = QD() + 2 * KD();
+    for (const DfOp & op : prog) {
+        if (op.type == DF_GEMV) {
+            const int rpc = gemv_rpc(op.A.rows, n_sm);
+            wb = std::max(wb, slice_layout(op.A, op.B.w != nullptr, op.norm_g != nullptr, rpc).total);
+            work = std::max(work, gemv_work_bytes(op.A.type, op.A.cols, op.nv, rpc));
+        } else {
+            work = std::max(work, ((size_t) QKVD * 4 + 127) / 128 * 128 + fused_attn_smem(max_keys, 1));
         }
     }
+    df_wbuf = (wb + 127) & ~(size_t) 127;
+    df_work = (work + 127) & ~(size_t) 127;
+    const size_t dyn = 2 * df_wbuf + df_work + df_att.size() * sizeof(FusedAttn) + (size_t) H * 4;
+    cudaFuncAttributes fa{};
+    QCHECK(cudaFuncGetAttributes(&fa, k_frame_dataflow));
+    if (dyn + fa.sharedSizeBytes > 227 * 1024) {
+        err = "dataflow frame kernel: shared memory too large for this context (" + std::to_string(dyn) + " B)";
+        return false;
+    }
+    QCHECK(cudaFuncSetAttribute(k_frame_dataflow, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) dyn));
+    df_dyn = dyn;
+    int nb = 0;
+    QCHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_frame_dataflow, DF_THREADS, dyn));
+    if (nb < 1) { err = "dataflow frame kernel does not fit on an SM"; return false; }
+
+    // tagged buffers: two slots each
+    const int slot_words[DB_N] = {H, 2 * H, 2 * QKVD, QD(), 2 * std::max(c.intermediate_size, c.code_pred_intermediate_size),
+                                  c.code_pred_vocab_size, c.codec_vocab_size};
+    size_t words = 0;
+    for (int b2 = 0; b2 < DB_N; ++b2) words += 2 * (size_t) slot_words[b2];
+    if (words > df_buf_words) {
+        if (d_dfbuf) cudaFree(d_dfbuf);
+        d_dfbuf = nullptr;
+        QCHECK(cudaMalloc(&d_dfbuf, words * 8));
+        df_buf_words = words;
+    }
+    QCHECK(cudaMemset(d_dfbuf, 0, words * 8));
+    df_tag_base = 1;
+    size_t off = 0;
+    for (int b2 = 0; b2 < DB_N; ++b2) {
+        df_bufp[b2] = d_dfbuf + off;
+        df_slot_words[b2] = slot_words[b2];
+        df_writes[b2] = wr[b2];
+        off += 2 * (size_t) slot_words[b2];
+    }
+
     // upload
     if (prog.size() > prog_cap) {
         if (d_prog) cudaFree(d_prog);
         prog_cap = prog.size();
-        QCHECK(cudaMalloc(&d_prog, sizeof(POp) * prog_cap));
+        QCHECK(cudaMalloc(&d_prog, sizeof(DfOp) * prog_cap));
     }
-    QCHECK(cudaMemcpy(d_prog, prog.data(), sizeof(POp) * prog.size(), cudaMemcpyHostToDevice));
-    if (!d_flags) {
-        QCHECK(cudaMalloc(&d_flags, sizeof(unsigned) * 1024));
-        QCHECK(cudaMalloc(&d_err, sizeof(int)));
+    QCHECK(cudaMemcpy(d_prog, prog.data(), sizeof(DfOp) * prog.size(), cudaMemcpyHostToDevice));
+    if (df_att.size() > att_cap) {
+        if (d_df_att) cudaFree(d_df_att);
+        att_cap = df_att.size();
+        QCHECK(cudaMalloc(&d_df_att, sizeof(FusedAttn) * att_cap));
     }
-    const size_t dyn = 2 * pk_wbuf + ((prog_smem + 127) & ~(size_t) 127);
-    cudaFuncAttributes fa{};
-    QCHECK(cudaFuncGetAttributes(&fa, k_frame_persistent));
-    if (dyn + fa.sharedSizeBytes > 227 * 1024) { err = "persistent kernel shared memory too large for this context"; return false; }
-    QCHECK(cudaFuncSetAttribute(k_frame_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) dyn));
-    pk_dyn = dyn;
-    int nb = 0;
-    QCHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_frame_persistent, PK_THREADS, dyn));
-    if (nb < 1) { err = "persistent frame kernel does not fit on an SM"; return false; }
+    QCHECK(cudaMemcpy(d_df_att, df_att.data(), sizeof(FusedAttn) * df_att.size(), cudaMemcpyHostToDevice));
+    if (!d_err) QCHECK(cudaMalloc(&d_err, sizeof(int)));
     prog_ok = true;
     return true;
 }
 
-bool Engine::launch_persistent(int n) {
-    PersistentArgs pa{};
-    pa.ops = d_prog; pa.n_ops = (int) prog.size(); pa.n_frames = n; pa.st = st; pa.sp = sp;
-    pa.out_codes = d_codes; pa.out_cap = codes_cap; pa.flags = d_flags; pa.err = d_err;
-    pa.n_pf0 = n_pf0;
-    for (int k = 0; k < n_pf0; ++k) pa.pf0[k] = pf0[k];
-    pa.wbuf_bytes = (int) pk_wbuf;
-    pa.trace = nullptr;
-    trace_n = 0;
-    if (getenv("QTTS_PK_TRACE")) {
-        const size_t need = (size_t) PK_TRACE_SLOTS * prog.size() * n;
-        if (need > trace_cap) {
-            if (d_trace) cudaFree(d_trace);
-            trace_cap = need;
-            QCHECK(cudaMalloc(&d_trace, sizeof(unsigned long long) * trace_cap));
-        }
-        QCHECK(cudaMemsetAsync(d_trace, 0, sizeof(unsigned long long) * need, stream));
-        pa.trace = d_trace;
-        trace_n = need;
+bool Engine::launch_dataflow(int n) {
+    const qtts_config & c = cfg;
+    const int n_ops = (int) prog.size();
+    // tags grow by n_ops per frame; restart from a cleared buffer before they wrap
+    if ((unsigned long long) df_tag_base + (unsigned long long)(n + 1) * n_ops >= 0xFFFFFFF0ull) {
+        QCHECK(cudaMemsetAsync(d_dfbuf, 0, df_buf_words * 8, stream));
+        df_tag_base = 1;
     }
-    pa.first_gemv[0] = pk_first[0];
-    pa.first_gemv[1] = pk_first[1];
-    QCHECK(cudaMemsetAsync(d_flags, 0, sizeof(unsigned) * n_sm, stream));
+    DfArgs a{};
+    a.ops = d_prog; a.n_ops = n_ops; a.n_frames = n; a.tag_base = df_tag_base;
+    for (int b = 0; b < DB_N; ++b) { a.buf[b] = df_bufp[b]; a.buf_slot[b] = df_slot_words[b]; a.buf_w[b] = df_writes[b]; }
+    a.att = d_df_att; a.n_att = (int) df_att.size();
+    a.st = st; a.sp = sp; a.out_codes = d_codes; a.out_cap = codes_cap; a.err = d_err;
+    a.codec_embd = codec_embd; a.cp_embd = d_cp_embd; a.trailing = trailing; a.pad = pad;
+    a.logits0 = logits; a.logits_out = logits; a.hidden = hidden;
+    a.eps = c.rms_norm_eps; a.H = c.hidden_size; a.n_cb = c.n_codebooks;
+    a.V0 = c.codec_vocab_size; a.V1 = c.code_pred_vocab_size;
+    a.wbuf_bytes = (int) df_wbuf; a.work_bytes = (int) df_work;
+    a.first[0] = df_first[0]; a.first[1] = df_first[1];
+    a.n_pf0 = n_df_pf0;
+    for (int k = 0; k < n_df_pf0; ++k) a.pf0[k] = df_pf0[k];
+    df_tag_base += (unsigned)((n + 1) * n_ops);
     QCHECK(cudaMemsetAsync(d_err, 0, sizeof(int), stream));
-    void * args[] = {&pa};
-    QCHECK(cudaLaunchCooperativeKernel((const void *) k_frame_persistent, dim3(n_sm), dim3(PK_THREADS), args,
-                                       pk_dyn, stream));
+    void * args[] = {&a};
+    QCHECK(cudaLaunchCooperativeKernel((const void *) k_frame_dataflow, dim3(n_sm), dim3(DF_THREADS), args, df_dyn,
+                                       stream));
     ++launches;
     return true;
 }
@@ -1323,8 +1347,9 @@ int Engine::begin(const qtts_generate_params * p) {
     }
     if (!sync("generate setup")) return -1;
     sess.st0 = hs;
-    if (use_persistent) {
-        if (!prog_ok && !build_program()) return -1;
+    if (use_dataflow) {
+        const int keys = std::min(n_ctx, plen + p->max_len + 1);   // the talker attention's longest row
+        if ((!prog_ok || keys > df_keys) && !build_program(std::max(keys, df_keys))) return -1;
         if (!graph_ok) { launches = 0; graph_ok = false; }
         launches_per_frame = 1;
     } else if (!graph_ok && !capture_graph()) return -1;
@@ -1361,8 +1386,8 @@ int Engine::run_frames(int n, int32_t * codes_out) {
     n = std::min(n, sess.max_len - sess.produced);
     if (n <= 0) return 0;
     if (cudaEventRecord(ev0, stream) != cudaSuccess) { err = "event"; return -1; }
-    if (use_persistent) {
-        if (!launch_persistent(n)) return -1;
+    if (use_dataflow) {
+        if (!launch_dataflow(n)) return -1;
     } else {
         for (int i = 0; i < n; ++i)
             if (cudaGraphLaunch(graph, stream) != cudaSuccess) { err = "graph launch failed"; return -1; }
@@ -1371,11 +1396,11 @@ int Engine::run_frames(int n, int32_t * codes_out) {
     DevState hs;
     int kerr = 0;
     if (cudaMemcpyAsync(&hs, st, sizeof(hs), cudaMemcpyDeviceToHost, stream) != cudaSuccess) { err = "state readback"; return -1; }
-    if (use_persistent && cudaMemcpyAsync(&kerr, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) {
+    if (use_dataflow && cudaMemcpyAsync(&kerr, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) {
         err = "error flag readback"; return -1;
     }
     if (!sync("frame loop")) return -1;
-    if (kerr) { err = "persistent frame kernel: grid barrier timed out"; sess.active = false; return -1; }
+    if (kerr) { err = "dataflow frame kernel: a wait timed out"; sess.active = false; return -1; }
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, ev0, ev1);
     timing.frames_ms += ms;
@@ -1984,26 +2009,6 @@ int32_t qtts_profile_frames(qtts_engine * h, int32_t n, qtts_kernel_stats * out,
     E.sess.produced = hs.n_out;
     E.sess.done = hs.done != 0;
     return got;
-}
-
-// Diagnostics of the persistent frame kernel (QTTS_PK_TRACE=1): the op types of
-// the frame program, and CTA 0's (start, work done) %globaltimer pairs of every
-// op of the last run.  Both return the number of values available.
-int32_t qtts_program_ops(const qtts_engine * h, int32_t * types, int32_t cap) {
-    if (!h) return -1;
-    const Engine & E = *reinterpret_cast<const Engine *>(h);
-    const int n = (int) E.prog.size();
-    for (int i = 0; i < n && i < cap; ++i) types[i] = E.prog[i].type;
-    return n;
-}
-int32_t qtts_op_trace(const qtts_engine * h, unsigned long long * out, int32_t cap) {
-    if (!h) return -1;
-    const Engine & E = *reinterpret_cast<const Engine *>(h);
-    if (!E.d_trace || !E.trace_n) return 0;
-    cudaSetDevice(E.dev);
-    const size_t n = std::min(E.trace_n, (size_t) std::max(cap, 0));
-    if (out && n) cudaMemcpy(out, E.d_trace, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost);
-    return (int32_t) E.trace_n;
 }
 
 int32_t qtts_get_timing(const qtts_engine * h, qtts_timing * out) {

@@ -1,0 +1,577 @@
+// frame_dataflow.cuh — the codec frame as one cooperative launch whose ops hand
+// activations to each other as tagged words.
+//
+// A frame of the batch-1 loop is a strict chain: every GEMV needs the whole
+// output vector of the op before it.  On B200 one such all-to-all hand-off
+// across the 148 SMs costs ~2.1 us whether it is a grid barrier followed by a
+// load or a poll of the data itself, so the frame time is (hand-offs) x (that
+// latency + the op's own work).  This kernel cuts both:
+//
+//   * activations travel as 64-bit words {F32 value, tag} (st_tagged): a
+//     consumer polls its input words until they carry the tag of the write it
+//     needs, so the data is the synchronisation (no barrier, no separate flag);
+//   * every CTA runs the samplers itself (the same decision everywhere, from
+//     the same logits and the same Philox draw) and builds the next input rows
+//     from the sampled code, so sampling and embedding gathers cost no hand-off;
+//   * the code-predictor step attention (<= 16 keys) runs as the O-projection's
+//     prologue, one warp per query head, in every CTA: no hand-off either;
+//   * each CTA keeps its own rows of the residual stream in shared memory (the
+//     O and down projections write the rows they later add to).
+//
+// A frame is 15 code-predictor passes x (5 layers x 4 GEMVs + head) + 28 talker
+// layers x (4 GEMVs + attention) + head = 456 hand-offs (548 launches in the
+// CUDA-graph frame).  Arithmetic is the CUDA-graph path's, op for op (the same
+// GEMV, attention, sampler and input-sum bodies, the same reduction orders), so
+// both give the same bits.
+//
+// Tags: the write of op k in frame f of a launch carries tag_base + f * n_ops +
+// k + 1; a tagged buffer has two slots, the w-th write of a frame going to slot
+// (f * writes_per_frame + w) & 1.  A slot is rewritten only after every reader
+// of its previous contents has finished: each GEMV uses all CTAs, so a CTA that
+// writes version n + 2 has read version n + 1 in full, which every CTA wrote
+// after reading version n.
+//
+// Every spin has an iteration limit; on expiry the kernel sets *err, waits
+// (bounded) for its own bulk copies in flight and returns (no GPU trap).
+#pragma once
+#include "kernels.cuh"
+
+namespace qtts {
+
+constexpr int DF_THREADS = 512;
+
+enum DfOpType : int { DF_GEMV = 1, DF_TATTN = 2 };
+
+// Where a GEMV's activation rows come from.
+enum DfPro : int {
+    PRO_POLL = 0,      // tagged rows of in_buf
+    PRO_CB0 = 1,       // sample codebook 0 (talker logits); rows [talker hidden, codec_embd[cb0]]
+    PRO_CBG = 2,       // sample code-predictor codebook cb; row cp_embd[cb - 1][code]
+    PRO_CBLAST = 3,    // sample the last codebook; row = the next talker step's input sum
+    PRO_CPATTN2 = 4,   // code-predictor 2-row prefill attention (F32 K/V of this pass)
+    PRO_CPATTN = 5,    // code-predictor step attention (1 row, F16 cache)
+};
+
+// Tagged buffers (two slots each).
+enum DfBuf : int { DB_X = 0, DB_XCP, DB_QKV, DB_ATT, DB_H, DB_LCP, DB_LT, DB_N };
+
+struct alignas(16) DfOp {
+    int type, pro, nv;
+    int in_buf, in_op, in_wr, in_row;   // tagged input: buffer, producer op (< 0: the previous frame's
+                                        // op in_op + n_ops), the producer's write index, first row
+    int out_buf, out_wr;                // tagged output and this op's write index of it in the frame
+    int cb, layer, n_past;              // sampler codebook; attention table entry; CP position
+    int slot, act, epi, head;           // weight buffer; activation mode; epilogue; 1: talker codec head
+    DMat A, B;
+    const float * norm_g;
+    DMat iA, iB;                        // slice copied into `slot` once this op is done (iA.w: none)
+    const float * iG;
+    DMat pA, pB;                        // slice prefetched into L2 once this op is done (pA.w: none)
+};
+
+struct DfArgs {
+    const DfOp * ops;
+    int n_ops, n_frames;
+    unsigned tag_base;
+    unsigned long long * buf[DB_N];     // tagged buffers, two slots each
+    int buf_slot[DB_N];                 // words per slot
+    int buf_w[DB_N];                    // writes per frame
+    const FusedAttn * att;              // attention table: code-predictor layers, then talker layers
+    int n_att;
+    DevState * st;
+    const SampleParams * sp;
+    int * out_codes;
+    int out_cap;
+    int * err;
+    const __half * codec_embd;
+    const __half * const * cp_embd;     // device array of n_cb - 1 tables
+    const float * trailing, * pad;
+    const float * logits0;              // talker logits before the launch (frame 0's codebook-0 input)
+    float * logits_out;                 // talker logits, written by every frame's head
+    float * hidden;                     // talker hidden state: read at launch, written by every frame's head
+    float eps;
+    int H, n_cb, V0, V1;
+    int wbuf_bytes, work_bytes;
+    int first[2];                       // the frame's first two GEMV ops (slices copied at launch)
+    int n_pf0;
+    int pf0[8];                         // GEMV ops prefetched into L2 at launch
+};
+
+__device__ __forceinline__ void df_prefetch_l2(const void * p, size_t bytes) {
+    const char * c = static_cast<const char *>(p);
+    while (bytes > 0) {
+        const unsigned n = (unsigned)(bytes > 65536 ? 65536 : bytes);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
+        c += n;
+        bytes -= n;
+    }
+}
+
+// This CTA's row slice of a weight matrix (the GEMV row split) into L2.
+__device__ __forceinline__ void df_prefetch_slice(const DMat & M, int cta, int ncta) {
+    if (!M.w) return;
+    const int rpc = gemv_rpc(M.rows, ncta);
+    const int r0 = cta * rpc, r1 = min(M.rows, r0 + rpc);
+    if (r0 >= r1) return;
+    const size_t es = M.type == W_F16 ? 2 : 1;
+    df_prefetch_l2(static_cast<const char *>(M.w) + (size_t) r0 * M.cols * es, (size_t)(r1 - r0) * M.cols * es);
+    if (M.type == W_Q8_0) df_prefetch_l2(M.d + (size_t) r0 * (M.cols / 32), (size_t)(r1 - r0) * (M.cols / 32) * 2);
+}
+
+__device__ __forceinline__ unsigned df_tag(const DfArgs & P, int f, int op) {
+    return P.tag_base + (unsigned) f * (unsigned) P.n_ops + (unsigned) op + 1u;
+}
+__device__ __forceinline__ unsigned long long * df_slot(const DfArgs & P, int b, int f, int wr) {
+    return P.buf[b] + (size_t)((unsigned)(f * P.buf_w[b] + wr) & 1u) * P.buf_slot[b];
+}
+// The op's tagged input in frame f: producer tag and slot.
+__device__ __forceinline__ unsigned df_in_tag(const DfArgs & P, const DfOp & op, int f) {
+    return op.in_op < 0 ? df_tag(P, f - 1, op.in_op + P.n_ops) : df_tag(P, f, op.in_op);
+}
+__device__ __forceinline__ const unsigned long long * df_in(const DfArgs & P, const DfOp & op, int f) {
+    return df_slot(P, op.in_buf, op.in_op < 0 ? f - 1 : f, op.in_wr);
+}
+
+// Polls word pairs p = tid, tid + nt, ... < npairs of `src` (at most MAXP per
+// thread, all in flight together) until both words carry `tag`, handing each
+// pair to sink(p, v0, v1).  False when the limit ran out or another CTA
+// reported an error.
+template <int MAXP, class Addr, class Sink>
+__device__ __forceinline__ bool df_poll_pairs_at(int npairs, unsigned tag, const Addr & addr, const Sink & sink,
+                                                 const int * err) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    unsigned pend = 0u;
+#pragma unroll
+    for (int k = 0; k < MAXP; ++k)
+        if (tid + k * nt < npairs) pend |= 1u << k;
+    for (unsigned long long it = 0; pend && it < QTTS_SPIN_LIMIT; ++it) {
+        unsigned long long a[MAXP], b[MAXP];
+#pragma unroll
+        for (int k = 0; k < MAXP; ++k)
+            if (pend >> k & 1u) ld_tagged2(addr(tid + k * nt), a[k], b[k]);
+#pragma unroll
+        for (int k = 0; k < MAXP; ++k)
+            if ((pend >> k & 1u) && tag_of(a[k]) == tag && tag_of(b[k]) == tag) {
+                sink(tid + k * nt, val_of(a[k]), val_of(b[k]));
+                pend &= ~(1u << k);
+            }
+        if ((it & 255u) == 255u && *(volatile const int *) err) break;
+    }
+    return pend == 0u;
+}
+template <int MAXP, class Sink>
+__device__ __forceinline__ bool df_poll_pairs(const unsigned long long * src, int npairs, unsigned tag,
+                                              const Sink & sink, const int * err) {
+    return df_poll_pairs_at<MAXP>(npairs, tag, [&](int p) { return src + 2 * (size_t) p; }, sink, err);
+}
+
+// N float quads (two word pairs each) of one lane, all in flight together.
+template <int N>
+__device__ __forceinline__ bool df_poll_quads(const unsigned long long * const * src, int n, unsigned tag, float4 * out,
+                                              const int * err) {
+    unsigned pend = (1u << n) - 1u;
+    for (unsigned long long it = 0; pend && it < QTTS_SPIN_LIMIT; ++it) {
+        unsigned long long w[N][4];
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if (pend >> k & 1u) {
+                ld_tagged2(src[k], w[k][0], w[k][1]);
+                ld_tagged2(src[k] + 2, w[k][2], w[k][3]);
+            }
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if ((pend >> k & 1u) && tag_of(w[k][0]) == tag && tag_of(w[k][1]) == tag && tag_of(w[k][2]) == tag &&
+                tag_of(w[k][3]) == tag) {
+                out[k] = make_float4(val_of(w[k][0]), val_of(w[k][1]), val_of(w[k][2]), val_of(w[k][3]));
+                pend &= ~(1u << k);
+            }
+        if ((it & 255u) == 255u && *(volatile const int *) err) break;
+    }
+    return pend == 0u;
+}
+
+// Rows [0, nv) of width cols (tagged) into the GEMV work area, two-plane layout.
+__device__ __forceinline__ bool df_poll_rows(const unsigned long long * src, int cols, int nv, unsigned tag, float * xs,
+                                             const int * err) {
+    return df_poll_pairs<6>(src, nv * cols / 2, tag,
+                            [&](int p, float v0, float v1) {
+                                const int e = 2 * p, v = e / cols, c = e - v * cols;
+                                *reinterpret_cast<float2 *>(xs + v * cols + xpos(c, cols)) = make_float2(v0, v1);
+                            },
+                            err);
+}
+
+// Output of a GEMV op: tagged words, optionally a plain copy, and this CTA's
+// residual rows when the op advances the residual stream.
+struct DfStore {
+    unsigned long long * out;
+    int ld;
+    unsigned tag;
+    float * plain;
+    float (*res)[8];
+    __device__ __forceinline__ void operator()(int r, int rl, int v, float val) const {
+        st_tagged(out + (size_t) v * ld + r, val, tag);
+        if (plain) plain[(size_t) v * ld + r] = val;
+        if (res) res[v][rl] = val;
+    }
+};
+
+// Code-predictor 2-row prefill attention of unit (query head hq, row i), one
+// warp, the arithmetic of fused_attn_body in F32 mode for M = 2: rows 0..i of
+// this pass are the keys; q and k get the per-head RMSNorm and NEOX RoPE of
+// their positions; scores by 8-lane groups of 16 dims each (xor butterfly 4, 2,
+// 1); softmax max / exp / double sum / e * (float)(1 / sum); P x V as position
+// groups summed in order.  kv_write: append row i's K/V (F16) to the cache.
+// Returns the output quad of dims 4 lane .. 4 lane + 3.
+__device__ __forceinline__ float4 df_cp_prefill_unit(const FusedAttn & a, int hq, int i, int n_past, const float4 qv,
+                                                     const float4 * kv, const float4 * vv, bool kv_write) {
+    const int lane = threadIdx.x & 31;
+    const int NKV = a.n_kv_heads, g = hq / (a.n_heads / NKV);
+    const size_t pstride = (size_t) NKV * QTTS_HD;
+    float xq[4] = {qv.x, qv.y, qv.z, qv.w};
+    head_norm_rope(xq, a.q_norm, a.eps, a.rope + (size_t)(n_past + i) * (QTTS_HD / 2), lane);
+    float xk[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        if (j > i) break;
+        xk[j][0] = kv[j].x; xk[j][1] = kv[j].y; xk[j][2] = kv[j].z; xk[j][3] = kv[j].w;
+        head_norm_rope(xk[j], a.k_norm, a.eps, a.rope + (size_t)(n_past + j) * (QTTS_HD / 2), lane);
+    }
+    if (kv_write) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            a.kc[(size_t)(n_past + i) * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = __float2half_rn(xk[i][k]);
+            a.vc[(size_t)(n_past + i) * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = __float2half_rn((&vv[i].x)[k]);
+        }
+    }
+    // score of key j: the 8-lane group sub = lane & 7 chains dims 16 sub .. 16 sub + 15 (lanes 4 sub .. 4 sub + 3)
+    const int sub = lane & 7;
+    float sc[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        float s = 0.0f;
+#pragma unroll
+        for (int d = 0; d < 16; ++d) {
+            const int src = 4 * sub + (d >> 2);
+            const float qd = __shfl_sync(0xffffffffu, xq[d & 3], src);
+            const float kd = __shfl_sync(0xffffffffu, xk[j <= i ? j : 0][d & 3], src);
+            s = fmaf(kd, qd, s);
+        }
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        sc[j] = __fmul_rn(s, a.scale);
+    }
+    const int n = i + 1;
+    const float mx = n == 2 ? fmaxf(sc[0], sc[1]) : sc[0];
+    const float e0 = qtts_expf(__fsub_rn(sc[0], mx));
+    const float e1 = n == 2 ? qtts_expf(__fsub_rn(sc[1], mx)) : 0.0f;
+    const double sum = n == 2 ? (double) e0 + (double) e1 : (double) e0;
+    const float inv = (float)(1.0 / sum);
+    const float p0 = __fmul_rn(e0, inv), p1 = __fmul_rn(e1, inv);
+    float o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float part0 = fmaf(p0, (&vv[0].x)[k], 0.0f);
+        const float part1 = n == 2 ? fmaf(p1, (&vv[1 < n ? 1 : 0].x)[k], 0.0f) : 0.0f;
+        float s = __fadd_rn(0.0f, part0);
+        s = __fadd_rn(s, part1);
+        o[k] = __fadd_rn(s, 0.0f);   // the position groups with no key
+    }
+    return make_float4(o[0], o[1], o[2], o[3]);
+}
+
+// Waits (bounded) for the copies still in flight into either weight buffer.
+__device__ __forceinline__ void df_drain(uint64_t * mbar, unsigned pending, unsigned phase) {
+    if (threadIdx.x != 0) return;
+    for (int b = 0; b < 2; ++b)
+        if (pending >> b & 1u) mbar_wait(mbar + b, phase >> b & 1u);
+}
+
+__global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ DfOp desc[2];
+    __shared__ __align__(8) uint64_t mbar[2];
+    __shared__ DevState s_st;                 // this CTA's frame state (presence set, codes)
+    __shared__ SampleParams s_sp;
+    __shared__ float s_res[2][8];             // this CTA's rows of the residual stream
+    __shared__ const __half * s_tab[QTTS_MAX_CB];
+    __shared__ int s_bad;
+    const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nt = blockDim.x, nw = nt >> 5;
+    uint8_t * work = smem + 2 * (size_t) P.wbuf_bytes;
+    FusedAttn * att = reinterpret_cast<FusedAttn *>(work + P.work_bytes);
+    float * hid = reinterpret_cast<float *>(att + P.n_att);
+    const int H = P.H;
+    const int rpc_h = gemv_rpc(H, ncta), r0_h = cta * rpc_h;
+    const int nrow_h = max(0, min(H, r0_h + rpc_h) - r0_h);
+    constexpr int NW = (int)(sizeof(DfOp) / 8);
+    static_assert(sizeof(DfOp) % 8 == 0 && NW <= DF_THREADS, "descriptor copy");
+    static_assert(sizeof(FusedAttn) % 8 == 0, "attention table copy");
+    unsigned phase = 0u, pending = 0u;
+
+    if (tid == 0) {
+        mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_sp = *P.sp;
+        if (cta != 0) s_sp.record_logits = 0;   // CTA 0 records the debug logits
+        s_bad = 0;
+    }
+    if (tid < NW) reinterpret_cast<unsigned long long *>(&desc[0])[tid] = reinterpret_cast<const unsigned long long *>(P.ops)[tid];
+    {
+        const int n8 = P.n_att * (int)(sizeof(FusedAttn) / 8);
+        for (int w = tid; w < n8; w += nt)
+            reinterpret_cast<unsigned long long *>(att)[w] = reinterpret_cast<const unsigned long long *>(P.att)[w];
+    }
+    for (int i = tid; i < (int)(sizeof(DevState) / 4); i += nt)
+        reinterpret_cast<int *>(&s_st)[i] = reinterpret_cast<const volatile int *>(P.st)[i];
+    for (int c = tid; c < H; c += nt) hid[c] = __ldcg(P.hidden + c);
+    if (tid >= 1 && tid < P.n_cb) s_tab[tid] = P.cp_embd[tid - 1];
+    __syncthreads();
+    if (tid == 0) {
+        for (int k = 0; k < P.n_pf0; ++k) {
+            df_prefetch_slice(P.ops[P.pf0[k]].A, cta, ncta);
+            df_prefetch_slice(P.ops[P.pf0[k]].B, cta, ncta);
+        }
+        for (int b = 0; b < 2; ++b) {
+            const DfOp & g = P.ops[P.first[b]];
+            issue_gemv_slice(g.A, g.B, g.norm_g, smem + (size_t) g.slot * P.wbuf_bytes, mbar + g.slot, cta, ncta);
+        }
+    }
+    pending = 3u;
+    const int pos0 = s_st.pos, frame0 = s_st.frame, n_tr = s_st.n_trailing;
+    const int QD = att[0].n_heads * QTTS_HD, KD = att[0].n_kv_heads * QTTS_HD;
+    bool stop = false, failed = false;
+
+    for (int f = 0; f < P.n_frames && !stop; ++f) {
+        const int frame = frame0 + f;
+        for (int k = 0; k < P.n_ops; ++k) {
+            const DfOp & op = desc[k & 1];
+            const int nx = k + 1 < P.n_ops ? k + 1 : 0;
+            const unsigned long long nword = tid < NW ? reinterpret_cast<const unsigned long long *>(P.ops + nx)[tid] : 0ull;
+            bool ok = true;
+            if (op.type == DF_GEMV) {
+                const int cols = op.A.cols;
+                const int rpc = gemv_rpc(op.A.rows, ncta);
+                const bool q8 = op.A.type == W_Q8_0;
+                const GemvWork W = op.nv == 1 ? gemv_work<1>(work, cols, rpc, q8) : gemv_work<2>(work, cols, rpc, q8);
+                float * xs = W.xs;
+                // ---- activation rows
+                if (op.pro == PRO_POLL) {
+                    ok = df_poll_rows(df_in(P, op, f) + (size_t) op.in_row * cols, cols, op.nv, df_in_tag(P, op, f),
+                                      xs, P.err);
+                } else if (op.pro == PRO_CB0 || op.pro == PRO_CBG || op.pro == PRO_CBLAST) {
+                    const int cb = op.cb, V = cb == 0 ? P.V0 : P.V1;
+                    int tok;
+                    if (cb == 0 && f == 0) {
+                        tok = sample_body_l<8>(
+                            [&](float * l) {
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) {
+                                    const int i = tid * 8 + e;
+                                    l[e] = i < V ? __ldcg(P.logits0 + i) : -INFINITY;
+                                }
+                            },
+                            V, cb, &s_st, s_sp, frame);
+                    } else {
+                        const unsigned long long * src = df_in(P, op, f);
+                        const unsigned tag = df_in_tag(P, op, f);
+                        tok = sample_body_l<8>(
+                            [&](float * l) {
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) l[e] = -INFINITY;
+                                const int np = max(0, min(4, (V - tid * 8) / 2));
+                                unsigned pend = (1u << np) - 1u;
+                                for (unsigned long long it = 0; pend && it < QTTS_SPIN_LIMIT; ++it) {
+                                    unsigned long long a[4], b[4];
+#pragma unroll
+                                    for (int q = 0; q < 4; ++q)
+                                        if (pend >> q & 1u) ld_tagged2(src + tid * 8 + 2 * q, a[q], b[q]);
+#pragma unroll
+                                    for (int q = 0; q < 4; ++q)
+                                        if ((pend >> q & 1u) && tag_of(a[q]) == tag && tag_of(b[q]) == tag) {
+                                            l[2 * q] = val_of(a[q]);
+                                            l[2 * q + 1] = val_of(b[q]);
+                                            pend &= ~(1u << q);
+                                        }
+                                    if ((it & 255u) == 255u && *(volatile const int *) P.err) break;
+                                }
+                                if (pend) s_bad = 1;
+                            },
+                            V, cb, &s_st, s_sp, frame);
+                    }
+                    __syncthreads();
+                    if (s_bad) {
+                        ok = false;
+                    } else if (cb == 0 && tok == s_sp.eos_id) {
+                        if (cta == 0 && tid == 0) sample_commit(tok, 0, P.st, s_sp, P.out_codes, P.out_cap, frame);
+                        stop = true;
+                    } else {
+                        if (tid == 0) {
+                            s_st.codes[cb] = tok;
+                            if (cb == 0) s_st.presence[tok >> 5] |= 1u << (tok & 31);
+                            if (cta == 0) sample_commit(tok, cb, P.st, s_sp, P.out_codes, P.out_cap, frame);
+                        }
+                        __syncthreads();
+                        // input rows of the pass (same values and sums as frame_inputs_body)
+                        for (int c = tid; c < H; c += nt) {
+                            float x0, x1 = 0.0f;
+                            if (op.pro == PRO_CB0) {
+                                x0 = hid[c];
+                                x1 = __half2float(P.codec_embd[(size_t) tok * H + c]);
+                            } else if (op.pro == PRO_CBG) {
+                                x0 = __half2float(s_tab[cb][(size_t) tok * H + c]);
+                            } else {
+                                float s = __half2float(P.codec_embd[(size_t) s_st.codes[0] * H + c]);
+                                for (int q = 1; q < P.n_cb; ++q)
+                                    s = __fadd_rn(s, __half2float(s_tab[q][(size_t) s_st.codes[q] * H + c]));
+                                const float t = frame < n_tr ? P.trailing[(size_t) frame * H + c] : P.pad[c];
+                                x0 = __fadd_rn(s, t);
+                            }
+                            xs[xpos(c, H)] = x0;
+                            if (op.nv == 2) xs[H + xpos(c, H)] = x1;
+                            const int rl = c - r0_h;
+                            if (rl >= 0 && rl < nrow_h) {
+                                s_res[0][rl] = x0;
+                                s_res[1][rl] = x1;
+                            }
+                        }
+                    }
+                } else {   // code-predictor attention into the O-projection's rows
+                    const FusedAttn & a = att[op.layer];
+                    const int NH = a.n_heads, G = NH / a.n_kv_heads;
+                    const unsigned long long * q = df_in(P, op, f);
+                    const unsigned tag = df_in_tag(P, op, f);
+                    bool wrote = false;
+                    if (op.pro == PRO_CPATTN) {
+                        for (int hq = warp; hq < NH; hq += nw) {
+                            const int g = hq / G;
+                            CpStepRegs R;
+                            cp_step_load(a, hq, op.n_past, R);
+                            const unsigned long long * srcs[3] = {q + (size_t) hq * QTTS_HD + lane * 4,
+                                                                  q + QD + (size_t) g * QTTS_HD + lane * 4,
+                                                                  q + QD + KD + (size_t) g * QTTS_HD + lane * 4};
+                            float4 in[3];
+                            // a lane that timed out makes the whole warp give up (the body shuffles over all lanes)
+                            if (!__all_sync(0xffffffffu, df_poll_quads<3>(srcs, 3, tag, in, P.err))) { s_bad = 1; break; }
+                            const bool w = cta == 0 && hq % G == 0;
+                            const float4 o = cp_step_compute(a, hq, op.n_past, R, in[0], in[1], in[2], w);
+                            wrote |= w;
+                            *reinterpret_cast<float4 *>(xs + xpos(hq * QTTS_HD + lane * 4, QD)) = o;
+                        }
+                    } else {
+                        const int QKVD = QD + 2 * KD;
+                        for (int u = warp; u < 2 * NH; u += nw) {
+                            const int hq = u % NH, i = u / NH, g = hq / G;
+                            const unsigned long long * srcs[5] = {
+                                q + (size_t) i * QKVD + (size_t) hq * QTTS_HD + lane * 4,
+                                q + QD + (size_t) g * QTTS_HD + lane * 4,
+                                q + QD + KD + (size_t) g * QTTS_HD + lane * 4,
+                                q + QKVD + QD + (size_t) g * QTTS_HD + lane * 4,
+                                q + QKVD + QD + KD + (size_t) g * QTTS_HD + lane * 4};
+                            float4 in[5] = {};
+                            if (!__all_sync(0xffffffffu, df_poll_quads<5>(srcs, i == 0 ? 3 : 5, tag, in, P.err))) {
+                                s_bad = 1;
+                                break;
+                            }
+                            const float4 kv[2] = {in[1], in[3]}, vv[2] = {in[2], in[4]};
+                            const bool w = cta == 0 && hq % G == 0;
+                            const float4 o = df_cp_prefill_unit(a, hq, i, op.n_past, in[0], kv, vv, w);
+                            wrote |= w;
+                            *reinterpret_cast<float4 *>(xs + i * QD + xpos(hq * QTTS_HD + lane * 4, QD)) = o;
+                        }
+                    }
+                    if (wrote) __threadfence();   // cache rows before this CTA's tagged outputs
+                }
+                if (__syncthreads_or(!ok || s_bad)) {
+                    failed = true;
+                } else if (!stop) {
+                    // residual rows of this CTA, then the GEMV
+                    if (op.epi == EPI_RESID) {
+                        const int rstride = (rpc + 3) & ~3;
+                        for (int t = tid; t < op.nv * nrow_h; t += nt)
+                            W.rs[(t / nrow_h) * rstride + t % nrow_h] = s_res[t / nrow_h][t % nrow_h];
+                        __syncthreads();
+                    }
+                    GemvArgs g{};
+                    g.A = op.A;
+                    g.B = op.B;
+                    g.nv = op.nv;
+                    g.norm_g = op.norm_g;
+                    g.eps = P.eps;
+                    g.act = op.act;
+                    g.epi = op.epi;
+                    g.xn_out = op.head == 1 ? P.hidden : nullptr;   // CTA 0: the plain talker hidden state
+                    g.ldxn = H;
+                    const DfStore store{df_slot(P, op.out_buf, f, op.out_wr), op.A.rows, df_tag(P, f, k),
+                                        op.head == 1 ? P.logits_out : nullptr, op.epi == EPI_RESID ? s_res : nullptr};
+                    const int b = op.slot;
+                    uint8_t * wb = smem + (size_t) b * P.wbuf_bytes;
+                    const unsigned par = phase >> b & 1u;
+                    const bool gok = op.nv == 1
+                        ? gemv_compute<1>(g, cta, ncta, wb, work, mbar + b, par, store, op.head == 1 ? hid : nullptr)
+                        : gemv_compute<2>(g, cta, ncta, wb, work, mbar + b, par, store, nullptr);
+                    if (!gok) failed = true;
+                    phase ^= 1u << b;
+                    pending &= ~(1u << b);
+                }
+            } else {   // DF_TATTN: talker attention, one query head per CTA
+                const FusedAttn & a0 = att[op.layer];
+                const int NH = a0.n_heads, G = NH / a0.n_kv_heads;
+                if (cta < NH) {
+                    const int hq = cta, g = hq / G;
+                    float * stage = reinterpret_cast<float *>(work);   // the q|k|v row, only this unit's parts
+                    const unsigned long long * q = df_in(P, op, f);
+                    // pair p < 64: q of head hq; 64..127: k of group g; 128..191: v of group g
+                    auto off = [&](int p) {
+                        const int part = p / (QTTS_HD / 2), c = 2 * (p % (QTTS_HD / 2));
+                        return (part == 0 ? hq * QTTS_HD : QD + (part == 2 ? KD : 0) + g * QTTS_HD) + c;
+                    };
+                    ok = df_poll_pairs_at<1>(3 * QTTS_HD / 2, df_in_tag(P, op, f), [&](int p) { return q + off(p); },
+                                             [&](int p, float v0, float v1) {
+                                                 *reinterpret_cast<float2 *>(stage + off(p)) = make_float2(v0, v1);
+                                             },
+                                             P.err);
+                    fence_acq_rel_gpu();   // the cached K/V rows other CTAs appended are read after this
+                    if (__syncthreads_or(!ok)) {
+                        failed = true;
+                    } else {
+                        FusedAttn a = a0;
+                        a.qkv = stage;
+                        a.fout = df_slot(P, op.out_buf, f, op.out_wr);
+                        a.ftag = df_tag(P, f, k);
+                        fused_attn_body(a, hq, work + ((size_t)(QD + 2 * KD) * 4 + 127) / 128 * 128, pos0 + f, frame);
+                    }
+                }
+            }
+            if (failed) {
+                if (tid == 0) atomicExch(P.err, 2);
+                break;
+            }
+            if (stop) break;
+            __syncthreads();   // everyone is done with desc[k & 1] and with the op's weight buffer
+            if (tid < NW) reinterpret_cast<unsigned long long *>(&desc[(k + 1) & 1])[tid] = nword;
+            if (op.type == DF_GEMV && tid == 0) {
+                if (op.iA.w) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue_gemv_slice(op.iA, op.iB, op.iG, smem + (size_t) op.slot * P.wbuf_bytes, mbar + op.slot,
+                                     cta, ncta);
+                }
+                df_prefetch_slice(op.pA, cta, ncta);
+                df_prefetch_slice(op.pB, cta, ncta);
+            }
+            if (op.type == DF_GEMV && op.iA.w) pending |= 1u << op.slot;
+            __syncthreads();
+        }
+        if (failed || stop) break;
+        if (cta == 0 && tid == 0) {
+            P.st->pos = pos0 + f + 1;
+            P.st->frame = frame + 1;
+            P.st->n_out += 1;
+        }
+    }
+    df_drain(mbar, pending, phase);
+}
+
+}  // namespace qtts

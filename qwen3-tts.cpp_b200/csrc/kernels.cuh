@@ -674,6 +674,8 @@ struct FusedAttn {
     uint8_t * xt;             // optional: output also as F16 tiles for the O-projection GEMM (row xt_row0 + i)
     int xt_np, xt_row0;
     int warp_heads;           // code-predictor step: one warp per query head (cp_step_attn_warp)
+    unsigned long long * fout;  // dataflow frame kernel: output as tagged words [M][ldo] instead of `out`
+    unsigned ftag;
 };
 
 constexpr int FA_THREADS = 512;
@@ -719,8 +721,8 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
         const int j = it * (FA_THREADS / 8) + warp * 4 + slot;
         if (j < nc) {
             const uint4 * kp = reinterpret_cast<const uint4 *>(kbase + (size_t) j * pstride + sub * 16);
-            kr[it][0] = kp[0];
-            kr[it][1] = kp[1];
+            kr[it][0] = __ldcg(kp);
+            kr[it][1] = __ldcg(kp + 1);
         } else {
             kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
         }
@@ -730,7 +732,7 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
         const __half2 * vp = reinterpret_cast<const __half2 *>(vbase + (size_t) pg * pstride) + d2;
         const size_t vstep = (size_t) FA_NPG * pstride / 2;
 #pragma unroll
-        for (int t = 0; t < FA_VIT; ++t) vr[t] = pg + t * FA_NPG < nc ? vp[t * vstep] : __float2half2_rn(0.0f);
+        for (int t = 0; t < FA_VIT; ++t) vr[t] = pg + t * FA_NPG < nc ? __ldcg(vp + t * vstep) : __float2half2_rn(0.0f);
     }
     if (warp == 0) {
         const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
@@ -778,8 +780,8 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
             if (p0 > 0) {
                 if (j < nc) {
                     const uint4 * kp = reinterpret_cast<const uint4 *>(kbase + (size_t) j * pstride + sub * 16);
-                    kr[it][0] = kp[0];
-                    kr[it][1] = kp[1];
+                    kr[it][0] = __ldcg(kp);
+                    kr[it][1] = __ldcg(kp + 1);
                 } else {
                     kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
                 }
@@ -840,7 +842,7 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
             const int j = p0 + pg + t * FA_NPG;
             float2 v;
             if (j < nc) {
-                if (p0 > 0) vr[t] = vp[t * vstep];
+                if (p0 > 0) vr[t] = __ldcg(vp + t * vstep);
                 v = __half22float2(vr[t]);
             } else if (j < n) {
                 v = make_float2(vn[(j - jn0) * QTTS_HD + 2 * d2], vn[(j - jn0) * QTTS_HD + 2 * d2 + 1]);
@@ -859,7 +861,12 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
         float s = 0.0f;
 #pragma unroll
         for (int q = 0; q < FA_NPG; ++q) s = __fadd_rn(s, part[q * QTTS_HD + tid]);
-        a.out[(size_t) i * a.ldo + (size_t) hq * QTTS_HD + tid] = s;
+        if (a.fout) {   // the KV rows this unit appended are ordered before the tagged output
+            __threadfence();
+            st_tagged(a.fout + (size_t) i * a.ldo + (size_t) hq * QTTS_HD + tid, s, a.ftag);
+        } else {
+            a.out[(size_t) i * a.ldo + (size_t) hq * QTTS_HD + tid] = s;
+        }
         if (a.xt)
             *reinterpret_cast<__half *>(a.xt + tc_x_off(a.xt_row0 + i, hq * QTTS_HD + tid, a.xt_np)) = __float2half_rn(s);
     }
@@ -878,40 +885,49 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
 // quads) is issued before the first use; the new row's K/V stay in registers.
 constexpr int CPA_MAX_KEYS = 16;
 
-// xt_row >= 0 and a.xt set: the output row is also written as F16 tiles (row
-// xt_row) for a tcgen05 O-projection.
-__device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int hq, const int n_past,
-                                                  const int xt_row = -1) {
+// Registers of one step-attention warp loaded before the q|k|v row is needed:
+// norm gains, RoPE row and the cached K halves / V quads.
+struct CpStepRegs {
+    float gq[4], gk[4];
+    float2 cs[4];
+    uint4 kr[8];
+    uint2 vr[CPA_MAX_KEYS];
+};
+
+// Cached K/V are read through L2 (ld.global.cg): within one launch of the
+// dataflow frame kernel another CTA rewrites these positions every frame.
+__device__ __forceinline__ void cp_step_load(const FusedAttn & a, const int hq, const int n_past, CpStepRegs & R) {
     const int lane = threadIdx.x & 31;
     const int NKV = a.n_kv_heads, G = a.n_heads / NKV, g = hq / G;
-    const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
     const size_t pstride = (size_t) NKV * QTTS_HD;
     const int h = lane & 1, jk = lane >> 1;
     const float2 * rp = a.rope + (size_t) n_past * (QTTS_HD / 2);
-    const float4 q4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) hq * QTTS_HD + lane * 4);
-    const float4 k4 = *reinterpret_cast<const float4 *>(a.qkv + QD + (size_t) g * QTTS_HD + lane * 4);
-    const float4 v4 = *reinterpret_cast<const float4 *>(a.qkv + QD + KD + (size_t) g * QTTS_HD + lane * 4);
-    float gq[4], gk[4];
-    float2 cs[4];
-    head_params(a.q_norm, rp, lane, gq, cs);
-    head_params(a.k_norm, rp, lane, gk, cs);
-    uint4 kr[8];
-    {
-        const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + (size_t) jk * pstride + (size_t) g * QTTS_HD + 64 * h);
+    head_params(a.q_norm, rp, lane, R.gq, R.cs);
+    head_params(a.k_norm, rp, lane, R.gk, R.cs);
+    const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + (size_t) jk * pstride + (size_t) g * QTTS_HD + 64 * h);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) kr[c] = jk < n_past ? kp[c] : make_uint4(0, 0, 0, 0);
-    }
-    uint2 vr[CPA_MAX_KEYS];
-    {
-        const __half * vb = a.vc + (size_t) g * QTTS_HD + lane * 4;
+    for (int c = 0; c < 8; ++c) R.kr[c] = jk < n_past ? __ldcg(kp + c) : make_uint4(0, 0, 0, 0);
+    const __half * vb = a.vc + (size_t) g * QTTS_HD + lane * 4;
 #pragma unroll
-        for (int j = 0; j < CPA_MAX_KEYS; ++j)
-            vr[j] = j < n_past ? *reinterpret_cast<const uint2 *>(vb + (size_t) j * pstride) : make_uint2(0, 0);
-    }
+    for (int j = 0; j < CPA_MAX_KEYS; ++j)
+        R.vr[j] = j < n_past ? __ldcg(reinterpret_cast<const uint2 *>(vb + (size_t) j * pstride)) : make_uint2(0, 0);
+}
+
+// The step attention of query head hq from its q row quad q4 and its group's new
+// k / v quads (lane l: dims 4l .. 4l + 3).  kv_write: this warp appends the
+// group's new K/V row to the cache (the group's first head).  Returns the output
+// quad of dims 4 lane .. 4 lane + 3.
+__device__ __forceinline__ float4 cp_step_compute(const FusedAttn & a, const int hq, const int n_past,
+                                                  const CpStepRegs & R, const float4 q4, const float4 k4,
+                                                  const float4 v4, const bool kv_write) {
+    const int lane = threadIdx.x & 31;
+    const int NKV = a.n_kv_heads, g = hq / (a.n_heads / NKV);
+    const size_t pstride = (size_t) NKV * QTTS_HD;
+    const int h = lane & 1, jk = lane >> 1;
     float xq[4] = {q4.x, q4.y, q4.z, q4.w};
     float xk[4] = {k4.x, k4.y, k4.z, k4.w};
-    head_norm_rope_v(xq, gq, cs, a.eps, lane);
-    head_norm_rope_v(xk, gk, cs, a.eps, lane);
+    head_norm_rope_v(xq, R.gq, R.cs, a.eps, lane);
+    head_norm_rope_v(xk, R.gk, R.cs, a.eps, lane);
     float kn[4], vn[4];   // the new row's k, v (F16-rounded), dims 4 lane .. 4 lane + 3
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -919,7 +935,7 @@ __device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int
         xq[k] = round_f16(xq[k]);
         kn[k] = __half2float(kh);
         vn[k] = __half2float(vh);
-        if (hq % G == 0) {
+        if (kv_write) {
             a.kc[(size_t) n_past * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = kh;
             a.vc[(size_t) n_past * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = vh;
         }
@@ -928,7 +944,7 @@ __device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int
     float acc = 0.0f;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const __half2 * hp = reinterpret_cast<const __half2 *>(&kr[c]);
+        const __half2 * hp = reinterpret_cast<const __half2 *>(&R.kr[c]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const int d = 8 * c + e, src = 16 * h + (d >> 2);     // lane holding dim 64h + d
@@ -952,8 +968,9 @@ __device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int
         const float pj = __shfl_sync(0xffffffffu, p, 2 * j);
         float v[4];
         if (j < n_past) {
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[j < CPA_MAX_KEYS ? j : 0].x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[j < CPA_MAX_KEYS ? j : 0].y));
+            const uint2 vq = R.vr[j < CPA_MAX_KEYS ? j : 0];
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&vq.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&vq.y));
             v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
         } else {
 #pragma unroll
@@ -962,18 +979,29 @@ __device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int
 #pragma unroll
         for (int k = 0; k < 4; ++k) o[k] = fmaf(pj, v[k], o[k]);
     }
-    *reinterpret_cast<float4 *>(a.out + (size_t) hq * QTTS_HD + lane * 4) = make_float4(o[0], o[1], o[2], o[3]);
+    return make_float4(o[0], o[1], o[2], o[3]);
+}
+
+// xt_row >= 0 and a.xt set: the output row is also written as F16 tiles (row
+// xt_row) for a tcgen05 O-projection.
+__device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int hq, const int n_past,
+                                                  const int xt_row = -1) {
+    const int lane = threadIdx.x & 31;
+    const int NKV = a.n_kv_heads, G = a.n_heads / NKV, g = hq / G;
+    const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
+    const float4 q4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) hq * QTTS_HD + lane * 4);
+    const float4 k4 = *reinterpret_cast<const float4 *>(a.qkv + QD + (size_t) g * QTTS_HD + lane * 4);
+    const float4 v4 = *reinterpret_cast<const float4 *>(a.qkv + QD + KD + (size_t) g * QTTS_HD + lane * 4);
+    CpStepRegs R;
+    cp_step_load(a, hq, n_past, R);
+    const float4 o = cp_step_compute(a, hq, n_past, R, q4, k4, v4, hq % G == 0);
+    *reinterpret_cast<float4 *>(a.out + (size_t) hq * QTTS_HD + lane * 4) = o;
     if (a.xt && xt_row >= 0) {
-        __align__(8) __half h4[4] = {__float2half_rn(o[0]), __float2half_rn(o[1]), __float2half_rn(o[2]),
-                                      __float2half_rn(o[3])};
+        __align__(8) __half h4[4] = {__float2half_rn(o.x), __float2half_rn(o.y), __float2half_rn(o.z),
+                                      __float2half_rn(o.w)};
         *reinterpret_cast<uint2 *>(a.xt + tc_x_off(xt_row, hq * QTTS_HD + lane * 4, a.xt_np)) =
             *reinterpret_cast<const uint2 *>(h4);
     }
-}
-
-// The persistent kernel's call (out of line: its registers stay with the caller's).
-__device__ __noinline__ void cp_step_attn_warp(const FusedAttn & a, const int hq, const int n_past) {
-    cp_step_attn_body(a, hq, n_past);
 }
 
 // Stand-alone launch (CUDA-graph frame path): one 32-thread CTA per query head.
@@ -1096,8 +1124,9 @@ __device__ double block_exscan_d(double v, double * total) {
 // cb == 0: codebook-0 rules of generate() (suppression, presence penalty, EOS
 // bias ramp).  cb >= 1: code-predictor sample_or_argmax.  PT elements per thread
 // (contiguous), blockDim.x * PT >= V.
-template <int PT>
-__device__ int sample_body(const float * logits, int V, int cb, const DevState * st, const SampleParams & P, int frame) {
+// `load(l)` fills this thread's PT logits l[e] of indices tid * PT + e (< V).
+template <int PT, class Load>
+__device__ int sample_body_l(const Load & load, int V, int cb, const DevState * st, const SampleParams & P, int frame) {
     __shared__ float redf[32];
     __shared__ double redd[32];
     __shared__ unsigned long long best;
@@ -1105,11 +1134,12 @@ __device__ int sample_body(const float * logits, int V, int cb, const DevState *
     const int tid = threadIdx.x;
     float l[PT];
     bool valid[PT];
+    load(l);
 #pragma unroll
     for (int e = 0; e < PT; ++e) {
         const int i = tid * PT + e;
         valid[e] = i < V;
-        l[e] = valid[e] ? logits[i] : -INFINITY;
+        if (!valid[e]) l[e] = -INFINITY;
         if (valid[e] && P.record_logits && frame < P.dbg_cap) {
             if (cb == 0) P.dbg_talker[(size_t) frame * V + i] = l[e];
             else P.dbg_cp[((size_t) frame * (P.n_cb - 1) + (cb - 1)) * V + i] = l[e];
@@ -1217,6 +1247,20 @@ __device__ int sample_body(const float * logits, int V, int cb, const DevState *
     return tok;
 }
 
+template <int PT>
+__device__ __forceinline__ int sample_body(const float * logits, int V, int cb, const DevState * st,
+                                           const SampleParams & P, int frame) {
+    return sample_body_l<PT>(
+        [&](float * l) {
+#pragma unroll
+            for (int e = 0; e < PT; ++e) {
+                const int i = threadIdx.x * PT + e;
+                l[e] = i < V ? logits[i] : -INFINITY;
+            }
+        },
+        V, cb, st, P, frame);
+}
+
 // Records a sampled token in the frame state (thread 0 only).
 __device__ __forceinline__ void sample_commit(int tok, int cb, DevState * st, const SampleParams & P, int * out_codes,
                                               int out_cap, int frame) {
@@ -1259,7 +1303,7 @@ struct InputArgs {
     float * out;                  // [rows][H]
     DevState * st;
     int n_cb;
-    const __half * step_tab;      // IN_CP_STEP: cp_embd[g - 1] (persistent path)
+    const __half * step_tab;      // IN_CP_STEP: cp_embd[g - 1]
 };
 
 // Inputs of the next pass, built by the sampling CTA right after it sampled:

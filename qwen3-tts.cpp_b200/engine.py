@@ -108,8 +108,6 @@ def lib():
         "qtts_attn_rows": (C.c_int32, [C.c_void_p]),
         "qtts_attn_row": (C.c_int32, [C.c_void_p, C.c_int32, _f32p, C.c_int32]),
         "qtts_get_timing": (C.c_int32, [C.c_void_p, C.POINTER(Timing)]),
-        "qtts_program_ops": (C.c_int32, [C.c_void_p, _i32p, C.c_int32]),
-        "qtts_op_trace": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64), C.c_int32]),
         "qtts_profile_frames": (C.c_int32, [C.c_void_p, C.c_int32, C.POINTER(KernelStats), C.c_int32]),
         "qtts_batch_create": (C.c_void_p, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
         "qtts_batch_begin": (C.c_int32, [C.c_void_p, C.c_int32, C.c_void_p]),
@@ -237,7 +235,7 @@ class Engine:
     @staticmethod
     def frame_kernel() -> str:
         """Name of the kernel that runs the frames (QTTS_FRAME_MODE selects it)."""
-        return "k_frame_persistent" if os.environ.get("QTTS_FRAME_MODE") == "persistent" else "frame_graph"
+        return "k_frame_dataflow" if os.environ.get("QTTS_FRAME_MODE") == "dataflow" else "frame_graph"
 
     def timing(self) -> dict:
         t = Timing()
@@ -320,18 +318,6 @@ class Engine:
             raise RuntimeError("profile_frames failed: " + self.error())
         return {"frames": got, **{KERNEL_CLASSES[i]: dict(launches=st[i].launches, ms=st[i].total_ms, bytes=st[i].bytes)
                                   for i in range(4)}}
-
-    def op_trace(self):
-        """(op types, timestamps [frames*ops][5]) of the last persistent run with QTTS_PK_TRACE=1:
-        CTA 0 op start, CTA 0 copies issued, latest weight arrival over CTAs, CTA 0 work done,
-        latest work done over CTAs (ns, %globaltimer)."""
-        n = lib().qtts_program_ops(self.h, None, 0)
-        types = np.zeros(max(n, 1), np.int32)
-        lib().qtts_program_ops(self.h, _p(types, C.c_int32), n)
-        m = lib().qtts_op_trace(self.h, None, 0)
-        tr = np.zeros(max(m, 1), np.uint64)
-        lib().qtts_op_trace(self.h, tr.ctypes.data_as(C.POINTER(C.c_uint64)), m)
-        return types[:n], tr[:m].reshape(-1, 5)
 
     def run_frames(self, n: int, codes_out: np.ndarray | None = None) -> int:
         ptr = None if codes_out is None else _p(codes_out, C.c_int32)

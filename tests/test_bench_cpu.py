@@ -22,8 +22,6 @@ import bench  # noqa: E402
     ("k_gemv_f16.md", "dram_bytes_per_algorithmic_byte"),
     ("k_gemv_q8.md", "dram_bytes_per_algorithmic_byte"),
     ("k_gemm_tc_batch16.md", "dram_bytes_per_algorithmic_byte"),
-    ("k_frame_persistent_f16.md", "dram_bytes_per_frame"),
-    ("k_frame_persistent_q8.md", "dram_bytes_per_frame"),
 ])
 def test_profile_figures_read_by_bench_exist(fname, key):
     v = bench._profile_figure(fname, key)

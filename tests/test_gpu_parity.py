@@ -274,14 +274,15 @@ def test_full_f16_config3_sampled(qtts, full_f16):
     eng.close()
 
 
-def test_persistent_kernel_matches_graph_path(qtts, tiny_f16, tiny_q8, monkeypatch):
-    """The persistent frame kernel and the kernel-per-op CUDA graph run the same
-    GEMV partitions and reductions: greedy codes and all logits are identical."""
+def test_dataflow_kernel_matches_graph_path(qtts, tiny_f16, tiny_q8, monkeypatch):
+    """The dataflow frame kernel and the kernel-per-op CUDA graph run the same
+    GEMV rows, attention, samplers and input sums in the same reduction orders:
+    greedy codes and all logits are identical."""
     rng = np.random.default_rng(25)
     text = text_ids(rng, 26)
     for path in (tiny_f16, tiny_q8):
         outs = []
-        for mode in ("graph", "persistent"):
+        for mode in ("graph", "dataflow"):
             monkeypatch.setenv("QTTS_FRAME_MODE", mode)
             eng = qtts.Engine(path, 0)
             outs.append(eng.generate(text, 20, speaker=np.zeros(256, np.float32), eos_bias=-1e9,
@@ -300,7 +301,7 @@ def test_rewind_replays_the_utterance(qtts, tiny_f16, monkeypatch):
     frame modes."""
     rng = np.random.default_rng(31)
     text = text_ids(rng, 20)
-    for mode in ("persistent", "graph"):
+    for mode in ("dataflow", "graph"):
         monkeypatch.setenv("QTTS_FRAME_MODE", mode)
         eng = qtts.Engine(tiny_f16, 0)
         eng.generate_begin(text, 12, speaker=np.zeros(256, np.float32), eos_bias=-1e9, rep_penalty=1.05)
