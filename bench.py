@@ -419,6 +419,19 @@ def run_ncu_workload(args):
                            temperature=0.0, top_k=0, eos_bias=-1e9)
         got = eng.run_frames(args.frames)
         print(f"frames={got} {eng.timing()}", file=sys.stderr)
+        if os.environ.get("QTTS_DF_TRACE") and got:
+            ops, tr = eng.frame_trace()
+            t = tr[: len(ops) * got].astype(np.int64)
+            nxt = np.append(t[1:, 0], t[-1, 3])
+            names = {16: "gemv", 17: "gemv+cb0", 18: "gemv+cbg", 19: "gemv+cblast", 20: "gemv+cpattn2",
+                     21: "gemv+cpattn", 32: "talker-attn"}
+            kinds = np.tile(ops, got)
+            for ty in sorted(set(ops.tolist())):
+                i = np.nonzero(kinds == ty)[0]
+                print(f"{names.get(ty, ty):12s} n={len(i) // got:4d}/frame  input(cta0) {(t[i, 1] - t[i, 0]).mean() / 1e3:6.2f}"
+                      f"  input(last cta) {(t[i, 2] - t[i, 0]).mean() / 1e3:6.2f}  done(cta0) {(t[i, 3] - t[i, 0]).mean() / 1e3:6.2f}"
+                      f"  next {(nxt[i] - t[i, 0]).mean() / 1e3:6.2f} us", file=sys.stderr)
+            print(f"frame span {(t[-1, 3] - t[0, 0]) / 1e3 / got:.1f} us", file=sys.stderr)
         eng.close()
         return 0
     path = pkg.synth_gguf.ensure_gguf(d, cfg_m, "f16", seed=0)

@@ -70,6 +70,22 @@ typedef struct qtts_timing {
     int32_t kernel_launches; /* engine kernels launched per frame */
 } qtts_timing;
 
+/* Stage timings of the last generate (no reference counterpart as an ABI; the
+ * reference prints the same stages under QWEN3_TTS_TIMING, src/tts_transformer.h:
+ * 20-54, src/tts_transformer.cpp:3311-3353).  With stage timing on, frames run
+ * kernel by kernel with CUDA events around every launch (slower than the frame
+ * graph), each launch charged to the talker step, the code predictor, or the
+ * samplers with their next-input embedding sums. */
+typedef struct qtts_stage_timing {
+    float prefill_build_ms;   /* host: text projection + prompt row assembly */
+    float prefill_forward_ms; /* device: forward_prefill */
+    float talker_ms;          /* device: talker steps (layers + codec head) */
+    float code_pred_ms;       /* device: code-predictor passes (layers + heads) */
+    float sample_embed_ms;    /* device: samplers and next-input embedding sums */
+    float total_ms;           /* host: the whole qtts_generate call */
+    int32_t frames;
+} qtts_stage_timing;
+
 /* Per-kernel-class statistics of qtts_profile_frames (classes: 0 = GEMV,
  * 1 = attention, 2 = sampling, 3 = other). */
 typedef struct qtts_kernel_stats {
@@ -166,6 +182,16 @@ int32_t qtts_set_attn_dump(qtts_engine * e, int32_t enabled, int32_t layer);
 int32_t qtts_attn_rows(const qtts_engine * e);
 int32_t qtts_attn_row(const qtts_engine * e, int32_t r, float * out, int32_t cap);
 int32_t qtts_get_timing(const qtts_engine * e, qtts_timing * out);
+/* Diagnostics of the dataflow frame kernel (QTTS_FRAME_MODE=dataflow), enabled
+ * by QTTS_DF_TRACE=1 at run time: the frame program's ops (type * 16 + input
+ * prologue; types 1 GEMV, 2 talker attention) and, for the last launch, four
+ * %globaltimer stamps per op and frame (CTA 0 start, CTA 0 input ready, latest
+ * input ready over the CTAs, CTA 0 done).  Both return the count available. */
+int32_t qtts_frame_ops(const qtts_engine * e, int32_t * ops, int32_t cap);
+int32_t qtts_frame_trace(const qtts_engine * e, unsigned long long * out, int32_t cap);
+/* Stage timing on (1) / off (0) for the following generate calls; 1 on success. */
+int32_t qtts_set_stage_timing(qtts_engine * e, int32_t enabled);
+int32_t qtts_get_stage_timing(const qtts_engine * e, qtts_stage_timing * out);
 /* Advance up to n frames of the active generation kernel by kernel (no CUDA
  * graph) with CUDA events around each launch; fills stats[0..n_classes).
  * Returns frames produced or -1.  For measurement only. */

@@ -150,10 +150,18 @@ struct Engine {
     int n_df_pf0 = 0;
     int df_pf_lead = 4;          // GEMVs between a slice's L2 prefetch and its use (QTTS_DF_PF_LEAD)
     size_t df_wbuf = 0, df_work = 0, df_dyn = 0;
+    unsigned long long * d_trace = nullptr;   // QTTS_DF_TRACE=1: per-op stamps of the last dataflow launch
+    size_t trace_cap = 0, trace_n = 0;
     int df_keys = 0;
     // eager profiling: CUDA events around every launch, accumulated per kernel class
     bool profiling = false;
-    struct ProfEv { int cls; double bytes; cudaEvent_t a, b; };
+    struct ProfEv { int cls; int stage; double bytes; cudaEvent_t a, b; };
+    // stage timing (qtts_set_stage_timing): frames run kernel by kernel with events,
+    // each launch charged to the talker step, the code predictor or the samplers
+    enum { STG_TALKER = 0, STG_CP = 1 };
+    int prof_stage = STG_TALKER;
+    bool stage_timing = false;
+    qtts_stage_timing stages{};
     std::vector<ProfEv> prof_evs;
     std::vector<cudaEvent_t> ev_pool;
     size_t ev_used = 0;
@@ -163,7 +171,7 @@ struct Engine {
     }
     void prof_begin(int cls, double bytes) {
         if (!profiling) return;
-        ProfEv p{cls, bytes, pool_event(), pool_event()};
+        ProfEv p{cls, prof_stage, bytes, pool_event(), pool_event()};
         cudaEventRecord(p.a, stream);
         prof_evs.push_back(p);
     }
@@ -185,7 +193,7 @@ struct Engine {
         if (d_prow) { cudaFree(d_prow); d_prow = nullptr; prow_cap = 0; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
                          cp_logits, hidden, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
-                         dbg_t, dbg_cp, d_attn, d_prog, d_df_att, d_dfbuf, d_err, logits0, hidden0};
+                         dbg_t, dbg_cp, d_attn, d_prog, d_df_att, d_dfbuf, d_err, logits0, hidden0, d_trace};
         for (void * p : ptrs) if (p) cudaFree(p);
         wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
         x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = tmp_a = tmp_b = nullptr;
@@ -193,6 +201,7 @@ struct Engine {
         d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
         dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_prog = nullptr; d_df_att = nullptr; d_dfbuf = nullptr;
         d_err = nullptr; df_buf_words = 0; prog_cap = 0; att_cap = 0; prog_ok = false;
+        d_trace = nullptr; trace_cap = trace_n = 0;
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         ev0 = ev1 = nullptr;
@@ -600,7 +609,10 @@ static bool gemv_shape(const DMat & A, bool dual, bool has_gain, int nvt, int n_
         if (smem <= QTTS_GEMV_SMEM_MAX) {
             *ncta_out = (A.rows + rpc - 1) / rpc;
             *slice_out = slice;
-            *smem_out = smem;
+            // at most two CTAs per SM, whatever the register count: a third resident
+            // CTA (of the next launch under programmatic dependent launch) measured
+            // slower (343 vs 384 frames/s), and 80 KB each leaves no room for it
+            *smem_out = std::max(smem, QTTS_GEMV_SMEM_2CTA);
             return true;
         }
         if (ncta >= A.rows) return false;
@@ -739,6 +751,7 @@ bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, in
 // (the next talker step), or nullptr for a plain sampler.
 bool Engine::enqueue_cp(bool sample_cb0, const InputArgs * last_in) {
     const qtts_config & c = cfg;
+    prof_stage = STG_CP;
     const int H = c.hidden_size, V1 = c.code_pred_vocab_size, NG = c.n_codebooks - 1;
     const int * done = &st->done;
     InputArgs ia{};
@@ -779,6 +792,7 @@ bool Engine::enqueue_cp(bool sample_cb0, const InputArgs * last_in) {
 
 bool Engine::enqueue_talker_step(const int * pos_ptr, int pos_static, const int * done, bool with_dump) {
     const qtts_config & c = cfg;
+    prof_stage = STG_TALKER;
     const int H = c.hidden_size;
     if (!layers(L, kc, vc, n_ctx, rope_t, x, 1, pos_ptr, pos_static, false, done, c.intermediate_size,
                 with_dump && attn_dump ? d_attn : nullptr, attn_layer))
@@ -1024,6 +1038,20 @@ bool Engine::launch_dataflow(int n) {
     a.n_pf0 = n_df_pf0;
     for (int k = 0; k < n_df_pf0; ++k) a.pf0[k] = df_pf0[k];
     df_tag_base += (unsigned)((n + 1) * n_ops);
+    a.trace = nullptr;
+    trace_n = 0;
+    if (getenv("QTTS_DF_TRACE")) {
+        const size_t need = (size_t) n * n_ops * DF_TRACE;
+        if (need > trace_cap) {
+            if (d_trace) cudaFree(d_trace);
+            d_trace = nullptr;
+            QCHECK(cudaMalloc(&d_trace, sizeof(unsigned long long) * need));
+            trace_cap = need;
+        }
+        QCHECK(cudaMemsetAsync(d_trace, 0, sizeof(unsigned long long) * need, stream));
+        a.trace = d_trace;
+        trace_n = need;
+    }
     QCHECK(cudaMemsetAsync(d_err, 0, sizeof(int), stream));
     void * args[] = {&a};
     QCHECK(cudaLaunchCooperativeKernel((const void *) k_frame_dataflow, dim3(n_sm), dim3(DF_THREADS), args, df_dyn,
@@ -1281,8 +1309,12 @@ int Engine::begin(const qtts_generate_params * p) {
     attn_rows.clear();
     std::vector<float> rows, trail, padv;
     const bool icl = p->ref_codec_tokens != nullptr;
+    stages = qtts_stage_timing{};
+    const auto t_build = std::chrono::steady_clock::now();
     if (icl) { if (!build_prefill_icl(p, rows, trail, padv)) return -1; }
     else if (!build_prefill(p, rows, trail, padv)) return -1;
+    stages.prefill_build_ms =
+        (float) std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_build).count();
     const int plen = (int)(rows.size() / H), tlen = (int)(trail.size() / H);
     const int required = plen + p->max_len + 8;
     if (n_ctx < required || n_ctx > std::max(required * 2, 512)) { if (!init_kv(required)) return -1; }
@@ -1322,6 +1354,7 @@ int Engine::begin(const qtts_generate_params * p) {
         }
     }
     if (!prefill(rows.data(), plen, 0, nullptr, nullptr)) return -1;
+    stages.prefill_forward_ms = timing.prefill_ms;
     if (tlen > 0 && cudaMemcpyAsync(trailing, trail.data(), sizeof(float) * tlen * H, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
         err = "upload trailing"; return -1;
     }
@@ -1386,7 +1419,16 @@ int Engine::run_frames(int n, int32_t * codes_out) {
     n = std::min(n, sess.max_len - sess.produced);
     if (n <= 0) return 0;
     if (cudaEventRecord(ev0, stream) != cudaSuccess) { err = "event"; return -1; }
-    if (use_dataflow) {
+    const bool staged = stage_timing && !use_dataflow;
+    if (staged) {   // kernel by kernel, events around every launch
+        profiling = true;
+        prof_evs.clear();
+        ev_used = 0;
+        bool ok = true;
+        for (int i = 0; i < n && ok; ++i) ok = enqueue_frame();
+        profiling = false;
+        if (!ok) return -1;
+    } else if (use_dataflow) {
         if (!launch_dataflow(n)) return -1;
     } else {
         for (int i = 0; i < n; ++i)
@@ -1406,6 +1448,19 @@ int Engine::run_frames(int n, int32_t * codes_out) {
     timing.frames_ms += ms;
     const int got = hs.n_out - sess.produced;
     timing.frames += got;
+    if (staged) {
+        for (auto & e : prof_evs) {
+            float t = 0.0f;
+            cudaEventElapsedTime(&t, e.a, e.b);
+            if (e.cls == KC_SAMPLE) stages.sample_embed_ms += t;
+            else if (e.stage == STG_CP) stages.code_pred_ms += t;
+            else stages.talker_ms += t;
+        }
+        prof_evs.clear();
+        stages.frames += got;
+    } else if (stage_timing) {   // one dataflow launch: the frame time as a whole
+        stages.frames += got;
+    }
     if (got > 0 && codes_out) {
         if (cudaMemcpy(codes_out, d_codes + (size_t) sess.produced * NCB, sizeof(int) * got * NCB, cudaMemcpyDeviceToHost) != cudaSuccess) {
             err = "codes readback"; return -1;
@@ -1902,6 +1957,7 @@ int32_t qtts_generate(qtts_engine * h, const qtts_generate_params * p, qtts_fram
     if (n_frames_out) *n_frames_out = 0;
     if (p->max_len <= 0) return 1;
     const int NCB = E.cfg.n_codebooks;
+    const auto t_call = std::chrono::steady_clock::now();
     if (E.begin(p) < 0) return 0;
     std::vector<int32_t> out;
     out.reserve((size_t) p->max_len * NCB);
@@ -1947,6 +2003,7 @@ int32_t qtts_generate(qtts_engine * h, const qtts_generate_params * p, qtts_fram
     if (codes_out) memcpy(codes_out, out.data(), out.size() * sizeof(int32_t));
     if (n_frames_out) *n_frames_out = n;
     E.sess.active = false;
+    E.stages.total_ms = (float) std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_call).count();
     return 1;
 }
 
@@ -2009,6 +2066,38 @@ int32_t qtts_profile_frames(qtts_engine * h, int32_t n, qtts_kernel_stats * out,
     E.sess.produced = hs.n_out;
     E.sess.done = hs.done != 0;
     return got;
+}
+
+// Diagnostics of the dataflow frame kernel (QTTS_DF_TRACE=1 at run time): the op
+// list of the frame program (type * 16 + prologue per op) and the per-op stamps of
+// the last launch ([frame][op][4]).  Both return the number of values available.
+int32_t qtts_frame_ops(const qtts_engine * h, int32_t * ops, int32_t cap) {
+    if (!h) return -1;
+    const Engine & E = *reinterpret_cast<const Engine *>(h);
+    const int n = (int) E.prog.size();
+    for (int i = 0; i < n && i < cap; ++i) ops[i] = E.prog[i].type * 16 + E.prog[i].pro;
+    return n;
+}
+int32_t qtts_frame_trace(const qtts_engine * h, unsigned long long * out, int32_t cap) {
+    if (!h) return -1;
+    const Engine & E = *reinterpret_cast<const Engine *>(h);
+    if (!E.d_trace || !E.trace_n) return 0;
+    cudaSetDevice(E.dev);
+    const size_t n = std::min(E.trace_n, (size_t) std::max(cap, 0));
+    if (out && n) cudaMemcpy(out, E.d_trace, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost);
+    return (int32_t) E.trace_n;
+}
+
+int32_t qtts_set_stage_timing(qtts_engine * h, int32_t enabled) {
+    if (!h) return 0;
+    reinterpret_cast<Engine *>(h)->stage_timing = enabled != 0;
+    return 1;
+}
+
+int32_t qtts_get_stage_timing(const qtts_engine * h, qtts_stage_timing * out) {
+    if (!h || !out) return 0;
+    *out = reinterpret_cast<const Engine *>(h)->stages;
+    return 1;
 }
 
 int32_t qtts_get_timing(const qtts_engine * h, qtts_timing * out) {

@@ -95,7 +95,17 @@ struct DfArgs {
     int first[2];                       // the frame's first two GEMV ops (slices copied at launch)
     int n_pf0;
     int pf0[8];                         // GEMV ops prefetched into L2 at launch
+    unsigned long long * trace;         // optional [n_frames][n_ops][DF_TRACE] %globaltimer stamps
 };
+// Trace stamps per op: CTA 0 start, CTA 0 input ready, latest input ready over
+// the CTAs, CTA 0 done.
+constexpr int DF_TRACE = 4;
+
+__device__ __forceinline__ unsigned long long df_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ void df_prefetch_l2(const void * p, size_t bytes) {
     const char * c = static_cast<const char *>(p);
@@ -348,6 +358,8 @@ __global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs P) {
         const int frame = frame0 + f;
         for (int k = 0; k < P.n_ops; ++k) {
             const DfOp & op = desc[k & 1];
+            unsigned long long * tr = P.trace ? P.trace + ((size_t) f * P.n_ops + k) * DF_TRACE : nullptr;
+            if (tr && cta == 0 && tid == 0) tr[0] = df_now();
             const int nx = k + 1 < P.n_ops ? k + 1 : 0;
             const unsigned long long nword = tid < NW ? reinterpret_cast<const unsigned long long *>(P.ops + nx)[tid] : 0ull;
             bool ok = true;
@@ -487,6 +499,11 @@ __global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs P) {
                 if (__syncthreads_or(!ok || s_bad)) {
                     failed = true;
                 } else if (!stop) {
+                    if (tr && tid == 0) {
+                        const unsigned long long t = df_now();
+                        if (cta == 0) tr[1] = t;
+                        atomicMax(tr + 2, t);
+                    }
                     // residual rows of this CTA, then the GEMV
                     if (op.epi == EPI_RESID) {
                         const int rstride = (rpc + 3) & ~3;
@@ -550,6 +567,7 @@ __global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs P) {
                 break;
             }
             if (stop) break;
+            if (tr && cta == 0 && tid == 0) tr[3] = df_now();
             __syncthreads();   // everyone is done with desc[k & 1] and with the op's weight buffer
             if (tid < NW) reinterpret_cast<unsigned long long *>(&desc[(k + 1) & 1])[tid] = nword;
             if (op.type == DF_GEMV && tid == 0) {

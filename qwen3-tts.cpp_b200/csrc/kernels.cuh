@@ -39,6 +39,7 @@ struct GemvArgs {
 };
 
 constexpr size_t QTTS_GEMV_SMEM_MAX = 200 * 1024;   // dynamic shared memory of a stand-alone k_gemv
+constexpr size_t QTTS_GEMV_SMEM_2CTA = 80 * 1024;   // minimum per launch: two CTAs per SM at most
 
 // Rows [r0, r1) of a GEMV belong to CTA `cta` of `ncta` (rpc = ceil(rows / ncta)).
 __host__ __device__ inline int gemv_rpc(int rows, int ncta) { return (rows + ncta - 1) / ncta; }

@@ -5,6 +5,7 @@
 #include "../../include/qwen3tts_b200.h"
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <random>
 
@@ -151,6 +152,50 @@ bool TTSTransformer::predict_codes_autoregressive(const float * hidden, int32_t 
 }
 
 namespace {
+// Stage timing report: compiled in with QWEN3_TTS_TIMING as in the reference, or
+// switched on at run time with the environment variable QWEN3_TTS_TIMING=1 (the
+// library is prebuilt).
+bool timing_requested() {
+#ifdef QWEN3_TTS_TIMING
+    return true;
+#else
+    const char * v = getenv("QWEN3_TTS_TIMING");
+    return v && *v && strcmp(v, "0") != 0;
+#endif
+}
+
+// The layout of the reference's report (src/tts_transformer.cpp:3311-3353).  The
+// frame graph is captured once per session, so graph build and allocation cost
+// nothing per frame; the device stage times are CUDA-event times.
+void print_timing_report(const qtts_stage_timing & t) {
+    const int nf = t.frames;
+    auto per = [nf](double ms) { return nf > 0 ? ms / nf : 0.0; };
+    fprintf(stderr, "\n=== Detailed Generation Timing (%d frames) ===\n", nf);
+    fprintf(stderr, "\n  Prefill:\n");
+    fprintf(stderr, "    Build graph:      %8.1f ms\n", (double) t.prefill_build_ms);
+    fprintf(stderr, "    Forward total:    %8.1f ms\n", (double) t.prefill_forward_ms);
+    fprintf(stderr, "      Graph build:    %8.1f ms\n", 0.0);
+    fprintf(stderr, "      Graph alloc:    %8.1f ms\n", 0.0);
+    fprintf(stderr, "      Compute:        %8.1f ms\n", (double) t.prefill_forward_ms);
+    fprintf(stderr, "      Data I/O:       %8.1f ms\n", 0.0);
+    fprintf(stderr, "\n  Talker forward_step (total / per-frame):\n");
+    fprintf(stderr, "    Total:            %8.1f ms   (%.3f ms/frame)\n", (double) t.talker_ms, per(t.talker_ms));
+    fprintf(stderr, "      Compute:        %8.1f ms   (%.3f ms/frame)\n", (double) t.talker_ms, per(t.talker_ms));
+    fprintf(stderr, "\n  Code predictor (total / per-frame):\n");
+    fprintf(stderr, "    Backend:          B200 engine\n");
+    fprintf(stderr, "    Total:            %8.1f ms   (%.3f ms/frame)\n", (double) t.code_pred_ms, per(t.code_pred_ms));
+    fprintf(stderr, "      Compute:        %8.1f ms   (%.3f ms/frame)\n", (double) t.code_pred_ms, per(t.code_pred_ms));
+    fprintf(stderr, "\n  Embed lookups:      %8.1f ms   (%.3f ms/frame)  (with the samplers)\n",
+            (double) t.sample_embed_ms, per(t.sample_embed_ms));
+    const double accounted = (double) t.prefill_build_ms + t.prefill_forward_ms + t.talker_ms + t.code_pred_ms +
+                             t.sample_embed_ms;
+    fprintf(stderr, "  Other/overhead:     %8.1f ms\n", (double) t.total_ms - accounted);
+    fprintf(stderr, "  -----------------------------------------\n");
+    fprintf(stderr, "  Total generate:     %8.1f ms\n", (double) t.total_ms);
+    if (nf > 0)
+        fprintf(stderr, "  Throughput:         %8.3f ms/frame (%.1f frames/s)\n", t.total_ms / nf, 1000.0 * nf / t.total_ms);
+}
+
 struct CbCtx { const TTSTransformer::FrameCallback * cb; };
 int32_t trampoline(const int32_t * codes, int32_t n, int32_t frame, void * user) {
     auto * c = static_cast<CbCtx *>(user);
@@ -165,7 +210,16 @@ bool TTSTransformer::generate_impl(const void * vp, std::vector<int32_t> & outpu
     output.assign((size_t) p->max_len * model_.config.n_codebooks, 0);
     CbCtx ctx{&on_frame};
     int32_t n = 0;
-    if (!qtts_generate(engine_, p, on_frame ? trampoline : nullptr, &ctx, output.data(), &n)) {
+    const bool timed = timing_requested();
+    if (timed) qtts_set_stage_timing(engine_, 1);
+    const bool ok = qtts_generate(engine_, p, on_frame ? trampoline : nullptr, &ctx, output.data(), &n) != 0;
+    if (timed) {
+        qtts_stage_timing t{};
+        qtts_get_stage_timing(engine_, &t);
+        qtts_set_stage_timing(engine_, 0);
+        if (ok) print_timing_report(t);
+    }
+    if (!ok) {
         error_msg_ = qtts_get_error(engine_);
         output.clear();
         return false;

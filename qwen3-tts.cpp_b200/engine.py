@@ -59,6 +59,12 @@ class Timing(C.Structure):
                 ("kernel_launches", C.c_int32)]
 
 
+class StageTiming(C.Structure):
+    _fields_ = [("prefill_build_ms", C.c_float), ("prefill_forward_ms", C.c_float), ("talker_ms", C.c_float),
+                ("code_pred_ms", C.c_float), ("sample_embed_ms", C.c_float), ("total_ms", C.c_float),
+                ("frames", C.c_int32)]
+
+
 class KernelStats(C.Structure):
     _fields_ = [("launches", C.c_int32), ("total_ms", C.c_float), ("bytes", C.c_double)]
 
@@ -108,6 +114,10 @@ def lib():
         "qtts_attn_rows": (C.c_int32, [C.c_void_p]),
         "qtts_attn_row": (C.c_int32, [C.c_void_p, C.c_int32, _f32p, C.c_int32]),
         "qtts_get_timing": (C.c_int32, [C.c_void_p, C.POINTER(Timing)]),
+        "qtts_set_stage_timing": (C.c_int32, [C.c_void_p, C.c_int32]),
+        "qtts_frame_ops": (C.c_int32, [C.c_void_p, _i32p, C.c_int32]),
+        "qtts_frame_trace": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64), C.c_int32]),
+        "qtts_get_stage_timing": (C.c_int32, [C.c_void_p, C.POINTER(StageTiming)]),
         "qtts_profile_frames": (C.c_int32, [C.c_void_p, C.c_int32, C.POINTER(KernelStats), C.c_int32]),
         "qtts_batch_create": (C.c_void_p, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
         "qtts_batch_begin": (C.c_int32, [C.c_void_p, C.c_int32, C.c_void_p]),
@@ -242,6 +252,14 @@ class Engine:
         lib().qtts_get_timing(self.h, C.byref(t))
         return dict(prefill_ms=t.prefill_ms, frames_ms=t.frames_ms, frames=t.frames, kernel_launches=t.kernel_launches)
 
+    def set_stage_timing(self, enabled: bool):
+        self._ok(lib().qtts_set_stage_timing(self.h, int(enabled)), "set_stage_timing")
+
+    def stage_timing(self) -> dict:
+        t = StageTiming()
+        lib().qtts_get_stage_timing(self.h, C.byref(t))
+        return {k: getattr(t, k) for k, _ in StageTiming._fields_}
+
     def _params(self, text, max_len, speaker, ref_text, ref_codes, language_id, rep_penalty, temperature, top_k,
                 instruct, eos_bias, target_frames, rep_loop_detect, seed):
         keep = []
@@ -318,6 +336,17 @@ class Engine:
             raise RuntimeError("profile_frames failed: " + self.error())
         return {"frames": got, **{KERNEL_CLASSES[i]: dict(launches=st[i].launches, ms=st[i].total_ms, bytes=st[i].bytes)
                                   for i in range(4)}}
+
+    def frame_trace(self):
+        """(ops [n_ops] = type * 16 + prologue, stamps [frames * n_ops][4]) of the last
+        dataflow launch with QTTS_DF_TRACE=1 (ns, %globaltimer)."""
+        n = lib().qtts_frame_ops(self.h, None, 0)
+        ops = np.zeros(max(n, 1), np.int32)
+        lib().qtts_frame_ops(self.h, _p(ops, C.c_int32), n)
+        m = lib().qtts_frame_trace(self.h, None, 0)
+        tr = np.zeros(max(m, 1), np.uint64)
+        lib().qtts_frame_trace(self.h, tr.ctypes.data_as(C.POINTER(C.c_uint64)), m)
+        return ops[:n], tr[:m].reshape(-1, 4)
 
     def run_frames(self, n: int, codes_out: np.ndarray | None = None) -> int:
         ptr = None if codes_out is None else _p(codes_out, C.c_int32)

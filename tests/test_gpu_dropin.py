@@ -68,7 +68,7 @@ def test_dropin_class_against_oracle(qtts, tiny_f16, tmp_path):
     ref_codes.tofile(os.path.join(d, "ref_codes.i32"))
     spk.tofile(os.path.join(d, "speaker.f32"))
     prefill.tofile(os.path.join(d, "prefill.f32"))
-    env = dict(os.environ, QWEN3_TTS_DEVICE="0")
+    env = dict(os.environ, QWEN3_TTS_DEVICE="0", QWEN3_TTS_TIMING="1")
     out = subprocess.run([exe, tiny_f16, d], capture_output=True, text=True, env=env, timeout=600)
     print(out.stdout, out.stderr[-2000:], file=sys.stderr)
     assert out.returncode == 0 and "DONE" in out.stdout, out.stdout
@@ -129,6 +129,11 @@ def test_dropin_class_against_oracle(qtts, tiny_f16, tmp_path):
     ref = legacy_predict_codes(tiny_f16, ch, prev)
     got = rd("cp_legacy_logits.f32", np.float32).reshape(15, 2048)
     assert np.abs(got - ref).max() < 2e-2 * max(1.0, np.abs(ref).max())
+
+    # the QWEN3_TTS_TIMING report after each generate (src/tts_transformer.cpp:3311-3353 layout)
+    assert out.stderr.count("=== Detailed Generation Timing (") == 2     # generate and generate_icl
+    assert "=== Detailed Generation Timing (8 frames) ===" in out.stderr
+    assert "Code predictor (total / per-frame):" in out.stderr and "Total generate:" in out.stderr
 
     # error convention: bool + get_error()
     assert lines["short_text_rejected"].startswith("1") and "at least 4" in lines["short_text_rejected"]

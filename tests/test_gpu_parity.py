@@ -313,3 +313,24 @@ def test_rewind_replays_the_utterance(qtts, tiny_f16, monkeypatch):
             assert eng.run_frames(12, b) == 12
             assert np.array_equal(a, b)
         eng.close()
+
+
+def test_stage_timing(qtts, tiny_f16):
+    """QWEN3_TTS_TIMING's stages (src/tts_transformer.h:20-54): with stage timing
+    on, every stage of a generate call has a positive time, the stages fit in the
+    call, and the codes are the frame graph's."""
+    rng = np.random.default_rng(32)
+    text = text_ids(rng, 20)
+    kw = dict(speaker=np.zeros(256, np.float32), eos_bias=-1e9, rep_penalty=1.05)
+    eng = qtts.Engine(tiny_f16, 0)
+    ref = eng.generate(text, 6, **kw)
+    eng.set_stage_timing(True)
+    out = eng.generate(text, 6, **kw)
+    t = eng.stage_timing()
+    eng.set_stage_timing(False)
+    eng.close()
+    assert np.array_equal(out["codes"], ref["codes"])
+    assert t["frames"] == 6
+    for k in ("prefill_build_ms", "prefill_forward_ms", "talker_ms", "code_pred_ms", "sample_embed_ms", "total_ms"):
+        assert t[k] > 0.0, (k, t)
+    assert t["prefill_forward_ms"] + t["talker_ms"] + t["code_pred_ms"] + t["sample_embed_ms"] <= t["total_ms"], t
