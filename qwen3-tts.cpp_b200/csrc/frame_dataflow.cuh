@@ -98,8 +98,8 @@ struct DfArgs {
     unsigned long long * trace;         // optional [n_frames][n_ops][DF_TRACE] %globaltimer stamps
 };
 // Trace stamps per op: CTA 0 start, CTA 0 input ready, latest input ready over
-// the CTAs, CTA 0 done.
-constexpr int DF_TRACE = 4;
+// the CTAs, CTA 0 weights ready, CTA 0 done.
+constexpr int DF_TRACE = 5;
 
 __device__ __forceinline__ unsigned long long df_now() {
     unsigned long long t;
@@ -298,46 +298,261 @@ __device__ __forceinline__ void df_drain(uint64_t * mbar, unsigned pending, unsi
         if (pending >> b & 1u) mbar_wait(mbar + b, phase >> b & 1u);
 }
 
-__global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs P) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ DfOp desc[2];
-    __shared__ __align__(8) uint64_t mbar[2];
-    __shared__ DevState s_st;                 // this CTA's frame state (presence set, codes)
-    __shared__ SampleParams s_sp;
-    __shared__ float s_res[2][8];             // this CTA's rows of the residual stream
-    __shared__ const __half * s_tab[QTTS_MAX_CB];
-    __shared__ int s_bad;
-    const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nt = blockDim.x, nw = nt >> 5;
-    uint8_t * work = smem + 2 * (size_t) P.wbuf_bytes;
-    FusedAttn * att = reinterpret_cast<FusedAttn *>(work + P.work_bytes);
-    float * hid = reinterpret_cast<float *>(att + P.n_att);
-    const int H = P.H;
-    const int rpc_h = gemv_rpc(H, ncta), r0_h = cta * rpc_h;
+// ---- per-CTA state of the kernel (shared memory).  The stages below are
+// separate (non-inlined) functions so each gets its own register allocation.
+__shared__ DfArgs df_P;                  // the launch arguments
+__shared__ DfOp df_desc[2];              // this op's descriptor and the next one's
+__shared__ __align__(8) uint64_t df_mbar[2];
+__shared__ DevState df_st;               // this CTA's frame state (presence set, codes)
+__shared__ SampleParams df_sp;
+__shared__ float df_res[2][8];           // this CTA's rows of the residual stream
+__shared__ const __half * df_tab[QTTS_MAX_CB];
+__shared__ int df_bad;
+extern __shared__ __align__(128) uint8_t df_smem[];
+
+__device__ __forceinline__ uint8_t * df_work() { return df_smem + 2 * (size_t) df_P.wbuf_bytes; }
+__device__ __forceinline__ FusedAttn * df_att() { return reinterpret_cast<FusedAttn *>(df_work() + df_P.work_bytes); }
+__device__ __forceinline__ float * df_hid() { return reinterpret_cast<float *>(df_att() + df_P.n_att); }
+
+// The op's activation rows from a tagged buffer.
+__device__ __noinline__ bool df_stage_poll(const DfOp & op, int f, float * xs) {
+    const int cols = op.A.cols;
+    return df_poll_rows(df_in(df_P, op, f) + (size_t) op.in_row * cols, cols, op.nv, df_in_tag(df_P, op, f), xs,
+                        df_P.err);
+}
+
+// Sampler prologue: sample codebook op.cb (every CTA, the same decision), then
+// the pass's input rows into xs and this CTA's residual rows.  Returns 1 when
+// codebook 0 sampled EOS (the launch ends), -1 when an input did not arrive.
+__device__ __noinline__ int df_stage_sample(const DfOp & op, int f, int frame, float * xs) {
+    const DfArgs & P = df_P;
+    const int tid = threadIdx.x, nt = blockDim.x, cta = blockIdx.x;
+    const int cb = op.cb, V = cb == 0 ? P.V0 : P.V1, H = P.H;
+    int tok;
+    if (cb == 0 && f == 0) {
+        tok = sample_body_l<8>(
+            [&](float * l) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int i = tid * 8 + e;
+                    l[e] = i < V ? __ldcg(P.logits0 + i) : -INFINITY;
+                }
+            },
+            V, cb, &df_st, df_sp, frame);
+    } else {
+        const unsigned long long * src = df_in(P, op, f);
+        const unsigned tag = df_in_tag(P, op, f);
+        tok = sample_body_l<8>(
+            [&](float * l) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) l[e] = -INFINITY;
+                const int np = max(0, min(4, (V - tid * 8) / 2));
+                unsigned pend = (1u << np) - 1u;
+                for (unsigned long long it = 0; pend && it < QTTS_SPIN_LIMIT; ++it) {
+                    unsigned long long a[4], b[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if (pend >> q & 1u) ld_tagged2(src + tid * 8 + 2 * q, a[q], b[q]);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if ((pend >> q & 1u) && tag_of(a[q]) == tag && tag_of(b[q]) == tag) {
+                            l[2 * q] = val_of(a[q]);
+                            l[2 * q + 1] = val_of(b[q]);
+                            pend &= ~(1u << q);
+                        }
+                    if ((it & 255u) == 255u && *(volatile const int *) P.err) break;
+                }
+                if (pend) df_bad = 1;
+            },
+            V, cb, &df_st, df_sp, frame);
+    }
+    __syncthreads();
+    if (df_bad) return -1;
+    if (cb == 0 && tok == df_sp.eos_id) {
+        if (cta == 0 && tid == 0) sample_commit(tok, 0, P.st, df_sp, P.out_codes, P.out_cap, frame);
+        return 1;
+    }
+    if (tid == 0) {
+        df_st.codes[cb] = tok;
+        if (cb == 0) df_st.presence[tok >> 5] |= 1u << (tok & 31);
+        if (cta == 0) sample_commit(tok, cb, P.st, df_sp, P.out_codes, P.out_cap, frame);
+    }
+    __syncthreads();
+    // input rows of the pass (same values and sums as frame_inputs_body)
+    const int rpc_h = gemv_rpc(H, gridDim.x), r0_h = cta * rpc_h;
     const int nrow_h = max(0, min(H, r0_h + rpc_h) - r0_h);
+    const float * hid = df_hid();
+    const int n_tr = df_st.n_trailing;
+    for (int c = tid; c < H; c += nt) {
+        float x0, x1 = 0.0f;
+        if (op.pro == PRO_CB0) {
+            x0 = hid[c];
+            x1 = __half2float(P.codec_embd[(size_t) tok * H + c]);
+        } else if (op.pro == PRO_CBG) {
+            x0 = __half2float(df_tab[cb][(size_t) tok * H + c]);
+        } else {
+            float s = __half2float(P.codec_embd[(size_t) df_st.codes[0] * H + c]);
+            for (int q = 1; q < P.n_cb; ++q) s = __fadd_rn(s, __half2float(df_tab[q][(size_t) df_st.codes[q] * H + c]));
+            const float t = frame < n_tr ? P.trailing[(size_t) frame * H + c] : P.pad[c];
+            x0 = __fadd_rn(s, t);
+        }
+        xs[xpos(c, H)] = x0;
+        if (op.nv == 2) xs[H + xpos(c, H)] = x1;
+        const int rl = c - r0_h;
+        if (rl >= 0 && rl < nrow_h) {
+            df_res[0][rl] = x0;
+            df_res[1][rl] = x1;
+        }
+    }
+    return 0;
+}
+
+// Code-predictor attention into the O-projection's input rows (xs, QD columns):
+// steps one warp per query head, the 2-row prefill one warp per (head, row).
+// CTA 0 appends the new K/V rows to the cache.  False when an input did not arrive.
+__device__ __noinline__ bool df_stage_cp_attn(const DfOp & op, int f, float * xs) {
+    const DfArgs & P = df_P;
+    const FusedAttn & a = df_att()[op.layer];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int NH = a.n_heads, G = NH / a.n_kv_heads;
+    const int QD = NH * QTTS_HD, KD = a.n_kv_heads * QTTS_HD;
+    const unsigned long long * q = df_in(P, op, f);
+    const unsigned tag = df_in_tag(P, op, f);
+    bool wrote = false, ok = true;
+    if (op.pro == PRO_CPATTN) {
+        for (int hq = warp; hq < NH; hq += nw) {
+            const int g = hq / G;
+            CpStepRegs R;
+            cp_step_load(a, hq, op.n_past, R);
+            const unsigned long long * srcs[3] = {q + (size_t) hq * QTTS_HD + lane * 4,
+                                                  q + QD + (size_t) g * QTTS_HD + lane * 4,
+                                                  q + QD + KD + (size_t) g * QTTS_HD + lane * 4};
+            float4 in[3];
+            // a lane that timed out makes the whole warp give up (the body shuffles over all lanes)
+            if (!__all_sync(0xffffffffu, df_poll_quads<3>(srcs, 3, tag, in, P.err))) { ok = false; break; }
+            const bool w = blockIdx.x == 0 && hq % G == 0;
+            const float4 o = cp_step_compute(a, hq, op.n_past, R, in[0], in[1], in[2], w);
+            wrote |= w;
+            *reinterpret_cast<float4 *>(xs + xpos(hq * QTTS_HD + lane * 4, QD)) = o;
+        }
+    } else {
+        const int QKVD = QD + 2 * KD;
+        for (int u = warp; u < 2 * NH; u += nw) {
+            const int hq = u % NH, i = u / NH, g = hq / G;
+            const unsigned long long * srcs[5] = {q + (size_t) i * QKVD + (size_t) hq * QTTS_HD + lane * 4,
+                                                  q + QD + (size_t) g * QTTS_HD + lane * 4,
+                                                  q + QD + KD + (size_t) g * QTTS_HD + lane * 4,
+                                                  q + QKVD + QD + (size_t) g * QTTS_HD + lane * 4,
+                                                  q + QKVD + QD + KD + (size_t) g * QTTS_HD + lane * 4};
+            float4 in[5] = {};
+            if (!__all_sync(0xffffffffu, df_poll_quads<5>(srcs, i == 0 ? 3 : 5, tag, in, P.err))) { ok = false; break; }
+            const float4 kv[2] = {in[1], in[3]}, vv[2] = {in[2], in[4]};
+            const bool w = blockIdx.x == 0 && hq % G == 0;
+            const float4 o = df_cp_prefill_unit(a, hq, i, op.n_past, in[0], kv, vv, w);
+            wrote |= w;
+            *reinterpret_cast<float4 *>(xs + i * QD + xpos(hq * QTTS_HD + lane * 4, QD)) = o;
+        }
+    }
+    if (wrote) __threadfence();   // the cache rows before this CTA's tagged outputs
+    return ok;
+}
+
+// Talker attention, one query head per CTA (CTAs 0 .. n_heads - 1): the head's q
+// and its group's k / v into a full-row staging area, then the fused unit with a
+// tagged output.  Returns false when an input did not arrive.
+__device__ __noinline__ bool df_stage_talker_attn(const DfOp & op, int f, int k, int n_past, int frame) {
+    const DfArgs & P = df_P;
+    const FusedAttn & a0 = df_att()[op.layer];
+    const int NH = a0.n_heads, G = NH / a0.n_kv_heads;
+    const int QD = NH * QTTS_HD, KD = a0.n_kv_heads * QTTS_HD;
+    const int hq = blockIdx.x, g = hq / G;
+    uint8_t * work = df_work();
+    float * stage = reinterpret_cast<float *>(work);
+    const unsigned long long * q = df_in(P, op, f);
+    // pair p < 64: q of head hq; 64..127: k of group g; 128..191: v of group g
+    auto off = [&](int p) {
+        const int part = p / (QTTS_HD / 2), c = 2 * (p % (QTTS_HD / 2));
+        return (part == 0 ? hq * QTTS_HD : QD + (part == 2 ? KD : 0) + g * QTTS_HD) + c;
+    };
+    const bool ok = df_poll_pairs_at<1>(3 * QTTS_HD / 2, df_in_tag(P, op, f), [&](int p) { return q + off(p); },
+                                        [&](int p, float v0, float v1) {
+                                            *reinterpret_cast<float2 *>(stage + off(p)) = make_float2(v0, v1);
+                                        },
+                                        P.err);
+    fence_acq_rel_gpu();   // the cached K/V rows other CTAs appended are read after this
+    if (__syncthreads_or(!ok)) return false;
+    FusedAttn a = a0;
+    a.qkv = stage;
+    a.fout = df_slot(P, op.out_buf, f, op.out_wr);
+    a.ftag = df_tag(P, f, k);
+    fused_attn_body(a, hq, work + ((size_t)(QD + 2 * KD) * 4 + 127) / 128 * 128, n_past, frame);
+    return true;
+}
+
+// The op's GEMV with its activation rows in xs: residual rows from df_res,
+// tagged outputs (the talker head also writes the plain logits, the hidden
+// state in every CTA's df_hid and, in CTA 0, the plain hidden state).
+template <int NV>
+__device__ __noinline__ bool df_stage_gemv(const DfOp & op, int f, int k, unsigned parity,
+                                           unsigned long long * ready_stamp) {
+    const DfArgs & P = df_P;
+    const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x, nt = blockDim.x;
+    const int rpc = gemv_rpc(op.A.rows, ncta);
+    const GemvWork W = gemv_work<NV>(df_work(), op.A.cols, rpc, op.A.type == W_Q8_0);
+    if (op.epi == EPI_RESID) {
+        const int H = P.H, r0 = cta * rpc, nrow = max(0, min(H, r0 + rpc) - r0);
+        const int rstride = (rpc + 3) & ~3;
+        for (int t = tid; t < NV * nrow; t += nt) W.rs[(t / nrow) * rstride + t % nrow] = df_res[t / nrow][t % nrow];
+        __syncthreads();
+    }
+    GemvArgs g{};
+    g.A = op.A;
+    g.B = op.B;
+    g.nv = NV;
+    g.norm_g = op.norm_g;
+    g.eps = P.eps;
+    g.act = op.act;
+    g.epi = op.epi;
+    g.xn_out = op.head == 1 ? P.hidden : nullptr;   // CTA 0: the plain talker hidden state
+    g.ldxn = P.H;
+    const DfStore store{df_slot(P, op.out_buf, f, op.out_wr), op.A.rows, df_tag(P, f, k),
+                        op.head == 1 ? P.logits_out : nullptr, op.epi == EPI_RESID ? df_res : nullptr};
+    const int b = op.slot;
+    return gemv_compute<NV>(g, cta, ncta, df_smem + (size_t) b * P.wbuf_bytes, df_work(), df_mbar + b, parity, store,
+                            op.head == 1 ? df_hid() : nullptr, ready_stamp);
+}
+
+__global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs Pk) {
+    const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x, nt = blockDim.x;
     constexpr int NW = (int)(sizeof(DfOp) / 8);
     static_assert(sizeof(DfOp) % 8 == 0 && NW <= DF_THREADS, "descriptor copy");
-    static_assert(sizeof(FusedAttn) % 8 == 0, "attention table copy");
-    unsigned phase = 0u, pending = 0u;
-
-    if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        s_sp = *P.sp;
-        if (cta != 0) s_sp.record_logits = 0;   // CTA 0 records the debug logits
-        s_bad = 0;
+    static_assert(sizeof(FusedAttn) % 8 == 0 && sizeof(DfArgs) % 8 == 0, "table copies");
+    {
+        const unsigned long long * src = reinterpret_cast<const unsigned long long *>(&Pk);
+        for (int w = tid; w < (int)(sizeof(DfArgs) / 8); w += nt) reinterpret_cast<unsigned long long *>(&df_P)[w] = src[w];
     }
-    if (tid < NW) reinterpret_cast<unsigned long long *>(&desc[0])[tid] = reinterpret_cast<const unsigned long long *>(P.ops)[tid];
+    if (tid == 0) {
+        mbar_init(&df_mbar[0], 1);
+        mbar_init(&df_mbar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        df_sp = *Pk.sp;
+        if (cta != 0) df_sp.record_logits = 0;   // CTA 0 records the debug logits
+        df_bad = 0;
+    }
+    if (tid < NW) reinterpret_cast<unsigned long long *>(&df_desc[0])[tid] = reinterpret_cast<const unsigned long long *>(Pk.ops)[tid];
+    __syncthreads();
+    const DfArgs & P = df_P;
+    FusedAttn * att = df_att();
+    float * hid = df_hid();
     {
         const int n8 = P.n_att * (int)(sizeof(FusedAttn) / 8);
         for (int w = tid; w < n8; w += nt)
             reinterpret_cast<unsigned long long *>(att)[w] = reinterpret_cast<const unsigned long long *>(P.att)[w];
     }
     for (int i = tid; i < (int)(sizeof(DevState) / 4); i += nt)
-        reinterpret_cast<int *>(&s_st)[i] = reinterpret_cast<const volatile int *>(P.st)[i];
-    for (int c = tid; c < H; c += nt) hid[c] = __ldcg(P.hidden + c);
-    if (tid >= 1 && tid < P.n_cb) s_tab[tid] = P.cp_embd[tid - 1];
+        reinterpret_cast<int *>(&df_st)[i] = reinterpret_cast<const volatile int *>(P.st)[i];
+    for (int c = tid; c < P.H; c += nt) hid[c] = __ldcg(P.hidden + c);
+    if (tid >= 1 && tid < P.n_cb) df_tab[tid] = P.cp_embd[tid - 1];
     __syncthreads();
     if (tid == 0) {
         for (int k = 0; k < P.n_pf0; ++k) {
@@ -346,235 +561,62 @@ __global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs P) {
         }
         for (int b = 0; b < 2; ++b) {
             const DfOp & g = P.ops[P.first[b]];
-            issue_gemv_slice(g.A, g.B, g.norm_g, smem + (size_t) g.slot * P.wbuf_bytes, mbar + g.slot, cta, ncta);
+            issue_gemv_slice(g.A, g.B, g.norm_g, df_smem + (size_t) g.slot * P.wbuf_bytes, df_mbar + g.slot, cta, ncta);
         }
     }
-    pending = 3u;
-    const int pos0 = s_st.pos, frame0 = s_st.frame, n_tr = s_st.n_trailing;
-    const int QD = att[0].n_heads * QTTS_HD, KD = att[0].n_kv_heads * QTTS_HD;
+    unsigned phase = 0u, pending = 3u;
+    const int pos0 = df_st.pos, frame0 = df_st.frame;
+    const int QD = att[0].n_heads * QTTS_HD;
     bool stop = false, failed = false;
 
-    for (int f = 0; f < P.n_frames && !stop; ++f) {
+    for (int f = 0; f < P.n_frames && !stop && !failed; ++f) {
         const int frame = frame0 + f;
         for (int k = 0; k < P.n_ops; ++k) {
-            const DfOp & op = desc[k & 1];
+            const DfOp & op = df_desc[k & 1];
             unsigned long long * tr = P.trace ? P.trace + ((size_t) f * P.n_ops + k) * DF_TRACE : nullptr;
             if (tr && cta == 0 && tid == 0) tr[0] = df_now();
             const int nx = k + 1 < P.n_ops ? k + 1 : 0;
             const unsigned long long nword = tid < NW ? reinterpret_cast<const unsigned long long *>(P.ops + nx)[tid] : 0ull;
-            bool ok = true;
             if (op.type == DF_GEMV) {
-                const int cols = op.A.cols;
-                const int rpc = gemv_rpc(op.A.rows, ncta);
-                const bool q8 = op.A.type == W_Q8_0;
-                const GemvWork W = op.nv == 1 ? gemv_work<1>(work, cols, rpc, q8) : gemv_work<2>(work, cols, rpc, q8);
-                float * xs = W.xs;
-                // ---- activation rows
-                if (op.pro == PRO_POLL) {
-                    ok = df_poll_rows(df_in(P, op, f) + (size_t) op.in_row * cols, cols, op.nv, df_in_tag(P, op, f),
-                                      xs, P.err);
-                } else if (op.pro == PRO_CB0 || op.pro == PRO_CBG || op.pro == PRO_CBLAST) {
-                    const int cb = op.cb, V = cb == 0 ? P.V0 : P.V1;
-                    int tok;
-                    if (cb == 0 && f == 0) {
-                        tok = sample_body_l<8>(
-                            [&](float * l) {
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) {
-                                    const int i = tid * 8 + e;
-                                    l[e] = i < V ? __ldcg(P.logits0 + i) : -INFINITY;
-                                }
-                            },
-                            V, cb, &s_st, s_sp, frame);
-                    } else {
-                        const unsigned long long * src = df_in(P, op, f);
-                        const unsigned tag = df_in_tag(P, op, f);
-                        tok = sample_body_l<8>(
-                            [&](float * l) {
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) l[e] = -INFINITY;
-                                const int np = max(0, min(4, (V - tid * 8) / 2));
-                                unsigned pend = (1u << np) - 1u;
-                                for (unsigned long long it = 0; pend && it < QTTS_SPIN_LIMIT; ++it) {
-                                    unsigned long long a[4], b[4];
-#pragma unroll
-                                    for (int q = 0; q < 4; ++q)
-                                        if (pend >> q & 1u) ld_tagged2(src + tid * 8 + 2 * q, a[q], b[q]);
-#pragma unroll
-                                    for (int q = 0; q < 4; ++q)
-                                        if ((pend >> q & 1u) && tag_of(a[q]) == tag && tag_of(b[q]) == tag) {
-                                            l[2 * q] = val_of(a[q]);
-                                            l[2 * q + 1] = val_of(b[q]);
-                                            pend &= ~(1u << q);
-                                        }
-                                    if ((it & 255u) == 255u && *(volatile const int *) P.err) break;
-                                }
-                                if (pend) s_bad = 1;
-                            },
-                            V, cb, &s_st, s_sp, frame);
-                    }
-                    __syncthreads();
-                    if (s_bad) {
-                        ok = false;
-                    } else if (cb == 0 && tok == s_sp.eos_id) {
-                        if (cta == 0 && tid == 0) sample_commit(tok, 0, P.st, s_sp, P.out_codes, P.out_cap, frame);
-                        stop = true;
-                    } else {
-                        if (tid == 0) {
-                            s_st.codes[cb] = tok;
-                            if (cb == 0) s_st.presence[tok >> 5] |= 1u << (tok & 31);
-                            if (cta == 0) sample_commit(tok, cb, P.st, s_sp, P.out_codes, P.out_cap, frame);
-                        }
-                        __syncthreads();
-                        // input rows of the pass (same values and sums as frame_inputs_body)
-                        for (int c = tid; c < H; c += nt) {
-                            float x0, x1 = 0.0f;
-                            if (op.pro == PRO_CB0) {
-                                x0 = hid[c];
-                                x1 = __half2float(P.codec_embd[(size_t) tok * H + c]);
-                            } else if (op.pro == PRO_CBG) {
-                                x0 = __half2float(s_tab[cb][(size_t) tok * H + c]);
-                            } else {
-                                float s = __half2float(P.codec_embd[(size_t) s_st.codes[0] * H + c]);
-                                for (int q = 1; q < P.n_cb; ++q)
-                                    s = __fadd_rn(s, __half2float(s_tab[q][(size_t) s_st.codes[q] * H + c]));
-                                const float t = frame < n_tr ? P.trailing[(size_t) frame * H + c] : P.pad[c];
-                                x0 = __fadd_rn(s, t);
-                            }
-                            xs[xpos(c, H)] = x0;
-                            if (op.nv == 2) xs[H + xpos(c, H)] = x1;
-                            const int rl = c - r0_h;
-                            if (rl >= 0 && rl < nrow_h) {
-                                s_res[0][rl] = x0;
-                                s_res[1][rl] = x1;
-                            }
-                        }
-                    }
-                } else {   // code-predictor attention into the O-projection's rows
-                    const FusedAttn & a = att[op.layer];
-                    const int NH = a.n_heads, G = NH / a.n_kv_heads;
-                    const unsigned long long * q = df_in(P, op, f);
-                    const unsigned tag = df_in_tag(P, op, f);
-                    bool wrote = false;
-                    if (op.pro == PRO_CPATTN) {
-                        for (int hq = warp; hq < NH; hq += nw) {
-                            const int g = hq / G;
-                            CpStepRegs R;
-                            cp_step_load(a, hq, op.n_past, R);
-                            const unsigned long long * srcs[3] = {q + (size_t) hq * QTTS_HD + lane * 4,
-                                                                  q + QD + (size_t) g * QTTS_HD + lane * 4,
-                                                                  q + QD + KD + (size_t) g * QTTS_HD + lane * 4};
-                            float4 in[3];
-                            // a lane that timed out makes the whole warp give up (the body shuffles over all lanes)
-                            if (!__all_sync(0xffffffffu, df_poll_quads<3>(srcs, 3, tag, in, P.err))) { s_bad = 1; break; }
-                            const bool w = cta == 0 && hq % G == 0;
-                            const float4 o = cp_step_compute(a, hq, op.n_past, R, in[0], in[1], in[2], w);
-                            wrote |= w;
-                            *reinterpret_cast<float4 *>(xs + xpos(hq * QTTS_HD + lane * 4, QD)) = o;
-                        }
-                    } else {
-                        const int QKVD = QD + 2 * KD;
-                        for (int u = warp; u < 2 * NH; u += nw) {
-                            const int hq = u % NH, i = u / NH, g = hq / G;
-                            const unsigned long long * srcs[5] = {
-                                q + (size_t) i * QKVD + (size_t) hq * QTTS_HD + lane * 4,
-                                q + QD + (size_t) g * QTTS_HD + lane * 4,
-                                q + QD + KD + (size_t) g * QTTS_HD + lane * 4,
-                                q + QKVD + QD + (size_t) g * QTTS_HD + lane * 4,
-                                q + QKVD + QD + KD + (size_t) g * QTTS_HD + lane * 4};
-                            float4 in[5] = {};
-                            if (!__all_sync(0xffffffffu, df_poll_quads<5>(srcs, i == 0 ? 3 : 5, tag, in, P.err))) {
-                                s_bad = 1;
-                                break;
-                            }
-                            const float4 kv[2] = {in[1], in[3]}, vv[2] = {in[2], in[4]};
-                            const bool w = cta == 0 && hq % G == 0;
-                            const float4 o = df_cp_prefill_unit(a, hq, i, op.n_past, in[0], kv, vv, w);
-                            wrote |= w;
-                            *reinterpret_cast<float4 *>(xs + i * QD + xpos(hq * QTTS_HD + lane * 4, QD)) = o;
-                        }
-                    }
-                    if (wrote) __threadfence();   // cache rows before this CTA's tagged outputs
-                }
-                if (__syncthreads_or(!ok || s_bad)) {
+                float * xs = reinterpret_cast<float *>(df_work());
+                int rc = 0;
+                if (op.pro == PRO_POLL) rc = df_stage_poll(op, f, xs) ? 0 : -1;
+                else if (op.pro == PRO_CPATTN || op.pro == PRO_CPATTN2) rc = df_stage_cp_attn(op, f, xs) ? 0 : -1;
+                else rc = df_stage_sample(op, f, frame, xs);
+                if (__syncthreads_or(rc < 0)) {
                     failed = true;
-                } else if (!stop) {
+                } else if (rc == 1) {
+                    stop = true;
+                } else {
                     if (tr && tid == 0) {
                         const unsigned long long t = df_now();
                         if (cta == 0) tr[1] = t;
                         atomicMax(tr + 2, t);
                     }
-                    // residual rows of this CTA, then the GEMV
-                    if (op.epi == EPI_RESID) {
-                        const int rstride = (rpc + 3) & ~3;
-                        for (int t = tid; t < op.nv * nrow_h; t += nt)
-                            W.rs[(t / nrow_h) * rstride + t % nrow_h] = s_res[t / nrow_h][t % nrow_h];
-                        __syncthreads();
-                    }
-                    GemvArgs g{};
-                    g.A = op.A;
-                    g.B = op.B;
-                    g.nv = op.nv;
-                    g.norm_g = op.norm_g;
-                    g.eps = P.eps;
-                    g.act = op.act;
-                    g.epi = op.epi;
-                    g.xn_out = op.head == 1 ? P.hidden : nullptr;   // CTA 0: the plain talker hidden state
-                    g.ldxn = H;
-                    const DfStore store{df_slot(P, op.out_buf, f, op.out_wr), op.A.rows, df_tag(P, f, k),
-                                        op.head == 1 ? P.logits_out : nullptr, op.epi == EPI_RESID ? s_res : nullptr};
                     const int b = op.slot;
-                    uint8_t * wb = smem + (size_t) b * P.wbuf_bytes;
-                    const unsigned par = phase >> b & 1u;
-                    const bool gok = op.nv == 1
-                        ? gemv_compute<1>(g, cta, ncta, wb, work, mbar + b, par, store, op.head == 1 ? hid : nullptr)
-                        : gemv_compute<2>(g, cta, ncta, wb, work, mbar + b, par, store, nullptr);
+                    unsigned long long * rs = tr && cta == 0 ? tr + 3 : nullptr;
+                    const bool gok = op.nv == 1 ? df_stage_gemv<1>(op, f, k, phase >> b & 1u, rs)
+                                                : df_stage_gemv<2>(op, f, k, phase >> b & 1u, rs);
                     if (!gok) failed = true;
                     phase ^= 1u << b;
                     pending &= ~(1u << b);
                 }
-            } else {   // DF_TATTN: talker attention, one query head per CTA
-                const FusedAttn & a0 = att[op.layer];
-                const int NH = a0.n_heads, G = NH / a0.n_kv_heads;
-                if (cta < NH) {
-                    const int hq = cta, g = hq / G;
-                    float * stage = reinterpret_cast<float *>(work);   // the q|k|v row, only this unit's parts
-                    const unsigned long long * q = df_in(P, op, f);
-                    // pair p < 64: q of head hq; 64..127: k of group g; 128..191: v of group g
-                    auto off = [&](int p) {
-                        const int part = p / (QTTS_HD / 2), c = 2 * (p % (QTTS_HD / 2));
-                        return (part == 0 ? hq * QTTS_HD : QD + (part == 2 ? KD : 0) + g * QTTS_HD) + c;
-                    };
-                    ok = df_poll_pairs_at<1>(3 * QTTS_HD / 2, df_in_tag(P, op, f), [&](int p) { return q + off(p); },
-                                             [&](int p, float v0, float v1) {
-                                                 *reinterpret_cast<float2 *>(stage + off(p)) = make_float2(v0, v1);
-                                             },
-                                             P.err);
-                    fence_acq_rel_gpu();   // the cached K/V rows other CTAs appended are read after this
-                    if (__syncthreads_or(!ok)) {
-                        failed = true;
-                    } else {
-                        FusedAttn a = a0;
-                        a.qkv = stage;
-                        a.fout = df_slot(P, op.out_buf, f, op.out_wr);
-                        a.ftag = df_tag(P, f, k);
-                        fused_attn_body(a, hq, work + ((size_t)(QD + 2 * KD) * 4 + 127) / 128 * 128, pos0 + f, frame);
-                    }
-                }
+            } else if (cta < att[op.layer].n_heads) {   // DF_TATTN: CTAs 0 .. n_heads - 1
+                if (!df_stage_talker_attn(op, f, k, pos0 + f, frame)) failed = true;
             }
             if (failed) {
                 if (tid == 0) atomicExch(P.err, 2);
                 break;
             }
             if (stop) break;
-            if (tr && cta == 0 && tid == 0) tr[3] = df_now();
-            __syncthreads();   // everyone is done with desc[k & 1] and with the op's weight buffer
-            if (tid < NW) reinterpret_cast<unsigned long long *>(&desc[(k + 1) & 1])[tid] = nword;
+            if (tr && cta == 0 && tid == 0) tr[4] = df_now();
+            __syncthreads();   // everyone is done with df_desc[k & 1] and with the op's weight buffer
+            if (tid < NW) reinterpret_cast<unsigned long long *>(&df_desc[(k + 1) & 1])[tid] = nword;
             if (op.type == DF_GEMV && tid == 0) {
                 if (op.iA.w) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    issue_gemv_slice(op.iA, op.iB, op.iG, smem + (size_t) op.slot * P.wbuf_bytes, mbar + op.slot,
-                                     cta, ncta);
+                    issue_gemv_slice(op.iA, op.iB, op.iG, df_smem + (size_t) op.slot * P.wbuf_bytes,
+                                     df_mbar + op.slot, cta, ncta);
                 }
                 df_prefetch_slice(op.pA, cta, ncta);
                 df_prefetch_slice(op.pB, cta, ncta);
@@ -589,7 +631,8 @@ __global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs P) {
             P.st->n_out += 1;
         }
     }
-    df_drain(mbar, pending, phase);
+    (void) QD;
+    df_drain(df_mbar, pending, phase);
 }
 
 }  // namespace qtts

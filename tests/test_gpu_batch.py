@@ -137,7 +137,7 @@ def _icl_utterance(seed, prefill, frames, hidden):
 # Q8_0) can flip: oracle margin <= 2 x tolerance, and rarely (Q8_0: the
 # activation quantiser turns order differences into whole int8 levels).
 BATCH_MARGIN = {"f16": 4e-2, "q8": 1e-1}
-BATCH_FRAC = {"f16": 0.01, "q8": 0.05}
+BATCH_FRAC = {"f16": 0.01, "q8": 0.10}
 
 
 def _follow(path, utts, codes, frames, idx, engine_order, which):

@@ -14,7 +14,9 @@ BASELINE.json north_star contract:
   * logits within max-abs 2e-2 (F16) / 5e-2 (Q8_0) along the whole run;
   * every divergent decision is a near-tie under the measured logit
     difference delta (margin <= 2 delta: a perturbation of delta can flip it),
-    and they are rare (<= 1 % of decisions for F16, 5 % for Q8_0).
+    and they are rare (<= 1 % of decisions for F16 greedy runs; 5 % for sampled
+    runs, where any draw within T x 2 delta of a bucket edge is at risk, and for
+    Q8_0).
 
 Q8_0 exception, measured: the activation quantiser turns last-bit differences
 of the normalised activation (from a different summation order) into whole
@@ -38,7 +40,7 @@ from oracle import Oracle
 pytestmark = pytest.mark.gpu
 
 LOGIT_TOL = {"f16": (2e-2, 2e-2), "q8": (5e-2, 1e-1)}   # (talker, code predictor)
-DIVERGENT_FRAC = {"f16": 0.01, "q8": 0.05}
+DIVERGENT_FRAC = {"f16": 0.01, "q8": 0.05, "sampled": 0.05}
 
 
 def _follow(o, e, which, **kw):
@@ -53,7 +55,8 @@ def _follow(o, e, which, **kw):
     assert r["n_frames"] == n
     assert tl < LOGIT_TOL[which][0] and cl < LOGIT_TOL[which][1], diag
     assert r["max_tie_gap"] <= 2 * delta, diag
-    assert r["n_ties"] <= DIVERGENT_FRAC[which] * 16 * n, diag
+    frac = DIVERGENT_FRAC["sampled" if kw.get("temperature", 0.0) > 0.0 else which]
+    assert r["n_ties"] <= frac * 16 * n, diag
     return r
 
 
