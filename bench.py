@@ -422,16 +422,22 @@ def run_ncu_workload(args):
         if os.environ.get("QTTS_DF_TRACE") and got:
             ops, tr = eng.frame_trace()
             t = tr[: len(ops) * got].astype(np.int64)
-            nxt = np.append(t[1:, 0], t[-1, 3])
+            nxt = np.append(t[1:, 0], t[-1, 6])
             names = {16: "gemv", 17: "gemv+cb0", 18: "gemv+cbg", 19: "gemv+cblast", 20: "gemv+cpattn2",
                      21: "gemv+cpattn", 32: "talker-attn"}
             kinds = np.tile(ops, got)
+            def col(i, c):   # mean of stamp c - start over the ops that recorded it (0: not recorded)
+                v = t[i, c]
+                v = v[v > 0] - t[i, 0][v > 0]
+                return v.mean() / 1e3 if len(v) else float("nan")
             for ty in sorted(set(ops.tolist())):
                 i = np.nonzero(kinds == ty)[0]
-                print(f"{names.get(ty, ty):12s} n={len(i) // got:4d}/frame  input(cta0) {(t[i, 1] - t[i, 0]).mean() / 1e3:6.2f}"
-                      f"  input(last cta) {(t[i, 2] - t[i, 0]).mean() / 1e3:6.2f}  done(cta0) {(t[i, 3] - t[i, 0]).mean() / 1e3:6.2f}"
-                      f"  next {(nxt[i] - t[i, 0]).mean() / 1e3:6.2f} us", file=sys.stderr)
-            print(f"frame span {(t[-1, 3] - t[0, 0]) / 1e3 / got:.1f} us", file=sys.stderr)
+                print(f"{names.get(ty, ty):12s} n={len(i) // got:4d}/frame  input {col(i, 1):5.2f}  last-cta-input"
+                      f" {col(i, 2):5.2f}  weights {col(i, 3):5.2f}  row0 {col(i, 4):5.2f}  rows-done {col(i, 5):5.2f}"
+                      f"  done {col(i, 6):5.2f}  barrier1 {col(i, 8):5.2f}  issued {col(i, 7):5.2f}  barrier2 {col(i, 9):5.2f}"
+                      f"  next {(nxt[i] - t[i, 0]).mean() / 1e3:5.2f} us",
+                      file=sys.stderr)
+            print(f"frame span {(t[-1, 6] - t[0, 0]) / 1e3 / got:.1f} us", file=sys.stderr)
         eng.close()
         return 0
     path = pkg.synth_gguf.ensure_gguf(d, cfg_m, "f16", seed=0)

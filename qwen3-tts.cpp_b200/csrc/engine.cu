@@ -334,7 +334,7 @@ bool Engine::load(const char * path, int device) {
         err = "hidden/ffn/text widths must be multiples of 256/32/32"; return false;
     }
     if (const char * m = getenv("QTTS_FRAME_MODE")) use_dataflow = strcmp(m, "dataflow") == 0;
-    if (const char * v = getenv("QTTS_DF_PF_LEAD")) df_pf_lead = std::max(2, atoi(v));
+    if (const char * v = getenv("QTTS_DF_PF_LEAD")) df_pf_lead = std::max(0, atoi(v));   // 0: no L2 prefetch
     if (!upload_weights(g)) return false;
     if (!alloc_activations()) return false;
     if (!init_cp_kv(16)) return false;
@@ -936,14 +936,16 @@ bool Engine::build_program(int max_keys) {
         if (prog[i].type == DF_GEMV) gi.push_back(i);
     const int m = (int) gi.size();
     if (m < 4 || (m & 1)) { err = "unexpected GEMV count in the frame program"; return false; }
-    const int lead = std::max(2, std::min(df_pf_lead, m - 1));
+    const int lead = df_pf_lead <= 0 ? 0 : std::max(2, std::min(df_pf_lead, m - 1));
     for (int j = 0; j < m; ++j) {
         DfOp & site = prog[gi[j]];
         site.slot = j & 1;
         const DfOp & nx = prog[gi[(j + 2) % m]];
         site.iA = nx.A; site.iB = nx.B; site.iG = nx.norm_g;
-        const DfOp & pf = prog[gi[(j + lead) % m]];
-        site.pA = pf.A; site.pB = pf.B;
+        if (lead) {
+            const DfOp & pf = prog[gi[(j + lead) % m]];
+            site.pA = pf.A; site.pB = pf.B;
+        }
     }
     df_first[0] = gi[0];
     df_first[1] = gi[1];
@@ -962,8 +964,32 @@ bool Engine::build_program(int max_keys) {
             work = std::max(work, ((size_t) QKVD * 4 + 127) / 128 * 128 + fused_attn_smem(max_keys, 1));
         }
     }
+    // Code-predictor step attention: its cached K/V rows (positions 0 .. n_past - 1,
+    // contiguous per layer) ride in the O-projection's weight slot behind the slice,
+    // copied with it (the 0.6B F16 layout fills the 88 KB gate/up slot exactly).
+    for (int j = 0; j < m; ++j) {
+        const DfOp & op = prog[gi[j]];
+        if (op.pro != PRO_CPATTN) continue;
+        const size_t so = (slice_layout(op.A, false, false, gemv_rpc(op.A.rows, n_sm)).total + 127) & ~(size_t) 127;
+        wb = std::max(wb, so + 2 * (size_t) op.n_past * NKV * QTTS_HD * 2);
+    }
     df_wbuf = (wb + 127) & ~(size_t) 127;
     df_work = (work + 127) & ~(size_t) 127;
+    for (int j = 0; j < m; ++j) {
+        DfOp & op = prog[gi[j]];
+        op.kv_off = -1;
+        if (op.pro != PRO_CPATTN) continue;
+        const size_t so = (slice_layout(op.A, false, false, gemv_rpc(op.A.rows, n_sm)).total + 127) & ~(size_t) 127;
+        const size_t kvb = (size_t) op.n_past * NKV * QTTS_HD * 2;
+        if (kvb > 32768 || op.n_past > CPA_MAX_KEYS) { err = "frame program: code-predictor context too long"; return false; }
+        op.kv_off = (int) so;
+        op.kv_bytes = (int) kvb;
+        DfOp & site = prog[gi[(j - 2 + m) % m]];
+        site.iK = cpk + (size_t) op.layer * cp_layer;
+        site.iV = cpv + (size_t) op.layer * cp_layer;
+        site.i_kv_bytes = (int) kvb;
+        site.i_kv_off = (int) so;
+    }
     const size_t dyn = 2 * df_wbuf + df_work + df_att.size() * sizeof(FusedAttn) + (size_t) H * 4;
     cudaFuncAttributes fa{};
     QCHECK(cudaFuncGetAttributes(&fa, k_frame_dataflow));

@@ -67,6 +67,9 @@ struct alignas(16) DfOp {
     DMat iA, iB;                        // slice copied into `slot` once this op is done (iA.w: none)
     const float * iG;
     DMat pA, pB;                        // slice prefetched into L2 once this op is done (pA.w: none)
+    const __half * iK, * iV;            // code-predictor K/V rows copied with that slice (iK: none)
+    int i_kv_bytes, i_kv_off;           // bytes of each, their offset in the slot
+    int kv_off, kv_bytes;               // this op's staged K/V rows (PRO_CPATTN; kv_off < 0: none)
 };
 
 struct DfArgs {
@@ -97,9 +100,11 @@ struct DfArgs {
     int pf0[8];                         // GEMV ops prefetched into L2 at launch
     unsigned long long * trace;         // optional [n_frames][n_ops][DF_TRACE] %globaltimer stamps
 };
-// Trace stamps per op: CTA 0 start, CTA 0 input ready, latest input ready over
-// the CTAs, CTA 0 weights ready, CTA 0 done.
-constexpr int DF_TRACE = 5;
+// Trace stamps per op (CTA 0 unless noted): start, input ready, latest input
+// ready over the CTAs, weights ready, first output row stored, last output row
+// stored, op done (thread 0), next slice copy and prefetches issued, past the
+// first end-of-op barrier, past the second.
+constexpr int DF_TRACE = 10;
 
 __device__ __forceinline__ unsigned long long df_now() {
     unsigned long long t;
@@ -177,8 +182,8 @@ __device__ __forceinline__ bool df_poll_pairs(const unsigned long long * src, in
 
 // N float quads (two word pairs each) of one lane, all in flight together.
 template <int N>
-__device__ __forceinline__ bool df_poll_quads(const unsigned long long * const * src, int n, unsigned tag, float4 * out,
-                                              const int * err) {
+__device__ __forceinline__ bool df_poll_quads(const unsigned long long * const (&src)[N], int n, unsigned tag,
+                                              float4 (&out)[N], const int * err) {
     unsigned pend = (1u << n) - 1u;
     for (unsigned long long it = 0; pend && it < QTTS_SPIN_LIMIT; ++it) {
         unsigned long long w[N][4];
@@ -219,10 +224,16 @@ struct DfStore {
     unsigned tag;
     float * plain;
     float (*res)[8];
+    unsigned long long * stamp;   // trace: [0] first row stored, [1] latest row stored (or nullptr)
     __device__ __forceinline__ void operator()(int r, int rl, int v, float val) const {
         st_tagged(out + (size_t) v * ld + r, val, tag);
         if (plain) plain[(size_t) v * ld + r] = val;
         if (res) res[v][rl] = val;
+        if (stamp) {
+            const unsigned long long t = df_now();
+            if (rl == 0 && v == 0) stamp[0] = t;
+            atomicMax(stamp + 1, t);
+        }
     }
 };
 
@@ -234,56 +245,61 @@ struct DfStore {
 // groups summed in order.  kv_write: append row i's K/V (F16) to the cache.
 // Returns the output quad of dims 4 lane .. 4 lane + 3.
 __device__ __forceinline__ float4 df_cp_prefill_unit(const FusedAttn & a, int hq, int i, int n_past, const float4 qv,
-                                                     const float4 * kv, const float4 * vv, bool kv_write) {
+                                                     const float4 k0, const float4 v0, const float4 k1, const float4 v1,
+                                                     bool kv_write) {
     const int lane = threadIdx.x & 31;
     const int NKV = a.n_kv_heads, g = hq / (a.n_heads / NKV);
     const size_t pstride = (size_t) NKV * QTTS_HD;
     float xq[4] = {qv.x, qv.y, qv.z, qv.w};
     head_norm_rope(xq, a.q_norm, a.eps, a.rope + (size_t)(n_past + i) * (QTTS_HD / 2), lane);
-    float xk[2][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        if (j > i) break;
-        xk[j][0] = kv[j].x; xk[j][1] = kv[j].y; xk[j][2] = kv[j].z; xk[j][3] = kv[j].w;
-        head_norm_rope(xk[j], a.k_norm, a.eps, a.rope + (size_t)(n_past + j) * (QTTS_HD / 2), lane);
-    }
+    float xk0[4] = {k0.x, k0.y, k0.z, k0.w}, xk1[4] = {k1.x, k1.y, k1.z, k1.w};
+    head_norm_rope(xk0, a.k_norm, a.eps, a.rope + (size_t) n_past * (QTTS_HD / 2), lane);
+    if (i == 1) head_norm_rope(xk1, a.k_norm, a.eps, a.rope + (size_t)(n_past + 1) * (QTTS_HD / 2), lane);
     if (kv_write) {
+        const float4 vi = i == 0 ? v0 : v1;
+        const float vq[4] = {vi.x, vi.y, vi.z, vi.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            a.kc[(size_t)(n_past + i) * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = __float2half_rn(xk[i][k]);
-            a.vc[(size_t)(n_past + i) * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = __float2half_rn((&vv[i].x)[k]);
+            a.kc[(size_t)(n_past + i) * pstride + (size_t) g * QTTS_HD + lane * 4 + k] =
+                __float2half_rn(i == 0 ? xk0[k] : xk1[k]);
+            a.vc[(size_t)(n_past + i) * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = __float2half_rn(vq[k]);
         }
     }
     // score of key j: the 8-lane group sub = lane & 7 chains dims 16 sub .. 16 sub + 15 (lanes 4 sub .. 4 sub + 3)
     const int sub = lane & 7;
-    float sc[2] = {0.0f, 0.0f};
+    float sc0, sc1;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
         float s = 0.0f;
+#pragma unroll 1
+        for (int dq = 0; dq < 4; ++dq) {   // dims 16 sub + 4 dq + e, in order
+            const int src = 4 * sub + dq;
 #pragma unroll
-        for (int d = 0; d < 16; ++d) {
-            const int src = 4 * sub + (d >> 2);
-            const float qd = __shfl_sync(0xffffffffu, xq[d & 3], src);
-            const float kd = __shfl_sync(0xffffffffu, xk[j <= i ? j : 0][d & 3], src);
-            s = fmaf(kd, qd, s);
+            for (int e = 0; e < 4; ++e) {
+                const float qd = __shfl_sync(0xffffffffu, xq[e], src);
+                const float kd = __shfl_sync(0xffffffffu, j == 0 ? xk0[e] : xk1[e], src);
+                s = fmaf(kd, qd, s);
+            }
         }
         s += __shfl_xor_sync(0xffffffffu, s, 4);
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         s += __shfl_xor_sync(0xffffffffu, s, 1);
-        sc[j] = __fmul_rn(s, a.scale);
+        if (j == 0) sc0 = __fmul_rn(s, a.scale);
+        else sc1 = __fmul_rn(s, a.scale);
     }
     const int n = i + 1;
-    const float mx = n == 2 ? fmaxf(sc[0], sc[1]) : sc[0];
-    const float e0 = qtts_expf(__fsub_rn(sc[0], mx));
-    const float e1 = n == 2 ? qtts_expf(__fsub_rn(sc[1], mx)) : 0.0f;
+    const float mx = n == 2 ? fmaxf(sc0, sc1) : sc0;
+    const float e0 = qtts_expf(__fsub_rn(sc0, mx));
+    const float e1 = n == 2 ? qtts_expf(__fsub_rn(sc1, mx)) : 0.0f;
     const double sum = n == 2 ? (double) e0 + (double) e1 : (double) e0;
     const float inv = (float)(1.0 / sum);
     const float p0 = __fmul_rn(e0, inv), p1 = __fmul_rn(e1, inv);
+    const float va[4] = {v0.x, v0.y, v0.z, v0.w}, vb[4] = {v1.x, v1.y, v1.z, v1.w};
     float o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const float part0 = fmaf(p0, (&vv[0].x)[k], 0.0f);
-        const float part1 = n == 2 ? fmaf(p1, (&vv[1 < n ? 1 : 0].x)[k], 0.0f) : 0.0f;
+        const float part0 = fmaf(p0, va[k], 0.0f);
+        const float part1 = n == 2 ? fmaf(p1, vb[k], 0.0f) : 0.0f;
         float s = __fadd_rn(0.0f, part0);
         s = __fadd_rn(s, part1);
         o[k] = __fadd_rn(s, 0.0f);   // the position groups with no key
@@ -298,16 +314,20 @@ __device__ __forceinline__ void df_drain(uint64_t * mbar, unsigned pending, unsi
         if (pending >> b & 1u) mbar_wait(mbar + b, phase >> b & 1u);
 }
 
-// ---- per-CTA state of the kernel (shared memory).  The stages below are
-// separate (non-inlined) functions so each gets its own register allocation.
+// ---- per-CTA state of the kernel (shared memory).  Everything the stages
+// keep per thread lives in registers: with ~215 KB of shared memory per SM the
+// L1 cache left for local memory is small, and a spilled register or a stack
+// frame would cost an L2 round trip per access.
 __shared__ DfArgs df_P;                  // the launch arguments
-__shared__ DfOp df_desc[2];              // this op's descriptor and the next one's
+__shared__ DfOp df_desc[3];              // ring: this op's descriptor, the next one's, and the one
+                                         // before, which the issuing warp may still be reading
 __shared__ __align__(8) uint64_t df_mbar[2];
 __shared__ DevState df_st;               // this CTA's frame state (presence set, codes)
 __shared__ SampleParams df_sp;
 __shared__ float df_res[2][8];           // this CTA's rows of the residual stream
 __shared__ const __half * df_tab[QTTS_MAX_CB];
 __shared__ int df_bad;
+__shared__ GemvArgs df_gemv;             // this op's GEMV arguments (built by thread 0)
 extern __shared__ __align__(128) uint8_t df_smem[];
 
 __device__ __forceinline__ uint8_t * df_work() { return df_smem + 2 * (size_t) df_P.wbuf_bytes; }
@@ -315,7 +335,7 @@ __device__ __forceinline__ FusedAttn * df_att() { return reinterpret_cast<FusedA
 __device__ __forceinline__ float * df_hid() { return reinterpret_cast<float *>(df_att() + df_P.n_att); }
 
 // The op's activation rows from a tagged buffer.
-__device__ __noinline__ bool df_stage_poll(const DfOp & op, int f, float * xs) {
+__device__ __forceinline__ bool df_stage_poll(const DfOp & op, int f, float * xs) {
     const int cols = op.A.cols;
     return df_poll_rows(df_in(df_P, op, f) + (size_t) op.in_row * cols, cols, op.nv, df_in_tag(df_P, op, f), xs,
                         df_P.err);
@@ -324,7 +344,7 @@ __device__ __noinline__ bool df_stage_poll(const DfOp & op, int f, float * xs) {
 // Sampler prologue: sample codebook op.cb (every CTA, the same decision), then
 // the pass's input rows into xs and this CTA's residual rows.  Returns 1 when
 // codebook 0 sampled EOS (the launch ends), -1 when an input did not arrive.
-__device__ __noinline__ int df_stage_sample(const DfOp & op, int f, int frame, float * xs) {
+__device__ __forceinline__ int df_stage_sample(const DfOp & op, int f, int frame, float * xs) {
     const DfArgs & P = df_P;
     const int tid = threadIdx.x, nt = blockDim.x, cta = blockIdx.x;
     const int cb = op.cb, V = cb == 0 ? P.V0 : P.V1, H = P.H;
@@ -410,7 +430,7 @@ __device__ __noinline__ int df_stage_sample(const DfOp & op, int f, int frame, f
 // Code-predictor attention into the O-projection's input rows (xs, QD columns):
 // steps one warp per query head, the 2-row prefill one warp per (head, row).
 // CTA 0 appends the new K/V rows to the cache.  False when an input did not arrive.
-__device__ __noinline__ bool df_stage_cp_attn(const DfOp & op, int f, float * xs) {
+__device__ __forceinline__ bool df_stage_cp_attn(const DfOp & op, int f, float * xs, unsigned parity) {
     const DfArgs & P = df_P;
     const FusedAttn & a = df_att()[op.layer];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -420,18 +440,36 @@ __device__ __noinline__ bool df_stage_cp_attn(const DfOp & op, int f, float * xs
     const unsigned tag = df_in_tag(P, op, f);
     bool wrote = false, ok = true;
     if (op.pro == PRO_CPATTN) {
-        for (int hq = warp; hq < NH; hq += nw) {
+        // the cached K/V rows arrived with this op's weight slice (same mbarrier phase)
+        uint8_t * wb = df_smem + (size_t) op.slot * P.wbuf_bytes;
+        const bool landed = threadIdx.x != 0 || mbar_wait(df_mbar + op.slot, parity);
+        float4 in[3];
+        int hq = warp;
+        bool got = true;
+        if (hq < NH) {
             const int g = hq / G;
+            const unsigned long long * const srcs[3] = {q + (size_t) hq * QTTS_HD + lane * 4,
+                                                        q + QD + (size_t) g * QTTS_HD + lane * 4,
+                                                        q + QD + KD + (size_t) g * QTTS_HD + lane * 4};
+            got = __all_sync(0xffffffffu, df_poll_quads<3>(srcs, 3, tag, in, P.err));
+        }
+        if (__syncthreads_or(!landed || !got)) return false;
+        for (; hq < NH; hq += nw) {
+            const int g = hq / G;
+            if (hq != warp) {   // more heads than warps: poll this head's rows now
+                const unsigned long long * const srcs[3] = {q + (size_t) hq * QTTS_HD + lane * 4,
+                                                            q + QD + (size_t) g * QTTS_HD + lane * 4,
+                                                            q + QD + KD + (size_t) g * QTTS_HD + lane * 4};
+                if (!__all_sync(0xffffffffu, df_poll_quads<3>(srcs, 3, tag, in, P.err))) { ok = false; break; }
+            }
             CpStepRegs R;
-            cp_step_load(a, hq, op.n_past, R);
-            const unsigned long long * srcs[3] = {q + (size_t) hq * QTTS_HD + lane * 4,
-                                                  q + QD + (size_t) g * QTTS_HD + lane * 4,
-                                                  q + QD + KD + (size_t) g * QTTS_HD + lane * 4};
-            float4 in[3];
-            // a lane that timed out makes the whole warp give up (the body shuffles over all lanes)
-            if (!__all_sync(0xffffffffu, df_poll_quads<3>(srcs, 3, tag, in, P.err))) { ok = false; break; }
+            const float2 * rp = a.rope + (size_t) op.n_past * (QTTS_HD / 2);
+            head_params(a.q_norm, rp, lane, R.gq, R.cs);
+            head_params(a.k_norm, rp, lane, R.gk, R.cs);
+            const CpKvSmem kv{reinterpret_cast<const __half *>(wb + op.kv_off),
+                              reinterpret_cast<const __half *>(wb + op.kv_off + op.kv_bytes), g, a.n_kv_heads};
             const bool w = blockIdx.x == 0 && hq % G == 0;
-            const float4 o = cp_step_compute(a, hq, op.n_past, R, in[0], in[1], in[2], w);
+            const float4 o = cp_step_compute_kv(a, hq, op.n_past, R, kv, in[0], in[1], in[2], w);
             wrote |= w;
             *reinterpret_cast<float4 *>(xs + xpos(hq * QTTS_HD + lane * 4, QD)) = o;
         }
@@ -439,16 +477,15 @@ __device__ __noinline__ bool df_stage_cp_attn(const DfOp & op, int f, float * xs
         const int QKVD = QD + 2 * KD;
         for (int u = warp; u < 2 * NH; u += nw) {
             const int hq = u % NH, i = u / NH, g = hq / G;
-            const unsigned long long * srcs[5] = {q + (size_t) i * QKVD + (size_t) hq * QTTS_HD + lane * 4,
-                                                  q + QD + (size_t) g * QTTS_HD + lane * 4,
-                                                  q + QD + KD + (size_t) g * QTTS_HD + lane * 4,
-                                                  q + QKVD + QD + (size_t) g * QTTS_HD + lane * 4,
-                                                  q + QKVD + QD + KD + (size_t) g * QTTS_HD + lane * 4};
+            const unsigned long long * const srcs[5] = {q + (size_t) i * QKVD + (size_t) hq * QTTS_HD + lane * 4,
+                                                        q + QD + (size_t) g * QTTS_HD + lane * 4,
+                                                        q + QD + KD + (size_t) g * QTTS_HD + lane * 4,
+                                                        q + QKVD + QD + (size_t) g * QTTS_HD + lane * 4,
+                                                        q + QKVD + QD + KD + (size_t) g * QTTS_HD + lane * 4};
             float4 in[5] = {};
             if (!__all_sync(0xffffffffu, df_poll_quads<5>(srcs, i == 0 ? 3 : 5, tag, in, P.err))) { ok = false; break; }
-            const float4 kv[2] = {in[1], in[3]}, vv[2] = {in[2], in[4]};
             const bool w = blockIdx.x == 0 && hq % G == 0;
-            const float4 o = df_cp_prefill_unit(a, hq, i, op.n_past, in[0], kv, vv, w);
+            const float4 o = df_cp_prefill_unit(a, hq, i, op.n_past, in[0], in[1], in[2], in[3], in[4], w);
             wrote |= w;
             *reinterpret_cast<float4 *>(xs + i * QD + xpos(hq * QTTS_HD + lane * 4, QD)) = o;
         }
@@ -460,12 +497,13 @@ __device__ __noinline__ bool df_stage_cp_attn(const DfOp & op, int f, float * xs
 // Talker attention, one query head per CTA (CTAs 0 .. n_heads - 1): the head's q
 // and its group's k / v into a full-row staging area, then the fused unit with a
 // tagged output.  Returns false when an input did not arrive.
-__device__ __noinline__ bool df_stage_talker_attn(const DfOp & op, int f, int k, int n_past, int frame) {
+__device__ __forceinline__ bool df_stage_talker_attn(const DfOp & op, int f, int k, int n_past, int frame) {
     const DfArgs & P = df_P;
     const FusedAttn & a0 = df_att()[op.layer];
     const int NH = a0.n_heads, G = NH / a0.n_kv_heads;
     const int QD = NH * QTTS_HD, KD = a0.n_kv_heads * QTTS_HD;
     const int hq = blockIdx.x, g = hq / G;
+    __syncthreads();   // everyone has read the entry's sizes before thread 0 updates it
     uint8_t * work = df_work();
     float * stage = reinterpret_cast<float *>(work);
     const unsigned long long * q = df_in(P, op, f);
@@ -480,11 +518,15 @@ __device__ __noinline__ bool df_stage_talker_attn(const DfOp & op, int f, int k,
                                         },
                                         P.err);
     fence_acq_rel_gpu();   // the cached K/V rows other CTAs appended are read after this
+    // this CTA's own copy of the table entry takes the staging area and the tagged output
+    // (a local copy of the struct would live in local memory)
+    FusedAttn & a = df_att()[op.layer];
+    if (threadIdx.x == 0) {
+        a.qkv = stage;
+        a.fout = df_slot(P, op.out_buf, f, op.out_wr);
+        a.ftag = df_tag(P, f, k);
+    }
     if (__syncthreads_or(!ok)) return false;
-    FusedAttn a = a0;
-    a.qkv = stage;
-    a.fout = df_slot(P, op.out_buf, f, op.out_wr);
-    a.ftag = df_tag(P, f, k);
     fused_attn_body(a, hq, work + ((size_t)(QD + 2 * KD) * 4 + 127) / 128 * 128, n_past, frame);
     return true;
 }
@@ -493,7 +535,7 @@ __device__ __noinline__ bool df_stage_talker_attn(const DfOp & op, int f, int k,
 // tagged outputs (the talker head also writes the plain logits, the hidden
 // state in every CTA's df_hid and, in CTA 0, the plain hidden state).
 template <int NV>
-__device__ __noinline__ bool df_stage_gemv(const DfOp & op, int f, int k, unsigned parity,
+__device__ __forceinline__ bool df_stage_gemv(const DfOp & op, int f, int k, unsigned parity,
                                            unsigned long long * ready_stamp) {
     const DfArgs & P = df_P;
     const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x, nt = blockDim.x;
@@ -503,135 +545,170 @@ __device__ __noinline__ bool df_stage_gemv(const DfOp & op, int f, int k, unsign
         const int H = P.H, r0 = cta * rpc, nrow = max(0, min(H, r0 + rpc) - r0);
         const int rstride = (rpc + 3) & ~3;
         for (int t = tid; t < NV * nrow; t += nt) W.rs[(t / nrow) * rstride + t % nrow] = df_res[t / nrow][t % nrow];
-        __syncthreads();
     }
-    GemvArgs g{};
-    g.A = op.A;
-    g.B = op.B;
-    g.nv = NV;
-    g.norm_g = op.norm_g;
-    g.eps = P.eps;
-    g.act = op.act;
-    g.epi = op.epi;
-    g.xn_out = op.head == 1 ? P.hidden : nullptr;   // CTA 0: the plain talker hidden state
-    g.ldxn = P.H;
+    GemvArgs & g = df_gemv;   // in shared memory: a local copy of the struct would live in local memory
+    if (tid == 0) {
+        g = GemvArgs{};
+        g.A = op.A;
+        g.B = op.B;
+        g.nv = NV;
+        g.norm_g = op.norm_g;
+        g.eps = P.eps;
+        g.act = op.act;
+        g.epi = op.epi;
+        g.xn_out = op.head == 1 ? P.hidden : nullptr;   // CTA 0: the plain talker hidden state
+        g.ldxn = P.H;
+    }
+    __syncthreads();
     const DfStore store{df_slot(P, op.out_buf, f, op.out_wr), op.A.rows, df_tag(P, f, k),
-                        op.head == 1 ? P.logits_out : nullptr, op.epi == EPI_RESID ? df_res : nullptr};
+                        op.head == 1 ? P.logits_out : nullptr, op.epi == EPI_RESID ? df_res : nullptr,
+                        ready_stamp ? ready_stamp + 1 : nullptr};
     const int b = op.slot;
     return gemv_compute<NV>(g, cta, ncta, df_smem + (size_t) b * P.wbuf_bytes, df_work(), df_mbar + b, parity, store,
                             op.head == 1 ? df_hid() : nullptr, ready_stamp);
 }
 
+__shared__ int df_pos0, df_frame0;     // frame state at launch
+
+// Trace stamps of op k in frame f (nullptr when tracing is off).  Recomputed at
+// each use so no register holds it across a stage.
+__device__ __forceinline__ unsigned long long * df_tr(int f, int k) {
+    return df_P.trace ? df_P.trace + ((size_t) f * df_P.n_ops + k) * DF_TRACE : nullptr;
+}
+__device__ __forceinline__ void df_stamp(int f, int k, int slot) {
+    unsigned long long * tr = df_tr(f, k);
+    if (tr && blockIdx.x == 0 && threadIdx.x == 0) tr[slot] = df_now();
+}
+
+// Loop state is kept to a few registers (frame, op, weight-buffer phases, two
+// flags): every stage below gets the rest of the 128 a thread has.
 __global__ void __launch_bounds__(DF_THREADS, 1) k_frame_dataflow(DfArgs Pk) {
-    const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x, nt = blockDim.x;
     constexpr int NW = (int)(sizeof(DfOp) / 8);
     static_assert(sizeof(DfOp) % 8 == 0 && NW <= DF_THREADS, "descriptor copy");
     static_assert(sizeof(FusedAttn) % 8 == 0 && sizeof(DfArgs) % 8 == 0, "table copies");
     {
         const unsigned long long * src = reinterpret_cast<const unsigned long long *>(&Pk);
-        for (int w = tid; w < (int)(sizeof(DfArgs) / 8); w += nt) reinterpret_cast<unsigned long long *>(&df_P)[w] = src[w];
+        for (int w = threadIdx.x; w < (int)(sizeof(DfArgs) / 8); w += blockDim.x)
+            reinterpret_cast<unsigned long long *>(&df_P)[w] = src[w];
     }
-    if (tid == 0) {
+    if (threadIdx.x == 0) {
         mbar_init(&df_mbar[0], 1);
         mbar_init(&df_mbar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         df_sp = *Pk.sp;
-        if (cta != 0) df_sp.record_logits = 0;   // CTA 0 records the debug logits
+        if (blockIdx.x != 0) df_sp.record_logits = 0;   // CTA 0 records the debug logits
         df_bad = 0;
     }
-    if (tid < NW) reinterpret_cast<unsigned long long *>(&df_desc[0])[tid] = reinterpret_cast<const unsigned long long *>(Pk.ops)[tid];
+    if (threadIdx.x < NW)
+        reinterpret_cast<unsigned long long *>(&df_desc[0])[threadIdx.x] = reinterpret_cast<const unsigned long long *>(Pk.ops)[threadIdx.x];
     __syncthreads();
-    const DfArgs & P = df_P;
-    FusedAttn * att = df_att();
-    float * hid = df_hid();
     {
+        const DfArgs & P = df_P;
+        const int tid = threadIdx.x, nt = blockDim.x;
         const int n8 = P.n_att * (int)(sizeof(FusedAttn) / 8);
         for (int w = tid; w < n8; w += nt)
-            reinterpret_cast<unsigned long long *>(att)[w] = reinterpret_cast<const unsigned long long *>(P.att)[w];
-    }
-    for (int i = tid; i < (int)(sizeof(DevState) / 4); i += nt)
-        reinterpret_cast<int *>(&df_st)[i] = reinterpret_cast<const volatile int *>(P.st)[i];
-    for (int c = tid; c < P.H; c += nt) hid[c] = __ldcg(P.hidden + c);
-    if (tid >= 1 && tid < P.n_cb) df_tab[tid] = P.cp_embd[tid - 1];
-    __syncthreads();
-    if (tid == 0) {
-        for (int k = 0; k < P.n_pf0; ++k) {
-            df_prefetch_slice(P.ops[P.pf0[k]].A, cta, ncta);
-            df_prefetch_slice(P.ops[P.pf0[k]].B, cta, ncta);
+            reinterpret_cast<unsigned long long *>(df_att())[w] = reinterpret_cast<const unsigned long long *>(P.att)[w];
+        for (int i = tid; i < (int)(sizeof(DevState) / 4); i += nt)
+            reinterpret_cast<int *>(&df_st)[i] = reinterpret_cast<const volatile int *>(P.st)[i];
+        for (int c = tid; c < P.H; c += nt) df_hid()[c] = __ldcg(P.hidden + c);
+        if (tid >= 1 && tid < P.n_cb) df_tab[tid] = P.cp_embd[tid - 1];
+        __syncthreads();
+        if (tid == 0) {
+            df_pos0 = df_st.pos;
+            df_frame0 = df_st.frame;
+            for (int k = 0; k < P.n_pf0; ++k) {
+                df_prefetch_slice(P.ops[P.pf0[k]].A, blockIdx.x, gridDim.x);
+                df_prefetch_slice(P.ops[P.pf0[k]].B, blockIdx.x, gridDim.x);
+            }
+            for (int b = 0; b < 2; ++b) {
+                const DfOp & g = P.ops[P.first[b]];
+                issue_gemv_slice(g.A, g.B, g.norm_g, df_smem + (size_t) g.slot * P.wbuf_bytes, df_mbar + g.slot,
+                                 blockIdx.x, gridDim.x);
+            }
         }
-        for (int b = 0; b < 2; ++b) {
-            const DfOp & g = P.ops[P.first[b]];
-            issue_gemv_slice(g.A, g.B, g.norm_g, df_smem + (size_t) g.slot * P.wbuf_bytes, df_mbar + g.slot, cta, ncta);
-        }
+        __syncthreads();
     }
     unsigned phase = 0u, pending = 3u;
-    const int pos0 = df_st.pos, frame0 = df_st.frame;
-    const int QD = att[0].n_heads * QTTS_HD;
     bool stop = false, failed = false;
 
-    for (int f = 0; f < P.n_frames && !stop && !failed; ++f) {
-        const int frame = frame0 + f;
-        for (int k = 0; k < P.n_ops; ++k) {
-            const DfOp & op = df_desc[k & 1];
-            unsigned long long * tr = P.trace ? P.trace + ((size_t) f * P.n_ops + k) * DF_TRACE : nullptr;
-            if (tr && cta == 0 && tid == 0) tr[0] = df_now();
-            const int nx = k + 1 < P.n_ops ? k + 1 : 0;
-            const unsigned long long nword = tid < NW ? reinterpret_cast<const unsigned long long *>(P.ops + nx)[tid] : 0ull;
+    unsigned seq = 0;   // ops run so far in this launch (descriptor ring position)
+    for (int f = 0; f < df_P.n_frames && !stop && !failed; ++f) {
+        for (int k = 0; k < df_P.n_ops; ++k, ++seq) {
+            const DfOp & op = df_desc[seq % 3];
+            df_stamp(f, k, 0);
+            // The next op's descriptor goes to the slot of op k - 2: every warp, the
+            // issuing warp included, finished with it before op k - 1's end barrier.
+            if (threadIdx.x < NW) {
+                const int nx = k + 1 < df_P.n_ops ? k + 1 : 0;
+                reinterpret_cast<unsigned long long *>(&df_desc[(seq + 1) % 3])[threadIdx.x] =
+                    reinterpret_cast<const unsigned long long *>(df_P.ops + nx)[threadIdx.x];
+            }
             if (op.type == DF_GEMV) {
                 float * xs = reinterpret_cast<float *>(df_work());
                 int rc = 0;
                 if (op.pro == PRO_POLL) rc = df_stage_poll(op, f, xs) ? 0 : -1;
-                else if (op.pro == PRO_CPATTN || op.pro == PRO_CPATTN2) rc = df_stage_cp_attn(op, f, xs) ? 0 : -1;
-                else rc = df_stage_sample(op, f, frame, xs);
+                else if (op.pro == PRO_CPATTN || op.pro == PRO_CPATTN2)
+                    rc = df_stage_cp_attn(op, f, xs, phase >> op.slot & 1u) ? 0 : -1;
+                else rc = df_stage_sample(op, f, df_frame0 + f, xs);
                 if (__syncthreads_or(rc < 0)) {
                     failed = true;
                 } else if (rc == 1) {
                     stop = true;
                 } else {
-                    if (tr && tid == 0) {
+                    unsigned long long * tr = df_tr(f, k);
+                    if (tr && threadIdx.x == 0) {
                         const unsigned long long t = df_now();
-                        if (cta == 0) tr[1] = t;
+                        if (blockIdx.x == 0) tr[1] = t;
                         atomicMax(tr + 2, t);
                     }
                     const int b = op.slot;
-                    unsigned long long * rs = tr && cta == 0 ? tr + 3 : nullptr;
+                    unsigned long long * rs = tr && blockIdx.x == 0 ? tr + 3 : nullptr;
                     const bool gok = op.nv == 1 ? df_stage_gemv<1>(op, f, k, phase >> b & 1u, rs)
                                                 : df_stage_gemv<2>(op, f, k, phase >> b & 1u, rs);
                     if (!gok) failed = true;
                     phase ^= 1u << b;
                     pending &= ~(1u << b);
                 }
-            } else if (cta < att[op.layer].n_heads) {   // DF_TATTN: CTAs 0 .. n_heads - 1
-                if (!df_stage_talker_attn(op, f, k, pos0 + f, frame)) failed = true;
+            } else if ((int) blockIdx.x < df_att()[op.layer].n_heads) {   // DF_TATTN: CTAs 0 .. n_heads - 1
+                if (!df_stage_talker_attn(op, f, k, df_pos0 + f, df_frame0 + f)) failed = true;
             }
             if (failed) {
-                if (tid == 0) atomicExch(P.err, 2);
+                if (threadIdx.x == 0) atomicExch(df_P.err, 2);
                 break;
             }
             if (stop) break;
-            if (tr && cta == 0 && tid == 0) tr[4] = df_now();
-            __syncthreads();   // everyone is done with df_desc[k & 1] and with the op's weight buffer
-            if (tid < NW) reinterpret_cast<unsigned long long *>(&df_desc[(k + 1) & 1])[tid] = nword;
-            if (op.type == DF_GEMV && tid == 0) {
+            df_stamp(f, k, 6);
+            __syncthreads();   // everyone is done with op k's descriptor and weight buffer
+            df_stamp(f, k, 8);
+            // The last warp issues the next copies into op k's buffer and then joins op k + 1;
+            // the others start op k + 1 at once (its descriptor was stored before this barrier,
+            // and it uses the other buffer and mbarrier).
+            if (op.type == DF_GEMV && threadIdx.x == blockDim.x - 32) {
                 if (op.iA.w) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    issue_gemv_slice(op.iA, op.iB, op.iG, df_smem + (size_t) op.slot * P.wbuf_bytes,
-                                     df_mbar + op.slot, cta, ncta);
+                    uint8_t * wb = df_smem + (size_t) op.slot * df_P.wbuf_bytes;
+                    issue_gemv_slice(op.iA, op.iB, op.iG, wb, df_mbar + op.slot, blockIdx.x, gridDim.x,
+                                     op.iK ? 2u * (unsigned) op.i_kv_bytes : 0u);
+                    if (op.iK) {   // the next op's code-predictor K/V rows, behind its slice
+                        bulk_g2s(wb + op.i_kv_off, op.iK, (unsigned) op.i_kv_bytes, df_mbar + op.slot);
+                        bulk_g2s(wb + op.i_kv_off + op.i_kv_bytes, op.iV, (unsigned) op.i_kv_bytes, df_mbar + op.slot);
+                    }
                 }
-                df_prefetch_slice(op.pA, cta, ncta);
-                df_prefetch_slice(op.pB, cta, ncta);
+                df_prefetch_slice(op.pA, blockIdx.x, gridDim.x);
+                df_prefetch_slice(op.pB, blockIdx.x, gridDim.x);
+                unsigned long long * tr = df_tr(f, k);
+                if (tr && blockIdx.x == 0) tr[7] = df_now();
             }
             if (op.type == DF_GEMV && op.iA.w) pending |= 1u << op.slot;
-            __syncthreads();
         }
         if (failed || stop) break;
-        if (cta == 0 && tid == 0) {
-            P.st->pos = pos0 + f + 1;
-            P.st->frame = frame + 1;
-            P.st->n_out += 1;
+        if (blockIdx.x == 0 && threadIdx.x == 0) {
+            df_P.st->pos = df_pos0 + f + 1;
+            df_P.st->frame = df_frame0 + f + 1;
+            df_P.st->n_out += 1;
         }
     }
-    (void) QD;
+    __syncthreads();   // the issuing warp's last copies are posted before thread 0 waits for them
     df_drain(df_mbar, pending, phase);
 }
 

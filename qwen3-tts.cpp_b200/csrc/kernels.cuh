@@ -71,25 +71,26 @@ __host__ __device__ inline size_t gemv_work_bytes(int type, int cols, int nv, in
 // One thread: copy the CTA's slice of (A, B) and the norm gain into `buf`,
 // completing on mbarrier m (expect_tx covers every byte, so the phase completes
 // even when this CTA owns no rows).
+// extra_bytes: further bulk copies the caller issues on the same mbarrier phase.
 __device__ __forceinline__ void issue_gemv_slice(const DMat & A, const DMat & B, const float * gain, uint8_t * buf,
-                                                 uint64_t * m, int cta, int ncta) {
+                                                 uint64_t * m, int cta, int ncta, unsigned extra_bytes = 0) {
     const int rpc = gemv_rpc(A.rows, ncta);
     const int r0 = cta * rpc, r1 = min(A.rows, r0 + rpc);
     const int nrow = r1 > r0 ? r1 - r0 : 0;
     const bool dual = B.w != nullptr;
     const SliceLayout L = slice_layout(A, dual, gain != nullptr, nrow);
-    mbar_expect_tx(m, nrow ? (unsigned) L.total : 0u);
+    mbar_expect_tx(m, (nrow ? (unsigned) L.total : 0u) + extra_bytes);
     if (!nrow) return;
     const size_t es = A.type == W_Q8_0 ? 1 : 2;
-    const DMat * mats[2] = {&A, &B};
     for (int k = 0; k < (dual ? 2 : 1); ++k) {
-        const char * src = static_cast<const char *>(mats[k]->w) + (size_t) r0 * A.cols * es;
+        const DMat & M = k ? B : A;   // (no array of pointers: it would live in local memory)
+        const char * src = static_cast<const char *>(M.w) + (size_t) r0 * A.cols * es;
         for (size_t o = 0; o < L.bA; o += 32768) {
             const unsigned n = (unsigned)(L.bA - o < 32768 ? L.bA - o : 32768);
             bulk_g2s(buf + k * L.bA + o, src + o, n, m);
         }
         if (L.bS)
-            bulk_g2s(buf + (dual ? 2 : 1) * L.bA + k * L.bS, mats[k]->d + (size_t) r0 * (A.cols / 32), (unsigned) L.bS, m);
+            bulk_g2s(buf + (dual ? 2 : 1) * L.bA + k * L.bS, M.d + (size_t) r0 * (A.cols / 32), (unsigned) L.bS, m);
     }
     if (gain) bulk_g2s(buf + L.gain_off, gain, (unsigned)(A.cols * 4), m);
 }
@@ -234,17 +235,26 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
     }
 
     if (!q8) {
+        // Rows rl and rl + nw of a warp share each activation load (the
+        // activation reads, not the weights, dominate shared-memory traffic);
+        // every row keeps its own accumulation chain.
         const uint8_t * wa = wsm;
         const uint8_t * wb = wsm + L.bA;
-        for (int rl = warp; rl < nrow; rl += nw) {
-            float acc[NV], accb[NV];
+        for (int rl = warp; rl < nrow; rl += 2 * nw) {
+            const int rl2 = rl + nw;
+            const bool two = rl2 < nrow;
+            float acc[NV], accb[NV], acc2[NV], accb2[NV];
 #pragma unroll
-            for (int v = 0; v < NV; ++v) acc[v] = accb[v] = 0.0f;
+            for (int v = 0; v < NV; ++v) acc[v] = accb[v] = acc2[v] = accb2[v] = 0.0f;
             const uint4 * ra = reinterpret_cast<const uint4 *>(wa + (size_t) rl * cols * 2);
             const uint4 * rb = reinterpret_cast<const uint4 *>(wb + (size_t) rl * cols * 2);
+            const uint4 * ra2 = reinterpret_cast<const uint4 *>(wa + (size_t)(two ? rl2 : rl) * cols * 2);
+            const uint4 * rb2 = reinterpret_cast<const uint4 *>(wb + (size_t)(two ? rl2 : rl) * cols * 2);
             for (int c = lane; c < h8; c += 32) {
                 const uint4 w = ra[c];
                 const uint4 w2 = dual ? rb[c] : make_uint4(0, 0, 0, 0);
+                const uint4 u = two ? ra2[c] : make_uint4(0, 0, 0, 0);
+                const uint4 u2 = (two && dual) ? rb2[c] : make_uint4(0, 0, 0, 0);
 #pragma unroll
                 for (int v = 0; v < NV; ++v) {
                     if (v >= nv) continue;
@@ -253,6 +263,10 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
                     const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                     acc[v] = dot8(w, xv, acc[v]);
                     if (dual) accb[v] = dot8(w2, xv, accb[v]);
+                    if (two) {
+                        acc2[v] = dot8(u, xv, acc2[v]);
+                        if (dual) accb2[v] = dot8(u2, xv, accb2[v]);
+                    }
                 }
             }
 #pragma unroll
@@ -261,6 +275,11 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
                 const float s1 = warp_sum(acc[v]);
                 const float s2 = dual ? warp_sum(accb[v]) : 0.0f;
                 if (lane == 0) store(r0 + rl, rl, v, gemv_epi(a, v, s1, s2, rs, rl, rstride));
+                if (two) {
+                    const float t1 = warp_sum(acc2[v]);
+                    const float t2 = dual ? warp_sum(accb2[v]) : 0.0f;
+                    if (lane == 0) store(r0 + rl2, rl2, v, gemv_epi(a, v, t1, t2, rs, rl2, rstride));
+                }
             }
         }
         return true;
@@ -693,7 +712,7 @@ __host__ __device__ inline size_t fused_attn_smem(int max_keys, int M) {
 }
 
 // n_past: position of query row 0; frame: dump row.
-__device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * smem, const int n_past,
+__device__ __forceinline__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * smem, const int n_past,
                                 const int frame) {
     const int NKV = a.n_kv_heads, G = a.n_heads / a.n_kv_heads;
     const int hq = unit % a.n_heads, i = unit / a.n_heads, g = hq / G;
@@ -887,7 +906,7 @@ __device__ void fused_attn_body(const FusedAttn & a, const int unit, uint8_t * s
 constexpr int CPA_MAX_KEYS = 16;
 
 // Registers of one step-attention warp loaded before the q|k|v row is needed:
-// norm gains, RoPE row and the cached K halves / V quads.
+// norm gains, RoPE row and the cached K halves (and, when preloaded, V quads).
 struct CpStepRegs {
     float gq[4], gk[4];
     float2 cs[4];
@@ -897,7 +916,13 @@ struct CpStepRegs {
 
 // Cached K/V are read through L2 (ld.global.cg): within one launch of the
 // dataflow frame kernel another CTA rewrites these positions every frame.
-__device__ __forceinline__ void cp_step_load(const FusedAttn & a, const int hq, const int n_past, CpStepRegs & R) {
+__device__ __forceinline__ uint2 cp_step_ld_v(const FusedAttn & a, const int hq, const int j) {
+    const int NKV = a.n_kv_heads, g = hq / (a.n_heads / NKV);
+    const __half * vb = a.vc + (size_t) g * QTTS_HD + (threadIdx.x & 31) * 4;
+    return __ldcg(reinterpret_cast<const uint2 *>(vb + (size_t) j * NKV * QTTS_HD));
+}
+__device__ __forceinline__ void cp_step_load(const FusedAttn & a, const int hq, const int n_past, CpStepRegs & R,
+                                             const bool with_v = true) {
     const int lane = threadIdx.x & 31;
     const int NKV = a.n_kv_heads, G = a.n_heads / NKV, g = hq / G;
     const size_t pstride = (size_t) NKV * QTTS_HD;
@@ -908,19 +933,74 @@ __device__ __forceinline__ void cp_step_load(const FusedAttn & a, const int hq, 
     const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + (size_t) jk * pstride + (size_t) g * QTTS_HD + 64 * h);
 #pragma unroll
     for (int c = 0; c < 8; ++c) R.kr[c] = jk < n_past ? __ldcg(kp + c) : make_uint4(0, 0, 0, 0);
-    const __half * vb = a.vc + (size_t) g * QTTS_HD + lane * 4;
+    if (with_v) {
 #pragma unroll
-    for (int j = 0; j < CPA_MAX_KEYS; ++j)
-        R.vr[j] = j < n_past ? __ldcg(reinterpret_cast<const uint2 *>(vb + (size_t) j * pstride)) : make_uint2(0, 0);
+        for (int j = 0; j < CPA_MAX_KEYS; ++j) R.vr[j] = j < n_past ? cp_step_ld_v(a, hq, j) : make_uint2(0, 0);
+    }
 }
 
 // The step attention of query head hq from its q row quad q4 and its group's new
 // k / v quads (lane l: dims 4l .. 4l + 3).  kv_write: this warp appends the
-// group's new K/V row to the cache (the group's first head).  Returns the output
-// quad of dims 4 lane .. 4 lane + 3.
+// group's new K/V row to the cache (the group's first head).  late_v: the cached
+// V quads are loaded here, after the scores (no registers held for them while
+// K is live); otherwise they come from R.  Returns the output quad of dims
+// 4 lane .. 4 lane + 3.
+// Cached K/V from registers (CpStepRegs, filled by cp_step_load).
+struct CpKvRegs {
+    static constexpr bool rolled = false;
+    CpStepRegs & R;
+    __device__ __forceinline__ uint4 k(int c) const { return R.kr[c]; }
+    __device__ __forceinline__ uint2 v(int j) const { return R.vr[j]; }
+    __device__ __forceinline__ void after_scores() const {}
+};
+// K from registers, V quads loaded from L2 once the score loop is done (no
+// registers held for them while K is live).
+struct CpKvLate {
+    static constexpr bool rolled = false;
+    CpStepRegs & R;
+    const FusedAttn & a;
+    int hq, n_past;
+    __device__ __forceinline__ uint4 k(int c) const { return R.kr[c]; }
+    __device__ __forceinline__ uint2 v(int j) const { return R.vr[j]; }
+    __device__ __forceinline__ void after_scores() const {
+        asm volatile("" ::: "memory");   // the V loads stay below the score loop
+#pragma unroll
+        for (int j = 0; j < CPA_MAX_KEYS; ++j) R.vr[j] = j < n_past ? cp_step_ld_v(a, hq, j) : make_uint2(0, 0);
+    }
+};
+// Cached K/V rows [pos][kv_head][128] F16 of positions 0 .. n_past - 1 staged in
+// shared memory: lane 2 jk + h reads dims [64h, 64h + 64) of key jk, lane l the
+// quad 4l .. 4l + 3 of V row j.
+struct CpKvSmem {
+    static constexpr bool rolled = true;
+    const __half * K, * V;
+    int g, nkv;
+    __device__ __forceinline__ uint4 k(int c) const {
+        const int lane = threadIdx.x & 31;
+        return reinterpret_cast<const uint4 *>(K + ((size_t)(lane >> 1) * nkv + g) * QTTS_HD + 64 * (lane & 1))[c];
+    }
+    __device__ __forceinline__ uint2 v(int j) const {
+        return *reinterpret_cast<const uint2 *>(V + ((size_t) j * nkv + g) * QTTS_HD + (threadIdx.x & 31) * 4);
+    }
+    __device__ __forceinline__ void after_scores() const {}
+};
+
+template <class KV>
+__device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const int hq, const int n_past,
+                                                     const CpStepRegs & R, const KV & kv, const float4 q4,
+                                                     const float4 k4, const float4 v4, const bool kv_write);
+
 __device__ __forceinline__ float4 cp_step_compute(const FusedAttn & a, const int hq, const int n_past,
-                                                  const CpStepRegs & R, const float4 q4, const float4 k4,
-                                                  const float4 v4, const bool kv_write) {
+                                                  CpStepRegs & R, const float4 q4, const float4 k4,
+                                                  const float4 v4, const bool kv_write, const bool late_v = false) {
+    if (!late_v) return cp_step_compute_kv(a, hq, n_past, R, CpKvRegs{R}, q4, k4, v4, kv_write);
+    return cp_step_compute_kv(a, hq, n_past, R, CpKvLate{R, a, hq, n_past}, q4, k4, v4, kv_write);
+}
+
+template <class KV>
+__device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const int hq, const int n_past,
+                                                     const CpStepRegs & R, const KV & kv, const float4 q4,
+                                                     const float4 k4, const float4 v4, const bool kv_write) {
     const int lane = threadIdx.x & 31;
     const int NKV = a.n_kv_heads, g = hq / (a.n_heads / NKV);
     const size_t pstride = (size_t) NKV * QTTS_HD;
@@ -943,18 +1023,26 @@ __device__ __forceinline__ float4 cp_step_compute(const FusedAttn & a, const int
     }
     // score of key jk over dims [64h, 64h + 64): q and the new k come from lanes 16h .. 16h + 15
     float acc = 0.0f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const __half2 * hp = reinterpret_cast<const __half2 *>(&R.kr[c]);
+    auto chunk = [&](const int c) {   // dims 64h + 8c .. 64h + 8c + 7
+        const uint4 kc4 = jk < n_past ? kv.k(c) : make_uint4(0, 0, 0, 0);
+        const __half2 * hp = reinterpret_cast<const __half2 *>(&kc4);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            const int d = 8 * c + e, src = 16 * h + (d >> 2);     // lane holding dim 64h + d
+            const int src = 16 * h + 2 * c + (e >> 2);     // lane holding dim 64h + 8c + e
             const float qd = __shfl_sync(0xffffffffu, xq[e & 3], src);
             const float kd_new = __shfl_sync(0xffffffffu, kn[e & 3], src);
             const float kd = jk < n_past ? (e & 1 ? __high2float(hp[e >> 1]) : __low2float(hp[e >> 1])) : kd_new;
             acc = fmaf(kd, qd, acc);
         }
+    };
+    if constexpr (KV::rolled) {   // K in shared memory: a rolled loop holds fewer registers
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) chunk(c);
+    } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) chunk(c);
     }
+    kv.after_scores();
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     const int n = n_past + 1;
     const float s = jk < n ? __fmul_rn(acc, a.scale) : -INFINITY;
@@ -963,13 +1051,11 @@ __device__ __forceinline__ float4 cp_step_compute(const FusedAttn & a, const int
     const double sum = warp_sum_d(h ? 0.0 : (double) e);
     const float p = round_f16(__fmul_rn(e, (float)(1.0 / sum)));
     float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int j = 0; j < CPA_MAX_KEYS + 1; ++j) {
-        if (j >= n) break;
+    auto key = [&](const int j) {   // keys in order: P x V chained per dim
         const float pj = __shfl_sync(0xffffffffu, p, 2 * j);
         float v[4];
         if (j < n_past) {
-            const uint2 vq = R.vr[j < CPA_MAX_KEYS ? j : 0];
+            const uint2 vq = kv.v(j < CPA_MAX_KEYS ? j : 0);
             const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&vq.x));
             const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&vq.y));
             v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
@@ -979,6 +1065,16 @@ __device__ __forceinline__ float4 cp_step_compute(const FusedAttn & a, const int
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) o[k] = fmaf(pj, v[k], o[k]);
+    };
+    if constexpr (KV::rolled) {
+#pragma unroll 1
+        for (int j = 0; j < n; ++j) key(j);
+    } else {
+#pragma unroll
+        for (int j = 0; j < CPA_MAX_KEYS + 1; ++j) {
+            if (j >= n) break;
+            key(j);
+        }
     }
     return make_float4(o[0], o[1], o[2], o[3]);
 }
@@ -1047,7 +1143,7 @@ constexpr int SAMPLE_MAX_V = 4096;
 
 // k-th largest key among valid elements (radix select, 8 bits per pass).
 template <int PT>
-__device__ uint32_t block_kth_largest(const uint32_t * key, const bool * valid, int k) {
+__device__ __forceinline__ uint32_t block_kth_largest(const uint32_t (&key)[PT], const bool (&valid)[PT], int k) {
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_prefix, s_k;
     const int tid = threadIdx.x;
@@ -1178,10 +1274,16 @@ __device__ int sample_body_l(const Load & load, int V, int cb, const DevState * 
                                          (unsigned long long)(0xFFFFFFFFu - (uint32_t)(tid * PT + e));
             mine = k > mine ? k : mine;
         }
+        // warp maximum first: one shared atomic per warp instead of one per thread
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, mine, o);
+            mine = other > mine ? other : mine;
+        }
         __syncthreads();
         if (tid == 0) best = 0ull;
         __syncthreads();
-        atomicMax(&best, mine);
+        if ((tid & 31) == 0) atomicMax(&best, mine);
         __syncthreads();
         tok = best == 0ull ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
     } else {
@@ -1233,13 +1335,17 @@ __device__ int sample_body_l(const Load & load, int V, int cb, const DevState * 
                 if (cum > target && cand == 0x7fffffff) cand = tid * PT + e;
             }
         }
-        atomicMin(&pick, cand);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, o));
+        if ((tid & 31) == 0) atomicMin(&pick, cand);
         __syncthreads();
         if (pick == 0x7fffffff) {  // rounding pushed the target past the last bucket
             __syncthreads();
             if (tid == 0) pick = -1;
             __syncthreads();
-            atomicMax(&pick, lastpos);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) lastpos = max(lastpos, __shfl_xor_sync(0xffffffffu, lastpos, o));
+            if ((tid & 31) == 0) atomicMax(&pick, lastpos);
             __syncthreads();
         }
         tok = pick < 0 ? 0 : pick;

@@ -338,15 +338,18 @@ class Engine:
                                   for i in range(4)}}
 
     def frame_trace(self):
-        """(ops [n_ops] = type * 16 + prologue, stamps [frames * n_ops][4]) of the last
-        dataflow launch with QTTS_DF_TRACE=1 (ns, %globaltimer)."""
+        """(ops [n_ops] = type * 16 + prologue, stamps [frames * n_ops][10]) of the last
+        dataflow launch with QTTS_DF_TRACE=1 (ns, %globaltimer; CTA 0 unless noted):
+        start, input ready, latest input ready over the CTAs, weights ready, first
+        output row stored, last output row stored, op done, next copies issued, past
+        the first end-of-op barrier, past the second."""
         n = lib().qtts_frame_ops(self.h, None, 0)
         ops = np.zeros(max(n, 1), np.int32)
         lib().qtts_frame_ops(self.h, _p(ops, C.c_int32), n)
         m = lib().qtts_frame_trace(self.h, None, 0)
         tr = np.zeros(max(m, 1), np.uint64)
         lib().qtts_frame_trace(self.h, tr.ctypes.data_as(C.POINTER(C.c_uint64)), m)
-        return ops[:n], tr[:m].reshape(-1, 4)
+        return ops[:n], tr[:m].reshape(-1, 10)
 
     def run_frames(self, n: int, codes_out: np.ndarray | None = None) -> int:
         ptr = None if codes_out is None else _p(codes_out, C.c_int32)
