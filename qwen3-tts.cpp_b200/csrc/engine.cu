@@ -609,10 +609,7 @@ static bool gemv_shape(const DMat & A, bool dual, bool has_gain, int nvt, int n_
         if (smem <= QTTS_GEMV_SMEM_MAX) {
             *ncta_out = (A.rows + rpc - 1) / rpc;
             *slice_out = slice;
-            // at most two CTAs per SM, whatever the register count: a third resident
-            // CTA (of the next launch under programmatic dependent launch) measured
-            // slower (343 vs 384 frames/s), and 80 KB each leaves no room for it
-            *smem_out = std::max(smem, QTTS_GEMV_SMEM_2CTA);
+            *smem_out = smem;
             return true;
         }
         if (ncta >= A.rows) return false;

@@ -39,7 +39,6 @@ struct GemvArgs {
 };
 
 constexpr size_t QTTS_GEMV_SMEM_MAX = 200 * 1024;   // dynamic shared memory of a stand-alone k_gemv
-constexpr size_t QTTS_GEMV_SMEM_2CTA = 80 * 1024;   // minimum per launch: two CTAs per SM at most
 
 // Rows [r0, r1) of a GEMV belong to CTA `cta` of `ncta` (rpc = ceil(rows / ncta)).
 __host__ __device__ inline int gemv_rpc(int rows, int ncta) { return (rows + ncta - 1) / ncta; }
@@ -235,26 +234,17 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
     }
 
     if (!q8) {
-        // Rows rl and rl + nw of a warp share each activation load (the
-        // activation reads, not the weights, dominate shared-memory traffic);
-        // every row keeps its own accumulation chain.
         const uint8_t * wa = wsm;
         const uint8_t * wb = wsm + L.bA;
-        for (int rl = warp; rl < nrow; rl += 2 * nw) {
-            const int rl2 = rl + nw;
-            const bool two = rl2 < nrow;
-            float acc[NV], accb[NV], acc2[NV], accb2[NV];
+        for (int rl = warp; rl < nrow; rl += nw) {
+            float acc[NV], accb[NV];
 #pragma unroll
-            for (int v = 0; v < NV; ++v) acc[v] = accb[v] = acc2[v] = accb2[v] = 0.0f;
+            for (int v = 0; v < NV; ++v) acc[v] = accb[v] = 0.0f;
             const uint4 * ra = reinterpret_cast<const uint4 *>(wa + (size_t) rl * cols * 2);
             const uint4 * rb = reinterpret_cast<const uint4 *>(wb + (size_t) rl * cols * 2);
-            const uint4 * ra2 = reinterpret_cast<const uint4 *>(wa + (size_t)(two ? rl2 : rl) * cols * 2);
-            const uint4 * rb2 = reinterpret_cast<const uint4 *>(wb + (size_t)(two ? rl2 : rl) * cols * 2);
             for (int c = lane; c < h8; c += 32) {
                 const uint4 w = ra[c];
                 const uint4 w2 = dual ? rb[c] : make_uint4(0, 0, 0, 0);
-                const uint4 u = two ? ra2[c] : make_uint4(0, 0, 0, 0);
-                const uint4 u2 = (two && dual) ? rb2[c] : make_uint4(0, 0, 0, 0);
 #pragma unroll
                 for (int v = 0; v < NV; ++v) {
                     if (v >= nv) continue;
@@ -263,10 +253,6 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
                     const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                     acc[v] = dot8(w, xv, acc[v]);
                     if (dual) accb[v] = dot8(w2, xv, accb[v]);
-                    if (two) {
-                        acc2[v] = dot8(u, xv, acc2[v]);
-                        if (dual) accb2[v] = dot8(u2, xv, accb2[v]);
-                    }
                 }
             }
 #pragma unroll
@@ -275,11 +261,6 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
                 const float s1 = warp_sum(acc[v]);
                 const float s2 = dual ? warp_sum(accb[v]) : 0.0f;
                 if (lane == 0) store(r0 + rl, rl, v, gemv_epi(a, v, s1, s2, rs, rl, rstride));
-                if (two) {
-                    const float t1 = warp_sum(acc2[v]);
-                    const float t2 = dual ? warp_sum(accb2[v]) : 0.0f;
-                    if (lane == 0) store(r0 + rl2, rl2, v, gemv_epi(a, v, t1, t2, rs, rl2, rstride));
-                }
             }
         }
         return true;
