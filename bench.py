@@ -399,7 +399,7 @@ def run_batch(args, cfg):
 def run_ncu_workload(args):
     """A small fixed workload for ncu captures (no timing, no JSON line):
     `frames`: the config's ICL prefill and --frames frames through the frame
-    loop (QTTS_FRAME_MODE selects graph or dataflow); `batch`: --batch
+    loop (QTTS_FRAME_MODE=graph selects the one-kernel-per-op frame); `batch`: --batch
     utterances with 64-position ICL prompts, --frames batched frames, then two
     eagerly profiled frames.  A few GB on the device at most."""
     pkg = _pkg()
@@ -419,25 +419,6 @@ def run_ncu_workload(args):
                            temperature=0.0, top_k=0, eos_bias=-1e9)
         got = eng.run_frames(args.frames)
         print(f"frames={got} {eng.timing()}", file=sys.stderr)
-        if os.environ.get("QTTS_DF_TRACE") and got:
-            ops, tr = eng.frame_trace()
-            t = tr[: len(ops) * got].astype(np.int64)
-            nxt = np.append(t[1:, 0], t[-1, 6])
-            names = {16: "gemv", 17: "gemv+cb0", 18: "gemv+cbg", 19: "gemv+cblast", 20: "gemv+cpattn2",
-                     21: "gemv+cpattn", 32: "talker-attn"}
-            kinds = np.tile(ops, got)
-            def col(i, c):   # mean of stamp c - start over the ops that recorded it (0: not recorded)
-                v = t[i, c]
-                v = v[v > 0] - t[i, 0][v > 0]
-                return v.mean() / 1e3 if len(v) else float("nan")
-            for ty in sorted(set(ops.tolist())):
-                i = np.nonzero(kinds == ty)[0]
-                print(f"{names.get(ty, ty):12s} n={len(i) // got:4d}/frame  input {col(i, 1):5.2f}  last-cta-input"
-                      f" {col(i, 2):5.2f}  weights {col(i, 3):5.2f}  row0 {col(i, 4):5.2f}  rows-done {col(i, 5):5.2f}"
-                      f"  done {col(i, 6):5.2f}  barrier1 {col(i, 8):5.2f}  issued {col(i, 7):5.2f}  barrier2 {col(i, 9):5.2f}"
-                      f"  next {(nxt[i] - t[i, 0]).mean() / 1e3:5.2f} us",
-                      file=sys.stderr)
-            print(f"frame span {(t[-1, 6] - t[0, 0]) / 1e3 / got:.1f} us", file=sys.stderr)
         eng.close()
         return 0
     path = pkg.synth_gguf.ensure_gguf(d, cfg_m, "f16", seed=0)
@@ -528,8 +509,8 @@ def main():
 
     # ---- device-resident timing: inputs in HBM.  The utterance of the config
     # (F frames after the prefill) is replayed K / F times: each replay rewinds
-    # the device frame state to frame 0 (no new prefill) and runs F frames in
-    # one dataflow-kernel launch (or F graph launches).
+    # the device frame state to frame 0 (no new prefill) and runs F frames as F
+    # launches of the frame CUDA graph.
     F = cfg["frames"]
     reps = max(1, (K + F - 1) // F)
     runs = [min(F, K - i * F) for i in range(reps)]   # whole replays, then the remainder of a partial one
@@ -598,26 +579,21 @@ def main():
     kv_pos_mean = plen + F / 2.0
     frame_bytes = WEIGHT_BYTES[args.config] + KV_TALKER_PER_POS * kv_pos_mean + KV_CP_PER_POS * 135
     prof_total = sum(prof[c]["ms"] for c in ("gemv", "attention", "sample", "other"))
-    persistent = launches_per_frame == 1
-    if persistent:
-        # one cooperative launch runs the frames of a replay: bytes per launch = those frames' weights + KV,
-        # duration = the timed region / launches (CUDA events on the engine stream)
-        kernel = f"{eng.frame_kernel()} (one cooperative launch per utterance replay of up to {F} frames)"
-        bytes_per_launch = frame_bytes * K / reps
-        achieved = bytes_per_launch / (ms_max / reps / 1e3) / 1e9
-        tpf = _profile_figure(f"{eng.frame_kernel()}_{args.config}.md", "dram_bytes_per_frame")
-        traffic = tpf * K / reps if tpf else None
-        launches_per_frame_k = reps / K
+    # the timed path: the frame CUDA graph; its launches overlap under programmatic dependent
+    # launch, so the unit is the frame (algorithmic bytes of a frame / device time per frame)
+    mode = eng.frame_mode()
+    if mode == "fused":
+        kernel = (f"frame CUDA graph, fused path ({launches_per_frame} launches per frame: k_ff_attn, k_ff_ffn, "
+                  "k_ff_head; programmatic dependent launch)")
+        ratio = _profile_figure(f"k_ff_{args.config}.md", "dram_bytes_per_algorithmic_byte")
     else:
-        # the timed path: the frame CUDA graph; its launches overlap under programmatic dependent
-        # launch, so the unit is the frame (algorithmic bytes of a frame / device time per frame)
         kernel = f"frame CUDA graph ({launches_per_frame} launches per frame, programmatic dependent launch)"
-        bytes_per_launch = frame_bytes
-        achieved = frame_bytes / (frame_ms / 1e3) / 1e9
         # ncu: DRAM bytes per algorithmic byte over captured frame GEMVs (the graph's bytes are GEMV weights)
         ratio = _profile_figure(f"k_gemv_{args.config}.md", "dram_bytes_per_algorithmic_byte")
-        traffic = ratio * frame_bytes if ratio else None
-        launches_per_frame_k = float(launches_per_frame)
+    bytes_per_launch = frame_bytes
+    achieved = frame_bytes / (frame_ms / 1e3) / 1e9
+    traffic = ratio * frame_bytes if ratio else None
+    launches_per_frame_k = float(launches_per_frame)
     line = {
         "metric": METRIC, "value": world * K / (ms_max / 1e3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": frame_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -632,6 +608,7 @@ def main():
                      "launches_per_frame": launches_per_frame_k,
                      "frame_algorithmic_bytes": frame_bytes,
                      "frame_algorithmic_gbs": frame_bytes / (frame_ms / 1e3) / 1e9,
+                     "frame_path": mode,
                      "eager_gemv_gbs_serialised": gemv_gbs,
                      "eager_gemv_share_serialised": g["ms"] / prof_total if prof_total else None},
         "kernel_classes": {c: {"launches_per_frame": prof[c]["launches"] / max(prof["frames"], 1),
@@ -641,7 +618,7 @@ def main():
                 "d2h_bytes_per_step": d2h_all / K,
                 "includes": f"{reps} x qtts_generate ({'+'.join(str(n) for n in runs)} frames): prompt upload, "
                             "prefill, frames, codes download"},
-        "gpu_launches": reps if persistent else launches_per_frame * K,
+        "gpu_launches": launches_per_frame * K,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:

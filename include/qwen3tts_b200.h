@@ -81,7 +81,9 @@ typedef struct qtts_stage_timing {
     float prefill_forward_ms; /* device: forward_prefill */
     float talker_ms;          /* device: talker steps (layers + codec head) */
     float code_pred_ms;       /* device: code-predictor passes (layers + heads) */
-    float sample_embed_ms;    /* device: samplers and next-input embedding sums */
+    float sample_embed_ms;    /* device: samplers and next-input embedding sums (fused frame path:
+                                 the launches that sample, each also running its pass's first
+                                 attention block) */
     float total_ms;           /* host: the whole qtts_generate call */
     int32_t frames;
 } qtts_stage_timing;
@@ -182,13 +184,19 @@ int32_t qtts_set_attn_dump(qtts_engine * e, int32_t enabled, int32_t layer);
 int32_t qtts_attn_rows(const qtts_engine * e);
 int32_t qtts_attn_row(const qtts_engine * e, int32_t r, float * out, int32_t cap);
 int32_t qtts_get_timing(const qtts_engine * e, qtts_timing * out);
-/* Diagnostics of the dataflow frame kernel (QTTS_FRAME_MODE=dataflow), enabled
- * by QTTS_DF_TRACE=1 at run time: the frame program's ops (type * 16 + input
- * prologue; types 1 GEMV, 2 talker attention) and, for the last launch, four
- * %globaltimer stamps per op and frame (CTA 0 start, CTA 0 input ready, latest
- * input ready over the CTAs, CTA 0 done).  Both return the count available. */
-int32_t qtts_frame_ops(const qtts_engine * e, int32_t * ops, int32_t cap);
-int32_t qtts_frame_trace(const qtts_engine * e, unsigned long long * out, int32_t cap);
+/* The frame path in use (no reference counterpart): 0 = one kernel per op (the
+ * default), 1 = two clustered kernels per transformer layer (QTTS_FRAME_MODE=fused
+ * at load time, where the model's shapes allow it). */
+int32_t qtts_get_frame_mode(const qtts_engine * e);
+/* Diagnostics of the fused frame path (no reference counterpart), on when
+ * QTTS_FF_TRACE=1 at load time: per launch of frame 1 of a run and per CTA (up
+ * to 256), eight %globaltimer stamps (start, dependency wait returned, input
+ * built, first GEMV done, first cluster barrier passed, attention or ffn_down
+ * partial done, second cluster barrier passed, end; 0 = not reached) into out
+ * [launch][256][8] (cap words), and kinds[launch] = kind * 4 + (samples ? 2 : 0)
+ * + rows - 1 (kind 0 attention block, 1 FFN block, 2 head).  Returns the number
+ * of launches (0 when tracing is off). */
+int32_t qtts_frame_trace(const qtts_engine * e, unsigned long long * out, int32_t cap, int32_t * kinds, int32_t kcap);
 /* Stage timing on (1) / off (0) for the following generate calls; 1 on success. */
 int32_t qtts_set_stage_timing(qtts_engine * e, int32_t enabled);
 int32_t qtts_get_stage_timing(const qtts_engine * e, qtts_stage_timing * out);

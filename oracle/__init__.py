@@ -117,18 +117,26 @@ class Oracle:
             L.orc_attn_rows.restype = C.c_int
             L.orc_attn_rows.argtypes = []
             L.orc_set_engine_order.argtypes = [C.c_int]
+            L.orc_set_frame_split.argtypes = [C.c_int]
             L.orc_expf.restype = C.c_float
             L.orc_expf.argtypes = [C.c_float]
             cls._lib = L
         return cls._lib
 
-    def __init__(self, path: str, threads: int | None = None, engine_order: bool = True):
+    def __init__(self, path: str, threads: int | None = None, engine_order: bool = True,
+                 frame_split: bool | None = None):
         """engine_order: run every reduction in the engine's order (the parity
         checker's mode; process-wide); False: plain sequential / AVX2 orders,
-        used for the CPU baseline timing."""
+        used for the CPU baseline timing.  frame_split: in generate()'s frame
+        loop, restate the engine's fused frame path (O-projection and ffn_down
+        as ordered partial sums, see oracle.cpp); default: on when
+        QTTS_FRAME_MODE=fused selects that path in the engine."""
         L = self.lib()
         L.orc_set_threads(int(threads) if threads else available_cpus())
         L.orc_set_engine_order(1 if engine_order else 0)
+        if frame_split is None:
+            frame_split = os.environ.get("QTTS_FRAME_MODE", "") == "fused"
+        L.orc_set_frame_split(1 if frame_split else 0)
         err = C.create_string_buffer(512)
         self.h = L.orc_load(path.encode(), err, 512)
         if not self.h:

@@ -459,6 +459,98 @@ static void mul_mat(const Tensor * W, const float * x, int n_vec, float * y, boo
     }
 }
 
+// ---- the engine's fused frame path (two clustered kernels per layer), restated
+// for the frame loop of orc_generate when split mode is on (engine order only).
+static bool g_split = false;      // orc_set_frame_split
+static bool g_in_frame = false;   // inside orc_generate's frame loop
+
+// FFN block shape: R intermediate rows per CTA (a Q8_0 32-block), N CTAs, and
+// clusters of C CTAs (the largest power of two <= 16 dividing N and H).
+static void ffn_split(int I, int H, bool q8, int & R, int & N, int & C) {
+    R = q8 ? 32 : 16;
+    N = I / R;
+    C = 16;
+    while (C > 1 && (N % C || H % C)) C /= 2;
+}
+
+// O-projection by kv group: partial g is the GEMV over the group's gc columns
+// (lane order of dot_f16_eng / dot_q8_eng over that slice); out = ((P_0 + P_1)
+// + ...) + P_{ng-1}.
+static void mul_mat_o_split(const Tensor * W, const float * x, int n_vec, float * y, int gc) {
+    const int cols = (int) W->ne[0], rows = (int) W->ne[1], ng = cols / gc;
+    if (W->type == T_F16) {
+        std::vector<float> xh((size_t) n_vec * cols);
+        for (size_t i = 0; i < xh.size(); ++i) xh[i] = round_f16(x[i]);
+        const uint16_t * w = (const uint16_t *) W->data;
+        #pragma omp parallel for schedule(static)
+        for (int r = 0; r < rows; ++r)
+            for (int v = 0; v < n_vec; ++v) {
+                float acc = 0.0f;
+                for (int g = 0; g < ng; ++g) {
+                    const float pg = dot_f16_eng(w + (size_t) r * cols + g * gc, xh.data() + (size_t) v * cols + g * gc, gc);
+                    acc = g == 0 ? pg : acc + pg;
+                }
+                y[(size_t) v * rows + r] = acc;
+            }
+        return;
+    }
+    const int nb = cols / 32, nbg = gc / 32;
+    std::vector<QBlocks> qx(n_vec);
+    for (int v = 0; v < n_vec; ++v) quantize_q8_0(x + (size_t) v * cols, cols, qx[v]);
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r)
+        for (int v = 0; v < n_vec; ++v) {
+            const uint8_t * row = W->data + (size_t) r * nb * 34;
+            float acc = 0.0f;
+            for (int g = 0; g < ng; ++g) {
+                const float pg = dot_q8_eng(row + (size_t) g * nbg * 34, qx[v].q.data() + g * gc, qx[v].d.data() + g * nbg, nbg);
+                acc = g == 0 ? pg : acc + pg;
+            }
+            y[(size_t) v * rows + r] = acc;
+        }
+}
+
+// ffn_down by intermediate slice (F16 weight cast to F32, F32 activation; Q8_0
+// quantises the activation per 32-block): CTA s of the FFN block owns rows
+// [s R, s R + R) of h; its partial of output r chains fmaf(W[r][j], h[j], acc)
+// over j in order (Q8_0: the block's isum x (d_w x d_a)); a cluster adds its
+// CTAs' partials in rank order, the output adds the clusters' in order.
+static void mul_mat_down_split(const Tensor * W, const float * h, int n_vec, float * y) {
+    const int I = (int) W->ne[0], H = (int) W->ne[1];
+    const bool q8 = W->type == T_Q8_0;
+    int R, N, C;
+    ffn_split(I, H, q8, R, N, C);
+    std::vector<QBlocks> qx(q8 ? n_vec : 0);
+    for (int v = 0; q8 && v < n_vec; ++v) quantize_q8_0(h + (size_t) v * I, I, qx[v]);
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < H; ++r)
+        for (int v = 0; v < n_vec; ++v) {
+            float out = 0.0f;
+            for (int cl = 0; cl < N / C; ++cl) {
+                float q = 0.0f;
+                for (int p = 0; p < C; ++p) {
+                    const int sl = cl * C + p;
+                    float d;
+                    if (q8) {
+                        const uint8_t * blk = W->data + ((size_t) r * (I / 32) + sl) * 34;
+                        uint16_t dw; memcpy(&dw, blk, 2);
+                        const int8_t * qw = (const int8_t *)(blk + 2);
+                        int32_t isum = 0;
+                        for (int k = 0; k < 32; ++k) isum += (int32_t) qw[k] * (int32_t) qx[v].q[(size_t) sl * 32 + k];
+                        d = (float) isum * (h2f(dw) * h2f(qx[v].d[sl]));
+                    } else {
+                        const uint16_t * w = (const uint16_t *) W->data + (size_t) r * I;
+                        d = 0.0f;
+                        for (int j = sl * R; j < sl * R + R; ++j) d = fmaf(h2f(w[j]), h[(size_t) v * I + j], d);
+                    }
+                    q = p == 0 ? d : q + d;
+                }
+                out = cl == 0 ? q : out + q;
+            }
+            y[(size_t) v * H + r] = out;
+        }
+}
+
 static void rms_norm(const float * x, int n, float eps, const float * gain, float * y) {
     double sum = 0.0;
     for (int i = 0; i < n; ++i) sum += (double)(x[i] * x[i]);
@@ -698,13 +790,16 @@ static void forward_stack(Model & m, std::vector<Layer> & layers, KV & cache, fl
                     }
                 }
             }
-        mul_mat(ly.o, att.data(), M, o.data());
+        const bool split = g_split && g_eng && g_in_frame;   // the engine's fused frame path
+        if (split) mul_mat_o_split(ly.o, att.data(), M, o.data(), (NH / NKV) * D);
+        else mul_mat(ly.o, att.data(), M, o.data());
         for (size_t t = 0; t < (size_t) M * H; ++t) X[t] = o[t] + X[t];
         for (int i = 0; i < M; ++i) rms_norm_in(&X[(size_t) i * H], H, c.eps, f32p(ly.ffn_norm), &xn[(size_t) i * H]);
         mul_mat(ly.gate, xn.data(), M, gt.data());
         mul_mat(ly.up, xn.data(), M, up.data());
         for (size_t t = 0; t < (size_t) M * ffn; ++t) hh[t] = silu(gt[t]) * up[t];
-        mul_mat(ly.down, hh.data(), M, dn.data(), /*f32_cast=*/true);
+        if (split) mul_mat_down_split(ly.down, hh.data(), M, dn.data());
+        else mul_mat(ly.down, hh.data(), M, dn.data(), /*f32_cast=*/true);
         for (size_t t = 0; t < (size_t) M * H; ++t) X[t] = dn[t] + X[t];
     }
 }
@@ -827,6 +922,7 @@ void orc_set_attn_dump(float * buf, int cap, int stride, int layer) {
 int orc_attn_rows() { return g_attn_rows; }
 // 1 (default): every reduction in the engine's order; 0: plain sequential / AVX2 orders.
 void orc_set_engine_order(int on) { g_eng = on != 0; }
+void orc_set_frame_split(int on) { g_split = on != 0; }
 float orc_expf(float x) { return qexpf(x); }
 int orc_get_threads() { return omp_get_max_threads(); }
 
@@ -1214,6 +1310,7 @@ int orc_generate(void * h, const orc_gen_args * a, orc_gen_result * r) {
     const int sup = V - 1024;
     std::vector<float> step(H), row(H);
     int dec = 0;
+    g_in_frame = true;
     for (int frame = 0; frame < a->max_len; ++frame) {
         if (a->talker_logits_out && frame < a->codes_cap) memcpy(a->talker_logits_out + (size_t) frame * V, logits.data(), V * 4);
         for (int i = sup; i < V; ++i) if (i != c.codec_eos) logits[i] = -INFINITY;
@@ -1289,6 +1386,7 @@ int orc_generate(void * h, const orc_gen_args * a, orc_gen_result * r) {
         orc_forward_step(h, step.data(), n_past, logits.data(), nullptr);
         n_past++;
     }
+    g_in_frame = false;
     r->n_frames = (int)(out.size() / NCB);
     if (a->codes_out) memcpy(a->codes_out, out.data(), (size_t) std::min(r->n_frames, a->codes_cap) * NCB * 4);
     return 0;

@@ -18,7 +18,7 @@
 //     step, with no host round trip inside a frame.
 #include "../../include/qwen3tts_b200.h"
 #include "gguf.hpp"
-#include "frame_dataflow.cuh"
+#include "frame_fused.cuh"
 #include "gemm_tc.cuh"
 #include "batch_engine.cuh"
 
@@ -130,29 +130,24 @@ struct Engine {
     int launches = 0;
     int launches_per_frame = 0;
     GenSession sess;
-    // dataflow frame kernel (one cooperative launch per run of frames)
-    bool use_dataflow = false;   // QTTS_FRAME_MODE=dataflow selects the single-launch frame kernel
-    std::vector<DfOp> prog;
-    std::vector<FusedAttn> df_att;
-    DfOp * d_prog = nullptr;
-    size_t prog_cap = 0;
-    FusedAttn * d_df_att = nullptr;
-    size_t att_cap = 0;
-    unsigned long long * d_dfbuf = nullptr;   // tagged activation buffers
-    size_t df_buf_words = 0;
-    unsigned long long * df_bufp[DB_N] = {};
-    int df_slot_words[DB_N] = {}, df_writes[DB_N] = {};
-    unsigned df_tag_base = 1;
-    int * d_err = nullptr;
-    bool prog_ok = false;
-    int df_first[2] = {0, 0};
-    int df_pf0[8];
-    int n_df_pf0 = 0;
-    int df_pf_lead = 4;          // GEMVs between a slice's L2 prefetch and its use (QTTS_DF_PF_LEAD)
-    size_t df_wbuf = 0, df_work = 0, df_dyn = 0;
-    unsigned long long * d_trace = nullptr;   // QTTS_DF_TRACE=1: per-op stamps of the last dataflow launch
-    size_t trace_cap = 0, trace_n = 0;
-    int df_keys = 0;
+    // frame path: FM_GRAPH (one kernel per op, the default) or FM_FUSED (two
+    // clustered kernels per layer; QTTS_FRAME_MODE=fused, where the model's shapes
+    // allow it)
+    enum { FM_GRAPH = 0, FM_FUSED = 1 };
+    int frame_mode = FM_GRAPH;
+    int * d_err = nullptr;        // set by a fused kernel whose bounded wait gave up
+    struct FfLayerW { DMat qkv_g, o_g, down_r; };
+    std::vector<FfLayerW> ffL, ffCP;
+    uint8_t * ffw = nullptr;      // repacked weights of the fused frame path
+    float * ff_part_o = nullptr, * ff_part_d = nullptr, * ff_xres = nullptr, * ff_xmid = nullptr;
+    int ff_CA = 16;               // attention block: CTAs per kv-group cluster
+    struct FfStack { int R = 0, N = 0, C = 0; };   // FFN block: rows per CTA, CTAs, cluster size
+    FfStack ffs_t, ffs_cp;
+    size_t ff_head_smem_t = 0, ff_head_smem_cp = 0;
+    int ff_max_keys = 0;          // the talker attention row length the captured frame serves
+    std::string ff_why;           // why the fused path is off (empty: on)
+    unsigned long long * d_fftrace = nullptr;   // QTTS_FF_TRACE=1: stamps of frame 1's launches
+    std::vector<int> ff_kinds;    // per launch of the frame: kind * 4 + (samples ? 2 : 0) + (nv - 1)
     // eager profiling: CUDA events around every launch, accumulated per kernel class
     bool profiling = false;
     struct ProfEv { int cls; int stage; double bytes; cudaEvent_t a, b; };
@@ -193,15 +188,15 @@ struct Engine {
         if (d_prow) { cudaFree(d_prow); d_prow = nullptr; prow_cap = 0; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
                          cp_logits, hidden, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
-                         dbg_t, dbg_cp, d_attn, d_prog, d_df_att, d_dfbuf, d_err, logits0, hidden0, d_trace};
+                         dbg_t, dbg_cp, d_attn, d_err, logits0, hidden0, ffw, ff_part_o, ff_part_d, ff_xres,
+                         ff_xmid, d_fftrace};
         for (void * p : ptrs) if (p) cudaFree(p);
         wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
         x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = tmp_a = tmp_b = nullptr;
         logits0 = hidden0 = nullptr;
         d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
-        dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_prog = nullptr; d_df_att = nullptr; d_dfbuf = nullptr;
-        d_err = nullptr; df_buf_words = 0; prog_cap = 0; att_cap = 0; prog_ok = false;
-        d_trace = nullptr; trace_cap = trace_n = 0;
+        dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_err = nullptr;
+        ffw = nullptr; ff_part_o = ff_part_d = ff_xres = ff_xmid = nullptr; d_fftrace = nullptr;
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         ev0 = ev1 = nullptr;
@@ -235,8 +230,9 @@ struct Engine {
     GemvArgs make_gemv(const DMat & A, const DMat * B, const float * xin, int ldx, int nv, const float * norm, int act,
                        float * y, int ldy, const float * resid, int ldr, int epi, float * xn_out, int ldxn,
                        const int * done, int * ncta_out, size_t * slice_out, size_t * smem_out);
-    bool build_program(int max_keys);   // max_keys: the longest talker attention row it serves
-    bool launch_dataflow(int n);
+    bool ff_prepare();                  // repacked weights, buffers and launch shapes of FM_FUSED
+    bool enqueue_frame_ff();
+    bool ff_layers(bool cp, int pass, const float * in_logits);
     bool sync(const char * what);
 
     // ------------------------------------------------------------ API pieces
@@ -333,11 +329,11 @@ bool Engine::load(const char * path, int device) {
     if (c.hidden_size % 256 || c.intermediate_size % 32 || c.code_pred_intermediate_size % 32 || c.text_embd_dim % 32) {
         err = "hidden/ffn/text widths must be multiples of 256/32/32"; return false;
     }
-    if (const char * m = getenv("QTTS_FRAME_MODE")) use_dataflow = strcmp(m, "dataflow") == 0;
-    if (const char * v = getenv("QTTS_DF_PF_LEAD")) df_pf_lead = std::max(0, atoi(v));   // 0: no L2 prefetch
     if (!upload_weights(g)) return false;
     if (!alloc_activations()) return false;
     if (!init_cp_kv(16)) return false;
+    const char * fm = getenv("QTTS_FRAME_MODE");
+    if (fm && strcmp(fm, "fused") == 0 && !ff_prepare()) return false;
     return true;
 }
 
@@ -551,7 +547,7 @@ bool Engine::init_kv(int ctx) {
     QCHECK(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) std::max<size_t>(smem, 48 * 1024)));
     n_ctx = ctx;
     n_used = 0;
-    graph_ok = false; prog_ok = false;
+    graph_ok = false;
     return true;
 }
 
@@ -569,7 +565,7 @@ bool Engine::init_cp_kv(int ctx) {
     QCHECK(cudaMalloc(&rope_cp, t.size() * sizeof(float2)));
     QCHECK(cudaMemcpy(rope_cp, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
     cp_ctx = ctx;
-    graph_ok = false; prog_ok = false;
+    graph_ok = false;
     return true;
 }
 
@@ -815,7 +811,7 @@ bool Engine::capture_graph() {
     cudaGraph_t gr = nullptr;
     QCHECK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
     launches = 0;
-    const bool ok = enqueue_frame();
+    const bool ok = frame_mode == FM_FUSED ? enqueue_frame_ff() : enqueue_frame();
     cudaError_t ce = cudaStreamEndCapture(stream, &gr);
     if (!ok) { if (gr) cudaGraphDestroy(gr); return false; }
     if (ce != cudaSuccess) { err = std::string("graph capture: ") + cudaGetErrorString(ce); return false; }
@@ -827,259 +823,302 @@ bool Engine::capture_graph() {
     return true;
 }
 
-// ---------------------------------------------------------------- dataflow frame program
-// The frame as k_frame_dataflow's op list: the same layers, heads and samplers
-// as enqueue_frame(), with each GEMV's input named by the op that produced it.
-// Pass g of the code predictor samples codebook g at its start (g = 0: the
-// talker logits), runs the code-predictor layers and lm_head[g]; the talker
-// step samples the last codebook, sums the next input and ends with the codec
-// head.
-bool Engine::build_program(int max_keys) {
+// ---------------------------------------------------------------- fused frame path
+static size_t ff_attn_smem(const DMat & qkv, const DMat & o, int H, int rows_g, int GD, int CA, int nv, int keys);
+// Repacked weights (group-major q|k|v and O, ffn_down in the FFN block's slice
+// order), partial-sum buffers and launch shapes of FM_FUSED.  Leaves frame_mode
+// at FM_GRAPH, with the reason in ff_why, when the model's shapes do not fit.
+bool Engine::ff_prepare() {
     const qtts_config & c = cfg;
-    df_keys = max_keys;
-    const int H = c.hidden_size, NG = c.n_codebooks - 1, NKV = c.n_key_value_heads;
-    prog.clear();
-    df_att.clear();
-    int wr[DB_N] = {0};
-    const size_t cp_layer = (size_t) cp_ctx * NKV * QTTS_HD, t_layer = (size_t) n_ctx * NKV * QTTS_HD;
-    for (size_t il = 0; il < CPL.size(); ++il)
-        df_att.push_back(fused_attn_args(CPL[il], cpk + il * cp_layer, cpv + il * cp_layer, rope_cp, 2, nullptr, 0, true,
-                                         nullptr, cp_ctx));
-    for (size_t il = 0; il < L.size(); ++il)
-        df_att.push_back(fused_attn_args(L[il], kc + il * t_layer, vc + il * t_layer, rope_t, 1, nullptr, 0, false,
-                                         attn_dump && (int) il == attn_layer ? d_attn : nullptr, n_ctx));
-    auto gemv_op = [&](const DMat & A, const DMat * B, int nv, int pro, const float * norm, int act, int epi,
-                       int out_buf) {
-        DfOp op{};
-        op.type = DF_GEMV; op.pro = pro; op.nv = nv; op.A = A;
-        if (B) op.B = *B;
-        op.norm_g = norm; op.act = act; op.epi = epi;
-        op.in_buf = -1; op.in_op = 0;
-        op.out_buf = out_buf; op.out_wr = wr[out_buf]++;
-        return op;
+    const int H = c.hidden_size, NH = c.n_attention_heads, NKV = c.n_key_value_heads;
+    const int G = NH / NKV, GD = G * QTTS_HD, rows_g = GD + 2 * QTTS_HD, QD = NH * QTTS_HD;
+    const bool q8 = L[0].qkv.type == W_Q8_0;
+    const size_t es = q8 ? 1 : 2;
+    auto stack = [&](int I, FfStack & S) -> bool {
+        S.R = q8 ? 32 : 16;
+        if (I % S.R) return false;
+        S.N = I / S.R;
+        S.C = FF_MAX_CLUSTER;
+        while (S.C > 1 && (S.N % S.C || H % S.C)) S.C /= 2;
+        return true;
     };
-    auto from = [&](DfOp & op, int buf, int producer, int row) {
-        op.in_buf = buf; op.in_op = producer; op.in_wr = prog[producer].out_wr; op.in_row = row;
+    ff_why.clear();
+    if (!stack(c.intermediate_size, ffs_t) || !stack(c.code_pred_intermediate_size, ffs_cp)) ff_why = "ffn width";
+    else if (rows_g % ff_CA || H % ff_CA || GD % 32) ff_why = "head layout";
+    else if (c.n_codebooks > QTTS_MAX_CB || c.codec_vocab_size > 4096 || c.code_pred_vocab_size > 4096) ff_why = "vocabulary";
+    else {
+        for (auto * Ls : {&L, &CPL})
+            for (auto & l : *Ls)
+                if (l.qkv.type != l.o.type || l.o.type != l.down.type || l.gate.type != l.down.type) ff_why = "mixed weight types";
+    }
+    if (ff_why.empty() && (NKV > FF_MAX_PART || ffs_t.N / ffs_t.C > FF_MAX_PART || ffs_cp.N / ffs_cp.C > FF_MAX_PART))
+        ff_why = "too many partial vectors";
+    if (!ff_why.empty()) return true;
+    // repacked copies
+    auto mat_size = [&](const DMat & m) { return (size_t) m.rows * m.cols * es + (q8 ? (size_t) m.rows * (m.cols / 32) * 2 : 0); };
+    size_t total = 0;
+    for (auto * Ls : {&L, &CPL})
+        for (auto & l : *Ls) total += mat_size(l.qkv) + mat_size(l.o) + mat_size(l.down) + 6 * 256;
+    QCHECK(cudaMalloc(&ffw, total));
+    size_t used = 0;
+    auto alloc = [&](size_t b) { uint8_t * p = ffw + used; used += (b + 255) & ~(size_t) 255; return p; };
+    auto fresh = [&](const DMat & src, int rows, int cols) {
+        DMat m = src;
+        m.rows = rows; m.cols = cols;
+        m.w = alloc((size_t) rows * cols * es);
+        m.d = q8 ? reinterpret_cast<const __half *>(alloc((size_t) rows * (cols / 32) * 2)) : nullptr;
+        return m;
     };
-    auto push = [&](const DfOp & op) { prog.push_back(op); return (int) prog.size() - 1; };
-    int head = -1;   // the last head op (its logits feed the next sampler)
-    for (int g = 0; g < NG; ++g) {
-        const int M = g == 0 ? 2 : 1;
-        int prev = -1;
-        for (size_t il = 0; il < CPL.size(); ++il) {
-            LayerW & l = CPL[il];
-            DfOp q = gemv_op(l.qkv, nullptr, M, il ? PRO_POLL : (g == 0 ? PRO_CB0 : PRO_CBG), l.attn_norm, ACT_F16,
-                             EPI_STORE, DB_QKV);
-            if (il) from(q, DB_XCP, prev, 0);
-            else if (g > 0) from(q, DB_LCP, head, 0);
-            else { q.in_buf = DB_LT; }   // the talker head of the previous frame: fixed up below
-            q.cb = g;
-            const int iq = push(q);
-            DfOp o = gemv_op(l.o, nullptr, M, g == 0 ? PRO_CPATTN2 : PRO_CPATTN, nullptr, ACT_F16, EPI_RESID, DB_XCP);
-            from(o, DB_QKV, iq, 0);
-            o.layer = (int) il; o.n_past = g == 0 ? 0 : g + 1;
-            const int io = push(o);
-            DfOp gu = gemv_op(l.gate, &l.up, M, PRO_POLL, l.ffn_norm, ACT_F16, EPI_SWIGLU, DB_H);
-            from(gu, DB_XCP, io, 0);
-            const int igu = push(gu);
-            DfOp dn = gemv_op(l.down, nullptr, M, PRO_POLL, nullptr, ACT_F32, EPI_RESID, DB_XCP);
-            from(dn, DB_H, igu, 0);
-            prev = push(dn);
+    auto copy_rows = [&](const DMat & dst, int dr, const DMat & src, int sr, int n) -> bool {
+        const size_t rb = (size_t) src.cols * es;
+        if (cudaMemcpy((uint8_t *) dst.w + dr * rb, (const uint8_t *) src.w + sr * rb, n * rb, cudaMemcpyDeviceToDevice) != cudaSuccess) return false;
+        if (q8) {
+            const size_t sb = (size_t)(src.cols / 32) * 2;
+            if (cudaMemcpy((uint8_t *) dst.d + dr * sb, (const uint8_t *) src.d + sr * sb, n * sb, cudaMemcpyDeviceToDevice) != cudaSuccess) return false;
         }
-        DfOp hd = gemv_op(cp_head[g], nullptr, 1, PRO_POLL, cp_out_norm, ACT_F16, EPI_STORE, DB_LCP);
-        from(hd, DB_XCP, prev, M - 1);
-        head = push(hd);
-    }
-    int prev = -1;
-    for (size_t il = 0; il < L.size(); ++il) {
-        LayerW & l = L[il];
-        DfOp q = gemv_op(l.qkv, nullptr, 1, il ? PRO_POLL : PRO_CBLAST, l.attn_norm, ACT_F16, EPI_STORE, DB_QKV);
-        if (il) from(q, DB_X, prev, 0);
-        else { from(q, DB_LCP, head, 0); q.cb = NG; }
-        const int iq = push(q);
-        DfOp t{};
-        t.type = DF_TATTN; t.layer = (int)(CPL.size() + il);
-        t.out_buf = DB_ATT; t.out_wr = wr[DB_ATT]++;
-        from(t, DB_QKV, iq, 0);
-        const int it = push(t);
-        DfOp o = gemv_op(l.o, nullptr, 1, PRO_POLL, nullptr, ACT_F16, EPI_RESID, DB_X);
-        from(o, DB_ATT, it, 0);
-        const int io = push(o);
-        DfOp gu = gemv_op(l.gate, &l.up, 1, PRO_POLL, l.ffn_norm, ACT_F16, EPI_SWIGLU, DB_H);
-        from(gu, DB_X, io, 0);
-        const int igu = push(gu);
-        DfOp dn = gemv_op(l.down, nullptr, 1, PRO_POLL, nullptr, ACT_F32, EPI_RESID, DB_X);
-        from(dn, DB_H, igu, 0);
-        prev = push(dn);
-    }
-    DfOp th = gemv_op(codec_head, nullptr, 1, PRO_POLL, out_norm, ACT_F16, EPI_STORE, DB_LT);
-    from(th, DB_X, prev, 0);
-    th.head = 1;
-    const int it_head = push(th);
-    const int n_ops = (int) prog.size();
-    prog[0].in_op = it_head - n_ops;   // previous frame's talker head
-    prog[0].in_wr = prog[it_head].out_wr;
-    if (wr[DB_LT] != 1) { err = "frame program: one talker head per frame expected"; return false; }
-    if (c.hidden_size != CPL[0].o.rows || CPL[0].o.rows != CPL[0].down.rows || L[0].o.rows != L[0].down.rows) {
-        err = "frame program: O and down projections must share the residual row split"; return false;
-    }
-
-    // Weight staging: GEMV j of the frame uses buffer j & 1 and its slice is
-    // copied once GEMV j - 2 is done (cyclically; the first two at launch); GEMV
-    // j prefetches the slice of GEMV j + df_pf_lead into L2.  The GEMV count per
-    // frame is even (15 (4 Lcp + 1) + 4 L + 1), so the parity holds across frames.
-    std::vector<int> gi;
-    for (int i = 0; i < n_ops; ++i)
-        if (prog[i].type == DF_GEMV) gi.push_back(i);
-    const int m = (int) gi.size();
-    if (m < 4 || (m & 1)) { err = "unexpected GEMV count in the frame program"; return false; }
-    const int lead = df_pf_lead <= 0 ? 0 : std::max(2, std::min(df_pf_lead, m - 1));
-    for (int j = 0; j < m; ++j) {
-        DfOp & site = prog[gi[j]];
-        site.slot = j & 1;
-        const DfOp & nx = prog[gi[(j + 2) % m]];
-        site.iA = nx.A; site.iB = nx.B; site.iG = nx.norm_g;
-        if (lead) {
-            const DfOp & pf = prog[gi[(j + lead) % m]];
-            site.pA = pf.A; site.pB = pf.B;
+        return true;
+    };
+    for (int which = 0; which < 2; ++which) {
+        std::vector<LayerW> & Ls = which ? CPL : L;
+        std::vector<FfLayerW> & F = which ? ffCP : ffL;
+        F.resize(Ls.size());
+        for (size_t il = 0; il < Ls.size(); ++il) {
+            const LayerW & l = Ls[il];
+            FfLayerW & f = F[il];
+            f.qkv_g = fresh(l.qkv, NKV * rows_g, H);
+            f.o_g = fresh(l.o, NKV * H, GD);
+            f.down_r = fresh(l.down, l.down.rows, l.down.cols);
+            for (int g = 0; g < NKV; ++g) {
+                const int d0 = g * rows_g;
+                if (!copy_rows(f.qkv_g, d0, l.qkv, g * GD, GD) ||
+                    !copy_rows(f.qkv_g, d0 + GD, l.qkv, QD + g * QTTS_HD, QTTS_HD) ||
+                    !copy_rows(f.qkv_g, d0 + GD + QTTS_HD, l.qkv, QD + NKV * QTTS_HD + g * QTTS_HD, QTTS_HD)) {
+                    err = "fused path: q|k|v regroup failed"; return false;
+                }
+                QCHECK(cudaMemcpy2D((uint8_t *) f.o_g.w + (size_t) g * H * GD * es, GD * es,
+                                    (const uint8_t *) l.o.w + (size_t) g * GD * es, (size_t) QD * es, GD * es, H,
+                                    cudaMemcpyDeviceToDevice));
+                if (q8)
+                    QCHECK(cudaMemcpy2D((uint8_t *) f.o_g.d + (size_t) g * H * (GD / 32) * 2, (GD / 32) * 2,
+                                        (const uint8_t *) l.o.d + (size_t)(g * GD / 32) * 2, (size_t)(QD / 32) * 2,
+                                        (GD / 32) * 2, H, cudaMemcpyDeviceToDevice));
+            }
+            k_ff_repack_down<<<1024, 256, 0, stream>>>(l.down, const_cast<void *>(f.down_r.w), const_cast<__half *>(f.down_r.d));
         }
     }
-    df_first[0] = gi[0];
-    df_first[1] = gi[1];
-    n_df_pf0 = 0;
-    for (int j = 2; j < lead && n_df_pf0 < 8; ++j) df_pf0[n_df_pf0++] = gi[j];
-
-    // shared memory: two weight buffers, the work area, the attention table, the hidden row
-    size_t wb = 0, work = 0;
-    const int QKVD = QD() + 2 * KD();
-    for (const DfOp & op : prog) {
-        if (op.type == DF_GEMV) {
-            const int rpc = gemv_rpc(op.A.rows, n_sm);
-            wb = std::max(wb, slice_layout(op.A, op.B.w != nullptr, op.norm_g != nullptr, rpc).total);
-            work = std::max(work, gemv_work_bytes(op.A.type, op.A.cols, op.nv, rpc));
-        } else {
-            work = std::max(work, ((size_t) QKVD * 4 + 127) / 128 * 128 + fused_attn_smem(max_keys, 1));
-        }
-    }
-    // Code-predictor step attention: its cached K/V rows (positions 0 .. n_past - 1,
-    // contiguous per layer) ride in the O-projection's weight slot behind the slice,
-    // copied with it (the 0.6B F16 layout fills the 88 KB gate/up slot exactly).
-    for (int j = 0; j < m; ++j) {
-        const DfOp & op = prog[gi[j]];
-        if (op.pro != PRO_CPATTN) continue;
-        const size_t so = (slice_layout(op.A, false, false, gemv_rpc(op.A.rows, n_sm)).total + 127) & ~(size_t) 127;
-        wb = std::max(wb, so + 2 * (size_t) op.n_past * NKV * QTTS_HD * 2);
-    }
-    df_wbuf = (wb + 127) & ~(size_t) 127;
-    df_work = (work + 127) & ~(size_t) 127;
-    for (int j = 0; j < m; ++j) {
-        DfOp & op = prog[gi[j]];
-        op.kv_off = -1;
-        if (op.pro != PRO_CPATTN) continue;
-        const size_t so = (slice_layout(op.A, false, false, gemv_rpc(op.A.rows, n_sm)).total + 127) & ~(size_t) 127;
-        const size_t kvb = (size_t) op.n_past * NKV * QTTS_HD * 2;
-        if (kvb > 32768 || op.n_past > CPA_MAX_KEYS) { err = "frame program: code-predictor context too long"; return false; }
-        op.kv_off = (int) so;
-        op.kv_bytes = (int) kvb;
-        DfOp & site = prog[gi[(j - 2 + m) % m]];
-        site.iK = cpk + (size_t) op.layer * cp_layer;
-        site.iV = cpv + (size_t) op.layer * cp_layer;
-        site.i_kv_bytes = (int) kvb;
-        site.i_kv_off = (int) so;
-    }
-    const size_t dyn = 2 * df_wbuf + df_work + df_att.size() * sizeof(FusedAttn) + (size_t) H * 4;
-    cudaFuncAttributes fa{};
-    QCHECK(cudaFuncGetAttributes(&fa, k_frame_dataflow));
-    if (dyn + fa.sharedSizeBytes > 227 * 1024) {
-        err = "dataflow frame kernel: shared memory too large for this context (" + std::to_string(dyn) + " B)";
-        return false;
-    }
-    QCHECK(cudaFuncSetAttribute(k_frame_dataflow, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) dyn));
-    df_dyn = dyn;
-    int nb = 0;
-    QCHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_frame_dataflow, DF_THREADS, dyn));
-    if (nb < 1) { err = "dataflow frame kernel does not fit on an SM"; return false; }
-
-    // tagged buffers: two slots each
-    const int slot_words[DB_N] = {H, 2 * H, 2 * QKVD, QD(), 2 * std::max(c.intermediate_size, c.code_pred_intermediate_size),
-                                  c.code_pred_vocab_size, c.codec_vocab_size};
-    size_t words = 0;
-    for (int b2 = 0; b2 < DB_N; ++b2) words += 2 * (size_t) slot_words[b2];
-    if (words > df_buf_words) {
-        if (d_dfbuf) cudaFree(d_dfbuf);
-        d_dfbuf = nullptr;
-        QCHECK(cudaMalloc(&d_dfbuf, words * 8));
-        df_buf_words = words;
-    }
-    QCHECK(cudaMemset(d_dfbuf, 0, words * 8));
-    df_tag_base = 1;
-    size_t off = 0;
-    for (int b2 = 0; b2 < DB_N; ++b2) {
-        df_bufp[b2] = d_dfbuf + off;
-        df_slot_words[b2] = slot_words[b2];
-        df_writes[b2] = wr[b2];
-        off += 2 * (size_t) slot_words[b2];
-    }
-
-    // upload
-    if (prog.size() > prog_cap) {
-        if (d_prog) cudaFree(d_prog);
-        prog_cap = prog.size();
-        QCHECK(cudaMalloc(&d_prog, sizeof(DfOp) * prog_cap));
-    }
-    QCHECK(cudaMemcpy(d_prog, prog.data(), sizeof(DfOp) * prog.size(), cudaMemcpyHostToDevice));
-    if (df_att.size() > att_cap) {
-        if (d_df_att) cudaFree(d_df_att);
-        att_cap = df_att.size();
-        QCHECK(cudaMalloc(&d_df_att, sizeof(FusedAttn) * att_cap));
-    }
-    QCHECK(cudaMemcpy(d_df_att, df_att.data(), sizeof(FusedAttn) * df_att.size(), cudaMemcpyHostToDevice));
+    QCHECK(cudaGetLastError());
+    QCHECK(cudaStreamSynchronize(stream));
+    const int ncl = std::max(ffs_t.N / ffs_t.C, ffs_cp.N / ffs_cp.C);
+    QCHECK(cudaMalloc(&ff_part_o, sizeof(float) * NKV * 2 * H));
+    QCHECK(cudaMalloc(&ff_part_d, sizeof(float) * ncl * 2 * H));
+    QCHECK(cudaMalloc(&ff_xres, sizeof(float) * 2 * H));
+    QCHECK(cudaMalloc(&ff_xmid, sizeof(float) * 2 * H));
     if (!d_err) QCHECK(cudaMalloc(&d_err, sizeof(int)));
-    prog_ok = true;
+    QCHECK(cudaMemset(d_err, 0, sizeof(int)));
+    for (auto fn : {(const void *) k_ff_attn<1>, (const void *) k_ff_attn<2>, (const void *) k_ff_ffn<1>,
+                    (const void *) k_ff_ffn<2>}) {
+        QCHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        QCHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    }
+    QCHECK(cudaFuncSetAttribute(k_ff_head, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX));
+    if (getenv("QTTS_FF_TRACE")) {
+        const size_t n = (size_t) 256 * FF_TRACE_CTAS * FF_TRACE_N;
+        QCHECK(cudaMalloc(&d_fftrace, n * sizeof(unsigned long long)));
+        QCHECK(cudaMemset(d_fftrace, 0, n * sizeof(unsigned long long)));
+    }
+    // attention block: the largest cluster (CTAs per kv group) whose NKV clusters are
+    // resident together at the talker's shared-memory size for 4096-key rows
+    ff_CA = 0;
+    for (int ca = FF_MAX_CLUSTER; ca >= 2 && !ff_CA; ca /= 2) {
+        if (rows_g % ca || H % ca) continue;
+        cudaLaunchConfig_t cl{};
+        cl.gridDim = dim3(NKV * ca);
+        cl.blockDim = dim3(FF_THREADS);
+        cl.dynamicSmemBytes = ff_attn_smem(L[0].qkv, L[0].o, H, rows_g, GD, ca, 2, 4096);
+        cudaLaunchAttribute at{};
+        at.id = cudaLaunchAttributeClusterDimension;
+        at.val.clusterDim.x = (unsigned) ca; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+        cl.attrs = &at;
+        cl.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k_ff_attn<2>, &cl) == cudaSuccess && n >= NKV) ff_CA = ca;
+        cudaGetLastError();
+    }
+    if (!ff_CA) { ff_why = "attention-block clusters do not fit"; return true; }
+    frame_mode = FM_FUSED;
     return true;
 }
 
-bool Engine::launch_dataflow(int n) {
+// Shared-memory bytes of the two clustered kernels.
+static size_t ff_attn_smem(const DMat & qkv, const DMat & o, int H, int rows_g, int GD, int CA, int nv, int keys) {
+    DMat Qg = qkv; Qg.rows = rows_g; Qg.cols = H;
+    DMat Og = o; Og.rows = H; Og.cols = GD;
+    const size_t wq = (slice_layout(Qg, false, true, rows_g / CA).total + 127) & ~(size_t) 127;
+    const size_t wo = (slice_layout(Og, false, false, H / CA).total + 127) & ~(size_t) 127;
+    size_t work = std::max(gemv_work_bytes(qkv.type, H, nv, rows_g / CA), gemv_work_bytes(o.type, GD, nv, H / CA));
+    work = std::max(work, fused_attn_smem(keys, nv));
+    return std::max(wq, wo) + ((work + 127) & ~(size_t) 127);
+}
+static size_t ff_ffn_work(int type, int H, int nv, int R) {
+    return (std::max(gemv_work_bytes(type, H, nv, R), (size_t) nv * H * 4) + 127) & ~(size_t) 127;
+}
+static size_t ff_ffn_smem(const DMat & gate, const DMat & down, int H, int nv, int R) {
+    const size_t wb_gu = (slice_layout(gate, true, true, R).total + 127) & ~(size_t) 127;
+    const size_t wb_dn = (ff_down_slice_bytes(down.type, R, H) + 127) & ~(size_t) 127;
+    return wb_gu + wb_dn + ff_ffn_work(down.type, H, nv, R) + (size_t) nv * R * 4;
+}
+
+namespace {
+struct FfLaunch {
+    int kind;                      // 0 attention block, 1 FFN block, 2 head
+    int nv, grid, cluster, stage;
+    bool samples;                  // the launch samples the pass's codebook in its prologue
+    size_t smem;
+    double bytes;
+    FfAttnArgs a;
+    FfFfnArgs f;
+    FfHeadArgs h;
+    std::vector<std::pair<const void *, size_t>> w;   // weight regions (prefetched by earlier launches)
+};
+void ff_regions(std::vector<std::pair<const void *, size_t>> & w, const DMat & m) {
+    const size_t es = m.type == W_Q8_0 ? 1 : 2;
+    w.push_back({m.w, (size_t) m.rows * m.cols * es});
+    if (m.type == W_Q8_0) w.push_back({m.d, (size_t) m.rows * (m.cols / 32) * 2});
+}
+}  // namespace
+
+// The frame as clustered launches: the code-predictor passes (pass 0 samples
+// codebook 0 from the talker logits, pass g codebook g), then the talker step
+// (its first layer samples the last codebook) and the codec head, which also
+// advances the frame state.
+bool Engine::enqueue_frame_ff() {
     const qtts_config & c = cfg;
-    const int n_ops = (int) prog.size();
-    // tags grow by n_ops per frame; restart from a cleared buffer before they wrap
-    if ((unsigned long long) df_tag_base + (unsigned long long)(n + 1) * n_ops >= 0xFFFFFFF0ull) {
-        QCHECK(cudaMemsetAsync(d_dfbuf, 0, df_buf_words * 8, stream));
-        df_tag_base = 1;
-    }
-    DfArgs a{};
-    a.ops = d_prog; a.n_ops = n_ops; a.n_frames = n; a.tag_base = df_tag_base;
-    for (int b = 0; b < DB_N; ++b) { a.buf[b] = df_bufp[b]; a.buf_slot[b] = df_slot_words[b]; a.buf_w[b] = df_writes[b]; }
-    a.att = d_df_att; a.n_att = (int) df_att.size();
-    a.st = st; a.sp = sp; a.out_codes = d_codes; a.out_cap = codes_cap; a.err = d_err;
-    a.codec_embd = codec_embd; a.cp_embd = d_cp_embd; a.trailing = trailing; a.pad = pad;
-    a.logits0 = logits; a.logits_out = logits; a.hidden = hidden;
-    a.eps = c.rms_norm_eps; a.H = c.hidden_size; a.n_cb = c.n_codebooks;
-    a.V0 = c.codec_vocab_size; a.V1 = c.code_pred_vocab_size;
-    a.wbuf_bytes = (int) df_wbuf; a.work_bytes = (int) df_work;
-    a.first[0] = df_first[0]; a.first[1] = df_first[1];
-    a.n_pf0 = n_df_pf0;
-    for (int k = 0; k < n_df_pf0; ++k) a.pf0[k] = df_pf0[k];
-    df_tag_base += (unsigned)((n + 1) * n_ops);
-    a.trace = nullptr;
-    trace_n = 0;
-    if (getenv("QTTS_DF_TRACE")) {
-        const size_t need = (size_t) n * n_ops * DF_TRACE;
-        if (need > trace_cap) {
-            if (d_trace) cudaFree(d_trace);
-            d_trace = nullptr;
-            QCHECK(cudaMalloc(&d_trace, sizeof(unsigned long long) * need));
-            trace_cap = need;
+    const int H = c.hidden_size, NH = c.n_attention_heads, NKV = c.n_key_value_heads;
+    const int G = NH / NKV, GD = G * QTTS_HD, rows_g = GD + 2 * QTTS_HD, NG = c.n_codebooks - 1;
+    const int V1 = c.code_pred_vocab_size;
+    FfFrame fr{};
+    fr.st = st; fr.err = d_err; fr.sp = sp; fr.out_codes = d_codes; fr.out_cap = codes_cap;
+    fr.codec_embd = codec_embd; fr.cp_embd = d_cp_embd; fr.hidden = hidden; fr.trailing = trailing; fr.pad = pad;
+    fr.H = H; fr.n_cb = c.n_codebooks; fr.V0 = c.codec_vocab_size; fr.V1 = V1; fr.eps = c.rms_norm_eps;
+    fr.trace = d_fftrace; fr.trace_frame = 1;
+    std::vector<FfLaunch> Ls;
+    const size_t cp_layer = (size_t) cp_ctx * NKV * QTTS_HD, t_layer = (size_t) n_ctx * NKV * QTTS_HD;
+    const double es = L[0].qkv.type == W_Q8_0 ? 34.0 / 32.0 : 2.0;
+    // one stack (code-predictor pass or talker step); in_mode/cb: the first layer's sampler
+    auto stack = [&](bool cp, int pass, int in_mode, int cb, const float * in_logits) {
+        std::vector<LayerW> & LW = cp ? CPL : L;
+        std::vector<FfLayerW> & FW = cp ? ffCP : ffL;
+        const FfStack & S = cp ? ffs_cp : ffs_t;
+        const int nv = cp && pass == 0 ? 2 : 1;
+        for (size_t il = 0; il < LW.size(); ++il) {
+            const LayerW & l = LW[il];
+            FfLaunch A{};
+            A.kind = 0; A.nv = nv; A.grid = NKV * ff_CA; A.cluster = ff_CA; A.stage = cp ? STG_CP : STG_TALKER;
+            A.samples = il == 0;
+            FfAttnArgs & a = A.a;
+            a.fr = fr;
+            if (il == 0) { a.in.mode = in_mode; a.in.cb = cb; a.in.logits = in_logits; }
+            else { a.in.mode = FIN_PART; a.in.base = ff_xmid; a.in.part = ff_part_d; a.in.np = S.N / S.C; }
+            a.in.x_out = ff_xres;
+            a.nv = nv; a.qkv = FW[il].qkv_g; a.attn_norm = l.attn_norm; a.o = FW[il].o_g;
+            a.qkv_buf = qkv; a.att_buf = att; a.part_out = ff_part_o;
+            if (cp) {
+                a.att = fused_attn_args(l, cpk + il * cp_layer, cpv + il * cp_layer, rope_cp, nv, nullptr,
+                                        pass == 0 ? 0 : pass + 1, pass == 0, nullptr, cp_ctx);
+                a.att_kind = pass == 0 ? FF_ATT_UNIT : FF_ATT_CPSTEP;
+                a.n_past = pass == 0 ? 0 : pass + 1;
+            } else {
+                a.att = fused_attn_args(l, kc + il * t_layer, vc + il * t_layer, rope_t, 1, &st->pos, 0, false,
+                                        attn_dump && (int) il == attn_layer ? d_attn : nullptr, n_ctx);
+                a.att_kind = FF_ATT_UNIT;
+            }
+            A.smem = ff_attn_smem(l.qkv, l.o, H, rows_g, GD, ff_CA, nv, cp ? 2 : ff_max_keys);
+            a.work_bytes = 0;
+            A.bytes = es * ((double) l.qkv.rows * l.qkv.cols + (double) l.o.rows * l.o.cols);
+            ff_regions(A.w, FW[il].qkv_g);
+            ff_regions(A.w, FW[il].o_g);
+            Ls.push_back(A);
+            FfLaunch B{};
+            B.kind = 1; B.nv = nv; B.grid = S.N; B.cluster = S.C; B.stage = A.stage;
+            FfFfnArgs & f = B.f;
+            f.fr = fr;
+            f.in.mode = FIN_PART; f.in.base = ff_xres; f.in.part = ff_part_o; f.in.np = NKV; f.in.x_out = ff_xmid;
+            f.nv = nv; f.gate = l.gate; f.up = l.up; f.ffn_norm = l.ffn_norm; f.down = FW[il].down_r; f.R = S.R;
+            f.part_out = ff_part_d;
+            f.set_presence = cp && pass == 0 && il == 0;
+            f.work_bytes = (int) ff_ffn_work(l.down.type, H, nv, S.R);
+            B.smem = ff_ffn_smem(l.gate, l.down, H, nv, S.R);
+            B.bytes = es * 3.0 * (double) l.gate.rows * l.gate.cols;
+            ff_regions(B.w, l.gate);
+            ff_regions(B.w, l.up);
+            ff_regions(B.w, FW[il].down_r);
+            Ls.push_back(B);
         }
-        QCHECK(cudaMemsetAsync(d_trace, 0, sizeof(unsigned long long) * need, stream));
-        a.trace = d_trace;
-        trace_n = need;
+        FfLaunch Hd{};
+        Hd.kind = 2; Hd.nv = 1; Hd.cluster = 1; Hd.stage = cp ? STG_CP : STG_TALKER;
+        FfHeadArgs & h = Hd.h;
+        const DMat & hm = cp ? cp_head[pass] : codec_head;
+        int ncta = 0;
+        size_t slice = 0, smem = 0;
+        h.g = make_gemv(hm, nullptr, nullptr, H, 1, cp ? cp_out_norm : out_norm, ACT_F16, cp ? cp_logits : logits,
+                        hm.rows, nullptr, 0, EPI_STORE, cp ? nullptr : hidden, H, nullptr, &ncta, &slice, &smem);
+        h.slice_bytes = slice;
+        h.base = ff_xmid; h.part = ff_part_d; h.np = S.N / S.C; h.nv_in = nv; h.in_row = nv - 1;
+        h.st = st; h.err = d_err; h.frame_end = cp ? 0 : 1;
+        Hd.grid = ncta; Hd.smem = smem;
+        Hd.bytes = (hm.type == W_Q8_0 ? 34.0 / 32.0 : 2.0) * (double) hm.rows * hm.cols;
+        ff_regions(Hd.w, hm);
+        Ls.push_back(Hd);
+        return ncta > 0;
+    };
+    for (int g = 0; g < NG; ++g)
+        if (!stack(true, g, g == 0 ? FIN_CB0 : FIN_CBG, g, g == 0 ? logits : cp_logits)) { err = "fused frame: head shape"; return false; }
+    if (!stack(false, 0, FIN_TALKER, NG, cp_logits)) { err = "fused frame: head shape"; return false; }
+    if (d_fftrace && Ls.size() > 256) { err = "fused frame: too many launches to trace"; return false; }
+    ff_kinds.clear();
+    for (size_t i = 0; i < Ls.size(); ++i) {
+        Ls[i].a.launch_id = Ls[i].f.launch_id = Ls[i].h.launch_id = (int) i;
+        Ls[i].h.fr = fr;
+        ff_kinds.push_back(Ls[i].kind * 4 + (Ls[i].samples ? 2 : 0) + (Ls[i].nv - 1));
     }
-    QCHECK(cudaMemsetAsync(d_err, 0, sizeof(int), stream));
-    void * args[] = {&a};
-    QCHECK(cudaLaunchCooperativeKernel((const void *) k_frame_dataflow, dim3(n_sm), dim3(DF_THREADS), args, df_dyn,
-                                       stream));
-    ++launches;
+    // each launch prefetches the weights of the next two into L2
+    for (size_t i = 0; i < Ls.size(); ++i) {
+        FfPrefetch pf{};
+        for (size_t k = i + 1; k < Ls.size() && k <= i + 2; ++k)
+            for (auto & r : Ls[k].w)
+                if (pf.n < FF_MAX_PF) { pf.p[pf.n] = r.first; pf.bytes[pf.n] = r.second; ++pf.n; }
+        if (Ls[i].kind == 0) Ls[i].a.pf = pf;
+        else if (Ls[i].kind == 1) Ls[i].f.pf = pf;
+        else Ls[i].h.pf = pf;
+    }
+    for (auto & X : Ls) {
+        cudaLaunchConfig_t cfgl{};
+        cfgl.gridDim = dim3(X.grid);
+        cfgl.blockDim = dim3(FF_THREADS);
+        cfgl.dynamicSmemBytes = X.smem;
+        cfgl.stream = stream;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        at[1].id = cudaLaunchAttributeClusterDimension;
+        at[1].val.clusterDim.x = (unsigned) X.cluster;
+        at[1].val.clusterDim.y = 1;
+        at[1].val.clusterDim.z = 1;
+        cfgl.attrs = at;
+        cfgl.numAttrs = X.kind == 2 ? 1 : 2;
+        prof_stage = X.stage;
+        // profile classes: a launch that samples is charged to sampling (it also runs its
+        // pass's first attention block), other attention blocks to attention, the rest to GEMV
+        prof_begin(X.kind == 0 ? (X.samples ? KC_SAMPLE : KC_ATTN) : KC_GEMV, X.bytes);
+        cudaError_t e;
+        if (X.kind == 0) e = X.nv == 2 ? cudaLaunchKernelEx(&cfgl, k_ff_attn<2>, X.a) : cudaLaunchKernelEx(&cfgl, k_ff_attn<1>, X.a);
+        else if (X.kind == 1) e = X.nv == 2 ? cudaLaunchKernelEx(&cfgl, k_ff_ffn<2>, X.f) : cudaLaunchKernelEx(&cfgl, k_ff_ffn<1>, X.f);
+        else e = cudaLaunchKernelEx(&cfgl, k_ff_head, X.h);
+        prof_end();
+        if (e != cudaSuccess) { err = std::string("fused frame launch: ") + cudaGetErrorString(e); return false; }
+        ++launches;
+    }
+    prof_stage = STG_TALKER;
     return true;
 }
 
@@ -1347,13 +1386,13 @@ int Engine::begin(const qtts_generate_params * p) {
         if (d_codes) cudaFree(d_codes);
         codes_cap = std::max(p->max_len, 256);
         if (cudaMalloc(&d_codes, sizeof(int) * codes_cap * c.n_codebooks) != cudaSuccess) { err = "alloc codes"; return -1; }
-        graph_ok = false; prog_ok = false;
+        graph_ok = false;
     }
     if (std::max(tlen, 1) > trailing_cap) {
         if (trailing) cudaFree(trailing);
         trailing_cap = std::max(tlen, 256);
         if (cudaMalloc(&trailing, sizeof(float) * trailing_cap * H) != cudaSuccess) { err = "alloc trailing"; return -1; }
-        graph_ok = false; prog_ok = false;
+        graph_ok = false;
     }
     if (attn_dump) {
         const size_t need = (size_t) p->max_len * c.n_attention_heads * n_ctx;
@@ -1361,7 +1400,7 @@ int Engine::begin(const qtts_generate_params * p) {
             if (d_attn) cudaFree(d_attn);
             attn_cap = need;
             if (cudaMalloc(&d_attn, sizeof(float) * attn_cap) != cudaSuccess) { err = "alloc attn dump"; return -1; }
-            graph_ok = false; prog_ok = false;
+            graph_ok = false;
         }
     }
     if (h_dbg_cap > 0 && (h_dbg_t || h_dbg_cp)) {
@@ -1401,14 +1440,14 @@ int Engine::begin(const qtts_generate_params * p) {
         cudaMemcpyAsync(hidden0, hidden, sizeof(float) * H, cudaMemcpyDeviceToDevice, stream) != cudaSuccess) {
         err = "snapshot prefill outputs"; return -1;
     }
+    if (d_err && cudaMemsetAsync(d_err, 0, sizeof(int), stream) != cudaSuccess) { err = "reset error flag"; return -1; }
     if (!sync("generate setup")) return -1;
     sess.st0 = hs;
-    if (use_dataflow) {
+    if (frame_mode == FM_FUSED) {
         const int keys = std::min(n_ctx, plen + p->max_len + 1);   // the talker attention's longest row
-        if ((!prog_ok || keys > df_keys) && !build_program(std::max(keys, df_keys))) return -1;
-        if (!graph_ok) { launches = 0; graph_ok = false; }
-        launches_per_frame = 1;
-    } else if (!graph_ok && !capture_graph()) return -1;
+        if (keys > ff_max_keys) { ff_max_keys = std::max(keys, 512); graph_ok = false; }
+    }
+    if (!graph_ok && !capture_graph()) return -1;
     sess.active = true;
     sess.max_len = p->max_len;
     sess.prefill_len = plen;
@@ -1442,17 +1481,15 @@ int Engine::run_frames(int n, int32_t * codes_out) {
     n = std::min(n, sess.max_len - sess.produced);
     if (n <= 0) return 0;
     if (cudaEventRecord(ev0, stream) != cudaSuccess) { err = "event"; return -1; }
-    const bool staged = stage_timing && !use_dataflow;
+    const bool staged = stage_timing;
     if (staged) {   // kernel by kernel, events around every launch
         profiling = true;
         prof_evs.clear();
         ev_used = 0;
         bool ok = true;
-        for (int i = 0; i < n && ok; ++i) ok = enqueue_frame();
+        for (int i = 0; i < n && ok; ++i) ok = frame_mode == FM_FUSED ? enqueue_frame_ff() : enqueue_frame();
         profiling = false;
         if (!ok) return -1;
-    } else if (use_dataflow) {
-        if (!launch_dataflow(n)) return -1;
     } else {
         for (int i = 0; i < n; ++i)
             if (cudaGraphLaunch(graph, stream) != cudaSuccess) { err = "graph launch failed"; return -1; }
@@ -1461,11 +1498,11 @@ int Engine::run_frames(int n, int32_t * codes_out) {
     DevState hs;
     int kerr = 0;
     if (cudaMemcpyAsync(&hs, st, sizeof(hs), cudaMemcpyDeviceToHost, stream) != cudaSuccess) { err = "state readback"; return -1; }
-    if (use_dataflow && cudaMemcpyAsync(&kerr, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) {
+    if (frame_mode == FM_FUSED && cudaMemcpyAsync(&kerr, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) {
         err = "error flag readback"; return -1;
     }
     if (!sync("frame loop")) return -1;
-    if (kerr) { err = "dataflow frame kernel: a wait timed out"; sess.active = false; return -1; }
+    if (kerr) { err = "fused frame kernels: a wait timed out"; sess.active = false; return -1; }
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, ev0, ev1);
     timing.frames_ms += ms;
@@ -1480,8 +1517,6 @@ int Engine::run_frames(int n, int32_t * codes_out) {
             else stages.talker_ms += t;
         }
         prof_evs.clear();
-        stages.frames += got;
-    } else if (stage_timing) {   // one dataflow launch: the frame time as a whole
         stages.frames += got;
     }
     if (got > 0 && codes_out) {
@@ -2045,7 +2080,7 @@ int32_t qtts_set_attn_dump(qtts_engine * h, int32_t enabled, int32_t layer) {
     if (layer < 0 || layer >= E.cfg.n_layers) { E.err = "attn dump layer out of range"; return 0; }
     E.attn_dump = enabled != 0;
     E.attn_layer = layer;
-    E.graph_ok = false; E.prog_ok = false;
+    E.graph_ok = false;
     return 1;
 }
 
@@ -2071,7 +2106,7 @@ int32_t qtts_profile_frames(qtts_engine * h, int32_t n, qtts_kernel_stats * out,
     E.prof_evs.clear();
     E.ev_used = 0;
     bool ok = true;
-    for (int i = 0; i < n && ok; ++i) ok = E.enqueue_frame();
+    for (int i = 0; i < n && ok; ++i) ok = E.frame_mode == Engine::FM_FUSED ? E.enqueue_frame_ff() : E.enqueue_frame();
     E.profiling = false;
     qtts::DevState hs;
     cudaMemcpyAsync(&hs, E.st, sizeof(hs), cudaMemcpyDeviceToHost, E.stream);
@@ -2091,24 +2126,21 @@ int32_t qtts_profile_frames(qtts_engine * h, int32_t n, qtts_kernel_stats * out,
     return got;
 }
 
-// Diagnostics of the dataflow frame kernel (QTTS_DF_TRACE=1 at run time): the op
-// list of the frame program (type * 16 + prologue per op) and the per-op stamps of
-// the last launch ([frame][op][4]).  Both return the number of values available.
-int32_t qtts_frame_ops(const qtts_engine * h, int32_t * ops, int32_t cap) {
+
+int32_t qtts_frame_trace(const qtts_engine * h, unsigned long long * out, int32_t cap, int32_t * kinds, int32_t kcap) {
     if (!h) return -1;
     const Engine & E = *reinterpret_cast<const Engine *>(h);
-    const int n = (int) E.prog.size();
-    for (int i = 0; i < n && i < cap; ++i) ops[i] = E.prog[i].type * 16 + E.prog[i].pro;
+    if (!E.d_fftrace) return 0;
+    const int n = (int) E.ff_kinds.size();
+    for (int i = 0; i < n && i < kcap; ++i) kinds[i] = E.ff_kinds[i];
+    const size_t words = (size_t) n * qtts::FF_TRACE_CTAS * qtts::FF_TRACE_N;
+    if (out && cap > 0) cudaMemcpy(out, E.d_fftrace, sizeof(unsigned long long) * std::min(words, (size_t) cap), cudaMemcpyDeviceToHost);
     return n;
 }
-int32_t qtts_frame_trace(const qtts_engine * h, unsigned long long * out, int32_t cap) {
+
+int32_t qtts_get_frame_mode(const qtts_engine * h) {
     if (!h) return -1;
-    const Engine & E = *reinterpret_cast<const Engine *>(h);
-    if (!E.d_trace || !E.trace_n) return 0;
-    cudaSetDevice(E.dev);
-    const size_t n = std::min(E.trace_n, (size_t) std::max(cap, 0));
-    if (out && n) cudaMemcpy(out, E.d_trace, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost);
-    return (int32_t) E.trace_n;
+    return reinterpret_cast<const Engine *>(h)->frame_mode;
 }
 
 int32_t qtts_set_stage_timing(qtts_engine * h, int32_t enabled) {

@@ -115,8 +115,8 @@ def lib():
         "qtts_attn_row": (C.c_int32, [C.c_void_p, C.c_int32, _f32p, C.c_int32]),
         "qtts_get_timing": (C.c_int32, [C.c_void_p, C.POINTER(Timing)]),
         "qtts_set_stage_timing": (C.c_int32, [C.c_void_p, C.c_int32]),
-        "qtts_frame_ops": (C.c_int32, [C.c_void_p, _i32p, C.c_int32]),
-        "qtts_frame_trace": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64), C.c_int32]),
+        "qtts_get_frame_mode": (C.c_int32, [C.c_void_p]),
+        "qtts_frame_trace": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64), C.c_int32, _i32p, C.c_int32]),
         "qtts_get_stage_timing": (C.c_int32, [C.c_void_p, C.POINTER(StageTiming)]),
         "qtts_profile_frames": (C.c_int32, [C.c_void_p, C.c_int32, C.POINTER(KernelStats), C.c_int32]),
         "qtts_batch_create": (C.c_void_p, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
@@ -242,10 +242,21 @@ class Engine:
     def set_seed(self, seed: int):
         lib().qtts_set_seed(self.h, int(seed))
 
-    @staticmethod
-    def frame_kernel() -> str:
-        """Name of the kernel that runs the frames (QTTS_FRAME_MODE selects it)."""
-        return "k_frame_dataflow" if os.environ.get("QTTS_FRAME_MODE") == "dataflow" else "frame_graph"
+    def frame_trace(self):
+        """(kinds [n_launches], stamps [n_launches][256][8]) of frame 1 of the last
+        run with QTTS_FF_TRACE=1 at load time (ns, %globaltimer, 0 = not reached);
+        kinds: kind * 4 + (samples ? 2 : 0) + rows - 1, kind 0 attention block, 1
+        FFN block, 2 head."""
+        kinds = np.zeros(512, np.int32)
+        n = lib().qtts_frame_trace(self.h, None, 0, _p(kinds, C.c_int32), 512)
+        tr = np.zeros((max(n, 1), 256, 8), np.uint64)
+        lib().qtts_frame_trace(self.h, tr.ctypes.data_as(C.POINTER(C.c_uint64)), tr.size, _p(kinds, C.c_int32), 512)
+        return kinds[:n], tr[:n]
+
+    def frame_mode(self) -> str:
+        """The frame path: "graph" (one kernel per op, the default) or "fused" (two
+        clustered kernels per layer; QTTS_FRAME_MODE=fused at load time)."""
+        return "fused" if lib().qtts_get_frame_mode(self.h) == 1 else "graph"
 
     def timing(self) -> dict:
         t = Timing()
@@ -336,20 +347,6 @@ class Engine:
             raise RuntimeError("profile_frames failed: " + self.error())
         return {"frames": got, **{KERNEL_CLASSES[i]: dict(launches=st[i].launches, ms=st[i].total_ms, bytes=st[i].bytes)
                                   for i in range(4)}}
-
-    def frame_trace(self):
-        """(ops [n_ops] = type * 16 + prologue, stamps [frames * n_ops][10]) of the last
-        dataflow launch with QTTS_DF_TRACE=1 (ns, %globaltimer; CTA 0 unless noted):
-        start, input ready, latest input ready over the CTAs, weights ready, first
-        output row stored, last output row stored, op done, next copies issued, past
-        the first end-of-op barrier, past the second."""
-        n = lib().qtts_frame_ops(self.h, None, 0)
-        ops = np.zeros(max(n, 1), np.int32)
-        lib().qtts_frame_ops(self.h, _p(ops, C.c_int32), n)
-        m = lib().qtts_frame_trace(self.h, None, 0)
-        tr = np.zeros(max(m, 1), np.uint64)
-        lib().qtts_frame_trace(self.h, tr.ctypes.data_as(C.POINTER(C.c_uint64)), m)
-        return ops[:n], tr[:m].reshape(-1, 10)
 
     def run_frames(self, n: int, codes_out: np.ndarray | None = None) -> int:
         ptr = None if codes_out is None else _p(codes_out, C.c_int32)

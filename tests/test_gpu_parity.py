@@ -274,24 +274,23 @@ def test_full_f16_config3_sampled(qtts, full_f16):
     eng.close()
 
 
-def test_dataflow_kernel_matches_graph_path(qtts, tiny_f16, tiny_q8, monkeypatch):
-    """The dataflow frame kernel and the kernel-per-op CUDA graph run the same
-    GEMV rows, attention, samplers and input sums in the same reduction orders:
-    greedy codes and all logits are identical."""
+def test_both_frame_paths_match_the_oracle(qtts, tiny_f16, tiny_q8, monkeypatch):
+    """The fused frame path (two clustered kernels per layer) and the
+    kernel-per-op CUDA graph each equal the oracle in their own reduction order:
+    greedy codes and every logit, bit for bit (the two paths differ from each
+    other only in how the O-projection and ffn_down are summed)."""
     rng = np.random.default_rng(25)
     text = text_ids(rng, 26)
+    kw = dict(speaker=np.zeros(256, np.float32), eos_bias=-1e9, rep_penalty=1.05)
     for path in (tiny_f16, tiny_q8):
-        outs = []
-        for mode in ("graph", "dataflow"):
+        for mode in ("graph", "fused"):
             monkeypatch.setenv("QTTS_FRAME_MODE", mode)
             eng = qtts.Engine(path, 0)
-            outs.append(eng.generate(text, 20, speaker=np.zeros(256, np.float32), eos_bias=-1e9,
-                                     rep_penalty=1.05, want_logits=True))
+            assert eng.frame_mode() == mode
+            e = eng.generate(text, 20, want_logits=True, **kw)
             eng.close()
-        a, b = outs
-        assert np.array_equal(a["codes"], b["codes"])
-        assert np.array_equal(a["talker_logits"][:20], b["talker_logits"][:20])
-        assert np.array_equal(a["cp_logits"], b["cp_logits"])
+            _check_follow(Oracle(path, threads=4, frame_split=mode == "fused"), e, f"{mode}", text=text, max_len=20,
+                          **kw)
 
 
 @pytest.mark.gpu
@@ -301,7 +300,7 @@ def test_rewind_replays_the_utterance(qtts, tiny_f16, monkeypatch):
     frame modes."""
     rng = np.random.default_rng(31)
     text = text_ids(rng, 20)
-    for mode in ("dataflow", "graph"):
+    for mode in ("fused", "graph"):
         monkeypatch.setenv("QTTS_FRAME_MODE", mode)
         eng = qtts.Engine(tiny_f16, 0)
         eng.generate_begin(text, 12, speaker=np.zeros(256, np.float32), eos_bias=-1e9, rep_penalty=1.05)
