@@ -145,6 +145,7 @@ struct Engine {
     FfStack ffs_t, ffs_cp;
     size_t ff_head_smem_t = 0, ff_head_smem_cp = 0;
     int ff_max_keys = 0;          // the talker attention row length the captured frame serves
+    int ff_pf_ahead = 1;          // launches whose weights each launch prefetches into L2 (QTTS_FF_PF)
     std::string ff_why;           // why the fused path is off (empty: on)
     unsigned long long * d_fftrace = nullptr;   // QTTS_FF_TRACE=1: stamps of frame 1's launches
     std::vector<int> ff_kinds;    // per launch of the frame: kind * 4 + (samples ? 2 : 0) + (nv - 1)
@@ -921,6 +922,7 @@ bool Engine::ff_prepare() {
         QCHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     }
     QCHECK(cudaFuncSetAttribute(k_ff_head, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX));
+    if (const char * v = getenv("QTTS_FF_PF")) ff_pf_ahead = std::max(0, atoi(v));
     if (getenv("QTTS_FF_TRACE")) {
         const size_t n = (size_t) 256 * FF_TRACE_CTAS * FF_TRACE_N;
         QCHECK(cudaMalloc(&d_fftrace, n * sizeof(unsigned long long)));
@@ -1084,7 +1086,7 @@ bool Engine::enqueue_frame_ff() {
     // each launch prefetches the weights of the next two into L2
     for (size_t i = 0; i < Ls.size(); ++i) {
         FfPrefetch pf{};
-        for (size_t k = i + 1; k < Ls.size() && k <= i + 2; ++k)
+        for (size_t k = i + 1; k < Ls.size() && k <= i + (size_t) ff_pf_ahead; ++k)
             for (auto & r : Ls[k].w)
                 if (pf.n < FF_MAX_PF) { pf.p[pf.n] = r.first; pf.bytes[pf.n] = r.second; ++pf.n; }
         if (Ls[i].kind == 0) Ls[i].a.pf = pf;

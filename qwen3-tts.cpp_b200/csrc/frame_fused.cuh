@@ -329,7 +329,7 @@ __device__ __forceinline__ void ff_drain(uint64_t * m, unsigned parity) {
 // weight buffer (the q|k|v slice + attn_norm gain, later the O slice) and the
 // work area (activation rows, then the attention scratch, then the O input).
 template <int NV>
-__global__ void __launch_bounds__(FF_THREADS) k_ff_attn(const FfAttnArgs A) {
+__global__ void __launch_bounds__(FF_THREADS, 2) k_ff_attn(const FfAttnArgs A) {
     extern __shared__ __align__(128) uint8_t ff_smem[];
     __shared__ __align__(8) uint64_t mbar[2];
     const int tid = threadIdx.x;
