@@ -52,7 +52,7 @@ CONFIGS = {
     "q8long": dict(wtype="q8_0", utts_per_gpu=32, p_lo=512, p_hi=512, frames=4096, e2e_frames=256,
                    workload="BASELINE configs[4]: long-form Q8_0 serving, 32 utterances per GPU (256 on 8), "
                             "ICL prefill 512, up to 4096 greedy frames each, paged F16 KV; Q8_0 projections as "
-                            "8-row GEMV chunks, F16 heads as tcgen05 GEMMs"),
+                            "kind::i8 tcgen05 GEMMs, F16 heads as kind::f16 tcgen05 GEMMs"),
 }
 
 
@@ -357,8 +357,9 @@ def run_batch(args, cfg):
     wkey = "f16" if cfg["wtype"] == "f16" else "q8"
     frame_bytes = WEIGHT_BYTES[wkey] + B * (KV_TALKER_PER_POS * kv_mean + KV_CP_PER_POS * 135)
     achieved = frame_bytes / (frame_ms / 1e3) / 1e9
-    # ncu DRAM / algorithmic bytes of the batched projections (tcgen05 GEMMs for F16, 8-row GEMVs for Q8_0)
-    ratio = _profile_figure("k_gemm_tc_batch16.md" if wkey == "f16" else "k_gemv_q8.md", "dram_bytes_per_algorithmic_byte")
+    # ncu DRAM / algorithmic bytes of the batched projections (kind::f16 / kind::i8 tcgen05 GEMMs)
+    ratio = _profile_figure("k_gemm_tc_batch16.md" if wkey == "f16" else "k_gemm_q8_batch32.md",
+                            "dram_bytes_per_algorithmic_byte")
     traffic = ratio * frame_bytes if ratio else None
     flops = 2.0 * (WEIGHT_BYTES["f16"] / 2.0) * B
     weak = "utts_per_gpu" in cfg
@@ -373,7 +374,7 @@ def run_batch(args, cfg):
                    "parallelism": f"LPT utterance sharding over {world} GPU(s), one batch per GPU",
                    "l2": "inputs larger than L2 (3.3 GB of weights + KV streamed per frame), no flush"},
         "roofline": {"bound": "hbm", "kernel": "batched frame (CUDA graph: tcgen05 GEMMs + paged attention)" if wkey == "f16"
-                     else "batched frame (CUDA graph: Q8_0 GEMV chunks, tcgen05 heads, paged attention)",
+                     else "batched frame (CUDA graph: kind::i8 tcgen05 GEMMs, kind::f16 heads, paged attention)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "frame_algorithmic_bytes": frame_bytes, "launches_per_frame": tm["launches_per_frame"],

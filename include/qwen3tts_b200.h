@@ -205,6 +205,19 @@ int32_t qtts_get_stage_timing(const qtts_engine * e, qtts_stage_timing * out);
  * Returns frames produced or -1.  For measurement only. */
 int32_t qtts_profile_frames(qtts_engine * e, int32_t n, qtts_kernel_stats * stats, int32_t n_classes);
 
+/* One Q8_0 GEMM on the tcgen05 tensor cores (kind::i8) as the batched path runs
+ * it for Q8_0 models (test entry; no reference counterpart; replaces the Q8_0
+ * ggml_mul_mat calls of src/tts_transformer.cpp:1659-1661, 1739-1750 for many
+ * sequences at once).  w (and w_up for SwiGLU): GGUF Q8_0 blocks [rows][cols/32]
+ * of 34 bytes (f16 d, 32 int8).  The activations x[m x cols] (optionally
+ * RMSNorm-ed with norm_gain) are quantised per 32-block as quantize_row_q8_0;
+ * y[m][r] = sum over blocks b in order of (float) isum_b * (d_w * d_a), the
+ * k-split partials (ksplit CTAs per 128-row tile; 0 = the engine's choice) added
+ * in rank order.  epi as qtts_op_gemm_tc.  rows (x2 for SwiGLU) % 128 == 0,
+ * cols % 128 == 0, m <= 128.  Returns the k-split used (>= 1), 0 on failure. */
+int32_t qtts_op_gemm_q8(int32_t device, const uint8_t * w, const uint8_t * w_up, int32_t rows, int32_t cols,
+                        const float * xin, int32_t m, const float * norm_gain, float eps, int32_t epi,
+                        const float * resid, int32_t ksplit, float * y);
 /* One tcgen05 tensor-core GEMM as the batched and prefill paths run it
  * (test entry; no reference counterpart): y[m][r] = sum_k W[r][k] * a[m][k],
  * W F16 row-major [rows x cols] (host), activations a = x[m x cols] after an

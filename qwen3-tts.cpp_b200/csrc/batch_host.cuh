@@ -6,6 +6,7 @@ namespace qtts {
 
 struct TiledLayer {
     uint8_t * qkv = nullptr, * o = nullptr, * gu = nullptr, * down = nullptr;
+    __half * sqkv = nullptr, * so = nullptr, * sgu = nullptr, * sdown = nullptr;   // Q8_0 block scales (q8_s_off)
 };
 
 // A weight matrix (or a gate/up pair, interleaved in 64-row groups) copied
@@ -53,6 +54,34 @@ struct TcGemm {
     }
 };
 
+// Q8_0 projection of m F32 rows on the tensor cores: quantise the rows per
+// 32-block into xq / xqs (k_pack_q8, optional RMSNorm), then the kind::i8 GEMM.
+// Returns the number of launches.
+inline int q8_project(cudaStream_t stream, uint8_t * xq, float * xqs, int * d_err, float eps, const uint8_t * wt,
+                      const __half * ws, int rows_w, int cols, const float * xin, int ldx, int m, const float * norm,
+                      int epi, float * y, int ldy, const float * resid) {
+    const int mp = (m + 15) / 16 * 16;
+    PackQ8Args pa{};
+    pa.x = xin; pa.ldx = ldx; pa.m_real = m; pa.np = mp; pa.cols = cols; pa.gain = norm;
+    pa.eps = eps; pa.out = xq; pa.dscale = xqs;
+    pdl_launch(k_pack_q8, dim3(mp), dim3(256), 0, stream, pa);
+    GemmQ8Args g{};
+    g.w = wt; g.ws = ws; g.x = xq; g.xs = xqs; g.rows_w = rows_w; g.cols = cols; g.np = mp; g.m_real = m;
+    g.epi = epi; g.y = y; g.ldy = ldy; g.resid = resid; g.ldr = ldy; g.err = d_err;
+    g.ksplit = q8_choose_split(g);
+    q8_launch(g, stream);
+    return 2;
+}
+
+// Tiles of a Q8_0 matrix (or gate/up pair) and its block scales for k_gemm_q8.
+inline bool tile_q8_check(const DMat & W, const DMat * W2, std::string & err) {
+    const int rows_w = W2 ? 2 * W.rows : W.rows;
+    if (W.type != W_Q8_0 || rows_w % TC_BM || W.cols % Q8_BK || (W2 && W.rows % (TC_BM / 2))) {
+        err = "Q8_0 tensor-core path: matrix shape"; return false;
+    }
+    return true;
+}
+
 struct BatchEngine {
     Engine * E = nullptr;
     int dev = 0;
@@ -61,7 +90,9 @@ struct BatchEngine {
     int Bmax = 0, B = 0, n_max = 0, max_frames = 0, max_pages = 0, n_pages = 0, trail_cap = 0;
     int H = 0, NH = 0, NKV = 0, QD = 0, KD = 0, QKVD = 0, FF = 0, CFF = 0, V0 = 0, V1 = 0, NCB = 0;
     std::vector<TiledLayer> TL, TCP;
-    bool q8 = false;   // Q8_0 layer weights: projections through k_gemv in 8-row chunks (heads stay F16 tcgen05)
+    bool q8 = false;   // Q8_0 layer weights: projections as kind::i8 tcgen05 GEMMs (heads stay F16 tcgen05)
+    uint8_t * xq = nullptr;                 // Q8_0 activation tiles
+    float * xqs = nullptr;                  // their block scales
     std::vector<uint8_t *> cp_head_t;
     uint8_t * codec_head_t = nullptr;
     std::vector<void *> owned;
@@ -120,6 +151,13 @@ struct BatchEngine {
         if (stream) cudaStreamDestroy(stream);
     }
 
+    bool tile_q8(const DMat & W, const DMat * W2, uint8_t ** out, __half ** sout) {
+        const int rows_w = W2 ? 2 * W.rows : W.rows;
+        if (!tile_q8_check(W, W2, err)) return false;
+        if (!alloc(out, (size_t) rows_w * W.cols) || !alloc(sout, (size_t) rows_w * (W.cols / 32) * 2)) return false;
+        k_tile_q8<<<rows_w, 128, 0, stream>>>(W, W2 ? *W2 : DMat{}, rows_w, *out, *sout);
+        return cudaGetLastError() == cudaSuccess;
+    }
     bool tile(const DMat & W, const DMat * W2, uint8_t ** out) {
         if (!tile_check(W, W2, err)) return false;
         if (!alloc(out, (size_t)(W2 ? 2 * W.rows : W.rows) * W.cols * 2)) return false;
@@ -150,8 +188,18 @@ struct BatchEngine {
                     return false;
             return true;
         };
+        auto tq = [&](std::vector<LayerW> & Ls, std::vector<TiledLayer> & T) {
+            for (size_t i = 0; i < Ls.size(); ++i)
+                if (!tile_q8(Ls[i].qkv, nullptr, &T[i].qkv, &T[i].sqkv) || !tile_q8(Ls[i].o, nullptr, &T[i].o, &T[i].so) ||
+                    !tile_q8(Ls[i].gate, &Ls[i].up, &T[i].gu, &T[i].sgu) ||
+                    !tile_q8(Ls[i].down, nullptr, &T[i].down, &T[i].sdown))
+                    return false;
+            return true;
+        };
         q8 = E->L[0].qkv.type == W_Q8_0;
         if (!q8 && (!tl(E->L, TL) || !tl(E->CPL, TCP))) return false;
+        if (q8 && (!tq(E->L, TL) || !tq(E->CPL, TCP))) return false;
+        if (q8 && 2 * bmax > Q8_MAX_N) { err = "Q8_0 batches: max_batch must be <= 64"; return false; }
         cp_head_t.resize(E->cp_head.size());
         for (size_t g = 0; g < E->cp_head.size(); ++g)
             if (!tile(E->cp_head[g], nullptr, &cp_head_t[g])) return false;
@@ -166,6 +214,7 @@ struct BatchEngine {
             !alloc(&xt2, (size_t) TC_MAX_N * maxc * 2) ||
             !alloc(&st, sizeof(DevState) * Bmax) || !alloc(&sp, sizeof(SampleParams)) ||
             !alloc(&codes, sizeof(int) * Bmax * max_frames * NCB) || !alloc(&d_err, sizeof(int)) ||
+            !alloc(&xq, (size_t) Q8_MAX_N * maxc) || !alloc(&xqs, sizeof(float) * Q8_MAX_N * (maxc / 32)) ||
             !alloc(&d_max_len, sizeof(int) * Bmax))
             return false;
         trail_cap = 1024;
@@ -192,6 +241,7 @@ struct BatchEngine {
         const size_t tcs = 201 * 1024;
         if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) tcs) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+            q8_set_attributes() != cudaSuccess ||
             cudaFuncSetAttribute(k_attn_paged, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int) paged_attn_smem(n_max, NH / NKV)) != cudaSuccess) {
             err = "kernel attributes (context too long?)"; return false;
@@ -221,24 +271,14 @@ struct BatchEngine {
     }
     int gemm_cls = BC_GEMM_QKV;
 
-    // Q8_0 projection of m F32 rows: k_gemv over chunks of 8 rows (each row's
-    // int8 block dots and sums are the batch-1 GEMV's, bit for bit).
-    void gemv_rows(const DMat & A, const DMat * A2, const float * xin, int ldx, int m, const float * norm, int epi,
-                   float * y, int ldy, const float * resid) {
-        for (int r0 = 0; r0 < m; r0 += QTTS_MAX_NV) {
-            const int nv = std::min(QTTS_MAX_NV, m - r0);
-            int ncta = 0;
-            size_t slice = 0, smem = 0;
-            const GemvArgs a = E->make_gemv(A, A2, xin + (size_t) r0 * ldx, ldx, nv, norm, ACT_F16, y + (size_t) r0 * ldy,
-                                            ldy, resid ? resid + (size_t) r0 * ldy : nullptr, ldy, epi, nullptr, 0, nullptr,
-                                            &ncta, &slice, &smem);
-            pb(gemm_cls);
-            if (nv == 1) pdl_launch(k_gemv<1>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
-            else if (nv == 2) pdl_launch(k_gemv<2>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
-            else pdl_launch(k_gemv<8>, dim3(ncta), dim3(QTTS_WARPS * 32), smem, stream, a, slice);
-            pe();
-            launches += 1;
-        }
+    // Q8_0 projection of m F32 rows on the tensor cores: quantise the rows per
+    // 32-block (k_pack_q8, optional RMSNorm) and run the kind::i8 GEMM.
+    void gemm_q8(const uint8_t * wt, const __half * ws, int rows_w, int cols, const float * xin, int ldx, int m,
+                 const float * norm, int epi, float * y, int ldy, const float * resid) {
+        pb(gemm_cls);
+        launches += q8_project(stream, xq, xqs, d_err, E->cfg.rms_norm_eps, wt, ws, rows_w, cols, xin, ldx, m, norm, epi,
+                               y, ldy, resid);
+        pe();
     }
 
     // One decoder layer's four projections over `rows` rows of X: tcgen05 GEMMs
@@ -249,22 +289,22 @@ struct BatchEngine {
         switch (which) {
             case 0:
                 gemm_cls = BC_GEMM_QKV;
-                if (q8) gemv_rows(l.qkv, nullptr, X, H, rows, l.attn_norm, EPI_STORE, qkv, QKVD, nullptr);
+                if (q8) gemm_q8(t.qkv, t.sqkv, QKVD, H, X, H, rows, l.attn_norm, TC_EPI_STORE, qkv, QKVD, nullptr);
                 else gemm(t.qkv, QKVD, H, X, H, rows, l.attn_norm, TC_ACT_F16, TC_EPI_STORE, qkv, QKVD, nullptr);
                 break;
             case 1:
                 gemm_cls = BC_GEMM_O;
-                if (q8) gemv_rows(l.o, nullptr, att, cols_o, rows, nullptr, EPI_RESID, X, H, X);
+                if (q8) gemm_q8(t.o, t.so, H, cols_o, att, cols_o, rows, nullptr, TC_EPI_RESID, X, H, X);
                 else gemm(t.o, H, QD, nullptr, QD, rows, nullptr, TC_ACT_F16, TC_EPI_RESID, X, H, X);
                 break;
             case 2:
                 gemm_cls = BC_GEMM_GU;
-                if (q8) gemv_rows(l.gate, &l.up, X, H, rows, l.ffn_norm, EPI_SWIGLU, hbuf, ffn, nullptr);
+                if (q8) gemm_q8(t.gu, t.sgu, 2 * ffn, H, X, H, rows, l.ffn_norm, TC_EPI_SWIGLU, hbuf, ffn, nullptr);
                 else gemm(t.gu, 2 * ffn, H, X, H, rows, l.ffn_norm, TC_ACT_F16, TC_EPI_SWIGLU, hbuf, ffn, nullptr, nullptr, true);
                 break;
             default:
                 gemm_cls = BC_GEMM_DOWN;
-                if (q8) gemv_rows(l.down, nullptr, hbuf, ffn, rows, nullptr, EPI_RESID, X, H, X);
+                if (q8) gemm_q8(t.down, t.sdown, H, ffn, hbuf, ffn, rows, nullptr, TC_EPI_RESID, X, H, X);
                 else gemm(t.down, H, ffn, nullptr, ffn, rows, nullptr, TC_ACT_SPLIT, TC_EPI_RESID, X, H, X);
                 break;
         }
@@ -274,7 +314,7 @@ struct BatchEngine {
         const int rows = B * M;
         for (size_t il = 0; il < E->CPL.size(); ++il) {
             const LayerW & l = E->CPL[il];
-            const TiledLayer t = q8 ? TiledLayer{} : TCP[il];
+            const TiledLayer t = TCP[il];
             proj(0, l, t, xcp, rows, CFF);
             FusedAttn fa{};
             fa.qkv = qkv; fa.ldq = QKVD; fa.n_heads = NH; fa.n_kv_heads = NKV; fa.q_norm = l.q_norm;
@@ -297,7 +337,7 @@ struct BatchEngine {
         const int G = NH / NKV;
         for (size_t il = 0; il < E->L.size(); ++il) {
             const LayerW & l = E->L[il];
-            const TiledLayer t = q8 ? TiledLayer{} : TL[il];
+            const TiledLayer t = TL[il];
             proj(0, l, t, x, B, FF);
             PagedAttnArgs pa{};
             pa.qkv = qkv; pa.ldq = QKVD; pa.n_heads = NH; pa.n_kv_heads = NKV; pa.n_layers = (int) E->L.size();
@@ -496,6 +536,9 @@ struct PrefillTC {
     float * qkv = nullptr, * att = nullptr, * hbuf = nullptr;
     uint8_t * xt = nullptr, * xt2 = nullptr;
     int * d_err = nullptr;
+    bool q8 = false;                        // Q8_0 weights: kind::i8 GEMMs
+    uint8_t * xq = nullptr;
+    float * xqs = nullptr;
 
     template <class T>
     bool alloc(T ** p, size_t bytes) {
@@ -516,13 +559,27 @@ struct PrefillTC {
         const qtts_config & c = eng->cfg;
         const int R = PREFILL_TC_ROWS, H = c.hidden_size, QD = eng->QD(), FF = c.intermediate_size;
         TL.resize(E->L.size());
+        q8 = E->L[0].qkv.type == W_Q8_0;
+        auto tq = [&](const DMat & W, const DMat * W2, uint8_t ** out, __half ** sout) {
+            const int rows_w = W2 ? 2 * W.rows : W.rows;
+            if (!tile_q8_check(W, W2, err)) return false;
+            if (!alloc(out, (size_t) rows_w * W.cols) || !alloc(sout, (size_t) rows_w * (W.cols / 32) * 2)) return false;
+            k_tile_q8<<<rows_w, 128, 0, E->stream>>>(W, W2 ? *W2 : DMat{}, rows_w, *out, *sout);
+            return cudaGetLastError() == cudaSuccess;
+        };
         for (size_t i = 0; i < E->L.size(); ++i) {
             LayerW & l = E->L[i];
-            if (!tile(l.qkv, nullptr, &TL[i].qkv) || !tile(l.o, nullptr, &TL[i].o) || !tile(l.gate, &l.up, &TL[i].gu) ||
-                !tile(l.down, nullptr, &TL[i].down))
-                return false;
+            TiledLayer & t = TL[i];
+            const bool ok = q8 ? tq(l.qkv, nullptr, &t.qkv, &t.sqkv) && tq(l.o, nullptr, &t.o, &t.so) &&
+                                     tq(l.gate, &l.up, &t.gu, &t.sgu) && tq(l.down, nullptr, &t.down, &t.sdown)
+                               : tile(l.qkv, nullptr, &t.qkv) && tile(l.o, nullptr, &t.o) && tile(l.gate, &l.up, &t.gu) &&
+                                     tile(l.down, nullptr, &t.down);
+            if (!ok) return false;
         }
         const int maxc = std::max(std::max(H, QD), FF);
+        if (q8 && (!alloc(&xq, (size_t) Q8_MAX_N * maxc) || !alloc(&xqs, sizeof(float) * Q8_MAX_N * (maxc / 32))))
+            return false;
+        if (q8 && q8_set_attributes() != cudaSuccess) { err = "prefill: kernel attributes"; return false; }
         if (!alloc(&qkv, sizeof(float) * R * eng->QKVD()) || !alloc(&att, sizeof(float) * R * QD) ||
             !alloc(&hbuf, sizeof(float) * R * FF) || !alloc(&xt, (size_t) TC_MAX_N * maxc * 2) ||
             !alloc(&xt2, (size_t) TC_MAX_N * maxc * 2) || !alloc(&d_err, sizeof(int)))
@@ -548,6 +605,21 @@ struct PrefillTC {
         for (size_t il = 0; il < E->L.size(); ++il) {
             const LayerW & l = E->L[il];
             const TiledLayer & w = TL[il];
+            if (q8) {
+                const float eps = c.rms_norm_eps;
+                int n = q8_project(E->stream, xq, xqs, d_err, eps, w.qkv, w.sqkv, QKVD, H, X, H, M, l.attn_norm,
+                                   TC_EPI_STORE, qkv, QKVD, nullptr);
+                E->prefill_attention(l, E->kc + il * layer_elems, E->vc + il * layer_elems, E->rope_t, qkv, QKVD, M,
+                                     nullptr, n_past, nullptr, att, QD, nullptr, 0, att_smem);
+                n += q8_project(E->stream, xq, xqs, d_err, eps, w.o, w.so, H, QD, att, QD, M, nullptr, TC_EPI_RESID, X,
+                                H, X);
+                n += q8_project(E->stream, xq, xqs, d_err, eps, w.gu, w.sgu, 2 * FF, H, X, H, M, l.ffn_norm,
+                                TC_EPI_SWIGLU, hbuf, FF, nullptr);
+                n += q8_project(E->stream, xq, xqs, d_err, eps, w.down, w.sdown, H, FF, hbuf, FF, M, nullptr,
+                                TC_EPI_RESID, X, H, X);
+                E->launches += n;
+                continue;
+            }
             t.pack(X, H, M, mp, H, l.attn_norm, TC_ACT_F16, nullptr);
             t.gemm(w.qkv, QKVD, H, xt, M, mp, TC_ACT_F16, TC_EPI_STORE, qkv, QKVD, nullptr, false, mp);
             E->prefill_attention(l, E->kc + il * layer_elems, E->vc + il * layer_elems, E->rope_t, qkv, QKVD, M,

@@ -19,6 +19,7 @@
 #include "../../include/qwen3tts_b200.h"
 #include "gguf.hpp"
 #include "frame_fused.cuh"
+#include "gemm_q8.cuh"
 #include "gemm_tc.cuh"
 #include "batch_engine.cuh"
 
@@ -1132,8 +1133,8 @@ bool Engine::prefill(const float * rows_host, int n, int n_past, float * hidden_
     if (n_ctx == 0 && !init_kv(std::max(256, n_past + n + 16))) return false;
     if (n_past + n > n_ctx) { err = "Context length exceeded"; return false; }
     // rows uploaded once; chunks of 8 rows through the GEMV path, or of up to 128
-    // rows through tcgen05 GEMMs (F16 weights; QTTS_PREFILL=gemv|tc, default tc
-    // for prompts of more than 8 rows)
+    // rows through tcgen05 GEMMs (kind::f16 for F16 weights, kind::i8 for Q8_0;
+    // QTTS_PREFILL=gemv|tc, default tc for prompts of more than 8 rows)
     if (n > prow_cap) {
         if (d_prow) cudaFree(d_prow);
         prow_cap = std::max(n, 256);
@@ -1142,8 +1143,7 @@ bool Engine::prefill(const float * rows_host, int n, int n_past, float * hidden_
         }
     }
     const char * pm = getenv("QTTS_PREFILL");
-    const bool f16w = L[0].qkv.type == W_F16;
-    const bool tc = f16w && (pm && *pm ? strcmp(pm, "tc") == 0 : n > QTTS_MAX_NV);
+    const bool tc = pm && *pm ? strcmp(pm, "tc") == 0 : n > QTTS_MAX_NV;
     const int chunk = tc ? PREFILL_TC_ROWS : QTTS_MAX_NV;
     QCHECK(cudaEventRecord(ev0, stream));
     QCHECK(cudaMemcpyAsync(d_prow, rows_host, sizeof(float) * (size_t) n * H, cudaMemcpyHostToDevice, stream));
@@ -1566,6 +1566,94 @@ extern "C" {
 // ---------------------------------------------------------------- kernel-level entry points
 // These run one engine kernel on caller-provided host data (device buffers are
 // allocated per call); the parity tests use them to check a kernel in isolation.
+int32_t qtts_op_gemm_q8(int32_t device, const uint8_t * w, const uint8_t * w_up, int32_t rows, int32_t cols,
+                        const float * xin, int32_t m, const float * norm_gain, float eps, int32_t epi,
+                        const float * resid, int32_t ksplit, float * y) {
+    using namespace qtts;
+    const bool swiglu = epi == TC_EPI_SWIGLU;
+    const int rows_w = swiglu ? 2 * rows : rows;
+    const int np = (m + 15) / 16 * 16, nb = cols / 32;
+    if (!w || !xin || !y || m <= 0 || rows <= 0 || rows_w % TC_BM || cols % Q8_BK || np > Q8_MAX_N ||
+        (swiglu && (!w_up || rows % (TC_BM / 2))) || (epi == TC_EPI_RESID && !resid) || epi < 0 || epi > 2 ||
+        ksplit < 0 || ksplit > 8)
+        return 0;
+    if (cudaSetDevice(device) != cudaSuccess) return 0;
+    void * dq = nullptr, * dd = nullptr, * dq2 = nullptr, * dd2 = nullptr, * dwt = nullptr, * dws = nullptr,
+         * dx = nullptr, * dxq = nullptr, * dxs = nullptr, * dy = nullptr, * dg = nullptr, * derr = nullptr;
+    bool ok = true;
+    std::string why;
+    auto chk = [&](cudaError_t e) {
+        if (e != cudaSuccess && ok) { ok = false; why = cudaGetErrorString(e); }
+    };
+    // GGUF blocks (f16 d + 32 int8) -> the engine's split planes
+    std::vector<int8_t> hq((size_t) rows * cols), hq2(swiglu ? (size_t) rows * cols : 0);
+    std::vector<uint16_t> hd((size_t) rows * nb), hd2(swiglu ? (size_t) rows * nb : 0);
+    for (int pass = 0; pass < (swiglu ? 2 : 1); ++pass) {
+        const uint8_t * src = pass ? w_up : w;
+        int8_t * q = pass ? hq2.data() : hq.data();
+        uint16_t * d = pass ? hd2.data() : hd.data();
+        for (size_t blk = 0; blk < (size_t) rows * nb; ++blk) {
+            memcpy(d + blk, src + blk * 34, 2);
+            memcpy(q + blk * 32, src + blk * 34 + 2, 32);
+        }
+    }
+    chk(cudaMalloc(&dq, hq.size()));
+    chk(cudaMalloc(&dd, hd.size() * 2));
+    if (swiglu) { chk(cudaMalloc(&dq2, hq2.size())); chk(cudaMalloc(&dd2, hd2.size() * 2)); }
+    chk(cudaMalloc(&dwt, (size_t) rows_w * cols));
+    chk(cudaMalloc(&dws, (size_t) rows_w * nb * 2));
+    chk(cudaMalloc(&dx, sizeof(float) * m * cols));
+    chk(cudaMalloc(&dxq, (size_t) np * cols));
+    chk(cudaMalloc(&dxs, sizeof(float) * np * nb));
+    chk(cudaMalloc(&dy, sizeof(float) * m * rows));
+    chk(cudaMalloc(&derr, sizeof(int)));
+    if (norm_gain) chk(cudaMalloc(&dg, sizeof(float) * cols));
+    int S = 0;
+    if (ok) {
+        chk(cudaMemcpy(dq, hq.data(), hq.size(), cudaMemcpyHostToDevice));
+        chk(cudaMemcpy(dd, hd.data(), hd.size() * 2, cudaMemcpyHostToDevice));
+        if (swiglu) {
+            chk(cudaMemcpy(dq2, hq2.data(), hq2.size(), cudaMemcpyHostToDevice));
+            chk(cudaMemcpy(dd2, hd2.data(), hd2.size() * 2, cudaMemcpyHostToDevice));
+        }
+        chk(cudaMemcpy(dx, xin, sizeof(float) * m * cols, cudaMemcpyHostToDevice));
+        if (resid) chk(cudaMemcpy(dy, resid, sizeof(float) * m * rows, cudaMemcpyHostToDevice));
+        if (norm_gain) chk(cudaMemcpy(dg, norm_gain, sizeof(float) * cols, cudaMemcpyHostToDevice));
+        chk(cudaMemset(derr, 0, sizeof(int)));
+    }
+    if (ok) {
+        DMat W{}, W2{};
+        W.type = W_Q8_0; W.rows = rows; W.cols = cols; W.w = dq; W.d = (const __half *) dd;
+        if (swiglu) { W2 = W; W2.w = dq2; W2.d = (const __half *) dd2; }
+        k_tile_q8<<<rows_w, 128>>>(W, W2, rows_w, (uint8_t *) dwt, (__half *) dws);
+        PackQ8Args pa{};
+        pa.x = (const float *) dx; pa.ldx = cols; pa.m_real = m; pa.np = np; pa.cols = cols;
+        pa.gain = (const float *) dg; pa.eps = eps; pa.out = (uint8_t *) dxq; pa.dscale = (float *) dxs;
+        k_pack_q8<<<np, 256>>>(pa);
+        GemmQ8Args g{};
+        g.w = (const uint8_t *) dwt; g.ws = (const __half *) dws; g.x = (const uint8_t *) dxq; g.xs = (const float *) dxs;
+        g.rows_w = rows_w; g.cols = cols; g.np = np; g.m_real = m; g.epi = epi; g.y = (float *) dy; g.ldy = rows;
+        g.resid = (const float *) dy; g.ldr = rows; g.err = (int *) derr;
+        g.ksplit = ksplit > 0 ? ksplit : q8_choose_split(g);
+        if (g.ksplit > cols / Q8_BK || q8_stages(np, cols, q8_partial_bytes(np, m, g.ksplit)) < 2) {
+            ok = false; why = "k-split does not fit";
+        }
+        S = g.ksplit;
+        chk(q8_set_attributes());
+        if (ok) chk(q8_launch(g, 0));
+        chk(cudaGetLastError());
+        chk(cudaDeviceSynchronize());
+        int herr = 0;
+        if (ok) chk(cudaMemcpy(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost));
+        if (herr && ok) { ok = false; why = "a bounded wait gave up (" + std::to_string(herr) + ")"; }
+        if (ok) chk(cudaMemcpy(y, dy, sizeof(float) * m * rows, cudaMemcpyDeviceToHost));
+    }
+    void * all[] = {dq, dd, dq2, dd2, dwt, dws, dx, dxq, dxs, dy, dg, derr};
+    for (void * p : all) if (p) cudaFree(p);
+    if (!ok) qtts::g_create_error = "qtts_op_gemm_q8: " + why;
+    return ok ? S : 0;
+}
+
 int32_t qtts_op_gemm_tc(int32_t device, const uint16_t * w, const uint16_t * w_up, int32_t rows, int32_t cols,
                         const float * xin, int32_t m, const float * norm_gain, float eps, int32_t act, int32_t epi,
                         const float * resid, float * y) {

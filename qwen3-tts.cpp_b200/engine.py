@@ -129,6 +129,8 @@ def lib():
         "qtts_batch_error": (C.c_char_p, [C.c_void_p]),
         "qtts_batch_profile": (C.c_int32, [C.c_void_p, C.c_int32, _f32p, _i32p]),
         "qtts_batch_free": (None, [C.c_void_p]),
+        "qtts_op_gemm_q8": (C.c_int32, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32,
+                                        _f32p, C.c_float, C.c_int32, _f32p, C.c_int32, _f32p]),
         "qtts_op_gemm_tc": (C.c_int32, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32,
                                         _f32p, C.c_float, C.c_int32, C.c_int32, _f32p, _f32p]),
         "qtts_op_gemv": (C.c_int32, [C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32, _f32p, C.c_int32, _f32p,
@@ -492,6 +494,27 @@ def op_gemm_tc(w, x, w_up=None, norm_gain=None, eps=1e-6, act=TC_ACT_F16, epi=TC
     if not rc:
         raise RuntimeError("qtts_op_gemm_tc failed")
     return y
+
+
+def op_gemm_q8(w, cols, x, w_up=None, norm_gain=None, eps=1e-6, epi=TC_EPI_STORE, resid=None, ksplit=0,
+               device: int = 0):
+    """Run the kind::i8 tensor-core GEMM once (see qtts_op_gemm_q8): w (and w_up)
+    are GGUF Q8_0 blocks (uint8, rows x cols/32 x 34 bytes).  Returns (y [m][rows],
+    the k-split used)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    rows = w.size // (cols // 32 * 34)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, cols)
+    m = x.shape[0]
+    wu = None if w_up is None else np.ascontiguousarray(w_up, dtype=np.uint8)
+    g = None if norm_gain is None else np.ascontiguousarray(norm_gain, dtype=np.float32)
+    r = None if resid is None else np.ascontiguousarray(resid, dtype=np.float32)
+    y = np.zeros((m, rows), np.float32)
+    s = lib().qtts_op_gemm_q8(device, w.ctypes.data_as(C.c_void_p), None if wu is None else wu.ctypes.data_as(C.c_void_p),
+                              rows, cols, _p(x, C.c_float), m, _p(g, C.c_float), eps, epi, _p(r, C.c_float), ksplit,
+                              _p(y, C.c_float))
+    if not s:
+        raise RuntimeError(lib().qtts_create_error().decode())
+    return y, s
 
 
 def op_sample(logits, cb: int, temperature=0.0, top_k=0, rep_penalty=1.0, presence=None, eos_bias=0.0,

@@ -26,8 +26,8 @@ def _utterances(rng, n, frames, hidden):
 
 @pytest.mark.parametrize("which,n", [("f16", 1), ("f16", 5), ("q8", 1), ("q8", 5)])
 def test_batch_matches_oracle(qtts, request, which, n):
-    """F16: tcgen05 GEMMs.  Q8_0: the projections run as 8-row GEMV chunks (the
-    batch-1 kernel's int8 block dots), the F16 heads as tcgen05 GEMMs."""
+    """F16: kind::f16 tcgen05 GEMMs.  Q8_0: the projections as kind::i8 tcgen05
+    GEMMs (exact int32 block dots), the F16 heads as kind::f16 GEMMs."""
     path = request.getfixturevalue("tiny_f16" if which == "f16" else "tiny_q8")
     rng = np.random.default_rng(40 + n)
     eng = qtts.Engine(path, 0)
@@ -42,8 +42,17 @@ def test_batch_matches_oracle(qtts, request, which, n):
     for i, u in enumerate(utts):
         assert codes[i].shape == (frames, 16)
         kw = {k: v for k, v in u.items() if k not in ("text", "max_len")}
-        r = o.generate(u["text"], frames, follow=codes[i], tie_tol=TIE_TOL, **kw)
-        assert r["n_mismatch"] == 0, (i, r["n_mismatch"], r["max_mismatch_gap"], r["first_mismatch"])
+        if which == "f16":
+            r = o.generate(u["text"], frames, follow=codes[i], tie_tol=TIE_TOL, **kw)
+            assert r["n_mismatch"] == 0, (i, r["n_mismatch"], r["max_mismatch_gap"], r["first_mismatch"])
+        else:
+            # Q8_0: the activation quantiser turns last-bit differences of the sums
+            # (tensor-core order vs the oracle's) into whole int8 levels, so the bar
+            # is the full-size tests' near-tie rule: every divergent decision within
+            # the Q8_0 margin, and rare
+            r = o.generate(u["text"], frames, follow=codes[i], tie_tol=1e9, **kw)
+            assert r["max_tie_gap"] <= BATCH_MARGIN["q8"], (i, r["max_tie_gap"], r["n_ties"])
+            assert r["n_ties"] <= BATCH_FRAC["q8"] * 16 * frames, (i, r["n_ties"])
         assert r["n_frames"] == frames
     b.close()
     eng.close()

@@ -1,5 +1,6 @@
 """Tensor-core prefill (tcgen05 GEMMs over up to 128 prompt rows per chunk, the
-default for F16 prompts of more than 8 rows) against the CPU oracle.
+default for prompts of more than 8 rows: kind::f16 for F16 weights, kind::i8
+for Q8_0) against the CPU oracle.
 
 The GEMMs accumulate in the MMA's order, not the oracle's, so this path is held
 to the north-star contract rather than to bit equality: prefill hidden rows and
@@ -83,19 +84,28 @@ def test_generate_plain_tc_prefill(qtts, tiny_f16, monkeypatch):
     eng.close()
 
 
-def test_q8_prompt_uses_gemv_prefill(qtts, tiny_q8, monkeypatch):
-    """Q8_0 weights have no tensor-core prefill: QTTS_PREFILL=tc gives the GEMV
-    path's bits."""
-    rng = np.random.default_rng(312)
-    rows = (rng.standard_normal((20, 256)) * 0.1).astype(np.float32)
-    outs = []
+@pytest.mark.parametrize("n_rows", [20, 150])
+def test_q8_tc_prefill_rows_match_oracle(qtts, tiny_q8, monkeypatch, n_rows):
+    """Q8_0 prompts through the kind::i8 tensor-core GEMMs (quantised
+    activations, exact int32 block dots, block sums in order): hidden rows and
+    logits within the Q8_0 bound 5e-2 of the oracle and of the GEMV prefill."""
+    rng = np.random.default_rng(312 + n_rows)
+    rows = (rng.standard_normal((n_rows, 256)) * 0.1).astype(np.float32)
+    outs = {}
     for mode in ("tc", "gemv"):
         monkeypatch.setenv("QTTS_PREFILL", mode)
         eng = qtts.Engine(tiny_q8, 0)
-        eng.init_kv_cache(64)
-        outs.append(eng.forward_prefill(rows, 0))
+        eng.init_kv_cache(256)
+        outs[mode] = eng.forward_prefill(rows, 0)
         eng.close()
-    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+    o = Oracle(tiny_q8, threads=4)
+    o.init_kv(256)
+    ho, lo = o.forward_prefill(rows, 0)
+    he, le = outs["tc"]
+    hg, lg = outs["gemv"]
+    assert np.abs(he - ho).max() < 5e-2 and np.abs(le - lo).max() < 5e-2
+    assert np.abs(he - hg).max() < 5e-2 and np.abs(le - lg).max() < 5e-2
+    assert not np.array_equal(le, lg)   # the tensor-core path ran (its sums differ in the last bits)
 
 
 def test_full_f16_config1_tc_prefill(qtts, full_f16, monkeypatch):
