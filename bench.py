@@ -400,9 +400,9 @@ def run_batch(args, cfg):
 def run_ncu_workload(args):
     """A small fixed workload for ncu captures (no timing, no JSON line):
     `frames`: the config's ICL prefill and --frames frames through the frame
-    loop (QTTS_FRAME_MODE=graph selects the one-kernel-per-op frame); `batch`: --batch
-    utterances with 64-position ICL prompts, --frames batched frames, then two
-    eagerly profiled frames.  A few GB on the device at most."""
+    loop (QTTS_FRAME_MODE=fused selects the clustered frame path); `batch`: --batch
+    utterances with 64-position ICL prompts (Q8_0 model for --config q8 / q8long),
+    --frames batched frames, then two eagerly profiled frames.  A few GB on the device at most."""
     pkg = _pkg()
     d = os.environ.get("QTTS_MODEL_DIR", os.path.join(ROOT, ".models"))
     cfg_m = pkg.synth_gguf.TINY if args.tiny else pkg.synth_gguf.FULL
@@ -422,7 +422,7 @@ def run_ncu_workload(args):
         print(f"frames={got} {eng.timing()}", file=sys.stderr)
         eng.close()
         return 0
-    path = pkg.synth_gguf.ensure_gguf(d, cfg_m, "f16", seed=0)
+    path = pkg.synth_gguf.ensure_gguf(d, cfg_m, "q8_0" if CONFIGS[args.config]["wtype"] == "q8_0" else "f16", seed=0)
     eng = pkg.Engine(path, 0)
     H = eng.cfg["hidden_size"]
     frames = args.frames + 2
