@@ -20,17 +20,21 @@
 // x 16 bytes) in k order; block j of a k-tile is core matrices 2j, 2j + 1.
 // Weight block scales are repacked as [row tile][k-tile][128 rows][4] F16.
 //
-// Roles (192 threads): warps 0-3 drain TMEM (warp w owns lanes 32w..32w+31 =
-// weight rows) and run the epilogue, warp 4 lane 0 streams W and X tiles
-// through a shared-memory ring, warp 5 allocates TMEM and lane 0 issues the
-// MMAs.  Every wait is bounded.
+// Roles (320 threads): warps 0-7 drain TMEM and run the epilogue (warp w reads
+// lanes 32 (w % 4) .. 32 (w % 4) + 31 = weight rows, and the 16-column chunks
+// w / 4, w / 4 + 2, ... of the activation columns), warp 8 lane 0 streams W and
+// X tiles through a shared-memory ring, warp 9 allocates TMEM and its lane 0
+// issues the MMAs.  Every wait is bounded.
 #pragma once
 #include "gemm_tc.cuh"
 
 namespace qtts {
 
 constexpr int Q8_BK = 128;          // int8 k per tile (four Q8_0 blocks)
-constexpr int Q8_THREADS = 192;
+constexpr int Q8_EPI_WARPS = 8;     // epilogue warps: two per TMEM lane quarter (column halves)
+constexpr int Q8_PRODUCER = Q8_EPI_WARPS * 32;        // thread that streams the tiles
+constexpr int Q8_MMA_WARP = Q8_EPI_WARPS + 1;         // warp that owns TMEM; its lane 0 issues the MMAs
+constexpr int Q8_THREADS = (Q8_EPI_WARPS + 2) * 32;
 constexpr int Q8_MAX_N = 128;       // activation rows (MMA N) per launch
 constexpr int Q8_MAX_STAGES = 8;
 
@@ -149,6 +153,14 @@ __device__ __forceinline__ void q8_mma(uint32_t tmem_d, uint64_t da, uint64_t db
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n"
         ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(0));
 }
+__device__ __forceinline__ void q8_ld16(uint32_t taddr, int (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                   "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                   "=r"(v[15])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void q8_ld32(uint32_t taddr, int (&v)[32]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
                  "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -161,16 +173,15 @@ __device__ __forceinline__ void q8_ld32(uint32_t taddr, int (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// TMEM: NBUF buffers of 4 blocks x np columns (one buffer per k-tile in flight),
-// within 512 columns including 32 columns of slack for np % 32 != 0.
+// TMEM: NBUF buffers of 4 blocks x np columns (one buffer per k-tile in flight).
 __host__ __device__ inline int q8_nbuf(int np) {
-    const int n = (512 - (np % 32 ? 32 : 0)) / (4 * np);
+    const int n = 512 / (4 * np);
     return n > 4 ? 4 : (n < 1 ? 1 : n);
 }
 __host__ __device__ inline size_t q8_stage_bytes(int np) { return (size_t) TC_BM * Q8_BK + (size_t) np * 128; }
-// Activation scales in shared memory, rows padded to a multiple of 32 (the
-// epilogue reads 32 columns at a time; padding rows hold 0).
-__host__ __device__ inline size_t q8_scale_bytes(int np, int cols) { return (size_t)((np + 31) & ~31) * (cols / 32) * 4; }
+// Activation scales in shared memory [np][cols / 32] (np is a multiple of 16,
+// the epilogue's column chunk).
+__host__ __device__ inline size_t q8_scale_bytes(int np, int cols) { return (size_t) np * (cols / 32) * 4; }
 __host__ __device__ inline size_t q8_partial_bytes(int np, int m_real, int ksplit) {
     if (ksplit <= 1) return 0;
     const int pc = m_real < np ? m_real : np;
@@ -185,13 +196,14 @@ __host__ __device__ inline size_t q8_smem_bytes(int np, int cols, size_t pbytes)
     return (size_t) q8_stages(np, cols, pbytes) * q8_stage_bytes(np) + q8_scale_bytes(np, cols) + pbytes + 1024;
 }
 
-template <int NACC>   // accumulators per thread (activation columns): >= np
+template <int NACC>   // accumulator columns of the launch (>= np); a thread holds NACC / 2
 __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
+    constexpr int NA = NACC / 2;   // columns per epilogue thread: 16-column chunks h, h + 2, h + 4, ...
     extern __shared__ __align__(128) uint8_t q8_smem[];
     __shared__ __align__(8) uint64_t full[Q8_MAX_STAGES], empty[Q8_MAX_STAGES], accf[4], acce[4];
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
-    __shared__ float s_swg[TC_BM / 2][33];
+    __shared__ float s_swg[2][TC_BM / 2][17];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = g.ksplit > 1 ? g.ksplit : 1;
     const int tn = blockIdx.x / S, rank = blockIdx.x % S;
@@ -205,18 +217,19 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
     const int nb = g.cols / 32;
     float * xsc = reinterpret_cast<float *>(q8_smem + NST * sbytes);          // activation scales [np][nb]
     float * P = reinterpret_cast<float *>(q8_smem + NST * sbytes + q8_scale_bytes(g.np, g.cols));   // k-split slots
-    // 32-column TMEM loads: a last partial chunk of a block (np % 32 != 0) reads up to
-    // 31 columns past the block, so the allocation covers them
     int ncols = 32;
-    while (ncols < NBUF * 4 * g.np + (g.np % 32 ? 32 : 0)) ncols <<= 1;
+    while (ncols < NBUF * 4 * g.np) ncols <<= 1;
+    // epilogue warp (q, h): TMEM lane quarter q = warp % 4 (weight rows 32q .. 32q + 31), column half h
+    const int q4 = warp & 3, hh = (warp >> 2) & 1;
+    const int r_tile = q4 * 32 + lane;
 
     const uint8_t * wsrc = g.w + ((size_t) tn * nk_all + k0) * wtile;
     const uint8_t * xsrc = g.x + (size_t) k0 * xtile;
     int issued = 0;
     pdl_trigger();
-    if (tid == 128) {
+    if (tid == Q8_PRODUCER) {
         for (int s = 0; s < NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 4; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4); }
+        for (int b = 0; b < 4; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], Q8_EPI_WARPS); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_fail = 0;
         for (int i = 0; i < nk && i < NST; ++i) {   // weight tiles are read-only: copy before the predecessor ends
@@ -225,7 +238,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
             issued = i + 1;
         }
     }
-    if (warp == 5) {
+    if (warp == Q8_MMA_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                      "r"(ncols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -235,18 +248,18 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     pdl_wait();   // activations, their scales, residuals and outputs follow the predecessor
-    if (tid == 128)
+    if (tid == Q8_PRODUCER)
         for (int i = 0; i < issued; ++i)
             bulk_g2s(q8_smem + i * sbytes + wtile, xsrc + (size_t) i * xtile, (unsigned) xtile, &full[i]);
-    for (int i = tid; i < ((g.np + 31) & ~31) * nb; i += Q8_THREADS) xsc[i] = i < g.np * nb ? g.xs[i] : 0.0f;
+    for (int i = tid; i < g.np * nb; i += Q8_THREADS) xsc[i] = g.xs[i];
     __syncthreads();
 
     const int pc = g.m_real < g.np ? g.m_real : g.np;   // output columns kept
-    float acc[NACC];
+    float acc[NA];
 #pragma unroll
-    for (int m = 0; m < NACC; ++m) acc[m] = 0.0f;
+    for (int i = 0; i < NA; ++i) acc[i] = 0.0f;
     bool ok = true;
-    if (tid == 128) {
+    if (tid == Q8_PRODUCER) {
         // producer: W tile and X k-tile into stage i % NST
         for (int i = issued; i < nk; ++i) {
             const int s = i % NST;
@@ -257,7 +270,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
             bulk_g2s(dst + wtile, xsrc + (size_t) i * xtile, (unsigned) xtile, &full[s]);
             issued = i + 1;
         }
-    } else if (tid == 160) {
+    } else if (tid == Q8_MMA_WARP * 32) {
         // MMA issuer: block j of k-tile i into TMEM columns (i % NBUF) * 4 np + j np
         const uint32_t idesc = q8_idesc(g.np);
         for (int i = 0; i < nk; ++i) {
@@ -273,10 +286,9 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
             tc_commit(&empty[s]);
             tc_commit(&accf[bf]);
         }
-    } else if (warp < 4) {
+    } else if (warp < Q8_EPI_WARPS) {
         // epilogue warps: block dots of k-tile i -> acc, in block order
-        const int r_tile = warp * 32 + lane;
-        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
         const __half * wsrow = g.ws + q8_s_off(tn * TC_BM + r_tile, k0 * 4, g.cols);   // [k-tile][128][4] F16
         uint2 wsn = __ldg(reinterpret_cast<const uint2 *>(wsrow));
         for (int i = 0; i < nk; ++i) {
@@ -294,15 +306,15 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
             for (int j = 0; j < 4; ++j) {
                 const int b = (k0 + i) * 4 + j;
 #pragma unroll
-                for (int c0 = 0; c0 < NACC; c0 += 32) {
-                    if (c0 < g.np) {   // warp-uniform
-                        int v[32];
-                        q8_ld32(trow + (uint32_t)((bf * 4 + j) * g.np + c0), v);
+                for (int c = 0; c < NA / 16; ++c) {
+                    const int col0 = (2 * c + hh) * 16;
+                    if (col0 < g.np) {   // warp-uniform
+                        int v[16];
+                        q8_ld16(trow + (uint32_t)((bf * 4 + j) * g.np + col0), v);
 #pragma unroll
-                        for (int t = 0; t < 32; ++t) {
-                            const int m = c0 + t;
-                            acc[m] = __fadd_rn(acc[m], __fmul_rn((float) v[t], __fmul_rn(dw[j], xsc[m * nb + b])));
-                        }
+                        for (int t = 0; t < 16; ++t)
+                            acc[c * 16 + t] = __fadd_rn(acc[c * 16 + t],
+                                                        __fmul_rn((float) v[t], __fmul_rn(dw[j], xsc[(col0 + t) * nb + b])));
                     }
                 }
             }
@@ -313,15 +325,15 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
     }
     const int bad = __syncthreads_or(!ok || s_fail);
     if (bad && tid == 0) atomicExch(g.err, 1);
+    const bool epi = warp < Q8_EPI_WARPS;
     if (S > 1) {
-        // k-split: the thread of TMEM row r pushes its partial row into slot [rank] of
+        // k-split: the thread of TMEM row r pushes its partial columns into slot [rank] of
         // the row's owner; after the cluster barrier each owner sums its slots in rank order
         const bool swg = g.epi == TC_EPI_SWIGLU;
         const int pc4 = (pc + 3) & ~3, ps = pc4 + 4;
         const int rs = (swg ? TC_BM / 2 : TC_BM) / S;
         const int orows = swg ? 2 * rs : rs;
-        if (!bad && warp < 4) {
-            const int r_tile = warp * 32 + lane;
+        if (!bad && epi) {
             const int gr = swg ? (r_tile & (TC_BM / 2 - 1)) : r_tile;
             const int owner = gr / rs;
             const int orow = (gr % rs) + (swg && r_tile >= TC_BM / 2 ? rs : 0);
@@ -329,11 +341,16 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
             uint32_t rdst;
             asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(dst), "r"((uint32_t) owner));
 #pragma unroll
-            for (int j = 0; j < NACC; j += 4)
-                if (j < pc4)
-                    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(rdst + (uint32_t) j * 4),
-                                 "f"(acc[j]), "f"(acc[j + 1]), "f"(acc[j + 2]), "f"(acc[j + 3])
-                                 : "memory");
+            for (int c = 0; c < NA / 16; ++c) {
+                const int col0 = (2 * c + hh) * 16;
+#pragma unroll
+                for (int t = 0; t < 16; t += 4)
+                    if (col0 + t < pc4)
+                        asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(rdst + (uint32_t)(col0 + t) * 4),
+                                     "f"(acc[c * 16 + t]), "f"(acc[c * 16 + t + 1]), "f"(acc[c * 16 + t + 2]),
+                                     "f"(acc[c * 16 + t + 3])
+                                     : "memory");
+            }
         }
         cluster_sync_all();
         if (!bad) {
@@ -367,52 +384,59 @@ __global__ void __launch_bounds__(Q8_THREADS, 1) k_gemm_q8(GemmQ8Args g) {
                 }
             }
         }
-    } else if (!bad && warp < 4) {
-        const int r_tile = warp * 32 + lane;
+    } else if (!bad && epi) {
         if (g.epi == TC_EPI_SWIGLU) {
-            // warps 0-1 hold gate rows, warps 2-3 the matching up rows (32 columns at a time)
+            // quarters 0-1 hold gate rows, 2-3 the matching up rows; one 16-column chunk per half at a time
 #pragma unroll
-            for (int c0 = 0; c0 < NACC; c0 += 32) {
-                if (c0 >= pc) continue;   // block-uniform
-                if (warp >= 2)
+            for (int c = 0; c < NA / 16; ++c) {
+                const int col0 = (2 * c + hh) * 16;
+                if (q4 >= 2)
 #pragma unroll
-                    for (int t = 0; t < 32; ++t) s_swg[r_tile - TC_BM / 2][t] = acc[c0 + t];
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (warp < 2) {
+                    for (int t = 0; t < 16; ++t) s_swg[hh][r_tile - TC_BM / 2][t] = acc[c * 16 + t];
+                asm volatile("bar.sync 1, %0;" ::"r"(Q8_EPI_WARPS * 32) : "memory");
+                if (q4 < 2) {
                     const int col = tn * (TC_BM / 2) + r_tile;
 #pragma unroll
-                    for (int t = 0; t < 32; ++t) {
-                        const int m = c0 + t;
-                        if (m < pc) g.y[(size_t) m * g.ldy + col] = __fmul_rn(silu(acc[c0 + t]), s_swg[r_tile][t]);
+                    for (int t = 0; t < 16; ++t) {
+                        const int m = col0 + t;
+                        if (m < pc) g.y[(size_t) m * g.ldy + col] = __fmul_rn(silu(acc[c * 16 + t]), s_swg[hh][r_tile][t]);
                     }
                 }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                asm volatile("bar.sync 1, %0;" ::"r"(Q8_EPI_WARPS * 32) : "memory");
             }
         } else {
             const int row = tn * TC_BM + r_tile;
 #pragma unroll
-            for (int m = 0; m < NACC; ++m) {
-                if (m >= pc) continue;
-                float o = acc[m];
-                if (g.epi == TC_EPI_RESID) o = __fadd_rn(o, g.resid[(size_t) m * g.ldr + row]);
-                g.y[(size_t) m * g.ldy + row] = o;
+            for (int c = 0; c < NA / 16; ++c) {
+                const int col0 = (2 * c + hh) * 16;
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+                    const int m = col0 + t;
+                    if (m >= pc) continue;
+                    float o = acc[c * 16 + t];
+                    if (g.epi == TC_EPI_RESID) o = __fadd_rn(o, g.resid[(size_t) m * g.ldr + row]);
+                    g.y[(size_t) m * g.ldy + row] = o;
+                }
             }
         }
     }
     // after a timeout: wait (bounded) for the copies still in flight, then free TMEM
-    if (tid == 128 && bad)
+    if (tid == Q8_PRODUCER && bad)
         for (int j = issued > NST ? issued - NST : 0; j < issued; ++j) mbar_wait(&full[j % NST], (j / NST) & 1);
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+    if (warp == Q8_MMA_WARP) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
 }
 
-// k-split: the smallest power of two giving >= 64 CTAs, at most 8 and at most
-// the k-tiles, while the ring and the partial slots fit.
-inline int q8_choose_split(const GemmQ8Args & g) {
+// k-split: the smallest power of two giving >= 128 CTAs (at most n_sm CTAs, one
+// per SM), at most 8 (clusters of 16 CTAs at one CTA per SM are not all
+// resident at once on B200) and at most the k-tiles, while the ring and the
+// partial slots fit.
+inline int q8_choose_split(const GemmQ8Args & g, int n_sm = 148) {
     const int tiles = g.rows_w / TC_BM, nk = g.cols / Q8_BK;
     int S = 1;
-    while (tiles * S < 64 && S < 8 && S * 2 <= nk && q8_stages(g.np, g.cols, q8_partial_bytes(g.np, g.m_real, S * 2)) >= 2)
+    while (tiles * S < 128 && tiles * S * 2 <= n_sm && S < 8 && S * 2 <= nk &&
+           q8_stages(g.np, g.cols, q8_partial_bytes(g.np, g.m_real, S * 2)) >= 2)
         S *= 2;
     return S;
 }
