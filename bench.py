@@ -298,10 +298,11 @@ def run_batch(args, cfg):
     max_pos = max(u.prefill for u in mine) + F + 1
     W = max(args.warmup, 3)
     PF = 2                                   # eagerly profiled frames after the timed region
-    K = max(1, min(args.steps, F - W - PF))
+    SK = max(0, min(args.skip_frames, F - W - PF - 1))   # untimed frames before the timed window
+    K = max(1, min(args.steps, F - W - PF - SK))
     bt = pkg.engine.Batch(eng, max_batch=B, max_positions=max_pos, max_frames=F)
     bt.begin(plist)
-    bt.run(W)
+    bt.run(W + SK)
     t0 = bt.timing()["frames_ms"]
     with ClockSampler(local) as clk:
         barrier()
@@ -353,7 +354,7 @@ def run_batch(args, cfg):
         return 0
     peak, peak_kind = _peaks()
     frame_ms = ms_max / K
-    kv_mean = float(np.mean([u.prefill for u in mine])) + W + K / 2.0
+    kv_mean = float(np.mean([u.prefill for u in mine])) + W + SK + K / 2.0
     wkey = "f16" if cfg["wtype"] == "f16" else "q8"
     frame_bytes = WEIGHT_BYTES[wkey] + B * (KV_TALKER_PER_POS * kv_mean + KV_CP_PER_POS * 135)
     achieved = frame_bytes / (frame_ms / 1e3) / 1e9
@@ -371,6 +372,7 @@ def run_batch(args, cfg):
                 f"P ~ U[{cfg['p_lo']},{cfg['p_hi']}])",
         "config": {"workload": cfg["workload"], "utterances": n_utts, "batch_per_gpu": B,
                    "frames_per_utterance": F, "frames_timed_per_sequence": K,
+                   "frames_before_timing": W + SK,
                    "parallelism": f"LPT utterance sharding over {world} GPU(s), one batch per GPU",
                    "l2": "inputs larger than L2 (3.3 GB of weights + KV streamed per frame), no flush"},
         "roofline": {"bound": "hbm", "kernel": "batched frame (CUDA graph: tcgen05 GEMMs + paged attention)" if wkey == "f16"
@@ -478,6 +480,9 @@ def main():
     ap.add_argument("--frames", type=int, default=2, help="--ncu-workload: frames to run")
     ap.add_argument("--batch", type=int, default=16, help="--ncu-workload batch: utterances")
     ap.add_argument("--tiny", action="store_true", help="--ncu-workload: the 2-layer test model")
+    ap.add_argument("--skip-frames", type=int, default=0,
+                    help="batch configs: untimed frames after the warm-up, so the timed window sits deeper in "
+                         "the utterance (longer KV contexts)")
     args = ap.parse_args()
     if args.ncu_workload:
         return run_ncu_workload(args)

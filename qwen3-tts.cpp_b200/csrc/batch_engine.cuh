@@ -49,30 +49,53 @@ struct PagedAttnArgs {
     float scale;
     float * out;              // [B][ldo]
     int ldo;
-    int n_max;                // capacity of the score buffer (positions)
+    int n_max;                // capacity of the score buffer (positions of one CTA's page range)
     uint8_t * xt;             // optional: output also as F16 tiles (row b) for the O-projection GEMM
     int xt_np;
+    int nsplit;               // CTAs per (sequence, kv head) along the pages (1: one CTA, exact softmax)
+    float * part;             // nsplit > 1: [B][NKV][nsplit][G][PA_PART] = max, sum, unnormalised P x V
 };
+constexpr int PA_PART = QTTS_HD + 2;
+constexpr int PA_MAX_SPLIT = 16;
 
 __host__ __device__ inline size_t paged_attn_smem(int n_max, int G) {
     return (size_t) PA_RING * BP_PAGE * QTTS_HD * 2 + (size_t) G * ((n_max + 3) & ~3) * 4 + (size_t) G * QTTS_HD * 4 +
            2 * QTTS_HD * 4 + (size_t)(PA_THREADS / 64) * G * QTTS_HD * 4 + 256;
 }
 
-// One CTA per (sequence b, kv head g): the G query heads of the group share
-// every K/V load.  Item i of the stream is page (i mod np) of K (i < np) or V.
+// One CTA per (sequence b, kv head g), or per (b, g, page range) when split
+// (a.nsplit > 1, long contexts at small batches): the G query heads of the
+// group share every K/V load.  Item i of the stream is page pg0 + (i mod npr)
+// of K (i < npr) or V.  Unsplit: exact two-pass softmax as ggml_soft_max
+// (global max, exp, double sum, p = e * (float)(1/sum) rounded to F16, P x V).
+// Split (flash-decoding): each range writes its local max m, sum l of
+// e = exp(s - m) and the unnormalised sum of e * V; k_attn_combine merges the
+// ranges in order (no F16 rounding of p there).
 __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[PA_RING];
     pdl_trigger();
     pdl_wait();
-    const int NKV = a.n_kv_heads, G = a.n_heads / NKV;
-    const int b = blockIdx.x / NKV, g = blockIdx.x % NKV;
+    const int NKV = a.n_kv_heads, G = a.n_heads / NKV, NS = a.nsplit > 1 ? a.nsplit : 1;
+    const int b = blockIdx.x / (NKV * NS), g = (blockIdx.x / NS) % NKV, sp = blockIdx.x % NS;
     const DevState & S = a.st[b];
     if (S.done) return;
-    const int pos = S.pos, n = pos + 1, np = (n + BP_PAGE - 1) / BP_PAGE;
+    const int pos = S.pos, n = pos + 1, np_all = (n + BP_PAGE - 1) / BP_PAGE;
+    const int chunk = (np_all + NS - 1) / NS;
+    const int pg0 = min(np_all, sp * chunk), npr = min(np_all, pg0 + chunk) - pg0;   // this CTA's pages
+    const int j0 = pg0 * BP_PAGE;                                                    // first position
+    const int n_loc = min(n, (pg0 + npr) * BP_PAGE) - j0;                            // positions here
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = PA_THREADS / 32;
-    const int nk4 = (n + 3) & ~3;
+    const int nk4 = (n_loc + 3) & ~3;
+    const bool has_pos = pos >= j0 && pos < j0 + n_loc;                              // the new row is here
+    if (NS > 1 && npr <= 0) {   // an empty range: a neutral partial
+        for (int t = tid; t < G * PA_PART; t += PA_THREADS) {
+            const int h = t / PA_PART, e = t % PA_PART;
+            a.part[((((size_t) b * NKV + g) * NS + sp) * G + h) * PA_PART + e] = e == 0 ? -INFINITY : 0.0f;
+        }
+        return;
+    }
+    const int np = npr;
     __half * ring = reinterpret_cast<__half *>(smem);
     float * sc = reinterpret_cast<float *>(smem + (size_t) PA_RING * BP_PAGE * QTTS_HD * 2);   // [G][nk4]
     float * qs = sc + G * ((a.n_max + 3) & ~3);                                                  // [G][128]
@@ -89,7 +112,7 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
         for (int s = 0; s < PA_RING; ++s) mbar_init(&full[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         for (int i = 0; i < PA_RING && i < nitems; ++i) {
-            const int kv = i >= np, page = i % np;
+            const int kv = i >= np, page = pg0 + i % np;
             mbar_expect_tx(&full[i], blk);
             bulk_g2s(ring + (size_t) i * BP_PAGE * QTTS_HD,
                      a.pool + bp_off(pt[page], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[i]);
@@ -108,7 +131,7 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
         head_norm_rope_v(x, gv, cs, a.eps, lane);
 #pragma unroll
         for (int k = 0; k < 4; ++k) qs[warp * QTTS_HD + lane * 4 + k] = round_f16(x[k]);
-    } else if (warp == G) {
+    } else if (warp == G && has_pos) {
         const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
         const float4 k4 = *reinterpret_cast<const float4 *>(row + QD + g * QTTS_HD + lane * 4);
         const float4 v4 = *reinterpret_cast<const float4 *>(row + QD + KD + g * QTTS_HD + lane * 4);
@@ -141,9 +164,9 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
         if (__syncthreads_or(!ok)) { ok = false; break; }
         const __half * kb = ring + (size_t) s * BP_PAGE * QTTS_HD;
         for (int p0 = warp * 4; p0 < BP_PAGE; p0 += nw * 4) {
-            const int p = p0 + slot, j = i * BP_PAGE + p;
+            const int p = p0 + slot, j = i * BP_PAGE + p;   // j: position within this CTA's range
             float kv[16];
-            if (j == pos) {
+            if (j + j0 == pos) {
 #pragma unroll
                 for (int d = 0; d < 16; ++d) kv[d] = kcur[sub * 16 + d];
             } else {
@@ -169,14 +192,14 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
                 acc += __shfl_xor_sync(0xffffffffu, acc, 4);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 2);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-                if (sub == 0 && j < n) sc[h * nk4 + j] = __fmul_rn(acc, a.scale);
+                if (sub == 0 && j < n_loc) sc[h * nk4 + j] = __fmul_rn(acc, a.scale);
             }
         }
         __syncthreads();   // slot s is free again
         const int nx = i + PA_RING;
         if (tid == 0 && nx < nitems) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            const int kv = nx >= np, page = nx % np;
+            const int kv = nx >= np, page = pg0 + nx % np;
             mbar_expect_tx(&full[s], blk);
             bulk_g2s(ring + (size_t) s * BP_PAGE * QTTS_HD,
                      a.pool + bp_off(pt[page], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[s]);
@@ -184,20 +207,26 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
         }
     }
     // softmax per head: max, expf, double sum, e * (float)(1/sum), rounded to F16
+    // (split: the range's max and sum go to the partial, e stays unnormalised)
+    __shared__ float s_ml[ATT_MAX_GROUP][2];
     if (ok && warp < G) {
         float * r = sc + warp * nk4;
         float mx = -INFINITY;
-        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, r[j]);
+        for (int j = lane; j < n_loc; j += 32) mx = fmaxf(mx, r[j]);
         mx = warp_max(mx);
         double sum = 0.0;
-        for (int j = lane; j < n; j += 32) {
+        for (int j = lane; j < n_loc; j += 32) {
             const float e = qtts_expf(__fsub_rn(r[j], mx));
             r[j] = e;
             sum += (double) e;
         }
         sum = warp_sum_d(sum);
-        const float inv = (float)(1.0 / sum);
-        for (int j = lane; j < n; j += 32) r[j] = round_f16(__fmul_rn(r[j], inv));
+        if (NS > 1) {
+            if (lane == 0) { s_ml[warp][0] = mx; s_ml[warp][1] = (float) sum; }
+        } else {
+            const float inv = (float)(1.0 / sum);
+            for (int j = lane; j < n_loc; j += 32) r[j] = round_f16(__fmul_rn(r[j], inv));
+        }
     }
     // P x V: thread (position group pq, dims 2 d2 .. 2 d2 + 1) for all G heads
     const int pq = tid >> 6, d2 = tid & 63;
@@ -210,10 +239,10 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
         if (__syncthreads_or(!ok)) { ok = false; break; }
         const __half * vb = ring + (size_t) s * BP_PAGE * QTTS_HD;
         for (int p = pq; p < BP_PAGE; p += PA_THREADS / 64) {
-            const int j = page * BP_PAGE + p;
-            if (j >= n) break;
+            const int j = page * BP_PAGE + p;   // position within this CTA's range
+            if (j >= n_loc) break;
             float2 v;
-            if (j == pos) v = make_float2(vcur[2 * d2], vcur[2 * d2 + 1]);
+            if (j + j0 == pos) v = make_float2(vcur[2 * d2], vcur[2 * d2 + 1]);
             else v = __half22float2(*reinterpret_cast<const __half2 *>(vb + (size_t) p * QTTS_HD + 2 * d2));
 #pragma unroll
             for (int h = 0; h < ATT_MAX_GROUP; ++h)
@@ -227,7 +256,7 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
         const int nx = i + PA_RING;
         if (tid == 0 && nx < nitems) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            const int kv = nx >= np, pg = nx % np;
+            const int kv = nx >= np, pg = pg0 + nx % np;
             mbar_expect_tx(&full[s], blk);
             bulk_g2s(ring + (size_t) s * BP_PAGE * QTTS_HD,
                      a.pool + bp_off(pt[pg], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[s]);
@@ -250,8 +279,43 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
     for (int t = tid; t < G * QTTS_HD; t += PA_THREADS) {
         float s = 0.0f;
         for (int q = 0; q < PA_THREADS / 64; ++q) s = __fadd_rn(s, part[q * G * QTTS_HD + t]);
+        if (NS > 1) {
+            const int h = t / QTTS_HD, d = t % QTTS_HD;
+            float * pp = a.part + ((((size_t) b * NKV + g) * NS + sp) * G + h) * PA_PART;
+            pp[2 + d] = s;
+            if (d == 0) { pp[0] = s_ml[h][0]; pp[1] = s_ml[h][1]; }
+            continue;
+        }
         a.out[(size_t) b * a.ldo + (size_t)(g * G) * QTTS_HD + t] = s;
         if (a.xt) *reinterpret_cast<__half *>(a.xt + tc_x_off(b, g * G * QTTS_HD + t, a.xt_np)) = __float2half_rn(s);
+    }
+}
+
+// Merge of the page ranges of a split paged attention, one CTA per (sequence,
+// kv head), thread d = dim: M = max of the ranges' maxima, then in range order
+// w = exp(m - M), L += l * w (double), O += o * w; out = O * (float)(1 / L).
+__global__ void __launch_bounds__(QTTS_HD) k_attn_combine(PagedAttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int NKV = a.n_kv_heads, G = a.n_heads / NKV, NS = a.nsplit;
+    const int b = blockIdx.x / NKV, g = blockIdx.x % NKV, d = threadIdx.x;
+    if (a.st[b].done) return;
+    for (int h = 0; h < G; ++h) {
+        const float * pp = a.part + (((size_t) b * NKV + g) * NS * G + h) * PA_PART;
+        float M = -INFINITY;
+        for (int s = 0; s < NS; ++s) M = fmaxf(M, pp[(size_t) s * G * PA_PART]);
+        double L = 0.0;
+        float O = 0.0f;
+        for (int s = 0; s < NS; ++s) {
+            const float * q = pp + (size_t) s * G * PA_PART;
+            if (q[0] == -INFINITY) continue;   // an empty range
+            const float w = qtts_expf(__fsub_rn(q[0], M));
+            L += (double) q[1] * (double) w;
+            O = fmaf(q[2 + d], w, O);
+        }
+        const float o = __fmul_rn(O, (float)(1.0 / L));
+        a.out[(size_t) b * a.ldo + (size_t)(g * G + h) * QTTS_HD + d] = o;
+        if (a.xt) *reinterpret_cast<__half *>(a.xt + tc_x_off(b, (g * G + h) * QTTS_HD + d, a.xt_np)) = __float2half_rn(o);
     }
 }
 

@@ -222,7 +222,8 @@ struct BatchEngine {
         max_pages = (n_max + BP_PAGE - 1) / BP_PAGE;
         n_pages = Bmax * max_pages;
         if (!alloc(&pool, sizeof(__half) * bp_page_elems((int) E->L.size(), NKV) * n_pages) ||
-            !alloc(&page_table, sizeof(int) * Bmax * max_pages))
+            !alloc(&page_table, sizeof(int) * Bmax * max_pages) ||
+            !alloc(&attn_part, sizeof(float) * Bmax * NKV * PA_MAX_SPLIT * (NH / NKV) * PA_PART))
             return false;
         std::vector<int> pt((size_t) Bmax * max_pages);
         for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int) i;   // static partition of the pool
@@ -333,6 +334,18 @@ struct BatchEngine {
         }
     }
 
+    // Page ranges per (sequence, kv head) of the talker attention: QTTS_ATTN_SPLIT,
+    // else 1 when the (sequence, kv head) CTAs alone cover the SMs or the capacity
+    // is below 1024 positions, else enough ranges to give every SM two CTAs (at
+    // most 16, at most the pages).
+    float * attn_part = nullptr;
+    int attn_split(int b) const {
+        int ns = 1;
+        if (const char * e = getenv("QTTS_ATTN_SPLIT")) ns = atoi(e);
+        else if (n_max >= 1024 && b * NKV < E->n_sm) ns = (2 * E->n_sm + b * NKV - 1) / (b * NKV);
+        return std::max(1, std::min(std::min(ns, PA_MAX_SPLIT), max_pages));
+    }
+
     void talker_layers() {
         const int G = NH / NKV;
         for (size_t il = 0; il < E->L.size(); ++il) {
@@ -345,9 +358,17 @@ struct BatchEngine {
             pa.rope = rope_t; pa.pool = pool; pa.page_table = page_table; pa.max_pages = max_pages; pa.st = st;
             pa.scale = 1.0f / sqrtf((float) QTTS_HD); pa.out = att; pa.ldo = QD; pa.n_max = n_max;
             pa.xt = q8 ? nullptr : xt2; pa.xt_np = (B + 15) / 16 * 16;
+            // split-KV over page ranges when (sequence, kv head) pairs alone leave SMs idle
+            const int ns = attn_split(B);
+            pa.nsplit = ns;
+            pa.part = attn_part;
+            const int chunk = (max_pages + ns - 1) / ns;
+            pa.n_max = std::min(n_max, chunk * BP_PAGE);
             pb(BC_ATTN_TALKER);
-            pdl_launch(k_attn_paged, dim3(B * NKV), dim3(PA_THREADS), paged_attn_smem(n_max, G), stream, pa);
+            pdl_launch(k_attn_paged, dim3(B * NKV * ns), dim3(PA_THREADS), paged_attn_smem(pa.n_max, G), stream, pa);
+            if (ns > 1) pdl_launch(k_attn_combine, dim3(B * NKV), dim3(QTTS_HD), 0, stream, pa);
             pe();
+            if (ns > 1) launches += 1;
             proj(1, l, t, x, B, FF);
             proj(2, l, t, x, B, FF);
             proj(3, l, t, x, B, FF);

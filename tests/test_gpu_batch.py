@@ -212,3 +212,23 @@ def test_full_q8_batch32_config5_shape(qtts, full_q8):
     b.close()
     eng.close()
     _follow(full_q8, lu, lc, long_frames, [0], engine_order=True, which="q8")
+
+
+@pytest.mark.parametrize("split", [3, 16])
+def test_split_kv_attention_matches_oracle(qtts, tiny_f16, monkeypatch, split):
+    """Talker attention split over KV page ranges (QTTS_ATTN_SPLIT; flash-decoding
+    partials merged in range order): prompts of 40-170 positions give 1-3 pages
+    per sequence, so ranges are full, partial and empty; every sequence follows
+    the oracle under the batched path's near-tie rule."""
+    monkeypatch.setenv("QTTS_ATTN_SPLIT", str(split))
+    eng = qtts.Engine(tiny_f16, 0)
+    H = eng.cfg["hidden_size"]
+    frames = 20
+    utts = [_icl_utterance(9100 + i, p, frames, H) for i, p in enumerate((150, 40, 100))]
+    b = qtts.engine.Batch(eng, max_batch=4, max_positions=256, max_frames=frames)
+    b.begin(utts)
+    assert b.run(frames) == 3 * frames
+    codes = b.codes()
+    b.close()
+    eng.close()
+    _follow(tiny_f16, utts, codes, frames, [0, 1, 2], engine_order=True, which="f16")
