@@ -56,6 +56,17 @@ struct PagedAttnArgs {
     float * part;             // nsplit > 1: [B][NKV][nsplit][G][PA_PART] = max, sum, unnormalised P x V
 };
 constexpr int PA_PART = QTTS_HD + 2;
+
+__device__ __forceinline__ void mbar_arrive_one(uint64_t * m) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(m)) : "memory");
+}
+// OR of a predicate over the compute warps (named barrier 1, PA_THREADS threads).
+__device__ __forceinline__ bool pa_sync_or(bool p) {
+    unsigned r;
+    asm volatile("{\n\t.reg .pred q, o;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred o, 1, %2, q;\n\tselp.u32 %0, 1, 0, o;\n\t}"
+                 : "=r"(r) : "r"((unsigned) p), "r"(PA_THREADS) : "memory");
+    return r != 0;
+}
 constexpr int PA_MAX_SPLIT = 16;
 
 __host__ __device__ inline size_t paged_attn_smem(int n_max, int G) {
@@ -71,12 +82,25 @@ __host__ __device__ inline size_t paged_attn_smem(int n_max, int G) {
 // Split (flash-decoding): each range writes its local max m, sum l of
 // e = exp(s - m) and the unnormalised sum of e * V; k_attn_combine merges the
 // ranges in order (no F16 rounding of p there).
-__global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
+//
+// Pipeline: warp PA_WARPS (the producer) keeps PA_RING page blocks in flight
+// through full / empty mbarriers; the eight compute warps wait on a slot's full
+// barrier themselves and release it with one arrival each, so no block-wide
+// barrier sits between pages (named barrier 1 joins the compute warps only
+// where the softmax needs every score).  Each lane keeps its 16 query dims of
+// the G heads in registers.
+constexpr int PA_WARPS = PA_THREADS / 32;          // compute warps
+constexpr int PA_BLOCK = PA_THREADS + 32;          // + the producer warp
+
+__device__ __forceinline__ void pa_sync_compute() { asm volatile("bar.sync 1, %0;" ::"r"(PA_THREADS) : "memory"); }
+
+template <int G>
+__device__ __forceinline__ void attn_paged_body(const PagedAttnArgs & a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[PA_RING];
-    pdl_trigger();
-    pdl_wait();
-    const int NKV = a.n_kv_heads, G = a.n_heads / NKV, NS = a.nsplit > 1 ? a.nsplit : 1;
+    __shared__ __align__(8) uint64_t full[PA_RING], empty[PA_RING];
+    __shared__ float s_ml[ATT_MAX_GROUP][2];
+    __shared__ int s_bad;
+    const int NKV = a.n_kv_heads, NS = a.nsplit > 1 ? a.nsplit : 1;
     const int b = blockIdx.x / (NKV * NS), g = (blockIdx.x / NS) % NKV, sp = blockIdx.x % NS;
     const DevState & S = a.st[b];
     if (S.done) return;
@@ -85,17 +109,17 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
     const int pg0 = min(np_all, sp * chunk), npr = min(np_all, pg0 + chunk) - pg0;   // this CTA's pages
     const int j0 = pg0 * BP_PAGE;                                                    // first position
     const int n_loc = min(n, (pg0 + npr) * BP_PAGE) - j0;                            // positions here
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = PA_THREADS / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nk4 = (n_loc + 3) & ~3;
     const bool has_pos = pos >= j0 && pos < j0 + n_loc;                              // the new row is here
     if (NS > 1 && npr <= 0) {   // an empty range: a neutral partial
-        for (int t = tid; t < G * PA_PART; t += PA_THREADS) {
+        for (int t = tid; t < G * PA_PART; t += blockDim.x) {
             const int h = t / PA_PART, e = t % PA_PART;
             a.part[((((size_t) b * NKV + g) * NS + sp) * G + h) * PA_PART + e] = e == 0 ? -INFINITY : 0.0f;
         }
         return;
     }
-    const int np = npr;
+    const int np = npr, nitems = 2 * np;
     __half * ring = reinterpret_cast<__half *>(smem);
     float * sc = reinterpret_cast<float *>(smem + (size_t) PA_RING * BP_PAGE * QTTS_HD * 2);   // [G][nk4]
     float * qs = sc + G * ((a.n_max + 3) & ~3);                                                  // [G][128]
@@ -105,20 +129,36 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
     const int * pt = a.page_table + (size_t) b * a.max_pages;
     const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
     const unsigned blk = BP_PAGE * QTTS_HD * 2;
-    const int nitems = 2 * np;
-
-    int issued = 0, consumed = 0;   // stream items (meaningful in thread 0, which issues and waits)
     if (tid == 0) {
-        for (int s = 0; s < PA_RING; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < PA_RING; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], PA_WARPS); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int i = 0; i < PA_RING && i < nitems; ++i) {
-            const int kv = i >= np, page = pg0 + i % np;
-            mbar_expect_tx(&full[i], blk);
-            bulk_g2s(ring + (size_t) i * BP_PAGE * QTTS_HD,
-                     a.pool + bp_off(pt[page], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[i]);
-            issued = i + 1;
-        }
+        s_bad = 0;
     }
+    __syncthreads();
+
+    if (warp == PA_WARPS) {
+        // producer: page blocks of K then V through the ring
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < nitems; ++i) {
+                const int s = i % PA_RING;
+                if (i >= PA_RING) {
+                    if (!mbar_wait(&empty[s], ((i / PA_RING) - 1) & 1)) { s_bad = 1; break; }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                }
+                const int kv = i >= np, page = pg0 + i % np;
+                mbar_expect_tx(&full[s], blk);
+                bulk_g2s(ring + (size_t) s * BP_PAGE * QTTS_HD,
+                         a.pool + bp_off(pt[page], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[s]);
+                issued = i + 1;
+            }
+            // no copy may be in flight when the CTA exits: wait (bounded) for the last ones
+            for (int i = issued > PA_RING ? issued - PA_RING : 0; i < issued; ++i)
+                mbar_wait(&full[i % PA_RING], (i / PA_RING) & 1);
+        }
+        return;
+    }
+
     // q heads and the new k/v row (the row is also appended to its page)
     const float * row = a.qkv + (size_t) b * a.ldq;
     if (warp < G) {
@@ -153,17 +193,24 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
             vcur[lane * 4 + k] = __half2float(vh);
         }
     }
-    __syncthreads();
+    pa_sync_compute();
 
     // scores: per page, 8 lanes per position (16 dims each), 4 positions per warp step
     const int sub = lane & 7, slot = lane >> 3;
+    float qr[G][16];
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+        for (int d = 0; d < 16; ++d) qr[h][d] = qs[h * QTTS_HD + sub * 16 + d];
     bool ok = true;
     for (int i = 0; i < np; ++i) {
         const int s = i % PA_RING;
-        if (tid == 0) { ok = mbar_wait(&full[s], (i / PA_RING) & 1); consumed += ok; }
-        if (__syncthreads_or(!ok)) { ok = false; break; }
+        bool got = true;
+        if (lane == 0) got = mbar_wait(&full[s], (i / PA_RING) & 1);
+        got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+        if (!got) { ok = false; break; }
         const __half * kb = ring + (size_t) s * BP_PAGE * QTTS_HD;
-        for (int p0 = warp * 4; p0 < BP_PAGE; p0 += nw * 4) {
+        for (int p0 = warp * 4; p0 < BP_PAGE; p0 += PA_WARPS * 4) {
             const int p = p0 + slot, j = i * BP_PAGE + p;   // j: position within this CTA's range
             float kv[16];
             if (j + j0 == pos) {
@@ -184,31 +231,22 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
                 }
             }
 #pragma unroll
-            for (int h = 0; h < ATT_MAX_GROUP; ++h) {
-                if (h >= G) break;
+            for (int h = 0; h < G; ++h) {
                 float acc = 0.0f;
 #pragma unroll
-                for (int d = 0; d < 16; ++d) acc = fmaf(kv[d], qs[h * QTTS_HD + sub * 16 + d], acc);
+                for (int d = 0; d < 16; ++d) acc = fmaf(kv[d], qr[h][d], acc);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 4);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 2);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 1);
                 if (sub == 0 && j < n_loc) sc[h * nk4 + j] = __fmul_rn(acc, a.scale);
             }
         }
-        __syncthreads();   // slot s is free again
-        const int nx = i + PA_RING;
-        if (tid == 0 && nx < nitems) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            const int kv = nx >= np, page = pg0 + nx % np;
-            mbar_expect_tx(&full[s], blk);
-            bulk_g2s(ring + (size_t) s * BP_PAGE * QTTS_HD,
-                     a.pool + bp_off(pt[page], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[s]);
-            issued = nx + 1;
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_one(&empty[s]);   // this warp is done with slot s
     }
     // softmax per head: max, expf, double sum, e * (float)(1/sum), rounded to F16
     // (split: the range's max and sum go to the partial, e stays unnormalised)
-    __shared__ float s_ml[ATT_MAX_GROUP][2];
+    ok = !pa_sync_or(!ok);
     if (ok && warp < G) {
         float * r = sc + warp * nk4;
         float mx = -INFINITY;
@@ -228,15 +266,18 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
             for (int j = lane; j < n_loc; j += 32) r[j] = round_f16(__fmul_rn(r[j], inv));
         }
     }
+    pa_sync_compute();
     // P x V: thread (position group pq, dims 2 d2 .. 2 d2 + 1) for all G heads
     const int pq = tid >> 6, d2 = tid & 63;
-    float acc[ATT_MAX_GROUP][2];
+    float acc[G][2];
 #pragma unroll
-    for (int h = 0; h < ATT_MAX_GROUP; ++h) acc[h][0] = acc[h][1] = 0.0f;
+    for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0.0f;
     for (int i = np; ok && i < nitems; ++i) {
         const int s = i % PA_RING, page = i - np;
-        if (tid == 0) { ok = mbar_wait(&full[s], (i / PA_RING) & 1); consumed += ok; }
-        if (__syncthreads_or(!ok)) { ok = false; break; }
+        bool got = true;
+        if (lane == 0) got = mbar_wait(&full[s], (i / PA_RING) & 1);
+        got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+        if (!got) { ok = false; break; }
         const __half * vb = ring + (size_t) s * BP_PAGE * QTTS_HD;
         for (int p = pq; p < BP_PAGE; p += PA_THREADS / 64) {
             const int j = page * BP_PAGE + p;   // position within this CTA's range
@@ -245,37 +286,23 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
             if (j + j0 == pos) v = make_float2(vcur[2 * d2], vcur[2 * d2 + 1]);
             else v = __half22float2(*reinterpret_cast<const __half2 *>(vb + (size_t) p * QTTS_HD + 2 * d2));
 #pragma unroll
-            for (int h = 0; h < ATT_MAX_GROUP; ++h)
-                if (h < G) {
-                    const float pj = sc[h * nk4 + j];
-                    acc[h][0] = fmaf(pj, v.x, acc[h][0]);
-                    acc[h][1] = fmaf(pj, v.y, acc[h][1]);
-                }
+            for (int h = 0; h < G; ++h) {
+                const float pj = sc[h * nk4 + j];
+                acc[h][0] = fmaf(pj, v.x, acc[h][0]);
+                acc[h][1] = fmaf(pj, v.y, acc[h][1]);
+            }
         }
-        __syncthreads();
-        const int nx = i + PA_RING;
-        if (tid == 0 && nx < nitems) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            const int kv = nx >= np, pg = pg0 + nx % np;
-            mbar_expect_tx(&full[s], blk);
-            bulk_g2s(ring + (size_t) s * BP_PAGE * QTTS_HD,
-                     a.pool + bp_off(pt[pg], a.layer, kv, g, 0, a.n_layers, NKV), blk, &full[s]);
-            issued = nx + 1;
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_one(&empty[s]);
     }
-    if (!ok) {
-        // a copy did not land within the wait limit: wait (bounded) for those still in flight
-        if (tid == 0)
-            for (int j = consumed; j < issued; ++j) mbar_wait(&full[j % PA_RING], (j / PA_RING) & 1);
-        return;
-    }
+    ok = !pa_sync_or(!ok);
+    if (!ok) return;   // (the producer drains the copies still in flight)
 #pragma unroll
-    for (int h = 0; h < ATT_MAX_GROUP; ++h)
-        if (h < G) {
-            part[(pq * G + h) * QTTS_HD + 2 * d2] = acc[h][0];
-            part[(pq * G + h) * QTTS_HD + 2 * d2 + 1] = acc[h][1];
-        }
-    __syncthreads();
+    for (int h = 0; h < G; ++h) {
+        part[(pq * G + h) * QTTS_HD + 2 * d2] = acc[h][0];
+        part[(pq * G + h) * QTTS_HD + 2 * d2 + 1] = acc[h][1];
+    }
+    pa_sync_compute();
     for (int t = tid; t < G * QTTS_HD; t += PA_THREADS) {
         float s = 0.0f;
         for (int q = 0; q < PA_THREADS / 64; ++q) s = __fadd_rn(s, part[q * G * QTTS_HD + t]);
@@ -289,6 +316,15 @@ __global__ void __launch_bounds__(PA_THREADS, 2) k_attn_paged(PagedAttnArgs a) {
         a.out[(size_t) b * a.ldo + (size_t)(g * G) * QTTS_HD + t] = s;
         if (a.xt) *reinterpret_cast<__half *>(a.xt + tc_x_off(b, g * G * QTTS_HD + t, a.xt_np)) = __float2half_rn(s);
     }
+}
+
+__global__ void __launch_bounds__(PA_BLOCK, 2) k_attn_paged(PagedAttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int G = a.n_heads / a.n_kv_heads;
+    if (G == 1) attn_paged_body<1>(a);
+    else if (G == 2) attn_paged_body<2>(a);
+    else attn_paged_body<4>(a);
 }
 
 // Merge of the page ranges of a split paged attention, one CTA per (sequence,

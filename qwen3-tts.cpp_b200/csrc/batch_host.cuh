@@ -365,7 +365,7 @@ struct BatchEngine {
             const int chunk = (max_pages + ns - 1) / ns;
             pa.n_max = std::min(n_max, chunk * BP_PAGE);
             pb(BC_ATTN_TALKER);
-            pdl_launch(k_attn_paged, dim3(B * NKV * ns), dim3(PA_THREADS), paged_attn_smem(pa.n_max, G), stream, pa);
+            pdl_launch(k_attn_paged, dim3(B * NKV * ns), dim3(PA_BLOCK), paged_attn_smem(pa.n_max, G), stream, pa);
             if (ns > 1) pdl_launch(k_attn_combine, dim3(B * NKV), dim3(QTTS_HD), 0, stream, pa);
             pe();
             if (ns > 1) launches += 1;
