@@ -403,7 +403,7 @@ def run_ncu_workload(args):
     """A small fixed workload for ncu captures (no timing, no JSON line):
     `frames`: the config's ICL prefill and --frames frames through the frame
     loop (QTTS_FRAME_MODE=fused selects the clustered frame path); `batch`: --batch
-    utterances with 64-position ICL prompts (Q8_0 model for --config q8 / q8long),
+    utterances with --prompt-position ICL prompts (Q8_0 model for --config q8 / q8long),
     --frames batched frames, then two eagerly profiled frames.  A few GB on the device at most."""
     pkg = _pkg()
     d = os.environ.get("QTTS_MODEL_DIR", os.path.join(ROOT, ".models"))
@@ -429,14 +429,15 @@ def run_ncu_workload(args):
     H = eng.cfg["hidden_size"]
     frames = args.frames + 2
     utts = []
+    P = max(16, args.prompt)   # talker prefill positions per utterance (ICL: 9 + reference frames)
     for i in range(args.batch):
         r = np.random.default_rng(2000 + i)
         utts.append(dict(text=r.integers(0, 151643, 24).astype(np.int32), max_len=frames,
                          speaker=r.standard_normal(H).astype(np.float32),
                          ref_text=r.integers(0, 151643, 30).astype(np.int32),
-                         ref_codes=r.integers(0, 2048, (55, 16)).astype(np.int32),
+                         ref_codes=r.integers(0, 2048, (P - 9, 16)).astype(np.int32),
                          rep_penalty=1.05, eos_bias=-1e9))
-    bt = pkg.engine.Batch(eng, max_batch=args.batch, max_positions=64 + frames + 1, max_frames=frames)
+    bt = pkg.engine.Batch(eng, max_batch=args.batch, max_positions=P + frames + 1, max_frames=frames)
     bt.begin(utts)
     got = bt.run(args.frames)
     prof = bt.profile(2)
@@ -480,6 +481,7 @@ def main():
     ap.add_argument("--frames", type=int, default=2, help="--ncu-workload: frames to run")
     ap.add_argument("--batch", type=int, default=16, help="--ncu-workload batch: utterances")
     ap.add_argument("--tiny", action="store_true", help="--ncu-workload: the 2-layer test model")
+    ap.add_argument("--prompt", type=int, default=64, help="--ncu-workload batch: prefill positions per utterance")
     ap.add_argument("--skip-frames", type=int, default=0,
                     help="batch configs: untimed frames after the warm-up, so the timed window sits deeper in "
                          "the utterance (longer KV contexts)")
