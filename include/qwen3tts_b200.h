@@ -68,6 +68,7 @@ typedef struct qtts_timing {
     float frames_ms;         /* frame loop of the last generate / run_frames */
     int32_t frames;          /* frames in frames_ms */
     int32_t kernel_launches; /* engine kernels launched per frame */
+    float load_ms;           /* load_model: GGUF parse, staged weight upload, repacking */
 } qtts_timing;
 
 /* Stage timings of the last generate (no reference counterpart as an ABI; the

@@ -97,6 +97,8 @@ struct Engine {
     float * logits = nullptr, * cp_logits = nullptr, * hidden = nullptr;
     float * logits0 = nullptr, * hidden0 = nullptr;   // prefill outputs kept for rewind
     float * tmp_a = nullptr, * tmp_b = nullptr;
+    float * d_ptext = nullptr;  // projected text rows of project_text [ptext_cap][H]
+    int ptext_cap = 0;
     int * d_ids = nullptr;
     int ids_cap = 0;
     float * d_prow = nullptr;   // prefill rows [prow_cap][H], uploaded once per prefill
@@ -189,12 +191,13 @@ struct Engine {
         if (ptc) { prefill_tc_free(ptc); ptc = nullptr; }
         if (d_prow) { cudaFree(d_prow); d_prow = nullptr; prow_cap = 0; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
-                         cp_logits, hidden, tmp_a, tmp_b, d_ids, st, sp, d_codes, trailing, pad,
+                         cp_logits, hidden, tmp_a, tmp_b, d_ptext, d_ids, st, sp, d_codes, trailing, pad,
                          dbg_t, dbg_cp, d_attn, d_err, logits0, hidden0, ffw, ff_part_o, ff_part_d, ff_xres,
                          ff_xmid, d_fftrace};
         for (void * p : ptrs) if (p) cudaFree(p);
         wbuf = nullptr; d_cp_embd = nullptr; rope_t = rope_cp = nullptr; kc = vc = cpk = cpv = nullptr;
-        x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = tmp_a = tmp_b = nullptr;
+        x = xcp = qkv = att = hbuf = logits = cp_logits = hidden = tmp_a = tmp_b = d_ptext = nullptr;
+        ptext_cap = 0;
         logits0 = hidden0 = nullptr;
         d_ids = nullptr; st = nullptr; sp = nullptr; d_codes = nullptr; trailing = pad = nullptr;
         dbg_t = dbg_cp = nullptr; d_attn = nullptr; d_err = nullptr;
@@ -274,6 +277,7 @@ bool Engine::load(const char * path, int device) {
         device = env && *env ? atoi(env) : 0;
     }
     dev = device;
+    const auto t_load = std::chrono::steady_clock::now();
     QCHECK(cudaSetDevice(dev));
     QCHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
     QCHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
@@ -336,7 +340,24 @@ bool Engine::load(const char * path, int device) {
     if (!init_cp_kv(16)) return false;
     const char * fm = getenv("QTTS_FRAME_MODE");
     if (fm && strcmp(fm, "fused") == 0 && !ff_prepare()) return false;
+    timing.load_ms = (float) std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_load).count();
     return true;
+}
+
+// Q8_0 GGUF blocks (f16 d + 32 int8, 34 bytes) -> the engine's int8 plane
+// [rows][cols] and scale plane [rows][cols/32]: one thread per block.
+__global__ void k_split_q8(const uint8_t * blocks, size_t n_blocks, int8_t * q, __half * d) {
+    for (size_t bi = (size_t) blockIdx.x * blockDim.x + threadIdx.x; bi < n_blocks; bi += (size_t) gridDim.x * blockDim.x) {
+        const uint8_t * src = blocks + bi * 34;
+        uint32_t w[8];
+        for (int k = 0; k < 8; ++k)
+            w[k] = (uint32_t) src[2 + 4 * k] | (uint32_t) src[3 + 4 * k] << 8 | (uint32_t) src[4 + 4 * k] << 16 |
+                   (uint32_t) src[5 + 4 * k] << 24;
+        uint4 * dst = reinterpret_cast<uint4 *>(q + bi * 32);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        d[bi] = __ushort_as_half((unsigned short)(src[0] | src[1] << 8));
+    }
 }
 
 bool Engine::upload_weights(const GgufFile & g) {
@@ -404,7 +425,26 @@ bool Engine::upload_weights(const GgufFile & g) {
     QCHECK(cudaMalloc(&wbuf, total));
     wbytes = total; wused = 0;
 
-    std::vector<uint8_t> stage;
+    // The file mapping is registered as pinned host memory where the platform
+    // allows it (read-only registration of a file mapping), so the uploads below
+    // are direct DMA; otherwise the driver stages the pageable copies itself.
+    // Q8_0 tensors go up as raw blocks and are split into planes on the device.
+    const bool registered =
+        cudaHostRegister(const_cast<uint8_t *>(g.map()), g.size(), cudaHostRegisterReadOnly) == cudaSuccess;
+    if (!registered) cudaGetLastError();
+    size_t q8_max = 0;
+    for (auto & kv : g.tensors())
+        if (kv.second.type == GGML_Q8_0) q8_max = std::max(q8_max, kv.second.nbytes);
+    uint8_t * q8_stage = nullptr;
+    if (q8_max && cudaMalloc(&q8_stage, q8_max) != cudaSuccess) { err = "alloc Q8_0 staging"; return false; }
+    struct Cleanup {
+        const GgufFile & g; bool reg; uint8_t * stage; cudaStream_t st;
+        ~Cleanup() {
+            cudaStreamSynchronize(st);
+            if (stage) cudaFree(stage);
+            if (reg) cudaHostUnregister(const_cast<uint8_t *>(g.map()));
+        }
+    } cleanup{g, registered, q8_stage, stream};
     auto alloc = [&](size_t bytes) -> uint8_t * {
         uint8_t * p = wbuf + wused;
         wused += (bytes + 255) & ~(size_t) 255;
@@ -412,7 +452,7 @@ bool Engine::upload_weights(const GgufFile & g) {
     };
     auto up_raw = [&](const GgufTensor * t) -> const void * {
         uint8_t * p = alloc(t->nbytes);
-        if (cudaMemcpy(p, t->data, t->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+        if (cudaMemcpyAsync(p, t->data, t->nbytes, cudaMemcpyHostToDevice, stream) != cudaSuccess) return nullptr;
         return p;
     };
     // Matrix upload; several GGUF tensors may be stacked along rows (QKV fusion).
@@ -429,7 +469,9 @@ bool Engine::upload_weights(const GgufFile & g) {
             uint8_t * p = alloc((size_t) m.rows * m.cols * 2);
             size_t off = 0;
             for (auto * t : parts) {
-                if (cudaMemcpy(p + off, t->data, t->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) { err = "upload failed"; return false; }
+                if (cudaMemcpyAsync(p + off, t->data, t->nbytes, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+                    err = "upload failed"; return false;
+                }
                 off += t->nbytes;
             }
             m.w = p; m.d = nullptr;
@@ -439,20 +481,13 @@ bool Engine::upload_weights(const GgufFile & g) {
             uint8_t * d = alloc((size_t) m.rows * nb * 2);
             size_t roff = 0;
             for (auto * t : parts) {
-                const size_t rows = (size_t) t->ne[1];
-                stage.resize(rows * m.cols + rows * nb * 2);
-                uint8_t * sq = stage.data();
-                uint8_t * sd = stage.data() + rows * m.cols;
-                for (size_t r = 0; r < rows; ++r)
-                    for (int b = 0; b < nb; ++b) {
-                        const uint8_t * blk = t->data + (r * nb + b) * 34;
-                        memcpy(sd + (r * nb + b) * 2, blk, 2);
-                        memcpy(sq + r * m.cols + (size_t) b * 32, blk + 2, 32);
-                    }
-                if (cudaMemcpy(q + roff * m.cols, sq, rows * m.cols, cudaMemcpyHostToDevice) != cudaSuccess ||
-                    cudaMemcpy(d + roff * nb * 2, sd, rows * nb * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+                const size_t rows = (size_t) t->ne[1], nblk = rows * nb;
+                // stream order: this copy waits for the previous split's reads of the staging buffer
+                if (cudaMemcpyAsync(q8_stage, t->data, t->nbytes, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
                     err = "upload failed"; return false;
                 }
+                k_split_q8<<<(unsigned) std::min<size_t>((nblk + 255) / 256, 4096), 256, 0, stream>>>(
+                    q8_stage, nblk, reinterpret_cast<int8_t *>(q + roff * m.cols), reinterpret_cast<__half *>(d + roff * nb * 2));
                 roff += rows;
             }
             m.w = q; m.d = reinterpret_cast<const __half *>(d);
@@ -494,6 +529,7 @@ bool Engine::upload_weights(const GgufFile & g) {
         if (!up_mat({T("code_pred.lm_head." + std::to_string(gi) + ".weight")}, cp_head[gi])) return false;
     }
     cfg.weight_type = L[0].qkv.type;
+    if (cudaStreamSynchronize(stream) != cudaSuccess || cudaGetLastError() != cudaSuccess) { err = "weight upload failed"; return false; }
     QCHECK(cudaMalloc(&d_cp_embd, sizeof(void *) * cp_embd.size()));
     QCHECK(cudaMemcpy(d_cp_embd, cp_embd.data(), sizeof(void *) * cp_embd.size(), cudaMemcpyHostToDevice));
     if (wused > wbytes) { err = "weight arena overflow"; return false; }
@@ -1227,26 +1263,41 @@ bool Engine::icl_codec_rows(const int32_t * codes, int n_frames, float * out_hos
     return sync("lookup_embedding_rows");
 }
 
-// project_text_tokens (src/tts_transformer.cpp:963-1028) on the device.
+// project_text_tokens (src/tts_transformer.cpp:963-1028) on the device: the
+// ids go up once, every 8-row chunk (gather, fc1 + bias + SiLU, fc2 + bias)
+// writes its rows into one device buffer, and the n rows come back with one
+// copy and one synchronisation.
 bool Engine::project_text(const int32_t * toks, int n, std::vector<float> & out) {
     const qtts_config & c = cfg;
     const int TD = c.text_embd_dim, H = c.hidden_size;
     if (n <= 0) { out.clear(); return true; }
     for (int i = 0; i < n; ++i)
         if (toks[i] < 0 || toks[i] >= c.text_vocab_size) { err = "Embedding token ID out of range"; return false; }
+    if (n > ids_cap) {
+        if (d_ids) cudaFree(d_ids);
+        ids_cap = std::max(n, 2 * ids_cap);
+        if (cudaMalloc(&d_ids, sizeof(int) * ids_cap) != cudaSuccess) { d_ids = nullptr; ids_cap = 0; err = "alloc ids"; return false; }
+    }
+    if (n > ptext_cap) {
+        if (d_ptext) cudaFree(d_ptext);
+        ptext_cap = std::max(n, 256);
+        if (cudaMalloc(&d_ptext, sizeof(float) * (size_t) ptext_cap * H) != cudaSuccess) {
+            d_ptext = nullptr; ptext_cap = 0; err = "alloc text rows"; return false;
+        }
+    }
     out.resize((size_t) n * H);
+    QCHECK(cudaMemcpyAsync(d_ids, toks, sizeof(int) * n, cudaMemcpyHostToDevice, stream));
     for (int c0 = 0; c0 < n; c0 += QTTS_MAX_NV) {
         const int m = std::min(QTTS_MAX_NV, n - c0);
-        QCHECK(cudaMemcpyAsync(d_ids, toks + c0, sizeof(int) * m, cudaMemcpyHostToDevice, stream));
-        k_gather_rows<<<m, 256, 0, stream>>>(text_embd, TD, d_ids, m, tmp_a);
+        float * y = d_ptext + (size_t) c0 * H;
+        k_gather_rows<<<m, 256, 0, stream>>>(text_embd, TD, d_ids + c0, m, tmp_a);
         if (!gemv(fc1, nullptr, tmp_a, TD, m, nullptr, ACT_F16, hbuf, TD, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
         k_bias_silu<<<32, 256, 0, stream>>>(hbuf, fc1_b, TD, TD, m);
-        if (!gemv(fc2, nullptr, hbuf, TD, m, nullptr, ACT_F16, tmp_b, H, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
-        k_bias_add<<<32, 256, 0, stream>>>(tmp_b, fc2_b, H, H, m);
-        QCHECK(cudaMemcpyAsync(out.data() + (size_t) c0 * H, tmp_b, sizeof(float) * m * H, cudaMemcpyDeviceToHost, stream));
-        if (!sync("project_text_tokens")) return false;
+        if (!gemv(fc2, nullptr, hbuf, TD, m, nullptr, ACT_F16, y, H, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
+        k_bias_add<<<32, 256, 0, stream>>>(y, fc2_b, H, H, m);
     }
-    return true;
+    QCHECK(cudaMemcpyAsync(out.data(), d_ptext, sizeof(float) * (size_t) n * H, cudaMemcpyDeviceToHost, stream));
+    return sync("project_text_tokens");
 }
 
 // build_prefill_graph (src/tts_transformer.cpp:1030-1186): host F32 assembly of

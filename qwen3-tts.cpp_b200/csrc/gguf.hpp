@@ -58,6 +58,8 @@ public:
         return it == tensors_.end() ? nullptr : &it->second;
     }
     const std::map<std::string, GgufTensor> & tensors() const { return tensors_; }
+    const uint8_t * map() const { return map_; }
+    size_t size() const { return size_; }
 
 private:
     bool parse(std::string & err) {

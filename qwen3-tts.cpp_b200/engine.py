@@ -56,7 +56,7 @@ class GenParams(C.Structure):
 
 class Timing(C.Structure):
     _fields_ = [("prefill_ms", C.c_float), ("frames_ms", C.c_float), ("frames", C.c_int32),
-                ("kernel_launches", C.c_int32)]
+                ("kernel_launches", C.c_int32), ("load_ms", C.c_float)]
 
 
 class StageTiming(C.Structure):
@@ -263,7 +263,8 @@ class Engine:
     def timing(self) -> dict:
         t = Timing()
         lib().qtts_get_timing(self.h, C.byref(t))
-        return dict(prefill_ms=t.prefill_ms, frames_ms=t.frames_ms, frames=t.frames, kernel_launches=t.kernel_launches)
+        return dict(prefill_ms=t.prefill_ms, frames_ms=t.frames_ms, frames=t.frames, kernel_launches=t.kernel_launches,
+                    load_ms=t.load_ms)
 
     def set_stage_timing(self, enabled: bool):
         self._ok(lib().qtts_set_stage_timing(self.h, int(enabled)), "set_stage_timing")
