@@ -276,6 +276,9 @@ def run_batch(args, cfg):
     from qtts_b200.scheduler import Utterance, lpt_partition
     F = cfg["frames"]
     rng = np.random.default_rng(4242)
+    if args.utts_per_gpu > 0:   # weak scaling: a fixed batch per GPU
+        cfg = dict(cfg, utts_per_gpu=args.utts_per_gpu)
+        cfg.pop("n_utts", None)
     n_utts = cfg["n_utts"] if "n_utts" in cfg else cfg["utts_per_gpu"] * world
     P = rng.integers(cfg["p_lo"], cfg["p_hi"] + 1, n_utts)
     utts = [Utterance(uid=i, prefill=int(P[i]), frames=F) for i in range(n_utts)]
@@ -482,6 +485,8 @@ def main():
     ap.add_argument("--batch", type=int, default=16, help="--ncu-workload batch: utterances")
     ap.add_argument("--tiny", action="store_true", help="--ncu-workload: the 2-layer test model")
     ap.add_argument("--prompt", type=int, default=64, help="--ncu-workload batch: prefill positions per utterance")
+    ap.add_argument("--utts-per-gpu", type=int, default=0,
+                    help="batch configs: utterances per GPU (weak scaling) instead of the config's total")
     ap.add_argument("--skip-frames", type=int, default=0,
                     help="batch configs: untimed frames after the warm-up, so the timed window sits deeper in "
                          "the utterance (longer KV contexts)")
