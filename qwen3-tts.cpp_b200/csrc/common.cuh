@@ -178,29 +178,6 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 constexpr unsigned long long QTTS_SPIN_LIMIT = 1ull << 22;   // polls before a bounded wait gives up
 
-// Tagged words of the dataflow frame kernel: one 64-bit word per activation, the
-// F32 value in the low half and the tag of the write in the high half.  The
-// word is written with one naturally aligned 8-byte store and read with 16-byte
-// loads of two words, each 8-byte half one transaction, so a reader that sees
-// the tag it expects also sees the value written with it: the data carries its
-// own synchronisation and needs no separate flag or barrier.  Stores and loads
-// go to L2 (.cg: no L1 allocation, so a poll never hits a stale L1 line), and
-// are issued without the ordering of strong (.relaxed.gpu) accesses, which
-// held each warp for a round trip per stored row.
-__device__ __forceinline__ void st_tagged(unsigned long long * p, float v, unsigned tag) {
-    const unsigned long long w = ((unsigned long long) tag << 32) | (unsigned long long) __float_as_uint(v);
-    asm volatile("st.global.cg.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-__device__ __forceinline__ void ld_tagged2(const unsigned long long * p, unsigned long long & a,
-                                           unsigned long long & b) {
-    asm volatile("ld.global.cg.v2.u64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
-}
-__device__ __forceinline__ unsigned tag_of(unsigned long long w) { return (unsigned)(w >> 32); }
-__device__ __forceinline__ float val_of(unsigned long long w) { return __uint_as_float((unsigned) w); }
-// Acquire side of a tagged read: later loads of data the producer wrote before
-// its tagged words (KV rows) are ordered after the observed tags.
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-
 // ---- shared-memory weight slices (TMA bulk copies completed on an mbarrier)
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

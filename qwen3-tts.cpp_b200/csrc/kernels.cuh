@@ -675,8 +675,6 @@ struct FusedAttn {
     uint8_t * xt;             // optional: output also as F16 tiles for the O-projection GEMM (row xt_row0 + i)
     int xt_np, xt_row0;
     int warp_heads;           // code-predictor step: one warp per query head (cp_step_attn_warp)
-    unsigned long long * fout;  // dataflow frame kernel: output as tagged words [M][ldo] instead of `out`
-    unsigned ftag;
 };
 
 constexpr int FA_THREADS = 512;
@@ -722,8 +720,8 @@ __device__ __forceinline__ void fused_attn_body(const FusedAttn & a, const int u
         const int j = it * (FA_THREADS / 8) + warp * 4 + slot;
         if (j < nc) {
             const uint4 * kp = reinterpret_cast<const uint4 *>(kbase + (size_t) j * pstride + sub * 16);
-            kr[it][0] = __ldcg(kp);
-            kr[it][1] = __ldcg(kp + 1);
+            kr[it][0] = kp[0];
+            kr[it][1] = kp[1];
         } else {
             kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
         }
@@ -733,7 +731,7 @@ __device__ __forceinline__ void fused_attn_body(const FusedAttn & a, const int u
         const __half2 * vp = reinterpret_cast<const __half2 *>(vbase + (size_t) pg * pstride) + d2;
         const size_t vstep = (size_t) FA_NPG * pstride / 2;
 #pragma unroll
-        for (int t = 0; t < FA_VIT; ++t) vr[t] = pg + t * FA_NPG < nc ? __ldcg(vp + t * vstep) : __float2half2_rn(0.0f);
+        for (int t = 0; t < FA_VIT; ++t) vr[t] = pg + t * FA_NPG < nc ? vp[t * vstep] : __float2half2_rn(0.0f);
     }
     if (warp == 0) {
         const float2 * rp = a.rope + (size_t) pos * (QTTS_HD / 2);
@@ -781,8 +779,8 @@ __device__ __forceinline__ void fused_attn_body(const FusedAttn & a, const int u
             if (p0 > 0) {
                 if (j < nc) {
                     const uint4 * kp = reinterpret_cast<const uint4 *>(kbase + (size_t) j * pstride + sub * 16);
-                    kr[it][0] = __ldcg(kp);
-                    kr[it][1] = __ldcg(kp + 1);
+                    kr[it][0] = kp[0];
+                    kr[it][1] = kp[1];
                 } else {
                     kr[it][0] = kr[it][1] = make_uint4(0, 0, 0, 0);
                 }
@@ -843,7 +841,7 @@ __device__ __forceinline__ void fused_attn_body(const FusedAttn & a, const int u
             const int j = p0 + pg + t * FA_NPG;
             float2 v;
             if (j < nc) {
-                if (p0 > 0) vr[t] = __ldcg(vp + t * vstep);
+                if (p0 > 0) vr[t] = vp[t * vstep];
                 v = __half22float2(vr[t]);
             } else if (j < n) {
                 v = make_float2(vn[(j - jn0) * QTTS_HD + 2 * d2], vn[(j - jn0) * QTTS_HD + 2 * d2 + 1]);
@@ -862,12 +860,7 @@ __device__ __forceinline__ void fused_attn_body(const FusedAttn & a, const int u
         float s = 0.0f;
 #pragma unroll
         for (int q = 0; q < FA_NPG; ++q) s = __fadd_rn(s, part[q * QTTS_HD + tid]);
-        if (a.fout) {   // the KV rows this unit appended are ordered before the tagged output
-            __threadfence();
-            st_tagged(a.fout + (size_t) i * a.ldo + (size_t) hq * QTTS_HD + tid, s, a.ftag);
-        } else {
-            a.out[(size_t) i * a.ldo + (size_t) hq * QTTS_HD + tid] = s;
-        }
+        a.out[(size_t) i * a.ldo + (size_t) hq * QTTS_HD + tid] = s;
         if (a.xt)
             *reinterpret_cast<__half *>(a.xt + tc_x_off(a.xt_row0 + i, hq * QTTS_HD + tid, a.xt_np)) = __float2half_rn(s);
     }
@@ -895,12 +888,12 @@ struct CpStepRegs {
     uint2 vr[CPA_MAX_KEYS];
 };
 
-// Cached K/V are read through L2 (ld.global.cg): within one launch of the
-// dataflow frame kernel another CTA rewrites these positions every frame.
+// Cached V quad of position j (written by earlier launches; no CTA of the
+// reading launch writes positions below n_past).
 __device__ __forceinline__ uint2 cp_step_ld_v(const FusedAttn & a, const int hq, const int j) {
     const int NKV = a.n_kv_heads, g = hq / (a.n_heads / NKV);
     const __half * vb = a.vc + (size_t) g * QTTS_HD + (threadIdx.x & 31) * 4;
-    return __ldcg(reinterpret_cast<const uint2 *>(vb + (size_t) j * NKV * QTTS_HD));
+    return *reinterpret_cast<const uint2 *>(vb + (size_t) j * NKV * QTTS_HD);
 }
 __device__ __forceinline__ void cp_step_load(const FusedAttn & a, const int hq, const int n_past, CpStepRegs & R,
                                              const bool with_v = true) {
@@ -913,7 +906,7 @@ __device__ __forceinline__ void cp_step_load(const FusedAttn & a, const int hq, 
     head_params(a.k_norm, rp, lane, R.gk, R.cs);
     const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + (size_t) jk * pstride + (size_t) g * QTTS_HD + 64 * h);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) R.kr[c] = jk < n_past ? __ldcg(kp + c) : make_uint4(0, 0, 0, 0);
+    for (int c = 0; c < 8; ++c) R.kr[c] = jk < n_past ? kp[c] : make_uint4(0, 0, 0, 0);
     if (with_v) {
 #pragma unroll
         for (int j = 0; j < CPA_MAX_KEYS; ++j) R.vr[j] = j < n_past ? cp_step_ld_v(a, hq, j) : make_uint2(0, 0);
@@ -928,7 +921,6 @@ __device__ __forceinline__ void cp_step_load(const FusedAttn & a, const int hq, 
 // 4 lane .. 4 lane + 3.
 // Cached K/V from registers (CpStepRegs, filled by cp_step_load).
 struct CpKvRegs {
-    static constexpr bool rolled = false;
     CpStepRegs & R;
     __device__ __forceinline__ uint4 k(int c) const { return R.kr[c]; }
     __device__ __forceinline__ uint2 v(int j) const { return R.vr[j]; }
@@ -937,7 +929,6 @@ struct CpKvRegs {
 // K from registers, V quads loaded from L2 once the score loop is done (no
 // registers held for them while K is live).
 struct CpKvLate {
-    static constexpr bool rolled = false;
     CpStepRegs & R;
     const FusedAttn & a;
     int hq, n_past;
@@ -949,23 +940,6 @@ struct CpKvLate {
         for (int j = 0; j < CPA_MAX_KEYS; ++j) R.vr[j] = j < n_past ? cp_step_ld_v(a, hq, j) : make_uint2(0, 0);
     }
 };
-// Cached K/V rows [pos][kv_head][128] F16 of positions 0 .. n_past - 1 staged in
-// shared memory: lane 2 jk + h reads dims [64h, 64h + 64) of key jk, lane l the
-// quad 4l .. 4l + 3 of V row j.
-struct CpKvSmem {
-    static constexpr bool rolled = true;
-    const __half * K, * V;
-    int g, nkv;
-    __device__ __forceinline__ uint4 k(int c) const {
-        const int lane = threadIdx.x & 31;
-        return reinterpret_cast<const uint4 *>(K + ((size_t)(lane >> 1) * nkv + g) * QTTS_HD + 64 * (lane & 1))[c];
-    }
-    __device__ __forceinline__ uint2 v(int j) const {
-        return *reinterpret_cast<const uint2 *>(V + ((size_t) j * nkv + g) * QTTS_HD + (threadIdx.x & 31) * 4);
-    }
-    __device__ __forceinline__ void after_scores() const {}
-};
-
 template <class KV>
 __device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const int hq, const int n_past,
                                                      const CpStepRegs & R, const KV & kv, const float4 q4,
@@ -1016,13 +990,8 @@ __device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const 
             acc = fmaf(kd, qd, acc);
         }
     };
-    if constexpr (KV::rolled) {   // K in shared memory: a rolled loop holds fewer registers
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) chunk(c);
-    } else {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) chunk(c);
-    }
+    for (int c = 0; c < 8; ++c) chunk(c);
     kv.after_scores();
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     const int n = n_past + 1;
@@ -1047,15 +1016,10 @@ __device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const 
 #pragma unroll
         for (int k = 0; k < 4; ++k) o[k] = fmaf(pj, v[k], o[k]);
     };
-    if constexpr (KV::rolled) {
-#pragma unroll 1
-        for (int j = 0; j < n; ++j) key(j);
-    } else {
 #pragma unroll
-        for (int j = 0; j < CPA_MAX_KEYS + 1; ++j) {
-            if (j >= n) break;
-            key(j);
-        }
+    for (int j = 0; j < CPA_MAX_KEYS + 1; ++j) {
+        if (j >= n) break;
+        key(j);
     }
     return make_float4(o[0], o[1], o[2], o[3]);
 }
