@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(FF_THREADS) k_ff_head(const FfHeadArgs A) {
         xs[xpos(c, H)] = ff_part_sum(A.part, A.base, A.np, (size_t) A.nv_in * H, (size_t) A.in_row * H + c);
     __syncthreads();
     ff_stamp(A.fr, A.launch_id, frame, 2);
-    const bool ok = gemv_compute<1>(A.g, blockIdx.x, gridDim.x, ff_smem, work, &mbar, 0u, GemvStorePlain{A.g.y, A.g.ldy});
+    const bool ok = gemv_compute<1>(A.g, blockIdx.x, gridDim.x, ff_smem, work, &mbar, 0u, GemvStorePlain{A.g});
     ff_stamp(A.fr, A.launch_id, frame, 3);
     if (!ok) {
         ff_drain(&mbar, 0u);

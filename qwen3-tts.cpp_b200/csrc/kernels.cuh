@@ -102,11 +102,11 @@ __device__ __forceinline__ float gemv_epi(const GemvArgs & a, int v, float accA,
     return accA;
 }
 
-// Plain output store of a stand-alone or CUDA-graph GEMV: y[v][r].
+// Plain output store of a stand-alone or CUDA-graph GEMV: y[v][r] (the pointer
+// and stride are read from the kernel arguments at the store).
 struct GemvStorePlain {
-    float * y;
-    int ldy;
-    __device__ __forceinline__ void operator()(int r, int, int v, float out) const { y[(size_t) v * ldy + r] = out; }
+    const GemvArgs & g;
+    __device__ __forceinline__ void operator()(int r, int, int v, float out) const { g.y[(size_t) v * g.ldy + r] = out; }
 };
 
 // Activation rows live in shared memory in a two-plane layout per row: column
@@ -131,30 +131,41 @@ __device__ __forceinline__ GemvWork gemv_work(uint8_t * work, int cols, int rpc,
     return w;
 }
 
+// Activation loaders, run by gemv_compute ahead of its first block barrier (in
+// the same function body: a separate load phase before the call measured ~3 %
+// slower per frame on B200).  GemvLoadNone: the caller filled the work area.
+struct GemvLoadNone {
+    static constexpr bool active = false;
+    __device__ __forceinline__ void operator()(const GemvWork &, int, int, int) const {}
+};
 // Activation rows from global memory into the two-plane layout (float4 i =
 // columns 4i..4i+3 -> plane i & 1, chunk i >> 1) and this CTA's residual rows.
 template <int NV>
-__device__ __forceinline__ void gemv_load_global(const GemvArgs & a, int r0, int nrow, int rpc, const GemvWork & w) {
-    const int cols = a.A.cols, tid = threadIdx.x, nt = blockDim.x;
-    const int rstride = (rpc + 3) & ~3;
-    const int c4 = cols >> 2, h8 = cols >> 3;
+struct GemvLoadGlobal {
+    static constexpr bool active = true;
+    const GemvArgs & a;
+    __device__ __forceinline__ void operator()(const GemvWork & w, int r0, int nrow, int rstride) const {
+        const int cols = a.A.cols, tid = threadIdx.x, nt = blockDim.x;
+        const int c4 = cols >> 2, h8 = cols >> 3;
+        const int nv = a.nv;
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-        if (v >= a.nv) break;
-        const float4 * src = reinterpret_cast<const float4 *>(a.x + (size_t) v * a.ldx);
-        float4 * dst = reinterpret_cast<float4 *>(w.xs + v * cols);
-        for (int i = tid; i < c4; i += nt) dst[(i & 1) * h8 + (i >> 1)] = src[i];
+        for (int v = 0; v < NV; ++v) {
+            if (v >= nv) break;
+            const float4 * src = reinterpret_cast<const float4 *>(a.x + (size_t) v * a.ldx);
+            float4 * dst = reinterpret_cast<float4 *>(w.xs + v * cols);
+            for (int i = tid; i < c4; i += nt) dst[(i & 1) * h8 + (i >> 1)] = src[i];
+        }
+        if (a.epi == EPI_RESID)
+            for (int v = 0; v < nv; ++v)
+                for (int r = tid; r < nrow; r += nt) w.rs[v * rstride + r] = a.resid[(size_t) v * a.ldr + r0 + r];
     }
-    if (a.epi == EPI_RESID)
-        for (int v = 0; v < a.nv; ++v)
-            for (int r = tid; r < nrow; r += nt) w.rs[v * rstride + r] = a.resid[(size_t) v * a.ldr + r0 + r];
-}
+};
 
 // GEMV over this CTA's rows [r0, r1) with the weight slice in shared memory
 // (`wsm`, layout slice_layout; complete once mbarrier `m` reaches `parity`, or
-// immediately when m == nullptr) and the activation rows already in the work
-// area (two-plane layout; callers synchronise the block after filling it).
-// Latency-oriented: one warp per row, two block barriers.  The RMSNorm sum of
+// immediately when m == nullptr) and the activation rows in the work area
+// (two-plane layout), written by `load` or, with GemvLoadNone, by the caller,
+// who synchronises the block after filling it.  Latency-oriented: one warp per row, two block barriers.  The RMSNorm sum of
 // squares is a double sum over the CTA (thread-strided partials, warp
 // butterfly, then the 16 warp partials in order); normalisation and F16
 // rounding happen once, in place.  Reduction order of a row: lane l
@@ -162,10 +173,11 @@ __device__ __forceinline__ void gemv_load_global(const GemvArgs & a, int r0, int
 // F16 chunk; one 32-block term per lane pair for Q8_0), then a butterfly over
 // the 32 lanes.  Outputs go through `store(r, rl, v, value)`; xn_smem (optional)
 // receives every CTA's unrounded normalised row 0 in column order.
-template <int NV, class Store>
+template <int NV, class Store, class Load = GemvLoadNone>
 __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, const int ncta, const uint8_t * wsm,
                                              uint8_t * work, uint64_t * m, unsigned parity, const Store & store,
-                                             float * xn_smem = nullptr, unsigned long long * ready_stamp = nullptr) {
+                                             float * xn_smem = nullptr, unsigned long long * ready_stamp = nullptr,
+                                             const Load & load = Load{}) {
     __shared__ double s_red[QTTS_WARPS][NV];
     const int cols = a.A.cols, rows = a.A.rows;
     const int rpc = gemv_rpc(rows, ncta);
@@ -181,6 +193,10 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
     int8_t * qa = W.qa;
     float * da = W.da;
     const int h8 = cols >> 3;
+    if (Load::active) {
+        load(W, r0, nrow, rstride);
+        __syncthreads();
+    }
 
     // 1. RMSNorm partial sums; thread 0 waits for the weight slice
     const bool has_norm = a.norm_g != nullptr;
@@ -350,16 +366,13 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
     return true;
 }
 
-// GEMV with activations and residuals read from global memory (gemv_load_global)
+// GEMV with activations and residuals read from global memory (GemvLoadGlobal)
 // and outputs stored to a.y.
 template <int NV>
 __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, const int ncta, const uint8_t * wsm,
                                            uint8_t * work, uint64_t * m, unsigned parity) {
-    const int rpc = gemv_rpc(a.A.rows, ncta);
-    const int r0 = cta * rpc, r1 = min(a.A.rows, r0 + rpc);
-    gemv_load_global<NV>(a, r0, r1 > r0 ? r1 - r0 : 0, rpc, gemv_work<NV>(work, a.A.cols, rpc, a.A.type == W_Q8_0));
-    __syncthreads();
-    return gemv_compute<NV>(a, cta, ncta, wsm, work, m, parity, GemvStorePlain{a.y, a.ldy});
+    return gemv_compute<NV>(a, cta, ncta, wsm, work, m, parity, GemvStorePlain{a}, nullptr, nullptr,
+                            GemvLoadGlobal<NV>{a});
 }
 
 // Stand-alone GEMV launch (CUDA-graph path, prefill, kernel tests): thread 0
@@ -879,91 +892,40 @@ __device__ __forceinline__ void fused_attn_body(const FusedAttn & a, const int u
 // quads) is issued before the first use; the new row's K/V stay in registers.
 constexpr int CPA_MAX_KEYS = 16;
 
-// Registers of one step-attention warp loaded before the q|k|v row is needed:
-// norm gains, RoPE row and the cached K halves (and, when preloaded, V quads).
-struct CpStepRegs {
-    float gq[4], gk[4];
-    float2 cs[4];
-    uint4 kr[8];
-    uint2 vr[CPA_MAX_KEYS];
-};
-
-// Cached V quad of position j (written by earlier launches; no CTA of the
-// reading launch writes positions below n_past).
-__device__ __forceinline__ uint2 cp_step_ld_v(const FusedAttn & a, const int hq, const int j) {
-    const int NKV = a.n_kv_heads, g = hq / (a.n_heads / NKV);
-    const __half * vb = a.vc + (size_t) g * QTTS_HD + (threadIdx.x & 31) * 4;
-    return *reinterpret_cast<const uint2 *>(vb + (size_t) j * NKV * QTTS_HD);
-}
-__device__ __forceinline__ void cp_step_load(const FusedAttn & a, const int hq, const int n_past, CpStepRegs & R,
-                                             const bool with_v = true) {
+// xt_row >= 0 and a.xt set: the output row is also written as F16 tiles (row
+// xt_row) for a tcgen05 O-projection.
+__device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int hq, const int n_past,
+                                                  const int xt_row = -1) {
     const int lane = threadIdx.x & 31;
     const int NKV = a.n_kv_heads, G = a.n_heads / NKV, g = hq / G;
+    const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
     const size_t pstride = (size_t) NKV * QTTS_HD;
     const int h = lane & 1, jk = lane >> 1;
     const float2 * rp = a.rope + (size_t) n_past * (QTTS_HD / 2);
-    head_params(a.q_norm, rp, lane, R.gq, R.cs);
-    head_params(a.k_norm, rp, lane, R.gk, R.cs);
-    const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + (size_t) jk * pstride + (size_t) g * QTTS_HD + 64 * h);
+    const float4 q4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) hq * QTTS_HD + lane * 4);
+    const float4 k4 = *reinterpret_cast<const float4 *>(a.qkv + QD + (size_t) g * QTTS_HD + lane * 4);
+    const float4 v4 = *reinterpret_cast<const float4 *>(a.qkv + QD + KD + (size_t) g * QTTS_HD + lane * 4);
+    float gq[4], gk[4];
+    float2 cs[4];
+    head_params(a.q_norm, rp, lane, gq, cs);
+    head_params(a.k_norm, rp, lane, gk, cs);
+    uint4 kr[8];
+    {
+        const uint4 * kp = reinterpret_cast<const uint4 *>(a.kc + (size_t) jk * pstride + (size_t) g * QTTS_HD + 64 * h);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) R.kr[c] = jk < n_past ? kp[c] : make_uint4(0, 0, 0, 0);
-    if (with_v) {
-#pragma unroll
-        for (int j = 0; j < CPA_MAX_KEYS; ++j) R.vr[j] = j < n_past ? cp_step_ld_v(a, hq, j) : make_uint2(0, 0);
+        for (int c = 0; c < 8; ++c) kr[c] = jk < n_past ? kp[c] : make_uint4(0, 0, 0, 0);
     }
-}
-
-// The step attention of query head hq from its q row quad q4 and its group's new
-// k / v quads (lane l: dims 4l .. 4l + 3).  kv_write: this warp appends the
-// group's new K/V row to the cache (the group's first head).  late_v: the cached
-// V quads are loaded here, after the scores (no registers held for them while
-// K is live); otherwise they come from R.  Returns the output quad of dims
-// 4 lane .. 4 lane + 3.
-// Cached K/V from registers (CpStepRegs, filled by cp_step_load).
-struct CpKvRegs {
-    CpStepRegs & R;
-    __device__ __forceinline__ uint4 k(int c) const { return R.kr[c]; }
-    __device__ __forceinline__ uint2 v(int j) const { return R.vr[j]; }
-    __device__ __forceinline__ void after_scores() const {}
-};
-// K from registers, V quads loaded from L2 once the score loop is done (no
-// registers held for them while K is live).
-struct CpKvLate {
-    CpStepRegs & R;
-    const FusedAttn & a;
-    int hq, n_past;
-    __device__ __forceinline__ uint4 k(int c) const { return R.kr[c]; }
-    __device__ __forceinline__ uint2 v(int j) const { return R.vr[j]; }
-    __device__ __forceinline__ void after_scores() const {
-        asm volatile("" ::: "memory");   // the V loads stay below the score loop
+    uint2 vr[CPA_MAX_KEYS];
+    {
+        const __half * vb = a.vc + (size_t) g * QTTS_HD + lane * 4;
 #pragma unroll
-        for (int j = 0; j < CPA_MAX_KEYS; ++j) R.vr[j] = j < n_past ? cp_step_ld_v(a, hq, j) : make_uint2(0, 0);
+        for (int j = 0; j < CPA_MAX_KEYS; ++j)
+            vr[j] = j < n_past ? *reinterpret_cast<const uint2 *>(vb + (size_t) j * pstride) : make_uint2(0, 0);
     }
-};
-template <class KV>
-__device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const int hq, const int n_past,
-                                                     const CpStepRegs & R, const KV & kv, const float4 q4,
-                                                     const float4 k4, const float4 v4, const bool kv_write);
-
-__device__ __forceinline__ float4 cp_step_compute(const FusedAttn & a, const int hq, const int n_past,
-                                                  CpStepRegs & R, const float4 q4, const float4 k4,
-                                                  const float4 v4, const bool kv_write, const bool late_v = false) {
-    if (!late_v) return cp_step_compute_kv(a, hq, n_past, R, CpKvRegs{R}, q4, k4, v4, kv_write);
-    return cp_step_compute_kv(a, hq, n_past, R, CpKvLate{R, a, hq, n_past}, q4, k4, v4, kv_write);
-}
-
-template <class KV>
-__device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const int hq, const int n_past,
-                                                     const CpStepRegs & R, const KV & kv, const float4 q4,
-                                                     const float4 k4, const float4 v4, const bool kv_write) {
-    const int lane = threadIdx.x & 31;
-    const int NKV = a.n_kv_heads, g = hq / (a.n_heads / NKV);
-    const size_t pstride = (size_t) NKV * QTTS_HD;
-    const int h = lane & 1, jk = lane >> 1;
     float xq[4] = {q4.x, q4.y, q4.z, q4.w};
     float xk[4] = {k4.x, k4.y, k4.z, k4.w};
-    head_norm_rope_v(xq, R.gq, R.cs, a.eps, lane);
-    head_norm_rope_v(xk, R.gk, R.cs, a.eps, lane);
+    head_norm_rope_v(xq, gq, cs, a.eps, lane);
+    head_norm_rope_v(xk, gk, cs, a.eps, lane);
     float kn[4], vn[4];   // the new row's k, v (F16-rounded), dims 4 lane .. 4 lane + 3
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -971,28 +933,25 @@ __device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const 
         xq[k] = round_f16(xq[k]);
         kn[k] = __half2float(kh);
         vn[k] = __half2float(vh);
-        if (kv_write) {
+        if (hq % G == 0) {
             a.kc[(size_t) n_past * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = kh;
             a.vc[(size_t) n_past * pstride + (size_t) g * QTTS_HD + lane * 4 + k] = vh;
         }
     }
     // score of key jk over dims [64h, 64h + 64): q and the new k come from lanes 16h .. 16h + 15
     float acc = 0.0f;
-    auto chunk = [&](const int c) {   // dims 64h + 8c .. 64h + 8c + 7
-        const uint4 kc4 = jk < n_past ? kv.k(c) : make_uint4(0, 0, 0, 0);
-        const __half2 * hp = reinterpret_cast<const __half2 *>(&kc4);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const __half2 * hp = reinterpret_cast<const __half2 *>(&kr[c]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            const int src = 16 * h + 2 * c + (e >> 2);     // lane holding dim 64h + 8c + e
+            const int d = 8 * c + e, src = 16 * h + (d >> 2);     // lane holding dim 64h + d
             const float qd = __shfl_sync(0xffffffffu, xq[e & 3], src);
             const float kd_new = __shfl_sync(0xffffffffu, kn[e & 3], src);
             const float kd = jk < n_past ? (e & 1 ? __high2float(hp[e >> 1]) : __low2float(hp[e >> 1])) : kd_new;
             acc = fmaf(kd, qd, acc);
         }
-    };
-#pragma unroll
-    for (int c = 0; c < 8; ++c) chunk(c);
-    kv.after_scores();
+    }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     const int n = n_past + 1;
     const float s = jk < n ? __fmul_rn(acc, a.scale) : -INFINITY;
@@ -1001,13 +960,14 @@ __device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const 
     const double sum = warp_sum_d(h ? 0.0 : (double) e);
     const float p = round_f16(__fmul_rn(e, (float)(1.0 / sum)));
     float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    auto key = [&](const int j) {   // keys in order: P x V chained per dim
+#pragma unroll
+    for (int j = 0; j < CPA_MAX_KEYS + 1; ++j) {
+        if (j >= n) break;
         const float pj = __shfl_sync(0xffffffffu, p, 2 * j);
         float v[4];
         if (j < n_past) {
-            const uint2 vq = kv.v(j < CPA_MAX_KEYS ? j : 0);
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&vq.x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&vq.y));
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[j < CPA_MAX_KEYS ? j : 0].x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[j < CPA_MAX_KEYS ? j : 0].y));
             v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
         } else {
 #pragma unroll
@@ -1015,32 +975,11 @@ __device__ __forceinline__ float4 cp_step_compute_kv(const FusedAttn & a, const 
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) o[k] = fmaf(pj, v[k], o[k]);
-    };
-#pragma unroll
-    for (int j = 0; j < CPA_MAX_KEYS + 1; ++j) {
-        if (j >= n) break;
-        key(j);
     }
-    return make_float4(o[0], o[1], o[2], o[3]);
-}
-
-// xt_row >= 0 and a.xt set: the output row is also written as F16 tiles (row
-// xt_row) for a tcgen05 O-projection.
-__device__ __forceinline__ void cp_step_attn_body(const FusedAttn & a, const int hq, const int n_past,
-                                                  const int xt_row = -1) {
-    const int lane = threadIdx.x & 31;
-    const int NKV = a.n_kv_heads, G = a.n_heads / NKV, g = hq / G;
-    const int QD = a.n_heads * QTTS_HD, KD = NKV * QTTS_HD;
-    const float4 q4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t) hq * QTTS_HD + lane * 4);
-    const float4 k4 = *reinterpret_cast<const float4 *>(a.qkv + QD + (size_t) g * QTTS_HD + lane * 4);
-    const float4 v4 = *reinterpret_cast<const float4 *>(a.qkv + QD + KD + (size_t) g * QTTS_HD + lane * 4);
-    CpStepRegs R;
-    cp_step_load(a, hq, n_past, R);
-    const float4 o = cp_step_compute(a, hq, n_past, R, q4, k4, v4, hq % G == 0);
-    *reinterpret_cast<float4 *>(a.out + (size_t) hq * QTTS_HD + lane * 4) = o;
+    *reinterpret_cast<float4 *>(a.out + (size_t) hq * QTTS_HD + lane * 4) = make_float4(o[0], o[1], o[2], o[3]);
     if (a.xt && xt_row >= 0) {
-        __align__(8) __half h4[4] = {__float2half_rn(o.x), __float2half_rn(o.y), __float2half_rn(o.z),
-                                      __float2half_rn(o.w)};
+        __align__(8) __half h4[4] = {__float2half_rn(o[0]), __float2half_rn(o[1]), __float2half_rn(o[2]),
+                                      __float2half_rn(o[3])};
         *reinterpret_cast<uint2 *>(a.xt + tc_x_off(xt_row, hq * QTTS_HD + lane * 4, a.xt_np)) =
             *reinterpret_cast<const uint2 *>(h4);
     }
