@@ -139,6 +139,7 @@ struct Engine {
     enum { FM_GRAPH = 0, FM_FUSED = 1 };
     int frame_mode = FM_GRAPH;
     int * d_err = nullptr;        // set by a fused kernel whose bounded wait gave up
+    size_t gemv_smem_floor = 0;   // dynamic shared memory floor of a GEMV launch (see alloc_activations)
     struct FfLayerW { DMat qkv_g, o_g, down_r; };
     std::vector<FfLayerW> ffL, ffCP;
     uint8_t * ffw = nullptr;      // repacked weights of the fused frame path
@@ -564,6 +565,14 @@ bool Engine::alloc_activations() {
     QCHECK(cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX));
     QCHECK(cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) QTTS_GEMV_SMEM_MAX));
     QCHECK(cudaFuncSetAttribute(k_fused_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    // The GEMV grid is two 512-thread CTAs per SM.  At 40 registers or fewer a
+    // third CTA would fit and the block scheduler packs three onto some SMs
+    // (measured 15 % slower per frame); should the kernel ever compile that
+    // small, a shared-memory floor keeps the residency at two.
+    int nb = 0, smem_sm = 0;
+    QCHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemv<1>, QTTS_WARPS * 32, 0));
+    QCHECK(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    gemv_smem_floor = nb > 2 ? (size_t) smem_sm / 3 + 1024 : 0;
     return true;
 }
 
@@ -663,6 +672,7 @@ GemvArgs Engine::make_gemv(const DMat & A, const DMat * B, const float * xin, in
     a.xn_out = xn_out; a.ldxn = ldxn; a.done = done;
     const int NVt = nv == 1 ? 1 : nv == 2 ? 2 : 8;
     if (!gemv_shape(A, B != nullptr, norm != nullptr, NVt, n_sm, ncta_out, slice_out, smem_out)) *ncta_out = 0;
+    *smem_out = std::max(*smem_out, gemv_smem_floor);
     return a;
 }
 

@@ -134,16 +134,41 @@ __device__ __forceinline__ GemvWork gemv_work(uint8_t * work, int cols, int rpc,
 // Activation loaders, run by gemv_compute ahead of its first block barrier (in
 // the same function body: a separate load phase before the call measured ~3 %
 // slower per frame on B200).  GemvLoadNone: the caller filled the work area.
+constexpr int GEMV_RPT = 6;   // activation values per thread held in registers (one row, cols <= 6 x threads)
+
+// Column of planar position p of the two-plane layout (see xpos).
+__device__ __forceinline__ int planar_col(int p, int cols) {
+    const int half = cols >> 1;
+    const int q = p >= half ? p - half : p;
+    return ((q >> 2) << 3) + (p >= half ? 4 : 0) + (q & 3);
+}
+
 struct GemvLoadNone {
-    static constexpr bool active = false;
+    static constexpr bool active = false, regs_ok = false;
     __device__ __forceinline__ void operator()(const GemvWork &, int, int, int) const {}
+    __device__ __forceinline__ void regs(float (&)[GEMV_RPT], const GemvWork &, int, int, int) const {}
 };
 // Activation rows from global memory into the two-plane layout (float4 i =
 // columns 4i..4i+3 -> plane i & 1, chunk i >> 1) and this CTA's residual rows.
 template <int NV>
 struct GemvLoadGlobal {
-    static constexpr bool active = true;
+    static constexpr bool active = true, regs_ok = NV == 1;
     const GemvArgs & a;
+    // One row, cols <= GEMV_RPT x threads: thread t loads the values of the
+    // planar positions p = t + k * threads that it reduces and normalises
+    // (column planar_col(p)) into xr[k], so the RMSNorm sum needs no block
+    // barrier first; residual rows go to the work area as above.
+    __device__ __forceinline__ void regs(float (&xr)[GEMV_RPT], const GemvWork & w, int r0, int nrow,
+                                         int rstride) const {
+        const int cols = a.A.cols, tid = threadIdx.x, nt = blockDim.x;
+#pragma unroll
+        for (int k = 0; k < GEMV_RPT; ++k) {
+            const int p = tid + k * nt;
+            xr[k] = p < cols ? a.x[planar_col(p, cols)] : 0.0f;
+        }
+        if (a.epi == EPI_RESID)
+            for (int r = tid; r < nrow; r += nt) w.rs[r] = a.resid[(size_t) r0 + r];
+    }
     __device__ __forceinline__ void operator()(const GemvWork & w, int r0, int nrow, int rstride) const {
         const int cols = a.A.cols, tid = threadIdx.x, nt = blockDim.x;
         const int c4 = cols >> 2, h8 = cols >> 3;
@@ -193,21 +218,38 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
     int8_t * qa = W.qa;
     float * da = W.da;
     const int h8 = cols >> 3;
-    if (Load::active) {
+    // inreg: this thread's activation values (planar positions tid + k nt) in xr.
+    // F16 weights only: with Q8_0 weights the frame measured slower either way
+    // (the quantiser reads the row back from shared memory in 32-column blocks).
+    const bool inreg = Load::regs_ok && !q8 && cols <= GEMV_RPT * nt;
+    float xr[GEMV_RPT];
+    if (inreg) {
+        load.regs(xr, W, r0, nrow, rstride);
+    } else if (Load::active) {
         load(W, r0, nrow, rstride);
         __syncthreads();
     }
 
-    // 1. RMSNorm partial sums; thread 0 waits for the weight slice
+    // 1. RMSNorm partial sums (positions p = tid, tid + nt, ... in order); thread 0
+    // waits for the weight slice
     const bool has_norm = a.norm_g != nullptr;
     if (has_norm) {
-#pragma unroll
-        for (int v = 0; v < NV; ++v) {
-            if (v >= nv) break;
+        if (inreg) {
             double ss = 0.0;
-            for (int p = tid; p < cols; p += nt) { const float t = xs[v * cols + p]; ss += (double) __fmul_rn(t, t); }
+#pragma unroll
+            for (int k = 0; k < GEMV_RPT; ++k)
+                if (tid + k * nt < cols) ss += (double) __fmul_rn(xr[k], xr[k]);
             ss = warp_sum_d(ss);
-            if (lane == 0) s_red[warp][v] = ss;
+            if (lane == 0) s_red[warp][0] = ss;
+        } else {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                if (v >= nv) break;
+                double ss = 0.0;
+                for (int p = tid; p < cols; p += nt) { const float t = xs[v * cols + p]; ss += (double) __fmul_rn(t, t); }
+                ss = warp_sum_d(ss);
+                if (lane == 0) s_red[warp][v] = ss;
+            }
         }
     }
     bool ok = true;
@@ -225,7 +267,7 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
 
     // 2. normalise (x * scale) * gain, round to F16 for F16 weights with an F16 activation
     const bool round16 = !q8 && a.act == ACT_F16;
-    if (has_norm || round16 || a.xn_out || xn_smem) {
+    if (inreg || has_norm || round16 || a.xn_out || xn_smem) {
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
             if (v >= nv) break;
@@ -235,15 +277,19 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
                 for (int w = 0; w < nw; ++w) ss += s_red[w][v];
                 scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(ss / (double) cols), a.eps)));
             }
-            const int half = cols >> 1;
-            for (int p = tid; p < cols; p += nt) {
-                const int q = p >= half ? p - half : p;              // column of planar position p
-                const int c = ((q >> 2) << 3) + (p >= half ? 4 : 0) + (q & 3);
-                float t = xs[v * cols + p];
+            auto put = [&](const int p, float t) {
+                const int c = planar_col(p, cols);
                 if (has_norm) t = __fmul_rn(__fmul_rn(t, scale), gain[c]);
                 if (a.xn_out && r0 == 0) a.xn_out[(size_t) v * a.ldxn + c] = t;   // hidden_states (post-norm, unrounded)
                 if (xn_smem && v == 0) xn_smem[c] = t;
                 xs[v * cols + p] = round16 ? round_f16(t) : t;
+            };
+            if (inreg) {
+#pragma unroll
+                for (int k = 0; k < GEMV_RPT; ++k)
+                    if (tid + k * nt < cols) put(tid + k * nt, xr[k]);
+            } else {
+                for (int p = tid; p < cols; p += nt) put(p, xs[v * cols + p]);
             }
         }
         __syncthreads();
@@ -378,9 +424,12 @@ __device__ __forceinline__ bool gemv_slice(const GemvArgs & a, const int cta, co
 // Stand-alone GEMV launch (CUDA-graph path, prefill, kernel tests): thread 0
 // stages this CTA's weight slice into shared memory with TMA bulk copies while
 // all threads load the activations.  Launched with programmatic dependent
-// launch, the copy starts while the previous kernel still runs.
+// launch, the copy starts while the previous kernel still runs.  Registers
+// capped at 48: two 512-thread CTAs per SM then leave a quarter of the register
+// file for the next kernel's CTAs (at 49-64 registers two CTAs take all of it,
+// measured 4 % slower per frame).
 template <int NV>
-__global__ void __launch_bounds__(QTTS_WARPS * 32) k_gemv(GemvArgs a, size_t slice_bytes) {
+__global__ void __maxnreg__(48) k_gemv(GemvArgs a, size_t slice_bytes) {
     pdl_trigger();
     const int rpc = gemv_rpc(a.A.rows, gridDim.x);
     if ((int) blockIdx.x * rpc >= a.A.rows) return;
