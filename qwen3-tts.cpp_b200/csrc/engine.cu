@@ -60,6 +60,29 @@ struct GenSession {
     DevState st0{};   // frame state right after the prefill (rewind target)
 };
 
+// Recipe of a prompt (build_prefill_graph, src/tts_transformer.cpp:1030-1186, and
+// build_prefill_graph_icl, :1188-1472), written on the host and carried out on
+// the device: the text tokens to project, the codec rows to gather, the speaker
+// row, the ICL reference frames, and each output row's terms in order.
+struct PromptSrc {
+    enum { NONE = 0, TEXT, CODEC, SPEAKER, ICL };
+    int kind = NONE, idx = 0;
+};
+struct PromptPlan {
+    std::vector<int32_t> text, codec, icl_codes;   // icl_codes: [n_icl][16]
+    int n_icl = 0;
+    const float * speaker = nullptr;               // host row, or nullptr
+    enum { PREFILL = 0, TRAILING, PAD };
+    struct Row { int dst, r; PromptSrc a, b; int zero_first; };
+    std::vector<Row> rows;
+    int plen = 0, tlen = 0;
+    void add(int dst, int r, PromptSrc a, PromptSrc b = {}, int zero_first = 0) {
+        rows.push_back({dst, r, a, b, zero_first});
+        if (dst == PREFILL) plen = std::max(plen, r + 1);
+        if (dst == TRAILING) tlen = std::max(tlen, r + 1);
+    }
+};
+
 struct Engine;
 struct PrefillTC;
 constexpr int PREFILL_TC_ROWS = 128;   // prompt rows per tensor-core chunk (hi/lo ffn_down doubles MMA N to 256)
@@ -101,8 +124,13 @@ struct Engine {
     int ptext_cap = 0;
     int * d_ids = nullptr;
     int ids_cap = 0;
-    float * d_prow = nullptr;   // prefill rows [prow_cap][H], uploaded once per prefill
+    float * d_prow = nullptr;   // prefill rows [prow_cap][H]: assembled on the device, or uploaded
     int prow_cap = 0;
+    float * d_asm = nullptr;    // prompt assembly terms: gathered codec rows, speaker row, ICL frame rows
+    int asm_cap = 0;
+    PromptRow * d_pops = nullptr;   // prompt row recipes for k_prompt_rows
+    int pops_cap = 0;
+    cudaEvent_t ev_asm0 = nullptr, ev_asm1 = nullptr;
     PrefillTC * ptc = nullptr;  // tensor-core prefill (created on first use)
 
     // frame state
@@ -191,6 +219,10 @@ struct Engine {
         if (graph) { cudaGraphExecDestroy(graph); graph = nullptr; }
         if (ptc) { prefill_tc_free(ptc); ptc = nullptr; }
         if (d_prow) { cudaFree(d_prow); d_prow = nullptr; prow_cap = 0; }
+        if (d_asm) { cudaFree(d_asm); d_asm = nullptr; asm_cap = 0; }
+        if (d_pops) { cudaFree(d_pops); d_pops = nullptr; pops_cap = 0; }
+        if (ev_asm0) { cudaEventDestroy(ev_asm0); ev_asm0 = nullptr; }
+        if (ev_asm1) { cudaEventDestroy(ev_asm1); ev_asm1 = nullptr; }
         void * ptrs[] = {wbuf, d_cp_embd, rope_t, rope_cp, kc, vc, cpk, cpv, x, xcp, qkv, att, hbuf, logits,
                          cp_logits, hidden, tmp_a, tmp_b, d_ptext, d_ids, st, sp, d_codes, trailing, pad,
                          dbg_t, dbg_cp, d_attn, d_err, logits0, hidden0, ffw, ff_part_o, ff_part_d, ff_xres,
@@ -245,11 +277,10 @@ struct Engine {
     bool prefill(const float * rows_host, int n, int n_past, float * hidden_out, float * logits_out);
     bool project_text(const int32_t * toks, int n, std::vector<float> & out);
     bool lookup(int table, const int32_t * ids, int n, std::vector<float> & out);
-    bool icl_codec_rows(const int32_t * codes, int n_frames, float * out_host);
-    bool build_prefill(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
-                       std::vector<float> & padv);
-    bool build_prefill_icl(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
-                           std::vector<float> & padv);
+    bool project_text_dev(const int * d_tok, int n);
+    bool grow_rows(float ** buf, int * cap, int n, const char * what);
+    bool plan_prompt(const qtts_generate_params * p, PromptPlan & P);
+    bool assemble_prompt(const PromptPlan & P);
     int begin(const qtts_generate_params * p);
     int run_frames(int n, int32_t * codes_out);
     int rewind();
@@ -1178,21 +1209,18 @@ bool Engine::prefill(const float * rows_host, int n, int n_past, float * hidden_
     if (n <= 0) { err = "n_tokens must be > 0"; return false; }
     if (n_ctx == 0 && !init_kv(std::max(256, n_past + n + 16))) return false;
     if (n_past + n > n_ctx) { err = "Context length exceeded"; return false; }
-    // rows uploaded once; chunks of 8 rows through the GEMV path, or of up to 128
+    // rows uploaded once (rows_host), or already assembled in d_prow (rows_host ==
+    // nullptr, generate); chunks of 8 rows through the GEMV path, or of up to 128
     // rows through tcgen05 GEMMs (kind::f16 for F16 weights, kind::i8 for Q8_0;
     // QTTS_PREFILL=gemv|tc, default tc for prompts of more than 8 rows)
-    if (n > prow_cap) {
-        if (d_prow) cudaFree(d_prow);
-        prow_cap = std::max(n, 256);
-        if (cudaMalloc(&d_prow, sizeof(float) * (size_t) prow_cap * H) != cudaSuccess) {
-            d_prow = nullptr; prow_cap = 0; err = "alloc prefill rows"; return false;
-        }
-    }
+    if (!rows_host && n > prow_cap) { err = "prefill rows not assembled"; return false; }
+    if (rows_host && !grow_rows(&d_prow, &prow_cap, n, "alloc prefill rows")) return false;
     const char * pm = getenv("QTTS_PREFILL");
     const bool tc = pm && *pm ? strcmp(pm, "tc") == 0 : n > QTTS_MAX_NV;
     const int chunk = tc ? PREFILL_TC_ROWS : QTTS_MAX_NV;
     QCHECK(cudaEventRecord(ev0, stream));
-    QCHECK(cudaMemcpyAsync(d_prow, rows_host, sizeof(float) * (size_t) n * H, cudaMemcpyHostToDevice, stream));
+    if (rows_host)
+        QCHECK(cudaMemcpyAsync(d_prow, rows_host, sizeof(float) * (size_t) n * H, cudaMemcpyHostToDevice, stream));
     for (int c0 = 0; c0 < n; c0 += chunk) {
         const int M = std::min(chunk, n - c0);
         float * X = d_prow + (size_t) c0 * H;
@@ -1243,43 +1271,40 @@ bool Engine::lookup(int table, const int32_t * ids, int n, std::vector<float> & 
     return true;
 }
 
-// Summed codec rows of n_frames reference frames ([n_frames][16] codes) into
-// out_host[n_frames][H]: one upload, one kernel, one download.
-bool Engine::icl_codec_rows(const int32_t * codes, int n_frames, float * out_host) {
-    const qtts_config & c = cfg;
-    const int H = c.hidden_size, NCB = std::min(16, c.n_codebooks);
-    for (int f = 0; f < n_frames; ++f)
-        for (int cb = 0; cb < NCB; ++cb) {
-            const int id = codes[(size_t) f * 16 + cb];
-            if (id < 0 || id >= (cb == 0 ? c.codec_vocab_size : c.code_pred_vocab_size)) {
-                err = "Embedding token ID out of range"; return false;
-            }
-        }
-    if ((size_t) n_frames * 16 > (size_t) ids_cap || n_frames > prow_cap) {
-        if (d_ids) cudaFree(d_ids);
-        ids_cap = std::max(ids_cap, n_frames * 16);
-        if (cudaMalloc(&d_ids, sizeof(int) * ids_cap) != cudaSuccess) { d_ids = nullptr; ids_cap = 0; err = "alloc ids"; return false; }
-        if (n_frames > prow_cap) {
-            if (d_prow) cudaFree(d_prow);
-            prow_cap = std::max(n_frames, 256);
-            if (cudaMalloc(&d_prow, sizeof(float) * (size_t) prow_cap * H) != cudaSuccess) {
-                d_prow = nullptr; prow_cap = 0; err = "alloc prefill rows"; return false;
-            }
-        }
+// Grows a device row buffer [cap][H] to at least n rows (contents not kept).
+bool Engine::grow_rows(float ** buf, int * cap, int n, const char * what) {
+    if (n <= *cap) return true;
+    if (*buf) cudaFree(*buf);
+    *cap = std::max(n, 256);
+    if (cudaMalloc(buf, sizeof(float) * (size_t) *cap * cfg.hidden_size) != cudaSuccess) {
+        *buf = nullptr; *cap = 0; err = what; return false;
     }
-    QCHECK(cudaMemcpyAsync(d_ids, codes, sizeof(int) * n_frames * 16, cudaMemcpyHostToDevice, stream));
-    k_icl_codec_rows<<<n_frames, 256, 0, stream>>>(codec_embd, d_cp_embd, d_ids, NCB, H, d_prow);
-    QCHECK(cudaMemcpyAsync(out_host, d_prow, sizeof(float) * (size_t) n_frames * H, cudaMemcpyDeviceToHost, stream));
-    return sync("lookup_embedding_rows");
+    return true;
 }
 
-// project_text_tokens (src/tts_transformer.cpp:963-1028) on the device: the
-// ids go up once, every 8-row chunk (gather, fc1 + bias + SiLU, fc2 + bias)
-// writes its rows into one device buffer, and the n rows come back with one
-// copy and one synchronisation.
-bool Engine::project_text(const int32_t * toks, int n, std::vector<float> & out) {
+// project_text_tokens (src/tts_transformer.cpp:963-1028) of n ids already on the
+// device into d_ptext rows [0, n): per 8-row chunk the gather, fc1 + bias + SiLU
+// and fc2 + bias.  Each row's arithmetic is independent of the chunking.
+bool Engine::project_text_dev(const int * d_tok, int n) {
     const qtts_config & c = cfg;
     const int TD = c.text_embd_dim, H = c.hidden_size;
+    if (!grow_rows(&d_ptext, &ptext_cap, n, "alloc text rows")) return false;
+    for (int c0 = 0; c0 < n; c0 += QTTS_MAX_NV) {
+        const int m = std::min(QTTS_MAX_NV, n - c0);
+        float * y = d_ptext + (size_t) c0 * H;
+        k_gather_rows<<<m, 256, 0, stream>>>(text_embd, TD, d_tok + c0, m, tmp_a);
+        if (!gemv(fc1, nullptr, tmp_a, TD, m, nullptr, ACT_F16, hbuf, TD, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
+        k_bias_silu<<<32, 256, 0, stream>>>(hbuf, fc1_b, TD, TD, m);
+        if (!gemv(fc2, nullptr, hbuf, TD, m, nullptr, ACT_F16, y, H, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
+        k_bias_add<<<32, 256, 0, stream>>>(y, fc2_b, H, H, m);
+    }
+    return true;
+}
+
+// qtts_project_text: the projected rows back to the host (one upload, one copy back).
+bool Engine::project_text(const int32_t * toks, int n, std::vector<float> & out) {
+    const qtts_config & c = cfg;
+    const int H = c.hidden_size;
     if (n <= 0) { out.clear(); return true; }
     for (int i = 0; i < n; ++i)
         if (toks[i] < 0 || toks[i] >= c.text_vocab_size) { err = "Embedding token ID out of range"; return false; }
@@ -1288,142 +1313,164 @@ bool Engine::project_text(const int32_t * toks, int n, std::vector<float> & out)
         ids_cap = std::max(n, 2 * ids_cap);
         if (cudaMalloc(&d_ids, sizeof(int) * ids_cap) != cudaSuccess) { d_ids = nullptr; ids_cap = 0; err = "alloc ids"; return false; }
     }
-    if (n > ptext_cap) {
-        if (d_ptext) cudaFree(d_ptext);
-        ptext_cap = std::max(n, 256);
-        if (cudaMalloc(&d_ptext, sizeof(float) * (size_t) ptext_cap * H) != cudaSuccess) {
-            d_ptext = nullptr; ptext_cap = 0; err = "alloc text rows"; return false;
-        }
-    }
     out.resize((size_t) n * H);
     QCHECK(cudaMemcpyAsync(d_ids, toks, sizeof(int) * n, cudaMemcpyHostToDevice, stream));
-    for (int c0 = 0; c0 < n; c0 += QTTS_MAX_NV) {
-        const int m = std::min(QTTS_MAX_NV, n - c0);
-        float * y = d_ptext + (size_t) c0 * H;
-        k_gather_rows<<<m, 256, 0, stream>>>(text_embd, TD, d_ids + c0, m, tmp_a);
-        if (!gemv(fc1, nullptr, tmp_a, TD, m, nullptr, ACT_F16, hbuf, TD, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
-        k_bias_silu<<<32, 256, 0, stream>>>(hbuf, fc1_b, TD, TD, m);
-        if (!gemv(fc2, nullptr, hbuf, TD, m, nullptr, ACT_F16, y, H, nullptr, 0, EPI_STORE, nullptr, 0, nullptr)) return false;
-        k_bias_add<<<32, 256, 0, stream>>>(y, fc2_b, H, H, m);
-    }
+    if (!project_text_dev(d_ids, n)) return false;
     QCHECK(cudaMemcpyAsync(out.data(), d_ptext, sizeof(float) * (size_t) n * H, cudaMemcpyDeviceToHost, stream));
     return sync("project_text_tokens");
 }
 
-// build_prefill_graph (src/tts_transformer.cpp:1030-1186): host F32 assembly of
-// projected text rows and codec embedding rows, as in the reference.
-bool Engine::build_prefill(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
-                           std::vector<float> & padv) {
+// The prompt recipe of generate (build_prefill_graph, src/tts_transformer.cpp:
+// 1030-1186) or generate_icl (build_prefill_graph_icl, :1188-1472): which text
+// tokens are projected, which codec rows are gathered, and each row's terms in
+// the reference's order.  Host-only; ids are checked here.
+bool Engine::plan_prompt(const qtts_generate_params * p, PromptPlan & P) {
     const qtts_config & c = cfg;
-    const int H = c.hidden_size;
-    if (!p->text_tokens) { err = "text_tokens is null"; return false; }
-    if (p->n_tokens < 4) { err = "Need at least 4 text tokens for prefill"; return false; }
-    int32_t special[3] = {c.tts_bos_token_id, c.tts_eos_token_id, c.tts_pad_token_id};
-    std::vector<float> sp3, role, first, cpe, te;
-    if (!project_text(special, 3, sp3) || !project_text(p->text_tokens, 3, role)) return false;
-    const float * bos = sp3.data();
-    const float * eos = sp3.data() + H;
-    padv.assign(sp3.data() + 2 * H, sp3.data() + 3 * H);
-    std::vector<int32_t> ctoks;
-    if (p->language_id < 0) ctoks = {c.codec_nothink_id, c.codec_think_bos_id, c.codec_think_eos_id};
-    else ctoks = {c.codec_think_id, c.codec_think_bos_id, p->language_id, c.codec_think_eos_id};
-    int32_t tail[2] = {c.codec_pad_id, c.codec_bos_id};
-    if (!lookup(0, ctoks.data(), (int) ctoks.size(), cpe) || !lookup(0, tail, 2, te)) return false;
-    const bool spk = p->speaker_embd != nullptr;
-    const int cin = (int) ctoks.size() + (spk ? 1 : 0) + 2;
-    std::vector<float> ci((size_t) cin * H);
-    memcpy(ci.data(), cpe.data(), cpe.size() * 4);
-    int dst = (int) ctoks.size();
-    if (spk) { memcpy(ci.data() + (size_t) dst * H, p->speaker_embd, H * 4); ++dst; }
-    memcpy(ci.data() + (size_t) dst * H, te.data(), te.size() * 4);
-    const int ov = cin - 1;
-    std::vector<float> cov((size_t) ov * H);
-    for (int t = 0; t < ov; ++t) {
-        const float * o = (t == ov - 1) ? bos : padv.data();
-        for (int d = 0; d < H; ++d) cov[(size_t) t * H + d] = o[d] + ci[(size_t) t * H + d];
+    const bool icl = p->ref_codec_tokens != nullptr;
+    using S = PromptSrc;
+    auto text = [&](int i) { return S{S::TEXT, i}; };
+    auto codec = [&](int i) { return S{S::CODEC, i}; };
+    if (icl) {
+        if (!p->text_tokens || p->n_tokens < 4) { err = "ICL: need at least 4 target text tokens"; return false; }
+        if (!p->ref_codec_tokens || p->n_ref_frames < 1) { err = "ICL: need at least 1 reference codec frame"; return false; }
+    } else {
+        if (!p->text_tokens) { err = "text_tokens is null"; return false; }
+        if (p->n_tokens < 4) { err = "Need at least 4 text tokens for prefill"; return false; }
     }
-    if (!project_text(p->text_tokens + 3, 1, first)) return false;
-    std::vector<float> fb(H);
-    for (int d = 0; d < H; ++d) fb[d] = first[d] + ci[(size_t)(cin - 1) * H + d];
-    std::vector<float> ins;
-    int ilen = 0;
-    if (p->instruct_tokens && p->n_instruct > 0) {
-        if (!project_text(p->instruct_tokens, p->n_instruct, ins)) return false;
-        ilen = p->n_instruct;
+    // projected text rows: 0 tts_bos, 1 tts_eos, 2 tts_pad, 3-5 the role tokens, then per mode
+    P.text = {c.tts_bos_token_id, c.tts_eos_token_id, c.tts_pad_token_id, p->text_tokens[0], p->text_tokens[1],
+              p->text_tokens[2]};
+    const S bos = text(0), eos = text(1), pad = text(2);
+    // codec prefix: think tokens (language or not), [speaker], codec_pad, codec_bos
+    if (icl || p->language_id < 0) P.codec = {c.codec_nothink_id, c.codec_think_bos_id, c.codec_think_eos_id};
+    else P.codec = {c.codec_think_id, c.codec_think_bos_id, p->language_id, c.codec_think_eos_id};
+    const int nthink = (int) P.codec.size();
+    P.codec.push_back(c.codec_pad_id);
+    P.codec.push_back(c.codec_bos_id);
+    P.speaker = p->speaker_embd;
+    std::vector<S> ci;
+    for (int i = 0; i < nthink; ++i) ci.push_back(codec(i));
+    if (P.speaker) ci.push_back(S{S::SPEAKER, 0});
+    ci.push_back(codec(nthink));
+    ci.push_back(codec(nthink + 1));
+    const int cin = (int) ci.size(), ov = cin - 1;
+    int r = 0;
+    if (!icl) {
+        int ilen = 0;
+        if (p->instruct_tokens && p->n_instruct > 0) {
+            ilen = p->n_instruct;
+            for (int i = 0; i < ilen; ++i) {
+                P.add(PromptPlan::PREFILL, r++, text((int) P.text.size()));
+                P.text.push_back(p->instruct_tokens[i]);
+            }
+        }
+        for (int k = 0; k < 3; ++k) P.add(PromptPlan::PREFILL, r++, text(3 + k));
+        for (int t = 0; t < ov; ++t) P.add(PromptPlan::PREFILL, r++, t == ov - 1 ? bos : pad, ci[t]);
+        P.add(PromptPlan::PREFILL, r++, text((int) P.text.size()), ci[cin - 1]);   // first text token + codec_bos
+        P.text.push_back(p->text_tokens[3]);
+        const int ntrail = std::max(0, p->n_tokens - 9);
+        for (int i = 0; i < ntrail; ++i) {
+            P.add(PromptPlan::TRAILING, i, text((int) P.text.size()));
+            P.text.push_back(p->text_tokens[4 + i]);
+        }
+        P.add(PromptPlan::TRAILING, ntrail, eos);
+    } else {
+        for (int k = 0; k < 3; ++k) P.add(PromptPlan::PREFILL, r++, text(3 + k));
+        for (int t = 0; t < ov; ++t) P.add(PromptPlan::PREFILL, r++, t == ov - 1 ? bos : pad, ci[t]);
+        // reference text [3, n_ref_text - 5) + target text [3, n_tokens - 5) + tts_eos
+        int rs = 3, re = p->n_ref_text - 5; if (re < rs) re = rs;
+        int ts = 3, tend = p->n_tokens - 5; if (tend < ts) tend = ts;
+        const int t0 = (int) P.text.size();
+        for (int i = rs; i < re && i < p->n_ref_text; ++i) P.text.push_back(p->ref_text_tokens[i]);
+        for (int i = ts; i < tend && i < p->n_tokens; ++i) P.text.push_back(p->text_tokens[i]);
+        P.text.push_back(c.tts_eos_token_id);
+        const int nt = (int) P.text.size() - t0;
+        const int nct = p->n_ref_frames + 1;
+        P.codec.push_back(c.codec_bos_id);   // codec row of ICL position 0
+        const S cbos = codec((int) P.codec.size() - 1);
+        // ICL rows: (0 + text or pad) + (codec_bos, then the summed reference frames)
+        for (int i = 0; i < nct; ++i)
+            P.add(PromptPlan::PREFILL, r++, i < nt ? text(t0 + i) : pad, i == 0 ? cbos : S{S::ICL, i - 1}, 1);
+        for (int i = nct; i < nt; ++i) P.add(PromptPlan::TRAILING, i - nct, text(t0 + i));
+        P.n_icl = p->n_ref_frames;
+        P.icl_codes.assign(p->ref_codec_tokens, p->ref_codec_tokens + (size_t) p->n_ref_frames * 16);
+        const int NCB = std::min(16, c.n_codebooks);
+        for (int f = 0; f < P.n_icl; ++f)
+            for (int cb = 0; cb < NCB; ++cb) {
+                const int id = P.icl_codes[(size_t) f * 16 + cb];
+                if (id < 0 || id >= (cb == 0 ? c.codec_vocab_size : c.code_pred_vocab_size)) {
+                    err = "Embedding token ID out of range"; return false;
+                }
+            }
     }
-    const int plen = ilen + 3 + ov + 1;
-    rows.assign((size_t) plen * H, 0.0f);
-    if (ilen) memcpy(rows.data(), ins.data(), ins.size() * 4);
-    memcpy(rows.data() + (size_t) ilen * H, role.data(), role.size() * 4);
-    memcpy(rows.data() + (size_t)(ilen + 3) * H, cov.data(), cov.size() * 4);
-    memcpy(rows.data() + (size_t)(plen - 1) * H, fb.data(), H * 4);
-    const int ntrail = std::max(0, p->n_tokens - 9);
-    std::vector<float> tp;
-    if (ntrail > 0 && !project_text(p->text_tokens + 4, ntrail, tp)) return false;
-    trail.assign((size_t)(ntrail + 1) * H, 0.0f);
-    if (ntrail > 0) memcpy(trail.data(), tp.data(), tp.size() * 4);
-    memcpy(trail.data() + (size_t) ntrail * H, eos, H * 4);
+    P.add(PromptPlan::PAD, 0, pad);
+    for (int32_t id : P.text)
+        if (id < 0 || id >= c.text_vocab_size) { err = "Embedding token ID out of range"; return false; }
+    for (int32_t id : P.codec)
+        if (id < 0 || id >= c.codec_vocab_size) { err = "Embedding token ID out of range"; return false; }
     return true;
 }
 
-// build_prefill_graph_icl (src/tts_transformer.cpp:1188-1472).
-bool Engine::build_prefill_icl(const qtts_generate_params * p, std::vector<float> & rows, std::vector<float> & trail,
-                               std::vector<float> & padv) {
+// Carries out a prompt recipe on the device: one upload of every id, the text
+// projection into d_ptext, the codec rows (k_gather_rows), the speaker row and
+// the ICL frame rows (k_icl_codec_rows) into d_asm, then k_prompt_rows writes
+// the prefill rows (d_prow), the trailing text rows and the pad row.  No row
+// crosses PCIe; the buffers it writes must be sized by the caller for trailing.
+bool Engine::assemble_prompt(const PromptPlan & P) {
     const qtts_config & c = cfg;
-    const int H = c.hidden_size;
-    if (!p->text_tokens || p->n_tokens < 4) { err = "ICL: need at least 4 target text tokens"; return false; }
-    if (!p->ref_codec_tokens || p->n_ref_frames < 1) { err = "ICL: need at least 1 reference codec frame"; return false; }
-    int32_t special[3] = {c.tts_bos_token_id, c.tts_eos_token_id, c.tts_pad_token_id};
-    std::vector<float> sp3, role, cpe, te;
-    if (!project_text(special, 3, sp3) || !project_text(p->text_tokens, 3, role)) return false;
-    const float * bos = sp3.data();
-    padv.assign(sp3.data() + 2 * H, sp3.data() + 3 * H);
-    int32_t ctoks[3] = {c.codec_nothink_id, c.codec_think_bos_id, c.codec_think_eos_id};
-    int32_t tail[2] = {c.codec_pad_id, c.codec_bos_id};
-    if (!lookup(0, ctoks, 3, cpe) || !lookup(0, tail, 2, te)) return false;
-    const bool spk = p->speaker_embd != nullptr;
-    const int cin = 3 + (spk ? 1 : 0) + 2;
-    std::vector<float> ci((size_t) cin * H);
-    memcpy(ci.data(), cpe.data(), cpe.size() * 4);
-    int dst = 3;
-    if (spk) { memcpy(ci.data() + (size_t) dst * H, p->speaker_embd, H * 4); ++dst; }
-    memcpy(ci.data() + (size_t) dst * H, te.data(), te.size() * 4);
-    const int ov = cin - 1;
-    rows.assign((size_t)(3 + ov) * H, 0.0f);
-    memcpy(rows.data(), role.data(), role.size() * 4);
-    for (int t = 0; t < ov; ++t) {
-        const float * o = (t == ov - 1) ? bos : padv.data();
-        for (int d = 0; d < H; ++d) rows[(size_t)(3 + t) * H + d] = o[d] + ci[(size_t) t * H + d];
+    const int H = c.hidden_size, NCB = std::min(16, c.n_codebooks);
+    const int nT = (int) P.text.size(), nC = (int) P.codec.size(), nI = P.n_icl;
+    const int nid = nT + nC + nI * 16;
+    if (nid > ids_cap) {
+        if (d_ids) cudaFree(d_ids);
+        ids_cap = std::max(nid, 2 * ids_cap);
+        if (cudaMalloc(&d_ids, sizeof(int) * ids_cap) != cudaSuccess) { d_ids = nullptr; ids_cap = 0; err = "alloc ids"; return false; }
     }
-    int rs = 3, re = p->n_ref_text - 5; if (re < rs) re = rs;
-    int ts = 3, tend = p->n_tokens - 5; if (tend < ts) tend = ts;
-    std::vector<int32_t> comb;
-    for (int i = rs; i < re && i < p->n_ref_text; ++i) comb.push_back(p->ref_text_tokens[i]);
-    for (int i = ts; i < tend && i < p->n_tokens; ++i) comb.push_back(p->text_tokens[i]);
-    comb.push_back(c.tts_eos_token_id);
-    const int nct = p->n_ref_frames + 1;
-    std::vector<float> cf((size_t) nct * H, 0.0f), r0;
-    int32_t cbos = c.codec_bos_id;
-    if (!lookup(0, &cbos, 1, r0)) return false;
-    memcpy(cf.data(), r0.data(), H * 4);
-    // per reference frame: codec_embd[cb0] then += code_pred_embd[cb-1][code], in
-    // codebook order, summed on the device in one pass (k_icl_codec_rows)
-    if (!icl_codec_rows(p->ref_codec_tokens, p->n_ref_frames, cf.data() + H)) return false;
-    const int nt = (int) comb.size();
-    std::vector<float> tp;
-    if (!project_text(comb.data(), nt, tp)) return false;
-    const int icl = nct;
-    const size_t base = rows.size() / H;
-    rows.resize((base + icl) * H, 0.0f);
-    for (int i = 0; i < icl; ++i) {
-        float * d = rows.data() + (base + i) * H;
-        const float * t = i < nt ? tp.data() + (size_t) i * H : padv.data();
-        for (int k = 0; k < H; ++k) d[k] = 0.0f + t[k];
-        const float * cr = cf.data() + (size_t) i * H;
-        for (int k = 0; k < H; ++k) d[k] += cr[k];
+    if (!grow_rows(&d_asm, &asm_cap, nC + 1 + nI, "alloc prompt terms") ||
+        !grow_rows(&d_prow, &prow_cap, P.plen, "alloc prefill rows"))
+        return false;
+    const int nr = (int) P.rows.size();
+    if (nr > pops_cap) {
+        if (d_pops) cudaFree(d_pops);
+        pops_cap = std::max(nr, 256);
+        if (cudaMalloc(&d_pops, sizeof(PromptRow) * pops_cap) != cudaSuccess) {
+            d_pops = nullptr; pops_cap = 0; err = "alloc prompt recipe"; return false;
+        }
     }
-    trail.clear();
-    if (nt > nct) trail.assign(tp.data() + (size_t) nct * H, tp.data() + (size_t) nt * H);
+    float * codec_rows = d_asm, * spk_row = d_asm + (size_t) nC * H, * icl_rows = d_asm + (size_t)(nC + 1) * H;
+    auto src = [&](const PromptSrc & s) -> const float * {
+        switch (s.kind) {
+            case PromptSrc::TEXT: return d_ptext + (size_t) s.idx * H;
+            case PromptSrc::CODEC: return codec_rows + (size_t) s.idx * H;
+            case PromptSrc::SPEAKER: return spk_row;
+            case PromptSrc::ICL: return icl_rows + (size_t) s.idx * H;
+            default: return nullptr;
+        }
+    };
+    std::vector<int32_t> ids;
+    ids.reserve(nid);
+    ids.insert(ids.end(), P.text.begin(), P.text.end());
+    ids.insert(ids.end(), P.codec.begin(), P.codec.end());
+    ids.insert(ids.end(), P.icl_codes.begin(), P.icl_codes.end());
+    if (!ev_asm0) { QCHECK(cudaEventCreate(&ev_asm0)); QCHECK(cudaEventCreate(&ev_asm1)); }
+    QCHECK(cudaEventRecord(ev_asm0, stream));
+    QCHECK(cudaMemcpyAsync(d_ids, ids.data(), sizeof(int) * nid, cudaMemcpyHostToDevice, stream));
+    if (!project_text_dev(d_ids, nT)) return false;
+    k_gather_rows<<<nC, 256, 0, stream>>>(codec_embd, H, d_ids + nT, nC, codec_rows);
+    if (P.speaker) QCHECK(cudaMemcpyAsync(spk_row, P.speaker, sizeof(float) * H, cudaMemcpyHostToDevice, stream));
+    if (nI) k_icl_codec_rows<<<nI, 256, 0, stream>>>(codec_embd, d_cp_embd, d_ids + nT + nC, NCB, H, icl_rows);
+    // (ICL rows: codec_embd[cb0] then += code_pred_embd[cb-1][code] in codebook order)
+    std::vector<PromptRow> ops(nr);
+    for (int i = 0; i < nr; ++i) {
+        const PromptPlan::Row & R = P.rows[i];
+        float * dst = R.dst == PromptPlan::PREFILL ? d_prow + (size_t) R.r * H
+                      : R.dst == PromptPlan::TRAILING ? trailing + (size_t) R.r * H : pad;
+        ops[i] = PromptRow{dst, src(R.a), src(R.b), R.zero_first};
+    }
+    QCHECK(cudaMemcpyAsync(d_pops, ops.data(), sizeof(PromptRow) * nr, cudaMemcpyHostToDevice, stream));
+    k_prompt_rows<<<nr, 256, 0, stream>>>(d_pops, H);
+    QCHECK(cudaGetLastError());
+    QCHECK(cudaEventRecord(ev_asm1, stream));
     return true;
 }
 
@@ -1432,15 +1479,13 @@ int Engine::begin(const qtts_generate_params * p) {
     const int H = c.hidden_size;
     sess = GenSession{};
     attn_rows.clear();
-    std::vector<float> rows, trail, padv;
-    const bool icl = p->ref_codec_tokens != nullptr;
+    PromptPlan plan;
     stages = qtts_stage_timing{};
     const auto t_build = std::chrono::steady_clock::now();
-    if (icl) { if (!build_prefill_icl(p, rows, trail, padv)) return -1; }
-    else if (!build_prefill(p, rows, trail, padv)) return -1;
-    stages.prefill_build_ms =
+    if (!plan_prompt(p, plan)) return -1;
+    const float plan_ms =
         (float) std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_build).count();
-    const int plen = (int)(rows.size() / H), tlen = (int)(trail.size() / H);
+    const int plen = plan.plen, tlen = plan.tlen;
     const int required = plen + p->max_len + 8;
     if (n_ctx < required || n_ctx > std::max(required * 2, 512)) { if (!init_kv(required)) return -1; }
     n_used = 0;
@@ -1478,14 +1523,12 @@ int Engine::begin(const qtts_generate_params * p) {
             }
         }
     }
-    if (!prefill(rows.data(), plen, 0, nullptr, nullptr)) return -1;
+    if (!assemble_prompt(plan)) return -1;   // prefill rows, trailing rows and the pad row, on the device
+    if (!prefill(nullptr, plen, 0, nullptr, nullptr)) return -1;
     stages.prefill_forward_ms = timing.prefill_ms;
-    if (tlen > 0 && cudaMemcpyAsync(trailing, trail.data(), sizeof(float) * tlen * H, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
-        err = "upload trailing"; return -1;
-    }
-    if (cudaMemcpyAsync(pad, padv.data(), sizeof(float) * H, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
-        err = "upload pad"; return -1;
-    }
+    float asm_ms = 0.0f;
+    cudaEventElapsedTime(&asm_ms, ev_asm0, ev_asm1);   // complete: prefill() synchronised the stream
+    stages.prefill_build_ms = plan_ms + asm_ms;
     DevState hs{};
     hs.pos = plen; hs.frame = 0; hs.done = 0; hs.n_out = 0; hs.n_trailing = tlen;
     SampleParams P{};

@@ -1474,6 +1474,27 @@ __global__ void k_icl_codec_rows(const __half * codec_embd, const __half * const
     }
 }
 
+// One row of the assembled prompt (prefill rows, trailing text rows, pad row):
+// dst = a, or 0 + a, then + b when b is set, in that order (the reference
+// builds these rows with ggml_add of the same terms,
+// src/tts_transformer.cpp:1030-1472).
+struct PromptRow {
+    float * dst;
+    const float * a, * b;
+    int zero_first;
+};
+
+// One CTA per row; every term is already an F32 row in device memory.
+__global__ void k_prompt_rows(const PromptRow * rows, int H) {
+    const PromptRow r = rows[blockIdx.x];
+    for (int d = threadIdx.x; d < H; d += blockDim.x) {
+        float v = r.a[d];
+        if (r.zero_first) v = __fadd_rn(0.0f, v);
+        if (r.b) v = __fadd_rn(v, r.b[d]);
+        r.dst[d] = v;
+    }
+}
+
 // y = silu(x + b) in place (text projection fc1 epilogue).
 __global__ void k_bias_silu(float * x, const float * b, int n, int ld, int rows) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * rows; i += gridDim.x * blockDim.x) {
