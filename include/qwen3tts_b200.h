@@ -78,7 +78,7 @@ typedef struct qtts_timing {
  * graph), each launch charged to the talker step, the code predictor, or the
  * samplers with their next-input embedding sums. */
 typedef struct qtts_stage_timing {
-    float prefill_build_ms;   /* host: text projection + prompt row assembly */
+    float prefill_build_ms;   /* host recipe + device text projection and prompt row assembly */
     float prefill_forward_ms; /* device: forward_prefill */
     float talker_ms;          /* device: talker steps (layers + codec head) */
     float code_pred_ms;       /* device: code-predictor passes (layers + heads) */
