@@ -788,7 +788,6 @@ bool Engine::layers(std::vector<LayerW> & Ls, __half * kbase, __half * vbase, in
             FusedAttn fa = fused_attn_args(l, kbase + il * layer_elems, vbase + il * layer_elems, rope, 1, nullptr,
                                            pos_static, false, nullptr, ctx);
             fa.done = done;
-            fa.warp_heads = 1;
             prof_begin(KC_ATTN, 0.0);
             pdl_launch(k_cp_step_attn, dim3(NH), dim3(32), 0, stream, fa);
             prof_end();

@@ -736,7 +736,6 @@ struct FusedAttn {
     const int * done;         // stand-alone launch: skip when *done
     uint8_t * xt;             // optional: output also as F16 tiles for the O-projection GEMM (row xt_row0 + i)
     int xt_np, xt_row0;
-    int warp_heads;           // code-predictor step: one warp per query head (cp_step_attn_warp)
 };
 
 constexpr int FA_THREADS = 512;
