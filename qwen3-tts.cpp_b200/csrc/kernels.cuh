@@ -251,6 +251,11 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
                 if (lane == 0) s_red[warp][v] = ss;
             }
         }
+    } else if (inreg) {   // no RMSNorm: the row goes to shared memory now, published by the barrier below
+        const bool r16 = !q8 && a.act == ACT_F16;
+#pragma unroll
+        for (int k = 0; k < GEMV_RPT; ++k)
+            if (tid + k * nt < cols) xs[tid + k * nt] = r16 ? round_f16(xr[k]) : xr[k];
     }
     bool ok = true;
     if (m && tid == 0) {
@@ -267,7 +272,7 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
 
     // 2. normalise (x * scale) * gain, round to F16 for F16 weights with an F16 activation
     const bool round16 = !q8 && a.act == ACT_F16;
-    if (inreg || has_norm || round16 || a.xn_out || xn_smem) {
+    if (inreg ? (has_norm || a.xn_out != nullptr) : (has_norm || round16 || a.xn_out || xn_smem)) {
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
             if (v >= nv) break;
