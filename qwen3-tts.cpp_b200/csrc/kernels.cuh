@@ -219,9 +219,10 @@ __device__ __forceinline__ bool gemv_compute(const GemvArgs & a, const int cta, 
     float * da = W.da;
     const int h8 = cols >> 3;
     // inreg: this thread's activation values (planar positions tid + k nt) in xr.
-    // F16 weights only: with Q8_0 weights the frame measured slower either way
-    // (the quantiser reads the row back from shared memory in 32-column blocks).
-    const bool inreg = Load::regs_ok && !q8 && cols <= GEMV_RPT * nt;
+    // With Q8_0 weights only without an RMSNorm: with one, the frame measured
+    // slower (the quantiser reads the row back from shared memory in 32-column
+    // blocks after the normalisation barrier).
+    const bool inreg = Load::regs_ok && cols <= GEMV_RPT * nt && (!q8 || a.norm_g == nullptr);
     float xr[GEMV_RPT];
     if (inreg) {
         load.regs(xr, W, r0, nrow, rstride);
